@@ -1,0 +1,373 @@
+"""Benchmark of the GDN prefill hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg5|cfg3] [--tokens T]
+
+Default workload (cfg5): one 65536-token sequence through causal_conv1d
+(8192 channels, width 4, SiLU) -> chunked gated delta rule (Hk 16 -> Hv 32,
+dk = dv = 128, q/k L2-normalised in kernel) -> gated RMSNorm (group 128,
+SiLU(z) gate).  The 32 value heads, their key heads and conv channels are
+split over the N ranks (one process per GPU, no collective on the data path);
+the sequence is the unit of work, so `value` = 65536 tokens / max-over-ranks
+step time ("scaling": "strong").  cfg3 is the varlen 8-sequence 16384-token
+GDN prefill alone.
+
+Inputs are seeded synthetic tensors (torch_npu_ops_b200.workloads), resident
+in HBM for `value`; each step touches > 1 GB, far above the 126 MB L2, so no
+flush is needed between steps.  `e2e` repeats the step through the public
+API with the step's inputs copied from pinned host memory and the output
+copied back inside the timed region.  `--impl reference` times the
+reference algorithm (the CPU oracle restating the reference's torch
+implementation) on the host cores instead.
+"""
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "GDN prefill tokens/s/GPU; norm/RoPE/conv1d HBM GB/s vs B200 peak"
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# -------------------------------------------------------------- workloads --
+def build_cfg5(rank, world, T, dev):
+    from torch_npu_ops_b200 import workloads
+    w = workloads.long_config5_shard(rank, world, T=T)
+    (v0, v1), (k0, k1) = w["heads"], w["k_heads"]
+    hv, hk = v1 - v0, k1 - k0
+    host = {"x": w["x"], "g": w["g"], "beta": w["beta"], "z": w["z"]}
+    dev_t = {n: t.to(dev) for n, t in host.items()}
+    consts = {"weight": w["weight"].to(dev), "bias": w["bias"].to(dev),
+              "norm_w": w["norm_w"].to(dev)}
+    C = w["x"].shape[1]
+    return {"T": T, "hv": hv, "hk": hk, "C": C, "host": host, "dev": dev_t, "consts": consts,
+            "lengths": [T]}
+
+
+def build_cfg3(dev):
+    from torch_npu_ops_b200 import workloads
+    w = workloads.chunk_config3()
+    host = {n: w[n] for n in ("q", "k", "v", "g", "beta", "initial_state")}
+    return {"T": int(w["cu_seqlens"][-1]), "hv": 32, "hk": 16, "host": host,
+            "dev": {n: t.to(dev) for n, t in host.items()},
+            "consts": {"cu": w["cu_seqlens"].to(dev)}, "lengths": w["lengths"]}
+
+
+def make_step(cfg, kind, dev):
+    """Returns step(inputs) -> output tensor, plus per-stage event hooks."""
+    import torch_npu_ops_b200 as ops
+    c = cfg["consts"]
+    if kind == "cfg3":
+        def step(inp, ev=None):
+            if ev: ev[0].record()
+            o, ht = ops.npu_chunk_gated_delta_rule(inp["q"], inp["k"], inp["v"], inp["g"],
+                                                   inp["beta"], None, inp["initial_state"], True,
+                                                   c["cu"])
+            if ev: ev[1].record()
+            return o
+        return step, ["gdn"]
+    T, hv, hk, d = cfg["T"], cfg["hv"], cfg["hk"], 128
+    state = torch.zeros(1, cfg["C"], 3, dtype=torch.bfloat16, device=dev)
+    qsl = torch.tensor([0, T], dtype=torch.int32, device=dev)
+
+    def step(inp, ev=None):
+        if ev: ev[0].record()
+        state.zero_()  # fresh prefill: zero conv history
+        y = ops.npu_causal_conv1d_update_v2(inp["x"], state, c["weight"], True, c["bias"],
+                                            query_start_loc=qsl)
+        if ev: ev[1].record()
+        q = y[:, : hk * d].view(1, T, hk, d)
+        k = y[:, hk * d: 2 * hk * d].view(1, T, hk, d)
+        v = y[:, 2 * hk * d:].view(1, T, hv, d)
+        o, _ = ops.npu_chunk_gated_delta_rule(q, k, v, inp["g"], inp["beta"], None, None, True,
+                                              None, False, True)
+        if ev: ev[2].record()
+        out = ops.layer_norm_fwd(o.view(-1, d), c["norm_w"], None, 1e-6, inp["z"].view(-1, d), d,
+                                 True, True)
+        if ev: ev[3].record()
+        return out
+    return step, ["conv", "gdn", "norm"]
+
+
+def stage_bytes(cfg, kind):
+    """Algorithmic HBM bytes per launch of the bandwidth-bound stages."""
+    if kind == "cfg3":
+        return {}
+    T, C, hv = cfg["T"], cfg["C"], cfg["hv"]
+    return {"conv": 2 * 2 * T * C + 2 * C * 5,
+            "norm": 3 * 2 * T * hv * 128 + 2 * 128 + 4 * T * hv}
+
+
+# ------------------------------------------------------------- reference ----
+def cpu_reference(kind, T_sample, reps=3):
+    """Times the CPU oracle (the reference's torch algorithm) on a bounded
+    sample of the workload with every host thread; returns tokens/s info."""
+    import oracle
+    from torch_npu_ops_b200 import workloads
+    torch.set_num_threads(os.cpu_count() or 1)
+    if kind == "cfg3":
+        w = workloads.chunk_config3(lengths=[T_sample // 2, T_sample - T_sample // 2])
+        fn = lambda: oracle.chunk_gated_delta_rule(w["q"], w["k"], w["v"], w["g"], w["beta"], None,
+                                                   w["initial_state"], True, w["cu_seqlens"])
+        sample = f"chunked GDN oracle, {T_sample} tokens (2 seqs), Hv 32"
+    else:
+        w = workloads.long_config5_shard(0, 1, T=T_sample)
+        d, hk, hv = 128, 16, 32
+        st = torch.zeros(1, w["x"].shape[1], 3, dtype=torch.bfloat16)
+        qsl = torch.tensor([0, T_sample], dtype=torch.int32)
+
+        def fn():
+            y = oracle.causal_conv1d_varlen(w["x"], st.clone(), w["weight"], w["bias"], True, qsl)
+            q = y[:, : hk * d].reshape(1, T_sample, hk, d)
+            k = y[:, hk * d: 2 * hk * d].reshape(1, T_sample, hk, d)
+            v = y[:, 2 * hk * d:].reshape(1, T_sample, hv, d)
+            o, _ = oracle.chunk_gated_delta_rule(q, k, v, w["g"], w["beta"], None, None, True,
+                                                 None, True)
+            return oracle.layer_norm_fwd(o.reshape(-1, d), w["norm_w"], None, 1e-6,
+                                         w["z"].reshape(-1, d), d, True, True)[0]
+        sample = (f"conv->chunk GDN->gated RMSNorm oracle on the first {T_sample} tokens of the "
+                  "65536-token sequence, all 32 heads")
+    fn()  # warm-up
+    ts = []
+    for _ in range(reps):
+        t = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t)
+    med = statistics.median(ts)
+    return {"value": T_sample / med, "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": sample, "seconds_per_sample": med}
+
+
+# ------------------------------------------------------------------ main ----
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="cfg5", choices=["cfg5", "cfg3"])
+    ap.add_argument("--tokens", type=int, default=65536)
+    ap.add_argument("--cpu-sample", type=int, default=8192)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    a = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    kind = a.workload
+    T = a.tokens if kind == "cfg5" else 16384
+    config = ({"workload": "cfg5: 1 x 65536-token prefill, conv1d(8192ch,w4,SiLU) -> chunked GDN "
+                           "(Hk16->Hv32, dk=dv=128, qk L2 in kernel) -> gated RMSNorm(g128)",
+               "tokens": T, "heads_per_gpu": 32 // max(1, world), "parallelism": f"head-shard x{world}",
+               "l2_flush": "inputs > L2 (>1 GB per step)"}
+              if kind == "cfg5" else
+              {"workload": "cfg3: 8 seqs / 16384 tokens varlen chunked GDN (Hk16->Hv32)",
+               "tokens": T, "parallelism": "replica", "l2_flush": "inputs > L2 (~0.45 GB per step)"})
+
+    if a.impl == "reference":
+        if rank != 0:
+            return
+        ref = cpu_reference(kind, a.cpu_sample)
+        for _ in range(max(0, a.warmup - 1)):
+            pass
+        line = {"impl": "reference", "metric": METRIC, "value": ref["value"], "unit": "tokens/s",
+                "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+                "ms_per_step": 1000.0 * ref["seconds_per_sample"], "higher_is_better": True,
+                "scaling": "strong" if kind == "cfg5" else "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic", "config": config,
+                "cpu_baseline": ref,
+                "e2e": {"value": ref["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    from torch_npu_ops_b200 import _lib, workloads
+    _lib.load()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    cfg = build_cfg5(rank, world, T, dev) if kind == "cfg5" else build_cfg3(dev)
+    step, stages = make_step(cfg, kind, dev)
+    inp = cfg["dev"]
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(a.warmup):
+        step(inp)
+    barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)]
+           for _ in range(a.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                          else local)
+    clocks.start()
+    l0 = _lib.launch_count()
+    barrier()
+    start.record()
+    for i in range(a.steps):
+        step(inp, evs[i])
+    stop.record()
+    barrier()
+    launches = _lib.launch_count() - l0
+    clk = clocks.stop()
+    elapsed = start.elapsed_time(stop)
+    stage_ms = {s: statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs)
+                for j, s in enumerate(stages)}
+    t_local = torch.tensor([elapsed], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t_local, op=torch.distributed.ReduceOp.MAX)
+    ms_step = t_local.item() / a.steps
+    value = T / (ms_step / 1000.0)
+
+    peaks = _peaks()
+    flops = workloads.chunk_flops(cfg["lengths"], cfg["hv"])
+    gdn_ms = stage_ms["gdn"]
+    achieved = flops / (gdn_ms / 1000.0) / 1e12
+    roofline = {"kernel": "chunk_gdn_fused_kernel", "bound": "tensor", "achieved": achieved,
+                "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops_sustained"],
+                "peak_source": f"{peaks['source']} sustained bf16",
+                "flops_per_launch": flops, "launch_ms": gdn_ms, "traffic": None}
+    kernels = {}
+    for s, byt in stage_bytes(cfg, kind).items():
+        gbs = byt / (stage_ms[s] / 1000.0) / 1e9
+        kernels[s] = {"ms": stage_ms[s], "bytes": byt, "GB/s": gbs,
+                      "frac_hbm": gbs / peaks["hbm_gbs"]}
+    kernels["gdn"] = {"ms": gdn_ms, "TFLOP/s": achieved}
+
+    e2e = None
+    if not a.no_e2e:
+        host = {n: t.pin_memory() for n, t in cfg["host"].items()}
+        dbuf = {n: torch.empty_like(t) for n, t in cfg["dev"].items()}
+        out0 = step(inp)
+        hout = torch.empty(out0.shape, dtype=out0.dtype, pin_memory=True)
+        h2d = sum(t.numel() * t.element_size() for t in host.values())
+        d2h = hout.numel() * hout.element_size()
+
+        def e2e_step():
+            for n in host:
+                dbuf[n].copy_(host[n], non_blocking=True)
+            out = step(dbuf)
+            hout.copy_(out, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        s2, t2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(a.steps):
+            e2e_step()
+        t2.record()
+        barrier()
+        te = torch.tensor([s2.elapsed_time(t2)], device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+        e2e = {"value": T / (te.item() / a.steps / 1000.0), "unit": "tokens/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "torch_npu_ops_b200 public API, pinned host <-> HBM copies inside the "
+                       "timed region"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_reference(kind, a.cpu_sample)
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step,
+                "higher_is_better": True, "scaling": "strong" if kind == "cfg5" else "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
+                "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": launches, "clocks": clk}
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,222 @@
+/*
+ * xops_b200 -- C ABI of the B200 (sm_100a) build of the xLLM GDN
+ * linear-attention and normalisation hot path.
+ *
+ * Every entry point takes raw device pointers, element counts/strides and a
+ * cudaStream_t (passed as void*), validates its arguments on the host before
+ * launching anything, enqueues its kernels on that stream and returns an
+ * xops_status_t.  Nothing synchronises the stream and nothing allocates
+ * device memory: where a kernel needs scratch, the caller passes a workspace
+ * sized by the matching *_workspace_size query.  On failure the call launches
+ * nothing (argument errors) and xops_last_error() holds a message for the
+ * calling thread.
+ *
+ * Each declaration names the reference interface it replaces (paths relative
+ * to the reference project root).  Layout conventions follow the reference:
+ * token-major [B, T, H, D] tensors, varlen batches as B == 1 plus int32
+ * cu_seqlens [N+1], grouped-query heads h -> h / (H / Hg).
+ */
+#ifndef XOPS_B200_H_
+#define XOPS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define XOPS_API __attribute__((visibility("default")))
+#else
+#define XOPS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  XOPS_OK = 0,
+  XOPS_ERR_INVALID_ARGUMENT = 1, /* bad shape / pointer / dtype (TORCH_CHECK) */
+  XOPS_ERR_UNSUPPORTED = 2,      /* valid request outside the compiled kernels */
+  XOPS_ERR_CUDA = 3,             /* launch or runtime error from CUDA */
+  XOPS_ERR_WORKSPACE = 4         /* workspace missing or too small */
+} xops_status_t;
+
+typedef enum { XOPS_F32 = 0, XOPS_BF16 = 1, XOPS_F16 = 2 } xops_dtype_t;
+
+/* Message of the last failing call on this thread ("" if none). */
+XOPS_API const char* xops_last_error(void);
+/* Library version string. */
+XOPS_API const char* xops_version(void);
+/* Number of kernel launches this library has issued (process-wide). */
+XOPS_API uint64_t xops_launch_count(void);
+
+/* ---------------------------------------------------------------- norms -- */
+
+/* y = x * rsqrt(sum(x^2) + eps) over the last axis; x, y [rows, cols], bf16
+ * or fp32, contiguous.  Replaces npu_l2norm_last_dim
+ * (triton_npu/torch_api/npu_triton_l2norm.cpp:52-108). */
+XOPS_API int xops_l2norm_last_dim(const void* x, void* y, int64_t rows, int64_t cols, float eps,
+                         int dtype, void* stream);
+
+/* Grouped LayerNorm / RMSNorm with optional bias and SiLU gate z.
+ * x, z [M, N] with row strides; y [M, N] (row stride stride_y); weight,
+ * bias [N]; mean (LayerNorm only, may be NULL for RMSNorm) and rstd are fp32
+ * [ngroups * M] indexed group * M + row.  norm_before_gate selects
+ * y = norm(x)*w(+b) * silu(z) (1) or norm(x * silu(z))*w(+b) (0).
+ * x/z/y dtype x_dtype; weight/bias dtype w_dtype.  Replaces layer_norm_fwd
+ * (triton_npu/torch_api/npu_triton_layernorm_fwd.cpp:48-333) and
+ * npu_ops::layer_norm_fwd / aclnnLayerNormFwd
+ * (ascendc_npu/layer_norm_fwd.cpp:24-82). */
+XOPS_API int xops_layer_norm_fwd(const void* x, const void* weight, const void* bias, const void* z,
+                        void* y, float* mean, float* rstd, int64_t M, int64_t N,
+                        int64_t group_size, int64_t stride_x_row, int64_t stride_z_row,
+                        int64_t stride_y_row, float eps, int norm_before_gate,
+                        int is_rms_norm, int x_dtype, int w_dtype, void* stream);
+
+/* Gemma RMSNorm y = x * rsqrt(mean(x^2) + eps) * (1 + gamma) over rows of
+ * length cols; rstd fp32 [rows].  Replaces npu_ops::npu_gemma_rms_norm /
+ * aclnnGemmaRmsNorm (ascendc_npu/gemma_rms_norm.cpp:28-57). */
+XOPS_API int xops_gemma_rms_norm(const void* x, const void* gamma, void* y, float* rstd, int64_t rows,
+                        int64_t cols, float eps, int x_dtype, int gamma_dtype, void* stream);
+
+/* ----------------------------------------------------------------- rope -- */
+
+/* Split packed [T, q_hidden + 2*kv_hidden] into q, k, v; per-head RMSNorm
+ * (weight [head_dim] shared by heads, optional bias) on q and k; NeoX
+ * rotate-half RoPE on the first rotary_dim dims with per-token sin/cos
+ * [T, rotary_dim]; v copied.  Outputs contiguous in the input dtype.
+ * rotary_dim == head_dim is the reference kernel; rotary_dim < head_dim is
+ * the partial-rotary extension.  Replaces npu_split_rmsnorm_rope
+ * (triton_npu/torch_api/npu_triton_split_rmsnorm_rope.cpp:57-143). */
+XOPS_API int xops_split_rmsnorm_rope(const void* input, const void* sin, const void* cos, void* q_out,
+                            void* k_out, void* v_out, const void* q_weight, const void* q_bias,
+                            const void* k_weight, const void* k_bias, int64_t num_tokens,
+                            int64_t q_hidden, int64_t kv_hidden, int64_t head_dim,
+                            int64_t rotary_dim, float eps, int dtype, int w_dtype,
+                            int sincos_dtype, void* stream);
+
+/* --------------------------------------------------------------- conv1d -- */
+
+/* Decode-style depthwise causal conv update.  x [batch, dim, seqlen] with
+ * strides (x_stride_b, x_stride_d, x_stride_t); out same shape, contiguous;
+ * conv_state [num_cache_lines, dim, state_len] contiguous, updated in place
+ * (state <- last state_len columns of cat(state, x)); weight [dim, width];
+ * bias [dim] or NULL; conv_state_indices [batch] int32 or NULL (identity);
+ * rows whose slot equals pad_slot_id are skipped.  Replaces
+ * npu_causal_conv1d_update (triton_npu/torch_api/npu_triton_causal_conv1d_update.cpp:22-137). */
+XOPS_API int xops_causal_conv1d_update(const void* x, void* conv_state, const void* weight,
+                              const void* bias, const int32_t* conv_state_indices, void* out,
+                              int64_t batch, int64_t dim, int64_t seqlen, int64_t width,
+                              int64_t state_len, int64_t num_cache_lines, int64_t x_stride_b,
+                              int64_t x_stride_d, int64_t x_stride_t, int silu,
+                              int32_t pad_slot_id, int dtype, void* stream);
+
+/* Varlen (prefill) depthwise causal conv: x [total_tokens, dim] token-major,
+ * out same; query_start_loc [batch+1] int32; conv_state
+ * [num_cache_lines, dim, width-1] holds each sequence's history and is
+ * updated in place to the last width-1 inputs of cat(history, x_seq).
+ * Replaces npu_causal_conv1d_update_v2 with query_start_loc
+ * (triton_npu/torch_api/npu_triton_causal_conv1d_update_v2.cpp:99-239). */
+XOPS_API int xops_causal_conv1d_varlen(const void* x, void* conv_state, const void* weight,
+                              const void* bias, const int32_t* query_start_loc,
+                              const int32_t* conv_state_indices, void* out, int64_t batch,
+                              int64_t total_tokens, int64_t dim, int64_t width,
+                              int64_t num_cache_lines, int silu, int32_t pad_slot_id, int dtype,
+                              void* stream);
+
+/* ---------------------------------------------------- gated delta rule -- */
+
+/* Token-serial gated delta rule (decode).  q, k [B, T, H, K], v [B, T, HV, V]
+ * bf16; g, beta [B, T, HV] fp32 (beta may be NULL = ones); o [B, T, HV, V]
+ * bf16; h0 fp32 state slots [*, HV, K, V] with slot stride h0_stride,
+ * read from slot ssm_state_indices[n] (or n); ht == h0 updates those slots
+ * in place, any other ht is [N, HV, K, V] (stride ht_stride) indexed by
+ * sequence.  Sequences: cu_seqlens [N+1] int32, or NULL with N == B rows of
+ * T tokens.  ssm_state_indices [N] int32 or NULL (slot n).  K, V <= 128
+ * (multiples of 32).  Replaces npu_fused_recurrent_gated_delta_rule
+ * (triton_npu/torch_api/npu_triton_recurrent_gated_delta_rule.cpp:54-246). */
+XOPS_API int xops_fused_recurrent_gated_delta_rule(const void* q, const void* k, const void* v,
+                                          const float* g, const float* beta, void* o,
+                                          const float* h0, float* ht,
+                                          const int32_t* cu_seqlens,
+                                          const int32_t* ssm_state_indices, int64_t B,
+                                          int64_t T, int64_t N, int64_t H, int64_t HV,
+                                          int64_t K, int64_t V, int64_t h0_stride,
+                                          int64_t ht_stride, float scale,
+                                          int use_qk_l2norm_in_kernel, void* stream);
+
+/* Chunked gated delta rule prefill, fused (cumsum, KKT, triangular inverse,
+ * WY transform, chunk-state recurrence and output pass in one kernel; no
+ * intermediate touches HBM).  q, k [B, T, Hg, K], v [B, T, H, V] bf16;
+ * g, beta [B, T, H] fp32; h0 [N, H, K, V] fp32 or NULL; o [B, T, H, V] bf16;
+ * ht [N, H, K, V] fp32 or NULL.  cu_seqlens [N+1] int32 with B == 1, or NULL
+ * with N == B.  K == V == 128, chunk 64.  q/k/v rows may be strided views
+ * (e.g. slices of a packed conv output): *_token_stride is the element
+ * distance between consecutive tokens (0 = contiguous), heads contiguous
+ * inside a token.  Needs no workspace.  Replaces
+ * npu_chunk_gated_delta_rule (triton_npu/torch_api/npu_triton_chunk_gated_delta_rule.cpp:556-642). */
+XOPS_API int xops_chunk_gated_delta_rule(const void* q, const void* k, const void* v, const float* g,
+                                const float* beta, const float* h0, void* o, float* ht,
+                                const int32_t* cu_seqlens, int64_t B, int64_t T, int64_t N,
+                                int64_t Hg, int64_t H, int64_t K, int64_t V,
+                                int64_t q_token_stride, int64_t k_token_stride,
+                                int64_t v_token_stride, float scale,
+                                int use_qk_l2norm_in_kernel, void* stream);
+
+/* ---- chunk pipeline sub-operators (the reference's decomposition) ---- */
+/* All take the same sequence description (cu_seqlens [N+1] int32 with B == 1
+ * or NULL with N == B) and chunk_size == 64. */
+
+/* g_cumsum [B, T, H] fp32 = per-chunk inclusive cumsum of g.  Replaces
+ * npu_chunk_local_cumsum (npu_triton_chunk_gated_delta_rule.cpp:151-227). */
+XOPS_API int xops_chunk_local_cumsum(const float* g, float* g_cumsum, const int32_t* cu_seqlens,
+                            int64_t B, int64_t T, int64_t N, int64_t H, int64_t chunk_size,
+                            void* stream);
+
+/* A [B, T, H, 64] fp32 = strict_tril(beta_i exp(g_i - g_j) k_i.k_j) per chunk.
+ * Replaces npu_chunk_scaled_dot_kkt_fwd (npu_triton_chunk_gated_delta_rule.cpp:229-297). */
+XOPS_API int xops_chunk_scaled_dot_kkt_fwd(const void* k, const float* beta, const float* g_cumsum,
+                                  float* A, const int32_t* cu_seqlens, int64_t B, int64_t T,
+                                  int64_t N, int64_t Hg, int64_t H, int64_t K,
+                                  int64_t chunk_size, void* stream);
+
+/* Ai [B, T, H, 64] (out_dtype) = (I + A_c)^-1 per chunk.  Replaces
+ * npu_solve_tril (npu_triton_chunk_gated_delta_rule.cpp:299-395). */
+XOPS_API int xops_solve_tril(const float* A, void* Ai, const int32_t* cu_seqlens, int64_t B, int64_t T,
+                    int64_t N, int64_t H, int64_t chunk_size, int out_dtype, void* stream);
+
+/* w [B, T, H, K] = Ai (beta e^g k), u [B, T, H, V] = Ai (beta v), bf16;
+ * Ai in ai_dtype.  Replaces npu_recompute_w_u_fwd
+ * (npu_triton_chunk_gated_delta_rule.cpp:397-475). */
+XOPS_API int xops_recompute_w_u_fwd(const void* k, const void* v, const float* beta,
+                           const float* g_cumsum, const void* Ai, int ai_dtype, void* w, void* u,
+                           const int32_t* cu_seqlens, int64_t B, int64_t T, int64_t N,
+                           int64_t Hg, int64_t H, int64_t K, int64_t V, void* stream);
+
+/* Chunk-state pass: h [B, NT, H, K, V] bf16 (state at every chunk start),
+ * v_new [B, T, H, V] bf16 (may be NULL), ht [N, H, K, V] fp32 (may be NULL);
+ * g_cumsum may be NULL (no gating); h0 fp32 or NULL.  NT = total chunks.
+ * Replaces npu_chunk_gated_delta_rule_fwd_h
+ * (npu_triton_chunk_gated_delta_rule.cpp:644-802). */
+XOPS_API int xops_chunk_gated_delta_rule_fwd_h(const void* k, const void* w, const void* u,
+                                      const float* g_cumsum, const float* h0, void* h,
+                                      void* v_new, float* ht, const int32_t* cu_seqlens,
+                                      int64_t B, int64_t T, int64_t N, int64_t Hg, int64_t H,
+                                      int64_t K, int64_t V, int64_t NT, void* stream);
+
+/* o [B, T, H, V] bf16 = scale (q h e^g + tril(q k^T e^{g_i-g_j}) v_new).
+ * Replaces npu_chunk_fwd_o (npu_triton_chunk_gated_delta_rule.cpp:477-554). */
+XOPS_API int xops_chunk_fwd_o(const void* q, const void* k, const void* v_new, const void* h,
+                     const float* g_cumsum, void* o, const int32_t* cu_seqlens, int64_t B,
+                     int64_t T, int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V,
+                     int64_t NT, float scale, void* stream);
+
+/* Total chunk count of a batch, computed on the host from a HOST copy of
+ * cu_seqlens (or B*ceil(T/64) when cu_seqlens_host is NULL). */
+XOPS_API int64_t xops_total_chunks(const int32_t* cu_seqlens_host, int64_t B, int64_t T, int64_t N,
+                          int64_t chunk_size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XOPS_B200_H_ */

@@ -1,0 +1,119 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol
+declared in include/*.h, and rejects bad arguments on the host (before any
+CUDA call) with the documented status codes."""
+
+import ctypes as C
+import glob
+import os
+import re
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(h).read()
+        names |= set(re.findall(r"XOPS_API\s+[\w\s\*]+?\b(xops_\w+)\s*\(", text))
+    return names
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from torch_npu_ops_b200 import _lib
+    return _lib.load()
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "xops_chunk_gated_delta_rule" in names
+    assert len(names) >= 18
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in sorted(_declared()):
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+
+
+def test_binding_covers_header():
+    from torch_npu_ops_b200 import _lib
+    assert _declared() == set(_lib.SIGNATURES), "ctypes signature table out of sync with header"
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.xops_version()
+
+
+def _call(lib, name, *args):
+    return getattr(lib, name)(*args), lib.xops_last_error().decode()
+
+
+def test_host_validation_layer_norm(lib):
+    rc, msg = _call(lib, "xops_layer_norm_fwd", None, None, None, None, None, None, None,
+                    4, 100, 30, 100, 0, 100, 1e-6, 1, 1, 1, 1, None)
+    assert rc == 1 and "divisible" in msg
+
+
+def test_host_validation_chunk_unsupported_dims(lib):
+    rc, msg = _call(lib, "xops_chunk_gated_delta_rule", None, None, None, None, None, None, None,
+                    None, None, 1, 64, 1, 1, 1, 64, 64, 0, 0, 0, 0.1, 0, None)
+    assert rc == 2 and "128" in msg
+
+
+def test_host_validation_gqa(lib):
+    rc, msg = _call(lib, "xops_chunk_gated_delta_rule", None, None, None, None, None, None, None,
+                    None, None, 1, 64, 1, 3, 4, 128, 128, 0, 0, 0, 0.1, 0, None)
+    assert rc == 1 and "divisible" in msg
+
+
+def test_host_validation_conv_width(lib):
+    rc, msg = _call(lib, "xops_causal_conv1d_varlen", None, None, None, None, None, None, None,
+                    2, 10, 64, 9, 2, 1, -1, 1, None)
+    assert rc == 1 and "width" in msg
+
+
+def test_empty_inputs_are_noops(lib):
+    # zero sequences / rows: nothing to launch, OK without touching the device
+    assert lib.xops_chunk_gated_delta_rule(None, None, None, None, None, None, None, None, None,
+                                           1, 0, 1, 1, 1, 128, 128, 0, 0, 0, 0.1, 0, None) == 0
+    assert lib.xops_layer_norm_fwd(None, None, None, None, None, None, None, 0, 128, 128, 128, 0,
+                                   128, 1e-6, 1, 1, 1, 1, None) == 0
+
+
+def test_total_chunks_host(lib):
+    cu = (C.c_int32 * 4)(0, 65, 66, 196)
+    assert lib.xops_total_chunks(cu, 1, 196, 3, 64) == 2 + 1 + 3
+    assert lib.xops_total_chunks(None, 2, 100, 2, 64) == 4
+
+
+def test_ops_fail_loudly_off_gpu():
+    """The host API has no CPU path: CPU tensors raise instead of computing."""
+    import torch_npu_ops_b200 as ops
+    x = torch.randn(4, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.npu_l2norm_last_dim(x)
+    q = torch.randn(1, 8, 2, 128, dtype=torch.bfloat16)
+    v = torch.randn(1, 8, 4, 128, dtype=torch.bfloat16)
+    g = torch.zeros(1, 8, 4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.npu_chunk_gated_delta_rule(q, q, v, g, g)
+
+
+def test_ops_reject_like_reference():
+    import torch_npu_ops_b200 as ops
+    q = torch.randn(1, 8, 2, 128)
+    v = torch.randn(1, 8, 4, 128)
+    g = torch.zeros(1, 8, 4)
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        ops.npu_chunk_gated_delta_rule(q, q, v, g, g)
+    with pytest.raises(RuntimeError, match="head_first"):
+        ops.npu_chunk_gated_delta_rule(q, q, v, g, g, head_first=True)
+    with pytest.raises(RuntimeError, match="query_start_loc"):
+        ops.npu_causal_conv1d_update(torch.randn(2, 8), torch.randn(2, 8, 3), torch.randn(8, 4),
+                                     query_start_loc=torch.tensor([0, 1, 2]))
+    with pytest.raises(RuntimeError, match="power of two"):
+        ops.npu_split_rmsnorm_rope(torch.randn(2, 30 * 5), torch.randn(2, 30), torch.randn(2, 30),
+                                   torch.randn(30), torch.randn(30), 90, 30, 30, 1e-6)

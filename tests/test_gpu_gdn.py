@@ -1,0 +1,203 @@
+"""GPU parity: chunked gated delta rule (fused op and the sub-operator
+pipeline) and the fused recurrent (decode) rule, against the CPU oracle and
+the reference's golden fixtures."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+import torch_npu_ops_b200 as ops
+from parity import BF16_MAXABS, assert_bf16, assert_fp32, assert_state, golden, rel_fro
+from torch_npu_ops_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _to(t):
+    return None if t is None else t.to(DEV)
+
+
+def _run_chunk(inp, l2=False, scale=None):
+    o, ht = ops.npu_chunk_gated_delta_rule(
+        _to(inp["q"]), _to(inp["k"]), _to(inp["v"]), _to(inp["g"]), _to(inp["beta"]), scale,
+        _to(inp["initial_state"]), True, _to(inp["cu_seqlens"]), False, l2)
+    torch.cuda.synchronize()
+    return o.cpu(), ht.cpu()
+
+
+def _oracle_chunk(inp, l2=False, scale=None):
+    return oracle.chunk_gated_delta_rule(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"], scale,
+                                         inp["initial_state"], True, inp["cu_seqlens"], l2)
+
+
+@pytest.mark.parametrize("case", golden("chunk_gated_delta_rule"), ids=lambda c: c["name"])
+def test_chunk_golden(case):
+    a = case["args"]
+    if a["q"].shape[-1] != 128 or a["v"].shape[-1] != 128:
+        pytest.skip("compiled for head_dim 128 (the reference kernels' constraint)")
+    inp = dict(a)
+    o, ht = _run_chunk(inp, a["use_qk_l2norm_in_kernel"])
+    ro, rh = _oracle_chunk(inp, a["use_qk_l2norm_in_kernel"])
+    assert_bf16(o, ro)
+    assert_state(ht, rh)
+    # and the reference's own output, within its test tolerance (1e-2)
+    assert_bf16(o, case["out"]["o"], tol=2e-2)
+
+
+def test_chunk_config3():
+    inp = workloads.chunk_config3()
+    o, ht = _run_chunk(inp)
+    ro, rh = _oracle_chunk(inp)
+    assert_bf16(o, ro)
+    assert_state(ht, rh)
+
+
+@pytest.mark.parametrize("lens,hk,hv,l2,h0", [
+    ([1, 63, 64, 65, 0, 129, 7], 2, 4, False, True),     # ragged tails, empty sequence
+    ([300], 1, 1, True, False),                         # in-kernel L2 norm, no initial state
+    ([64] * 5, 4, 4, False, True),                      # no GQA, exact chunk multiples
+    ([1000, 24], 2, 6, True, True),                     # GQA group 3
+])
+def test_chunk_varlen_edges(lens, hk, hv, l2, h0):
+    inp = workloads.chunk_config3(hk=hk, hv=hv, lengths=lens, seed=sum(lens))
+    if not h0:
+        inp["initial_state"] = None
+    if l2:  # raw (un-normalised) q/k so the in-kernel norm matters
+        g = torch.Generator().manual_seed(9)
+        inp["q"] = torch.randn(inp["q"].shape, generator=g).to(torch.bfloat16)
+        inp["k"] = torch.randn(inp["k"].shape, generator=g).to(torch.bfloat16)
+    o, ht = ops.npu_chunk_gated_delta_rule(
+        _to(inp["q"]), _to(inp["k"]), _to(inp["v"]), _to(inp["g"]), _to(inp["beta"]), None,
+        _to(inp["initial_state"]), True, _to(inp["cu_seqlens"]), False, l2)
+    ro, rh = oracle.chunk_gated_delta_rule(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"],
+                                           None, inp["initial_state"], True, inp["cu_seqlens"], l2)
+    assert_bf16(o, ro)
+    keep = [i for i, L in enumerate(lens) if L > 0 or h0]
+    assert_state(ht.cpu()[keep], rh[keep])
+
+
+def test_chunk_batched_no_cu_and_scale():
+    g = torch.Generator().manual_seed(21)
+    B, T = 3, 150
+    q = F.normalize(torch.randn(B, T, 2, 128, generator=g), dim=-1).to(torch.bfloat16)
+    k = F.normalize(torch.randn(B, T, 2, 128, generator=g), dim=-1).to(torch.bfloat16)
+    v = torch.randn(B, T, 4, 128, generator=g).to(torch.bfloat16)
+    gate = F.logsigmoid(torch.randn(B, T, 4, generator=g))
+    beta = torch.sigmoid(torch.randn(B, T, 4, generator=g))
+    h0 = 0.1 * torch.randn(B, 4, 128, 128, generator=g)
+    o, ht = ops.npu_chunk_gated_delta_rule(_to(q), _to(k), _to(v), _to(gate), _to(beta), 0.05,
+                                           _to(h0), True, None)
+    ro, rh = oracle.chunk_gated_delta_rule(q, k, v, gate, beta, 0.05, h0, True, None)
+    assert_bf16(o, ro)
+    assert_state(ht, rh)
+
+
+def test_chunk_strided_qkv_views():
+    """q/k/v as slices of one packed [T, (2*Hk + Hv) * 128] tensor (the conv
+    output layout) give the same result as contiguous inputs."""
+    inp = workloads.chunk_config3(hk=2, hv=4, lengths=[200, 77], seed=4)
+    T = 277
+    packed = torch.cat([inp["q"].reshape(T, -1), inp["k"].reshape(T, -1), inp["v"].reshape(T, -1)],
+                       dim=1).to(DEV)
+    qv = packed[:, :256].view(1, T, 2, 128)
+    kv = packed[:, 256:512].view(1, T, 2, 128)
+    vv = packed[:, 512:].view(1, T, 4, 128)
+    o1, h1 = ops.npu_chunk_gated_delta_rule(qv, kv, vv, _to(inp["g"]), _to(inp["beta"]), None,
+                                            _to(inp["initial_state"]), True, _to(inp["cu_seqlens"]))
+    o2, h2 = ops.npu_chunk_gated_delta_rule(_to(inp["q"]), _to(inp["k"]), _to(inp["v"]),
+                                            _to(inp["g"]), _to(inp["beta"]), None,
+                                            _to(inp["initial_state"]), True, _to(inp["cu_seqlens"]))
+    assert torch.equal(o1, o2) and torch.equal(h1, h2)
+
+
+def test_chunk_subops_pipeline():
+    """cumsum -> kkt -> solve_tril -> w/u -> fwd_h -> fwd_o on the GPU, each
+    stage against the oracle's same stage, and the composition against the
+    fused op."""
+    inp = workloads.chunk_config3(hk=2, hv=4, lengths=[130, 1, 64, 250], seed=8)
+    q, k, v, g, beta, h0, cu = (inp[n] for n in ("q", "k", "v", "g", "beta", "initial_state",
+                                                 "cu_seqlens"))
+    gc = ops.npu_chunk_local_cumsum(_to(g), 64, _to(cu))
+    rgc = oracle.chunk_local_cumsum(g, 64, cu)
+    assert_fp32(gc, rgc)
+    A = ops.npu_chunk_scaled_dot_kkt_fwd(_to(k), _to(beta), gc, 64, _to(cu))
+    rA = oracle.chunk_scaled_dot_kkt_fwd(k, beta, rgc, 64, cu)
+    assert (A.cpu() - rA).abs().max().item() < 2e-3 * max(1.0, rA.abs().max().item())
+    Ai = ops.npu_solve_tril(A, 64, _to(cu), torch.float32)
+    rAi = oracle.solve_tril(rA, 64, cu)
+    assert rel_fro(Ai, rAi) < 1e-3
+    w, u = ops.npu_recompute_w_u_fwd(_to(k), _to(v), _to(beta), gc, Ai, _to(cu))
+    rw, ru = oracle.recompute_w_u_fwd(k, v, beta, rgc, rAi, cu)
+    assert_bf16(w, rw)
+    assert_bf16(u, ru)
+    h, vn, ht = ops.npu_chunk_gated_delta_rule_fwd_h(_to(k), w, u, gc, _to(h0), True, 64, True,
+                                                     _to(cu))
+    rh, rvn, rht = oracle.chunk_gated_delta_rule_fwd_h(k, w.cpu(), u.cpu(), rgc, h0, True, 64, True,
+                                                       cu)
+    assert h.shape == rh.shape
+    assert_bf16(h, rh)
+    assert_bf16(vn, rvn)
+    assert_state(ht, rht)
+    o = ops.npu_chunk_fwd_o(_to(q), _to(k), vn, h, gc, 128 ** -0.5, 64, _to(cu))
+    ro = oracle.chunk_fwd_o(q, k, vn.cpu(), h.cpu(), rgc, 128 ** -0.5, 64, cu)
+    assert_bf16(o, ro)
+    of, _ = ops.npu_chunk_gated_delta_rule(_to(q), _to(k), _to(v), _to(g), _to(beta), None,
+                                           _to(h0), True, _to(cu))
+    assert_bf16(o, of, tol=2 * BF16_MAXABS)
+
+
+@pytest.mark.parametrize("case", golden("fused_recurrent_gated_delta_rule"), ids=lambda c: c["name"])
+def test_recurrent_golden(case):
+    a = case["args"]
+    st = a["initial_state"].clone().to(DEV)
+    idx = torch.arange(st.shape[0], dtype=torch.int32, device=DEV)
+    o, ht = ops.npu_fused_recurrent_gated_delta_rule(
+        _to(a["q"]), _to(a["k"]), _to(a["v"]), _to(a["g"]), _to(a["beta"]), a["scale"], st, True,
+        _to(a["cu_seqlens"]), idx, None, a["use_qk_l2norm_in_kernel"])
+    assert ht.data_ptr() == st.data_ptr()
+    st_ref = a["initial_state"].clone()
+    ro, _ = oracle.fused_recurrent_gated_delta_rule(a["q"], a["k"], a["v"], a["g"], a["beta"],
+                                                    a["scale"], st_ref, True, a["cu_seqlens"],
+                                                    idx.cpu(), a["use_qk_l2norm_in_kernel"])
+    assert_bf16(o, ro)
+    assert_state(st, st_ref)
+
+
+def test_recurrent_config4_inplace():
+    w = workloads.decode_config4()
+    st = w["state"].clone().to(DEV)
+    o, ht = ops.npu_fused_recurrent_gated_delta_rule(
+        _to(w["q"]), _to(w["k"]), _to(w["v"]), _to(w["g"]), _to(w["beta"]), None, st, True,
+        _to(w["cu_seqlens"]), _to(w["ssm_state_indices"]), None, True)
+    st_ref = w["state"].clone()
+    ro, _ = oracle.fused_recurrent_gated_delta_rule(w["q"], w["k"], w["v"], w["g"], w["beta"], None,
+                                                    st_ref, True, w["cu_seqlens"],
+                                                    w["ssm_state_indices"], True)
+    assert_bf16(o, ro)
+    assert_state(st, st_ref)
+
+
+def test_recurrent_slots_not_inplace_multitoken():
+    g = torch.Generator().manual_seed(5)
+    N, H, HV, D = 3, 2, 4, 128
+    lens = [2, 5, 1]
+    T = sum(lens)
+    q = torch.randn(1, T, H, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, T, H, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, T, HV, D, generator=g).to(torch.bfloat16)
+    gate = F.logsigmoid(torch.randn(1, T, HV, generator=g))
+    beta = torch.sigmoid(torch.randn(1, T, HV, generator=g))
+    pool = torch.randn(7, HV, D, D, generator=g)
+    slots = torch.tensor([5, 0, 3], dtype=torch.int32)
+    cu = torch.tensor([0, 2, 7, 8], dtype=torch.int32)
+    pool_d = pool.clone().to(DEV)
+    o, fin = ops.npu_fused_recurrent_gated_delta_rule(_to(q), _to(k), _to(v), _to(gate), _to(beta),
+                                                      0.3, pool_d, False, _to(cu), _to(slots),
+                                                      None, True)
+    assert torch.equal(pool_d.cpu(), pool)  # not in place: pool untouched
+    ro, rfin = oracle.fused_recurrent_gated_delta_rule(q, k, v, gate, beta, 0.3, pool.clone(),
+                                                       False, cu, slots, True)
+    assert_bf16(o, ro)
+    assert_state(fin, rfin)

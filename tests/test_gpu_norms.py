@@ -1,0 +1,88 @@
+"""GPU parity: layer_norm_fwd (LN / RMS / gated), gemma_rms_norm, l2norm."""
+
+import pytest
+import torch
+
+import oracle
+import torch_npu_ops_b200 as ops
+from parity import assert_bf16, assert_fp32, golden
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _to(t):
+    return None if t is None else t.to(DEV)
+
+
+@pytest.mark.parametrize("case", golden("layer_norm_fwd"), ids=lambda c: c["name"])
+def test_layer_norm_golden(case):
+    a = case["args"]
+    y = ops.layer_norm_fwd(_to(a["x"]), _to(a["weight"]), _to(a["bias"]), a["eps"], _to(a["z"]),
+                           a["group_size"], a["norm_before_gate"], a["is_rms_norm"])
+    ref, _, _ = oracle.layer_norm_fwd(a["x"], a["weight"], a["bias"], a["eps"], a["z"],
+                                      a["group_size"], a["norm_before_gate"], a["is_rms_norm"])
+    if a["x"].dtype == torch.float32:
+        assert_fp32(y, ref)
+        assert_fp32(y, case["out"]["y"])
+    else:
+        assert_bf16(y, ref)
+
+
+CASES = [  # (M, N, group, rms, bias, z, before, xdtype, wdtype)
+    (8192, 128, 128, True, False, True, True, torch.bfloat16, torch.bfloat16),  # gated RMSNorm cfg4
+    (256, 2048, 2048, False, True, False, True, torch.bfloat16, torch.bfloat16),  # LayerNorm cfg4
+    (1024, 128, 128, True, False, True, True, torch.bfloat16, torch.float32),
+    (300, 512, 128, False, True, True, False, torch.float32, torch.float32),
+    (37, 4096, 4096, True, True, False, True, torch.bfloat16, torch.float32),
+    (5, 8192, 8192, False, False, True, False, torch.float32, torch.float32),
+    (64, 96, 96, True, False, False, True, torch.float32, torch.float32),
+]
+
+
+@pytest.mark.parametrize("M,N,G,rms,bias,z,before,xdt,wdt", CASES)
+def test_layer_norm_vs_oracle(M, N, G, rms, bias, z, before, xdt, wdt):
+    g = torch.Generator().manual_seed(M * 7 + N)
+    x = torch.randn(M, N, generator=g).to(xdt)
+    w = (1 + 0.1 * torch.randn(N, generator=g)).to(wdt)
+    b = (0.1 * torch.randn(N, generator=g)).to(wdt) if bias else None
+    zz = torch.randn(M, N, generator=g).to(xdt) if z else None
+    y, mean, rstd = ops.layer_norm_fwd_with_stats(_to(x), _to(w), _to(b), 1e-6, _to(zz), G,
+                                                  before, rms)
+    ry, rmean, rrstd = oracle.layer_norm_fwd(x, w, b, 1e-6, zz, G, before, rms)
+    (assert_fp32 if xdt == torch.float32 else assert_bf16)(y, ry)
+    assert_fp32(rstd, rrstd)
+    if not rms:
+        assert_fp32(mean, rmean, tol=1e-3)
+
+
+def test_layer_norm_strided_rows():
+    x = torch.randn(64, 256, dtype=torch.bfloat16)
+    full = torch.randn(64, 512, dtype=torch.bfloat16)
+    full[:, :256] = x
+    w = torch.randn(256, dtype=torch.bfloat16)
+    y = ops.layer_norm_fwd(full.to(DEV)[:, :256], w.to(DEV), None, 1e-6, None, 128, True, True)
+    assert_bf16(y, oracle.layer_norm_fwd(x, w, None, 1e-6, None, 128, True, True)[0])
+
+
+@pytest.mark.parametrize("shape,dt", [((256, 2048), torch.bfloat16), ((4, 128, 4096), torch.float16),
+                                      ((4, 128, 4096), torch.float32), ((3, 100), torch.bfloat16)])
+def test_gemma_rms_norm(shape, dt):
+    g = torch.Generator().manual_seed(1234)
+    x = torch.randn(*shape, generator=g).to(dt)
+    gamma = (0.1 * torch.randn(shape[-1], generator=g)).to(dt)
+    rstd, y = ops.npu_gemma_rms_norm(x.to(DEV), gamma.to(DEV), 1e-6)
+    rr, ry = oracle.gemma_rms_norm(x, gamma, 1e-6)
+    assert rstd.shape == rr.shape and y.shape == x.shape
+    assert_fp32(rstd, rr)
+    (assert_fp32 if dt == torch.float32 else assert_bf16)(y, ry)
+    rstd2, y2 = ops.npu_python_extension_lib.gemma_rms_norm(x.to(DEV), gamma.to(DEV), 1e-6)
+    assert torch.equal(y2, y)
+
+
+@pytest.mark.parametrize("case", golden("l2norm"), ids=lambda c: c["name"])
+def test_l2norm_golden(case):
+    x = case["args"]["x"]
+    y = ops.npu_l2norm_last_dim(x.to(DEV), case["args"]["eps"])
+    ref = oracle.l2norm_last_dim(x, case["args"]["eps"])
+    (assert_fp32 if x.dtype == torch.float32 else assert_bf16)(y, ref)

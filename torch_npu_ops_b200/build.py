@@ -1,0 +1,116 @@
+"""Build ``libxops_b200.so`` (all sm_100a kernels + the C ABI) in-tree.
+
+``python -m torch_npu_ops_b200.build [--force] [-j N]``
+
+Each ``csrc/*.cu`` is compiled by nvcc for ``sm_100a`` into ``_build/`` and
+the objects are linked into ``torch_npu_ops_b200/libxops_b200.so``.  A file is
+rebuilt when it, or any header under ``csrc/`` or ``include/``, is newer than
+its object.  No torch headers are involved: the library is plain CUDA C++
+with an ``extern "C"`` surface.
+"""
+
+import argparse
+import concurrent.futures as cf
+import glob
+import os
+import re
+import shutil
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+BUILD = os.path.join(ROOT, "_build")
+LIB = os.path.join(PKG, "libxops_b200.so")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",
+              "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+              "-Xptxas", "-warn-spills"]
+
+
+def _nvcc():
+    for c in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
+        if c and os.path.exists(c):
+            return c
+    raise RuntimeError("nvcc not found (set NVCC or install the CUDA toolkit)")
+
+
+_INC = re.compile(r'^\s*#\s*include\s*"([^"]+)"', re.M)
+
+
+def _deps(path, seen=None):
+    """The file and every local header it includes, transitively."""
+    seen = set() if seen is None else seen
+    if path in seen:
+        return seen
+    seen.add(path)
+    with open(path) as f:
+        text = f.read()
+    for name in _INC.findall(text):
+        for d in (os.path.dirname(path), CSRC, INCLUDE):
+            cand = os.path.join(d, name)
+            if os.path.exists(cand):
+                _deps(cand, seen)
+                break
+    return seen
+
+
+def _stale(src, obj):
+    if not os.path.exists(obj):
+        return True
+    m = os.path.getmtime(obj)
+    return any(os.path.getmtime(d) > m for d in _deps(src))
+
+
+def _compile(nvcc, src, obj, verbose):
+    cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC, "-c", src, "-o", obj]
+    if verbose:
+        cmd += ["-Xptxas", "-v"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    return src, r.returncode, r.stdout + r.stderr
+
+
+def build(force=False, jobs=None, verbose=False):
+    """Compile what is stale and (re)link the shared library; returns its path."""
+    nvcc = _nvcc()
+    os.makedirs(BUILD, exist_ok=True)
+    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    todo = []
+    objs = []
+    for s in srcs:
+        o = os.path.join(BUILD, os.path.basename(s)[:-3] + ".o")
+        objs.append(o)
+        if force or _stale(s, o):
+            todo.append((s, o))
+    failed = []
+    if todo:
+        with cf.ThreadPoolExecutor(max_workers=jobs or min(len(todo), os.cpu_count() or 4)) as ex:
+            for src, rc, out in ex.map(lambda so: _compile(nvcc, so[0], so[1], verbose), todo):
+                if out.strip() and (rc != 0 or verbose):
+                    sys.stderr.write(f"--- {os.path.basename(src)}\n{out}\n")
+                if rc != 0:
+                    failed.append(src)
+    if failed:
+        raise RuntimeError("nvcc failed for: " + ", ".join(os.path.basename(f) for f in failed))
+    if todo or not os.path.exists(LIB):
+        cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("link failed:\n" + r.stdout + r.stderr)
+    return LIB
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-j", type=int, default=None)
+    ap.add_argument("-v", "--verbose", action="store_true", help="pass -Xptxas -v")
+    a = ap.parse_args()
+    print(build(a.force, a.j, a.verbose))
+
+
+if __name__ == "__main__":
+    main()

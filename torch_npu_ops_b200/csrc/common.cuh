@@ -1,0 +1,116 @@
+// Shared device helpers for the sm_100a kernels behind the xops C ABI.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "xops_b200.h"
+
+namespace xops {
+
+// ---- status plumbing (defined in capi.cu) --------------------------------
+int set_error(int status, const char* fmt, ...);
+int check_launch(const char* what);
+
+#define XOPS_REQUIRE(cond, ...)                                              \
+  do {                                                                       \
+    if (!(cond)) return ::xops::set_error(XOPS_ERR_INVALID_ARGUMENT,         \
+                                          __VA_ARGS__);                      \
+  } while (0)
+
+#define XOPS_UNSUPPORTED(cond, ...)                                          \
+  do {                                                                       \
+    if (!(cond)) return ::xops::set_error(XOPS_ERR_UNSUPPORTED, __VA_ARGS__); \
+  } while (0)
+
+// ---- scalar conversions ---------------------------------------------------
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) {
+  return __float2half_rn(v);
+}
+
+// ---- vector loads: N contiguous elements of T as fp32 ---------------------
+// Callers guarantee 16-byte alignment where N*sizeof(T) == 16.
+template <typename T, int N>
+__device__ __forceinline__ void load_vec(const T* __restrict__ p, float (&out)[N]) {
+  constexpr int BYTES = N * (int)sizeof(T);
+  if constexpr (BYTES % 16 == 0) {
+    constexpr int CH = BYTES / 16;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      uint4 raw = __ldg(reinterpret_cast<const uint4*>(p) + c);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 16 / (int)sizeof(T); ++i) out[c * (16 / sizeof(T)) + i] = to_f32<T>(e[i]);
+    }
+  } else if constexpr (BYTES % 8 == 0) {
+    constexpr int CH = BYTES / 8;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      uint2 raw = __ldg(reinterpret_cast<const uint2*>(p) + c);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 8 / (int)sizeof(T); ++i) out[c * (8 / sizeof(T)) + i] = to_f32<T>(e[i]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = to_f32<T>(p[i]);
+  }
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void store_vec(T* __restrict__ p, const float (&v)[N]) {
+  constexpr int BYTES = N * (int)sizeof(T);
+  if constexpr (BYTES % 16 == 0) {
+    constexpr int PER = 16 / (int)sizeof(T);
+#pragma unroll
+    for (int c = 0; c < BYTES / 16; ++c) {
+      uint4 raw;
+      T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < PER; ++i) e[i] = from_f32<T>(v[c * PER + i]);
+      reinterpret_cast<uint4*>(p)[c] = raw;
+    }
+  } else if constexpr (BYTES % 8 == 0) {
+    constexpr int PER = 8 / (int)sizeof(T);
+#pragma unroll
+    for (int c = 0; c < BYTES / 8; ++c) {
+      uint2 raw;
+      T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < PER; ++i) e[i] = from_f32<T>(v[c * PER + i]);
+      reinterpret_cast<uint2*>(p)[c] = raw;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) p[i] = from_f32<T>(v[i]);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + __expf(-x)); }
+
+__host__ __device__ __forceinline__ int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace xops

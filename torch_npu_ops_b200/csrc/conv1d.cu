@@ -1,0 +1,345 @@
+// Depthwise causal conv1d with SiLU: varlen prefill and decode update.
+//
+// Both are HBM-bound streaming kernels.  A thread owns VEC = 8 adjacent
+// channels (one 16-byte bf16 vector per token), so consecutive threads read
+// consecutive 16-byte pieces of a token row and every access is coalesced.
+//
+// Prefill (causal_conv1d_update_v2 with query_start_loc semantics,
+// triton_npu/triton_src/test_causal_conv1d_update_v2.py:260-339, one
+// sequence at a time): a CTA takes one tile of TILE_T consecutive tokens of
+// one sequence; each thread slides its window of width-1 previous inputs
+// down the tile in registers, so x is read once (plus width-1 halo rows per
+// tile, which hit L2) and out written once.  The history before a
+// sequence's first token comes from conv_state; the CTA that owns a
+// sequence's first tile is the only one that reads or writes that state
+// line, and it writes the final state straight from x, so no two CTAs race
+// on a state line.
+//
+// Decode (causal_conv1d_update_ref, test_causal_conv1d_update.py:1158-1210;
+// continuous-batching slot lookup and pad-slot skip as the decode kernels,
+// :783-792): per (row, channel vector) read state + x, write out + state.
+#include "common.cuh"
+
+namespace xops {
+namespace {
+
+constexpr int VEC = 8;
+constexpr int TILE_T = 64;
+constexpr int MAXW = 8;
+
+// Finds the sequence that owns flattened tile `tile` given per-sequence tile
+// counts, by a linear scan over query_start_loc done cooperatively by the
+// block (sequences are few; this is cheap next to the tile's traffic).
+__device__ __forceinline__ void locate_tile(const int32_t* __restrict__ qsl, int nseq,
+                                            int64_t tile, int* s_seq, int64_t* s_t0) {
+  if (threadIdx.x == 0) {
+    int64_t acc = 0;
+    int seq = -1;
+    int64_t t0 = 0;
+    for (int i = 0; i < nseq; ++i) {
+      const int64_t s = qsl[i], e = qsl[i + 1];
+      const int64_t n = e > s ? (e - s + TILE_T - 1) / TILE_T : 0;
+      if (tile < acc + n) {
+        seq = i;
+        t0 = s + (tile - acc) * TILE_T;
+        break;
+      }
+      acc += n;
+    }
+    *s_seq = seq;
+    *s_t0 = t0;
+  }
+  __syncthreads();
+}
+
+template <typename T, int W>
+__global__ void __launch_bounds__(256) conv1d_varlen_kernel(
+    const T* __restrict__ x, T* __restrict__ state, const T* __restrict__ weight,
+    const T* __restrict__ bias, const int32_t* __restrict__ qsl,
+    const int32_t* __restrict__ slots, T* __restrict__ out, int nseq, int64_t dim, bool silu,
+    int32_t pad_slot) {
+  __shared__ int s_seq;
+  __shared__ int64_t s_t0;
+  locate_tile(qsl, nseq, blockIdx.y, &s_seq, &s_t0);
+  const int seq = s_seq;
+  if (seq < 0) return;
+  const int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * VEC;
+  if (c0 >= dim) return;
+  const int64_t sstart = qsl[seq], send = qsl[seq + 1];
+  const int64_t t0 = s_t0;
+  const int64_t t1 = min(t0 + (int64_t)TILE_T, send);
+  const int line = slots ? slots[seq] : seq;
+  if (slots && line == pad_slot) return;
+  constexpr int H = W - 1;  // history length == state_len
+
+  float w[VEC][W], b[VEC];
+#pragma unroll
+  for (int c = 0; c < VEC; ++c) {
+#pragma unroll
+    for (int j = 0; j < W; ++j) w[c][j] = to_f32<T>(weight[(c0 + c) * W + j]);
+    b[c] = bias ? to_f32<T>(bias[c0 + c]) : 0.f;
+  }
+  // window: hist[j][c] = input at position t-H+j (j = 0 oldest)
+  float hist[H > 0 ? H : 1][VEC];
+  const bool first_tile = (t0 == sstart);
+  T* st_line = state + ((int64_t)line * dim + c0) * H;
+  float st_old[H > 0 ? H : 1][VEC];
+  if (first_tile) {
+#pragma unroll
+    for (int c = 0; c < VEC; ++c)
+#pragma unroll
+      for (int j = 0; j < H; ++j) st_old[j][c] = to_f32<T>(st_line[c * H + j]);
+#pragma unroll
+    for (int j = 0; j < H; ++j)
+#pragma unroll
+      for (int c = 0; c < VEC; ++c) hist[j][c] = st_old[j][c];
+  } else {
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      float tmp[VEC];
+      load_vec<T, VEC>(x + (t0 - H + j) * dim + c0, tmp);
+#pragma unroll
+      for (int c = 0; c < VEC; ++c) hist[j][c] = tmp[c];
+    }
+  }
+  for (int64_t t = t0; t < t1; ++t) {
+    float cur[VEC], o[VEC];
+    load_vec<T, VEC>(x + t * dim + c0, cur);
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) {
+      float acc = b[c];
+#pragma unroll
+      for (int j = 0; j < H; ++j) acc = fmaf(hist[j][c], w[c][j], acc);
+      acc = fmaf(cur[c], w[c][H], acc);
+      o[c] = silu ? silu_f(acc) : acc;
+    }
+    store_vec<T, VEC>(out + t * dim + c0, o);
+#pragma unroll
+    for (int j = 0; j + 1 < H; ++j)
+#pragma unroll
+      for (int c = 0; c < VEC; ++c) hist[j][c] = hist[j + 1][c];
+    if constexpr (H > 0) {
+#pragma unroll
+      for (int c = 0; c < VEC; ++c) hist[H - 1][c] = cur[c];
+    }
+  }
+  if (first_tile) {
+    // final state = last H entries of cat(old_state, x_seq), read from x
+    const int64_t len = send - sstart;
+    float nst[H > 0 ? H : 1][VEC];
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const int64_t pos = len - H + j;  // position in cat coords relative to seq start
+      if (pos >= 0) {
+        float tmp[VEC];
+        load_vec<T, VEC>(x + (sstart + pos) * dim + c0, tmp);
+#pragma unroll
+        for (int c = 0; c < VEC; ++c) nst[j][c] = tmp[c];
+      } else {
+#pragma unroll
+        for (int c = 0; c < VEC; ++c) nst[j][c] = st_old[H + pos][c];
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < VEC; ++c)
+#pragma unroll
+      for (int j = 0; j < H; ++j) st_line[c * H + j] = from_f32<T>(nst[j][c]);
+  }
+}
+
+// Decode: one thread per (row, channel vector); general seqlen/state_len.
+template <typename T, int W>
+__global__ void __launch_bounds__(256) conv1d_update_kernel(
+    const T* __restrict__ x, T* __restrict__ state, const T* __restrict__ weight,
+    const T* __restrict__ bias, const int32_t* __restrict__ slots, T* __restrict__ out,
+    int64_t batch, int64_t dim, int64_t seqlen, int64_t state_len, int64_t sxb, int64_t sxd,
+    int64_t sxt, bool silu, int32_t pad_slot) {
+  const int64_t nvec = dim / VEC;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= batch * nvec) return;
+  const int64_t row = gid / nvec;
+  const int64_t c0 = (gid - row * nvec) * VEC;
+  const int line = slots ? slots[row] : (int)row;
+  if (slots && line == pad_slot) return;
+  T* st = state + ((int64_t)line * dim + c0) * state_len;
+  for (int c = 0; c < VEC; ++c) {
+    const int64_t ch = c0 + c;
+    float wv[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) wv[j] = to_f32<T>(weight[ch * W + j]);
+    const float bv = bias ? to_f32<T>(bias[ch]) : 0.f;
+    T* s = st + (int64_t)c * state_len;
+    // cat = [s_0 .. s_{L-1}, x_0 .. x_{n-1}]; out_t uses cat[L + t - (W-1) .. L + t]
+    for (int64_t t = 0; t < seqlen; ++t) {
+      float acc = bv;
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const int64_t p = state_len + t - (W - 1) + j;
+        const float val = p < state_len ? to_f32<T>(s[p])
+                                        : to_f32<T>(x[row * sxb + ch * sxd + (p - state_len) * sxt]);
+        acc = fmaf(val, wv[j], acc);
+      }
+      out[(row * dim + ch) * seqlen + t] = from_f32<T>(silu ? silu_f(acc) : acc);
+    }
+    // state <- last state_len entries of cat
+    const int64_t total = state_len + seqlen;
+    for (int64_t j = 0; j < state_len; ++j) {
+      const int64_t p = total - state_len + j;
+      const float val = p < state_len ? to_f32<T>(s[p])
+                                      : to_f32<T>(x[row * sxb + ch * sxd + (p - state_len) * sxt]);
+      s[j] = from_f32<T>(val);
+    }
+  }
+}
+
+// Decode fast path (width 4, state_len 3, seqlen 1): vectorised state/x/w.
+template <typename T>
+__global__ void __launch_bounds__(256) conv1d_decode_w4_kernel(
+    const T* __restrict__ x, T* __restrict__ state, const T* __restrict__ weight,
+    const T* __restrict__ bias, const int32_t* __restrict__ slots, T* __restrict__ out,
+    int64_t batch, int64_t dim, int64_t sxb, bool silu, int32_t pad_slot) {
+  const int64_t nvec = dim / VEC;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= batch * nvec) return;
+  const int64_t row = gid / nvec;
+  const int64_t c0 = (gid - row * nvec) * VEC;
+  const int line = slots ? slots[row] : (int)row;
+  if (slots && line == pad_slot) return;
+  float xs[VEC], st[3 * VEC], w[4 * VEC], o[VEC];
+  load_vec<T, VEC>(x + row * sxb + c0, xs);
+  T* sp = state + ((int64_t)line * dim + c0) * 3;
+  load_vec<T, 3 * VEC>(sp, st);
+  load_vec<T, 4 * VEC>(weight + c0 * 4, w);
+#pragma unroll
+  for (int c = 0; c < VEC; ++c) {
+    float acc = bias ? to_f32<T>(bias[c0 + c]) : 0.f;
+    acc = fmaf(st[3 * c + 0], w[4 * c + 0], acc);
+    acc = fmaf(st[3 * c + 1], w[4 * c + 1], acc);
+    acc = fmaf(st[3 * c + 2], w[4 * c + 2], acc);
+    acc = fmaf(xs[c], w[4 * c + 3], acc);
+    o[c] = silu ? silu_f(acc) : acc;
+  }
+  store_vec<T, VEC>(out + row * dim + c0, o);
+  float ns[3 * VEC];
+#pragma unroll
+  for (int c = 0; c < VEC; ++c) {
+    ns[3 * c + 0] = st[3 * c + 1];
+    ns[3 * c + 1] = st[3 * c + 2];
+    ns[3 * c + 2] = xs[c];
+  }
+  store_vec<T, 3 * VEC>(sp, ns);
+}
+
+template <typename T>
+int launch_varlen_w(int W, const void* x, void* state, const void* w, const void* b,
+                    const int32_t* qsl, const int32_t* slots, void* out, int nseq,
+                    int64_t tiles, int64_t dim, bool silu, int32_t pad, cudaStream_t st) {
+  const int threads = 128;
+  dim3 grid((unsigned)cdiv64(dim / VEC, threads), (unsigned)tiles);
+  switch (W) {
+#define XOPS_CV(WW)                                                                           \
+  case WW:                                                                                    \
+    conv1d_varlen_kernel<T, WW><<<grid, threads, 0, st>>>((const T*)x, (T*)state, (const T*)w, \
+                                                         (const T*)b, qsl, slots, (T*)out,    \
+                                                         nseq, dim, silu, pad);               \
+    return check_launch("causal_conv1d_varlen");
+    XOPS_CV(2) XOPS_CV(3) XOPS_CV(4) XOPS_CV(5) XOPS_CV(6)
+#undef XOPS_CV
+    default:
+      return set_error(XOPS_ERR_UNSUPPORTED, "causal_conv1d_varlen: width %d not in [2, 6]", W);
+  }
+}
+
+}  // namespace
+}  // namespace xops
+
+using namespace xops;
+
+extern "C" int xops_causal_conv1d_varlen(const void* x, void* conv_state, const void* weight,
+                                         const void* bias, const int32_t* query_start_loc,
+                                         const int32_t* conv_state_indices, void* out,
+                                         int64_t batch, int64_t total_tokens, int64_t dim,
+                                         int64_t width, int64_t num_cache_lines, int silu,
+                                         int32_t pad_slot_id, int dtype, void* stream) {
+  XOPS_REQUIRE(batch >= 0 && total_tokens >= 0 && dim > 0, "causal_conv1d_varlen: bad shape");
+  XOPS_REQUIRE(width >= 2 && width <= 6, "causal_conv1d_varlen expects width in [2, 6], got %lld",
+               (long long)width);
+  XOPS_REQUIRE(dim % VEC == 0, "causal_conv1d_varlen: dim must be a multiple of %d", VEC);
+  XOPS_REQUIRE(dtype == XOPS_BF16 || dtype == XOPS_F32 || dtype == XOPS_F16,
+               "causal_conv1d_varlen: bad dtype");
+  XOPS_REQUIRE(conv_state_indices || num_cache_lines >= batch,
+               "causal_conv1d_varlen: conv_state has fewer lines than sequences");
+  if (batch == 0 || total_tokens == 0) return XOPS_OK;
+  XOPS_REQUIRE(x && conv_state && weight && query_start_loc && out,
+               "causal_conv1d_varlen: null pointer");
+  XOPS_REQUIRE(aligned16(x) && aligned16(out), "causal_conv1d_varlen: x/out must be 16-byte aligned");
+  // upper bound on tiles: sum ceil(len/TILE) <= total/TILE + batch
+  const int64_t tiles = total_tokens / TILE_T + batch;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case XOPS_BF16:
+      return launch_varlen_w<__nv_bfloat16>((int)width, x, conv_state, weight, bias,
+                                            query_start_loc, conv_state_indices, out, (int)batch,
+                                            tiles, dim, silu != 0, pad_slot_id, st);
+    case XOPS_F16:
+      return launch_varlen_w<__half>((int)width, x, conv_state, weight, bias, query_start_loc,
+                                     conv_state_indices, out, (int)batch, tiles, dim, silu != 0,
+                                     pad_slot_id, st);
+    default:
+      return launch_varlen_w<float>((int)width, x, conv_state, weight, bias, query_start_loc,
+                                    conv_state_indices, out, (int)batch, tiles, dim, silu != 0,
+                                    pad_slot_id, st);
+  }
+}
+
+extern "C" int xops_causal_conv1d_update(const void* x, void* conv_state, const void* weight,
+                                         const void* bias, const int32_t* conv_state_indices,
+                                         void* out, int64_t batch, int64_t dim, int64_t seqlen,
+                                         int64_t width, int64_t state_len,
+                                         int64_t num_cache_lines, int64_t x_stride_b,
+                                         int64_t x_stride_d, int64_t x_stride_t, int silu,
+                                         int32_t pad_slot_id, int dtype, void* stream) {
+  XOPS_REQUIRE(batch >= 0 && dim > 0 && seqlen >= 1, "causal_conv1d_update: bad shape");
+  XOPS_REQUIRE(width >= 1 && width <= MAXW, "causal_conv1d_update: width must be in [1, %d]", MAXW);
+  XOPS_REQUIRE(state_len >= width - 1, "causal_conv1d_update: state_len < width - 1");
+  XOPS_REQUIRE(dim % VEC == 0, "causal_conv1d_update: dim must be a multiple of %d", VEC);
+  XOPS_REQUIRE(dtype == XOPS_BF16 || dtype == XOPS_F32 || dtype == XOPS_F16,
+               "causal_conv1d_update: bad dtype");
+  XOPS_REQUIRE(conv_state_indices || num_cache_lines >= batch,
+               "causal_conv1d_update: conv_state has fewer lines than batch rows");
+  if (batch == 0) return XOPS_OK;
+  XOPS_REQUIRE(x && conv_state && weight && out, "causal_conv1d_update: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t n = batch * (dim / VEC);
+  const unsigned blocks = (unsigned)cdiv64(n, 256);
+  const bool fast = width == 4 && state_len == 3 && seqlen == 1 && x_stride_d == 1 &&
+                    aligned16(x) && aligned16(out) && aligned16(conv_state) &&
+                    aligned16(weight) && (x_stride_b % VEC) == 0;
+  auto run = [&](auto tag) {
+    using T = decltype(tag);
+    if (fast) {
+      conv1d_decode_w4_kernel<T><<<blocks, 256, 0, st>>>(
+          (const T*)x, (T*)conv_state, (const T*)weight, (const T*)bias, conv_state_indices,
+          (T*)out, batch, dim, x_stride_b, silu != 0, pad_slot_id);
+      return check_launch("causal_conv1d_update");
+    }
+    switch (width) {
+#define XOPS_CU(WW)                                                                             \
+  case WW:                                                                                      \
+    conv1d_update_kernel<T, WW><<<blocks, 256, 0, st>>>(                                        \
+        (const T*)x, (T*)conv_state, (const T*)weight, (const T*)bias, conv_state_indices,     \
+        (T*)out, batch, dim, seqlen, state_len, x_stride_b, x_stride_d, x_stride_t, silu != 0, \
+        pad_slot_id);                                                                           \
+    return check_launch("causal_conv1d_update");
+      XOPS_CU(1) XOPS_CU(2) XOPS_CU(3) XOPS_CU(4) XOPS_CU(5) XOPS_CU(6) XOPS_CU(7) XOPS_CU(8)
+#undef XOPS_CU
+      default:
+        return (int)XOPS_ERR_UNSUPPORTED;
+    }
+  };
+  switch (dtype) {
+    case XOPS_BF16: return run(__nv_bfloat16{});
+    case XOPS_F16: return run(__half{});
+    default: return run(float{});
+  }
+}

@@ -1,0 +1,292 @@
+// Building blocks shared by the chunked gated-delta-rule kernels: bf16
+// warp-tile MMA fragments, cp.async tile loads, the 64x64 unit-lower-
+// triangular inverse and per-chunk sequence bookkeeping.
+#pragma once
+
+#include "common.cuh"
+
+namespace xops {
+namespace gdn {
+
+constexpr int BT = 64;     // chunk length (tokens)
+constexpr int LD128 = 136;  // bf16 row stride of 128-wide smem tiles (+16 B pad)
+constexpr int LD64 = 72;    // bf16 row stride of 64-wide smem tiles
+constexpr int LDF = 65;     // fp32 row stride of 64x64 tiles
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+// D(16x8, fp32) += A(16x16, bf16 row) * B(16x8, bf16 col)
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// A fragment (rows m0..m0+15, k0..k0+15) of a row-major [m][k] tile.
+__device__ __forceinline__ void frag_a(uint32_t (&a)[4], const bf16* base, int ld, int m0, int k0,
+                                       int lane) {
+  ldsm_x4(a, base + (m0 + (lane & 15)) * ld + k0 + ((lane >> 4) << 3));
+}
+// A fragment of A = S^T where S is stored row-major [k][m].
+__device__ __forceinline__ void frag_a_t(uint32_t (&a)[4], const bf16* base, int ld, int m0,
+                                         int k0, int lane) {
+  ldsm_x4_t(a, base + (k0 + (lane & 7) + ((lane >> 4) << 3)) * ld + m0 + (((lane >> 3) & 1) << 3));
+}
+// B fragments of two n-tiles (n0..n0+15, k0..k0+15) from storage [n][k].
+__device__ __forceinline__ void frag_b_nk(uint32_t (&b)[4], const bf16* base, int ld, int n0,
+                                          int k0, int lane) {
+  ldsm_x4(b, base + (n0 + (lane & 7) + ((lane >> 4) << 3)) * ld + k0 + (((lane >> 3) & 1) << 3));
+}
+// B fragments of two n-tiles from storage [k][n].
+__device__ __forceinline__ void frag_b_kn(uint32_t (&b)[4], const bf16* base, int ld, int n0,
+                                          int k0, int lane) {
+  ldsm_x4_t(b, base + (k0 + (lane & 7) + (((lane >> 3) & 1) << 3)) * ld + n0 + ((lane >> 4) << 3));
+}
+
+// acc[NT][4] += A(16 x KD, rows m0) * B(KD x 8*NT, cols n0) ; A [m][k], B [k][n]
+template <int NT, int KD>
+__device__ __forceinline__ void warp_gemm_a_bkn(float (&acc)[NT][4], const bf16* A, int lda, int m0,
+                                                const bf16* B, int ldb, int n0, int lane) {
+#pragma unroll
+  for (int k0 = 0; k0 < KD; k0 += 16) {
+    uint32_t a[4];
+    frag_a(a, A, lda, m0, k0, lane);
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      frag_b_kn(b, B, ldb, n0 + 8 * j, k0, lane);
+      mma16816(acc[j], a, b[0], b[1]);
+      mma16816(acc[j + 1], a, b[2], b[3]);
+    }
+  }
+}
+
+// acc[NT][4] += A(16 x KD) * B with B stored [n][k]
+template <int NT, int KD>
+__device__ __forceinline__ void warp_gemm_a_bnk(float (&acc)[NT][4], const bf16* A, int lda, int m0,
+                                                const bf16* B, int ldb, int n0, int lane) {
+#pragma unroll
+  for (int k0 = 0; k0 < KD; k0 += 16) {
+    uint32_t a[4];
+    frag_a(a, A, lda, m0, k0, lane);
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      frag_b_nk(b, B, ldb, n0 + 8 * j, k0, lane);
+      mma16816(acc[j], a, b[0], b[1]);
+      mma16816(acc[j + 1], a, b[2], b[3]);
+    }
+  }
+}
+
+// acc[NT][4] += S^T(16 x KD) * B, S stored [k][m], B stored [k][n]
+template <int NT, int KD>
+__device__ __forceinline__ void warp_gemm_at_bkn(float (&acc)[NT][4], const bf16* S, int lds,
+                                                 int m0, const bf16* B, int ldb, int n0, int lane) {
+#pragma unroll
+  for (int k0 = 0; k0 < KD; k0 += 16) {
+    uint32_t a[4];
+    frag_a_t(a, S, lds, m0, k0, lane);
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      frag_b_kn(b, B, ldb, n0 + 8 * j, k0, lane);
+      mma16816(acc[j], a, b[0], b[1]);
+      mma16816(acc[j + 1], a, b[2], b[3]);
+    }
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// 16-byte async copy global -> shared; src_bytes == 0 zero-fills.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)),
+               "l"(gmem), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
+
+// Loads a [64 x 128] bf16 tile (rows t0..t0+63 with global row stride
+// `stride` elements; rows >= L are zero) into smem with row stride LD128.
+__device__ __forceinline__ void load_tile_64x128(bf16* dst, const bf16* src, int64_t stride, int L,
+                                                 int tid, int nthreads) {
+  for (int e = tid; e < 64 * 16; e += nthreads) {
+    const int r = e >> 4, c = (e & 15) << 3;
+    const bool ok = r < L;
+    cp_async16(dst + r * LD128 + c, src + (int64_t)(ok ? r : 0) * stride + c, ok ? 16 : 0);
+  }
+}
+
+// T = (I + A)^-1 for a strictly lower 64x64 A (fp32, stride LDF), by blocks:
+// 16x16 diagonal inverses (forward substitution, one thread per column),
+// then T21 = -T22 A21 T11 merges 16 -> 32 -> 64.  sM is fp32 scratch of
+// 32 x 33.  All 256 threads participate; ends with a barrier.
+__device__ __forceinline__ void tri_inverse_64(const float* __restrict__ sA, float* __restrict__ sT,
+                                               float* __restrict__ sM, int tid) {
+  for (int e = tid; e < 64 * 64; e += 256) sT[(e >> 6) * LDF + (e & 63)] = 0.f;
+  __syncthreads();
+  if (tid < 64) {
+    const int b = tid >> 4, c = tid & 15;
+    const float* Ab = sA + (16 * b) * LDF + 16 * b;
+    float x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = (i == c) ? 1.f : 0.f;
+#pragma unroll
+    for (int i = 1; i < 16; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int m = 0; m < i; ++m) s = fmaf(Ab[i * LDF + m], x[m], s);
+      if (i > c) x[i] = -s;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) sT[(16 * b + i) * LDF + 16 * b + c] = x[i];
+  }
+  __syncthreads();
+  // 16 -> 32: blocks (1,0) and (3,2)
+  for (int idx = tid; idx < 512; idx += 256) {
+    const int p = idx >> 8, e = idx & 255, rr = e >> 4, cc = e & 15;
+    const int r = 2 * p + 1, c = 2 * p;
+    float s = 0.f;
+    for (int m = cc; m < 16; ++m) s = fmaf(sA[(16 * r + rr) * LDF + 16 * c + m], sT[(16 * c + m) * LDF + 16 * c + cc], s);
+    sM[p * 256 + rr * 16 + cc] = s;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < 512; idx += 256) {
+    const int p = idx >> 8, e = idx & 255, rr = e >> 4, cc = e & 15;
+    const int r = 2 * p + 1, c = 2 * p;
+    float s = 0.f;
+    for (int m = 0; m <= rr; ++m) s = fmaf(sT[(16 * r + rr) * LDF + 16 * r + m], sM[p * 256 + m * 16 + cc], s);
+    sT[(16 * r + rr) * LDF + 16 * c + cc] = -s;
+  }
+  __syncthreads();
+  // 32 -> 64: block rows 32..63, cols 0..31
+  for (int idx = tid; idx < 1024; idx += 256) {
+    const int rr = idx >> 5, cc = idx & 31;
+    float s = 0.f;
+    for (int m = cc; m < 32; ++m) s = fmaf(sA[(32 + rr) * LDF + m], sT[m * LDF + cc], s);
+    sM[rr * 33 + cc] = s;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < 1024; idx += 256) {
+    const int rr = idx >> 5, cc = idx & 31;
+    float s = 0.f;
+    for (int m = 0; m <= rr; ++m) s = fmaf(sT[(32 + rr) * LDF + 32 + m], sM[m * 33 + cc], s);
+    sT[(32 + rr) * LDF + cc] = -s;
+  }
+  __syncthreads();
+}
+
+// Inclusive cumsum of g[0..63] (rows >= L zero) by warp 0 into sG; returns
+// nothing, sG[L-1] is the chunk's last cumulative gate.
+__device__ __forceinline__ void chunk_cumsum_warp(const float* __restrict__ graw, float* sG,
+                                                  int lane) {
+  const float a = graw[2 * lane], b = graw[2 * lane + 1];
+  float pair = a + b, incl = pair;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  const float excl = incl - pair;
+  sG[2 * lane] = excl + a;
+  sG[2 * lane + 1] = excl + a + b;
+}
+
+// (start, end) of sequence n.
+__device__ __forceinline__ void seq_span(const int32_t* cu, int64_t n, int64_t T, int64_t& bos,
+                                         int64_t& eos) {
+  if (cu) {
+    bos = cu[n];
+    eos = cu[n + 1];
+  } else {
+    bos = n * T;
+    eos = bos + T;
+  }
+}
+
+// Maps a flattened chunk slot to (sequence, chunk start).  Returns false for
+// slots past the last chunk.  One thread scans; the result is broadcast by
+// the caller through shared memory.
+__device__ __forceinline__ bool locate_chunk(const int32_t* cu, int64_t N, int64_t T, int64_t slot,
+                                             int64_t& seq, int64_t& t0, int64_t& eos,
+                                             int64_t& chunk_in_seq) {
+  if (!cu) {
+    const int64_t per = (T + BT - 1) / BT;
+    if (per == 0) return false;
+    seq = slot / per;
+    if (seq >= N) return false;
+    chunk_in_seq = slot - seq * per;
+    t0 = seq * T + chunk_in_seq * BT;
+    eos = seq * T + T;
+    return true;
+  }
+  int64_t acc = 0;
+  for (int64_t i = 0; i < N; ++i) {
+    const int64_t s = cu[i], e = cu[i + 1];
+    const int64_t nc = e > s ? (e - s + BT - 1) / BT : 0;
+    if (slot < acc + nc) {
+      seq = i;
+      chunk_in_seq = slot - acc;
+      t0 = s + chunk_in_seq * BT;
+      eos = e;
+      return true;
+    }
+    acc += nc;
+  }
+  return false;
+}
+
+// Chunk offset (number of chunks before sequence n).
+__device__ __forceinline__ int64_t chunk_offset(const int32_t* cu, int64_t n, int64_t T) {
+  if (!cu) return n * ((T + BT - 1) / BT);
+  int64_t acc = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t len = (int64_t)cu[i + 1] - cu[i];
+    acc += len > 0 ? (len + BT - 1) / BT : 0;
+  }
+  return acc;
+}
+
+// Opts a kernel into more than 48 KB of dynamic shared memory, once per
+// device (the attribute is per device; every GPU a process uses needs it).
+inline int ensure_smem_attr(const void* fn, size_t bytes, const char* what) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(XOPS_ERR_CUDA, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess)
+    return set_error(XOPS_ERR_CUDA, "%s: shared-memory attribute (%zu B): %s", what, bytes,
+                     cudaGetErrorString(e));
+  return XOPS_OK;
+}
+
+}  // namespace gdn
+}  // namespace xops

@@ -1,0 +1,471 @@
+// Row-group normalisations: layer_norm_fwd (LayerNorm / RMSNorm with bias and
+// SiLU gate), gemma_rms_norm and the last-axis L2 norm.
+//
+// All three are HBM-bound: one read of x (and z), one write of y.  A warp owns
+// one (row, group) segment and keeps it in registers (EPL elements per lane,
+// loaded as 8- or 16-byte vectors, fully coalesced across the warp); the
+// statistics are warp-shuffle reductions, so there is no shared memory and no
+// block-wide barrier.  Segments longer than 32*64 elements use a block per
+// segment with a two-pass loop over global memory.
+#include "common.cuh"
+
+namespace xops {
+namespace {
+
+// ----------------------------------------------------------------------------
+// layer_norm_fwd: grouped LN/RMS, optional bias, optional gate z.
+// Follows layer_norm_fwd_kernel (triton_npu/triton_src/test_layernorm_fwd.py:
+// 1125-1187): mean/rstd at group*M + row; gate silu(z) = z*sigmoid(z) applied
+// before the statistics (norm_before_gate == 0) or to the output (== 1).
+// ----------------------------------------------------------------------------
+template <typename TX, typename TW, int EPL, bool RMS, bool HAS_Z, bool HAS_B>
+__global__ void __launch_bounds__(256) layer_norm_warp_kernel(
+    const TX* __restrict__ x, const TW* __restrict__ w, const TW* __restrict__ b,
+    const TX* __restrict__ z, TX* __restrict__ y, float* __restrict__ mean_out,
+    float* __restrict__ rstd_out, int64_t M, int64_t ngroups, int64_t sx, int64_t sz,
+    int64_t sy, float eps, bool norm_before_gate) {
+  constexpr int G = EPL * 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t seg = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (seg >= M * ngroups) return;
+  const int64_t row = seg / ngroups;
+  const int64_t grp = seg - row * ngroups;
+  const int64_t col0 = grp * G + (int64_t)lane * EPL;
+
+  float xv[EPL], zv[EPL];
+  load_vec<TX, EPL>(x + row * sx + col0, xv);
+  if constexpr (HAS_Z) {
+    load_vec<TX, EPL>(z + row * sz + col0, zv);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) zv[i] = zv[i] * sigmoid_f(zv[i]);
+    if (!norm_before_gate) {
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) xv[i] *= zv[i];
+    }
+  }
+  float mu = 0.f;
+  if constexpr (!RMS) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) s += xv[i];
+    mu = warp_sum(s) * (1.0f / G);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const float d = xv[i] - mu;
+    ss += d * d;
+  }
+  const float var = warp_sum(ss) * (1.0f / G);
+  const float rstd = rsqrtf(var + eps);
+  if (lane == 0) {
+    rstd_out[grp * M + row] = rstd;
+    if constexpr (!RMS) mean_out[grp * M + row] = mu;
+  }
+  float wv[EPL], bv[EPL], out[EPL];
+  load_vec<TW, EPL>(w + col0, wv);
+  if constexpr (HAS_B) load_vec<TW, EPL>(b + col0, bv);
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    float t = (xv[i] - mu) * rstd * wv[i];
+    if constexpr (HAS_B) t += bv[i];
+    if constexpr (HAS_Z) {
+      if (norm_before_gate) t *= zv[i];
+    }
+    out[i] = t;
+  }
+  store_vec<TX, EPL>(y + row * sy + col0, out);
+}
+
+// Long segments: one block per (row, group), two passes over global memory.
+template <typename TX, typename TW, bool RMS, bool HAS_Z, bool HAS_B>
+__global__ void __launch_bounds__(512) layer_norm_block_kernel(
+    const TX* __restrict__ x, const TW* __restrict__ w, const TW* __restrict__ b,
+    const TX* __restrict__ z, TX* __restrict__ y, float* __restrict__ mean_out,
+    float* __restrict__ rstd_out, int64_t M, int64_t ngroups, int64_t G, int64_t sx,
+    int64_t sz, int64_t sy, float eps, bool norm_before_gate) {
+  __shared__ float red[2][32];
+  const int64_t row = blockIdx.x / ngroups;
+  const int64_t grp = blockIdx.x - row * ngroups;
+  const TX* xr = x + row * sx + grp * G;
+  const TX* zr = HAS_Z ? z + row * sz + grp * G : nullptr;
+  auto load_x = [&](int64_t c) {
+    float v = to_f32<TX>(xr[c]);
+    if constexpr (HAS_Z) {
+      if (!norm_before_gate) {
+        const float zz = to_f32<TX>(zr[c]);
+        v *= zz * sigmoid_f(zz);
+      }
+    }
+    return v;
+  };
+  float s = 0.f, ss = 0.f;
+  for (int64_t c = threadIdx.x; c < G; c += blockDim.x) {
+    const float v = load_x(c);
+    s += v;
+    ss += v * v;
+  }
+  s = warp_sum(s);
+  ss = warp_sum(ss);
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) { red[0][wid] = s; red[1][wid] = ss; }
+  __syncthreads();
+  if (wid == 0) {
+    s = lane < nw ? red[0][lane] : 0.f;
+    ss = lane < nw ? red[1][lane] : 0.f;
+    s = warp_sum(s);
+    ss = warp_sum(ss);
+    if (lane == 0) { red[0][0] = s; red[1][0] = ss; }
+  }
+  __syncthreads();
+  const float inv_g = 1.0f / (float)G;
+  const float mu = RMS ? 0.f : red[0][0] * inv_g;
+  // E[x^2] - mu^2 in fp32 is accurate for normalised activations; the
+  // reference kernels compute the same two moments.
+  const float var = fmaxf(red[1][0] * inv_g - mu * mu, 0.f);
+  const float rstd = rsqrtf(var + eps);
+  if (threadIdx.x == 0) {
+    rstd_out[grp * M + row] = rstd;
+    if constexpr (!RMS) mean_out[grp * M + row] = mu;
+  }
+  TX* yr = y + row * sy + grp * G;
+  for (int64_t c = threadIdx.x; c < G; c += blockDim.x) {
+    float t = (load_x(c) - mu) * rstd * to_f32<TW>(w[grp * G + c]);
+    if constexpr (HAS_B) t += to_f32<TW>(b[grp * G + c]);
+    if constexpr (HAS_Z) {
+      if (norm_before_gate) {
+        const float zz = to_f32<TX>(zr[c]);
+        t *= zz * sigmoid_f(zz);
+      }
+    }
+    yr[c] = from_f32<TX>(t);
+  }
+}
+
+template <typename TX, typename TW, int EPL, bool RMS, bool HAS_Z, bool HAS_B>
+int launch_ln_warp(const void* x, const void* w, const void* b, const void* z, void* y,
+                   float* mean, float* rstd, int64_t M, int64_t ng, int64_t sx, int64_t sz,
+                   int64_t sy, float eps, bool nbg, cudaStream_t st) {
+  const int64_t segs = M * ng;
+  const int64_t blocks = cdiv64(segs, 8);
+  layer_norm_warp_kernel<TX, TW, EPL, RMS, HAS_Z, HAS_B><<<(unsigned)blocks, 256, 0, st>>>(
+      (const TX*)x, (const TW*)w, (const TW*)b, (const TX*)z, (TX*)y, mean, rstd, M, ng, sx, sz,
+      sy, eps, nbg);
+  return check_launch("layer_norm_fwd");
+}
+
+template <typename TX, typename TW, bool RMS, bool HAS_Z, bool HAS_B>
+int dispatch_ln(const void* x, const void* w, const void* b, const void* z, void* y, float* mean,
+                float* rstd, int64_t M, int64_t N, int64_t G, int64_t sx, int64_t sz, int64_t sy,
+                float eps, bool nbg, cudaStream_t st) {
+  const int64_t ng = N / G;
+  // warp path: G = 32 * EPL, vector width must divide each lane's slice
+  switch (G) {
+#define XOPS_LN_CASE(EPL)                                                                   \
+  case 32 * EPL:                                                                            \
+    return launch_ln_warp<TX, TW, EPL, RMS, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, \
+                                                          sx, sz, sy, eps, nbg, st);
+    XOPS_LN_CASE(1)
+    XOPS_LN_CASE(2)
+    XOPS_LN_CASE(4)
+    XOPS_LN_CASE(8)
+    XOPS_LN_CASE(16)
+    XOPS_LN_CASE(32)
+    XOPS_LN_CASE(64)
+#undef XOPS_LN_CASE
+    default:
+      break;
+  }
+  const int threads = G >= 4096 ? 512 : 256;
+  layer_norm_block_kernel<TX, TW, RMS, HAS_Z, HAS_B><<<(unsigned)(M * ng), threads, 0, st>>>(
+      (const TX*)x, (const TW*)w, (const TW*)b, (const TX*)z, (TX*)y, mean, rstd, M, ng, G, sx,
+      sz, sy, eps, nbg);
+  return check_launch("layer_norm_fwd");
+}
+
+template <typename TX, typename TW>
+int dispatch_ln_flags(const void* x, const void* w, const void* b, const void* z, void* y,
+                      float* mean, float* rstd, int64_t M, int64_t N, int64_t G, int64_t sx,
+                      int64_t sz, int64_t sy, float eps, bool nbg, bool rms, cudaStream_t st) {
+  const bool hz = z != nullptr, hb = b != nullptr;
+#define XOPS_LN_FLAGS(R, Z, B)                                                                \
+  if (rms == R && hz == Z && hb == B)                                                         \
+    return dispatch_ln<TX, TW, R, Z, B>(x, w, b, z, y, mean, rstd, M, N, G, sx, sz, sy, eps, \
+                                        nbg, st);
+  XOPS_LN_FLAGS(true, true, true)
+  XOPS_LN_FLAGS(true, true, false)
+  XOPS_LN_FLAGS(true, false, true)
+  XOPS_LN_FLAGS(true, false, false)
+  XOPS_LN_FLAGS(false, true, true)
+  XOPS_LN_FLAGS(false, true, false)
+  XOPS_LN_FLAGS(false, false, true)
+  XOPS_LN_FLAGS(false, false, false)
+#undef XOPS_LN_FLAGS
+  return set_error(XOPS_ERR_UNSUPPORTED, "layer_norm_fwd: unreachable flag combination");
+}
+
+// ----------------------------------------------------------------------------
+// gemma_rms_norm: y = x * rsqrt(mean(x^2)+eps) * (1 + gamma); rstd per row.
+// ----------------------------------------------------------------------------
+template <typename TX, typename TW, int EPL>
+__global__ void __launch_bounds__(256) gemma_warp_kernel(const TX* __restrict__ x,
+                                                         const TW* __restrict__ gamma,
+                                                         TX* __restrict__ y,
+                                                         float* __restrict__ rstd_out,
+                                                         int64_t rows, float eps) {
+  constexpr int N = EPL * 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float xv[EPL], gv[EPL];
+  load_vec<TX, EPL>(x + row * N + lane * EPL, xv);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) ss += xv[i] * xv[i];
+  const float rstd = rsqrtf(warp_sum(ss) * (1.0f / N) + eps);
+  if (lane == 0) rstd_out[row] = rstd;
+  load_vec<TW, EPL>(gamma + lane * EPL, gv);
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) xv[i] = xv[i] * rstd * (1.0f + gv[i]);
+  store_vec<TX, EPL>(y + row * N + lane * EPL, xv);
+}
+
+template <typename TX, typename TW>
+__global__ void __launch_bounds__(512) gemma_block_kernel(const TX* __restrict__ x,
+                                                          const TW* __restrict__ gamma,
+                                                          TX* __restrict__ y,
+                                                          float* __restrict__ rstd_out,
+                                                          int64_t N, float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const TX* xr = x + row * N;
+  float ss = 0.f;
+  for (int64_t c = threadIdx.x; c < N; c += blockDim.x) {
+    const float v = to_f32<TX>(xr[c]);
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) red[wid] = ss;
+  __syncthreads();
+  if (wid == 0) {
+    ss = warp_sum(lane < nw ? red[lane] : 0.f);
+    if (lane == 0) red[0] = ss;
+  }
+  __syncthreads();
+  const float rstd = rsqrtf(red[0] / (float)N + eps);
+  if (threadIdx.x == 0) rstd_out[row] = rstd;
+  for (int64_t c = threadIdx.x; c < N; c += blockDim.x)
+    y[row * N + c] = from_f32<TX>(to_f32<TX>(xr[c]) * rstd * (1.0f + to_f32<TW>(gamma[c])));
+}
+
+template <typename TX, typename TW>
+int dispatch_gemma(const void* x, const void* g, void* y, float* rstd, int64_t rows, int64_t N,
+                   float eps, cudaStream_t st) {
+  const unsigned blocks = (unsigned)cdiv64(rows, 8);
+  switch (N) {
+#define XOPS_G_CASE(EPL)                                                                     \
+  case 32 * EPL:                                                                             \
+    gemma_warp_kernel<TX, TW, EPL><<<blocks, 256, 0, st>>>((const TX*)x, (const TW*)g, (TX*)y, \
+                                                           rstd, rows, eps);                 \
+    return check_launch("gemma_rms_norm");
+    XOPS_G_CASE(2)
+    XOPS_G_CASE(4)
+    XOPS_G_CASE(8)
+    XOPS_G_CASE(16)
+    XOPS_G_CASE(32)
+    XOPS_G_CASE(64)
+#undef XOPS_G_CASE
+    default:
+      break;
+  }
+  gemma_block_kernel<TX, TW><<<(unsigned)rows, 512, 0, st>>>((const TX*)x, (const TW*)g, (TX*)y,
+                                                             rstd, N, eps);
+  return check_launch("gemma_rms_norm");
+}
+
+// ----------------------------------------------------------------------------
+// l2norm over the last axis (l2norm_fwd_kernel2_loop semantics,
+// triton_npu/triton_src/test_l2norm.py:17-60): y = x * rsqrt(sum x^2 + eps).
+// ----------------------------------------------------------------------------
+template <typename T, int EPL>
+__global__ void __launch_bounds__(256) l2norm_warp_kernel(const T* __restrict__ x,
+                                                          T* __restrict__ y, int64_t rows,
+                                                          float eps) {
+  constexpr int N = EPL * 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float v[EPL];
+  load_vec<T, EPL>(x + row * N + lane * EPL, v);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) ss += v[i] * v[i];
+  const float r = rsqrtf(warp_sum(ss) + eps);
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) v[i] *= r;
+  store_vec<T, EPL>(y + row * N + lane * EPL, v);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) l2norm_generic_kernel(const T* __restrict__ x,
+                                                             T* __restrict__ y, int64_t rows,
+                                                             int64_t N, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float ss = 0.f;
+  for (int64_t c = lane; c < N; c += 32) {
+    const float v = to_f32<T>(x[row * N + c]);
+    ss += v * v;
+  }
+  const float r = rsqrtf(warp_sum(ss) + eps);
+  for (int64_t c = lane; c < N; c += 32) y[row * N + c] = from_f32<T>(to_f32<T>(x[row * N + c]) * r);
+}
+
+template <typename T>
+int dispatch_l2(const void* x, void* y, int64_t rows, int64_t N, float eps, cudaStream_t st) {
+  const unsigned blocks = (unsigned)cdiv64(rows, 8);
+  switch (N) {
+#define XOPS_L2_CASE(EPL)                                                                \
+  case 32 * EPL:                                                                         \
+    l2norm_warp_kernel<T, EPL><<<blocks, 256, 0, st>>>((const T*)x, (T*)y, rows, eps); \
+    return check_launch("l2norm_last_dim");
+    XOPS_L2_CASE(2)
+    XOPS_L2_CASE(4)
+    XOPS_L2_CASE(8)
+#undef XOPS_L2_CASE
+    default:
+      break;
+  }
+  l2norm_generic_kernel<T><<<blocks, 256, 0, st>>>((const T*)x, (T*)y, rows, N, eps);
+  return check_launch("l2norm_last_dim");
+}
+
+bool valid_dtype(int d) { return d == XOPS_F32 || d == XOPS_BF16 || d == XOPS_F16; }
+
+}  // namespace
+}  // namespace xops
+
+using namespace xops;
+
+extern "C" int xops_layer_norm_fwd(const void* x, const void* weight, const void* bias,
+                                   const void* z, void* y, float* mean, float* rstd, int64_t M,
+                                   int64_t N, int64_t group_size, int64_t stride_x_row,
+                                   int64_t stride_z_row, int64_t stride_y_row, float eps,
+                                   int norm_before_gate, int is_rms_norm, int x_dtype,
+                                   int w_dtype, void* stream) {
+  XOPS_REQUIRE(M >= 0 && N > 0, "layer_norm_fwd: bad shape M=%lld N=%lld", (long long)M,
+               (long long)N);
+  if (group_size <= 0) group_size = N;
+  XOPS_REQUIRE(N % group_size == 0, "layer_norm_fwd: N=%lld not divisible by group_size=%lld",
+               (long long)N, (long long)group_size);
+  XOPS_REQUIRE(valid_dtype(x_dtype) && valid_dtype(w_dtype), "layer_norm_fwd: bad dtype");
+  if (M == 0) return XOPS_OK;
+  XOPS_REQUIRE(x && weight && y && rstd, "layer_norm_fwd: null pointer");
+  XOPS_REQUIRE(is_rms_norm || mean, "layer_norm_fwd: LayerNorm needs a mean buffer");
+  XOPS_REQUIRE(stride_x_row >= N && stride_y_row >= N && (!z || stride_z_row >= N),
+               "layer_norm_fwd: row stride smaller than N");
+  // vector loads need 16-byte aligned segments when the warp path is used
+  const int xs = x_dtype == XOPS_F32 ? 4 : 2;
+  const bool aligned = aligned16(x) && aligned16(y) && (!z || aligned16(z)) && aligned16(weight) &&
+                       (!bias || aligned16(bias)) && (stride_x_row * xs) % 16 == 0 &&
+                       (stride_y_row * xs) % 16 == 0 && (!z || (stride_z_row * xs) % 16 == 0);
+  const int64_t G = aligned ? group_size : -1;  // -1 forces the scalar block path
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool nbg = norm_before_gate != 0, rms = is_rms_norm != 0;
+  auto run = [&](auto tx, auto tw) {
+    using TX = decltype(tx);
+    using TW = decltype(tw);
+    if (G < 0) {
+      // unaligned views: block kernel (scalar accesses)
+      const int64_t ng = N / group_size;
+      const bool hz = z != nullptr, hb = bias != nullptr;
+#define XOPS_LNB(R, Z, B)                                                                    \
+  if (rms == R && hz == Z && hb == B) {                                                      \
+    layer_norm_block_kernel<TX, TW, R, Z, B><<<(unsigned)(M * ng), 256, 0, st>>>(            \
+        (const TX*)x, (const TW*)weight, (const TW*)bias, (const TX*)z, (TX*)y, mean, rstd, M, \
+        ng, group_size, stride_x_row, stride_z_row, stride_y_row, eps, nbg);                 \
+    return check_launch("layer_norm_fwd");                                                   \
+  }
+      XOPS_LNB(true, true, true) XOPS_LNB(true, true, false) XOPS_LNB(true, false, true)
+      XOPS_LNB(true, false, false) XOPS_LNB(false, true, true) XOPS_LNB(false, true, false)
+      XOPS_LNB(false, false, true) XOPS_LNB(false, false, false)
+#undef XOPS_LNB
+      return (int)XOPS_ERR_UNSUPPORTED;
+    }
+    return dispatch_ln_flags<TX, TW>(x, weight, bias, z, y, mean, rstd, M, N, group_size,
+                                     stride_x_row, stride_z_row, stride_y_row, eps, nbg, rms, st);
+  };
+  auto with_w = [&](auto tx) {
+    switch (w_dtype) {
+      case XOPS_F32: return run(tx, float{});
+      case XOPS_BF16: return run(tx, __nv_bfloat16{});
+      default: return run(tx, __half{});
+    }
+  };
+  switch (x_dtype) {
+    case XOPS_F32: return with_w(float{});
+    case XOPS_BF16: return with_w(__nv_bfloat16{});
+    default: return with_w(__half{});
+  }
+}
+
+extern "C" int xops_gemma_rms_norm(const void* x, const void* gamma, void* y, float* rstd,
+                                   int64_t rows, int64_t cols, float eps, int x_dtype,
+                                   int gamma_dtype, void* stream) {
+  XOPS_REQUIRE(rows >= 0 && cols > 0, "gemma_rms_norm: bad shape");
+  XOPS_REQUIRE(valid_dtype(x_dtype) && valid_dtype(gamma_dtype), "gemma_rms_norm: bad dtype");
+  if (rows == 0) return XOPS_OK;
+  XOPS_REQUIRE(x && gamma && y && rstd, "gemma_rms_norm: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool aligned = aligned16(x) && aligned16(y) && aligned16(gamma);
+  const int64_t n = aligned ? cols : -cols;
+  auto run = [&](auto tx, auto tw) {
+    using TX = decltype(tx);
+    using TW = decltype(tw);
+    if (n < 0) {
+      gemma_block_kernel<TX, TW><<<(unsigned)rows, 512, 0, st>>>((const TX*)x, (const TW*)gamma,
+                                                                 (TX*)y, rstd, cols, eps);
+      return check_launch("gemma_rms_norm");
+    }
+    return dispatch_gemma<TX, TW>(x, gamma, y, rstd, rows, cols, eps, st);
+  };
+  auto with_w = [&](auto tx) {
+    switch (gamma_dtype) {
+      case XOPS_F32: return run(tx, float{});
+      case XOPS_BF16: return run(tx, __nv_bfloat16{});
+      default: return run(tx, __half{});
+    }
+  };
+  switch (x_dtype) {
+    case XOPS_F32: return with_w(float{});
+    case XOPS_BF16: return with_w(__nv_bfloat16{});
+    default: return with_w(__half{});
+  }
+}
+
+extern "C" int xops_l2norm_last_dim(const void* x, void* y, int64_t rows, int64_t cols, float eps,
+                                    int dtype, void* stream) {
+  XOPS_REQUIRE(rows >= 0 && cols > 0, "l2norm_last_dim: bad shape");
+  XOPS_REQUIRE(dtype == XOPS_F32 || dtype == XOPS_BF16, "l2norm_last_dim: dtype must be bf16/fp32");
+  if (rows == 0) return XOPS_OK;
+  XOPS_REQUIRE(x && y, "l2norm_last_dim: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool aligned = aligned16(x) && aligned16(y);
+  const int64_t n = aligned ? cols : 1;  // 1 never matches a vector case
+  if (dtype == XOPS_F32) {
+    if (!aligned) {
+      l2norm_generic_kernel<float><<<(unsigned)cdiv64(rows, 8), 256, 0, st>>>(
+          (const float*)x, (float*)y, rows, cols, eps);
+      return check_launch("l2norm_last_dim");
+    }
+    return dispatch_l2<float>(x, y, rows, cols, eps, st);
+  }
+  if (!aligned || n == 1) {
+    l2norm_generic_kernel<__nv_bfloat16><<<(unsigned)cdiv64(rows, 8), 256, 0, st>>>(
+        (const __nv_bfloat16*)x, (__nv_bfloat16*)y, rows, cols, eps);
+    return check_launch("l2norm_last_dim");
+  }
+  return dispatch_l2<__nv_bfloat16>(x, y, rows, cols, eps, st);
+}

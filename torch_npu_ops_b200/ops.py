@@ -1,0 +1,518 @@
+"""Host-side mirror of the reference's operator API for the GDN / norm hot
+path, on top of the C ABI (``include/xops_b200.h``).
+
+Names, argument meaning, defaults, output allocation and error behaviour
+follow ``xllm::kernel::npu`` (triton_npu/torch_api/triton_ops_api.h:29-198),
+``npu_ops`` (ascendc_npu/ascendc_ops_api.h:24-39) and the pybind schemas of
+``npu_python_extension_lib`` (npu_python_extension/op_register.cpp:52-63).
+Validation failures raise ``RuntimeError`` (what the reference's
+``TORCH_CHECK`` raises in Python).  Every op launches on the current CUDA
+stream of the input's device and never synchronises; there is no CPU path.
+"""
+
+import math
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+
+
+def _check(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _dt(t, what):
+    _check(t.dtype in _DT, f"{what}: unsupported dtype {t.dtype}")
+    return _DT[t.dtype]
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None:
+            _check(t.is_cuda, "tensors must be on a CUDA device")
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _i32(t):
+    return None if t is None else t.to(torch.int32).contiguous()
+
+
+# --------------------------------------------------------------------- norms
+def npu_l2norm_last_dim(x, eps=1e-6):
+    """``x * rsqrt(sum(x^2) + eps)`` over the last axis, bf16
+    (npu_triton_l2norm.cpp:52-108 requires bf16; fp32 is also accepted)."""
+    _cuda(x)
+    _check(x.dim() >= 1, "npu_l2norm_last_dim expects x.dim() >= 1")
+    _check(x.dtype in (torch.bfloat16, torch.float32), "x tensor must be bfloat16")
+    xc = x.contiguous()
+    y = torch.empty_like(xc)
+    cols = x.shape[-1]
+    _check(cols > 0, "npu_l2norm_last_dim expects hidden dim > 0")
+    rows = xc.numel() // cols
+    _check(rows > 0, "npu_l2norm_last_dim expects non-empty input")
+    _lib.call("xops_l2norm_last_dim", xc.data_ptr(), y.data_ptr(), rows, cols, float(eps),
+              _dt(x, "npu_l2norm_last_dim"), _stream(x))
+    return y.view(x.shape)
+
+
+def _layer_norm(x, weight, bias, eps, z, group_size, norm_before_gate, is_rms_norm):
+    _cuda(x, weight, bias, z)
+    n = x.shape[-1]
+    x2 = x.reshape(-1, n)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    gs = n if group_size is None or group_size < 0 else int(group_size)
+    _check(gs > 0 and n % gs == 0, f"layer_norm_fwd: N={n} not divisible by group_size={gs}")
+    _check(weight.shape == (n,), "layer_norm_fwd: weight must have shape (N,)")
+    if bias is not None:
+        _check(bias.shape == (n,), "layer_norm_fwd: bias must have shape (N,)")
+        _check(bias.dtype == weight.dtype, "layer_norm_fwd: bias dtype must match weight")
+    z2 = None
+    if z is not None:
+        z2 = z.reshape(-1, n)
+        if z2.stride(-1) != 1:
+            z2 = z2.contiguous()
+        _check(z2.shape == (m, n), "layer_norm_fwd: z must have the shape of x")
+        _check(z2.dtype == x.dtype, "layer_norm_fwd: z dtype must match x")
+    w = weight.contiguous()
+    b = bias.contiguous() if bias is not None else None
+    ng = n // gs
+    y = torch.empty((m, n), dtype=x.dtype, device=x.device)
+    rstd = torch.empty(ng * m, dtype=torch.float32, device=x.device)
+    mean = None if is_rms_norm else torch.empty(ng * m, dtype=torch.float32, device=x.device)
+    _lib.call("xops_layer_norm_fwd", x2.data_ptr(), w.data_ptr(), _ptr(b), _ptr(z2), y.data_ptr(),
+              _ptr(mean), rstd.data_ptr(), m, n, gs, x2.stride(0),
+              z2.stride(0) if z2 is not None else 0, y.stride(0), float(eps),
+              int(bool(norm_before_gate)), int(bool(is_rms_norm)), _dt(x, "layer_norm_fwd"),
+              _dt(w, "layer_norm_fwd"), _stream(x))
+    return y.view(x.shape), mean, rstd
+
+
+def layer_norm_fwd(x, weight, bias=None, eps=1e-6, z=None, group_size=-1, norm_before_gate=True,
+                   is_rms_norm=False):
+    """Grouped LayerNorm / RMSNorm with optional bias and SiLU gate z; returns
+    y with x's shape and dtype (npu_triton_layernorm_fwd.cpp:48-333; group
+    sizes beyond 128 take the same kernel family, with bias)."""
+    return _layer_norm(x, weight, bias, eps, z, group_size, norm_before_gate, is_rms_norm)[0]
+
+
+def layer_norm_fwd_with_stats(x, weight, bias=None, eps=1e-6, z=None, group_size=-1,
+                              norm_before_gate=True, is_rms_norm=False):
+    """``layer_norm_fwd`` that also returns the fp32 ``mean`` (None for RMS)
+    and ``rstd`` vectors, indexed ``group * M + row`` like the reference
+    kernels (test_layernorm_fwd.py:1163-1165)."""
+    return _layer_norm(x, weight, bias, eps, z, group_size, norm_before_gate, is_rms_norm)
+
+
+def npu_gemma_rms_norm(x, gamma, epsilon=1e-6):
+    """Gemma RMSNorm; returns ``(rstd, y)`` with rstd fp32 of shape
+    ``x.shape[:-gamma.dim()] + (1,)*gamma.dim()`` (ascendc_npu/gemma_rms_norm.cpp:28-57)."""
+    _cuda(x, gamma)
+    gd = gamma.dim()
+    _check(gd >= 1 and x.dim() >= gd and tuple(x.shape[x.dim() - gd:]) == tuple(gamma.shape),
+           "gemma_rms_norm: gamma must match the trailing dims of x")
+    n = gamma.numel()
+    xc = x.contiguous()
+    g = gamma.contiguous()
+    rows = xc.numel() // n if n else 0
+    y = torch.empty_like(xc)
+    lead = tuple(x.shape[: x.dim() - gd])
+    rstd = torch.empty(lead + (1,) * gd if x.dim() > gd else (1,) * x.dim(),
+                       dtype=torch.float32, device=x.device)
+    _lib.call("xops_gemma_rms_norm", xc.data_ptr(), g.data_ptr(), y.data_ptr(), rstd.data_ptr(),
+              rows, n, float(epsilon), _dt(x, "gemma_rms_norm"), _dt(g, "gemma_rms_norm"),
+              _stream(x))
+    return rstd, y
+
+
+# ---------------------------------------------------------------------- rope
+def npu_split_rmsnorm_rope(input, sin, cos, q_weight, k_weight, q_hidden_size, kv_hidden_size,
+                           head_dim, eps, q_bias=None, k_bias=None, bias=False):
+    """Split packed qkv, per-head RMSNorm on q/k, NeoX RoPE, copy v; returns
+    ``(q, k, v)`` (npu_triton_split_rmsnorm_rope.cpp:57-143).  ``sin``/``cos``
+    may be narrower than ``head_dim`` (partial rotary: the first
+    ``sin.size(1)`` dims rotate)."""
+    _check(input.dim() == 2, "split_rmsnorm_rope input must be a 2D tensor")
+    _check(sin.dim() == 2 and cos.dim() == 2, "split_rmsnorm_rope sin and cos must be 2D tensors")
+    _check(q_weight.dim() == 1 and k_weight.dim() == 1,
+           "split_rmsnorm_rope q_weight and k_weight must be 1D tensors")
+    _check(head_dim > 0 and (head_dim & (head_dim - 1)) == 0,
+           "split_rmsnorm_rope head_dim must be a power of two")
+    _check(kv_hidden_size > 0 and q_hidden_size % kv_hidden_size == 0,
+           "split_rmsnorm_rope q_hidden_size must be divisible by kv_hidden_size")
+    _check(kv_hidden_size % head_dim == 0,
+           "split_rmsnorm_rope kv_hidden_size must be divisible by head_dim")
+    _check(input.size(1) == q_hidden_size + 2 * kv_hidden_size,
+           "split_rmsnorm_rope input hidden size mismatch")
+    rd = sin.size(1)
+    _check(sin.size(0) == input.size(0) and cos.size(0) == input.size(0) and cos.size(1) == rd
+           and 0 < rd <= head_dim, "split_rmsnorm_rope sin/cos shape mismatch")
+    _check(q_weight.size(0) == head_dim and k_weight.size(0) == head_dim,
+           "split_rmsnorm_rope q/k weight shape mismatch")
+    _check(q_weight.dtype == k_weight.dtype, "split_rmsnorm_rope q/k weight dtype mismatch")
+    _check(sin.dtype == cos.dtype, "split_rmsnorm_rope sin/cos dtype mismatch")
+    _cuda(input, sin, cos, q_weight, k_weight, q_bias, k_bias)
+    t = input.size(0)
+    inp = input.contiguous()
+    s, c = sin.contiguous(), cos.contiguous()
+    qw, kw = q_weight.contiguous(), k_weight.contiguous()
+    use_b = bool(bias) and q_bias is not None and k_bias is not None
+    qb = q_bias.to(qw.dtype).contiguous() if use_b else None
+    kb = k_bias.to(qw.dtype).contiguous() if use_b else None
+    q = torch.empty((t, q_hidden_size), dtype=input.dtype, device=input.device)
+    k = torch.empty((t, kv_hidden_size), dtype=input.dtype, device=input.device)
+    v = torch.empty((t, kv_hidden_size), dtype=input.dtype, device=input.device)
+    _lib.call("xops_split_rmsnorm_rope", inp.data_ptr(), s.data_ptr(), c.data_ptr(), q.data_ptr(),
+              k.data_ptr(), v.data_ptr(), qw.data_ptr(), _ptr(qb), kw.data_ptr(), _ptr(kb), t,
+              q_hidden_size, kv_hidden_size, head_dim, rd, float(eps),
+              _dt(input, "split_rmsnorm_rope"), _dt(qw, "split_rmsnorm_rope"),
+              _dt(s, "split_rmsnorm_rope"), _stream(input))
+    return q, k, v
+
+
+# -------------------------------------------------------------------- conv1d
+def npu_causal_conv1d_update(x, conv_state, weight, activation=True, bias=None,
+                             cache_seqlens=None, conv_state_indices=None, num_accepted_tokens=None,
+                             query_start_loc=None, max_query_len=-1, intermediate_conv_window=None,
+                             pad_slot_id=-1, validate_data=False):
+    """Decode conv update (npu_triton_causal_conv1d_update.cpp:22-137).
+    x: [batch, dim] or [batch, dim, seqlen]; conv_state [lines, dim,
+    state_len] is updated IN PLACE; returns out shaped like x.  Like the
+    reference, ``query_start_loc``, ``cache_seqlens`` and
+    ``num_accepted_tokens`` are rejected here (use
+    ``npu_causal_conv1d_update_v2`` for varlen batches)."""
+    _check(query_start_loc is None,
+           "Current op does not support non-empty values for query_start_loc.")
+    _check(cache_seqlens is None and num_accepted_tokens is None,
+           "currently causal_conv1d_update don't support input cache_len and mtp scenerios.")
+    _cuda(x, conv_state, weight, bias, conv_state_indices)
+    squeeze = x.dim() == 2
+    x3 = x.unsqueeze(-1) if squeeze else x
+    _check(x3.dim() == 3 and conv_state.dim() == 3 and weight.dim() == 2,
+           "causal_conv1d_update: bad tensor ranks")
+    batch, dim, seqlen = x3.shape
+    width = weight.size(1)
+    _check(weight.size(0) == dim and conv_state.size(1) == dim, "causal_conv1d_update: dim mismatch")
+    _check(conv_state.is_contiguous(), "causal_conv1d_update: conv_state must be contiguous")
+    _check(conv_state.dtype == x.dtype and weight.dtype == x.dtype,
+           "causal_conv1d_update: x, conv_state and weight must share a dtype")
+    w = weight.contiguous()
+    b = bias.to(x.dtype).contiguous() if bias is not None else None
+    idx = _i32(conv_state_indices)
+    if idx is not None:
+        _check(idx.numel() == batch, "causal_conv1d_update: conv_state_indices batch mismatch")
+    out = torch.empty((batch, dim, seqlen), dtype=x.dtype, device=x.device)
+    _lib.call("xops_causal_conv1d_update", x3.data_ptr(), conv_state.data_ptr(), w.data_ptr(),
+              _ptr(b), _ptr(idx), out.data_ptr(), batch, dim, seqlen, width, conv_state.size(2),
+              conv_state.size(0), x3.stride(0), x3.stride(1), x3.stride(2), int(bool(activation)),
+              int(pad_slot_id), _dt(x, "causal_conv1d_update"), _stream(x))
+    return out.squeeze(-1) if squeeze else out
+
+
+def npu_causal_conv1d_update_v2(x, conv_state, weight, activation=True, bias=None,
+                                conv_state_indices=None, query_start_loc=None, max_query_len=-1,
+                                pad_slot_id=-1, block_idx_last_scheduled_token=None,
+                                initial_state_idx=None, validate_data=False,
+                                num_accepted_tokens=None):
+    """Varlen conv (npu_triton_causal_conv1d_update_v2.cpp:99-239).  With
+    ``query_start_loc`` x is [num_tokens, dim] token-major and every
+    sequence convolves over cat(conv_state history, its tokens); without it
+    x is [B, D] or [B, D, T] (each row one sequence of T tokens).
+    conv_state [lines, dim, width-1] is updated IN PLACE.  The APC
+    (``block_idx_last_scheduled_token``/``initial_state_idx``) and
+    speculative (``num_accepted_tokens``) slot tables are outside this
+    build's scope and rejected."""
+    _check(weight.dim() == 2, "causal_conv1d_update_v2 expects weight shape [dim, width].")
+    _check((block_idx_last_scheduled_token is None) == (initial_state_idx is None),
+           "causal_conv1d_update_v2 expects both APC tensors or neither.")
+    _check(block_idx_last_scheduled_token is None and num_accepted_tokens is None,
+           "causal_conv1d_update_v2: APC and speculative slot tables are not supported")
+    _check(conv_state.dim() == 3,
+           "causal_conv1d_update_v2 expects conv_state shape [num_cache_lines, dim, state_len].")
+    _cuda(x, conv_state, weight, bias, conv_state_indices, query_start_loc)
+    width = weight.size(1)
+    _check(1 <= width <= 6, f"causal_conv1d_update_v2 expects width in [1, 6], got {width}")
+    unsq = False
+    if query_start_loc is not None:
+        _check(x.dim() == 2, "causal_conv1d_update_v2 expects x to be 2D [num_tokens, dim] "
+                             "when query_start_loc is provided.")
+        qsl = _i32(query_start_loc)
+        _check(qsl.dim() == 1 and qsl.numel() >= 2,
+               "query_start_loc must be 1D with shape [batch + 1].")
+        xv = x.contiguous()
+        batch = qsl.numel() - 1
+    else:
+        unsq = x.dim() == 2
+        xw = x.unsqueeze(-1) if unsq else x
+        _check(xw.dim() == 3, "causal_conv1d_update_v2 expects x to have shape [B, D] or [B, D, T] "
+                              "when query_start_loc is not provided.")
+        batch, _, seqlen = xw.shape
+        xv = xw.transpose(1, 2).contiguous().view(batch * seqlen, xw.size(1))
+        qsl = torch.arange(0, (batch + 1) * seqlen, seqlen, dtype=torch.int32, device=x.device)
+    dim = xv.size(1)
+    _check(weight.size(0) == dim, f"weight dim mismatch. Expected {dim}, got {weight.size(0)}")
+    _check(conv_state.size(1) == dim,
+           f"conv_state dim mismatch. Expected {dim}, got {conv_state.size(1)}")
+    _check(conv_state.size(2) == width - 1,
+           "causal_conv1d_update_v2: conv_state must hold exactly width - 1 history columns")
+    _check(conv_state.is_contiguous(), "causal_conv1d_update_v2: conv_state must be contiguous")
+    _check(conv_state.dtype == xv.dtype and weight.dtype == xv.dtype,
+           "causal_conv1d_update_v2: x, conv_state and weight must share a dtype")
+    if bias is not None:
+        _check(bias.dim() == 1 and bias.size(0) == dim,
+               "bias must have shape [dim] for causal_conv1d_update_v2.")
+    b = bias.to(xv.dtype).contiguous() if bias is not None else None
+    idx = _i32(conv_state_indices)
+    if idx is not None:
+        if idx.dim() == 2:
+            idx = idx[:, 0].contiguous()
+        _check(idx.numel() == batch,
+               f"conv_state_indices batch mismatch. Expected {batch}, got {idx.numel()}")
+    out = torch.empty_like(xv)
+    if width == 1:  # no history: pointwise scale + bias
+        y = xv.float() * weight[:, 0].float() + (b.float() if b is not None else 0.0)
+        out = (torch.nn.functional.silu(y) if activation else y).to(xv.dtype)
+    else:
+        _lib.call("xops_causal_conv1d_varlen", xv.data_ptr(), conv_state.data_ptr(),
+                  weight.contiguous().data_ptr(), _ptr(b), qsl.data_ptr(), _ptr(idx),
+                  out.data_ptr(), batch, xv.size(0), dim, width, conv_state.size(0),
+                  int(bool(activation)), int(pad_slot_id), _dt(xv, "causal_conv1d_update_v2"),
+                  _stream(x))
+    if query_start_loc is not None:
+        return out
+    out = out.view(batch, -1, dim).transpose(1, 2)
+    return out.squeeze(-1) if unsq else out
+
+
+# ---------------------------------------------------------- gated delta rule
+def _seq_info(q, cu_seqlens):
+    b, t = q.shape[0], q.shape[1]
+    if cu_seqlens is None:
+        return None, b, t, b
+    _check(b == 1, "variable-length mode expects batch size B=1")
+    cu = _i32(cu_seqlens)
+    return cu, b, t, cu.numel() - 1
+
+
+def npu_fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None, initial_state=None,
+                                         inplace_final_state=True, cu_seqlens=None,
+                                         ssm_state_indices=None, num_accepted_tokens=None,
+                                         use_qk_l2norm_in_kernel=False):
+    """Token-serial gated delta rule; returns ``(o, final_state)``
+    (npu_triton_recurrent_gated_delta_rule.cpp:54-246).  ``initial_state``
+    is required; with ``inplace_final_state`` the final state is written back
+    into it (slot ``ssm_state_indices[n]`` for sequence n) and returned."""
+    _check(num_accepted_tokens is None,
+           "npu_fused_recurrent_gated_delta_rule: speculative decoding is not supported")
+    if cu_seqlens is None:
+        _check(q.shape[0] == 1, "batch size is not 1 when cu_seqlens is not provided")
+    _check(initial_state is not None,
+           "initial_state must be provided when inplace_final_state is "
+           + ("true" if inplace_final_state else "false"))
+    _cuda(q, k, v, g, beta, initial_state, cu_seqlens, ssm_state_indices)
+    _check(q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16,
+           "npu_fused_recurrent_gated_delta_rule expects q/k/v to be bfloat16")
+    _check(initial_state.dtype == torch.float32, "initial_state must be float32")
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    _check(q.shape == k.shape and v.shape[:2] == (B, T), "q/k/v shape mismatch")
+    scale = float(scale) if scale is not None else 1.0 / math.sqrt(K)
+    cu = _i32(cu_seqlens)
+    N = cu.numel() - 1 if cu is not None else B
+    gg = g.to(torch.float32).contiguous()
+    bb = beta.to(torch.float32).contiguous() if beta is not None else None
+    idx = _i32(ssm_state_indices)
+    if idx is not None:
+        if idx.dim() == 2:
+            idx = idx[:, 0].contiguous()
+        _check(idx.numel() == N, "ssm_state_indices must have one slot per sequence")
+    _check(initial_state.is_contiguous() or initial_state.stride(0) >= HV * K * V,
+           "initial_state slots must be contiguous")
+    _check(initial_state.shape[1:] == (HV, K, V), "initial_state must be [slots, HV, K, V]")
+    if inplace_final_state:
+        final = initial_state
+    else:
+        final = torch.empty((N, HV, K, V), dtype=torch.float32, device=q.device)
+    o = torch.empty((B, T, HV, V), dtype=q.dtype, device=q.device)
+    qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+    _lib.call("xops_fused_recurrent_gated_delta_rule", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+              gg.data_ptr(), _ptr(bb), o.data_ptr(), initial_state.data_ptr(), final.data_ptr(),
+              _ptr(cu), _ptr(idx),
+              B, T, N, H, HV, K, V, initial_state.stride(0), final.stride(0), scale,
+              int(bool(use_qk_l2norm_in_kernel)), _stream(q))
+    return o, final
+
+
+def _token_rows(x, B):
+    """x [B, T, H, D] as rows of tokens: heads and dims contiguous inside a
+    token, any 16-byte aligned token stride (slices of a packed projection
+    need no copy); otherwise a contiguous copy."""
+    ok = (x.stride(3) == 1 and x.stride(2) == x.shape[3] and x.stride(1) % 8 == 0
+          and (B == 1 or x.stride(0) == x.shape[1] * x.stride(1)) and x.data_ptr() % 16 == 0)
+    return x if ok else x.contiguous()
+
+
+def npu_chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None,
+                               output_final_state=False, cu_seqlens=None, head_first=False,
+                               use_qk_l2norm_in_kernel=False):
+    """Chunked gated delta rule prefill, fused into one kernel; returns
+    ``(o, final_state or None)`` (npu_triton_chunk_gated_delta_rule.cpp:556-642).
+    ``initial_state`` (bf16 or fp32) is read, never modified."""
+    _check(not head_first, "chunk_gated_delta_rule torch_api only supports head_first=false.")
+    _check(q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16,
+           "chunk_gated_delta_rule expects q/k/v to be bfloat16.")
+    if initial_state is not None:
+        _check(initial_state.dtype in (torch.bfloat16, torch.float32),
+               "chunk_gated_delta_rule expects initial_state to be bfloat16 or float32, got "
+               f"{initial_state.dtype}")
+    _cuda(q, k, v, g, beta, initial_state, cu_seqlens)
+    B, T, Hg, K = q.shape
+    H, V = v.shape[2], v.shape[3]
+    _check(q.shape == k.shape, "q and k must have the same shape.")
+    _check(H % Hg == 0, "chunk_gated_delta_rule expects num_heads_v to be divisible by "
+                        f"num_heads_qk, got {H} and {Hg}")
+    _check(beta.dim() == 3 and tuple(beta.shape) == (B, T, H), "beta must have shape [B, T, H].")
+    _check(g.dim() == 3 and tuple(g.shape) == (B, T, H), "g must have shape [B, T, H].")
+    cu, _, _, N = _seq_info(q, cu_seqlens)
+    scale_v = float(scale) if scale is not None else K ** -0.5
+    h0 = initial_state.to(torch.float32).contiguous() if initial_state is not None else None
+    if h0 is not None:
+        _check(tuple(h0.shape) == (N, H, K, V), "initial_state must have shape [N, H, K, V]")
+    o = torch.empty((B, T, H, V), dtype=v.dtype, device=v.device)
+    ht = torch.empty((N, H, K, V), dtype=torch.float32, device=v.device) if output_final_state else None
+    qc, kc, vc = _token_rows(q, B), _token_rows(k, B), _token_rows(v, B)
+    gg, bb = g.to(torch.float32).contiguous(), beta.to(torch.float32).contiguous()
+    _lib.call("xops_chunk_gated_delta_rule", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+              gg.data_ptr(), bb.data_ptr(), _ptr(h0), o.data_ptr(), _ptr(ht), _ptr(cu), B, T, N,
+              Hg, H, K, V, qc.stride(1), kc.stride(1), vc.stride(1), scale_v,
+              int(bool(use_qk_l2norm_in_kernel)), _stream(q))
+    return o, ht
+
+
+# ---- chunk pipeline sub-operators (reference decomposition, chunk.py:31-73)
+def _ncu(q_like, cu_seqlens):
+    cu, b, t, n = _seq_info(q_like, cu_seqlens)
+    return cu, b, t, n
+
+
+def npu_chunk_local_cumsum(g, chunk_size, cu_seqlens=None):
+    """Per-chunk inclusive cumsum of g [B, T, H] (fp32 out)
+    (npu_triton_chunk_gated_delta_rule.cpp:151-227)."""
+    gf = g.to(torch.float32).contiguous()
+    _check(gf.dim() == 3, "chunk_local_cumsum expects g to have shape [B, T, H].")
+    _check(chunk_size > 0 and (chunk_size & (chunk_size - 1)) == 0,
+           f"chunk_local_cumsum expects chunk_size to be a power of two, got {chunk_size}")
+    _cuda(gf, cu_seqlens)
+    cu, B, T, N = _ncu(gf, cu_seqlens)
+    out = torch.empty_like(gf)
+    _lib.call("xops_chunk_local_cumsum", gf.data_ptr(), out.data_ptr(), _ptr(cu), B, T, N,
+              gf.shape[2], chunk_size, _stream(gf))
+    return out
+
+
+def npu_chunk_scaled_dot_kkt_fwd(k, beta, g_cumsum, chunk_size, cu_seqlens=None):
+    """A [B, T, H, 64] fp32 = strict_tril(beta_i e^{g_i-g_j} k_i.k_j)
+    (npu_triton_chunk_gated_delta_rule.cpp:229-297)."""
+    _cuda(k, beta, g_cumsum, cu_seqlens)
+    _check(k.dtype == torch.bfloat16, "chunk_scaled_dot_kkt_fwd expects bf16 k")
+    B, T, Hg, K = k.shape
+    H = beta.shape[-1]
+    cu, _, _, N = _ncu(k, cu_seqlens)
+    A = torch.zeros((B, T, H, chunk_size), dtype=torch.float32, device=k.device)
+    bb = beta.to(torch.float32).contiguous()
+    gc = g_cumsum.to(torch.float32).contiguous() if g_cumsum is not None else None
+    _lib.call("xops_chunk_scaled_dot_kkt_fwd", k.contiguous().data_ptr(), bb.data_ptr(), _ptr(gc),
+              A.data_ptr(), _ptr(cu), B, T, N, Hg, H, K, chunk_size, _stream(k))
+    return A
+
+
+def npu_solve_tril(A, chunk_size, cu_seqlens=None, output_dtype=torch.bfloat16):
+    """(I + A_c)^-1 per chunk, [B, T, H, 64] in ``output_dtype``
+    (npu_triton_chunk_gated_delta_rule.cpp:299-395)."""
+    _cuda(A, cu_seqlens)
+    Af = A.to(torch.float32).contiguous()
+    B, T, H, BT = Af.shape
+    cu, _, _, N = _ncu(Af, cu_seqlens)
+    Ai = torch.zeros((B, T, H, BT), dtype=output_dtype, device=A.device)
+    _lib.call("xops_solve_tril", Af.data_ptr(), Ai.data_ptr(), _ptr(cu), B, T, N, H, chunk_size,
+              _dt(Ai, "solve_tril"), _stream(A))
+    return Ai
+
+
+def npu_recompute_w_u_fwd(k, v, beta, g_cumsum, A, cu_seqlens=None):
+    """WY transform: ``w = Ai (beta e^g k)``, ``u = Ai (beta v)`` (bf16)
+    (npu_triton_chunk_gated_delta_rule.cpp:397-475)."""
+    _cuda(k, v, beta, g_cumsum, A, cu_seqlens)
+    B, T, Hg, K = k.shape
+    H, V = v.shape[2], v.shape[3]
+    cu, _, _, N = _ncu(k, cu_seqlens)
+    w = torch.empty((B, T, H, K), dtype=k.dtype, device=k.device)
+    u = torch.empty_like(v)
+    Ac = A.contiguous()
+    _lib.call("xops_recompute_w_u_fwd", k.contiguous().data_ptr(), v.contiguous().data_ptr(),
+              beta.to(torch.float32).contiguous().data_ptr(),
+              g_cumsum.to(torch.float32).contiguous().data_ptr(), Ac.data_ptr(),
+              _dt(Ac, "recompute_w_u_fwd"), w.data_ptr(), u.data_ptr(), _ptr(cu), B, T, N, Hg, H,
+              K, V, _stream(k))
+    return w, u
+
+
+def npu_chunk_gated_delta_rule_fwd_h(k, w, u, g=None, initial_state=None,
+                                     output_final_state=False, chunk_size=64, save_new_value=True,
+                                     cu_seqlens=None, chunk_offsets=None):
+    """Chunk-state pass; returns ``(h [B, NT, H, K, V] bf16, v_new bf16 or
+    None, final_state fp32 or None)``
+    (npu_triton_chunk_gated_delta_rule.cpp:644-802)."""
+    _check(chunk_size == 64, "chunk_gated_delta_rule_fwd_h only supports chunk_size=64 in "
+                             "the current compiled binary.")
+    for t, nm in ((k, "k"), (w, "w"), (u, "u")):
+        _check(t.dtype == torch.bfloat16,
+               f"chunk_gated_delta_rule_fwd_h expects {nm} to be bfloat16, got {t.dtype}")
+    _cuda(k, w, u, g, initial_state, cu_seqlens)
+    B, T, Hg, K = k.shape
+    H, V = u.shape[2], u.shape[3]
+    cu, _, _, N = _ncu(k, cu_seqlens)
+    if cu is not None:
+        NT = int(_lib.load().xops_total_chunks(cu.cpu().numpy().ctypes.data, B, T, N, 64)) \
+            if chunk_offsets is None else int(chunk_offsets.reshape(-1)[-1].item())
+    else:
+        NT = (T + 63) // 64
+    h = torch.empty((B, NT, H, K, V), dtype=k.dtype, device=k.device)
+    v_new = torch.empty_like(u) if save_new_value else None
+    ht = torch.empty((N, H, K, V), dtype=torch.float32, device=k.device) if output_final_state else None
+    h0 = initial_state.to(torch.float32).contiguous() if initial_state is not None else None
+    gc = g.to(torch.float32).contiguous() if g is not None else None
+    _lib.call("xops_chunk_gated_delta_rule_fwd_h", k.contiguous().data_ptr(),
+              w.contiguous().data_ptr(), u.contiguous().data_ptr(), _ptr(gc), _ptr(h0),
+              h.data_ptr(), _ptr(v_new), _ptr(ht), _ptr(cu), B, T, N, Hg, H, K, V,
+              B * NT if cu is None else NT, _stream(k))
+    return h, v_new, ht
+
+
+def npu_chunk_fwd_o(q, k, v, h, g_cumsum, scale, chunk_size=64, cu_seqlens=None):
+    """``o = scale (q h e^g + tril(q k^T e^{g_i-g_j}) v)`` per chunk, bf16
+    (npu_triton_chunk_gated_delta_rule.cpp:477-554); ``v`` is v_new and
+    ``h`` the per-chunk states from ``npu_chunk_gated_delta_rule_fwd_h``."""
+    _check(chunk_size == 64, "chunk_fwd_o only supports chunk_size=64")
+    _cuda(q, k, v, h, g_cumsum, cu_seqlens)
+    B, T, Hg, K = q.shape
+    H, V = v.shape[2], v.shape[3]
+    cu, _, _, N = _ncu(q, cu_seqlens)
+    o = torch.empty_like(v)
+    gc = g_cumsum.to(torch.float32).contiguous() if g_cumsum is not None else None
+    hh = h.to(torch.bfloat16).contiguous()
+    _lib.call("xops_chunk_fwd_o", q.contiguous().data_ptr(), k.contiguous().data_ptr(),
+              v.contiguous().data_ptr(), hh.data_ptr(), _ptr(gc), o.data_ptr(), _ptr(cu), B, T, N,
+              Hg, H, K, V, hh.shape[1], float(scale), _stream(q))
+    return o
