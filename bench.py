@@ -277,15 +277,14 @@ def main():
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
+    clocks = ClockSampler(local)
+    clocks.start()
     for _ in range(a.warmup):
         step(inp)
     barrier()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(stages) + 1)]
            for _ in range(a.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
-                          else local)
-    clocks.start()
     l0 = _lib.launch_count()
     barrier()
     start.record()
@@ -294,8 +293,14 @@ def main():
     stop.record()
     barrier()
     launches = _lib.launch_count() - l0
-    clk = clocks.stop()
     elapsed = start.elapsed_time(stop)
+    # short timed regions: keep the same load running ~1 s so the sampler
+    # (100 ms period) sees the clocks under this workload
+    t_end = time.time() + max(0.0, 1.0 - elapsed / 1000.0)
+    while time.time() < t_end:
+        step(inp)
+        torch.cuda.synchronize()
+    clk = clocks.stop()
     stage_ms = {s: statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs)
                 for j, s in enumerate(stages)}
     t_local = torch.tensor([elapsed], device=dev)

@@ -46,7 +46,7 @@ def test_rope_shapes(T, qh, kvh, hd, rd, dt):
     inp = torch.randn(T, (qh + 2 * kvh) * hd, generator=g).to(dt)
     qw = (1 + 0.1 * torch.randn(hd, generator=g)).to(dt)
     kw = (1 + 0.1 * torch.randn(hd, generator=g)).to(dt)
-    sin, cos = torch.randn(T, rd, generator=g), torch.randn(T, rd, generator=g)
+    sin, cos = workloads.neox_sin_cos(torch.arange(T) * 7, rd, 1e6)
     q, k, v = ops.npu_split_rmsnorm_rope(_to(inp), _to(sin), _to(cos), _to(qw), _to(kw), qh * hd,
                                          kvh * hd, hd, 1e-6)
     rq, rk, rv = oracle.split_rmsnorm_rope(inp, sin, cos, qw, kw, qh * hd, kvh * hd, hd, 1e-6)

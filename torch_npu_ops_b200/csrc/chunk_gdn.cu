@@ -9,13 +9,15 @@
 // Per chunk (gc = in-chunk cumsum of g, D_ij = e^{gc_i - gc_j} for i >= j):
 //   A   = strict_tril(beta_i D_ij k_i.k_j)          Gram on tensor cores
 //   T   = (I + A)^-1                                 blocked inverse, fp32
-//   T'  = T diag(beta),  T'' = T diag(beta e^{gc})    folded into bf16 operands
-//   v'  = T' v - T'' k S                             (= u - w S)
+//   T'  = (T - I) diag(beta), T'' = T diag(beta e^{gc}) folded into bf16 operands
+//   v'  = beta v + T' v - T'' k S                    (= u - w S)
 //   o   = scale ((q e^{gc}) S + tril(q k^T D) v')
 //   S  <- e^{gc_last} S + k^T (v' e^{gc_last - gc}) split into bf16 hi + lo
-// Precision: beta is folded into T instead of v, so v enters the tensor core
-// exactly; the state update uses a two-term bf16 split of the scaled v' so
-// the accumulated fp32 state tracks the fp32 recurrence to ~1e-5 relative.
+// Precision: beta is folded into the off-diagonal of T instead of into v, so v
+// enters the tensor core exactly and the dominant beta_i v_i term of u stays
+// fp32; the state update uses a two-term bf16 split of the scaled v' so the
+// accumulated fp32 state tracks the fp32 recurrence to ~1e-5 relative (a
+// bf16 beta on the diagonal, or a bf16 u, costs ~2e-3).
 //
 // Tensor-core work uses warp-level mma.sync m16n8k16 (bf16 in, fp32
 // accumulate) with ldmatrix fragment loads from padded shared tiles.
@@ -150,10 +152,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_gdn_fused_kernel(
 
     // ---- (I + A)^-1 and the folded operands --------------------------------
     tri_inverse_64(sm.u1.A, sm.u3.T, sm.u2.M, tid);
+    // T' holds only the strictly lower part of T diag(beta): the unit
+    // diagonal's beta_i v_i term is added in fp32 below, so the dominant
+    // term of u never goes through a bf16 rounding of beta.
     for (int e = tid; e < BT * BT; e += NTHREADS) {
       const int i = e >> 6, j = e & 63;
       const float tv = sm.u3.T[i * LDF + j] * sm.beta[j];
-      sm.tp[i * LD64 + j] = __float2bfloat16_rn(tv);
+      sm.tp[i * LD64 + j] = __float2bfloat16_rn(i == j ? 0.f : tv);
       sm.tpp[i * LD64 + j] = __float2bfloat16_rn(tv * __expf(sm.gc[j]));
     }
     __syncthreads();
@@ -162,7 +167,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) chunk_gdn_fused_kernel(
     const int mi = warp & 3, ni = warp >> 2;
     const int m0 = 16 * mi, n0 = 64 * ni;
     float U[8][4], O[8][4];
-    zero_acc(U);
+    {
+      const float b0 = sm.beta[m0 + g8], b1 = sm.beta[m0 + g8 + 8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int r = m0 + g8, c = n0 + 8 * j + 2 * t4;
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sm.v[r * LD128 + c]));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sm.v[(r + 8) * LD128 + c]));
+        U[j][0] = b0 * a.x; U[j][1] = b0 * a.y; U[j][2] = b1 * b.x; U[j][3] = b1 * b.y;
+      }
+    }
     zero_acc(O);
     warp_gemm_a_bkn<8, 64>(U, sm.tp, LD64, m0, sm.v, LD128, n0, lane);
     {

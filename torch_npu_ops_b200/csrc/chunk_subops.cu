@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(256) recompute_wu_kernel(
       tv = to_f32<TA>(Ai[((p.t0 + i) * H + h) * BT + j]) * beta[(p.t0 + j) * H + h];
       eg = __expf(gc[(p.t0 + j) * H + h]);
     }
-    tp[i * LD64 + j] = __float2bfloat16_rn(tv);
+    tp[i * LD64 + j] = __float2bfloat16_rn(i == j ? 0.f : tv);  // diagonal added in fp32
     tpp[i * LD64 + j] = __float2bfloat16_rn(tv * eg);
   }
   cp_async_wait_all();
@@ -151,7 +151,15 @@ __global__ void __launch_bounds__(256) recompute_wu_kernel(
   const int m0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
   const int g8 = lane >> 2, t4 = lane & 3;
   float U[8][4], W[8][4];
-  zero_acc(U);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {  // u starts from Ai_ii * beta_i * v_i in fp32
+    const int r = m0 + g8, c = n0 + 8 * j + 2 * t4;
+    const float d0 = r < p.L ? to_f32<TA>(Ai[((p.t0 + r) * H + h) * BT + r]) * beta[(p.t0 + r) * H + h] : 0.f;
+    const float d1 = r + 8 < p.L ? to_f32<TA>(Ai[((p.t0 + r + 8) * H + h) * BT + r + 8]) * beta[(p.t0 + r + 8) * H + h] : 0.f;
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sv[r * LD128 + c]));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sv[(r + 8) * LD128 + c]));
+    U[j][0] = d0 * a.x; U[j][1] = d0 * a.y; U[j][2] = d1 * b.x; U[j][3] = d1 * b.y;
+  }
   zero_acc(W);
   warp_gemm_a_bkn<8, 64>(U, tp, LD64, m0, sv, LD128, n0, lane);
   warp_gemm_a_bkn<8, 64>(W, tpp, LD64, m0, sk, LD128, n0, lane);

@@ -484,8 +484,11 @@ def npu_chunk_gated_delta_rule_fwd_h(k, w, u, g=None, initial_state=None,
     H, V = u.shape[2], u.shape[3]
     cu, _, _, N = _ncu(k, cu_seqlens)
     if cu is not None:
-        NT = int(_lib.load().xops_total_chunks(cu.cpu().numpy().ctypes.data, B, T, N, 64)) \
-            if chunk_offsets is None else int(chunk_offsets.reshape(-1)[-1].item())
+        if chunk_offsets is not None:
+            NT = int(chunk_offsets.reshape(-1)[-1].item())
+        else:  # host copy of the offsets, as the reference does (cpp:77-113)
+            cu_host = cu.cpu()
+            NT = int(_lib.load().xops_total_chunks(cu_host.data_ptr(), B, T, N, 64))
     else:
         NT = (T + 63) // 64
     h = torch.empty((B, NT, H, K, V), dtype=k.dtype, device=k.device)
