@@ -226,7 +226,11 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=8192)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="for profiler runs: no clock soak, no e2e, no CPU baseline")
     a = ap.parse_args()
+    if a.profile:
+        a.no_e2e = a.no_cpu_baseline = True
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -296,7 +300,7 @@ def main():
     elapsed = start.elapsed_time(stop)
     # short timed regions: keep the same load running ~1 s so the sampler
     # (100 ms period) sees the clocks under this workload
-    t_end = time.time() + max(0.0, 1.0 - elapsed / 1000.0)
+    t_end = time.time() + (0.0 if a.profile else max(0.0, 1.0 - elapsed / 1000.0))
     while time.time() < t_end:
         step(inp)
         torch.cuda.synchronize()

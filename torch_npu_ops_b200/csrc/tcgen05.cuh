@@ -1,0 +1,186 @@
+// Thin inline-PTX layer over the sm_100a tensor-core path: TMEM allocation,
+// shared-memory matrix descriptors, tcgen05.mma (kind::f16, bf16 in / fp32
+// accumulate, one CTA), tcgen05.commit -> mbarrier, TMEM <-> register moves
+// and bounded mbarrier waits.
+//
+// Descriptor encodings follow the PTX ISA "tcgen05 matrix descriptors" and
+// "instruction descriptor" tables (the same bit layout CuTe's
+// UMMA::SmemDescriptor / UMMA::InstrDescriptor name):
+//   smem desc  [0,14) start>>4 | [16,30) LBO>>4 | [32,46) SBO>>4 |
+//              [46,48) version=1 | [49,52) base offset | [61,64) layout
+//   instr desc [4,6) D fmt (1=f32) | [7,10) A fmt (1=bf16) | [10,13) B fmt |
+//              13 negate A | 14 negate B | 15 A MN-major | 16 B MN-major |
+//              [17,23) N>>3 | [24,29) M>>4
+//
+// Operand tiles use the 128-byte swizzle (SW128): 8 rows of 128 B form a
+// 1024 B atom whose 16 B chunks are XOR-permuted by (row & 7); tiles start on
+// 1024 B boundaries.  A [rows x 128] bf16 tile is stored as two column halves
+// of [rows x 64], each rows*128 B.  The same bytes serve as a K-major operand
+// (rows = M/N, K along the row) and as an MN-major operand (rows = K).
+#pragma once
+
+#include <stdint.h>
+
+namespace xops {
+namespace tc {
+
+constexpr uint32_t SW128 = 2;  // layout type field value
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Byte offset of element (row, col) inside an SW128 bf16 tile with `rows`
+// rows and 128 columns stored as two [rows x 64] halves.
+__device__ __forceinline__ uint32_t sw128_offset(int row, int col, int rows) {
+  const int half = col >> 6, c = col & 63;
+  const int chunk = (c >> 3) ^ (row & 7);
+  return (uint32_t)(half * rows * 128 + row * 128 + chunk * 16 + (c & 7) * 2);
+}
+// Same for a 64-column tile (one half).
+__device__ __forceinline__ uint32_t sw128_offset64(int row, int col) {
+  return (uint32_t)(row * 128 + (((col >> 3) ^ (row & 7)) << 4) + (col & 7) * 2);
+}
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                              uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // version (sm_100)
+  d |= (uint64_t)SW128 << 61;
+  return d;
+}
+
+// K-major SW128 operand, K-step j (16 bf16) of a [rows x 128] tile.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int rows, int kstep) {
+  const uint32_t a = tile + (uint32_t)((kstep >> 2) * rows * 128 + (kstep & 3) * 32);
+  return smem_desc(a, 16, 1024);
+}
+// K-major SW128 operand of a [rows x 64] tile (64-wide K), K-step j.
+__device__ __forceinline__ uint64_t desc_kmajor64(uint32_t tile, int kstep) {
+  return smem_desc(tile + (uint32_t)(kstep * 32), 16, 1024);
+}
+// MN-major SW128 operand: the tile is [K rows x MN 128 cols] (two halves of
+// 64 MN elements, LBO = distance between halves), K-step j = rows 16j..16j+15.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile, int krows, int kstep) {
+  return smem_desc(tile + (uint32_t)(kstep * 16 * 128), (uint32_t)(krows * 128), 1024);
+}
+
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn,
+                                                  bool neg_b = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((neg_b ? 1u : 0u) << 14) |
+         ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A * B ; single issuing thread.
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate));
+}
+
+// Arrive on the mbarrier once every tcgen05 op issued so far by this thread
+// has completed.
+__device__ __forceinline__ void commit(uint64_t* mbar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+          smem_addr(mbar)));
+}
+
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+// Make generic-proxy smem writes visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+// ---- TMEM allocation (one warp) ---------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                   smem_addr(dst_smem)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols));
+}
+
+// ---- TMEM <-> registers: lane = this thread's row, 32 consecutive columns ---
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(
+          taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31])));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+
+// ---- mbarriers -----------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and the caller records an error and bails
+// out) if the phase never completes within `limit` polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+}  // namespace tc
+}  // namespace xops
