@@ -45,6 +45,7 @@ SIGNATURES = {
     "xops_chunk_fwd_o": [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                          _i64, _f, _p],
     "xops_total_chunks": [_p, _i64, _i64, _i64, _i64],
+    "xops_device_error_count": [],
 }
 _RESTYPES = {"xops_last_error": C.c_char_p, "xops_version": C.c_char_p,
              "xops_launch_count": C.c_uint64, "xops_total_chunks": C.c_int64}

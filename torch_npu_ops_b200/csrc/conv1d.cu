@@ -102,25 +102,35 @@ __global__ void __launch_bounds__(256) conv1d_varlen_kernel(
       for (int c = 0; c < VEC; ++c) hist[j][c] = tmp[c];
     }
   }
-  for (int64_t t = t0; t < t1; ++t) {
-    float cur[VEC], o[VEC];
-    load_vec<T, VEC>(x + t * dim + c0, cur);
+  // UNROLL token rows are loaded before any is consumed, so each thread keeps
+  // UNROLL independent 16-byte loads in flight.
+  constexpr int UNROLL = 8;
+  for (int64_t tb = t0; tb < t1; tb += UNROLL) {
+    float cur[UNROLL][VEC];
 #pragma unroll
-    for (int c = 0; c < VEC; ++c) {
-      float acc = b[c];
+    for (int u = 0; u < UNROLL; ++u)
+      if (tb + u < t1) load_vec<T, VEC>(x + (tb + u) * dim + c0, cur[u]);
 #pragma unroll
-      for (int j = 0; j < H; ++j) acc = fmaf(hist[j][c], w[c][j], acc);
-      acc = fmaf(cur[c], w[c][H], acc);
-      o[c] = silu ? silu_f(acc) : acc;
-    }
-    store_vec<T, VEC>(out + t * dim + c0, o);
+    for (int u = 0; u < UNROLL; ++u) {
+      if (tb + u >= t1) break;
+      float o[VEC];
 #pragma unroll
-    for (int j = 0; j + 1 < H; ++j)
+      for (int c = 0; c < VEC; ++c) {
+        float acc = b[c];
 #pragma unroll
-      for (int c = 0; c < VEC; ++c) hist[j][c] = hist[j + 1][c];
-    if constexpr (H > 0) {
+        for (int j = 0; j < H; ++j) acc = fmaf(hist[j][c], w[c][j], acc);
+        acc = fmaf(cur[u][c], w[c][H], acc);
+        o[c] = silu ? silu_f(acc) : acc;
+      }
+      store_vec<T, VEC>(out + (tb + u) * dim + c0, o);
 #pragma unroll
-      for (int c = 0; c < VEC; ++c) hist[H - 1][c] = cur[c];
+      for (int j = 0; j + 1 < H; ++j)
+#pragma unroll
+        for (int c = 0; c < VEC; ++c) hist[j][c] = hist[j + 1][c];
+      if constexpr (H > 0) {
+#pragma unroll
+        for (int c = 0; c < VEC; ++c) hist[H - 1][c] = cur[u][c];
+      }
     }
   }
   if (first_tile) {

@@ -77,6 +77,90 @@ __global__ void __launch_bounds__(256) layer_norm_warp_kernel(
   store_vec<TX, EPL>(y + row * sy + col0, out);
 }
 
+// Short segments (G * sizeof(TX) <= 512 B, e.g. the gated RMSNorm's 128-wide
+// groups): a lane owns one 16-byte vector, LPR = G / VEC lanes hold a
+// segment, a warp covers 32 / LPR segments per pass and UNROLL passes are
+// loaded before any is reduced, so every lane keeps 2 * UNROLL 16-byte loads
+// (x and z) in flight.  Reductions are xor-shuffles inside the LPR-lane group.
+template <typename TX, typename TW, int G, bool RMS, bool HAS_Z, bool HAS_B>
+__global__ void __launch_bounds__(256) layer_norm_packed_kernel(
+    const TX* __restrict__ x, const TW* __restrict__ w, const TW* __restrict__ b,
+    const TX* __restrict__ z, TX* __restrict__ y, float* __restrict__ mean_out,
+    float* __restrict__ rstd_out, int64_t M, int64_t ngroups, int64_t sx, int64_t sz,
+    int64_t sy, float eps, bool norm_before_gate) {
+  constexpr int VEC = 16 / (int)sizeof(TX);
+  constexpr int LPR = G / VEC;
+  static_assert(LPR >= 1 && LPR <= 32 && (LPR & (LPR - 1)) == 0, "bad packing");
+  constexpr int SPW = 32 / LPR;  // segments per warp pass
+  constexpr int UNROLL = 4;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane / LPR, li = lane % LPR;
+  const int64_t total = M * ngroups;
+  const int64_t warp_global = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t seg0 = warp_global * (SPW * UNROLL);
+  float xv[UNROLL][VEC], zv[UNROLL][VEC];
+  int64_t row[UNROLL], grp[UNROLL];
+  bool live[UNROLL];
+#pragma unroll
+  for (int u = 0; u < UNROLL; ++u) {
+    const int64_t seg = seg0 + u * SPW + sub;
+    live[u] = seg < total;
+    row[u] = live[u] ? seg / ngroups : 0;
+    grp[u] = live[u] ? seg - row[u] * ngroups : 0;
+    if (live[u]) {
+      load_vec<TX, VEC>(x + row[u] * sx + grp[u] * G + li * VEC, xv[u]);
+      if constexpr (HAS_Z) load_vec<TX, VEC>(z + row[u] * sz + grp[u] * G + li * VEC, zv[u]);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < UNROLL; ++u) {
+    if constexpr (HAS_Z) {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) zv[u][i] = zv[u][i] * sigmoid_f(zv[u][i]);
+      if (!norm_before_gate) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) xv[u][i] *= zv[u][i];
+      }
+    }
+    float mu = 0.f;
+    if constexpr (!RMS) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) s += xv[u][i];
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      mu = s * (1.0f / G);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const float d = xv[u][i] - mu;
+      ss += d * d;
+    }
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rstd = rsqrtf(ss * (1.0f / G) + eps);
+    if (!live[u]) continue;
+    if (li == 0) {
+      rstd_out[grp[u] * M + row[u]] = rstd;
+      if constexpr (!RMS) mean_out[grp[u] * M + row[u]] = mu;
+    }
+    float wv[VEC], bv[VEC], out[VEC];
+    load_vec<TW, VEC>(w + grp[u] * G + li * VEC, wv);
+    if constexpr (HAS_B) load_vec<TW, VEC>(b + grp[u] * G + li * VEC, bv);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      float t = (xv[u][i] - mu) * rstd * wv[i];
+      if constexpr (HAS_B) t += bv[i];
+      if constexpr (HAS_Z) {
+        if (norm_before_gate) t *= zv[u][i];
+      }
+      out[i] = t;
+    }
+    store_vec<TX, VEC>(y + row[u] * sy + grp[u] * G + li * VEC, out);
+  }
+}
+
 // Long segments: one block per (row, group), two passes over global memory.
 template <typename TX, typename TW, bool RMS, bool HAS_Z, bool HAS_B>
 __global__ void __launch_bounds__(512) layer_norm_block_kernel(
@@ -159,6 +243,27 @@ int dispatch_ln(const void* x, const void* w, const void* b, const void* z, void
                 float* rstd, int64_t M, int64_t N, int64_t G, int64_t sx, int64_t sz, int64_t sy,
                 float eps, bool nbg, cudaStream_t st) {
   const int64_t ng = N / G;
+  // packed path: 16-byte lanes, several short segments per warp
+  constexpr int VEC = 16 / (int)sizeof(TX);
+#define XOPS_LN_PACKED(GG)                                                                  \
+  if (G == GG && GG % VEC == 0 && GG / VEC <= 32) {                                         \
+    constexpr int SPW = 32 / (GG / VEC > 0 ? GG / VEC : 1);                                 \
+    const int64_t warps = cdiv64(M * ng, (int64_t)SPW * 4);                                 \
+    layer_norm_packed_kernel<TX, TW, GG, RMS, HAS_Z, HAS_B><<<(unsigned)cdiv64(warps, 8), 256, \
+                                                              0, st>>>(                     \
+        (const TX*)x, (const TW*)w, (const TW*)b, (const TX*)z, (TX*)y, mean, rstd, M, ng, sx, \
+        sz, sy, eps, nbg);                                                                  \
+    return check_launch("layer_norm_fwd");                                                  \
+  }
+  if constexpr (sizeof(TX) == 2) {
+    XOPS_LN_PACKED(64)
+    XOPS_LN_PACKED(128)
+    XOPS_LN_PACKED(256)
+  } else {
+    XOPS_LN_PACKED(64)
+    XOPS_LN_PACKED(128)
+  }
+#undef XOPS_LN_PACKED
   // warp path: G = 32 * EPL, vector width must divide each lane's slice
   switch (G) {
 #define XOPS_LN_CASE(EPL)                                                                   \
