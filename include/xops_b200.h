@@ -144,23 +144,32 @@ XOPS_API int xops_fused_recurrent_gated_delta_rule(const void* q, const void* k,
                                           int64_t ht_stride, float scale,
                                           int use_qk_l2norm_in_kernel, void* stream);
 
-/* Chunked gated delta rule prefill, fused (cumsum, KKT, triangular inverse,
- * WY transform, chunk-state recurrence and output pass in one kernel; no
- * intermediate touches HBM).  q, k [B, T, Hg, K], v [B, T, H, V] bf16;
- * g, beta [B, T, H] fp32; h0 [N, H, K, V] fp32 or NULL; o [B, T, H, V] bf16;
- * ht [N, H, K, V] fp32 or NULL.  cu_seqlens [N+1] int32 with B == 1, or NULL
- * with N == B.  K == V == 128, chunk 64.  q/k/v rows may be strided views
- * (e.g. slices of a packed conv output): *_token_stride is the element
- * distance between consecutive tokens (0 = contiguous), heads contiguous
- * inside a token.  Needs no workspace.  Replaces
- * npu_chunk_gated_delta_rule (triton_npu/torch_api/npu_triton_chunk_gated_delta_rule.cpp:556-642). */
+/* Chunked gated delta rule prefill on the tensor cores.  q, k [B, T, Hg, K],
+ * v [B, T, H, V] bf16; g, beta [B, T, H] fp32; h0 [N, H, K, V] fp32 or NULL;
+ * o [B, T, H, V] bf16; ht [N, H, K, V] fp32 or NULL.  cu_seqlens [N+1] int32
+ * with B == 1, or NULL with N == B.  K == V == 128, chunk 64.  q/k/v rows may
+ * be strided views (e.g. slices of a packed conv output): *_token_stride is
+ * the element distance between consecutive tokens (0 = contiguous), heads
+ * contiguous inside a token.  Two launches: a chunk-parallel preparation
+ * kernel (WY factors into `workspace`) and the chunk-serial state kernel
+ * (per-chunk states and v_new never leave the SM).  `workspace` must hold
+ * xops_chunk_gated_delta_rule_workspace_size() bytes, 16-byte aligned.
+ * Replaces npu_chunk_gated_delta_rule
+ * (triton_npu/torch_api/npu_triton_chunk_gated_delta_rule.cpp:556-642). */
 XOPS_API int xops_chunk_gated_delta_rule(const void* q, const void* k, const void* v, const float* g,
                                 const float* beta, const float* h0, void* o, float* ht,
                                 const int32_t* cu_seqlens, int64_t B, int64_t T, int64_t N,
                                 int64_t Hg, int64_t H, int64_t K, int64_t V,
                                 int64_t q_token_stride, int64_t k_token_stride,
                                 int64_t v_token_stride, float scale,
-                                int use_qk_l2norm_in_kernel, void* stream);
+                                int use_qk_l2norm_in_kernel, void* workspace,
+                                int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes xops_chunk_gated_delta_rule needs (an upper bound computed
+ * from shapes only, no device access); varlen = cu_seqlens given. */
+XOPS_API int64_t xops_chunk_gated_delta_rule_workspace_size(int64_t B, int64_t T, int64_t N,
+                                                   int64_t Hg, int64_t H, int64_t K,
+                                                   int use_qk_l2norm_in_kernel, int varlen);
 
 /* ---- chunk pipeline sub-operators (the reference's decomposition) ---- */
 /* All take the same sequence description (cu_seqlens [N+1] int32 with B == 1

@@ -59,13 +59,13 @@ def test_host_validation_layer_norm(lib):
 
 def test_host_validation_chunk_unsupported_dims(lib):
     rc, msg = _call(lib, "xops_chunk_gated_delta_rule", None, None, None, None, None, None, None,
-                    None, None, 1, 64, 1, 1, 1, 64, 64, 0, 0, 0, 0.1, 0, None)
+                    None, None, 1, 64, 1, 1, 1, 64, 64, 0, 0, 0, 0.1, 0, None, 0, None)
     assert rc == 2 and "128" in msg
 
 
 def test_host_validation_gqa(lib):
     rc, msg = _call(lib, "xops_chunk_gated_delta_rule", None, None, None, None, None, None, None,
-                    None, None, 1, 64, 1, 3, 4, 128, 128, 0, 0, 0, 0.1, 0, None)
+                    None, None, 1, 64, 1, 3, 4, 128, 128, 0, 0, 0, 0.1, 0, None, 0, None)
     assert rc == 1 and "divisible" in msg
 
 
@@ -78,9 +78,19 @@ def test_host_validation_conv_width(lib):
 def test_empty_inputs_are_noops(lib):
     # zero sequences / rows: nothing to launch, OK without touching the device
     assert lib.xops_chunk_gated_delta_rule(None, None, None, None, None, None, None, None, None,
-                                           1, 0, 1, 1, 1, 128, 128, 0, 0, 0, 0.1, 0, None) == 0
+                                           1, 0, 1, 1, 1, 128, 128, 0, 0, 0, 0.1, 0, None, 0, None) == 0
     assert lib.xops_layer_norm_fwd(None, None, None, None, None, None, None, 0, 128, 128, 128, 0,
                                    128, 1e-6, 1, 1, 1, 1, None) == 0
+
+
+def test_chunk_workspace_rules(lib):
+    assert lib.xops_chunk_gated_delta_rule_workspace_size(1, 16384, 8, 16, 32, 128, 0, 1) == \
+        (16384 // 64 + 8) * 32 * 32768
+    with_l2 = lib.xops_chunk_gated_delta_rule_workspace_size(2, 100, 2, 2, 4, 128, 1, 0)
+    assert with_l2 == 2 * 2 * 4 * 32768 + 2 * 2 * 100 * 2 * 128 * 2 + 256
+    rc, msg = _call(lib, "xops_chunk_gated_delta_rule", 16, 16, 16, 16, 16, None, 16, None, None,
+                    1, 64, 1, 1, 1, 128, 128, 0, 0, 0, 0.1, 0, None, 0, None)
+    assert rc == 4 and "workspace" in msg
 
 
 def test_total_chunks_host(lib):

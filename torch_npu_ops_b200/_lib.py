@@ -33,7 +33,8 @@ SIGNATURES = {
                                               _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f, _int,
                                               _p],
     "xops_chunk_gated_delta_rule": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
-                                    _i64, _i64, _i64, _i64, _i64, _i64, _f, _int, _p],
+                                    _i64, _i64, _i64, _i64, _i64, _i64, _f, _int, _p, _i64, _p],
+    "xops_chunk_gated_delta_rule_workspace_size": [_i64, _i64, _i64, _i64, _i64, _i64, _int, _int],
     "xops_chunk_local_cumsum": [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
     "xops_chunk_scaled_dot_kkt_fwd": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                       _i64, _p],
@@ -48,7 +49,8 @@ SIGNATURES = {
     "xops_device_error_count": [],
 }
 _RESTYPES = {"xops_last_error": C.c_char_p, "xops_version": C.c_char_p,
-             "xops_launch_count": C.c_uint64, "xops_total_chunks": C.c_int64}
+             "xops_launch_count": C.c_uint64, "xops_total_chunks": C.c_int64,
+             "xops_chunk_gated_delta_rule_workspace_size": C.c_int64}
 
 _lock = threading.Lock()
 _lib = None

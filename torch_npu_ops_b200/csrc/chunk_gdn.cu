@@ -1,0 +1,690 @@
+// Chunked gated delta rule prefill on the sm_100a tensor cores.
+//
+// Two kernels, both built on tcgen05.mma (M = 128, bf16 operands from
+// 128-byte-swizzled shared tiles, fp32 accumulators in TMEM):
+//
+// 1. chunk_prep_kernel -- fully parallel over (64-token chunk, key head).
+//    Everything of a chunk that does not depend on the recurrent state:
+//      G    = [k; q] k^T                          (one MMA, shared by the
+//                                                  value heads of the key head)
+//      A    = strict_tril(beta_i D_ij (k k^T)_ij),  D_ij = e^{gc_i - gc_j}
+//      T    = (I + A)^-1                          (blocked, fp32, CUDA cores)
+//      T'   = (T - I) diag(beta)                  -> workspace (bf16)
+//      w    = T diag(beta e^{gc}) k               (MMA)   -> workspace (bf16)
+//      Aqk  = tril(q k^T * D)                     -> workspace (bf16)
+//    per value head, where gc is the in-chunk cumsum of g.
+//
+// 2. chunk_chain_kernel -- one CTA per (sequence, value head) walks the
+//    chunks in order.  Warp-specialised: warp 0 prefetches the next chunk's
+//    tiles (k, q, v from the inputs; w, T', Aqk from the workspace) into a
+//    second stage with cp.async; warp 1 issues every MMA from one thread;
+//    warps 2-9 hold the fp32 state S^T[v][kk] in registers (64 values per
+//    thread) and run the epilogues.  Per chunk:
+//      D_u   = v^T T'^T             (issued one chunk ahead)
+//      D_u  += S^T (-w)^T           (so v_new^T = D_u + beta_i v_i, fp32)
+//      D_qh  = S^T q^T
+//      dS    = vt_hi^T k + vt_lo^T k,  vt = v_new e^{gc_last - gc} split bf16 hi+lo
+//      D_o   = e^{gc} D_qh + v_new^T Aqk^T
+//      S    <- e^{gc_last} S + dS,  o = scale * D_o
+//    The beta_i v_i diagonal term stays fp32 and the hi/lo split keeps the
+//    fp32 state within ~1e-5 of the fp32 recurrence.
+//
+// The workspace (chunks x value heads x 32 KB, plus L2-normalised q/k when
+// use_qk_l2norm_in_kernel) replaces the reference's A, Ai, w, u, h and v_new
+// intermediates (npu_triton_chunk_gated_delta_rule.cpp:556-642); per-chunk
+// states and v_new never leave the SM.
+//
+// Every wait is a bounded mbarrier poll: on timeout the CTA records an
+// error in a device flag (xops_device_error_count) and returns.
+#include "gdn_common.cuh"
+#include "tcgen05.cuh"
+
+namespace xops {
+namespace gdn {
+
+__device__ int g_tc_error = 0;
+
+namespace {
+
+constexpr uint32_t WAIT_LIMIT = 1u << 26;
+constexpr int WS_CHUNK = 32768;   // workspace bytes per (chunk, value head)
+constexpr int WS_W = 0, WS_TP = 16384, WS_AQK = 24576;
+
+__device__ __forceinline__ uint64_t kdesc(uint32_t tile, uint32_t half_stride, int kstep) {
+  return tc::smem_desc(tile + (uint32_t)((kstep >> 2) * half_stride + (kstep & 3) * 32), 16, 1024);
+}
+__device__ __forceinline__ uint64_t kdesc64(uint32_t tile, int kstep) {
+  return tc::smem_desc(tile + (uint32_t)(kstep * 32), 16, 1024);
+}
+// MN-major: tile rows = K index (16 per k-step), LBO = distance between MN halves
+__device__ __forceinline__ uint64_t mndesc(uint32_t tile, uint32_t half_stride, int kstep) {
+  return tc::smem_desc(tile + (uint32_t)(kstep * 2048), half_stride, 1024);
+}
+// 16-byte chunk c of row r of an SW128 tile (c < 8: first half)
+__device__ __forceinline__ uint32_t chunk_off(int r, int c, uint32_t half_stride) {
+  return (uint32_t)((c >> 3) * half_stride + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+__device__ __forceinline__ uint32_t elem_off(int r, int col, uint32_t half_stride) {
+  return (uint32_t)((col >> 6) * half_stride + r * 128 + ((((col & 63) >> 3) ^ (r & 7)) << 4) +
+                    (col & 7) * 2);
+}
+__device__ __forceinline__ uint32_t tm_addr(uint32_t base, int quarter, uint32_t col) {
+  return base + ((uint32_t)(quarter * 32) << 16) + col;
+}
+__device__ __forceinline__ void record_error() { atomicExch(&g_tc_error, 1); }
+
+// [64 x 128] bf16 rows (global row stride in elements) -> SW128 tile
+__device__ __forceinline__ void cp_tile128(unsigned char* dst, uint32_t half_stride,
+                                           const bf16* src, int64_t stride, int L, int t,
+                                           int nthr) {
+  for (int e = t; e < 64 * 16; e += nthr) {
+    const int r = e >> 4, c = e & 15;
+    const bool ok = r < L;
+    cp_async16(dst + chunk_off(r, c, half_stride), src + (int64_t)(ok ? r : 0) * stride + c * 8,
+               ok ? 16 : 0);
+  }
+}
+// [64 x 64] bf16 row-major (contiguous) -> SW128 64-wide tile
+__device__ __forceinline__ void cp_tile64(unsigned char* dst, const bf16* src, int t, int nthr) {
+  for (int e = t; e < 64 * 8; e += nthr) {
+    const int r = e >> 3, c = e & 7;
+    cp_async16(dst + (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)), src + r * 64 + c * 8, 16);
+  }
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(src_bytes));
+}
+
+// ============================================================================
+// q/k L2 normalisation pre-pass: x / sqrt(sum x^2 + 1e-6) per 128-wide head,
+// rounded to bf16 (npu_l2norm_last_dim, npu_triton_chunk_gated_delta_rule.cpp:608-609).
+// One warp per (token, head); reads strided token rows, writes contiguous.
+// ============================================================================
+__global__ void __launch_bounds__(256) l2norm_heads_kernel(const bf16* __restrict__ x,
+                                                           bf16* __restrict__ y, int64_t rows,
+                                                           int64_t heads, int64_t tstride) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int64_t t = r / heads, hh = r - t * heads;
+  const uint2 raw = *reinterpret_cast<const uint2*>(x + t * tstride + hh * 128 + lane * 4);
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  const float2 a = __bfloat1622float2(p[0]), b = __bfloat1622float2(p[1]);
+  const float rn = rsqrtf(warp_sum(a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y) + 1e-6f);
+  uint2 out;
+  out.x = pack_bf16(a.x * rn, a.y * rn);
+  out.y = pack_bf16(b.x * rn, b.y * rn);
+  *reinterpret_cast<uint2*>(y + r * 128 + lane * 4) = out;
+}
+
+// ============================================================================
+// Kernel 1: per-chunk preparation
+// ============================================================================
+constexpr int P_NT = 256;
+constexpr int P_OFF_KQ = 0;        // [K h0 | Q h0 | K h1 | Q h1], 8 KB each
+constexpr int P_KQ_HALF = 16384;
+constexpr int P_OFF_Q = 8192;
+constexpr int P_OFF_TPP = 32768;   // T'' [64 x 64] SW128
+constexpr int P_OFF_FA = 40960;    // fp32 A [64 x LDF]
+constexpr int P_OFF_FT = P_OFF_FA + 64 * LDF * 4;
+constexpr int P_OFF_FM = P_OFF_FT + 64 * LDF * 4;
+constexpr int P_OFF_G = P_OFF_FM + 32 * 33 * 4;
+constexpr int P_SMEM = P_OFF_G + 3 * 64 * 4 + 1024;
+constexpr uint32_t P_TM_G = 0, P_TM_W = 64, P_TM_COLS = 128;
+
+__global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
+    const float* __restrict__ beta, unsigned char* __restrict__ ws,
+    const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H,
+    int64_t q_stride, int64_t k_stride) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_sh;
+  __shared__ int64_t pos[4];
+  __shared__ int ok_sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int quarter = warp & 3, colhalf = warp >> 2;
+  const int hk = blockIdx.y;
+  if (tid == 0) {
+    int64_t seq = 0, t0 = 0, eos = 0, cis = 0;
+    const bool ok = locate_chunk(cu, N, T, blockIdx.x, seq, t0, eos, cis);
+    pos[0] = ok ? chunk_offset(cu, seq, T) + cis : -1;
+    pos[1] = t0;
+    pos[2] = eos;
+    ok_sh = ok ? 1 : 0;
+  }
+  __syncthreads();
+  if (!ok_sh) return;
+  const int64_t gci = pos[0], t0 = pos[1];
+  const int L = (int)((pos[2] - t0) < BT ? (pos[2] - t0) : BT);
+  float* graw = reinterpret_cast<float*>(sm + P_OFF_G);
+  float* gcs = graw + 64;
+  float* bet = gcs + 64;
+  const uint32_t sb = tc::smem_addr(sm);
+
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_sh, P_TM_COLS);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::mbar_fence_init();
+  }
+  cp_tile128(sm + P_OFF_KQ, P_KQ_HALF, k + t0 * k_stride + (int64_t)hk * 128, k_stride, L, tid, P_NT);
+  cp_tile128(sm + P_OFF_Q, P_KQ_HALF, q + t0 * q_stride + (int64_t)hk * 128, q_stride, L, tid, P_NT);
+  cp_async_commit();
+  cp_async_wait_all();
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tm = tmem_sh;
+  uint32_t phase = 0;
+  bool alive = true;
+  if (tid == 0) {
+    const uint32_t id = tc::idesc_bf16(128, 64, false, false);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      tc::mma_bf16(tm + P_TM_G, kdesc(sb + P_OFF_KQ, P_KQ_HALF, j), kdesc(sb + P_OFF_KQ, P_KQ_HALF, j),
+                   id, j > 0);
+    tc::commit(&bar);
+  }
+  auto wait_mma = [&]() {
+    const bool ok = tc::mbar_wait(&bar, phase, WAIT_LIMIT);
+    phase ^= 1u;
+    if (!ok) {
+      record_error();
+      atomicExch(&ok_sh, 0);
+    }
+    tc::fence_after();
+    __syncthreads();
+    alive = ok_sh != 0;
+  };
+  wait_mma();
+
+  const int grp = (int)(H / Hg);
+  for (int hv = hk * grp; alive && hv < (hk + 1) * grp; ++hv) {
+    unsigned char* wsb = ws + (gci * H + hv) * (int64_t)WS_CHUNK;
+    if (tid < 64) {
+      graw[tid] = tid < L ? g[(t0 + tid) * H + hv] : 0.f;
+      bet[tid] = tid < L ? beta[(t0 + tid) * H + hv] : 0.f;
+    }
+    __syncthreads();
+    if (warp == 0) chunk_cumsum_warp(graw, gcs, lane);
+    __syncthreads();
+    // Gram epilogue
+    {
+      const int row = quarter * 32 + lane;
+      const int c0 = colhalf * 32;
+      float vals[32];
+      tc::tmem_ld32(tm_addr(tm, quarter, P_TM_G + c0), vals);
+      tc::tmem_wait_ld();
+      if (row < 64) {
+        float* fa = reinterpret_cast<float*>(sm + P_OFF_FA);
+        const float bi = bet[row], gi = gcs[row];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int j = c0 + c;
+          fa[row * LDF + j] = (j < row) ? vals[c] * bi * __expf(fminf(gi - gcs[j], 0.f)) : 0.f;
+        }
+      } else {
+        const int i = row - 64;
+        const float gi = gcs[i];
+        bf16* aq = reinterpret_cast<bf16*>(wsb + WS_AQK) + i * 64 + c0;
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          float e[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int j = c0 + c + u;
+            e[u] = (j <= i) ? vals[c + u] * __expf(fminf(gi - gcs[j], 0.f)) : 0.f;
+          }
+          uint4 pk;
+          pk.x = pack_bf16(e[0], e[1]); pk.y = pack_bf16(e[2], e[3]);
+          pk.z = pack_bf16(e[4], e[5]); pk.w = pack_bf16(e[6], e[7]);
+          *reinterpret_cast<uint4*>(aq + c) = pk;
+        }
+      }
+    }
+    __syncthreads();
+    {
+      float* fa = reinterpret_cast<float*>(sm + P_OFF_FA);
+      float* ft = reinterpret_cast<float*>(sm + P_OFF_FT);
+      float* fm = reinterpret_cast<float*>(sm + P_OFF_FM);
+      tri_inverse_64(fa, ft, fm, tid);
+      bf16* tpg = reinterpret_cast<bf16*>(wsb + WS_TP);
+      for (int e = tid; e < 64 * 8; e += P_NT) {
+        const int i = e >> 3, cc = e & 7;
+        float tp[8], tpp[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = cc * 8 + u;
+          const float tv = ft[i * LDF + j] * bet[j];
+          tp[u] = (i == j) ? 0.f : tv;
+          tpp[u] = tv * __expf(gcs[j]);
+        }
+        uint4 a, b;
+        a.x = pack_bf16(tp[0], tp[1]); a.y = pack_bf16(tp[2], tp[3]);
+        a.z = pack_bf16(tp[4], tp[5]); a.w = pack_bf16(tp[6], tp[7]);
+        b.x = pack_bf16(tpp[0], tpp[1]); b.y = pack_bf16(tpp[2], tpp[3]);
+        b.z = pack_bf16(tpp[4], tpp[5]); b.w = pack_bf16(tpp[6], tpp[7]);
+        *reinterpret_cast<uint4*>(tpg + i * 64 + cc * 8) = a;
+        *reinterpret_cast<uint4*>(sm + P_OFF_TPP + (uint32_t)(i * 128 + ((cc ^ (i & 7)) << 4))) = b;
+      }
+    }
+    tc::fence_proxy_async();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (tid == 0) {
+      const uint32_t id = tc::idesc_bf16(128, 64, true, false);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        tc::mma_bf16(tm + P_TM_W, mndesc(sb + P_OFF_KQ, P_KQ_HALF, j), kdesc64(sb + P_OFF_TPP, j), id,
+                     j > 0);
+      tc::commit(&bar);
+    }
+    wait_mma();
+    if (!alive) break;
+    {  // w [t][kk] (bf16, row-major) from w^T in TMEM (lane = kk)
+      const int kk = quarter * 32 + lane;
+      const int c0 = colhalf * 32;
+      float vals[32];
+      tc::tmem_ld32(tm_addr(tm, quarter, P_TM_W + c0), vals);
+      tc::tmem_wait_ld();
+      bf16* wg = reinterpret_cast<bf16*>(wsb + WS_W);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) wg[(c0 + c) * 128 + kk] = __float2bfloat16_rn(vals[c]);
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tm, P_TM_COLS);
+}
+
+// ============================================================================
+// Kernel 2: the chunk chain
+// ============================================================================
+constexpr int C_NT = 320;                 // 10 warps: producer, MMA, 8 epilogue
+constexpr int STAGE = 81920;              // bytes per pipeline stage
+constexpr int S_K = 0, S_Q = 16384, S_V = 32768, S_W = 49152, S_TP = 65536, S_AQK = 73728;
+constexpr int C_OFF_HT = 2 * STAGE;       // S^T bf16 [128 x 128], halves 16 KB apart
+constexpr int C_OFF_VTH = C_OFF_HT;       // aliases HT (disjoint lifetimes)
+constexpr int C_OFF_VTL = C_OFF_HT + 16384;
+constexpr int C_OFF_VN = C_OFF_HT + 32768;
+constexpr int C_OFF_GB = C_OFF_VN + 16384;  // per stage: g[64], beta[64] ; then gc[2][64]
+constexpr int C_SMEM = C_OFF_GB + 2 * 512 + 2 * 256 + 1024;
+constexpr uint32_t C_TM_U = 0, C_TM_QH = 64, C_TM_O = 128, C_TM_DS = 256, C_TM_COLS = 512;
+
+__global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
+    const float* __restrict__ g, const float* __restrict__ beta, const float* __restrict__ h0,
+    const unsigned char* __restrict__ ws, bf16* __restrict__ o, float* __restrict__ ht,
+    const int32_t* __restrict__ cu, int64_t T, int64_t Hg, int64_t H, int64_t q_stride,
+    int64_t k_stride, int64_t v_stride, float scale) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  __shared__ uint64_t full[2], empty[2], bar_ht, bar_vq, bar_vt, bar_so;
+  __shared__ uint32_t tmem_sh;
+  __shared__ int abort_sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t n = blockIdx.x / H;
+  const int h = (int)(blockIdx.x - n * H);
+  const int hk = (int)(h / (H / Hg));
+  int64_t bos, eos;
+  seq_span(cu, n, T, bos, eos);
+  const int NC = (int)((eos - bos + BT - 1) / BT);
+  const int64_t boh = chunk_offset(cu, n, T);
+  const uint32_t sb = tc::smem_addr(sm);
+  constexpr int K = 128, V = 128;
+
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_sh, C_TM_COLS);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    tc::mbar_init(&bar_ht, 1);
+    tc::mbar_init(&bar_vq, 1);
+    tc::mbar_init(&bar_vt, 1);
+    tc::mbar_init(&bar_so, 1);
+    tc::mbar_fence_init();
+    abort_sh = 0;
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tm = tmem_sh;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    for (int c = 0; c < NC; ++c) {
+      const int s = c & 1;
+      if (c >= 2 && !tc::mbar_wait(&empty[s], ((c - 2) >> 1) & 1, WAIT_LIMIT)) {
+        record_error();
+        atomicExch(&abort_sh, 1);
+      }
+      if (*(volatile int*)&abort_sh) break;
+      const int64_t t0 = bos + (int64_t)c * BT;
+      const int L = (int)((eos - t0) < BT ? (eos - t0) : BT);
+      unsigned char* st = sm + s * STAGE;
+      const unsigned char* wsb = ws + ((boh + c) * H + h) * (int64_t)WS_CHUNK;
+      cp_tile128(st + S_K, 8192, k + t0 * k_stride + (int64_t)hk * K, k_stride, L, lane, 32);
+      cp_tile128(st + S_Q, 8192, q + t0 * q_stride + (int64_t)hk * K, q_stride, L, lane, 32);
+      cp_tile128(st + S_V, 8192, v + t0 * v_stride + (int64_t)h * V, v_stride, L, lane, 32);
+      cp_tile128(st + S_W, 8192, reinterpret_cast<const bf16*>(wsb + WS_W), 128, 64, lane, 32);
+      cp_tile64(st + S_TP, reinterpret_cast<const bf16*>(wsb + WS_TP), lane, 32);
+      cp_tile64(st + S_AQK, reinterpret_cast<const bf16*>(wsb + WS_AQK), lane, 32);
+      float* gb = reinterpret_cast<float*>(sm + C_OFF_GB + s * 512);
+      for (int i = lane; i < 64; i += 32) {
+        const bool ok = i < L;
+        const int64_t idx = ok ? (t0 + i) * H + h : 0;
+        cp_async4(gb + i, g + idx, ok ? 4 : 0);
+        cp_async4(gb + 64 + i, beta + idx, ok ? 4 : 0);
+      }
+      cp_async_commit();
+      cp_async_wait_all();
+      tc::fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&full[s]);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && NC > 0) {
+      const uint32_t id_u = tc::idesc_bf16(128, 64, true, false);
+      const uint32_t id_vn = tc::idesc_bf16(128, 64, false, false, true);
+      const uint32_t id_qh = tc::idesc_bf16(128, 64, false, false);
+      const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
+      auto issue_u = [&](int c) {
+        const uint32_t st = sb + (c & 1) * STAGE;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::mma_bf16(tm + C_TM_U, mndesc(st + S_V, 8192, j), kdesc64(st + S_TP, j), id_u, j > 0);
+      };
+      bool live = tc::mbar_wait(&full[0], 0, WAIT_LIMIT);
+      if (live) issue_u(0);
+      for (int c = 0; c < NC && live; ++c) {
+        const int s = c & 1;
+        const uint32_t st = sb + s * STAGE;
+        if (!(live = tc::mbar_wait(&bar_ht, c & 1, WAIT_LIMIT))) break;
+        tc::fence_after();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          tc::mma_bf16(tm + C_TM_U, kdesc(sb + C_OFF_HT, 16384, j), kdesc(st + S_W, 8192, j), id_vn,
+                       true);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          tc::mma_bf16(tm + C_TM_QH, kdesc(sb + C_OFF_HT, 16384, j), kdesc(st + S_Q, 8192, j), id_qh,
+                       j > 0);
+        tc::commit(&bar_vq);
+        if (!(live = tc::mbar_wait(&bar_vt, c & 1, WAIT_LIMIT))) break;
+        tc::fence_after();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::mma_bf16(tm + C_TM_DS, kdesc64(sb + C_OFF_VTH, j), mndesc(st + S_K, 8192, j), id_s,
+                       j > 0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::mma_bf16(tm + C_TM_DS, kdesc64(sb + C_OFF_VTL, j), mndesc(st + S_K, 8192, j), id_s,
+                       true);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::mma_bf16(tm + C_TM_O, kdesc64(sb + C_OFF_VN, j), kdesc64(st + S_AQK, j), id_qh, true);
+        tc::commit(&bar_so);
+        tc::commit(&empty[s]);
+        if (c + 1 < NC) {
+          if (!(live = tc::mbar_wait(&full[s ^ 1], ((c + 1) >> 1) & 1, WAIT_LIMIT))) break;
+          issue_u(c + 1);
+        }
+      }
+      if (!live) {
+        record_error();
+        atomicExch(&abort_sh, 1);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue warps
+    const int cw = warp - 2;             // 0..7 (warps 2-9 cover each lane quarter twice)
+    const int quarter = warp & 3;        // TMEM lane quarter
+    const int colhalf = cw >> 2;         // 0/1
+    const int vrow = quarter * 32 + lane;
+    const int kc0 = colhalf * 64;        // state columns owned
+    const int tc0 = colhalf * 32;        // token columns owned in 64-wide regions
+    float S[64];
+    {
+      const float* src = h0 ? h0 + ((int64_t)n * H + h) * K * V : nullptr;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) S[i] = src ? src[(kc0 + i) * V + vrow] : 0.f;
+    }
+    float gl_prev = 0.f;
+    int L_prev = 0;
+    int64_t t0_prev = 0;
+    bool live = true;
+    auto sync_chain = [&]() { tc::named_sync(1, 256); };
+    auto wait_uniform = [&](uint64_t* b, uint32_t par) -> bool {
+      const bool ok = tc::mbar_wait(b, par, WAIT_LIMIT);
+      if (!ok) {
+        record_error();
+        atomicExch(&abort_sh, 1);
+      }
+      tc::fence_after();
+      sync_chain();
+      return *(volatile int*)&abort_sh == 0;
+    };
+    auto write_out = [&](int64_t tb, int Lc) {  // o = scale * D_o (previous chunk)
+      float ov[32];
+      tc::tmem_ld32(tm_addr(tm, quarter, C_TM_O + tc0), ov);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 32; ++c)
+        if (tc0 + c < Lc) o[(tb + tc0 + c) * (H * V) + (int64_t)h * V + vrow] = __float2bfloat16_rn(ov[c] * scale);
+    };
+    auto apply_ds = [&](float dl) {  // S = e^{gl} S + dS
+#pragma unroll
+      for (int cb = 0; cb < 2; ++cb) {
+        float d[32];
+        tc::tmem_ld32(tm_addr(tm, quarter, C_TM_DS + kc0 + cb * 32), d);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) S[cb * 32 + i] = fmaf(S[cb * 32 + i], dl, d[i]);
+      }
+    };
+    for (int c = 0; c < NC && live; ++c) {
+      const int s = c & 1;
+      const unsigned char* st = sm + s * STAGE;
+      if (c > 0) {
+        if (!(live = wait_uniform(&bar_so, (c - 1) & 1))) break;
+        write_out(t0_prev, L_prev);
+        apply_ds(__expf(gl_prev));
+      }
+      // E0: bf16 S^T -> HT
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        uint4 pk;
+        pk.x = pack_bf16(S[8 * m + 0], S[8 * m + 1]);
+        pk.y = pack_bf16(S[8 * m + 2], S[8 * m + 3]);
+        pk.z = pack_bf16(S[8 * m + 4], S[8 * m + 5]);
+        pk.w = pack_bf16(S[8 * m + 6], S[8 * m + 7]);
+        *reinterpret_cast<uint4*>(sm + C_OFF_HT + chunk_off(vrow, (kc0 >> 3) + m, 16384)) = pk;
+      }
+      tc::fence_proxy_async();
+      tc::fence_before();
+      sync_chain();
+      if (cw == 0 && lane == 0) tc::mbar_arrive(&bar_ht);
+      // stage s gates: cumsum
+      if (!(live = wait_uniform(&full[s], (c >> 1) & 1))) break;
+      const float* gb = reinterpret_cast<const float*>(sm + C_OFF_GB + s * 512);
+      float* gcs = reinterpret_cast<float*>(sm + C_OFF_GB + 1024 + s * 256);
+      if (cw == 0) chunk_cumsum_warp(gb, gcs, lane);
+      sync_chain();
+      const int64_t t0 = bos + (int64_t)c * BT;
+      const int L = (int)((eos - t0) < BT ? (eos - t0) : BT);
+      const float gl = gcs[L - 1];
+      if (!(live = wait_uniform(&bar_vq, c & 1))) break;
+      // E1: v_new, vt hi/lo, o_inter
+      {
+        float du[32], qh[32];
+        tc::tmem_ld32(tm_addr(tm, quarter, C_TM_U + tc0), du);
+        tc::tmem_ld32(tm_addr(tm, quarter, C_TM_QH + tc0), qh);
+        tc::tmem_wait_ld();
+        const float* bet = gb + 64;
+#pragma unroll
+        for (int cc = 0; cc < 32; cc += 8) {
+          float vn[8], th[8], tl[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int i = tc0 + cc + u;
+            const float vi = __bfloat162float(
+                *reinterpret_cast<const bf16*>(st + S_V + elem_off(i, vrow, 8192)));
+            vn[u] = du[cc + u] + bet[i] * vi;
+            const float sc = vn[u] * __expf(fminf(gl - gcs[i], 0.f));
+            th[u] = __bfloat162float(__float2bfloat16_rn(sc));
+            tl[u] = sc - th[u];
+            qh[cc + u] *= __expf(gcs[i]);
+          }
+          const uint32_t off = (uint32_t)(vrow * 128 + ((((tc0 + cc) >> 3) ^ (vrow & 7)) << 4));
+          uint4 a, b2, d;
+          a.x = pack_bf16(vn[0], vn[1]); a.y = pack_bf16(vn[2], vn[3]);
+          a.z = pack_bf16(vn[4], vn[5]); a.w = pack_bf16(vn[6], vn[7]);
+          b2.x = pack_bf16(th[0], th[1]); b2.y = pack_bf16(th[2], th[3]);
+          b2.z = pack_bf16(th[4], th[5]); b2.w = pack_bf16(th[6], th[7]);
+          d.x = pack_bf16(tl[0], tl[1]); d.y = pack_bf16(tl[2], tl[3]);
+          d.z = pack_bf16(tl[4], tl[5]); d.w = pack_bf16(tl[6], tl[7]);
+          *reinterpret_cast<uint4*>(sm + C_OFF_VN + off) = a;
+          *reinterpret_cast<uint4*>(sm + C_OFF_VTH + off) = b2;
+          *reinterpret_cast<uint4*>(sm + C_OFF_VTL + off) = d;
+        }
+        tc::tmem_st32(tm_addr(tm, quarter, C_TM_O + tc0), qh);
+        tc::tmem_wait_st();
+      }
+      tc::fence_proxy_async();
+      tc::fence_before();
+      sync_chain();
+      if (cw == 0 && lane == 0) tc::mbar_arrive(&bar_vt);
+      gl_prev = gl;
+      L_prev = L;
+      t0_prev = t0;
+    }
+    if (live && NC > 0) {
+      if ((live = wait_uniform(&bar_so, (NC - 1) & 1))) {
+        write_out(t0_prev, L_prev);
+        apply_ds(__expf(gl_prev));
+      }
+    }
+    if (live && ht) {
+      float* dst = ht + ((int64_t)n * H + h) * K * V;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) dst[(kc0 + i) * V + vrow] = S[i];
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tm, C_TM_COLS);
+}
+
+}  // namespace
+}  // namespace gdn
+}  // namespace xops
+
+using namespace xops;
+
+static int64_t chunk_bound(const int32_t* cu, int64_t B, int64_t T, int64_t N) {
+  return cu ? T / gdn::BT + N : B * ((T + gdn::BT - 1) / gdn::BT);
+}
+
+extern "C" int64_t xops_chunk_gated_delta_rule_workspace_size(int64_t B, int64_t T, int64_t N,
+                                                              int64_t Hg, int64_t H, int64_t K,
+                                                              int use_qk_l2norm_in_kernel,
+                                                              int varlen) {
+  if (B < 1 || T < 0 || N < 0 || Hg < 1 || H < 1 || K <= 0) return -1;
+  const int64_t chunks = varlen ? T / gdn::BT + N : B * ((T + gdn::BT - 1) / gdn::BT);
+  int64_t bytes = chunks * H * (int64_t)gdn::WS_CHUNK;
+  if (use_qk_l2norm_in_kernel) bytes += 2 * B * T * Hg * K * 2 + 256;
+  return bytes;
+}
+
+extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const void* v,
+                                           const float* g, const float* beta, const float* h0,
+                                           void* o, float* ht, const int32_t* cu_seqlens,
+                                           int64_t B, int64_t T, int64_t N, int64_t Hg,
+                                           int64_t H, int64_t K, int64_t V,
+                                           int64_t q_token_stride, int64_t k_token_stride,
+                                           int64_t v_token_stride, float scale,
+                                           int use_qk_l2norm_in_kernel, void* workspace,
+                                           int64_t workspace_bytes, void* stream) {
+  XOPS_REQUIRE(B >= 1 && T >= 0 && N >= 0 && Hg >= 1 && H >= 1,
+               "chunk_gated_delta_rule: bad shape");
+  XOPS_REQUIRE(H % Hg == 0,
+               "chunk_gated_delta_rule expects num_heads_v to be divisible by num_heads_qk, got "
+               "%lld and %lld", (long long)H, (long long)Hg);
+  XOPS_REQUIRE(cu_seqlens || N == B, "chunk_gated_delta_rule: without cu_seqlens N must equal B");
+  XOPS_REQUIRE(!cu_seqlens || B == 1, "chunk_gated_delta_rule: cu_seqlens requires B == 1");
+  XOPS_UNSUPPORTED(K == 128 && V == 128,
+                   "chunk_gated_delta_rule: only K == V == 128 is compiled (got %lld, %lld)",
+                   (long long)K, (long long)V);
+  if (q_token_stride == 0) q_token_stride = Hg * K;
+  if (k_token_stride == 0) k_token_stride = Hg * K;
+  if (v_token_stride == 0) v_token_stride = H * V;
+  XOPS_REQUIRE(q_token_stride >= Hg * K && k_token_stride >= Hg * K && v_token_stride >= H * V &&
+                   q_token_stride % 8 == 0 && k_token_stride % 8 == 0 && v_token_stride % 8 == 0,
+               "chunk_gated_delta_rule: token strides must cover the heads and be multiples of 8");
+  if (N == 0 || T == 0) return XOPS_OK;
+  XOPS_REQUIRE(q && k && v && g && beta && o, "chunk_gated_delta_rule: null pointer");
+  XOPS_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o),
+               "chunk_gated_delta_rule: tensors must be 16-byte aligned");
+  const int64_t need = xops_chunk_gated_delta_rule_workspace_size(
+      B, T, N, Hg, H, K, use_qk_l2norm_in_kernel, cu_seqlens != nullptr);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace))
+    return set_error(XOPS_ERR_WORKSPACE,
+                     "chunk_gated_delta_rule: workspace of %lld bytes (16-byte aligned) required, "
+                     "got %lld", (long long)need, (long long)workspace_bytes);
+  cudaStream_t st = (cudaStream_t)stream;
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  const gdn::bf16* qq = (const gdn::bf16*)q;
+  const gdn::bf16* kk = (const gdn::bf16*)k;
+  int64_t qs = q_token_stride, ks = k_token_stride;
+  const int64_t nchunks = chunk_bound(cu_seqlens, B, T, N);
+  if (use_qk_l2norm_in_kernel) {
+    gdn::bf16* qn = reinterpret_cast<gdn::bf16*>(ws + nchunks * H * (int64_t)gdn::WS_CHUNK);
+    gdn::bf16* kn = qn + B * T * Hg * K;
+    const int64_t rows = B * T * Hg;
+    gdn::l2norm_heads_kernel<<<(unsigned)cdiv64(rows, 8), 256, 0, st>>>(qq, qn, rows, Hg, qs);
+    if (int rc = check_launch("chunk_gated_delta_rule(l2norm q)")) return rc;
+    gdn::l2norm_heads_kernel<<<(unsigned)cdiv64(rows, 8), 256, 0, st>>>(kk, kn, rows, Hg, ks);
+    if (int rc = check_launch("chunk_gated_delta_rule(l2norm k)")) return rc;
+    qq = qn;
+    kk = kn;
+    qs = ks = Hg * K;
+  }
+  if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_prep_kernel, gdn::P_SMEM,
+                                     "chunk_gated_delta_rule(prep)"))
+    return rc;
+  gdn::chunk_prep_kernel<<<dim3((unsigned)nchunks, (unsigned)Hg), gdn::P_NT, gdn::P_SMEM, st>>>(
+      qq, kk, g, beta, ws, cu_seqlens, N, T, Hg, H, qs, ks);
+  if (int rc = check_launch("chunk_gated_delta_rule(prep)")) return rc;
+  if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_chain_kernel, gdn::C_SMEM,
+                                     "chunk_gated_delta_rule(chain)"))
+    return rc;
+  gdn::chunk_chain_kernel<<<(unsigned)(N * H), gdn::C_NT, gdn::C_SMEM, st>>>(
+      qq, kk, (const gdn::bf16*)v, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, T, Hg, H, qs,
+      ks, v_token_stride, scale);
+  return check_launch("chunk_gated_delta_rule(chain)");
+}
+
+extern "C" int xops_device_error_count(void) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, gdn::g_tc_error, sizeof(int)) != cudaSuccess) return -1;
+  const int zero = 0;
+  cudaMemcpyToSymbol(gdn::g_tc_error, &zero, sizeof(int));
+  return v;
+}

@@ -393,10 +393,14 @@ def npu_chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None,
     ht = torch.empty((N, H, K, V), dtype=torch.float32, device=v.device) if output_final_state else None
     qc, kc, vc = _token_rows(q, B), _token_rows(k, B), _token_rows(v, B)
     gg, bb = g.to(torch.float32).contiguous(), beta.to(torch.float32).contiguous()
+    l2 = int(bool(use_qk_l2norm_in_kernel))
+    wsb = _lib.load().xops_chunk_gated_delta_rule_workspace_size(B, T, N, Hg, H, K, l2,
+                                                                 int(cu is not None))
+    ws = torch.empty(max(int(wsb), 16), dtype=torch.uint8, device=q.device)
     _lib.call("xops_chunk_gated_delta_rule", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(),
               gg.data_ptr(), bb.data_ptr(), _ptr(h0), o.data_ptr(), _ptr(ht), _ptr(cu), B, T, N,
-              Hg, H, K, V, qc.stride(1), kc.stride(1), vc.stride(1), scale_v,
-              int(bool(use_qk_l2norm_in_kernel)), _stream(q))
+              Hg, H, K, V, qc.stride(1), kc.stride(1), vc.stride(1), scale_v, l2, ws.data_ptr(),
+              ws.numel(), _stream(q))
     return o, ht
 
 
