@@ -103,13 +103,66 @@ def build(force=False, jobs=None, verbose=False):
     return LIB
 
 
+TORCH_API_SRCS = ["torch_api/ops_impl.cpp", "torch_api/op_register.cpp",
+                  "runtime/kernel_registry.cpp"]
+
+
+def _ext_path():
+    import sysconfig
+    return os.path.join(PKG, "_C" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_torch_api(force=False, jobs=None):
+    """Compile the C++ torch API (xllm::kernel::npu / npu_ops + the pybind
+    module ``torch_npu_ops_b200._C``) against libtorch, linked to
+    libxops_b200.so with an $ORIGIN rpath."""
+    import sysconfig
+    import torch
+    from torch.utils import cpp_extension as ce
+    out = _ext_path()
+    srcs = [os.path.join(CSRC, s) for s in TORCH_API_SRCS]
+    objs = [os.path.join(BUILD, "api_" + os.path.basename(s)[:-4] + ".o") for s in srcs]
+    cxx = os.environ.get("CXX", "g++")
+    inc = ce.include_paths(device_type="cuda") + [sysconfig.get_paths()["include"], INCLUDE, CSRC,
+                                                  os.path.join(CSRC, "torch_api")]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    flags = ["-O2", "-std=c++17", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+             "-DTORCH_EXTENSION_NAME=_C", "-DTORCH_API_INCLUDE_EXTENSION_H", "-w"]
+    todo = [(s, o) for s, o in zip(srcs, objs) if force or _stale(s, o)]
+    os.makedirs(BUILD, exist_ok=True)
+
+    def cc(so):
+        cmd = [cxx, *flags, *[f"-I{d}" for d in inc], "-c", so[0], "-o", so[1]]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        return so[0], r.returncode, r.stdout + r.stderr
+
+    if todo:
+        with cf.ThreadPoolExecutor(max_workers=jobs or len(todo)) as ex:
+            for src, rc, txt in ex.map(cc, todo):
+                if rc != 0:
+                    raise RuntimeError(f"g++ failed for {src}:\n{txt[-4000:]}")
+    if todo or not os.path.exists(out) or os.path.getmtime(LIB) > os.path.getmtime(out):
+        libdirs = ce.library_paths(device_type="cuda")
+        cmd = [cxx, "-shared", "-o", out, *objs, *[f"-L{d}" for d in libdirs], "-L" + PKG,
+               "-lxops_b200", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda",
+               "-ltorch_python", "-Wl,-rpath,$ORIGIN",
+               *[f"-Wl,-rpath,{d}" for d in libdirs]]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("link of the torch API failed:\n" + r.stdout + r.stderr)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-j", type=int, default=None)
     ap.add_argument("-v", "--verbose", action="store_true", help="pass -Xptxas -v")
+    ap.add_argument("--no-torch-api", action="store_true", help="skip the C++ torch API module")
     a = ap.parse_args()
     print(build(a.force, a.j, a.verbose))
+    if not a.no_torch_api:
+        print(build_torch_api(a.force, a.j))
 
 
 if __name__ == "__main__":

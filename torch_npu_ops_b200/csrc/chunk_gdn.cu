@@ -126,11 +126,10 @@ constexpr int P_OFF_KQ = 0;        // [K h0 | Q h0 | K h1 | Q h1], 8 KB each
 constexpr int P_KQ_HALF = 16384;
 constexpr int P_OFF_Q = 8192;
 constexpr int P_OFF_TPP = 32768;   // T'' [64 x 64] SW128
-constexpr int P_OFF_FA = 40960;    // fp32 A [64 x LDF]
-constexpr int P_OFF_FT = P_OFF_FA + 64 * LDF * 4;
-constexpr int P_OFF_FM = P_OFF_FT + 64 * LDF * 4;
-constexpr int P_OFF_G = P_OFF_FM + 32 * 33 * 4;
-constexpr int P_SMEM = P_OFF_G + 3 * 64 * 4 + 1024;
+constexpr int P_OFF_FA = 40960;    // fp32 A, then T = (I+A)^-1 in place [64 x LDF]
+constexpr int P_OFF_FM = P_OFF_FA + 64 * LDF * 4;
+constexpr int P_OFF_G = P_OFF_FM + 32 * 33 * 4;  // graw, gc, beta, e^gc
+constexpr int P_SMEM = P_OFF_G + 4 * 64 * 4 + 1024;
 constexpr uint32_t P_TM_G = 0, P_TM_W = 64, P_TM_COLS = 128;
 
 __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
@@ -163,6 +162,7 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
   float* graw = reinterpret_cast<float*>(sm + P_OFF_G);
   float* gcs = graw + 64;
   float* bet = gcs + 64;
+  float* egc = bet + 64;
   const uint32_t sb = tc::smem_addr(sm);
 
   if (warp == 0) {
@@ -213,7 +213,12 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
       bet[tid] = tid < L ? beta[(t0 + tid) * H + hv] : 0.f;
     }
     __syncthreads();
-    if (warp == 0) chunk_cumsum_warp(graw, gcs, lane);
+    if (warp == 0) {
+      chunk_cumsum_warp(graw, gcs, lane);
+      __syncwarp();
+      egc[lane] = __expf(gcs[lane]);
+      egc[lane + 32] = __expf(gcs[lane + 32]);
+    }
     __syncthreads();
     // Gram epilogue
     {
@@ -251,10 +256,9 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
     }
     __syncthreads();
     {
-      float* fa = reinterpret_cast<float*>(sm + P_OFF_FA);
-      float* ft = reinterpret_cast<float*>(sm + P_OFF_FT);
+      float* ft = reinterpret_cast<float*>(sm + P_OFF_FA);
       float* fm = reinterpret_cast<float*>(sm + P_OFF_FM);
-      tri_inverse_64(fa, ft, fm, tid);
+      tri_inverse_64_inplace(ft, fm, tid);
       bf16* tpg = reinterpret_cast<bf16*>(wsb + WS_TP);
       for (int e = tid; e < 64 * 8; e += P_NT) {
         const int i = e >> 3, cc = e & 7;
@@ -264,7 +268,7 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
           const int j = cc * 8 + u;
           const float tv = ft[i * LDF + j] * bet[j];
           tp[u] = (i == j) ? 0.f : tv;
-          tpp[u] = tv * __expf(gcs[j]);
+          tpp[u] = tv * egc[j];
         }
         uint4 a, b;
         a.x = pack_bf16(tp[0], tp[1]); a.y = pack_bf16(tp[2], tp[3]);
@@ -318,8 +322,9 @@ constexpr int C_OFF_HT = 2 * STAGE;       // S^T bf16 [128 x 128], halves 16 KB 
 constexpr int C_OFF_VTH = C_OFF_HT;       // aliases HT (disjoint lifetimes)
 constexpr int C_OFF_VTL = C_OFF_HT + 16384;
 constexpr int C_OFF_VN = C_OFF_HT + 32768;
-constexpr int C_OFF_GB = C_OFF_VN + 16384;  // per stage: g[64], beta[64] ; then gc[2][64]
-constexpr int C_SMEM = C_OFF_GB + 2 * 512 + 2 * 256 + 1024;
+constexpr int C_OFF_GB = C_OFF_VN + 16384;  // per stage: g[64], beta[64]
+constexpr int C_OFF_TAB = C_OFF_GB + 2 * 512; // gc[64], e^gc[64], e^{gl-gc}[64]
+constexpr int C_SMEM = C_OFF_TAB + 3 * 256 + 1024;
 constexpr uint32_t C_TM_U = 0, C_TM_QH = 64, C_TM_O = 128, C_TM_DS = 256, C_TM_COLS = 512;
 
 __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
@@ -334,9 +339,28 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
   __shared__ uint64_t full[2], empty[2], bar_ht, bar_vq, bar_vt, bar_so;
   __shared__ uint32_t tmem_sh;
   __shared__ int abort_sh;
+  __shared__ int64_t seq_sh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t n = blockIdx.x / H;
-  const int h = (int)(blockIdx.x - n * H);
+  // Longest sequences first: CTA rank r serves the r-th longest sequence
+  // (ties by index), so the longest chains start in the first wave.
+  const int64_t rank = blockIdx.x / H;
+  const int h = (int)(blockIdx.x - rank * H);
+  if (!cu) {
+    if (tid == 0) seq_sh = rank;
+  } else {
+    const int64_t nseq = gridDim.x / H;
+    for (int64_t j = tid; j < nseq; j += blockDim.x) {
+      const int64_t lj = (int64_t)cu[j + 1] - cu[j];
+      int64_t r = 0;
+      for (int64_t m = 0; m < nseq; ++m) {
+        const int64_t lm = (int64_t)cu[m + 1] - cu[m];
+        r += (lm > lj) || (lm == lj && m < j);
+      }
+      if (r == rank) seq_sh = j;
+    }
+  }
+  __syncthreads();
+  const int64_t n = seq_sh;
   const int hk = (int)(h / (H / Hg));
   int64_t bos, eos;
   seq_span(cu, n, T, bos, eos);
@@ -460,6 +484,9 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     const int vrow = quarter * 32 + lane;
     const int kc0 = colhalf * 64;        // state columns owned
     const int tc0 = colhalf * 32;        // token columns owned in 64-wide regions
+    float* gcs = reinterpret_cast<float*>(sm + C_OFF_TAB);  // gc, e^gc, e^{gl-gc}
+    float* egc = gcs + 64;
+    float* edc = gcs + 128;
     float S[64];
     {
       const float* src = h0 ? h0 + ((int64_t)n * H + h) * K * V : nullptr;
@@ -482,21 +509,26 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       return *(volatile int*)&abort_sh == 0;
     };
     auto write_out = [&](int64_t tb, int Lc) {  // o = scale * D_o (previous chunk)
-      float ov[32];
-      tc::tmem_ld32(tm_addr(tm, quarter, C_TM_O + tc0), ov);
-      tc::tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        if (tc0 + c < Lc) o[(tb + tc0 + c) * (H * V) + (int64_t)h * V + vrow] = __float2bfloat16_rn(ov[c] * scale);
+      for (int half = 0; half < 2; ++half) {
+        float ov[16];
+        tc::tmem_ld16(tm_addr(tm, quarter, C_TM_O + tc0 + half * 16), ov);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int i = tc0 + half * 16 + c;
+          if (i < Lc) o[(tb + i) * (H * V) + (int64_t)h * V + vrow] = __float2bfloat16_rn(ov[c] * scale);
+        }
+      }
     };
     auto apply_ds = [&](float dl) {  // S = e^{gl} S + dS
 #pragma unroll
-      for (int cb = 0; cb < 2; ++cb) {
-        float d[32];
-        tc::tmem_ld32(tm_addr(tm, quarter, C_TM_DS + kc0 + cb * 32), d);
+      for (int cb = 0; cb < 4; ++cb) {
+        float d[16];
+        tc::tmem_ld16(tm_addr(tm, quarter, C_TM_DS + kc0 + cb * 16), d);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) S[cb * 32 + i] = fmaf(S[cb * 32 + i], dl, d[i]);
+        for (int i = 0; i < 16; ++i) S[cb * 16 + i] = fmaf(S[cb * 16 + i], dl, d[i]);
       }
     };
     for (int c = 0; c < NC && live; ++c) {
@@ -504,10 +536,9 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       const unsigned char* st = sm + s * STAGE;
       if (c > 0) {
         if (!(live = wait_uniform(&bar_so, (c - 1) & 1))) break;
-        write_out(t0_prev, L_prev);
         apply_ds(__expf(gl_prev));
       }
-      // E0: bf16 S^T -> HT
+      // E0: bf16 S^T -> HT, then let the MMA warp go
 #pragma unroll
       for (int m = 0; m < 8; ++m) {
         uint4 pk;
@@ -521,50 +552,65 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       tc::fence_before();
       sync_chain();
       if (cw == 0 && lane == 0) tc::mbar_arrive(&bar_ht);
-      // stage s gates: cumsum
+      // previous chunk's output overlaps this chunk's first MMAs
+      if (c > 0) write_out(t0_prev, L_prev);
+      // gates of this chunk: cumsum and the two exponential tables
       if (!(live = wait_uniform(&full[s], (c >> 1) & 1))) break;
       const float* gb = reinterpret_cast<const float*>(sm + C_OFF_GB + s * 512);
-      float* gcs = reinterpret_cast<float*>(sm + C_OFF_GB + 1024 + s * 256);
-      if (cw == 0) chunk_cumsum_warp(gb, gcs, lane);
-      sync_chain();
       const int64_t t0 = bos + (int64_t)c * BT;
       const int L = (int)((eos - t0) < BT ? (eos - t0) : BT);
+      if (cw == 0) {
+        chunk_cumsum_warp(gb, gcs, lane);
+        __syncwarp();
+        const float glc = gcs[L - 1];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = lane + 32 * u;
+          egc[i] = __expf(gcs[i]);
+          edc[i] = __expf(fminf(glc - gcs[i], 0.f));
+        }
+      }
+      sync_chain();
       const float gl = gcs[L - 1];
       if (!(live = wait_uniform(&bar_vq, c & 1))) break;
-      // E1: v_new, vt hi/lo, o_inter
+      // E1: v_new, vt hi/lo, o_inter (16 tokens at a time)
       {
-        float du[32], qh[32];
-        tc::tmem_ld32(tm_addr(tm, quarter, C_TM_U + tc0), du);
-        tc::tmem_ld32(tm_addr(tm, quarter, C_TM_QH + tc0), qh);
-        tc::tmem_wait_ld();
         const float* bet = gb + 64;
 #pragma unroll
-        for (int cc = 0; cc < 32; cc += 8) {
-          float vn[8], th[8], tl[8];
+        for (int half = 0; half < 2; ++half) {
+          const int tb = tc0 + half * 16;
+          float du[16], qh[16];
+          tc::tmem_ld16(tm_addr(tm, quarter, C_TM_U + tb), du);
+          tc::tmem_ld16(tm_addr(tm, quarter, C_TM_QH + tb), qh);
+          tc::tmem_wait_ld();
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int i = tc0 + cc + u;
-            const float vi = __bfloat162float(
-                *reinterpret_cast<const bf16*>(st + S_V + elem_off(i, vrow, 8192)));
-            vn[u] = du[cc + u] + bet[i] * vi;
-            const float sc = vn[u] * __expf(fminf(gl - gcs[i], 0.f));
-            th[u] = __bfloat162float(__float2bfloat16_rn(sc));
-            tl[u] = sc - th[u];
-            qh[cc + u] *= __expf(gcs[i]);
+          for (int cc = 0; cc < 16; cc += 8) {
+            float vn[8], th[8], tl[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int i = tb + cc + u;
+              const float vi = __bfloat162float(
+                  *reinterpret_cast<const bf16*>(st + S_V + elem_off(i, vrow, 8192)));
+              vn[u] = fmaf(bet[i], vi, du[cc + u]);
+              const float sc = vn[u] * edc[i];
+              th[u] = __bfloat162float(__float2bfloat16_rn(sc));
+              tl[u] = sc - th[u];
+              qh[cc + u] *= egc[i];
+            }
+            const uint32_t off = (uint32_t)(vrow * 128 + ((((tb + cc) >> 3) ^ (vrow & 7)) << 4));
+            uint4 a, b2, d;
+            a.x = pack_bf16(vn[0], vn[1]); a.y = pack_bf16(vn[2], vn[3]);
+            a.z = pack_bf16(vn[4], vn[5]); a.w = pack_bf16(vn[6], vn[7]);
+            b2.x = pack_bf16(th[0], th[1]); b2.y = pack_bf16(th[2], th[3]);
+            b2.z = pack_bf16(th[4], th[5]); b2.w = pack_bf16(th[6], th[7]);
+            d.x = pack_bf16(tl[0], tl[1]); d.y = pack_bf16(tl[2], tl[3]);
+            d.z = pack_bf16(tl[4], tl[5]); d.w = pack_bf16(tl[6], tl[7]);
+            *reinterpret_cast<uint4*>(sm + C_OFF_VN + off) = a;
+            *reinterpret_cast<uint4*>(sm + C_OFF_VTH + off) = b2;
+            *reinterpret_cast<uint4*>(sm + C_OFF_VTL + off) = d;
           }
-          const uint32_t off = (uint32_t)(vrow * 128 + ((((tc0 + cc) >> 3) ^ (vrow & 7)) << 4));
-          uint4 a, b2, d;
-          a.x = pack_bf16(vn[0], vn[1]); a.y = pack_bf16(vn[2], vn[3]);
-          a.z = pack_bf16(vn[4], vn[5]); a.w = pack_bf16(vn[6], vn[7]);
-          b2.x = pack_bf16(th[0], th[1]); b2.y = pack_bf16(th[2], th[3]);
-          b2.z = pack_bf16(th[4], th[5]); b2.w = pack_bf16(th[6], th[7]);
-          d.x = pack_bf16(tl[0], tl[1]); d.y = pack_bf16(tl[2], tl[3]);
-          d.z = pack_bf16(tl[4], tl[5]); d.w = pack_bf16(tl[6], tl[7]);
-          *reinterpret_cast<uint4*>(sm + C_OFF_VN + off) = a;
-          *reinterpret_cast<uint4*>(sm + C_OFF_VTH + off) = b2;
-          *reinterpret_cast<uint4*>(sm + C_OFF_VTL + off) = d;
+          tc::tmem_st16(tm_addr(tm, quarter, C_TM_O + tb), qh);
         }
-        tc::tmem_st32(tm_addr(tm, quarter, C_TM_O + tc0), qh);
         tc::tmem_wait_st();
       }
       tc::fence_proxy_async();
@@ -577,8 +623,8 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     }
     if (live && NC > 0) {
       if ((live = wait_uniform(&bar_so, (NC - 1) & 1))) {
-        write_out(t0_prev, L_prev);
         apply_ds(__expf(gl_prev));
+        write_out(t0_prev, L_prev);
       }
     }
     if (live && ht) {

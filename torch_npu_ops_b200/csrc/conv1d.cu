@@ -53,7 +53,7 @@ __device__ __forceinline__ void locate_tile(const int32_t* __restrict__ qsl, int
 }
 
 template <typename T, int W>
-__global__ void __launch_bounds__(256) conv1d_varlen_kernel(
+__global__ void __launch_bounds__(128, 3) conv1d_varlen_kernel(
     const T* __restrict__ x, T* __restrict__ state, const T* __restrict__ weight,
     const T* __restrict__ bias, const int32_t* __restrict__ qsl,
     const int32_t* __restrict__ slots, T* __restrict__ out, int nseq, int64_t dim, bool silu,
@@ -104,22 +104,35 @@ __global__ void __launch_bounds__(256) conv1d_varlen_kernel(
   }
   // UNROLL token rows are loaded before any is consumed, so each thread keeps
   // UNROLL independent 16-byte loads in flight.
+  // (kept as raw 16-byte words until used, so the batch costs 4 registers
+  // per bf16 row instead of 8).
   constexpr int UNROLL = 8;
+  constexpr int RW = VEC * (int)sizeof(T) / 16;
   for (int64_t tb = t0; tb < t1; tb += UNROLL) {
-    float cur[UNROLL][VEC];
+    uint4 raw[UNROLL][RW];
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u)
-      if (tb + u < t1) load_vec<T, VEC>(x + (tb + u) * dim + c0, cur[u]);
+      if (tb + u < t1) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + (tb + u) * dim + c0);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) raw[u][r] = __ldg(src + r);
+      }
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       if (tb + u >= t1) break;
+      float cur_u[VEC];
+      {
+        const T* e = reinterpret_cast<const T*>(raw[u]);
+#pragma unroll
+        for (int c = 0; c < VEC; ++c) cur_u[c] = to_f32<T>(e[c]);
+      }
       float o[VEC];
 #pragma unroll
       for (int c = 0; c < VEC; ++c) {
         float acc = b[c];
 #pragma unroll
         for (int j = 0; j < H; ++j) acc = fmaf(hist[j][c], w[c][j], acc);
-        acc = fmaf(cur[u][c], w[c][H], acc);
+        acc = fmaf(cur_u[c], w[c][H], acc);
         o[c] = silu ? silu_f(acc) : acc;
       }
       store_vec<T, VEC>(out + (tb + u) * dim + c0, o);
@@ -129,7 +142,7 @@ __global__ void __launch_bounds__(256) conv1d_varlen_kernel(
         for (int c = 0; c < VEC; ++c) hist[j][c] = hist[j + 1][c];
       if constexpr (H > 0) {
 #pragma unroll
-        for (int c = 0; c < VEC; ++c) hist[H - 1][c] = cur[u][c];
+        for (int c = 0; c < VEC; ++c) hist[H - 1][c] = cur_u[c];
       }
     }
   }

@@ -204,6 +204,84 @@ __device__ __forceinline__ void tri_inverse_64(const float* __restrict__ sA, flo
   __syncthreads();
 }
 
+// In-place variant: sA (strictly lower A, fp32, stride LDF, zero upper part)
+// is overwritten by T = (I + A)^-1.  Same blocking as tri_inverse_64; every
+// block of T replaces the block of A it no longer needs, products are
+// register-tiled (2x2 outputs per thread in the 32x32 merge).  sM: 32 x 33
+// fp32 scratch.  All 256 threads participate; ends with a barrier.
+__device__ __forceinline__ void tri_inverse_64_inplace(float* __restrict__ sA,
+                                                       float* __restrict__ sM, int tid) {
+  // 16x16 diagonal blocks: column c of block b by forward substitution
+  float x[16];
+  const int b = tid >> 4, c = tid & 15;
+  if (tid < 64) {
+    const float* Ab = sA + (16 * b) * LDF + 16 * b;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = (i == c) ? 1.f : 0.f;
+#pragma unroll
+    for (int i = 1; i < 16; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int m = 0; m < i; ++m) s = fmaf(Ab[i * LDF + m], x[m], s);
+      if (i > c) x[i] = -s;
+    }
+  }
+  __syncthreads();
+  if (tid < 64) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) sA[(16 * b + i) * LDF + 16 * b + c] = x[i];
+  }
+  __syncthreads();
+  // 16 -> 32: T10 = -T11 A10 T00 and T32 = -T33 A32 T22; one output pair per thread
+  {
+    const int p = tid >> 7, e = tid & 127, rr = e >> 3, cc = (e & 7) * 2;
+    const int r = 2 * p + 1, cb = 2 * p;
+    float s0 = 0.f, s1 = 0.f;
+    for (int m = cc; m < 16; ++m) {
+      const float a = sA[(16 * r + rr) * LDF + 16 * cb + m];
+      s0 = fmaf(a, sA[(16 * cb + m) * LDF + 16 * cb + cc], s0);
+      s1 = fmaf(a, sA[(16 * cb + m) * LDF + 16 * cb + cc + 1], s1);
+    }
+    sM[p * 256 + rr * 16 + cc] = s0;
+    sM[p * 256 + rr * 16 + cc + 1] = s1;
+    __syncthreads();
+    s0 = s1 = 0.f;
+    for (int m = 0; m <= rr; ++m) {
+      const float t = sA[(16 * r + rr) * LDF + 16 * r + m];
+      s0 = fmaf(t, sM[p * 256 + m * 16 + cc], s0);
+      s1 = fmaf(t, sM[p * 256 + m * 16 + cc + 1], s1);
+    }
+    sA[(16 * r + rr) * LDF + 16 * cb + cc] = -s0;
+    sA[(16 * r + rr) * LDF + 16 * cb + cc + 1] = -s1;
+  }
+  __syncthreads();
+  // 32 -> 64: T[32:64][0:32] = -T11 (A10 T00); 2x2 outputs per thread
+  {
+    const int rr = (tid >> 4) * 2, cc = (tid & 15) * 2;
+    float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f;
+    for (int m = cc; m < 32; ++m) {
+      const float a0 = sA[(32 + rr) * LDF + m], a1 = sA[(33 + rr) * LDF + m];
+      const float t0 = sA[m * LDF + cc], t1 = sA[m * LDF + cc + 1];
+      s00 = fmaf(a0, t0, s00); s01 = fmaf(a0, t1, s01);
+      s10 = fmaf(a1, t0, s10); s11 = fmaf(a1, t1, s11);
+    }
+    sM[rr * 33 + cc] = s00; sM[rr * 33 + cc + 1] = s01;
+    sM[(rr + 1) * 33 + cc] = s10; sM[(rr + 1) * 33 + cc + 1] = s11;
+    __syncthreads();
+    s00 = s01 = s10 = s11 = 0.f;
+    for (int m = 0; m <= rr + 1; ++m) {
+      const float u0 = sA[(32 + rr) * LDF + 32 + m];
+      const float u1 = sA[(33 + rr) * LDF + 32 + m];
+      const float q0 = sM[m * 33 + cc], q1 = sM[m * 33 + cc + 1];
+      s00 = fmaf(u0, q0, s00); s01 = fmaf(u0, q1, s01);
+      s10 = fmaf(u1, q0, s10); s11 = fmaf(u1, q1, s11);
+    }
+    sA[(32 + rr) * LDF + cc] = -s00; sA[(32 + rr) * LDF + cc + 1] = -s01;
+    sA[(33 + rr) * LDF + cc] = -s10; sA[(33 + rr) * LDF + cc + 1] = -s11;
+  }
+  __syncthreads();
+}
+
 // Inclusive cumsum of g[0..63] (rows >= L zero) by warp 0 into sG; returns
 // nothing, sG[L-1] is the chunk's last cumulative gate.
 __device__ __forceinline__ void chunk_cumsum_warp(const float* __restrict__ graw, float* sG,

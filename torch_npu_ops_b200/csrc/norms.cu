@@ -98,7 +98,8 @@ __global__ void __launch_bounds__(256) layer_norm_packed_kernel(
   const int64_t total = M * ngroups;
   const int64_t warp_global = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t seg0 = warp_global * (SPW * UNROLL);
-  float xv[UNROLL][VEC], zv[UNROLL][VEC];
+  // x and z stay raw 16-byte words until their segment is processed
+  uint4 xr[UNROLL], zr[UNROLL];
   int64_t row[UNROLL], grp[UNROLL];
   bool live[UNROLL];
 #pragma unroll
@@ -108,25 +109,40 @@ __global__ void __launch_bounds__(256) layer_norm_packed_kernel(
     row[u] = live[u] ? seg / ngroups : 0;
     grp[u] = live[u] ? seg - row[u] * ngroups : 0;
     if (live[u]) {
-      load_vec<TX, VEC>(x + row[u] * sx + grp[u] * G + li * VEC, xv[u]);
-      if constexpr (HAS_Z) load_vec<TX, VEC>(z + row[u] * sz + grp[u] * G + li * VEC, zv[u]);
+      xr[u] = __ldg(reinterpret_cast<const uint4*>(x + row[u] * sx + grp[u] * G + li * VEC));
+      if constexpr (HAS_Z)
+        zr[u] = __ldg(reinterpret_cast<const uint4*>(z + row[u] * sz + grp[u] * G + li * VEC));
+    } else {
+      xr[u] = make_uint4(0, 0, 0, 0);
+      zr[u] = make_uint4(0, 0, 0, 0);
     }
   }
 #pragma unroll
   for (int u = 0; u < UNROLL; ++u) {
+    float xv[1][VEC], zv[1][VEC];
+    {
+      const TX* ex = reinterpret_cast<const TX*>(&xr[u]);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) xv[0][i] = to_f32<TX>(ex[i]);
+      if constexpr (HAS_Z) {
+        const TX* ez = reinterpret_cast<const TX*>(&zr[u]);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) zv[0][i] = to_f32<TX>(ez[i]);
+      }
+    }
     if constexpr (HAS_Z) {
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) zv[u][i] = zv[u][i] * sigmoid_f(zv[u][i]);
+      for (int i = 0; i < VEC; ++i) zv[0][i] = zv[0][i] * sigmoid_f(zv[0][i]);
       if (!norm_before_gate) {
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) xv[u][i] *= zv[u][i];
+        for (int i = 0; i < VEC; ++i) xv[0][i] *= zv[0][i];
       }
     }
     float mu = 0.f;
     if constexpr (!RMS) {
       float s = 0.f;
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) s += xv[u][i];
+      for (int i = 0; i < VEC; ++i) s += xv[0][i];
 #pragma unroll
       for (int o = LPR / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
       mu = s * (1.0f / G);
@@ -134,7 +150,7 @@ __global__ void __launch_bounds__(256) layer_norm_packed_kernel(
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
-      const float d = xv[u][i] - mu;
+      const float d = xv[0][i] - mu;
       ss += d * d;
     }
 #pragma unroll
@@ -150,10 +166,10 @@ __global__ void __launch_bounds__(256) layer_norm_packed_kernel(
     if constexpr (HAS_B) load_vec<TW, VEC>(b + grp[u] * G + li * VEC, bv);
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
-      float t = (xv[u][i] - mu) * rstd * wv[i];
+      float t = (xv[0][i] - mu) * rstd * wv[i];
       if constexpr (HAS_B) t += bv[i];
       if constexpr (HAS_Z) {
-        if (norm_before_gate) t *= zv[u][i];
+        if (norm_before_gate) t *= zv[0][i];
       }
       out[i] = t;
     }

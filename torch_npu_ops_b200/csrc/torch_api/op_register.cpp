@@ -1,0 +1,98 @@
+// Python module of the C++ torch API.  The first two functions keep the
+// schemas of the reference's pybind module npu_python_extension_lib
+// (npu_python_extension/op_register.cpp:52-63); the rest expose the
+// xllm::kernel::npu operators and the runtime registry.
+#include <torch/extension.h>
+
+#include "../runtime/kernel_registry.h"
+#include "ascendc_ops_api.h"
+#include "triton_ops_api.h"
+
+namespace py = pybind11;
+namespace xn = xllm::kernel::npu;
+
+namespace {
+
+std::tuple<torch::Tensor, torch::Tensor> py_gemma_rms_norm(const torch::Tensor& x,
+                                                           const torch::Tensor& gamma,
+                                                           double epsilon) {
+  torch::Tensor rstd, y;
+  npu_ops::npu_gemma_rms_norm(x, gamma, epsilon, rstd, y);
+  return std::make_tuple(rstd, y);
+}
+
+torch::Tensor py_layer_norm_fwd(const torch::Tensor& x, const torch::Tensor& weight,
+                                const c10::optional<torch::Tensor>& bias, double eps,
+                                const c10::optional<torch::Tensor>& z, int64_t group_size,
+                                bool norm_before_gate, bool is_rms_norm) {
+  return npu_ops::layer_norm_fwd(x, weight, bias, eps, z, group_size, norm_before_gate,
+                                 is_rms_norm);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("gemma_rms_norm", &py_gemma_rms_norm, "Gemma RMSNorm -> (rstd, y)");
+  m.def("layer_norm_fwd", &py_layer_norm_fwd, "grouped LayerNorm/RMSNorm with SiLU gate",
+        py::arg("x"), py::arg("weight"), py::arg("bias"), py::arg("eps"), py::arg("z"),
+        py::arg("group_size"), py::arg("norm_before_gate"), py::arg("is_rms_norm"));
+  m.def("npu_l2norm_last_dim",
+        [](torch::Tensor x, double eps) { return xn::npu_l2norm_last_dim(x, eps); },
+        py::arg("x"), py::arg("eps") = 1e-6);
+  m.def("npu_split_rmsnorm_rope",
+        [](torch::Tensor input, torch::Tensor sin, torch::Tensor cos, torch::Tensor qw,
+           torch::Tensor kw, int64_t qh, int64_t kvh, int64_t hd, double eps,
+           std::optional<torch::Tensor> qb, std::optional<torch::Tensor> kb, bool bias) {
+          return xn::npu_split_rmsnorm_rope(input, sin, cos, qw, kw, qh, kvh, hd, eps, qb, kb,
+                                            bias);
+        },
+        py::arg("input"), py::arg("sin"), py::arg("cos"), py::arg("q_weight"),
+        py::arg("k_weight"), py::arg("q_hidden_size"), py::arg("kv_hidden_size"),
+        py::arg("head_dim"), py::arg("eps"), py::arg("q_bias") = py::none(),
+        py::arg("k_bias") = py::none(), py::arg("bias") = false);
+  m.def("npu_causal_conv1d_update",
+        [](torch::Tensor x, torch::Tensor st, torch::Tensor w, bool act,
+           std::optional<torch::Tensor> b, std::optional<torch::Tensor> idx, int32_t pad) {
+          return xn::npu_causal_conv1d_update(x, st, w, act, b, std::nullopt, idx, std::nullopt,
+                                              std::nullopt, -1, std::nullopt, pad, false);
+        },
+        py::arg("x"), py::arg("conv_state"), py::arg("weight"), py::arg("activation") = true,
+        py::arg("bias") = py::none(), py::arg("conv_state_indices") = py::none(),
+        py::arg("pad_slot_id") = -1);
+  m.def("npu_causal_conv1d_update_v2",
+        [](torch::Tensor x, torch::Tensor st, torch::Tensor w, bool act,
+           std::optional<torch::Tensor> b, std::optional<torch::Tensor> idx,
+           std::optional<torch::Tensor> qsl, int32_t max_q, int32_t pad) {
+          return xn::npu_causal_conv1d_update_v2(x, st, w, act, b, idx, qsl, max_q, pad);
+        },
+        py::arg("x"), py::arg("conv_state"), py::arg("weight"), py::arg("activation") = true,
+        py::arg("bias") = py::none(), py::arg("conv_state_indices") = py::none(),
+        py::arg("query_start_loc") = py::none(), py::arg("max_query_len") = -1,
+        py::arg("pad_slot_id") = -1);
+  m.def("npu_fused_recurrent_gated_delta_rule",
+        [](torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
+           std::optional<torch::Tensor> beta, std::optional<float> scale,
+           std::optional<torch::Tensor> h0, bool inplace, std::optional<torch::Tensor> cu,
+           std::optional<torch::Tensor> idx, bool l2) {
+          return xn::npu_fused_recurrent_gated_delta_rule(q, k, v, g, beta, scale, h0, inplace,
+                                                          cu, idx, std::nullopt, l2);
+        },
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("g"), py::arg("beta") = py::none(),
+        py::arg("scale") = py::none(), py::arg("initial_state") = py::none(),
+        py::arg("inplace_final_state") = true, py::arg("cu_seqlens") = py::none(),
+        py::arg("ssm_state_indices") = py::none(), py::arg("use_qk_l2norm_in_kernel") = false);
+  m.def("npu_chunk_gated_delta_rule",
+        [](torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+           std::optional<float> scale, std::optional<torch::Tensor> h0, bool out_final,
+           std::optional<torch::Tensor> cu, bool head_first, bool l2) {
+          return xn::npu_chunk_gated_delta_rule(q, k, v, g, beta, scale, h0, out_final, cu,
+                                                head_first, l2);
+        },
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("g"), py::arg("beta"),
+        py::arg("scale") = py::none(), py::arg("initial_state") = py::none(),
+        py::arg("output_final_state") = false, py::arg("cu_seqlens") = py::none(),
+        py::arg("head_first") = false, py::arg("use_qk_l2norm_in_kernel") = false);
+  m.def("kernel_entry_point", [](const std::string& name) {
+    return xn::KernelRegistry::get_instance().entry_point(name);
+  });
+}
