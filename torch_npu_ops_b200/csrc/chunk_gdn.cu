@@ -9,7 +9,7 @@
 //                                                  value heads of the key head)
 //      A    = strict_tril(beta_i D_ij (k k^T)_ij),  D_ij = e^{gc_i - gc_j}
 //      T    = (I + A)^-1                          (blocked, fp32, CUDA cores)
-//      T'   = (T - I) diag(beta)                  -> workspace (bf16)
+//      T'   = T diag(beta)                        -> workspace (bf16)
 //      w    = T diag(beta e^{gc}) k               (MMA)   -> workspace (bf16)
 //      Aqk  = tril(q k^T * D)                     -> workspace (bf16)
 //    per value head, where gc is the in-chunk cumsum of g.
@@ -18,10 +18,10 @@
 //    chunks in order.  Warp-specialised: warp 0 prefetches the next chunk's
 //    tiles (k, q, v from the inputs; w, T', Aqk from the workspace) into a
 //    second stage with cp.async; warp 1 issues every MMA from one thread;
-//    warps 2-9 hold the fp32 state S^T[v][kk] in registers (64 values per
+//    warps 2-17 hold the fp32 state S^T[v][kk] in registers (32 values per
 //    thread) and run the epilogues.  Per chunk:
-//      D_u   = v^T T'^T             (issued one chunk ahead)
-//      D_u  += S^T (-w)^T           (so v_new^T = D_u + beta_i v_i, fp32)
+//      D_u   = v^T T'^T + v^T diag(beta - bf16(beta))   (issued one chunk ahead)
+//      D_u  += S^T (-w)^T           (so v_new^T = D_u, beta_i v_i kept fp32)
 //      D_qh  = S^T q^T
 //      dS    = vt_hi^T k + vt_lo^T k,  vt = v_new e^{gc_last - gc} split bf16 hi+lo
 //      D_o   = e^{gc} D_qh + v_new^T Aqk^T
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
         for (int u = 0; u < 8; ++u) {
           const int j = cc * 8 + u;
           const float tv = ft[i * LDF + j] * bet[j];
-          tp[u] = (i == j) ? 0.f : tv;
+          tp[u] = tv;  // diagonal = bf16(beta_i); the chain adds beta_i - bf16(beta_i)
           tpp[u] = tv * egc[j];
         }
         uint4 a, b;
@@ -315,14 +315,19 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
 // ============================================================================
 // Kernel 2: the chunk chain
 // ============================================================================
-constexpr int C_NT = 320;                 // 10 warps: producer, MMA, 8 epilogue
+constexpr int C_EPI_WARPS = 16;           // epilogue warps: 4 per TMEM lane quarter
+constexpr int C_NT = 32 * (2 + C_EPI_WARPS);  // producer, MMA, epilogue
+constexpr int C_EPI_THREADS = 32 * C_EPI_WARPS;
+constexpr int C_SCOLS = 128 / (C_EPI_WARPS / 4);  // state columns per epilogue thread
+constexpr int C_TCOLS = 64 / (C_EPI_WARPS / 4);   // token columns per epilogue thread
 constexpr int STAGE = 81920;              // bytes per pipeline stage
 constexpr int S_K = 0, S_Q = 16384, S_V = 32768, S_W = 49152, S_TP = 65536, S_AQK = 73728;
 constexpr int C_OFF_HT = 2 * STAGE;       // S^T bf16 [128 x 128], halves 16 KB apart
 constexpr int C_OFF_VTH = C_OFF_HT;       // aliases HT (disjoint lifetimes)
 constexpr int C_OFF_VTL = C_OFF_HT + 16384;
 constexpr int C_OFF_VN = C_OFF_HT + 32768;
-constexpr int C_OFF_GB = C_OFF_VN + 16384;  // per stage: g[64], beta[64]
+constexpr int C_OFF_TPL = C_OFF_VN + 16384;   // diag(beta - bf16(beta)) [64 x 64]
+constexpr int C_OFF_GB = C_OFF_TPL + 8192;    // per stage: g[64], beta[64]
 constexpr int C_OFF_TAB = C_OFF_GB + 2 * 512; // gc[64], e^gc[64], e^{gl-gc}[64]
 constexpr int C_SMEM = C_OFF_TAB + 3 * 256 + 1024;
 constexpr uint32_t C_TM_U = 0, C_TM_QH = 64, C_TM_O = 128, C_TM_DS = 256, C_TM_COLS = 512;
@@ -385,6 +390,8 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     tc::mbar_fence_init();
     abort_sh = 0;
   }
+  for (int e = tid; e < 8192 / 16; e += C_NT)  // diagonal-correction tile starts at zero
+    reinterpret_cast<uint4*>(sm + C_OFF_TPL)[e] = make_uint4(0, 0, 0, 0);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -429,11 +436,25 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       const uint32_t id_vn = tc::idesc_bf16(128, 64, false, false, true);
       const uint32_t id_qh = tc::idesc_bf16(128, 64, false, false);
       const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
+      // D_u = v^T T'^T with T' = T diag(beta) in bf16, plus v^T diag(beta -
+      // bf16(beta)): the unit diagonal's beta_i v_i term is exact to ~2^-17.
+      // The correction tile's previous use (M_u of the last chunk) finished
+      // before this thread saw bar_vt, so its diagonal can be rewritten here.
       auto issue_u = [&](int c) {
         const uint32_t st = sb + (c & 1) * STAGE;
+        const float* bt = reinterpret_cast<const float*>(sm + C_OFF_GB + (c & 1) * 512) + 64;
+        for (int i = 0; i < 64; ++i) {
+          const float b = bt[i];
+          *reinterpret_cast<bf16*>(sm + C_OFF_TPL + elem_off(i, i, 8192)) =
+              __float2bfloat16_rn(b - __bfloat162float(__float2bfloat16_rn(b)));
+        }
+        tc::fence_proxy_async();
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           tc::mma_bf16(tm + C_TM_U, mndesc(st + S_V, 8192, j), kdesc64(st + S_TP, j), id_u, j > 0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::mma_bf16(tm + C_TM_U, mndesc(st + S_V, 8192, j), kdesc64(sb + C_OFF_TPL, j), id_u, true);
       };
       bool live = tc::mbar_wait(&full[0], 0, WAIT_LIMIT);
       if (live) issue_u(0);
@@ -478,26 +499,26 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     }
   } else {
     // ------------------------------------------------------------ epilogue warps
-    const int cw = warp - 2;             // 0..7 (warps 2-9 cover each lane quarter twice)
+    const int cw = warp - 2;             // 0..15: four warps per TMEM lane quarter
     const int quarter = warp & 3;        // TMEM lane quarter
-    const int colhalf = cw >> 2;         // 0/1
+    const int colq = cw >> 2;            // which quarter of the columns this warp owns
     const int vrow = quarter * 32 + lane;
-    const int kc0 = colhalf * 64;        // state columns owned
-    const int tc0 = colhalf * 32;        // token columns owned in 64-wide regions
+    const int kc0 = colq * C_SCOLS;      // state columns owned
+    const int tc0 = colq * C_TCOLS;      // token columns owned in 64-wide regions
     float* gcs = reinterpret_cast<float*>(sm + C_OFF_TAB);  // gc, e^gc, e^{gl-gc}
     float* egc = gcs + 64;
     float* edc = gcs + 128;
-    float S[64];
+    float S[C_SCOLS];
     {
       const float* src = h0 ? h0 + ((int64_t)n * H + h) * K * V : nullptr;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) S[i] = src ? src[(kc0 + i) * V + vrow] : 0.f;
+      for (int i = 0; i < C_SCOLS; ++i) S[i] = src ? src[(kc0 + i) * V + vrow] : 0.f;
     }
     float gl_prev = 0.f;
     int L_prev = 0;
     int64_t t0_prev = 0;
     bool live = true;
-    auto sync_chain = [&]() { tc::named_sync(1, 256); };
+    auto sync_chain = [&]() { tc::named_sync(1, C_EPI_THREADS); };
     auto wait_uniform = [&](uint64_t* b, uint32_t par) -> bool {
       const bool ok = tc::mbar_wait(b, par, WAIT_LIMIT);
       if (!ok) {
@@ -508,22 +529,20 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       sync_chain();
       return *(volatile int*)&abort_sh == 0;
     };
+    static_assert(C_TCOLS == 16 && C_SCOLS == 32, "epilogue tiling assumes 16 warps");
     auto write_out = [&](int64_t tb, int Lc) {  // o = scale * D_o (previous chunk)
+      float ov[16];
+      tc::tmem_ld16(tm_addr(tm, quarter, C_TM_O + tc0), ov);
+      tc::tmem_wait_ld();
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float ov[16];
-        tc::tmem_ld16(tm_addr(tm, quarter, C_TM_O + tc0 + half * 16), ov);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int i = tc0 + half * 16 + c;
-          if (i < Lc) o[(tb + i) * (H * V) + (int64_t)h * V + vrow] = __float2bfloat16_rn(ov[c] * scale);
-        }
+      for (int c = 0; c < 16; ++c) {
+        const int i = tc0 + c;
+        if (i < Lc) o[(tb + i) * (H * V) + (int64_t)h * V + vrow] = __float2bfloat16_rn(ov[c] * scale);
       }
     };
     auto apply_ds = [&](float dl) {  // S = e^{gl} S + dS
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
+      for (int cb = 0; cb < 2; ++cb) {
         float d[16];
         tc::tmem_ld16(tm_addr(tm, quarter, C_TM_DS + kc0 + cb * 16), d);
         tc::tmem_wait_ld();
@@ -533,14 +552,14 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     };
     for (int c = 0; c < NC && live; ++c) {
       const int s = c & 1;
-      const unsigned char* st = sm + s * STAGE;
+      (void)s;
       if (c > 0) {
         if (!(live = wait_uniform(&bar_so, (c - 1) & 1))) break;
         apply_ds(__expf(gl_prev));
       }
       // E0: bf16 S^T -> HT, then let the MMA warp go
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
+      for (int m = 0; m < C_SCOLS / 8; ++m) {
         uint4 pk;
         pk.x = pack_bf16(S[8 * m + 0], S[8 * m + 1]);
         pk.y = pack_bf16(S[8 * m + 2], S[8 * m + 3]);
@@ -573,12 +592,10 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       sync_chain();
       const float gl = gcs[L - 1];
       if (!(live = wait_uniform(&bar_vq, c & 1))) break;
-      // E1: v_new, vt hi/lo, o_inter (16 tokens at a time)
+      // E1: v_new (= D_u, exact diagonal included), vt hi/lo, o_inter
       {
-        const float* bet = gb + 64;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int tb = tc0 + half * 16;
+        {
+          const int tb = tc0;
           float du[16], qh[16];
           tc::tmem_ld16(tm_addr(tm, quarter, C_TM_U + tb), du);
           tc::tmem_ld16(tm_addr(tm, quarter, C_TM_QH + tb), qh);
@@ -589,9 +606,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const int i = tb + cc + u;
-              const float vi = __bfloat162float(
-                  *reinterpret_cast<const bf16*>(st + S_V + elem_off(i, vrow, 8192)));
-              vn[u] = fmaf(bet[i], vi, du[cc + u]);
+              vn[u] = du[cc + u];
               const float sc = vn[u] * edc[i];
               th[u] = __bfloat162float(__float2bfloat16_rn(sc));
               tl[u] = sc - th[u];
@@ -630,7 +645,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     if (live && ht) {
       float* dst = ht + ((int64_t)n * H + h) * K * V;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) dst[(kc0 + i) * V + vrow] = S[i];
+      for (int i = 0; i < C_SCOLS; ++i) dst[(kc0 + i) * V + vrow] = S[i];
     }
   }
   tc::fence_before();
