@@ -78,6 +78,54 @@ def test_chunk_varlen_edges(lens, hk, hv, l2, h0):
     assert_state(ht.cpu()[keep], rh[keep])
 
 
+def _segmented(B, T, N, hk, hv, varlen):
+    """True when the host plan cuts the chain into segments (the workspace
+    then carries segment states beyond the per-chunk part)."""
+    from torch_npu_ops_b200 import _lib
+    lib = _lib.load()
+    chunks = T // 64 + N if varlen else B * ((T + 63) // 64)
+    return lib.xops_chunk_gated_delta_rule_workspace_size(B, T, N, hk, hv, 128, 0, int(varlen)) > \
+        chunks * hv * 32768
+
+
+@pytest.mark.parametrize("lens,hk,hv,l2", [
+    ([8192], 1, 2, False),                     # one long sequence: 16 segments of 8 chunks
+    ([5000, 130, 64, 1, 0, 3000], 1, 2, True),  # long and short sequences share the plan
+    ([16384], 2, 4, False),                    # GQA, longer segments
+])
+def test_chunk_segmented_chain(lens, hk, hv, l2):
+    """Long sequences on few heads run as local / transition / output passes
+    over segments plus a combine of the segment states; results match the
+    serial recurrence of the oracle."""
+    assert _segmented(1, sum(lens), len(lens), hk, hv, True)
+    inp = workloads.chunk_config3(hk=hk, hv=hv, lengths=lens, seed=len(lens) + hv)
+    o, ht = ops.npu_chunk_gated_delta_rule(
+        _to(inp["q"]), _to(inp["k"]), _to(inp["v"]), _to(inp["g"]), _to(inp["beta"]), None,
+        _to(inp["initial_state"]), True, _to(inp["cu_seqlens"]), False, l2)
+    ro, rh = oracle.chunk_gated_delta_rule(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"],
+                                           None, inp["initial_state"], True, inp["cu_seqlens"], l2)
+    assert_bf16(o, ro)
+    assert_state(ht, rh)
+
+
+def test_chunk_segmented_batched_no_cu():
+    """Equal-length batch without cu_seqlens on the segmented plan."""
+    B, T, hk, hv = 2, 4096, 1, 2
+    assert _segmented(B, T, B, hk, hv, False)
+    g = torch.Generator().manual_seed(21)
+    q = F.normalize(torch.randn(B, T, hk, 128, generator=g), dim=-1).to(torch.bfloat16)
+    k = F.normalize(torch.randn(B, T, hk, 128, generator=g), dim=-1).to(torch.bfloat16)
+    v = torch.randn(B, T, hv, 128, generator=g).to(torch.bfloat16)
+    gate, beta = workloads.gdn_gates(B * T, hv, g)
+    gate, beta = gate.reshape(B, T, hv), beta.reshape(B, T, hv)
+    h0 = 0.02 * torch.randn(B, hv, 128, 128, generator=g)
+    o, ht = ops.npu_chunk_gated_delta_rule(_to(q), _to(k), _to(v), _to(gate), _to(beta), None,
+                                           _to(h0), True, None)
+    ro, rh = oracle.chunk_gated_delta_rule(q, k, v, gate, beta, None, h0, True, None)
+    assert_bf16(o, ro)
+    assert_state(ht, rh)
+
+
 def test_chunk_batched_no_cu_and_scale():
     g = torch.Generator().manual_seed(21)
     B, T = 3, 150

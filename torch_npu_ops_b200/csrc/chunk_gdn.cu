@@ -10,7 +10,7 @@
 //      A    = strict_tril(beta_i D_ij (k k^T)_ij),  D_ij = e^{gc_i - gc_j}
 //      T    = (I + A)^-1                          (blocked, fp32, CUDA cores)
 //      T'   = T diag(beta)                        -> workspace (bf16)
-//      w    = T diag(beta e^{gc}) k               (MMA)   -> workspace (bf16)
+//      -w   = -T diag(beta e^{gc}) k              (MMA)   -> workspace (bf16)
 //      Aqk  = tril(q k^T * D)                     -> workspace (bf16)
 //    per value head, where gc is the in-chunk cumsum of g.
 //
@@ -36,6 +36,9 @@
 //
 // Every wait is a bounded mbarrier poll: on timeout the CTA records an
 // error in a device flag (xops_device_error_count) and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "gdn_common.cuh"
 #include "tcgen05.cuh"
 
@@ -84,17 +87,6 @@ __device__ __forceinline__ void cp_tile128(unsigned char* dst, uint32_t half_str
                ok ? 16 : 0);
   }
 }
-// [64 x 64] bf16 row-major (contiguous) -> SW128 64-wide tile
-__device__ __forceinline__ void cp_tile64(unsigned char* dst, const bf16* src, int t, int nthr) {
-  for (int e = t; e < 64 * 8; e += nthr) {
-    const int r = e >> 3, c = e & 7;
-    cp_async16(dst + (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)), src + r * 64 + c * 8, 16);
-  }
-}
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, int src_bytes) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem),
-               "r"(src_bytes));
-}
 
 // ============================================================================
 // q/k L2 normalisation pre-pass: x / sqrt(sum x^2 + 1e-6) per 128-wide head,
@@ -132,7 +124,7 @@ constexpr int P_OFF_G = P_OFF_FM + 32 * 33 * 4;  // graw, gc, beta, e^gc
 constexpr int P_SMEM = P_OFF_G + 4 * 64 * 4 + 1024;
 constexpr uint32_t P_TM_G = 0, P_TM_W = 64, P_TM_COLS = 128;
 
-__global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
+__global__ void __launch_bounds__(P_NT, 3) chunk_prep_kernel(
     const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
     const float* __restrict__ beta, unsigned char* __restrict__ ws,
     const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H,
@@ -238,7 +230,6 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
       } else {
         const int i = row - 64;
         const float gi = gcs[i];
-        bf16* aq = reinterpret_cast<bf16*>(wsb + WS_AQK) + i * 64 + c0;
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
           float e[8];
@@ -250,7 +241,7 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
           uint4 pk;
           pk.x = pack_bf16(e[0], e[1]); pk.y = pack_bf16(e[2], e[3]);
           pk.z = pack_bf16(e[4], e[5]); pk.w = pack_bf16(e[6], e[7]);
-          *reinterpret_cast<uint4*>(aq + c) = pk;
+          *reinterpret_cast<uint4*>(wsb + WS_AQK + chunk_off(i, (c0 + c) >> 3, 0)) = pk;
         }
       }
     }
@@ -259,7 +250,6 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
       float* ft = reinterpret_cast<float*>(sm + P_OFF_FA);
       float* fm = reinterpret_cast<float*>(sm + P_OFF_FM);
       tri_inverse_64_inplace(ft, fm, tid);
-      bf16* tpg = reinterpret_cast<bf16*>(wsb + WS_TP);
       for (int e = tid; e < 64 * 8; e += P_NT) {
         const int i = e >> 3, cc = e & 7;
         float tp[8], tpp[8];
@@ -275,7 +265,7 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
         a.z = pack_bf16(tp[4], tp[5]); a.w = pack_bf16(tp[6], tp[7]);
         b.x = pack_bf16(tpp[0], tpp[1]); b.y = pack_bf16(tpp[2], tpp[3]);
         b.z = pack_bf16(tpp[4], tpp[5]); b.w = pack_bf16(tpp[6], tpp[7]);
-        *reinterpret_cast<uint4*>(tpg + i * 64 + cc * 8) = a;
+        *reinterpret_cast<uint4*>(wsb + WS_TP + chunk_off(i, cc, 0)) = a;
         *reinterpret_cast<uint4*>(sm + P_OFF_TPP + (uint32_t)(i * 128 + ((cc ^ (i & 7)) << 4))) = b;
       }
     }
@@ -293,15 +283,20 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
     }
     wait_mma();
     if (!alive) break;
-    {  // w [t][kk] (bf16, row-major) from w^T in TMEM (lane = kk)
+    {  // -w [t][kk] (bf16, row-major) from w^T in TMEM (lane = kk); stored
+       // negated so the chain forms [-w; q] S in one N = 128 product
       const int kk = quarter * 32 + lane;
       const int c0 = colhalf * 32;
       float vals[32];
       tc::tmem_ld32(tm_addr(tm, quarter, P_TM_W + c0), vals);
       tc::tmem_wait_ld();
-      bf16* wg = reinterpret_cast<bf16*>(wsb + WS_W);
+      // c0 is a multiple of 8, so the swizzle of token c0 + c depends on c & 7 only
+      unsigned char* wrow = wsb + WS_W + (kk >> 6) * 8192 + (kk & 7) * 2 + c0 * 128;
+      const int kc = (kk & 63) >> 3;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) wg[(c0 + c) * 128 + kk] = __float2bfloat16_rn(vals[c]);
+      for (int c = 0; c < 32; ++c)
+        *reinterpret_cast<bf16*>(wrow + c * 128 + ((kc ^ (c & 7)) << 4)) =
+            __float2bfloat16_rn(-vals[c]);
     }
     tc::fence_before();
     __syncthreads();
@@ -317,59 +312,147 @@ __global__ void __launch_bounds__(P_NT) chunk_prep_kernel(
 // ============================================================================
 constexpr int C_EPI_WARPS = 16;           // epilogue warps: 4 per TMEM lane quarter
 constexpr int C_NT = 32 * (2 + C_EPI_WARPS);  // producer, MMA, epilogue
-constexpr int C_EPI_THREADS = 32 * C_EPI_WARPS;
 constexpr int C_SCOLS = 128 / (C_EPI_WARPS / 4);  // state columns per epilogue thread
 constexpr int C_TCOLS = 64 / (C_EPI_WARPS / 4);   // token columns per epilogue thread
 constexpr int STAGE = 81920;              // bytes per pipeline stage
-constexpr int S_K = 0, S_Q = 16384, S_V = 32768, S_W = 49152, S_TP = 65536, S_AQK = 73728;
-constexpr int C_OFF_HT = 2 * STAGE;       // S^T bf16 [128 x 128], halves 16 KB apart
-constexpr int C_OFF_VTH = C_OFF_HT;       // aliases HT (disjoint lifetimes)
-constexpr int C_OFF_VTL = C_OFF_HT + 16384;
-constexpr int C_OFF_VN = C_OFF_HT + 32768;
-constexpr int C_OFF_TPL = C_OFF_VN + 16384;   // diag(beta - bf16(beta)) [64 x 64]
-constexpr int C_OFF_GB = C_OFF_TPL + 8192;    // per stage: g[64], beta[64]
-constexpr int C_OFF_TAB = C_OFF_GB + 2 * 512; // gc[64], e^gc[64], e^{gl-gc}[64]
-constexpr int C_SMEM = C_OFF_TAB + 3 * 256 + 1024;
-constexpr uint32_t C_TM_U = 0, C_TM_QH = 64, C_TM_O = 128, C_TM_DS = 256, C_TM_COLS = 512;
+// WQ: one [128 x 128] SW128 tile, halves 16 KB apart: rows 0-63 = -w, 64-127 = q.
+constexpr int S_K = 0, S_WQ = 16384, S_V = 49152, S_TP = 65536, S_AQK = 73728;
+constexpr int C_OFF_TPL = 2 * STAGE;          // diag(beta - bf16(beta)) [64 x 64]
+constexpr int C_OFF_TAB = C_OFF_TPL + 8192;   // 4 slots (chunk & 3): e^{gl-gc}[64], e^{gc}[64], gl
+constexpr int C_TAB = 1024;
+constexpr int C_OFF_OST = C_OFF_TAB + 4 * C_TAB;  // output transpose: [warp][16 x 32] bf16
+constexpr int C_SMEM = C_OFF_OST + C_EPI_WARPS * 2048 + 1024;
+// TMEM columns.  fp32 accumulators: D_u, D_qh (adjacent: one N = 128 product
+// fills both), D_o, dS.  bf16 A operands written by the epilogue (packed in
+// pairs, so a [128 x K] operand takes K/2 columns): S^T, vt hi, vt lo, v_new.
+constexpr uint32_t C_TM_U = 0, C_TM_QH = 64, C_TM_O = 128, C_TM_HT = 192, C_TM_DS = 256,
+                   C_TM_VTH = 384, C_TM_VTL = 416, C_TM_VN = 448, C_TM_COLS = 512;
+constexpr int KV = 128 * 128;
 
+// Work of one chain CTA.  A CTA walks chunks [c0, c1) of one (sequence,
+// value head) starting from a given state:
+//   ITEM_OUT    the real recurrence, writing o (and the end state if asked)
+//   ITEM_LOCAL  the recurrence from a zero state, no output: the segment's
+//               additive part B
+//   ITEM_TRANS  the recurrence from the identity with v = 0, no output: the
+//               segment's transition X, so that S_end^T = S_start^T X + B^T
+enum : int { ITEM_OUT = 0, ITEM_LOCAL = 1, ITEM_TRANS = 2 };
+
+// Segment-parallel schedule for long sequences.  seg = 0: one ITEM_OUT per
+// (sequence, head), longest sequences first.  seg > 0: every sequence is cut
+// into segments of `seg` chunks; phase 1 runs segment 0 (ITEM_OUT) and the
+// LOCAL / TRANS items of the middle segments; chunk_combine_kernel chains the
+// segment start states; phase 3 runs segments 1.. with outputs.
+struct ChainPlan {
+  int seg;
+  int phase;
+  float* scratch;  // [slot][H][3][K*V]: start state, B, X (slot = segment index over all sequences)
+};
+
+__device__ __forceinline__ float* seg_state(const ChainPlan& p, int64_t slot, int64_t H, int h,
+                                            int which) {
+  return p.scratch + ((slot * H + h) * 3 + which) * (int64_t)KV;
+}
+__device__ __forceinline__ int seq_chunks(const int32_t* cu, int64_t n, int64_t T) {
+  int64_t bos, eos;
+  seq_span(cu, n, T, bos, eos);
+  return (int)((eos - bos + BT - 1) / BT);
+}
+
+// q, k, v are read through 2-D tensor maps (rows = tokens, 64 x 64 boxes,
+// 128-byte swizzle): the box lands exactly as one half of an SW128 tile.
 __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
-    const float* __restrict__ g, const float* __restrict__ beta, const float* __restrict__ h0,
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ g,
+    const float* __restrict__ beta, const float* __restrict__ h0,
     const unsigned char* __restrict__ ws, bf16* __restrict__ o, float* __restrict__ ht,
-    const int32_t* __restrict__ cu, int64_t T, int64_t Hg, int64_t H, int64_t q_stride,
-    int64_t k_stride, int64_t v_stride, float scale) {
+    const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H, float scale,
+    ChainPlan plan) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  __shared__ uint64_t full[2], empty[2], bar_ht, bar_vq, bar_vt, bar_so;
+  __shared__ uint64_t full[2], empty[2], early_free[2], tma[2], bar_ht, bar_v, bar_q, bar_vt,
+      bar_s, bar_o, bar_od, bar_fin;
   __shared__ uint32_t tmem_sh;
   __shared__ int abort_sh;
-  __shared__ int64_t seq_sh;
+  __shared__ int64_t it_n;
+  __shared__ int it_valid, it_kind, it_c0, it_c1;
+  __shared__ const float* it_init;
+  __shared__ float* it_out;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // Longest sequences first: CTA rank r serves the r-th longest sequence
-  // (ties by index), so the longest chains start in the first wave.
-  const int64_t rank = blockIdx.x / H;
-  const int h = (int)(blockIdx.x - rank * H);
-  if (!cu) {
-    if (tid == 0) seq_sh = rank;
-  } else {
-    const int64_t nseq = gridDim.x / H;
-    for (int64_t j = tid; j < nseq; j += blockDim.x) {
-      const int64_t lj = (int64_t)cu[j + 1] - cu[j];
-      int64_t r = 0;
-      for (int64_t m = 0; m < nseq; ++m) {
-        const int64_t lm = (int64_t)cu[m + 1] - cu[m];
-        r += (lm > lj) || (lm == lj && m < j);
+  const int64_t idx = blockIdx.x / H;
+  const int h = (int)(blockIdx.x - idx * H);
+  if (tid == 0) it_valid = 0;
+  __syncthreads();
+  if (plan.seg == 0) {
+    // Longest sequences first: CTA rank r serves the r-th longest sequence
+    // (ties by index), so the longest chains start in the first wave.
+    if (!cu || N > 4096) {
+      if (tid == 0 && idx < N) { it_n = idx; it_valid = 1; }
+    } else {
+      for (int64_t j = tid; j < N; j += blockDim.x) {
+        const int64_t lj = (int64_t)cu[j + 1] - cu[j];
+        int64_t r = 0;
+        for (int64_t m = 0; m < N; ++m) {
+          const int64_t lm = (int64_t)cu[m + 1] - cu[m];
+          r += (lm > lj) || (lm == lj && m < j);
+        }
+        if (r == idx) { it_n = j; it_valid = 1; }
       }
-      if (r == rank) seq_sh = j;
+    }
+    __syncthreads();
+    if (tid == 0 && it_valid) {
+      const int64_t n = it_n;
+      it_kind = ITEM_OUT;
+      it_c0 = 0;
+      it_c1 = seq_chunks(cu, n, T);
+      it_init = h0 ? h0 + (n * H + h) * KV : nullptr;
+      it_out = ht ? ht + (n * H + h) * KV : nullptr;
+    }
+  } else if (tid == 0) {
+    int64_t acc = 0, slot = 0;
+    for (int64_t n = 0; n < N; ++n) {
+      const int nc = seq_chunks(cu, n, T);
+      const int nseg = nc > plan.seg ? (nc + plan.seg - 1) / plan.seg : 1;
+      const int64_t cnt = plan.phase == 1 ? 1 + 2 * (nseg > 2 ? nseg - 2 : 0) : nseg - 1;
+      if (idx < acc + cnt) {
+        const int j = (int)(idx - acc);
+        int s;
+        it_n = n;
+        it_valid = 1;
+        if (plan.phase == 1 && j == 0) {
+          s = 0;
+          it_kind = ITEM_OUT;
+          it_init = h0 ? h0 + (n * H + h) * KV : nullptr;
+          it_out = nseg == 1 ? (ht ? ht + (n * H + h) * KV : nullptr)
+                             : seg_state(plan, slot + 1, H, h, 0);
+        } else if (plan.phase == 1) {
+          s = 1 + (j - 1) / 2;
+          it_kind = ((j - 1) & 1) ? ITEM_TRANS : ITEM_LOCAL;
+          it_init = nullptr;
+          it_out = seg_state(plan, slot + s, H, h, it_kind == ITEM_LOCAL ? 1 : 2);
+        } else {
+          s = 1 + j;
+          it_kind = ITEM_OUT;
+          it_init = seg_state(plan, slot + s, H, h, 0);
+          it_out = s == nseg - 1 ? (ht ? ht + (n * H + h) * KV : nullptr) : nullptr;
+        }
+        it_c0 = s * plan.seg;
+        it_c1 = (s + 1) * plan.seg < nc ? (s + 1) * plan.seg : nc;
+        break;
+      }
+      acc += cnt;
+      slot += nseg;
     }
   }
   __syncthreads();
-  const int64_t n = seq_sh;
+  if (!it_valid) return;  // uniform: spare CTAs of an upper-bound grid
+  const int64_t n = it_n;
+  const int kind = it_kind, c0 = it_c0, NI = it_c1 - it_c0;
+  const bool has_v = kind != ITEM_TRANS, write_o = kind == ITEM_OUT;
   const int hk = (int)(h / (H / Hg));
   int64_t bos, eos;
   seq_span(cu, n, T, bos, eos);
-  const int NC = (int)((eos - bos + BT - 1) / BT);
   const int64_t boh = chunk_offset(cu, n, T);
   const uint32_t sb = tc::smem_addr(sm);
   constexpr int K = 128, V = 128;
@@ -382,11 +465,17 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     for (int s = 0; s < 2; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
+      tc::mbar_init(&early_free[s], 1);
+      tc::mbar_init(&tma[s], 1);
     }
-    tc::mbar_init(&bar_ht, 1);
-    tc::mbar_init(&bar_vq, 1);
-    tc::mbar_init(&bar_vt, 1);
-    tc::mbar_init(&bar_so, 1);
+    tc::mbar_init(&bar_ht, C_EPI_WARPS);
+    tc::mbar_init(&bar_v, 1);
+    tc::mbar_init(&bar_vt, C_EPI_WARPS);
+    tc::mbar_init(&bar_s, 1);
+    tc::mbar_init(&bar_o, C_EPI_WARPS);
+    tc::mbar_init(&bar_od, 1);
+    tc::mbar_init(&bar_q, 1);
+    tc::mbar_init(&bar_fin, 1);
     tc::mbar_fence_init();
     abort_sh = 0;
   }
@@ -399,9 +488,14 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    for (int c = 0; c < NC; ++c) {
-      const int s = c & 1;
-      if (c >= 2 && !tc::mbar_wait(&empty[s], ((c - 2) >> 1) & 1, WAIT_LIMIT)) {
+    // Loads chunk i into stage i & 1, and computes its gate tables and the
+    // diagonal correction tile, so the epilogue and MMA warps only consume.
+    for (int i = 0; i < NI; ++i) {
+      const int s = i & 1, c = c0 + i;
+      // The stage is released in two parts: v, T', -w, q once chunk i-2's
+      // [-w; q] product is done (early_free), k and Aqk once its state and
+      // output products are (empty).
+      if (i >= 2 && !tc::mbar_wait(&early_free[s], ((i - 2) >> 1) & 1, WAIT_LIMIT)) {
         record_error();
         atomicExch(&abort_sh, 1);
       }
@@ -410,45 +504,101 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       const int L = (int)((eos - t0) < BT ? (eos - t0) : BT);
       unsigned char* st = sm + s * STAGE;
       const unsigned char* wsb = ws + ((boh + c) * H + h) * (int64_t)WS_CHUNK;
-      cp_tile128(st + S_K, 8192, k + t0 * k_stride + (int64_t)hk * K, k_stride, L, lane, 32);
-      cp_tile128(st + S_Q, 8192, q + t0 * q_stride + (int64_t)hk * K, q_stride, L, lane, 32);
-      cp_tile128(st + S_V, 8192, v + t0 * v_stride + (int64_t)h * V, v_stride, L, lane, 32);
-      cp_tile128(st + S_W, 8192, reinterpret_cast<const bf16*>(wsb + WS_W), 128, 64, lane, 32);
-      cp_tile64(st + S_TP, reinterpret_cast<const bf16*>(wsb + WS_TP), lane, 32);
-      cp_tile64(st + S_AQK, reinterpret_cast<const bf16*>(wsb + WS_AQK), lane, 32);
-      float* gb = reinterpret_cast<float*>(sm + C_OFF_GB + s * 512);
-      for (int i = lane; i < 64; i += 32) {
-        const bool ok = i < L;
-        const int64_t idx = ok ? (t0 + i) * H + h : 0;
-        cp_async4(gb + i, g + idx, ok ? 4 : 0);
-        cp_async4(gb + 64 + i, beta + idx, ok ? 4 : 0);
+      const int y = (int)t0;
+      if (lane == 0) {
+        // the workspace pieces are stored as shared-memory images already
+        const uint32_t bytes = 32768 + (write_o ? 16384 + 8192 : 0) + (has_v ? 16384 + 8192 : 0);
+        tc::mbar_arrive_expect_tx(&tma[s], bytes);
+        for (int hf = 0; hf < 2; ++hf) {
+          tc::bulk_load(st + S_WQ + hf * 16384, wsb + WS_W + hf * 8192, 8192, &tma[s]);
+          if (write_o)
+            tc::tma_load_2d(st + S_WQ + 8192 + hf * 16384, &tm_q, hk * K + hf * 64, y, &tma[s]);
+          if (has_v) tc::tma_load_2d(st + S_V + hf * 8192, &tm_v, h * V + hf * 64, y, &tma[s]);
+        }
+        if (has_v) tc::bulk_load(st + S_TP, wsb + WS_TP, 8192, &tma[s]);
       }
-      cp_async_commit();
-      cp_async_wait_all();
+      if (i >= 2 && !tc::mbar_wait(&empty[s], ((i - 2) >> 1) & 1, WAIT_LIMIT)) {
+        record_error();
+        atomicExch(&abort_sh, 1);
+      }
+      if (lane == 0 && !*(volatile int*)&abort_sh) {
+        for (int hf = 0; hf < 2; ++hf)
+          tc::tma_load_2d(st + S_K + hf * 8192, &tm_k, hk * K + hf * 64, y, &tma[s]);
+        if (write_o) tc::bulk_load(st + S_AQK, wsb + WS_AQK, 8192, &tma[s]);
+      }
+      // gates of tokens 2*lane, 2*lane+1: in-chunk cumsum (same association
+      // as chunk_cumsum_warp, so it matches the preparation kernel bit for bit)
+      float ga = 0.f, gb2 = 0.f, ba = 0.f, bb = 0.f;
+      const int i0 = 2 * lane;
+      if (i0 < L) {
+        ga = g[(t0 + i0) * H + h];
+        ba = beta[(t0 + i0) * H + h];
+      }
+      if (i0 + 1 < L) {
+        gb2 = g[(t0 + i0 + 1) * H + h];
+        bb = beta[(t0 + i0 + 1) * H + h];
+      }
+      const float pair = ga + gb2;
+      float incl = pair;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const float nb = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += nb;
+      }
+      const float excl = incl - pair;
+      const float gc0 = excl + ga, gc1 = excl + ga + gb2;
+      const float gl = __shfl_sync(0xffffffffu, gc1, 31);
+      float* tab = reinterpret_cast<float*>(sm + C_OFF_TAB + (i & 3) * C_TAB);
+      tab[i0] = __expf(fminf(gl - gc0, 0.f));
+      tab[i0 + 1] = __expf(fminf(gl - gc1, 0.f));
+      tab[64 + i0] = __expf(gc0);
+      tab[64 + i0 + 1] = __expf(gc1);
+      if (lane == 0) tab[128] = gl;
+      if (has_v) {
+        // the previous chunk's D_u product (the last reader of the tile) is
+        // complete once bar_v of that chunk has fired
+        if (i >= 1 && !tc::mbar_wait(&bar_v, (i - 1) & 1, WAIT_LIMIT)) {
+          record_error();
+          atomicExch(&abort_sh, 1);
+        }
+        *reinterpret_cast<bf16*>(sm + C_OFF_TPL + elem_off(i0, i0, 8192)) =
+            __float2bfloat16_rn(ba - __bfloat162float(__float2bfloat16_rn(ba)));
+        *reinterpret_cast<bf16*>(sm + C_OFF_TPL + elem_off(i0 + 1, i0 + 1, 8192)) =
+            __float2bfloat16_rn(bb - __bfloat162float(__float2bfloat16_rn(bb)));
+      }
+      if (!tc::mbar_wait(&tma[s], (i >> 1) & 1, WAIT_LIMIT)) {
+        record_error();
+        atomicExch(&abort_sh, 1);
+        break;
+      }
+      if (L < BT) {
+        // rows past the sequence end came from the next sequence (or the
+        // tensor's zero fill): clear them so the chunk sees only its tokens
+        for (int e = lane; e < (BT - L) * 16; e += 32) {
+          const int r = L + (e >> 4), part = e & 15, hf = part >> 3, c16 = part & 7;
+          const uint32_t off = (uint32_t)(hf * 8192 + r * 128 + c16 * 16);
+          *reinterpret_cast<uint4*>(st + S_K + off) = make_uint4(0, 0, 0, 0);
+          if (has_v) *reinterpret_cast<uint4*>(st + S_V + off) = make_uint4(0, 0, 0, 0);
+          if (write_o)
+            *reinterpret_cast<uint4*>(st + S_WQ + 8192 + hf * 16384 + r * 128 + c16 * 16) =
+                make_uint4(0, 0, 0, 0);
+        }
+      }
       tc::fence_proxy_async();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&full[s]);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && NC > 0) {
+    if (lane == 0 && NI > 0) {
       const uint32_t id_u = tc::idesc_bf16(128, 64, true, false);
-      const uint32_t id_vn = tc::idesc_bf16(128, 64, false, false, true);
-      const uint32_t id_qh = tc::idesc_bf16(128, 64, false, false);
+      const uint32_t id_vq = tc::idesc_bf16(128, 64, false, false);
       const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
+      const uint32_t id_o = tc::idesc_bf16(128, 64, false, false);
       // D_u = v^T T'^T with T' = T diag(beta) in bf16, plus v^T diag(beta -
       // bf16(beta)): the unit diagonal's beta_i v_i term is exact to ~2^-17.
-      // The correction tile's previous use (M_u of the last chunk) finished
-      // before this thread saw bar_vt, so its diagonal can be rewritten here.
-      auto issue_u = [&](int c) {
-        const uint32_t st = sb + (c & 1) * STAGE;
-        const float* bt = reinterpret_cast<const float*>(sm + C_OFF_GB + (c & 1) * 512) + 64;
-        for (int i = 0; i < 64; ++i) {
-          const float b = bt[i];
-          *reinterpret_cast<bf16*>(sm + C_OFF_TPL + elem_off(i, i, 8192)) =
-              __float2bfloat16_rn(b - __bfloat162float(__float2bfloat16_rn(b)));
-        }
-        tc::fence_proxy_async();
+      auto issue_u = [&](int i) {
+        const uint32_t st = sb + (i & 1) * STAGE;
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           tc::mma_bf16(tm + C_TM_U, mndesc(st + S_V, 8192, j), kdesc64(st + S_TP, j), id_u, j > 0);
@@ -456,46 +606,70 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         for (int j = 0; j < 4; ++j)
           tc::mma_bf16(tm + C_TM_U, mndesc(st + S_V, 8192, j), kdesc64(sb + C_OFF_TPL, j), id_u, true);
       };
-      bool live = tc::mbar_wait(&full[0], 0, WAIT_LIMIT);
-      if (live) issue_u(0);
-      for (int c = 0; c < NC && live; ++c) {
-        const int s = c & 1;
+      bool live = true;
+      if (has_v) {
+        live = tc::mbar_wait(&full[0], 0, WAIT_LIMIT);
+        tc::fence_after();
+        if (live) issue_u(0);
+      }
+      for (int i = 0; i < NI && live; ++i) {
+        const int s = i & 1;
         const uint32_t st = sb + s * STAGE;
-        if (!(live = tc::mbar_wait(&bar_ht, c & 1, WAIT_LIMIT))) break;
+        if (!has_v && !(live = tc::mbar_wait(&full[s], (i >> 1) & 1, WAIT_LIMIT))) break;
+        if (!(live = tc::mbar_wait(&bar_ht, i & 1, WAIT_LIMIT))) break;
         tc::fence_after();
-#pragma unroll
+        // D_u (+)= S^T (-w)^T, A = bf16 S^T in TMEM: the state path gets its
+        // own barrier; D_qh = S^T q^T follows while the epilogue forms vt.
+        // (Loops kept rolled so their descriptors are not hoisted into registers.)
+#pragma unroll 1
         for (int j = 0; j < 8; ++j)
-          tc::mma_bf16(tm + C_TM_U, kdesc(sb + C_OFF_HT, 16384, j), kdesc(st + S_W, 8192, j), id_vn,
-                       true);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          tc::mma_bf16(tm + C_TM_QH, kdesc(sb + C_OFF_HT, 16384, j), kdesc(st + S_Q, 8192, j), id_qh,
-                       j > 0);
-        tc::commit(&bar_vq);
-        if (!(live = tc::mbar_wait(&bar_vt, c & 1, WAIT_LIMIT))) break;
-        tc::fence_after();
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          tc::mma_bf16(tm + C_TM_DS, kdesc64(sb + C_OFF_VTH, j), mndesc(st + S_K, 8192, j), id_s,
-                       j > 0);
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          tc::mma_bf16(tm + C_TM_DS, kdesc64(sb + C_OFF_VTL, j), mndesc(st + S_K, 8192, j), id_s,
-                       true);
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          tc::mma_bf16(tm + C_TM_O, kdesc64(sb + C_OFF_VN, j), kdesc64(st + S_AQK, j), id_qh, true);
-        tc::commit(&bar_so);
-        tc::commit(&empty[s]);
-        if (c + 1 < NC) {
-          if (!(live = tc::mbar_wait(&full[s ^ 1], ((c + 1) >> 1) & 1, WAIT_LIMIT))) break;
-          issue_u(c + 1);
+          tc::mma_bf16_ts(tm + C_TM_U, tm + C_TM_HT + 8 * j, kdesc(st + S_WQ, 16384, j), id_vq,
+                          has_v || j > 0);
+        tc::commit(&bar_v);
+        if (write_o) {
+#pragma unroll 1
+          for (int j = 0; j < 8; ++j)
+            tc::mma_bf16_ts(tm + C_TM_QH, tm + C_TM_HT + 8 * j, kdesc(st + S_WQ + 8192, 16384, j),
+                            id_vq, j > 0);
+          tc::commit(&bar_q);
         }
+        tc::commit(&early_free[s]);
+        if (!(live = tc::mbar_wait(&bar_vt, i & 1, WAIT_LIMIT))) break;
+        tc::fence_after();
+        // dS = vt_hi^T k + vt_lo^T k
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::mma_bf16_ts(tm + C_TM_DS, tm + C_TM_VTH + 8 * j, mndesc(st + S_K, 8192, j), id_s,
+                          j > 0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::mma_bf16_ts(tm + C_TM_DS, tm + C_TM_VTL + 8 * j, mndesc(st + S_K, 8192, j), id_s,
+                          true);
+        tc::commit(&bar_s);
+        // the next chunk's D_u runs while the epilogue applies dS
+        if (has_v && i + 1 < NI) {
+          if (!(live = tc::mbar_wait(&full[s ^ 1], ((i + 1) >> 1) & 1, WAIT_LIMIT))) break;
+          tc::fence_after();
+          issue_u(i + 1);
+        }
+        if (write_o) {
+          // D_o += v_new^T Aqk^T, once the epilogue has put e^{gc} D_qh there
+          if (!(live = tc::mbar_wait(&bar_o, i & 1, WAIT_LIMIT))) break;
+          tc::fence_after();
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tc::mma_bf16_ts(tm + C_TM_O, tm + C_TM_VN + 8 * j, kdesc64(st + S_AQK, j), id_o, true);
+          tc::commit(&bar_od);
+        }
+        tc::commit(&empty[s]);
       }
       if (!live) {
         record_error();
         atomicExch(&abort_sh, 1);
       }
+      // every MMA has landed before TMEM is released
+      tc::commit(&bar_fin);
+      if (!tc::mbar_wait(&bar_fin, 0, WAIT_LIMIT)) record_error();
     }
   } else {
     // ------------------------------------------------------------ epilogue warps
@@ -505,44 +679,64 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     const int vrow = quarter * 32 + lane;
     const int kc0 = colq * C_SCOLS;      // state columns owned
     const int tc0 = colq * C_TCOLS;      // token columns owned in 64-wide regions
-    float* gcs = reinterpret_cast<float*>(sm + C_OFF_TAB);  // gc, e^gc, e^{gl-gc}
-    float* egc = gcs + 64;
-    float* edc = gcs + 128;
     float S[C_SCOLS];
     {
-      const float* src = h0 ? h0 + ((int64_t)n * H + h) * K * V : nullptr;
+      const float* src = it_init;
 #pragma unroll
-      for (int i = 0; i < C_SCOLS; ++i) S[i] = src ? src[(kc0 + i) * V + vrow] : 0.f;
+      for (int i = 0; i < C_SCOLS; ++i)
+        S[i] = kind == ITEM_TRANS ? (kc0 + i == vrow ? 1.f : 0.f)
+                                  : (src ? src[(kc0 + i) * V + vrow] : 0.f);
     }
     float gl_prev = 0.f;
     int L_prev = 0;
     int64_t t0_prev = 0;
     bool live = true;
-    auto sync_chain = [&]() { tc::named_sync(1, C_EPI_THREADS); };
-    auto wait_uniform = [&](uint64_t* b, uint32_t par) -> bool {
-      const bool ok = tc::mbar_wait(b, par, WAIT_LIMIT);
-      if (!ok) {
+    // Each thread waits on its own; a timeout flags the CTA and every role
+    // leaves its loop (no named barrier inside the loop can strand a warp).
+    auto wait_ok = [&](uint64_t* b, uint32_t par) -> bool {
+      if (!tc::mbar_wait(b, par, WAIT_LIMIT)) {
         record_error();
         atomicExch(&abort_sh, 1);
+        return false;
       }
       tc::fence_after();
-      sync_chain();
-      return *(volatile int*)&abort_sh == 0;
+      return true;
+    };
+    // all 32 lanes' TMEM writes have landed: one arrive per warp (the epilogue
+    // writes no shared memory, so no proxy fence is needed)
+    auto warp_arrive = [&](uint64_t* b) {
+      tc::tmem_wait_st();
+      tc::fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(b);
     };
     static_assert(C_TCOLS == 16 && C_SCOLS == 32, "epilogue tiling assumes 16 warps");
-    auto write_out = [&](int64_t tb, int Lc) {  // o = scale * D_o (previous chunk)
+    // o = scale * D_o of a finished chunk.  A warp owns 16 tokens x 32 values
+    // (lane = value): it transposes them through its shared buffer so that
+    // each lane stores two 16-byte pieces of token rows.
+    unsigned char* ost = sm + C_OFF_OST + cw * 2048;
+    auto write_out = [&](int64_t tb, int Lc) {
       float ov[16];
       tc::tmem_ld16(tm_addr(tm, quarter, C_TM_O + tc0), ov);
       tc::tmem_wait_ld();
+      __syncwarp();  // the previous transpose has been read out
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const int i = tc0 + c;
-        if (i < Lc) o[(tb + i) * (H * V) + (int64_t)h * V + vrow] = __float2bfloat16_rn(ov[c] * scale);
+      for (int c = 0; c < 16; ++c)
+        *reinterpret_cast<bf16*>(ost + c * 64 + lane * 2) = __float2bfloat16_rn(ov[c] * scale);
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = (lane >> 2) + 8 * j, m = lane & 3;  // token row, 8-value piece
+        if (tc0 + r < Lc) {
+          const uint4 piece = *reinterpret_cast<const uint4*>(ost + r * 64 + m * 16);
+          *reinterpret_cast<uint4*>(o + (tb + tc0 + r) * (H * V) + (int64_t)h * V + quarter * 32 +
+                                    m * 8) = piece;
+        }
       }
     };
     auto apply_ds = [&](float dl) {  // S = e^{gl} S + dS
 #pragma unroll
-      for (int cb = 0; cb < 2; ++cb) {
+      for (int cb = 0; cb < 2; ++cb) {  // 16 columns at a time keeps registers under 96
         float d[16];
         tc::tmem_ld16(tm_addr(tm, quarter, C_TM_DS + kc0 + cb * 16), d);
         tc::tmem_wait_ld();
@@ -550,100 +744,77 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         for (int i = 0; i < 16; ++i) S[cb * 16 + i] = fmaf(S[cb * 16 + i], dl, d[i]);
       }
     };
-    for (int c = 0; c < NC && live; ++c) {
-      const int s = c & 1;
-      (void)s;
-      if (c > 0) {
-        if (!(live = wait_uniform(&bar_so, (c - 1) & 1))) break;
+    for (int i = 0; i < NI; ++i) {
+      const int s = i & 1;
+      if (i > 0) {
+        if (!(live = wait_ok(&bar_s, (i - 1) & 1))) break;
         apply_ds(__expf(gl_prev));
       }
-      // E0: bf16 S^T -> HT, then let the MMA warp go
-#pragma unroll
-      for (int m = 0; m < C_SCOLS / 8; ++m) {
-        uint4 pk;
-        pk.x = pack_bf16(S[8 * m + 0], S[8 * m + 1]);
-        pk.y = pack_bf16(S[8 * m + 2], S[8 * m + 3]);
-        pk.z = pack_bf16(S[8 * m + 4], S[8 * m + 5]);
-        pk.w = pack_bf16(S[8 * m + 6], S[8 * m + 7]);
-        *reinterpret_cast<uint4*>(sm + C_OFF_HT + chunk_off(vrow, (kc0 >> 3) + m, 16384)) = pk;
-      }
-      tc::fence_proxy_async();
-      tc::fence_before();
-      sync_chain();
-      if (cw == 0 && lane == 0) tc::mbar_arrive(&bar_ht);
-      // previous chunk's output overlaps this chunk's first MMAs
-      if (c > 0) write_out(t0_prev, L_prev);
-      // gates of this chunk: cumsum and the two exponential tables
-      if (!(live = wait_uniform(&full[s], (c >> 1) & 1))) break;
-      const float* gb = reinterpret_cast<const float*>(sm + C_OFF_GB + s * 512);
-      const int64_t t0 = bos + (int64_t)c * BT;
-      const int L = (int)((eos - t0) < BT ? (eos - t0) : BT);
-      if (cw == 0) {
-        chunk_cumsum_warp(gb, gcs, lane);
-        __syncwarp();
-        const float glc = gcs[L - 1];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int i = lane + 32 * u;
-          egc[i] = __expf(gcs[i]);
-          edc[i] = __expf(fminf(glc - gcs[i], 0.f));
-        }
-      }
-      sync_chain();
-      const float gl = gcs[L - 1];
-      if (!(live = wait_uniform(&bar_vq, c & 1))) break;
-      // E1: v_new (= D_u, exact diagonal included), vt hi/lo, o_inter
+      if (*(volatile int*)&abort_sh) { live = false; break; }
+      // E0: bf16 S^T -> TMEM (columns kc0/2 .. kc0/2 + 15), then let the MMA warp go
       {
-        {
-          const int tb = tc0;
-          float du[16], qh[16];
-          tc::tmem_ld16(tm_addr(tm, quarter, C_TM_U + tb), du);
-          tc::tmem_ld16(tm_addr(tm, quarter, C_TM_QH + tb), qh);
-          tc::tmem_wait_ld();
+        uint32_t pk[16];
 #pragma unroll
-          for (int cc = 0; cc < 16; cc += 8) {
-            float vn[8], th[8], tl[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int i = tb + cc + u;
-              vn[u] = du[cc + u];
-              const float sc = vn[u] * edc[i];
-              th[u] = __bfloat162float(__float2bfloat16_rn(sc));
-              tl[u] = sc - th[u];
-              qh[cc + u] *= egc[i];
-            }
-            const uint32_t off = (uint32_t)(vrow * 128 + ((((tb + cc) >> 3) ^ (vrow & 7)) << 4));
-            uint4 a, b2, d;
-            a.x = pack_bf16(vn[0], vn[1]); a.y = pack_bf16(vn[2], vn[3]);
-            a.z = pack_bf16(vn[4], vn[5]); a.w = pack_bf16(vn[6], vn[7]);
-            b2.x = pack_bf16(th[0], th[1]); b2.y = pack_bf16(th[2], th[3]);
-            b2.z = pack_bf16(th[4], th[5]); b2.w = pack_bf16(th[6], th[7]);
-            d.x = pack_bf16(tl[0], tl[1]); d.y = pack_bf16(tl[2], tl[3]);
-            d.z = pack_bf16(tl[4], tl[5]); d.w = pack_bf16(tl[6], tl[7]);
-            *reinterpret_cast<uint4*>(sm + C_OFF_VN + off) = a;
-            *reinterpret_cast<uint4*>(sm + C_OFF_VTH + off) = b2;
-            *reinterpret_cast<uint4*>(sm + C_OFF_VTL + off) = d;
-          }
-          tc::tmem_st16(tm_addr(tm, quarter, C_TM_O + tb), qh);
-        }
-        tc::tmem_wait_st();
+        for (int m = 0; m < 16; ++m) pk[m] = pack_bf16(S[2 * m], S[2 * m + 1]);
+        tc::tmem_st16u(tm_addr(tm, quarter, C_TM_HT + kc0 / 2), pk);
       }
-      tc::fence_proxy_async();
-      tc::fence_before();
-      sync_chain();
-      if (cw == 0 && lane == 0) tc::mbar_arrive(&bar_vt);
-      gl_prev = gl;
+      warp_arrive(&bar_ht);
+      if (!(live = wait_ok(&full[s], (i >> 1) & 1))) break;
+      if (!(live = wait_ok(&bar_v, i & 1))) break;
+      const float* tab = reinterpret_cast<const float*>(sm + C_OFF_TAB + (i & 3) * C_TAB);
+      const int64_t t0 = bos + (int64_t)(c0 + i) * BT;
+      const int L = (int)((eos - t0) < BT ? (eos - t0) : BT);
+      // E1a: v_new = D_u (exact diagonal included); vt = v_new e^{gl-gc} as
+      // bf16 hi + lo for the state product (critical path: hand it over first)
+      float du[16];
+      tc::tmem_ld16(tm_addr(tm, quarter, C_TM_U + tc0), du);
+      tc::tmem_wait_ld();
+      {
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float s0 = du[2 * u] * tab[tc0 + 2 * u];
+          const float s1 = du[2 * u + 1] * tab[tc0 + 2 * u + 1];
+          const float h0f = __bfloat162float(__float2bfloat16_rn(s0));
+          const float h1f = __bfloat162float(__float2bfloat16_rn(s1));
+          hi[u] = pack_bf16(h0f, h1f);
+          lo[u] = pack_bf16(s0 - h0f, s1 - h1f);
+        }
+        tc::tmem_st8u(tm_addr(tm, quarter, C_TM_VTH + tc0 / 2), hi);
+        tc::tmem_st8u(tm_addr(tm, quarter, C_TM_VTL + tc0 / 2), lo);
+      }
+      warp_arrive(&bar_vt);
+      gl_prev = tab[128];
+      if (write_o) {
+        // previous chunk's output (its product also frees D_o and v_new)
+        // overlaps this chunk's state product
+        if (i > 0) {
+          if (!(live = wait_ok(&bar_od, (i - 1) & 1))) break;
+          write_out(t0_prev, L_prev);
+        }
+        // E1b: D_o = e^{gc} D_qh, bf16 v_new -> TMEM
+        if (!(live = wait_ok(&bar_q, i & 1))) break;
+        float qh[16];
+        tc::tmem_ld16(tm_addr(tm, quarter, C_TM_QH + tc0), qh);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 16; ++u) qh[u] *= tab[64 + tc0 + u];
+        tc::tmem_st16(tm_addr(tm, quarter, C_TM_O + tc0), qh);
+        uint32_t vn[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) vn[u] = pack_bf16(du[2 * u], du[2 * u + 1]);
+        tc::tmem_st8u(tm_addr(tm, quarter, C_TM_VN + tc0 / 2), vn);
+        warp_arrive(&bar_o);
+      }
       L_prev = L;
       t0_prev = t0;
     }
-    if (live && NC > 0) {
-      if ((live = wait_uniform(&bar_so, (NC - 1) & 1))) {
-        apply_ds(__expf(gl_prev));
-        write_out(t0_prev, L_prev);
-      }
+    if (live && NI > 0) {
+      if ((live = wait_ok(&bar_s, (NI - 1) & 1))) apply_ds(__expf(gl_prev));
+      if (live && write_o && (live = wait_ok(&bar_od, (NI - 1) & 1))) write_out(t0_prev, L_prev);
     }
-    if (live && ht) {
-      float* dst = ht + ((int64_t)n * H + h) * K * V;
+    if (live && it_out) {
+      float* dst = it_out;
 #pragma unroll
       for (int i = 0; i < C_SCOLS; ++i) dst[(kc0 + i) * V + vrow] = S[i];
     }
@@ -651,6 +822,78 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
   tc::fence_before();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tm, C_TM_COLS);
+}
+
+// ============================================================================
+// Kernel 3: segment start states, h_{s+1} = X_s^T h_s + B_s (fp32)
+// ============================================================================
+// Serial over the middle segments of one (sequence, head); the value columns
+// are independent, so CTA x owns columns [16x, 16x + 16).  X_s^T is staged in
+// shared memory per step (row stride 129 keeps the column walk conflict-free).
+constexpr int CB_NT = 256, CB_COLS = 16, CB_LD = 129;
+constexpr int CB_SMEM = (128 * CB_LD + 128 * CB_COLS) * 4;
+
+__global__ void __launch_bounds__(CB_NT) chunk_combine_kernel(const int32_t* __restrict__ cu,
+                                                              int64_t N, int64_t T, int64_t H,
+                                                              ChainPlan plan) {
+  extern __shared__ float cbs[];
+  float* xt = cbs;                   // X^T [kk][r]
+  float* cur = cbs + 128 * CB_LD;    // h_s[:, cols]  [r][CB_COLS]
+  __shared__ int64_t slot_sh;
+  __shared__ int nseg_sh;
+  const int tid = threadIdx.x;
+  const int64_t n = blockIdx.y / H;
+  const int h = (int)(blockIdx.y - n * H);
+  const int v0 = blockIdx.x * CB_COLS;
+  if (tid == 0) {
+    int64_t slot = 0;
+    int nseg = 1;
+    for (int64_t m = 0; m <= n; ++m) {
+      const int nc = seq_chunks(cu, m, T);
+      nseg = nc > plan.seg ? (nc + plan.seg - 1) / plan.seg : 1;
+      if (m < n) slot += nseg;
+    }
+    slot_sh = slot;
+    nseg_sh = nseg;
+  }
+  __syncthreads();
+  const int nseg = nseg_sh;
+  if (nseg < 3) return;
+  const int64_t slot = slot_sh;
+  const int kk = tid >> 1, cb = (tid & 1) * 8;
+  {
+    const float* h1 = seg_state(plan, slot + 1, H, h, 0);
+    for (int e = tid; e < 128 * CB_COLS; e += CB_NT)
+      cur[e] = h1[(e / CB_COLS) * 128 + v0 + (e % CB_COLS)];
+  }
+  for (int s = 1; s <= nseg - 2; ++s) {
+    const float* xs = seg_state(plan, slot + s, H, h, 2);
+    const float* bs = seg_state(plan, slot + s, H, h, 1);
+    float* nx = seg_state(plan, slot + s + 1, H, h, 0);
+    for (int e = tid; e < 128 * 32; e += CB_NT) {
+      const int r = e >> 5, q4 = e & 31;
+      const float4 x = reinterpret_cast<const float4*>(xs + r * 128)[q4];
+      float* d = xt + r * CB_LD + q4 * 4;
+      d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+    }
+    __syncthreads();
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = bs[kk * 128 + v0 + cb + c];
+#pragma unroll 4
+    for (int r = 0; r < 128; ++r) {
+      const float m = xt[kk * CB_LD + r];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[c] = fmaf(m, cur[r * CB_COLS + cb + c], acc[c]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      cur[kk * CB_COLS + cb + c] = acc[c];
+      nx[kk * 128 + v0 + cb + c] = acc[c];
+    }
+    __syncthreads();
+  }
 }
 
 }  // namespace
@@ -663,6 +906,86 @@ static int64_t chunk_bound(const int32_t* cu, int64_t B, int64_t T, int64_t N) {
   return cu ? T / gdn::BT + N : B * ((T + gdn::BT - 1) / gdn::BT);
 }
 
+// Segment length (in chunks) for the chain, 0 = unsegmented.  The host does
+// not know the sequence lengths (cu_seqlens stays on the device), so the plan
+// assumes the worst case of one sequence holding every chunk and picks the
+// segment count P minimising (phase-1 waves + phase-3 waves) x segment length
+// + combine steps, counted in chunk steps on a 148-SM B200.  Segmenting runs
+// each chunk of a middle segment three times (local, transition, output) on
+// otherwise idle SMs, so it only pays when (sequence, head) pairs are scarce.
+static int chain_segment_chunks(int64_t B, int64_t T, int64_t N, int64_t H, bool varlen) {
+  constexpr int64_t kSMs = 148;
+  const int64_t C = (T + gdn::BT - 1) / gdn::BT;  // longest possible chain
+  (void)B;
+  if (N * H >= kSMs || C < 32) return 0;
+  const int64_t others = varlen ? (N - 1) * H : 0;  // the other sequences' first items
+  const int64_t pairs = varlen ? H : N * H;
+  const double plain = (double)((N * H + kSMs - 1) / kSMs) * (double)C;
+  double best = plain;
+  int best_seg = 0;
+  for (int64_t P = 3; P <= 64; ++P) {
+    const int64_t seg = (C + P - 1) / P;
+    if (seg < 8) break;
+    const int64_t nseg = (C + seg - 1) / seg;
+    const int64_t items1 = pairs * (1 + 2 * (nseg - 2)) + others;
+    const int64_t items3 = pairs * (nseg - 1);
+    const double cost = (double)((items1 + kSMs - 1) / kSMs + (items3 + kSMs - 1) / kSMs) * seg +
+                        (double)(nseg - 2);
+    if (cost < best) {
+      best = cost;
+      best_seg = (int)seg;
+    }
+  }
+  return best < 0.9 * plain ? best_seg : 0;
+}
+
+// Upper bound of the segment slots (sum over sequences of their segment count).
+static int64_t chain_segment_slots(int64_t T, int64_t N, bool varlen, int seg) {
+  if (seg == 0) return 0;
+  const int64_t C = (T + gdn::BT - 1) / gdn::BT;
+  if (!varlen) return N * ((C + seg - 1) / seg);
+  return (C + N + seg - 1) / seg + N;
+}
+
+static int64_t round_up256(int64_t x) { return (x + 255) / 256 * 256; }
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// bf16 rows of `cols` elements, `rows` rows `stride` elements apart, moved
+// as box_cols x box_rows boxes (64 x 64 with the 128-byte swizzle by
+// default).  Loads read rows past `rows` as zero; stores drop them.
+static int token_rows_map(CUtensorMap* m, const void* base, int64_t cols, int64_t rows,
+                          int64_t stride, const char* what, uint32_t box_cols = 64,
+                          uint32_t box_rows = 64, bool swizzle = true) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return set_error(XOPS_ERR_CUDA, "%s: cuTensorMapEncodeTiled is unavailable", what);
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(stride * 2)};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(XOPS_ERR_CUDA, "%s: tensor map encoding failed (%d)", what, (int)r);
+  return XOPS_OK;
+}
+
 extern "C" int64_t xops_chunk_gated_delta_rule_workspace_size(int64_t B, int64_t T, int64_t N,
                                                               int64_t Hg, int64_t H, int64_t K,
                                                               int use_qk_l2norm_in_kernel,
@@ -670,7 +993,9 @@ extern "C" int64_t xops_chunk_gated_delta_rule_workspace_size(int64_t B, int64_t
   if (B < 1 || T < 0 || N < 0 || Hg < 1 || H < 1 || K <= 0) return -1;
   const int64_t chunks = varlen ? T / gdn::BT + N : B * ((T + gdn::BT - 1) / gdn::BT);
   int64_t bytes = chunks * H * (int64_t)gdn::WS_CHUNK;
-  if (use_qk_l2norm_in_kernel) bytes += 2 * B * T * Hg * K * 2 + 256;
+  if (use_qk_l2norm_in_kernel) bytes += round_up256(2 * B * T * Hg * K * 2);
+  const int seg = chain_segment_chunks(B, T, N, H, varlen != 0);
+  bytes += chain_segment_slots(T, N, varlen != 0, seg) * H * 3 * (int64_t)gdn::KV * 4;
   return bytes;
 }
 
@@ -736,10 +1061,43 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
   if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_chain_kernel, gdn::C_SMEM,
                                      "chunk_gated_delta_rule(chain)"))
     return rc;
-  gdn::chunk_chain_kernel<<<(unsigned)(N * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-      qq, kk, (const gdn::bf16*)v, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, T, Hg, H, qs,
-      ks, v_token_stride, scale);
-  return check_launch("chunk_gated_delta_rule(chain)");
+  CUtensorMap mq, mk, mv;
+  if (int rc = token_rows_map(&mq, qq, Hg * K, B * T, qs, "chunk_gated_delta_rule(q map)"))
+    return rc;
+  if (int rc = token_rows_map(&mk, kk, Hg * K, B * T, ks, "chunk_gated_delta_rule(k map)"))
+    return rc;
+  if (int rc = token_rows_map(&mv, v, H * V, B * T, v_token_stride,
+                              "chunk_gated_delta_rule(v map)"))
+    return rc;
+  const bool varlen = cu_seqlens != nullptr;
+  const int seg = chain_segment_chunks(B, T, N, H, varlen);
+  gdn::ChainPlan plan{seg, 1, nullptr};
+  if (seg == 0) {
+    gdn::chunk_chain_kernel<<<(unsigned)(N * H), gdn::C_NT, gdn::C_SMEM, st>>>(
+        mq, mk, mv, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+        plan);
+    return check_launch("chunk_gated_delta_rule(chain)");
+  }
+  // Segment-parallel chain: grids are upper bounds, spare CTAs exit at once.
+  int64_t off = nchunks * H * (int64_t)gdn::WS_CHUNK;
+  if (use_qk_l2norm_in_kernel) off += round_up256(2 * B * T * Hg * K * 2);
+  plan.scratch = reinterpret_cast<float*>(ws + off);
+  const int64_t slots = chain_segment_slots(T, N, varlen, seg);
+  gdn::chunk_chain_kernel<<<(unsigned)((N + 2 * slots) * H), gdn::C_NT, gdn::C_SMEM, st>>>(
+      mq, mk, mv, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+        plan);
+  if (int rc = check_launch("chunk_gated_delta_rule(chain, first segments)")) return rc;
+  if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_combine_kernel, gdn::CB_SMEM,
+                                     "chunk_gated_delta_rule(combine)"))
+    return rc;
+  gdn::chunk_combine_kernel<<<dim3(128 / gdn::CB_COLS, (unsigned)(N * H)), gdn::CB_NT,
+                              gdn::CB_SMEM, st>>>(cu_seqlens, N, T, H, plan);
+  if (int rc = check_launch("chunk_gated_delta_rule(combine)")) return rc;
+  plan.phase = 3;
+  gdn::chunk_chain_kernel<<<(unsigned)(slots * H), gdn::C_NT, gdn::C_SMEM, st>>>(
+      mq, mk, mv, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+        plan);
+  return check_launch("chunk_gated_delta_rule(chain, remaining segments)");
 }
 
 extern "C" int xops_device_error_count(void) {
