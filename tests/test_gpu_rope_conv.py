@@ -88,6 +88,28 @@ def test_conv_prefill_config2():
     assert torch.equal(st_d.cpu(), st_ref)
 
 
+@pytest.mark.parametrize("lens,dim,width,dt", [
+    ([300, 5, 1000], 264, 2, torch.bfloat16),   # partial 256-channel slab, width 2
+    ([129, 31, 2], 520, 6, torch.float16),      # width 6 (5-row halo), fp16
+    ([33, 64, 95], 1024, 4, torch.bfloat16),    # tiles ending mid-box
+])
+def test_conv_varlen_widths_and_slabs(lens, dim, width, dt):
+    g = torch.Generator().manual_seed(dim + width)
+    T = sum(lens)
+    x = torch.randn(T, dim, generator=g).to(dt)
+    st = torch.randn(len(lens), dim, width - 1, generator=g).to(dt)
+    wt = (0.5 * torch.randn(dim, width, generator=g)).to(dt)
+    b = (0.5 * torch.randn(dim, generator=g)).to(dt)
+    qsl = torch.tensor([0] + torch.cumsum(torch.tensor(lens), 0).tolist(), dtype=torch.int32)
+    st_d = st.clone().to(DEV)
+    y = ops.npu_causal_conv1d_update_v2(x.to(DEV), st_d, wt.to(DEV), True, b.to(DEV),
+                                        query_start_loc=qsl.to(DEV))
+    st_ref = st.clone()
+    ref = oracle.causal_conv1d_varlen(x, st_ref, wt, b, True, qsl)
+    assert_bf16(y, ref)
+    assert torch.equal(st_d.cpu(), st_ref)
+
+
 def test_conv_varlen_ragged_and_slots():
     g = torch.Generator().manual_seed(11)
     lens = [1, 2, 3, 64, 65, 0, 200, 7]

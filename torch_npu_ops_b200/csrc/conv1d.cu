@@ -18,6 +18,12 @@
 // Decode (causal_conv1d_update_ref, test_causal_conv1d_update.py:1158-1210;
 // continuous-batching slot lookup and pad-slot skip as the decode kernels,
 // :783-792): per (row, channel vector) read state + x, write out + state.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace xops {
@@ -253,6 +259,297 @@ __global__ void __launch_bounds__(256) conv1d_decode_w4_kernel(
   store_vec<T, 3 * VEC>(sp, ns);
 }
 
+// ----------------------------------------------------------------------------
+// Prefill for 16-bit inputs, TMA-fed.  A persistent CTA walks tiles of
+// RB_T = 64 tokens x RB_C = 256 channels (one sequence per tile).  Warp 0
+// streams each tile plus its W-1 halo rows into a ring of RB_NS shared
+// stages with one TMA box per tile, so the loads in flight per SM do not
+// depend on registers (three CTAs per SM keep six tiles in flight); warps
+// 1-8 slide the window over 16 of the tile's tokens for 4 channels per lane
+// (8-byte shared reads, coalesced 8-byte global writes; a warp covers 128
+// channels).  The halo of a sequence's first tile comes from conv_state,
+// and the lanes that read a state line are the ones that write its final
+// value, as in the per-thread kernel above.
+// ----------------------------------------------------------------------------
+constexpr int RB_T = 64, RB_C = 256, RB_NS = 2, RB_STAGE = 35840;  // (64 + 5) rows x 512 B, rounded
+constexpr int RB_NT = 32 + 256;
+constexpr int RB_CV = 4;  // channels per consumer lane
+constexpr int RB_SMEM = RB_NS * RB_STAGE + 1024;
+constexpr uint32_t RB_WAIT = 1u << 26;
+
+struct RbTile {
+  int64_t t0, sstart, send;
+  int seq, line, slab;
+};
+
+__device__ __forceinline__ void rb_mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(bar)), "r"(count));
+}
+__device__ __forceinline__ bool rb_mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(bar);
+  for (uint32_t i = 0; i < RB_WAIT; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+__device__ __forceinline__ void rb_mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];\n" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(bar)) : "memory");
+}
+__device__ __forceinline__ void rb_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;\n" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void rb_tma_load(void* dst, const void* tmap, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y),
+      "r"((uint32_t)__cvta_generic_to_shared(bar)) : "memory");
+}
+
+__device__ int g_conv_error = 0;
+
+template <typename T, int W>
+__global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
+    const __grid_constant__ CUtensorMap xmap, const T* __restrict__ x, T* __restrict__ state,
+    const T* __restrict__ weight, const T* __restrict__ bias, const int32_t* __restrict__ qsl,
+    const int32_t* __restrict__ slots, T* __restrict__ out, int nseq, int64_t dim,
+    int64_t tiles_per_slab, int64_t total_tiles, int box_c, bool silu, int32_t pad_slot) {
+  constexpr int H = W - 1;
+  extern __shared__ unsigned char rb_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(rb_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  __shared__ uint64_t full[RB_NS], empty[RB_NS];
+  __shared__ RbTile info[RB_NS];
+  __shared__ int abort_sh;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int s = 0; s < RB_NS; ++s) {
+      rb_mbar_init(&full[s], 1);
+      rb_mbar_init(&empty[s], 8);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    abort_sh = 0;
+  }
+  __syncthreads();
+  auto fail = [&]() {
+    atomicExch(&g_conv_error, 1);
+    atomicExch(&abort_sh, 1);
+  };
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int64_t k = 0;; ++k) {
+        const int64_t idx = blockIdx.x + k * gridDim.x;
+        if (idx >= total_tiles) break;
+        const int s = (int)(k % RB_NS);
+        if (k >= RB_NS && !rb_mbar_wait(&empty[s], (uint32_t)((k / RB_NS - 1) & 1))) {
+          fail();
+          break;
+        }
+        if (*(volatile int*)&abort_sh) break;
+        RbTile ti;
+        ti.slab = (int)(idx / tiles_per_slab);
+        int64_t r = idx - (int64_t)ti.slab * tiles_per_slab, acc = 0;
+        ti.seq = -1;
+        ti.t0 = ti.sstart = ti.send = 0;
+        for (int i = 0; i < nseq; ++i) {
+          const int64_t a = qsl[i], e = qsl[i + 1];
+          const int64_t n = e > a ? (e - a + RB_T - 1) / RB_T : 0;
+          if (r < acc + n) {
+            ti.seq = i;
+            ti.sstart = a;
+            ti.send = e;
+            ti.t0 = a + (r - acc) * RB_T;
+            break;
+          }
+          acc += n;
+        }
+        ti.line = ti.seq >= 0 ? (slots ? slots[ti.seq] : ti.seq) : 0;
+        info[s] = ti;
+        if (ti.seq < 0) {  // past the slab's last tile (the count is an upper bound)
+          rb_mbar_arrive(&full[s]);
+          continue;
+        }
+        rb_expect_tx(&full[s], (uint32_t)((RB_T + H) * box_c * sizeof(T)));
+        rb_tma_load(sm + s * RB_STAGE, &xmap, ti.slab * RB_C, (int)(ti.t0 - H), &full[s]);
+      }
+    }
+    return;
+  }
+  // consumers: warp pair = 16-token group; lane = 4 channels as two fp32
+  // pairs, so the taps and the SiLU run as packed f32x2 instructions
+  const int cw = warp - 1, tg = cw >> 1, quad = (cw & 1) * 32 + lane;
+  int cur_slab = -1;
+  float2 w[2][W], b[2];
+  for (int64_t k = 0;; ++k) {
+    const int64_t idx = blockIdx.x + k * gridDim.x;
+    if (idx >= total_tiles) break;
+    const int s = (int)(k % RB_NS);
+    if (!rb_mbar_wait(&full[s], (uint32_t)((k / RB_NS) & 1))) {
+      fail();
+      break;
+    }
+    const RbTile ti = info[s];
+    const int64_t c0 = (int64_t)ti.slab * RB_C + quad * RB_CV;
+    const bool live = ti.seq >= 0 && c0 < dim && !(slots && ti.line == pad_slot);
+    if (live) {
+      if (ti.slab != cur_slab) {
+        cur_slab = ti.slab;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+#pragma unroll
+          for (int j = 0; j < W; ++j)
+            w[p][j] = make_float2(to_f32<T>(weight[(c0 + 2 * p) * W + j]),
+                                  to_f32<T>(weight[(c0 + 2 * p + 1) * W + j]));
+          b[p] = bias ? make_float2(to_f32<T>(bias[c0 + 2 * p]), to_f32<T>(bias[c0 + 2 * p + 1]))
+                      : make_float2(0.f, 0.f);
+        }
+      }
+      const unsigned char* stg = sm + s * RB_STAGE + quad * (RB_CV * 2) + tg * 16 * (box_c * 2);
+      const int rstride = box_c * 2;
+      float2 hist[H > 0 ? H : 1][2];
+      const bool first = ti.t0 == ti.sstart && tg == 0;
+      T* st_line = state + ((int64_t)ti.line * dim + c0) * H;
+      if (first) {
+#pragma unroll
+        for (int j = 0; j < H; ++j)
+#pragma unroll
+          for (int p = 0; p < 2; ++p)
+            hist[j][p] = make_float2(to_f32<T>(st_line[(2 * p) * H + j]),
+                                     to_f32<T>(st_line[(2 * p + 1) * H + j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < H; ++j) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(stg + j * rstride);
+          hist[j][0] = unpack2<T>(raw.x);
+          hist[j][1] = unpack2<T>(raw.y);
+        }
+      }
+      const int64_t tb = ti.t0 + tg * 16;
+      const int64_t nvalid = ti.send - tb;  // tokens of this group inside the sequence
+      T* dst = out + tb * dim + c0;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(stg + (H + u) * rstride);
+        float2 cur[2] = {unpack2<T>(raw.x), unpack2<T>(raw.y)};
+        uint2 packed;
+        uint32_t* pk = &packed.x;
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          float2 a = b[p];
+#pragma unroll
+          for (int j = 0; j < H; ++j) a = ffma2(hist[j][p], w[p][j], a);
+          a = ffma2(cur[p], w[p][H], a);
+          pk[p] = pack2<T>(silu ? silu2_lowp(a) : a);
+        }
+        if (u < nvalid) *reinterpret_cast<uint2*>(dst + (int64_t)u * dim) = packed;
+#pragma unroll
+        for (int j = 0; j + 1 < H; ++j) {
+          hist[j][0] = hist[j + 1][0];
+          hist[j][1] = hist[j + 1][1];
+        }
+        if constexpr (H > 0) {
+          hist[H - 1][0] = cur[0];
+          hist[H - 1][1] = cur[1];
+        }
+      }
+      if (first) {
+        // final state = last H entries of cat(old_state, x_seq).  Entry j
+        // reads old-state index len + j > j when it comes from the old state,
+        // so writing index j in increasing order never clobbers a later read.
+        const int64_t len = ti.send - ti.sstart;
+#pragma unroll
+        for (int j = 0; j < H; ++j) {
+          const int64_t pos = len - H + j;
+          float v[RB_CV];
+          if (pos >= 0) {
+            load_vec<T, RB_CV>(x + (ti.sstart + pos) * dim + c0, v);
+          } else {
+#pragma unroll
+            for (int c = 0; c < RB_CV; ++c) v[c] = to_f32<T>(st_line[c * H + H + pos]);
+          }
+#pragma unroll
+          for (int c = 0; c < RB_CV; ++c) st_line[c * H + j] = from_f32<T>(v[c]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) rb_mbar_arrive(&empty[s]);
+  }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point.
+static PFN_cuTensorMapEncodeTiled_v12000 conv_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+template <typename T>
+int launch_varlen_tma(int W, const void* x, void* state, const void* w, const void* b,
+                      const int32_t* qsl, const int32_t* slots, void* out, int nseq,
+                      int64_t total, int64_t dim, bool silu, int32_t pad, cudaStream_t st) {
+  auto enc = conv_map_encoder();
+  if (!enc) return set_error(XOPS_ERR_CUDA, "causal_conv1d_varlen: cuTensorMapEncodeTiled is unavailable");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)dim, (cuuint64_t)total};
+  cuuint64_t strides[1] = {(cuuint64_t)(dim * (int64_t)sizeof(T))};
+  const int box_c = (int)std::min<int64_t>(dim, RB_C);  // slab width; dim is a multiple of 8
+  cuuint32_t box[2] = {(cuuint32_t)box_c, (cuuint32_t)(RB_T + W - 1)};
+  cuuint32_t es[2] = {1, 1};
+  const CUresult r = enc(&m, sizeof(T) == 2 ? (std::is_same<T, __half>::value
+                                                   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16)
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                         2, const_cast<void*>(x), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(XOPS_ERR_CUDA, "causal_conv1d_varlen: tensor map encoding failed (%d)", (int)r);
+  // exact tile count per channel slab: sum over sequences of ceil(len / RB_T)
+  // is bounded by total / RB_T + nseq; the kernel maps tiles exactly from
+  // query_start_loc, so the bound only sizes the slab stride
+  const int64_t tiles_per_slab = total / RB_T + nseq;
+  const int64_t slabs = (dim + RB_C - 1) / RB_C;
+  const int64_t total_tiles = slabs * tiles_per_slab;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned grid = (unsigned)std::min<int64_t>(total_tiles, 2 * (int64_t)sms);
+  switch (W) {
+#define XOPS_CT(WW)                                                                            \
+  case WW: {                                                                                   \
+    auto kern = conv1d_varlen_tma_kernel<T, WW>;                                               \
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, RB_SMEM) !=     \
+        cudaSuccess)                                                                           \
+      return set_error(XOPS_ERR_CUDA, "causal_conv1d_varlen: shared-memory attribute failed"); \
+    kern<<<grid, RB_NT, RB_SMEM, st>>>(m, (const T*)x, (T*)state, (const T*)w, (const T*)b,    \
+                                       qsl, slots, (T*)out, nseq, dim, tiles_per_slab,          \
+                                       total_tiles, box_c, silu, pad);                          \
+    return check_launch("causal_conv1d_varlen");                                               \
+  }
+    XOPS_CT(2) XOPS_CT(3) XOPS_CT(4) XOPS_CT(5) XOPS_CT(6)
+#undef XOPS_CT
+    default:
+      return set_error(XOPS_ERR_UNSUPPORTED, "causal_conv1d_varlen: width %d not in [2, 6]", W);
+  }
+}
+
 template <typename T>
 int launch_varlen_w(int W, const void* x, void* state, const void* w, const void* b,
                     const int32_t* qsl, const int32_t* slots, void* out, int nseq,
@@ -301,13 +598,14 @@ extern "C" int xops_causal_conv1d_varlen(const void* x, void* conv_state, const 
   cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
     case XOPS_BF16:
-      return launch_varlen_w<__nv_bfloat16>((int)width, x, conv_state, weight, bias,
-                                            query_start_loc, conv_state_indices, out, (int)batch,
-                                            tiles, dim, silu != 0, pad_slot_id, st);
+      return launch_varlen_tma<__nv_bfloat16>((int)width, x, conv_state, weight, bias,
+                                              query_start_loc, conv_state_indices, out,
+                                              (int)batch, total_tokens, dim, silu != 0,
+                                              pad_slot_id, st);
     case XOPS_F16:
-      return launch_varlen_w<__half>((int)width, x, conv_state, weight, bias, query_start_loc,
-                                     conv_state_indices, out, (int)batch, tiles, dim, silu != 0,
-                                     pad_slot_id, st);
+      return launch_varlen_tma<__half>((int)width, x, conv_state, weight, bias, query_start_loc,
+                                       conv_state_indices, out, (int)batch, total_tokens, dim,
+                                       silu != 0, pad_slot_id, st);
     default:
       return launch_varlen_w<float>((int)width, x, conv_state, weight, bias, query_start_loc,
                                     conv_state_indices, out, (int)batch, tiles, dim, silu != 0,
