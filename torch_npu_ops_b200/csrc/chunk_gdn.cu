@@ -117,14 +117,17 @@ constexpr int P_NT = 256;
 constexpr int P_OFF_KQ = 0;        // [K h0 | Q h0 | K h1 | Q h1], 8 KB each
 constexpr int P_KQ_HALF = 16384;
 constexpr int P_OFF_Q = 8192;
-constexpr int P_OFF_TPP = 32768;   // T'' [64 x 64] SW128
-constexpr int P_OFF_FA = 40960;    // fp32 A, then T = (I+A)^-1 in place [64 x LDF]
-constexpr int P_OFF_FM = P_OFF_FA + 64 * LDF * 4;
-constexpr int P_OFF_G = P_OFF_FM + 32 * 33 * 4;  // graw, gc, beta, e^gc
+// q is dead once the Gram product has read it: its two 8 KB halves then hold
+// T'' (SW128, for the w product) and the inverse's scratch, which keeps the
+// CTA at ~50 KB so four fit on an SM
+constexpr int P_OFF_TPP = P_OFF_Q;            // T'' [64 x 64] SW128
+constexpr int P_OFF_FM = P_OFF_Q + P_KQ_HALF; // inverse scratch (<= 32 x 33 fp32)
+constexpr int P_OFF_FA = 32768;    // fp32 A, then T = (I+A)^-1 in place [64 x LDF]
+constexpr int P_OFF_G = P_OFF_FA + 64 * LDF * 4;  // graw, gc, beta, e^gc
 constexpr int P_SMEM = P_OFF_G + 4 * 64 * 4 + 1024;
 constexpr uint32_t P_TM_G = 0, P_TM_W = 64, P_TM_COLS = 128;
 
-__global__ void __launch_bounds__(P_NT, 3) chunk_prep_kernel(
+__global__ void __launch_bounds__(P_NT, 4) chunk_prep_kernel(
     const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
     const float* __restrict__ beta, unsigned char* __restrict__ ws,
     const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H,
@@ -168,6 +171,14 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_kernel(
   cp_tile128(sm + P_OFF_KQ, P_KQ_HALF, k + t0 * k_stride + (int64_t)hk * 128, k_stride, L, tid, P_NT);
   cp_tile128(sm + P_OFF_Q, P_KQ_HALF, q + t0 * q_stride + (int64_t)hk * 128, q_stride, L, tid, P_NT);
   cp_async_commit();
+  // gates of the first value head load while k and q land; each head's
+  // loop iteration fetches the next head's
+  const int grp = (int)(H / Hg);
+  float g_next = 0.f, b_next = 0.f;
+  if (tid < L) {
+    g_next = g[(t0 + tid) * H + hk * grp];
+    b_next = beta[(t0 + tid) * H + hk * grp];
+  }
   cp_async_wait_all();
   tc::fence_proxy_async();
   tc::fence_before();
@@ -197,12 +208,16 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_kernel(
   };
   wait_mma();
 
-  const int grp = (int)(H / Hg);
   for (int hv = hk * grp; alive && hv < (hk + 1) * grp; ++hv) {
     unsigned char* wsb = ws + (gci * H + hv) * (int64_t)WS_CHUNK;
     if (tid < 64) {
-      graw[tid] = tid < L ? g[(t0 + tid) * H + hv] : 0.f;
-      bet[tid] = tid < L ? beta[(t0 + tid) * H + hv] : 0.f;
+      graw[tid] = g_next;
+      bet[tid] = b_next;
+      g_next = b_next = 0.f;
+      if (tid < L && hv + 1 < (hk + 1) * grp) {
+        g_next = g[(t0 + tid) * H + hv + 1];
+        b_next = beta[(t0 + tid) * H + hv + 1];
+      }
     }
     __syncthreads();
     if (warp == 0) {

@@ -211,25 +211,46 @@ __device__ __forceinline__ void tri_inverse_64(const float* __restrict__ sA, flo
 // fp32 scratch.  All 256 threads participate; ends with a barrier.
 __device__ __forceinline__ void tri_inverse_64_inplace(float* __restrict__ sA,
                                                        float* __restrict__ sM, int tid) {
-  // 16x16 diagonal blocks: column c of block b by forward substitution
-  float x[16];
-  const int b = tid >> 4, c = tid & 15;
-  if (tid < 64) {
-    const float* Ab = sA + (16 * b) * LDF + 16 * b;
+  // 8x8 diagonal blocks: column c of block b by forward substitution (the
+  // serial chain is at most 28 FMAs)
+  {
+    float x[8];
+    const int b = tid >> 3, c = tid & 7;
+    if (tid < 64) {
+      const float* Ab = sA + (8 * b) * LDF + 8 * b;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] = (i == c) ? 1.f : 0.f;
+      for (int i = 0; i < 8; ++i) x[i] = (i == c) ? 1.f : 0.f;
 #pragma unroll
-    for (int i = 1; i < 16; ++i) {
-      float s = 0.f;
+      for (int i = 1; i < 8; ++i) {
+        float s = 0.f;
 #pragma unroll
-      for (int m = 0; m < i; ++m) s = fmaf(Ab[i * LDF + m], x[m], s);
-      if (i > c) x[i] = -s;
+        for (int m = 0; m < i; ++m) s = fmaf(Ab[i * LDF + m], x[m], s);
+        if (i > c) x[i] = -s;
+      }
     }
-  }
-  __syncthreads();
-  if (tid < 64) {
+    __syncthreads();
+    if (tid < 64) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) sA[(16 * b + i) * LDF + 16 * b + c] = x[i];
+      for (int i = 0; i < 8; ++i) sA[(8 * b + i) * LDF + 8 * b + c] = x[i];
+    }
+    __syncthreads();
+  }
+  // 8 -> 16 in each 16x16 diagonal block p: T10 = -T11 (A10 T00), one output
+  // per thread
+  {
+    const int p = tid >> 6, e = tid & 63, rr = e >> 3, cc = e & 7;
+    const int r0 = 16 * p + 8, c0 = 16 * p;  // A10 / T10 at rows r0.., cols c0..
+    float s = 0.f;
+#pragma unroll
+    for (int m = 0; m < 8; ++m)
+      if (m >= cc) s = fmaf(sA[(r0 + rr) * LDF + c0 + m], sA[(c0 + m) * LDF + c0 + cc], s);
+    sM[p * 64 + rr * 8 + cc] = s;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int m = 0; m < 8; ++m)
+      if (m <= rr) t = fmaf(sA[(r0 + rr) * LDF + r0 + m], sM[p * 64 + m * 8 + cc], t);
+    sA[(r0 + rr) * LDF + c0 + cc] = -t;
   }
   __syncthreads();
   // 16 -> 32: T10 = -T11 A10 T00 and T32 = -T33 A32 T22; one output pair per thread
