@@ -171,6 +171,24 @@ XOPS_API int64_t xops_chunk_gated_delta_rule_workspace_size(int64_t B, int64_t T
                                                    int64_t Hg, int64_t H, int64_t K,
                                                    int use_qk_l2norm_in_kernel, int varlen);
 
+/* xops_chunk_gated_delta_rule without a caller workspace, for callers that
+ * cannot allocate device memory when they run.  This entry has no
+ * counterpart in the reference.  Its scratch is one fixed 64 MiB array of
+ * the library's own device memory, so problems whose
+ * xops_chunk_gated_delta_rule_workspace_size() exceeds 64 MiB are rejected
+ * with XOPS_ERR_WORKSPACE.  The array's address is looked up on the first
+ * call on each device: make that call before any stream capture.  All calls
+ * on a device share the array, so calls that may overlap on the GPU (e.g.
+ * unordered streams) race; keep them ordered.  Arguments are those of
+ * xops_chunk_gated_delta_rule minus the workspace. */
+XOPS_API int xops_chunk_gated_delta_rule_noalloc(const void* q, const void* k, const void* v,
+                                        const float* g, const float* beta, const float* h0,
+                                        void* o, float* ht, const int32_t* cu_seqlens, int64_t B,
+                                        int64_t T, int64_t N, int64_t Hg, int64_t H, int64_t K,
+                                        int64_t V, int64_t q_token_stride,
+                                        int64_t k_token_stride, int64_t v_token_stride,
+                                        float scale, int use_qk_l2norm_in_kernel, void* stream);
+
 /* ---- chunk pipeline sub-operators (the reference's decomposition) ---- */
 /* All take the same sequence description (cu_seqlens [N+1] int32 with B == 1
  * or NULL with N == B) and chunk_size == 64. */

@@ -35,6 +35,9 @@ SIGNATURES = {
     "xops_chunk_gated_delta_rule": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _i64, _i64, _i64, _i64, _f, _int, _p, _i64, _p],
     "xops_chunk_gated_delta_rule_workspace_size": [_i64, _i64, _i64, _i64, _i64, _i64, _int, _int],
+    "xops_chunk_gated_delta_rule_noalloc": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
+                                            _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f, _int,
+                                            _p],
     "xops_chunk_local_cumsum": [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
     "xops_chunk_scaled_dot_kkt_fwd": [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                       _i64, _p],

@@ -39,6 +39,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "gdn_common.cuh"
 #include "tcgen05.cuh"
 
@@ -1121,4 +1123,75 @@ extern "C" int xops_device_error_count(void) {
   const int zero = 0;
   cudaMemcpyToSymbol(gdn::g_tc_error, &zero, sizeof(int));
   return v;
+}
+
+// ---------------------------------------------------------------------------
+// Chunked gated delta rule for callers that cannot allocate device memory
+// when they run: some serving setups reserve every device byte up front, or
+// run where the caching allocator is not available.  The computation is the
+// one of xops_chunk_gated_delta_rule; only its scratch differs: instead of a
+// caller workspace it uses one fixed array of this library's own device
+// memory, kStaticScratchBytes long.  Problems whose workspace would exceed
+// that size are rejected (XOPS_ERR_WORKSPACE) rather than partially served.
+//
+// The array's device address is looked up once per device with
+// cudaGetSymbolAddress, on the first call made on that device; make that
+// first call before any stream capture begins.  The array is shared by every
+// call on a device, so two calls whose kernels may overlap on the GPU (for
+// example on two streams without ordering between them) race on it; keep
+// such calls ordered.  No scratch byte needs to start at zero: every byte
+// the kernels read is written earlier in the same call.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int64_t kStaticScratchBytes = 64ll << 20;  // 64 MiB
+constexpr int kMaxDevices = 64;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+std::mutex g_static_scratch_mu;
+void* g_static_scratch_ptr[kMaxDevices] = {};
+
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return set_error(XOPS_ERR_CUDA, "chunk_gated_delta_rule_noalloc: cudaGetDevice: %s",
+                     cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(XOPS_ERR_UNSUPPORTED, "chunk_gated_delta_rule_noalloc: device %d >= %d", dev,
+                     kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (!g_static_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(XOPS_ERR_CUDA,
+                       "chunk_gated_delta_rule_noalloc: cudaGetSymbolAddress of the scratch: %s",
+                       cudaGetErrorString(e));
+    g_static_scratch_ptr[dev] = p;
+  }
+  *out = g_static_scratch_ptr[dev];
+  return XOPS_OK;
+}
+}  // namespace
+
+extern "C" int xops_chunk_gated_delta_rule_noalloc(
+    const void* q, const void* k, const void* v, const float* g, const float* beta,
+    const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
+    int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
+    int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
+    void* stream) {
+  const int64_t need = xops_chunk_gated_delta_rule_workspace_size(
+      B, T, N, Hg, H, K, use_qk_l2norm_in_kernel, cu_seqlens != nullptr);
+  if (need < 0)
+    return set_error(XOPS_ERR_INVALID_ARGUMENT, "chunk_gated_delta_rule_noalloc: bad shape");
+  if (need > kStaticScratchBytes)
+    return set_error(XOPS_ERR_WORKSPACE,
+                     "chunk_gated_delta_rule_noalloc: this problem needs %lld bytes of scratch but "
+                     "the fixed scratch holds %lld; call xops_chunk_gated_delta_rule with a "
+                     "workspace instead",
+                     (long long)need, (long long)kStaticScratchBytes);
+  void* ws = nullptr;
+  if (int rc = static_scratch(&ws)) return rc;
+  return xops_chunk_gated_delta_rule(q, k, v, g, beta, h0, o, ht, cu_seqlens, B, T, N, Hg, H, K,
+                                     V, q_token_stride, k_token_stride, v_token_stride, scale,
+                                     use_qk_l2norm_in_kernel, ws, kStaticScratchBytes, stream);
 }
