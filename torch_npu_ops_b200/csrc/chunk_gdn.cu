@@ -844,18 +844,30 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
 // ============================================================================
 // Kernel 3: segment start states, h_{s+1} = X_s^T h_s + B_s (fp32)
 // ============================================================================
-// Serial over the middle segments of one (sequence, head); the value columns
-// are independent, so CTA x owns columns [16x, 16x + 16).  X_s^T is staged in
-// shared memory per step (row stride 129 keeps the column walk conflict-free).
-constexpr int CB_NT = 256, CB_COLS = 16, CB_LD = 129;
-constexpr int CB_SMEM = (128 * CB_LD + 128 * CB_COLS) * 4;
+// Serial over the middle segments of one (sequence, head).  The value columns
+// are independent, so CTA x owns columns [8x, 8x + 8): thread (kk, half)
+// computes 4 of them for row kk.  The transitions X_s do not depend on the
+// states, so X_{s+1} streams into the second of two shared buffers (cp.async)
+// while step s computes; the serial part of a step is one 128-term dot
+// product per output.  Rows are 132 floats apart: 16-byte aligned, and a
+// quarter-warp's 16-byte row reads fall in distinct banks.
+constexpr int CB_NT = 256, CB_COLS = 8, CB_LD = 132;
+constexpr int CB_SMEM = (2 * 128 * CB_LD + 128 * CB_COLS) * 4 + 16;
+
+__device__ __forceinline__ void cb_load_x(float* dst, const float* src, int tid) {
+  for (int e = tid; e < 128 * 32; e += CB_NT) {
+    const int r = e >> 5, q4 = e & 31;
+    cp_async16(dst + r * CB_LD + q4 * 4, src + r * 128 + q4 * 4, 16);
+  }
+  cp_async_commit();
+}
 
 __global__ void __launch_bounds__(CB_NT) chunk_combine_kernel(const int32_t* __restrict__ cu,
                                                               int64_t N, int64_t T, int64_t H,
                                                               ChainPlan plan) {
-  extern __shared__ float cbs[];
-  float* xt = cbs;                   // X^T [kk][r]
-  float* cur = cbs + 128 * CB_LD;    // h_s[:, cols]  [r][CB_COLS]
+  extern __shared__ __align__(16) float cbs[];
+  float* xbuf = cbs;                      // two X^T buffers [kk][r], rows CB_LD apart
+  float* cur = cbs + 2 * 128 * CB_LD;     // h_s[:, cols]  [r][CB_COLS]
   __shared__ int64_t slot_sh;
   __shared__ int nseg_sh;
   const int tid = threadIdx.x;
@@ -877,38 +889,43 @@ __global__ void __launch_bounds__(CB_NT) chunk_combine_kernel(const int32_t* __r
   const int nseg = nseg_sh;
   if (nseg < 3) return;
   const int64_t slot = slot_sh;
-  const int kk = tid >> 1, cb = (tid & 1) * 8;
+  const int kk = tid >> 1, cb = (tid & 1) * 4;
+  cb_load_x(xbuf, seg_state(plan, slot + 1, H, h, 2), tid);
   {
     const float* h1 = seg_state(plan, slot + 1, H, h, 0);
     for (int e = tid; e < 128 * CB_COLS; e += CB_NT)
       cur[e] = h1[(e / CB_COLS) * 128 + v0 + (e % CB_COLS)];
   }
   for (int s = 1; s <= nseg - 2; ++s) {
-    const float* xs = seg_state(plan, slot + s, H, h, 2);
-    const float* bs = seg_state(plan, slot + s, H, h, 1);
-    float* nx = seg_state(plan, slot + s + 1, H, h, 0);
-    for (int e = tid; e < 128 * 32; e += CB_NT) {
-      const int r = e >> 5, q4 = e & 31;
-      const float4 x = reinterpret_cast<const float4*>(xs + r * 128)[q4];
-      float* d = xt + r * CB_LD + q4 * 4;
-      d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+    const float* xs_cur = xbuf + ((s - 1) & 1) * 128 * CB_LD;
+    if (s + 1 <= nseg - 2) {
+      cb_load_x(xbuf + (s & 1) * 128 * CB_LD, seg_state(plan, slot + s + 1, H, h, 2), tid);
+      cp_async_wait_group<1>();  // X_s has landed; X_{s+1} may still be in flight
+    } else {
+      cp_async_wait_all();
     }
+    const float4 bv =
+        *reinterpret_cast<const float4*>(seg_state(plan, slot + s, H, h, 1) + kk * 128 + v0 + cb);
     __syncthreads();
-    float acc[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[c] = bs[kk * 128 + v0 + cb + c];
+    float acc[4] = {bv.x, bv.y, bv.z, bv.w};
+    const float* xrow = xs_cur + kk * CB_LD;
 #pragma unroll 4
-    for (int r = 0; r < 128; ++r) {
-      const float m = xt[kk * CB_LD + r];
+    for (int r = 0; r < 128; r += 4) {
+      const float4 xv = *reinterpret_cast<const float4*>(xrow + r);
+      const float xr[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-      for (int c = 0; c < 8; ++c) acc[c] = fmaf(m, cur[r * CB_COLS + cb + c], acc[c]);
+      for (int u = 0; u < 4; ++u) {
+        const float4 hv = *reinterpret_cast<const float4*>(cur + (r + u) * CB_COLS + cb);
+        acc[0] = fmaf(xr[u], hv.x, acc[0]);
+        acc[1] = fmaf(xr[u], hv.y, acc[1]);
+        acc[2] = fmaf(xr[u], hv.z, acc[2]);
+        acc[3] = fmaf(xr[u], hv.w, acc[3]);
+      }
     }
-    __syncthreads();
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      cur[kk * CB_COLS + cb + c] = acc[c];
-      nx[kk * 128 + v0 + cb + c] = acc[c];
-    }
+    __syncthreads();  // every thread is done reading h_s and X_s
+    *reinterpret_cast<float4*>(cur + kk * CB_COLS + cb) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(seg_state(plan, slot + s + 1, H, h, 0) + kk * 128 + v0 + cb) =
+        make_float4(acc[0], acc[1], acc[2], acc[3]);
     __syncthreads();
   }
 }

@@ -133,6 +133,11 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
+// At most N of this thread's committed cp.async groups still pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
 
 // Loads a [64 x 128] bf16 tile (rows t0..t0+63 with global row stride
 // `stride` elements; rows >= L are zero) into smem with row stride LD128.
