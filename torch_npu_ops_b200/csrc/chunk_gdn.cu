@@ -696,13 +696,19 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     const int vrow = quarter * 32 + lane;
     const int kc0 = colq * C_SCOLS;      // state columns owned
     const int tc0 = colq * C_TCOLS;      // token columns owned in 64-wide regions
-    float S[C_SCOLS];
+    // the state as fp32 pairs (columns 2m, 2m+1), updated with packed f32x2
+    // instructions: the epilogue is issue-bound, 16 warps on 4 schedulers
+    float2 S[C_SCOLS / 2];
     {
       const float* src = it_init;
 #pragma unroll
-      for (int i = 0; i < C_SCOLS; ++i)
-        S[i] = kind == ITEM_TRANS ? (kc0 + i == vrow ? 1.f : 0.f)
-                                  : (src ? src[(kc0 + i) * V + vrow] : 0.f);
+      for (int m = 0; m < C_SCOLS / 2; ++m) {
+        const int c = kc0 + 2 * m;
+        S[m] = kind == ITEM_TRANS
+                   ? make_float2(c == vrow ? 1.f : 0.f, c + 1 == vrow ? 1.f : 0.f)
+                   : (src ? make_float2(src[c * V + vrow], src[(c + 1) * V + vrow])
+                          : make_float2(0.f, 0.f));
+      }
     }
     float gl_prev = 0.f;
     int L_prev = 0;
@@ -738,8 +744,11 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       tc::tmem_wait_ld();
       __syncwarp();  // the previous transpose has been read out
 #pragma unroll
-      for (int c = 0; c < 16; ++c)
-        *reinterpret_cast<bf16*>(ost + c * 64 + lane * 2) = __float2bfloat16_rn(ov[c] * scale);
+      for (int c = 0; c < 16; c += 2) {
+        const uint32_t w = pack2<bf16>(fmul2(make_float2(ov[c], ov[c + 1]), make_float2(scale, scale)));
+        *reinterpret_cast<uint16_t*>(ost + c * 64 + lane * 2) = (uint16_t)(w & 0xffffu);
+        *reinterpret_cast<uint16_t*>(ost + (c + 1) * 64 + lane * 2) = (uint16_t)(w >> 16);
+      }
       __syncwarp();
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
@@ -752,13 +761,15 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       }
     };
     auto apply_ds = [&](float dl) {  // S = e^{gl} S + dS
+      const float2 dl2 = make_float2(dl, dl);
 #pragma unroll
       for (int cb = 0; cb < 2; ++cb) {  // 16 columns at a time keeps registers under 96
         float d[16];
         tc::tmem_ld16(tm_addr(tm, quarter, C_TM_DS + kc0 + cb * 16), d);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) S[cb * 16 + i] = fmaf(S[cb * 16 + i], dl, d[i]);
+        for (int m = 0; m < 8; ++m)
+          S[cb * 8 + m] = ffma2(S[cb * 8 + m], dl2, make_float2(d[2 * m], d[2 * m + 1]));
       }
     };
     for (int i = 0; i < NI; ++i) {
@@ -772,7 +783,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       {
         uint32_t pk[16];
 #pragma unroll
-        for (int m = 0; m < 16; ++m) pk[m] = pack_bf16(S[2 * m], S[2 * m + 1]);
+        for (int m = 0; m < 16; ++m) pk[m] = pack2<bf16>(S[m]);
         tc::tmem_st16u(tm_addr(tm, quarter, C_TM_HT + kc0 / 2), pk);
       }
       warp_arrive(&bar_ht);
@@ -789,13 +800,16 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       {
         uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float s0 = du[2 * u] * tab[tc0 + 2 * u];
-          const float s1 = du[2 * u + 1] * tab[tc0 + 2 * u + 1];
-          const float h0f = __bfloat162float(__float2bfloat16_rn(s0));
-          const float h1f = __bfloat162float(__float2bfloat16_rn(s1));
-          hi[u] = pack_bf16(h0f, h1f);
-          lo[u] = pack_bf16(s0 - h0f, s1 - h1f);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 e4 = *reinterpret_cast<const float4*>(tab + tc0 + 4 * q4);
+#pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            const int u = 2 * q4 + p;
+            const float2 sc = fmul2(make_float2(du[2 * u], du[2 * u + 1]),
+                                    p == 0 ? make_float2(e4.x, e4.y) : make_float2(e4.z, e4.w));
+            hi[u] = pack2<bf16>(sc);
+            lo[u] = pack2<bf16>(fsub2(sc, unpack2<bf16>(hi[u])));
+          }
         }
         tc::tmem_st8u(tm_addr(tm, quarter, C_TM_VTH + tc0 / 2), hi);
         tc::tmem_st8u(tm_addr(tm, quarter, C_TM_VTL + tc0 / 2), lo);
@@ -815,11 +829,16 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         tc::tmem_ld16(tm_addr(tm, quarter, C_TM_QH + tc0), qh);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int u = 0; u < 16; ++u) qh[u] *= tab[64 + tc0 + u];
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 e4 = *reinterpret_cast<const float4*>(tab + 64 + tc0 + 4 * q4);
+          const float2 a = fmul2(make_float2(qh[4 * q4], qh[4 * q4 + 1]), make_float2(e4.x, e4.y));
+          const float2 b = fmul2(make_float2(qh[4 * q4 + 2], qh[4 * q4 + 3]), make_float2(e4.z, e4.w));
+          qh[4 * q4] = a.x; qh[4 * q4 + 1] = a.y; qh[4 * q4 + 2] = b.x; qh[4 * q4 + 3] = b.y;
+        }
         tc::tmem_st16(tm_addr(tm, quarter, C_TM_O + tc0), qh);
         uint32_t vn[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) vn[u] = pack_bf16(du[2 * u], du[2 * u + 1]);
+        for (int u = 0; u < 8; ++u) vn[u] = pack2<bf16>(make_float2(du[2 * u], du[2 * u + 1]));
         tc::tmem_st8u(tm_addr(tm, quarter, C_TM_VN + tc0 / 2), vn);
         warp_arrive(&bar_o);
       }
@@ -833,7 +852,10 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     if (live && it_out) {
       float* dst = it_out;
 #pragma unroll
-      for (int i = 0; i < C_SCOLS; ++i) dst[(kc0 + i) * V + vrow] = S[i];
+      for (int m = 0; m < C_SCOLS / 2; ++m) {
+        dst[(kc0 + 2 * m) * V + vrow] = S[m].x;
+        dst[(kc0 + 2 * m + 1) * V + vrow] = S[m].y;
+      }
     }
   }
   tc::fence_before();
