@@ -37,6 +37,11 @@ CASES = [  # (M, N, group, rms, bias, z, before, xdtype, wdtype)
     (37, 4096, 4096, True, True, False, True, torch.bfloat16, torch.float32),
     (5, 8192, 8192, False, False, True, False, torch.float32, torch.float32),
     (64, 96, 96, True, False, False, True, torch.float32, torch.float32),
+    # streaming (bulk-copy) path: 16-bit, contiguous rows, >= 8192 segments
+    (2048, 512, 64, False, True, True, False, torch.bfloat16, torch.bfloat16),  # LN, gate first
+    (4100, 512, 128, True, True, True, True, torch.bfloat16, torch.float32),     # partial tile
+    (1000, 2048, 256, True, False, True, True, torch.float16, torch.float16),
+    (3000, 768, 256, False, False, False, True, torch.bfloat16, torch.bfloat16),  # LN, no gate
 ]
 
 

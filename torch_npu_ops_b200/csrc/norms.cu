@@ -7,7 +7,10 @@
 // statistics are warp-shuffle reductions, so there is no shared memory and no
 // block-wide barrier.  Segments longer than 32*64 elements use a block per
 // segment with a two-pass loop over global memory.
+#include <algorithm>
+
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace xops {
 namespace {
@@ -254,11 +257,182 @@ int launch_ln_warp(const void* x, const void* w, const void* b, const void* z, v
   return check_launch("layer_norm_fwd");
 }
 
+
+// ----------------------------------------------------------------------------
+// Short-group path for 16-bit tensors with contiguous rows (the gated
+// RMSNorm's 128-wide groups of [tokens x heads*128]): the (row, group)
+// segments are then contiguous in memory, so a tile of segments of x (and z)
+// is one contiguous range.  A persistent CTA streams tiles of ~16 KB per
+// tensor with 1-D bulk copies into a ring of RN_NS shared stages (warp 0),
+// and 8 consumer warps normalise them: LPR = G / 8 lanes per segment, one
+// 16-byte piece each, shuffle reductions inside the lane group, 16-byte
+// stores of y.  Loads in flight per SM no longer depend on registers.
+// ----------------------------------------------------------------------------
+constexpr int RN_NS = 3, RN_TILE_BYTES = 16384, RN_NT = 32 + 256;
+constexpr uint32_t RN_WAIT = 1u << 26;
+__device__ int g_norm_error = 0;
+
+template <typename TX, typename TW, int G, bool RMS, bool HAS_Z, bool HAS_B>
+__global__ void __launch_bounds__(RN_NT, 2) layer_norm_stream_kernel(
+    const TX* __restrict__ x, const TW* __restrict__ w, const TW* __restrict__ b,
+    const TX* __restrict__ z, TX* __restrict__ y, float* __restrict__ mean_out,
+    float* __restrict__ rstd_out, int64_t M, int64_t ngroups, float eps, bool norm_before_gate) {
+  constexpr int SEGS = RN_TILE_BYTES / (G * 2);   // segments per tile
+  constexpr int LPR = G / 8;                       // lanes per segment
+  constexpr int SPW = 32 / LPR;                    // segments per warp pass
+  constexpr int STAGE = (HAS_Z ? 2 : 1) * RN_TILE_BYTES;
+  extern __shared__ unsigned char rn_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(rn_raw) + 127) & ~static_cast<uintptr_t>(127));
+  __shared__ uint64_t full[RN_NS], empty[RN_NS];
+  __shared__ int abort_sh;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t total = M * ngroups;
+  const int64_t tiles = (total + SEGS - 1) / SEGS;
+  if (tid == 0) {
+    for (int s = 0; s < RN_NS; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 8);
+    }
+    tc::mbar_fence_init();
+    abort_sh = 0;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int64_t k = 0;; ++k) {
+        const int64_t t = blockIdx.x + k * gridDim.x;
+        if (t >= tiles) break;
+        const int s = (int)(k % RN_NS);
+        if (k >= RN_NS && !tc::mbar_wait(&empty[s], (uint32_t)((k / RN_NS - 1) & 1), RN_WAIT)) {
+          atomicExch(&g_norm_error, 1);
+          atomicExch(&abort_sh, 1);
+          break;
+        }
+        if (*(volatile int*)&abort_sh) break;
+        const int64_t s0 = t * SEGS;
+        const int n = (int)(total - s0 < SEGS ? total - s0 : SEGS);
+        const uint32_t bytes = (uint32_t)n * G * 2;
+        unsigned char* st = sm + s * STAGE;
+        tc::mbar_arrive_expect_tx(&full[s], (HAS_Z ? 2 : 1) * bytes);
+        tc::bulk_load(st, x + s0 * G, bytes, &full[s]);
+        if constexpr (HAS_Z) tc::bulk_load(st + RN_TILE_BYTES, z + s0 * G, bytes, &full[s]);
+      }
+    }
+    return;
+  }
+  const int cw = warp - 1, sub = lane / LPR, li = lane % LPR;
+  for (int64_t k = 0;; ++k) {
+    const int64_t t = blockIdx.x + k * gridDim.x;
+    if (t >= tiles) break;
+    const int s = (int)(k % RN_NS);
+    if (!tc::mbar_wait(&full[s], (uint32_t)((k / RN_NS) & 1), RN_WAIT)) {
+      atomicExch(&g_norm_error, 1);
+      break;
+    }
+    const unsigned char* st = sm + s * STAGE;
+    const int64_t s0 = t * SEGS;
+#pragma unroll
+    for (int p = 0; p < SEGS / (8 * SPW); ++p) {
+      const int si = (p * 8 + cw) * SPW + sub;  // segment in tile
+      const int64_t seg = s0 + si;
+      const bool live = seg < total;
+      const uint4 xr = *reinterpret_cast<const uint4*>(st + si * (G * 2) + li * 16);
+      float2 xv[4] = {unpack2<TX>(xr.x), unpack2<TX>(xr.y), unpack2<TX>(xr.z), unpack2<TX>(xr.w)};
+      float2 gz[4];
+      if constexpr (HAS_Z) {
+        const uint4 zr =
+            *reinterpret_cast<const uint4*>(st + RN_TILE_BYTES + si * (G * 2) + li * 16);
+        gz[0] = silu2_lowp(unpack2<TX>(zr.x));
+        gz[1] = silu2_lowp(unpack2<TX>(zr.y));
+        gz[2] = silu2_lowp(unpack2<TX>(zr.z));
+        gz[3] = silu2_lowp(unpack2<TX>(zr.w));
+        if (!norm_before_gate) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) xv[u] = fmul2(xv[u], gz[u]);
+        }
+      }
+      float mu = 0.f;
+      if constexpr (!RMS) {
+        float sum = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sum += xv[u].x + xv[u].y;
+#pragma unroll
+        for (int o = LPR / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        mu = sum * (1.0f / G);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) xv[u] = fsub2(xv[u], make_float2(mu, mu));
+      }
+      float2 ss2 = fmul2(xv[0], xv[0]);
+#pragma unroll
+      for (int u = 1; u < 4; ++u) ss2 = ffma2(xv[u], xv[u], ss2);
+      float ss = ss2.x + ss2.y;
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rstd = rsqrtf(ss * (1.0f / G) + eps);
+      if (live) {
+        const uint32_t row = (uint32_t)(seg / ngroups), grp = (uint32_t)(seg - (int64_t)row * ngroups);
+        if (li == 0) {
+          rstd_out[(int64_t)grp * M + row] = rstd;
+          if constexpr (!RMS) mean_out[(int64_t)grp * M + row] = mu;
+        }
+        float wv[8], bv[8];
+        load_vec<TW, 8>(w + (int64_t)grp * G + li * 8, wv);
+        if constexpr (HAS_B) load_vec<TW, 8>(b + (int64_t)grp * G + li * 8, bv);
+        uint4 out;
+        uint32_t* po = &out.x;
+        const float2 r2 = make_float2(rstd, rstd);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float2 v = fmul2(fmul2(xv[u], r2), make_float2(wv[2 * u], wv[2 * u + 1]));
+          if constexpr (HAS_B) v = fadd2(v, make_float2(bv[2 * u], bv[2 * u + 1]));
+          if constexpr (HAS_Z) {
+            if (norm_before_gate) v = fmul2(v, gz[u]);
+          }
+          po[u] = pack2<TX>(v);
+        }
+        *reinterpret_cast<uint4*>(y + seg * G + li * 8) = out;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&empty[s]);
+  }
+}
+
+template <typename TX, typename TW, int GG, bool RMS, bool HAS_Z, bool HAS_B>
+int launch_ln_stream(const void* x, const void* w, const void* b, const void* z, void* y,
+                     float* mean, float* rstd, int64_t M, int64_t ng, float eps, bool nbg,
+                     cudaStream_t st) {
+  constexpr int SEGS = RN_TILE_BYTES / (GG * 2);
+  constexpr int SMEM = RN_NS * (HAS_Z ? 2 : 1) * RN_TILE_BYTES + 128;
+  auto kern = layer_norm_stream_kernel<TX, TW, GG, RMS, HAS_Z, HAS_B>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+    return set_error(XOPS_ERR_CUDA, "layer_norm_fwd: shared-memory attribute failed");
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t tiles = cdiv64(M * ng, SEGS);
+  const unsigned grid = (unsigned)std::min<int64_t>(tiles, 2 * (int64_t)sms);
+  kern<<<grid, RN_NT, SMEM, st>>>((const TX*)x, (const TW*)w, (const TW*)b, (const TX*)z, (TX*)y,
+                                  mean, rstd, M, ng, eps, nbg);
+  return check_launch("layer_norm_fwd");
+}
+
 template <typename TX, typename TW, bool RMS, bool HAS_Z, bool HAS_B>
 int dispatch_ln(const void* x, const void* w, const void* b, const void* z, void* y, float* mean,
                 float* rstd, int64_t M, int64_t N, int64_t G, int64_t sx, int64_t sz, int64_t sy,
                 float eps, bool nbg, cudaStream_t st) {
   const int64_t ng = N / G;
+  // streaming path: 16-bit, contiguous rows (segments adjacent in memory),
+  // enough segments to keep a grid of persistent CTAs busy
+  if constexpr (sizeof(TX) == 2) {
+    const bool contiguous = sx == N && sy == N && (!HAS_Z || sz == N);
+    if (contiguous && M * ng >= 8192 && M * ng < (int64_t(1) << 31)) {
+      if (G == 64) return launch_ln_stream<TX, TW, 64, RMS, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st);
+      if (G == 128) return launch_ln_stream<TX, TW, 128, RMS, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st);
+      if (G == 256) return launch_ln_stream<TX, TW, 256, RMS, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st);
+    }
+  }
   // packed path: 16-byte lanes, several short segments per warp
   constexpr int VEC = 16 / (int)sizeof(TX);
 #define XOPS_LN_PACKED(GG)                                                                  \
