@@ -178,7 +178,7 @@ def stage_bytes(cfg, kind):
 
 
 # ------------------------------------------------------------- reference ----
-def cpu_reference(kind, T_sample, reps=3):
+def cpu_reference(kind, T_sample, reps=3, warmup=1):
     """Times the CPU oracle (the reference's torch algorithm) on a bounded
     sample of the workload with every host thread; returns tokens/s info."""
     import oracle
@@ -206,7 +206,8 @@ def cpu_reference(kind, T_sample, reps=3):
                                          w["z"].reshape(-1, d), d, True, True)[0]
         sample = (f"conv->chunk GDN->gated RMSNorm oracle on the first {T_sample} tokens of the "
                   "65536-token sequence, all 32 heads")
-    fn()  # warm-up
+    for _ in range(max(1, warmup)):
+        fn()
     ts = []
     for _ in range(reps):
         t = time.perf_counter()
@@ -218,13 +219,85 @@ def cpu_reference(kind, T_sample, reps=3):
 
 
 # ------------------------------------------------------------------ main ----
+def kernel_sweep(dev, peaks):
+    """Achieved HBM bandwidth of every bandwidth-bound operator at its
+    configuration size and at a size well above L2: CUDA events around each
+    launch, L2 flushed (256 MB written) before every launch, median of 10.
+    Bytes are the algorithmic bytes (every input read once, every output
+    written once)."""
+    import statistics
+    import torch_npu_ops_b200 as ops
+    from torch_npu_ops_b200 import workloads
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def timed(fn, reps=10):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            ts.append(s.elapsed_time(e))
+        return statistics.median(ts)
+
+    out = {}
+
+    def add(name, fn, nbytes):
+        ms = timed(fn)
+        gbs = nbytes / (ms / 1000.0) / 1e9
+        out[name] = {"bytes": int(nbytes), "ms": ms, "GB/s": gbs, "frac_hbm": gbs / peaks["hbm_gbs"]}
+
+    for T in (128, 16384):  # a1: cfg1 shape, and a token sweep point
+        r = workloads.rope_config1(T=T)
+        t = [x.to(dev) for x in r["tensors"]]
+        add(f"split_rmsnorm_rope fp32 T={T}", lambda: ops.npu_split_rmsnorm_rope(*t, **r["kwargs"]),
+            4 * T * (5120 + 5120) + 2 * 4 * T * 64 + 2 * 4 * 256)
+    for Bd in (256, 4096):  # a3: cfg2 decode, and a larger batch
+        d = workloads.conv_decode_config2(batch=Bd)
+        cx, cs, cw, cb = (d[k].to(dev) for k in ("x", "conv_state", "weight", "bias"))
+        add(f"causal_conv1d_update B={Bd}",
+            lambda: ops.npu_causal_conv1d_update(cx, cs, cw, True, cb),
+            2 * 2 * Bd * 8192 + 2 * 2 * Bd * 8192 * 3 + 2 * 8192 * 5)
+    dec = workloads.decode_config4()
+    a = {n: (t.to(dev) if torch.is_tensor(t) else t) for n, t in dec.items()}
+    st = a["state"].clone()
+    add("fused_recurrent_gated_delta_rule cfg4 B=256",  # a10
+        lambda: ops.npu_fused_recurrent_gated_delta_rule(
+            a["q"], a["k"], a["v"], a["g"], a["beta"], None, st, True, a["cu_seqlens"],
+            a["ssm_state_indices"], None, True),
+        2 * st.numel() * 4 + 2 * a["q"].numel() * 2 + 2 * a["v"].numel() * 2 + 2 * a["g"].numel() * 4)
+    for M in (8192, 2097152):  # a11: cfg4 (256 x 32 heads) and the cfg5 size
+        x = torch.randn(M, 128, device=dev).to(torch.bfloat16)
+        z = torch.randn(M, 128, device=dev).to(torch.bfloat16)
+        w = torch.ones(128, device=dev, dtype=torch.bfloat16)
+        add(f"gated RMSNorm g128 rows={M}",
+            lambda: ops.layer_norm_fwd(x, w, None, 1e-6, z, 128, True, True), 3 * 2 * M * 128 + 4 * M)
+    for M in (256, 65536):  # a12 / a13: cfg4 hidden [256, 2048], and a large batch
+        x = torch.randn(M, 2048, device=dev).to(torch.bfloat16)
+        w = torch.ones(2048, device=dev, dtype=torch.bfloat16)
+        b = torch.zeros(2048, device=dev, dtype=torch.bfloat16)
+        add(f"layer_norm_fwd [{M},2048]",
+            lambda: ops.layer_norm_fwd(x, w, b, 1e-6, None, 2048, True, False),
+            2 * 2 * M * 2048 + 8 * M + 4 * 2048)
+        add(f"gemma_rms_norm [{M},2048]", lambda: ops.npu_gemma_rms_norm(x, w, 1e-6),
+            2 * 2 * M * 2048 + 4 * M + 2 * 2048)
+    x = torch.randn(65536 * 16, 128, device=dev).to(torch.bfloat16)  # a14: q/k heads of cfg5
+    add("l2norm_last_dim [1048576,128]", lambda: ops.npu_l2norm_last_dim(x, 1e-6), 2 * 2 * x.numel())
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cfg5", choices=["cfg5", "cfg3"])
+    ap.add_argument("--workload", default="cfg5", choices=["cfg5", "cfg3", "kernels"],
+                    help="kernels: HBM bandwidth of every bandwidth-bound operator")
     ap.add_argument("--tokens", type=int, default=65536)
     ap.add_argument("--cpu-sample", type=int, default=8192)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -251,9 +324,7 @@ def main():
     if a.impl == "reference":
         if rank != 0:
             return
-        ref = cpu_reference(kind, a.cpu_sample)
-        for _ in range(max(0, a.warmup - 1)):
-            pass
+        ref = cpu_reference(kind, a.cpu_sample, reps=a.steps, warmup=a.warmup)
         line = {"impl": "reference", "metric": METRIC, "value": ref["value"], "unit": "tokens/s",
                 "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
                 "ms_per_step": 1000.0 * ref["seconds_per_sample"], "higher_is_better": True,
@@ -269,6 +340,14 @@ def main():
     _lib.load()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if kind == "kernels":
+        if rank == 0:
+            peaks = _peaks()
+            print(json.dumps({"metric": "HBM GB/s of the bandwidth-bound operators",
+                              "workload": "kernels", "l2_flush": "256 MB written before each launch",
+                              "hbm_peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"],
+                              "kernels": kernel_sweep(dev, peaks)}))
+        return
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
