@@ -42,6 +42,13 @@ CASES = [  # (M, N, group, rms, bias, z, before, xdtype, wdtype)
     (4100, 512, 128, True, True, True, True, torch.bfloat16, torch.float32),     # partial tile
     (1000, 2048, 256, True, False, True, True, torch.float16, torch.float16),
     (3000, 768, 256, False, False, False, True, torch.bfloat16, torch.bfloat16),  # LN, no gate
+    # wide streaming path: one warp per segment, >= 4 MB of x
+    (1100, 2048, 2048, False, True, False, True, torch.bfloat16, torch.bfloat16),  # LN cfg4 row
+    (600, 4096, 1024, True, False, True, False, torch.bfloat16, torch.float32),    # gate first
+    (520, 8192, 8192, False, True, True, True, torch.float16, torch.float16),      # 1 seg / tile
+    (4200, 1024, 512, True, True, False, True, torch.bfloat16, torch.bfloat16),    # 4 / warp
+    (130, 16384, 16384, False, False, False, True, torch.bfloat16, torch.bfloat16),
+    (4099, 1040, 520, False, True, False, True, torch.bfloat16, torch.bfloat16),   # odd tiles
 ]
 
 
@@ -71,7 +78,10 @@ def test_layer_norm_strided_rows():
 
 
 @pytest.mark.parametrize("shape,dt", [((256, 2048), torch.bfloat16), ((4, 128, 4096), torch.float16),
-                                      ((4, 128, 4096), torch.float32), ((3, 100), torch.bfloat16)])
+                                      ((4, 128, 4096), torch.float32), ((3, 100), torch.bfloat16),
+                                      ((2048, 2048), torch.bfloat16),   # wide streaming path
+                                      ((1100, 4000), torch.float16),
+                                      ((9000, 128), torch.bfloat16)])   # narrow streaming path
 def test_gemma_rms_norm(shape, dt):
     g = torch.Generator().manual_seed(1234)
     x = torch.randn(*shape, generator=g).to(dt)
@@ -91,3 +101,14 @@ def test_l2norm_golden(case):
     y = ops.npu_l2norm_last_dim(x.to(DEV), case["args"]["eps"])
     ref = oracle.l2norm_last_dim(x, case["args"]["eps"])
     (assert_fp32 if x.dtype == torch.float32 else assert_bf16)(y, ref)
+
+
+@pytest.mark.parametrize("shape", [(20000, 128), (9000, 64), (9000, 256), (3000, 1024), (700, 4104)])
+def test_l2norm_streaming(shape):
+    """bf16 rows large enough for the bulk-copy streaming path (narrow and wide)."""
+    from torch_npu_ops_b200 import _lib
+    g = torch.Generator().manual_seed(shape[0] + shape[1])
+    x = (3 * torch.randn(*shape, generator=g)).to(torch.bfloat16)
+    y = ops.npu_l2norm_last_dim(x.to(DEV), 1e-6)
+    assert_bf16(y, oracle.l2norm_last_dim(x, 1e-6))
+    assert _lib.load().xops_device_error_count() == 0

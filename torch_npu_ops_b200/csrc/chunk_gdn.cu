@@ -1161,7 +1161,9 @@ extern "C" int xops_device_error_count(void) {
   if (cudaMemcpyFromSymbol(&v, gdn::g_tc_error, sizeof(int)) != cudaSuccess) return -1;
   const int zero = 0;
   cudaMemcpyToSymbol(gdn::g_tc_error, &zero, sizeof(int));
-  return v;
+  const int vn = xops::take_norm_error(), vc = xops::take_conv_error();
+  if (vn < 0 || vc < 0) return -1;
+  return v + vn + vc;
 }
 
 // ---------------------------------------------------------------------------

@@ -13,6 +13,10 @@ namespace xops {
 // ---- status plumbing (defined in capi.cu) --------------------------------
 int set_error(int status, const char* fmt, ...);
 int check_launch(const char* what);
+// wait-timeout flags of the streaming kernels: value since the last call
+// (then cleared), -1 when the flag cannot be read
+int take_norm_error();
+int take_conv_error();
 
 #define XOPS_REQUIRE(cond, ...)                                              \
   do {                                                                       \

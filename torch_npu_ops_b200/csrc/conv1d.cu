@@ -571,6 +571,14 @@ int launch_varlen_w(int W, const void* x, void* state, const void* w, const void
 }
 
 }  // namespace
+
+int take_conv_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_conv_error, sizeof(int)) != cudaSuccess) return -1;
+  const int zero = 0;
+  cudaMemcpyToSymbol(g_conv_error, &zero, sizeof(int));
+  return v;
+}
 }  // namespace xops
 
 using namespace xops;

@@ -259,21 +259,105 @@ int launch_ln_warp(const void* x, const void* w, const void* b, const void* z, v
 
 
 // ----------------------------------------------------------------------------
-// Short-group path for 16-bit tensors with contiguous rows (the gated
-// RMSNorm's 128-wide groups of [tokens x heads*128]): the (row, group)
-// segments are then contiguous in memory, so a tile of segments of x (and z)
-// is one contiguous range.  A persistent CTA streams tiles of ~16 KB per
-// tensor with 1-D bulk copies into a ring of RN_NS shared stages (warp 0),
-// and 8 consumer warps normalise them: LPR = G / 8 lanes per segment, one
-// 16-byte piece each, shuffle reductions inside the lane group, 16-byte
-// stores of y.  Loads in flight per SM no longer depend on registers.
+// Streaming path for 16-bit tensors with contiguous rows.  The (row, group)
+// segments are then contiguous in memory, so a tile of whole segments of x
+// (and z) is one contiguous range.  A persistent CTA streams tiles with 1-D
+// bulk copies into a ring of RN_NS shared stages (warp 0 issues them) and 8
+// consumer warps normalise from shared memory and store y with 16-byte
+// stores, so the bytes in flight per SM do not depend on registers.
+//
+// One kernel family serves the three operators; KIND selects the statistics
+// and the affine step:
+//   LN     y = (x - mean) * rstd * w (+ b),  mean and rstd written
+//   RMS    y = x * rstd * w (+ b),           rstd written
+//   GEMMA  y = x * rstd * (1 + w),           rstd written (one group per row)
+//   L2     y = x * rsqrt(sum x^2 + eps),     nothing else written
+// with rstd = rsqrt(mean of squares (centred for LN) + eps) and the SiLU gate
+// z * sigmoid(z) applied to x before the statistics or to y after them.
+//
+// Narrow segments (G <= 256): LPR = G / 8 lanes share one segment, one 16-byte
+// piece each, shuffle reductions inside the lane group.
+// Wide segments (256 < G <= 16384): one warp per segment, lane-strided 16-byte
+// pieces, one pass over shared memory per statistic plus the output pass.
 // ----------------------------------------------------------------------------
+enum NormKind { K_LN = 0, K_RMS = 1, K_GEMMA = 2, K_L2 = 3 };
 constexpr int RN_NS = 3, RN_TILE_BYTES = 16384, RN_NT = 32 + 256;
 constexpr uint32_t RN_WAIT = 1u << 26;
 __device__ int g_norm_error = 0;
 
-template <typename TX, typename TW, int G, bool RMS, bool HAS_Z, bool HAS_B>
-__global__ void __launch_bounds__(RN_NT, 2) layer_norm_stream_kernel(
+// the affine step of one 8-element piece: v = xhat (already centred and
+// scaled by rstd), w / b / gate per element
+template <typename TW, int KIND, bool HAS_Z, bool HAS_B>
+__device__ __forceinline__ void norm_affine(float2 (&v)[4], const TW* __restrict__ w,
+                                            const TW* __restrict__ b, const float2 (&gz)[4],
+                                            bool gate_after) {
+  if constexpr (KIND == K_L2) return;
+  float wv[8], bv[8];
+  load_vec<TW, 8>(w, wv);
+  if constexpr (HAS_B) load_vec<TW, 8>(b, bv);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    float2 wu = make_float2(wv[2 * u], wv[2 * u + 1]);
+    if constexpr (KIND == K_GEMMA) wu = fadd2(wu, make_float2(1.f, 1.f));
+    v[u] = fmul2(v[u], wu);
+    if constexpr (HAS_B) v[u] = fadd2(v[u], make_float2(bv[2 * u], bv[2 * u + 1]));
+    if constexpr (HAS_Z) {
+      if (gate_after) v[u] = fmul2(v[u], gz[u]);
+    }
+  }
+}
+
+template <typename TX>
+__device__ __forceinline__ void unpack8(const uint4 r, float2 (&v)[4]) {
+  v[0] = unpack2<TX>(r.x);
+  v[1] = unpack2<TX>(r.y);
+  v[2] = unpack2<TX>(r.z);
+  v[3] = unpack2<TX>(r.w);
+}
+template <typename TX>
+__device__ __forceinline__ uint4 pack8(const float2 (&v)[4]) {
+  return make_uint4(pack2<TX>(v[0]), pack2<TX>(v[1]), pack2<TX>(v[2]), pack2<TX>(v[3]));
+}
+template <typename TX>
+__device__ __forceinline__ void silu8(const uint4 r, float2 (&g)[4]) {
+  g[0] = silu2_lowp(unpack2<TX>(r.x));
+  g[1] = silu2_lowp(unpack2<TX>(r.y));
+  g[2] = silu2_lowp(unpack2<TX>(r.z));
+  g[3] = silu2_lowp(unpack2<TX>(r.w));
+}
+
+// Producer / ring bookkeeping shared by both widths.  Tiles hold SPT whole
+// segments of G elements; tile t of the grid-strided sequence goes to stage
+// k % RN_NS of the CTA that owns it.
+template <typename TX, bool HAS_Z>
+__device__ __forceinline__ void norm_stream_produce(const TX* __restrict__ x,
+                                                    const TX* __restrict__ z, unsigned char* sm,
+                                                    uint64_t* full, uint64_t* empty,
+                                                    int* abort_sh, int64_t total, int64_t G,
+                                                    int64_t spt, int tile_bytes, int stage) {
+  const int64_t tiles = (total + spt - 1) / spt;
+  for (int64_t k = 0;; ++k) {
+    const int64_t t = blockIdx.x + k * gridDim.x;
+    if (t >= tiles) break;
+    const int s = (int)(k % RN_NS);
+    if (k >= RN_NS && !tc::mbar_wait(&empty[s], (uint32_t)((k / RN_NS - 1) & 1), RN_WAIT)) {
+      atomicExch(&g_norm_error, 1);
+      atomicExch(abort_sh, 1);
+      break;
+    }
+    if (*(volatile int*)abort_sh) break;
+    const int64_t s0 = t * spt;
+    const int64_t n = total - s0 < spt ? total - s0 : spt;
+    const uint32_t bytes = (uint32_t)(n * G * 2);
+    unsigned char* st = sm + s * stage;
+    tc::mbar_arrive_expect_tx(&full[s], (HAS_Z ? 2 : 1) * bytes);
+    tc::bulk_load(st, x + s0 * G, bytes, &full[s]);
+    if constexpr (HAS_Z) tc::bulk_load(st + tile_bytes, z + s0 * G, bytes, &full[s]);
+  }
+}
+
+template <typename TX, typename TW, int G, int KIND, bool HAS_Z, bool HAS_B>
+__global__ void __launch_bounds__(RN_NT, 2) norm_stream_kernel(
     const TX* __restrict__ x, const TW* __restrict__ w, const TW* __restrict__ b,
     const TX* __restrict__ z, TX* __restrict__ y, float* __restrict__ mean_out,
     float* __restrict__ rstd_out, int64_t M, int64_t ngroups, float eps, bool norm_before_gate) {
@@ -299,29 +383,13 @@ __global__ void __launch_bounds__(RN_NT, 2) layer_norm_stream_kernel(
   }
   __syncthreads();
   if (warp == 0) {
-    if (lane == 0) {
-      for (int64_t k = 0;; ++k) {
-        const int64_t t = blockIdx.x + k * gridDim.x;
-        if (t >= tiles) break;
-        const int s = (int)(k % RN_NS);
-        if (k >= RN_NS && !tc::mbar_wait(&empty[s], (uint32_t)((k / RN_NS - 1) & 1), RN_WAIT)) {
-          atomicExch(&g_norm_error, 1);
-          atomicExch(&abort_sh, 1);
-          break;
-        }
-        if (*(volatile int*)&abort_sh) break;
-        const int64_t s0 = t * SEGS;
-        const int n = (int)(total - s0 < SEGS ? total - s0 : SEGS);
-        const uint32_t bytes = (uint32_t)n * G * 2;
-        unsigned char* st = sm + s * STAGE;
-        tc::mbar_arrive_expect_tx(&full[s], (HAS_Z ? 2 : 1) * bytes);
-        tc::bulk_load(st, x + s0 * G, bytes, &full[s]);
-        if constexpr (HAS_Z) tc::bulk_load(st + RN_TILE_BYTES, z + s0 * G, bytes, &full[s]);
-      }
-    }
+    if (lane == 0)
+      norm_stream_produce<TX, HAS_Z>(x, z, sm, full, empty, &abort_sh, total, G, SEGS,
+                                     RN_TILE_BYTES, STAGE);
     return;
   }
   const int cw = warp - 1, sub = lane / LPR, li = lane % LPR;
+  constexpr float INV = KIND == K_L2 ? 1.0f : 1.0f / G;
   for (int64_t k = 0;; ++k) {
     const int64_t t = blockIdx.x + k * gridDim.x;
     if (t >= tiles) break;
@@ -337,23 +405,18 @@ __global__ void __launch_bounds__(RN_NT, 2) layer_norm_stream_kernel(
       const int si = (p * 8 + cw) * SPW + sub;  // segment in tile
       const int64_t seg = s0 + si;
       const bool live = seg < total;
-      const uint4 xr = *reinterpret_cast<const uint4*>(st + si * (G * 2) + li * 16);
-      float2 xv[4] = {unpack2<TX>(xr.x), unpack2<TX>(xr.y), unpack2<TX>(xr.z), unpack2<TX>(xr.w)};
-      float2 gz[4];
+      float2 xv[4], gz[4];
+      unpack8<TX>(*reinterpret_cast<const uint4*>(st + si * (G * 2) + li * 16), xv);
       if constexpr (HAS_Z) {
-        const uint4 zr =
-            *reinterpret_cast<const uint4*>(st + RN_TILE_BYTES + si * (G * 2) + li * 16);
-        gz[0] = silu2_lowp(unpack2<TX>(zr.x));
-        gz[1] = silu2_lowp(unpack2<TX>(zr.y));
-        gz[2] = silu2_lowp(unpack2<TX>(zr.z));
-        gz[3] = silu2_lowp(unpack2<TX>(zr.w));
+        silu8<TX>(*reinterpret_cast<const uint4*>(st + RN_TILE_BYTES + si * (G * 2) + li * 16),
+                  gz);
         if (!norm_before_gate) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) xv[u] = fmul2(xv[u], gz[u]);
         }
       }
       float mu = 0.f;
-      if constexpr (!RMS) {
+      if constexpr (KIND == K_LN) {
         float sum = 0.f;
 #pragma unroll
         for (int u = 0; u < 4; ++u) sum += xv[u].x + xv[u].y;
@@ -369,29 +432,22 @@ __global__ void __launch_bounds__(RN_NT, 2) layer_norm_stream_kernel(
       float ss = ss2.x + ss2.y;
 #pragma unroll
       for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float rstd = rsqrtf(ss * (1.0f / G) + eps);
+      const float rstd = rsqrtf(ss * INV + eps);
       if (live) {
         const uint32_t row = (uint32_t)(seg / ngroups), grp = (uint32_t)(seg - (int64_t)row * ngroups);
-        if (li == 0) {
-          rstd_out[(int64_t)grp * M + row] = rstd;
-          if constexpr (!RMS) mean_out[(int64_t)grp * M + row] = mu;
+        if constexpr (KIND != K_L2) {
+          if (li == 0) {
+            rstd_out[(int64_t)grp * M + row] = rstd;
+            if constexpr (KIND == K_LN) mean_out[(int64_t)grp * M + row] = mu;
+          }
         }
-        float wv[8], bv[8];
-        load_vec<TW, 8>(w + (int64_t)grp * G + li * 8, wv);
-        if constexpr (HAS_B) load_vec<TW, 8>(b + (int64_t)grp * G + li * 8, bv);
-        uint4 out;
-        uint32_t* po = &out.x;
         const float2 r2 = make_float2(rstd, rstd);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          float2 v = fmul2(fmul2(xv[u], r2), make_float2(wv[2 * u], wv[2 * u + 1]));
-          if constexpr (HAS_B) v = fadd2(v, make_float2(bv[2 * u], bv[2 * u + 1]));
-          if constexpr (HAS_Z) {
-            if (norm_before_gate) v = fmul2(v, gz[u]);
-          }
-          po[u] = pack2<TX>(v);
-        }
-        *reinterpret_cast<uint4*>(y + seg * G + li * 8) = out;
+        for (int u = 0; u < 4; ++u) xv[u] = fmul2(xv[u], r2);
+        norm_affine<TW, KIND, HAS_Z, HAS_B>(xv, KIND == K_L2 ? w : w + (int64_t)grp * G + li * 8,
+                                            HAS_B ? b + (int64_t)grp * G + li * 8 : b, gz,
+                                            norm_before_gate);
+        *reinterpret_cast<uint4*>(y + seg * G + li * 8) = pack8<TX>(xv);
       }
     }
     __syncwarp();
@@ -399,23 +455,251 @@ __global__ void __launch_bounds__(RN_NT, 2) layer_norm_stream_kernel(
   }
 }
 
-template <typename TX, typename TW, int GG, bool RMS, bool HAS_Z, bool HAS_B>
-int launch_ln_stream(const void* x, const void* w, const void* b, const void* z, void* y,
-                     float* mean, float* rstd, int64_t M, int64_t ng, float eps, bool nbg,
-                     cudaStream_t st) {
-  constexpr int SEGS = RN_TILE_BYTES / (GG * 2);
-  constexpr int SMEM = RN_NS * (HAS_Z ? 2 : 1) * RN_TILE_BYTES + 128;
-  auto kern = layer_norm_stream_kernel<TX, TW, GG, RMS, HAS_Z, HAS_B>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
-    return set_error(XOPS_ERR_CUDA, "layer_norm_fwd: shared-memory attribute failed");
+// 8 weights (16 or 32 bytes) as fp32 pairs, from shared or global memory
+template <typename TW>
+__device__ __forceinline__ void lds_w8(const TW* p, float2 (&v)[4]) {
+  if constexpr (sizeof(TW) == 2) {
+    unpack8<TW>(*reinterpret_cast<const uint4*>(p), v);
+  } else {
+    const float4 a = reinterpret_cast<const float4*>(p)[0];
+    const float4 c = reinterpret_cast<const float4*>(p)[1];
+    v[0] = make_float2(a.x, a.y);
+    v[1] = make_float2(a.z, a.w);
+    v[2] = make_float2(c.x, c.y);
+    v[3] = make_float2(c.z, c.w);
+  }
+}
+template <typename TW>
+__device__ __forceinline__ void ldg_w8(const TW* __restrict__ p, float2 (&v)[4]) {
+  float f[8];
+  load_vec<TW, 8>(p, f);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) v[u] = make_float2(f[2 * u], f[2 * u + 1]);
+}
+
+// Wide segments: tiles of SPT = tile_bytes / (2G) whole segments; segment j
+// of the CTA's stream (counted across its tiles) belongs to consumer warp
+// j % 8, so every warp stays busy even when a tile holds fewer than 8
+// segments.  A warp makes one pass over its segment in shared memory per
+// statistic (mean for LN, the sum of squares) and one output pass; a gate
+// applied before the statistics is recomputed in each pass rather than
+// stored, which keeps the stage at 16-bit width.  The weight (and bias) rows,
+// N = ngroups * G elements, are copied once per CTA into shared memory behind
+// the ring when they fit (wsm), so the output pass never waits on L2 for them.
+template <typename TX, typename TW, int KIND, bool HAS_Z, bool HAS_B>
+__global__ void __launch_bounds__(RN_NT, 2) norm_wide_stream_kernel(
+    const TX* __restrict__ x, const TW* __restrict__ w, const TW* __restrict__ b,
+    const TX* __restrict__ z, TX* __restrict__ y, float* __restrict__ mean_out,
+    float* __restrict__ rstd_out, int M, int ngroups, int G, int spt, int tile_bytes, bool wsm,
+    float eps, bool norm_before_gate) {
+  extern __shared__ unsigned char rn_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(rn_raw) + 127) & ~static_cast<uintptr_t>(127));
+  __shared__ uint64_t full[RN_NS], empty[RN_NS];
+  __shared__ int abort_sh;
+  const int stage = (HAS_Z ? 2 : 1) * tile_bytes;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int N = ngroups * G;
+  const int total = M * ngroups;
+  const int tiles = (total + spt - 1) / spt;
+  TW* sw = reinterpret_cast<TW*>(sm + RN_NS * stage);
+  TW* sb = sw + N;
+  if (tid == 0) {
+    for (int s = 0; s < RN_NS; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 8);
+    }
+    tc::mbar_fence_init();
+    abort_sh = 0;
+  }
+  if (KIND != K_L2 && wsm) {
+    constexpr int VW = 16 / (int)sizeof(TW);
+    for (int i = tid; i < N / VW; i += blockDim.x) {
+      reinterpret_cast<uint4*>(sw)[i] = __ldg(reinterpret_cast<const uint4*>(w) + i);
+      if constexpr (HAS_B) reinterpret_cast<uint4*>(sb)[i] = __ldg(reinterpret_cast<const uint4*>(b) + i);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0)
+      norm_stream_produce<TX, HAS_Z>(x, z, sm, full, empty, &abort_sh, total, G, spt, tile_bytes,
+                                     stage);
+    return;
+  }
+  const int cw = warp - 1;
+  const int nch = G >> 3;  // 16-byte pieces per segment
+  const float inv = KIND == K_L2 ? 1.0f : 1.0f / (float)G;
+  const bool gate_before = HAS_Z && !norm_before_gate;
+  for (int k = 0;; ++k) {
+    const int t = blockIdx.x + k * gridDim.x;
+    if (t >= tiles) break;
+    const int s = k % RN_NS;
+    if (!tc::mbar_wait(&full[s], (uint32_t)((k / RN_NS) & 1), RN_WAIT)) {
+      atomicExch(&g_norm_error, 1);
+      break;
+    }
+    const unsigned char* st = sm + s * stage;
+    const int s0 = t * spt;
+    const int n = total - s0 < spt ? total - s0 : spt;
+    // first segment of this tile that warp cw owns
+    int i = (int)((cw - ((int64_t)k * spt) % 8 + 8) % 8);
+    for (; i < n; i += 8) {
+      const int seg = s0 + i;
+      const uint4* xs = reinterpret_cast<const uint4*>(st + i * G * 2);
+      const uint4* zs = reinterpret_cast<const uint4*>(st + tile_bytes + i * G * 2);
+      auto load = [&](int c, float2 (&v)[4], float2 (&g)[4]) {
+        unpack8<TX>(xs[c], v);
+        if constexpr (HAS_Z) {
+          silu8<TX>(zs[c], g);
+          if (gate_before) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = fmul2(v[u], g[u]);
+          }
+        }
+      };
+      float mu = 0.f;
+      if constexpr (KIND == K_LN) {
+        float2 a2 = make_float2(0.f, 0.f);
+#pragma unroll 4
+        for (int c = lane; c < nch; c += 32) {
+          float2 v[4], g[4];
+          load(c, v, g);
+          a2 = fadd2(a2, fadd2(fadd2(v[0], v[1]), fadd2(v[2], v[3])));
+        }
+        mu = warp_sum(a2.x + a2.y) * inv;
+      }
+      const float2 m2 = make_float2(mu, mu);
+      float2 q2 = make_float2(0.f, 0.f);
+#pragma unroll 4
+      for (int c = lane; c < nch; c += 32) {
+        float2 v[4], g[4];
+        load(c, v, g);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if constexpr (KIND == K_LN) v[u] = fsub2(v[u], m2);
+          q2 = ffma2(v[u], v[u], q2);
+        }
+      }
+      const float rstd = rsqrtf(warp_sum(q2.x + q2.y) * inv + eps);
+      const int row = seg / ngroups, grp = seg - row * ngroups;
+      if constexpr (KIND != K_L2) {
+        if (lane == 0) {
+          rstd_out[(int64_t)grp * M + row] = rstd;
+          if constexpr (KIND == K_LN) mean_out[(int64_t)grp * M + row] = mu;
+        }
+      }
+      const float2 r2 = make_float2(rstd, rstd);
+      const TW* wg = (wsm ? sw : w) + grp * G;
+      const TW* bg = (wsm ? sb : b) + (HAS_B ? grp * G : 0);
+      uint4* yo = reinterpret_cast<uint4*>(y + (int64_t)seg * G);
+#pragma unroll 2
+      for (int c = lane; c < nch; c += 32) {
+        float2 v[4], g[4], wv[4], bv[4];
+        load(c, v, g);
+        if constexpr (KIND != K_L2) {
+          if (wsm) {
+            lds_w8<TW>(wg + c * 8, wv);
+            if constexpr (HAS_B) lds_w8<TW>(bg + c * 8, bv);
+          } else {
+            ldg_w8<TW>(wg + c * 8, wv);
+            if constexpr (HAS_B) ldg_w8<TW>(bg + c * 8, bv);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if constexpr (KIND == K_LN) v[u] = fsub2(v[u], m2);
+          v[u] = fmul2(v[u], r2);
+          if constexpr (KIND == K_GEMMA) v[u] = ffma2(v[u], wv[u], v[u]);  // x (1 + w)
+          if constexpr (KIND == K_LN || KIND == K_RMS) {
+            if constexpr (HAS_B) v[u] = ffma2(v[u], wv[u], bv[u]);
+            else v[u] = fmul2(v[u], wv[u]);
+          }
+          if constexpr (HAS_Z) {
+            if (!gate_before) v[u] = fmul2(v[u], g[u]);
+          }
+        }
+        yo[c] = pack8<TX>(v);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&empty[s]);
+  }
+}
+
+int sm_count() {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+template <typename TX, typename TW, int GG, int KIND, bool HAS_Z, bool HAS_B>
+int launch_norm_stream(const void* x, const void* w, const void* b, const void* z, void* y,
+                       float* mean, float* rstd, int64_t M, int64_t ng, float eps, bool nbg,
+                       cudaStream_t st, const char* what) {
+  constexpr int SEGS = RN_TILE_BYTES / (GG * 2);
+  constexpr int SMEM = RN_NS * (HAS_Z ? 2 : 1) * RN_TILE_BYTES + 128;
+  auto kern = norm_stream_kernel<TX, TW, GG, KIND, HAS_Z, HAS_B>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
+    return set_error(XOPS_ERR_CUDA, "%s: shared-memory attribute failed", what);
   const int64_t tiles = cdiv64(M * ng, SEGS);
-  const unsigned grid = (unsigned)std::min<int64_t>(tiles, 2 * (int64_t)sms);
+  const unsigned grid = (unsigned)std::min<int64_t>(tiles, 2 * (int64_t)sm_count());
   kern<<<grid, RN_NT, SMEM, st>>>((const TX*)x, (const TW*)w, (const TW*)b, (const TX*)z, (TX*)y,
                                   mean, rstd, M, ng, eps, nbg);
-  return check_launch("layer_norm_fwd");
+  return check_launch(what);
+}
+
+// wide segments: 32 KB tiles per tensor (16 KB with a gate), three stages,
+// two CTAs per SM; up to 16 KB of weight and bias rows staged behind the ring
+constexpr int RN_WB_BYTES = 16384;
+template <typename TX, typename TW, int KIND, bool HAS_Z, bool HAS_B>
+int launch_norm_wide(const void* x, const void* w, const void* b, const void* z, void* y,
+                     float* mean, float* rstd, int64_t M, int64_t ng, int64_t G, float eps,
+                     bool nbg, cudaStream_t st, const char* what) {
+  constexpr int TB = HAS_Z ? 16384 : 32768;
+  const int64_t wb = KIND == K_L2 ? 0 : ng * G * (int64_t)sizeof(TW) * (HAS_B ? 2 : 1);
+  const bool wsm = KIND != K_L2 && wb <= RN_WB_BYTES;
+  const int smem = RN_NS * (HAS_Z ? 2 : 1) * TB + 128 + (wsm ? (int)wb : 0);
+  const int spt = (int)(TB / (G * 2));
+  auto kern = norm_wide_stream_kernel<TX, TW, KIND, HAS_Z, HAS_B>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           RN_NS * (HAS_Z ? 2 : 1) * TB + 128 + RN_WB_BYTES) != cudaSuccess)
+    return set_error(XOPS_ERR_CUDA, "%s: shared-memory attribute failed", what);
+  const int64_t tiles = cdiv64(M * ng, spt);
+  const unsigned grid = (unsigned)std::min<int64_t>(tiles, 2 * (int64_t)sm_count());
+  kern<<<grid, RN_NT, smem, st>>>((const TX*)x, (const TW*)w, (const TW*)b, (const TX*)z, (TX*)y,
+                                  mean, rstd, (int)M, (int)ng, (int)G, spt, TB, wsm, eps, nbg);
+  return check_launch(what);
+}
+
+// Streaming dispatch shared by the three operators.  Returns -1 when the
+// shape is not a streaming shape (the caller then uses the register paths).
+// Streaming needs 16-bit data, contiguous rows, 16-byte-aligned bases,
+// G % 8 == 0 and enough bytes to fill a persistent grid.
+template <typename TX, typename TW, int KIND, bool HAS_Z, bool HAS_B>
+int dispatch_stream(const void* x, const void* w, const void* b, const void* z, void* y,
+                    float* mean, float* rstd, int64_t M, int64_t N, int64_t G, float eps,
+                    bool nbg, cudaStream_t st, const char* what) {
+  if constexpr (sizeof(TX) != 2) {
+    return -1;
+  } else {
+    const int64_t ng = N / G;
+    const int64_t segs = M * ng;
+    if (segs >= (int64_t(1) << 31) || G % 8 != 0) return -1;
+    if (!aligned16(x) || !aligned16(y) || (HAS_Z && !aligned16(z))) return -1;
+    if (KIND != K_L2 && !aligned16(w)) return -1;
+    if (HAS_B && !aligned16(b)) return -1;
+    if (G <= 256) {
+      if (segs < 8192) return -1;
+      if (G == 64) return launch_norm_stream<TX, TW, 64, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st, what);
+      if (G == 128) return launch_norm_stream<TX, TW, 128, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st, what);
+      if (G == 256) return launch_norm_stream<TX, TW, 256, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st, what);
+      return -1;
+    }
+    if (G > (HAS_Z ? 8192 : 16384) || segs * G * 2 < (int64_t(4) << 20)) return -1;
+    return launch_norm_wide<TX, TW, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, G, eps,
+                                                        nbg, st, what);
+  }
 }
 
 template <typename TX, typename TW, bool RMS, bool HAS_Z, bool HAS_B>
@@ -423,15 +707,11 @@ int dispatch_ln(const void* x, const void* w, const void* b, const void* z, void
                 float* rstd, int64_t M, int64_t N, int64_t G, int64_t sx, int64_t sz, int64_t sy,
                 float eps, bool nbg, cudaStream_t st) {
   const int64_t ng = N / G;
-  // streaming path: 16-bit, contiguous rows (segments adjacent in memory),
-  // enough segments to keep a grid of persistent CTAs busy
-  if constexpr (sizeof(TX) == 2) {
-    const bool contiguous = sx == N && sy == N && (!HAS_Z || sz == N);
-    if (contiguous && M * ng >= 8192 && M * ng < (int64_t(1) << 31)) {
-      if (G == 64) return launch_ln_stream<TX, TW, 64, RMS, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st);
-      if (G == 128) return launch_ln_stream<TX, TW, 128, RMS, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st);
-      if (G == 256) return launch_ln_stream<TX, TW, 256, RMS, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st);
-    }
+  // streaming path: 16-bit, contiguous rows (segments adjacent in memory)
+  if (sx == N && sy == N && (!HAS_Z || sz == N)) {
+    const int rc = dispatch_stream<TX, TW, RMS ? K_RMS : K_LN, HAS_Z, HAS_B>(
+        x, w, b, z, y, mean, rstd, M, N, G, eps, nbg, st, "layer_norm_fwd");
+    if (rc >= 0) return rc;
   }
   // packed path: 16-byte lanes, several short segments per warp
   constexpr int VEC = 16 / (int)sizeof(TX);
@@ -637,6 +917,17 @@ int dispatch_l2(const void* x, void* y, int64_t rows, int64_t N, float eps, cuda
   return check_launch("l2norm_last_dim");
 }
 
+}  // namespace
+
+int take_norm_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_norm_error, sizeof(int)) != cudaSuccess) return -1;
+  const int zero = 0;
+  cudaMemcpyToSymbol(g_norm_error, &zero, sizeof(int));
+  return v;
+}
+
+namespace {
 bool valid_dtype(int d) { return d == XOPS_F32 || d == XOPS_BF16 || d == XOPS_F16; }
 
 }  // namespace
@@ -719,6 +1010,10 @@ extern "C" int xops_gemma_rms_norm(const void* x, const void* gamma, void* y, fl
   auto run = [&](auto tx, auto tw) {
     using TX = decltype(tx);
     using TW = decltype(tw);
+    const int rc = dispatch_stream<TX, TW, K_GEMMA, false, false>(
+        x, gamma, nullptr, nullptr, y, nullptr, rstd, rows, cols, cols, eps, true, st,
+        "gemma_rms_norm");
+    if (rc >= 0) return rc;
     if (n < 0) {
       gemma_block_kernel<TX, TW><<<(unsigned)rows, 512, 0, st>>>((const TX*)x, (const TW*)gamma,
                                                                  (TX*)y, rstd, cols, eps);
@@ -757,6 +1052,10 @@ extern "C" int xops_l2norm_last_dim(const void* x, void* y, int64_t rows, int64_
     }
     return dispatch_l2<float>(x, y, rows, cols, eps, st);
   }
+  const int rc = dispatch_stream<__nv_bfloat16, __nv_bfloat16, K_L2, false, false>(
+      x, nullptr, nullptr, nullptr, y, nullptr, nullptr, rows, cols, cols, eps, true, st,
+      "l2norm_last_dim");
+  if (rc >= 0) return rc;
   if (!aligned || n == 1) {
     l2norm_generic_kernel<__nv_bfloat16><<<(unsigned)cdiv64(rows, 8), 256, 0, st>>>(
         (const __nv_bfloat16*)x, (__nv_bfloat16*)y, rows, cols, eps);
