@@ -238,8 +238,9 @@ XOPS_API int xops_chunk_fwd_o(const void* q, const void* k, const void* v_new, c
                      int64_t NT, float scale, void* stream);
 
 /* Number of device-side wait timeouts recorded by the tensor-core and the
- * bulk-copy streaming kernels (chunked GDN, conv1d, the norms) since the last call (0 when healthy); synchronises the device and resets
- * the counter.  A kernel that times out on an internal barrier writes no
+ * bulk-copy streaming kernels (chunked GDN, conv1d, the norms, RoPE) since
+ * the last call (0 when healthy); synchronises the device and resets the
+ * counter.  A kernel that times out on an internal barrier writes no
  * further output and returns instead of hanging. */
 XOPS_API int xops_device_error_count(void);
 

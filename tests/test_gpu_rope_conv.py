@@ -38,18 +38,29 @@ def test_rope_config1():
     assert torch.equal(v.cpu(), rv)
 
 
-@pytest.mark.parametrize("T,qh,kvh,hd,rd,dt", [(333, 8, 1, 128, 128, torch.bfloat16),
-                                               (17, 4, 4, 64, 32, torch.float32),
-                                               (64, 16, 2, 256, 64, torch.bfloat16)])
-def test_rope_shapes(T, qh, kvh, hd, rd, dt):
+@pytest.mark.parametrize("T,qh,kvh,hd,rd,dt,bias", [
+    (333, 8, 1, 128, 128, torch.bfloat16, False),
+    (17, 4, 4, 64, 32, torch.float32, False),
+    (64, 16, 2, 256, 64, torch.bfloat16, False),
+    # >= 4 MB of input: the bulk-copy streaming path
+    (1024, 16, 2, 256, 64, torch.float32, False),    # cfg1 heads at 1024 tokens
+    (2000, 8, 1, 128, 128, torch.float32, True),     # full rotary, bias
+    (1500, 16, 2, 256, 64, torch.bfloat16, True),
+    (700, 4, 2, 512, 200, torch.float32, False),     # rotary half not a lane multiple
+    (800, 4, 2, 256, 42, torch.float32, True),       # cos/sin rows not 16-byte multiples
+])
+def test_rope_shapes(T, qh, kvh, hd, rd, dt, bias):
     g = torch.Generator().manual_seed(T)
     inp = torch.randn(T, (qh + 2 * kvh) * hd, generator=g).to(dt)
     qw = (1 + 0.1 * torch.randn(hd, generator=g)).to(dt)
     kw = (1 + 0.1 * torch.randn(hd, generator=g)).to(dt)
+    qb = (0.1 * torch.randn(hd, generator=g)).to(dt) if bias else None
+    kb = (0.1 * torch.randn(hd, generator=g)).to(dt) if bias else None
     sin, cos = workloads.neox_sin_cos(torch.arange(T) * 7, rd, 1e6)
     q, k, v = ops.npu_split_rmsnorm_rope(_to(inp), _to(sin), _to(cos), _to(qw), _to(kw), qh * hd,
-                                         kvh * hd, hd, 1e-6)
-    rq, rk, rv = oracle.split_rmsnorm_rope(inp, sin, cos, qw, kw, qh * hd, kvh * hd, hd, 1e-6)
+                                         kvh * hd, hd, 1e-6, _to(qb), _to(kb), bias)
+    rq, rk, rv = oracle.split_rmsnorm_rope(inp, sin, cos, qw, kw, qh * hd, kvh * hd, hd, 1e-6,
+                                           qb, kb, bias)
     check = assert_fp32 if dt == torch.float32 else assert_bf16
     check(q, rq)
     check(k, rk)

@@ -1162,8 +1162,9 @@ extern "C" int xops_device_error_count(void) {
   const int zero = 0;
   cudaMemcpyToSymbol(gdn::g_tc_error, &zero, sizeof(int));
   const int vn = xops::take_norm_error(), vc = xops::take_conv_error();
-  if (vn < 0 || vc < 0) return -1;
-  return v + vn + vc;
+  const int vr = xops::take_rope_error();
+  if (vn < 0 || vc < 0 || vr < 0) return -1;
+  return v + vn + vc + vr;
 }
 
 // ---------------------------------------------------------------------------

@@ -17,6 +17,7 @@ int check_launch(const char* what);
 // (then cleared), -1 when the flag cannot be read
 int take_norm_error();
 int take_conv_error();
+int take_rope_error();
 
 #define XOPS_REQUIRE(cond, ...)                                              \
   do {                                                                       \
@@ -184,5 +185,17 @@ __device__ __forceinline__ uint32_t pack2<__half>(float2 v) {
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Opt a persistent streaming kernel into `bytes` of dynamic shared memory and
+// the largest shared-memory carveout: without the carveout the driver may
+// pick a smaller split that leaves room for only one of the CTAs an SM is
+// meant to hold.
+template <typename K>
+inline bool set_stream_smem(K kern, int bytes) {
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
+             cudaSuccess &&
+         cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                              (int)cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+}
 
 }  // namespace xops

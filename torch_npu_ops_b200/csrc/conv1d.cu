@@ -535,8 +535,7 @@ int launch_varlen_tma(int W, const void* x, void* state, const void* w, const vo
 #define XOPS_CT(WW)                                                                            \
   case WW: {                                                                                   \
     auto kern = conv1d_varlen_tma_kernel<T, WW>;                                               \
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, RB_SMEM) !=     \
-        cudaSuccess)                                                                           \
+    if (!set_stream_smem(kern, RB_SMEM))                                                        \
       return set_error(XOPS_ERR_CUDA, "causal_conv1d_varlen: shared-memory attribute failed"); \
     kern<<<grid, RB_NT, RB_SMEM, st>>>(m, (const T*)x, (T*)state, (const T*)w, (const T*)b,    \
                                        qsl, slots, (T*)out, nseq, dim, tiles_per_slab,          \

@@ -640,6 +640,8 @@ int launch_norm_stream(const void* x, const void* w, const void* b, const void* 
   constexpr int SEGS = RN_TILE_BYTES / (GG * 2);
   constexpr int SMEM = RN_NS * (HAS_Z ? 2 : 1) * RN_TILE_BYTES + 128;
   auto kern = norm_stream_kernel<TX, TW, GG, KIND, HAS_Z, HAS_B>;
+  // two 96 KB CTAs fit the default carveout, which leaves L1 room for the
+  // weight rows this kernel reads through it
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
     return set_error(XOPS_ERR_CUDA, "%s: shared-memory attribute failed", what);
   const int64_t tiles = cdiv64(M * ng, SEGS);
@@ -662,8 +664,7 @@ int launch_norm_wide(const void* x, const void* w, const void* b, const void* z,
   const int smem = RN_NS * (HAS_Z ? 2 : 1) * TB + 128 + (wsm ? (int)wb : 0);
   const int spt = (int)(TB / (G * 2));
   auto kern = norm_wide_stream_kernel<TX, TW, KIND, HAS_Z, HAS_B>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           RN_NS * (HAS_Z ? 2 : 1) * TB + 128 + RN_WB_BYTES) != cudaSuccess)
+  if (!set_stream_smem(kern, RN_NS * (HAS_Z ? 2 : 1) * TB + 128 + RN_WB_BYTES))
     return set_error(XOPS_ERR_CUDA, "%s: shared-memory attribute failed", what);
   const int64_t tiles = cdiv64(M * ng, spt);
   const unsigned grid = (unsigned)std::min<int64_t>(tiles, 2 * (int64_t)sm_count());

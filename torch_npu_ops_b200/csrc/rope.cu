@@ -13,6 +13,7 @@
 // shuffle reduction and the rotate-half partner comes from a per-warp
 // shared-memory row, so any even rotary_dim works.
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace xops {
 namespace {
@@ -76,12 +77,302 @@ __global__ void __launch_bounds__(256) split_rmsnorm_rope_kernel(
   store_vec<T, EPL>(dst + lane * EPL, v);
 }
 
+// ----------------------------------------------------------------------------
+// Streaming path for large token counts.  The packed input [T, heads * HD] is
+// a flat list of T * heads head segments of HD elements; a persistent CTA
+// streams tiles of whole segments (32 KB) into a ring of RP_NS shared stages
+// with 1-D bulk copies (warp 0), together with the cos / sin rows of the
+// tokens the tile touches (when those rows are 16-byte multiples), and 8
+// consumer warps take two segments at a time: v heads are copied out, q / k
+// heads are normalised and rotated.  The rotate-half partner of a slice is
+// the slice of lane +- (rotary_dim / 2) / EPL (a shuffle) when rotary_dim / 2
+// is a multiple of the lane width, else it is recomputed from the raw input
+// of element d +- rotary_dim / 2 in the stage (same r, weight and bias).
+// Weight and bias rows live in shared memory for the whole kernel.
+// ----------------------------------------------------------------------------
+constexpr int RP_NS = 3, RP_TILE = 32768, RP_NT = 32 + 256;
+constexpr uint32_t RP_WAIT = 1u << 26;
+__device__ int g_rope_error = 0;
+
+struct RopeStage {
+  int stage;    // bytes per ring stage: x tile, then cos rows, then sin rows
+  int cs;       // bytes reserved for each table's rows in a stage (0: read global)
+  int maxtok;   // tokens one tile can touch
+};
+
+template <typename T, typename TW, typename TS, int HD>
+__global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
+    const T* __restrict__ in, const TS* __restrict__ sin_t, const TS* __restrict__ cos_t,
+    T* __restrict__ qo, T* __restrict__ ko, T* __restrict__ vo, const TW* __restrict__ qw,
+    const TW* __restrict__ qb, const TW* __restrict__ kw, const TW* __restrict__ kb,
+    int64_t T_, int qh, int kvh, int rd, RopeStage L, float eps) {
+  constexpr int EPL = HD / 32;                // elements per lane
+  constexpr int SEG = HD * (int)sizeof(T);    // bytes per head segment
+  constexpr int SPT = RP_TILE / SEG;          // segments per tile
+  static_assert(SPT % 8 == 0, "a tile must give every consumer warp the same count");
+  static_assert(EPL % 4 == 0 && EPL * sizeof(T) % 16 == 0, "lane slice must be whole vectors");
+  extern __shared__ unsigned char rp_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(rp_raw) + 127) & ~static_cast<uintptr_t>(127));
+  float* swt = reinterpret_cast<float*>(sm + RP_NS * L.stage);  // qw | qb | kw | kb as fp32
+  __shared__ uint64_t full[RP_NS], empty[RP_NS];
+  __shared__ int abort_sh;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int heads = qh + 2 * kvh;
+  const int64_t total = T_ * heads;
+  const int64_t tiles = (total + SPT - 1) / SPT;
+  const bool has_b = qb != nullptr;
+  const bool staged = L.cs > 0;
+  if (tid == 0) {
+    for (int s = 0; s < RP_NS; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 8);
+    }
+    tc::mbar_fence_init();
+    abort_sh = 0;
+  }
+  for (int i = tid; i < HD; i += blockDim.x) {
+    swt[i] = to_f32<TW>(qw[i]);
+    swt[2 * HD + i] = to_f32<TW>(kw[i]);
+    swt[HD + i] = has_b ? to_f32<TW>(qb[i]) : 0.f;
+    swt[3 * HD + i] = has_b ? to_f32<TW>(kb[i]) : 0.f;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int64_t k = 0;; ++k) {
+        const int64_t t = blockIdx.x + k * gridDim.x;
+        if (t >= tiles) break;
+        const int s = (int)(k % RP_NS);
+        if (k >= RP_NS && !tc::mbar_wait(&empty[s], (uint32_t)((k / RP_NS - 1) & 1), RP_WAIT)) {
+          atomicExch(&g_rope_error, 1);
+          atomicExch(&abort_sh, 1);
+          break;
+        }
+        if (*(volatile int*)&abort_sh) break;
+        const int64_t s0 = t * SPT;
+        const int64_t n = total - s0 < SPT ? total - s0 : SPT;
+        unsigned char* st = sm + s * L.stage;
+        uint32_t cb = 0;
+        int64_t tf = 0;
+        if (staged) {
+          tf = s0 / heads;
+          cb = (uint32_t)(((s0 + n - 1) / heads - tf + 1) * rd * (int64_t)sizeof(TS));
+        }
+        tc::mbar_arrive_expect_tx(&full[s], (uint32_t)(n * SEG) + 2 * cb);
+        tc::bulk_load(st, in + s0 * HD, (uint32_t)(n * SEG), &full[s]);
+        if (staged) {
+          tc::bulk_load(st + RP_TILE, cos_t + tf * rd, cb, &full[s]);
+          tc::bulk_load(st + RP_TILE + L.cs, sin_t + tf * rd, cb, &full[s]);
+        }
+      }
+    }
+    return;
+  }
+  const int cw = warp - 1;
+  const int half = rd >> 1;
+  const int d0 = lane * EPL;
+  // vec: half is a multiple of EPL, so this lane's slice lies wholly in
+  // [0, half), [half, rd) or [rd, HD) and its partner slice is the one of
+  // lane +- half / EPL
+  const bool vec = half % EPL == 0;
+  const int src = !vec ? lane : d0 < half ? lane + half / EPL : d0 < rd ? lane - half / EPL : lane;
+  const bool rot = d0 < rd;
+  constexpr int NSEG = EPL <= 8 ? 2 : 1;  // segments in flight per warp
+  constexpr int P = EPL / 2;              // element pairs per lane
+  for (int64_t k = 0;; ++k) {
+    const int64_t t = blockIdx.x + k * gridDim.x;
+    if (t >= tiles) break;
+    const int s = (int)(k % RP_NS);
+    if (!tc::mbar_wait(&full[s], (uint32_t)((k / RP_NS) & 1), RP_WAIT)) {
+      atomicExch(&g_rope_error, 1);
+      break;
+    }
+    const unsigned char* stb = sm + s * L.stage;
+    const T* st = reinterpret_cast<const T*>(stb);
+    const TS* scos = reinterpret_cast<const TS*>(stb + RP_TILE);
+    const TS* ssin = reinterpret_cast<const TS*>(stb + RP_TILE + L.cs);
+    const int64_t s0 = t * SPT;
+    const int64_t tf = s0 / heads;          // first token of the tile
+    const int h0 = (int)(s0 - tf * heads);  // its head
+#pragma unroll 1
+    for (int i0 = cw; i0 < SPT; i0 += 8 * NSEG) {
+      // element pairs (2j, 2j + 1) of the lane's slice as packed fp32 pairs
+      float2 x[NSEG][P];
+      float ss[NSEG];
+      int dt[NSEG], hh[NSEG];  // token offset from tf, head
+      bool live[NSEG];
+#pragma unroll
+      for (int u = 0; u < NSEG; ++u) {
+        const int i = i0 + 8 * u;
+        live[u] = i < SPT && s0 + i < total;
+        const int a = h0 + (live[u] ? i : 0);
+        dt[u] = a / heads;
+        hh[u] = live[u] ? a - dt[u] * heads : heads - 1;
+        const T* xs = st + (live[u] ? i : 0) * HD;
+#pragma unroll
+        for (int c = 0; c < EPL * (int)sizeof(T) / 16; ++c) {
+          const uint4 r = reinterpret_cast<const uint4*>(xs + d0)[c];
+          if constexpr (sizeof(T) == 4) {
+            x[u][2 * c] = make_float2(__uint_as_float(r.x), __uint_as_float(r.y));
+            x[u][2 * c + 1] = make_float2(__uint_as_float(r.z), __uint_as_float(r.w));
+          } else {
+            x[u][4 * c] = unpack2<T>(r.x);
+            x[u][4 * c + 1] = unpack2<T>(r.y);
+            x[u][4 * c + 2] = unpack2<T>(r.z);
+            x[u][4 * c + 3] = unpack2<T>(r.w);
+          }
+        }
+      }
+      // the rotate-half sign, folded into sin
+      const float sg = d0 < half ? -1.f : 1.f;
+#pragma unroll
+      for (int u = 0; u < NSEG; ++u) {
+        float2 q2 = fmul2(x[u][0], x[u][0]);
+#pragma unroll
+        for (int j = 1; j < P; ++j) q2 = ffma2(x[u][j], x[u][j], q2);
+        ss[u] = q2.x + q2.y;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int u = 0; u < NSEG; ++u) ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], o);
+      }
+#pragma unroll
+      for (int u = 0; u < NSEG; ++u) {
+        const bool is_v = hh[u] >= qh + kvh;
+        const bool is_q = hh[u] < qh;
+        const bool apply = rot && !is_v;
+        float2 v[P];
+        const float r = rsqrtf(ss[u] * (1.0f / HD) + eps);
+        const float2 r2 = make_float2(r, r);
+        const float* wrow = swt + (is_q ? 0 : 2 * HD);
+        const float* brow = wrow + HD;
+#pragma unroll
+        for (int j = 0; j < P; j += 2) {
+          const float4 w4 = *reinterpret_cast<const float4*>(wrow + d0 + 2 * j);
+          const float4 b4 = *reinterpret_cast<const float4*>(brow + d0 + 2 * j);
+          v[j] = ffma2(fmul2(x[u][j], r2), make_float2(w4.x, w4.y), make_float2(b4.x, b4.y));
+          v[j + 1] = ffma2(fmul2(x[u][j + 1], r2), make_float2(w4.z, w4.w), make_float2(b4.z, b4.w));
+        }
+        // cos / sin of element d of this segment's token
+        const int64_t tok_u = tf + dt[u];
+        auto cos_at = [&](int d) {
+          return staged ? to_f32<TS>(scos[dt[u] * rd + d]) : to_f32<TS>(cos_t[tok_u * rd + d]);
+        };
+        auto sin_at = [&](int d) {
+          return staged ? to_f32<TS>(ssin[dt[u] * rd + d]) : to_f32<TS>(sin_t[tok_u * rd + d]);
+        };
+        if (vec) {
+          // every lane shuffles (uniform); only rotated, live q / k slices use
+          // it.  Pair j of every lane is read by the shuffles before any lane
+          // updates its own pair j.
+          const bool cs_vec = staged && sizeof(TS) == 4;
+#pragma unroll
+          for (int j = 0; j < P; ++j) {
+            const float2 pv = make_float2(__shfl_sync(0xffffffffu, v[j].x, src),
+                                          __shfl_sync(0xffffffffu, v[j].y, src));
+            if (apply) {
+              float2 c2, s2;
+              if (cs_vec) {
+                c2 = *reinterpret_cast<const float2*>(scos + dt[u] * rd + d0 + 2 * j);
+                s2 = *reinterpret_cast<const float2*>(ssin + dt[u] * rd + d0 + 2 * j);
+              } else {
+                c2 = make_float2(cos_at(d0 + 2 * j), cos_at(d0 + 2 * j + 1));
+                s2 = make_float2(sin_at(d0 + 2 * j), sin_at(d0 + 2 * j + 1));
+              }
+              v[j] = ffma2(v[j], c2, fmul2(pv, fmul2(s2, make_float2(sg, sg))));
+            }
+          }
+        } else if (apply) {
+          // partner from the raw input in the stage, normalised the same way
+          const T* xs = st + (i0 + 8 * u) * HD;
+#pragma unroll
+          for (int j = 0; j < EPL; ++j) {
+            const int d = d0 + j;
+            if (d < rd) {
+              const int p = d < half ? d + half : d - half;
+              const float pvv = to_f32<T>(xs[p]) * r * wrow[p] + brow[p];
+              float& e = (j & 1) ? v[j >> 1].y : v[j >> 1].x;
+              e = e * cos_at(d) + (d < half ? -pvv : pvv) * sin_at(d);
+            }
+          }
+        }
+        if (!live[u]) continue;
+        const int64_t tok = tok_u;
+        T* dst = is_v ? vo + tok * (int64_t)kvh * HD + (int64_t)(hh[u] - qh - kvh) * HD
+                 : is_q ? qo + tok * (int64_t)qh * HD + (int64_t)hh[u] * HD
+                        : ko + tok * (int64_t)kvh * HD + (int64_t)(hh[u] - qh) * HD;
+        const float2* o = is_v ? x[u] : v;
+#pragma unroll
+        for (int c = 0; c < EPL * (int)sizeof(T) / 16; ++c) {
+          uint4 w;
+          if constexpr (sizeof(T) == 4) {
+            w = make_uint4(__float_as_uint(o[2 * c].x), __float_as_uint(o[2 * c].y),
+                           __float_as_uint(o[2 * c + 1].x), __float_as_uint(o[2 * c + 1].y));
+          } else {
+            w = make_uint4(pack2<T>(o[4 * c]), pack2<T>(o[4 * c + 1]), pack2<T>(o[4 * c + 2]),
+                           pack2<T>(o[4 * c + 3]));
+          }
+          reinterpret_cast<uint4*>(dst + d0)[c] = w;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&empty[s]);
+  }
+}
+
+template <typename T, typename TW, typename TS, int HD>
+int launch_rope_stream(const void* in, const void* s, const void* c, void* q, void* k, void* v,
+                       const void* qw, const void* qb, const void* kw, const void* kb,
+                       int64_t T_, int qh, int kvh, int rd, float eps, cudaStream_t st) {
+  constexpr int SPT = RP_TILE / (HD * (int)sizeof(T));
+  constexpr int WB = 4 * HD * 4;
+  const int heads = qh + 2 * kvh;
+  RopeStage L;
+  L.maxtok = (SPT - 1) / heads + 2;
+  // cos / sin rows ride in the stage when every tile's first row starts on a
+  // 16-byte boundary and three stages still fit in shared memory
+  const int64_t row = (int64_t)rd * sizeof(TS);
+  L.cs = (row % 16 == 0 && aligned16(s) && aligned16(c)) ? (int)((L.maxtok * row + 127) / 128 * 128) : 0;
+  L.stage = RP_TILE + 2 * L.cs;
+  if (RP_NS * L.stage + WB + 128 > 227 * 1024) {
+    L.cs = 0;
+    L.stage = RP_TILE;
+  }
+  const int smem = RP_NS * L.stage + WB + 128;
+  auto kern = split_rmsnorm_rope_stream_kernel<T, TW, TS, HD>;
+  if (!set_stream_smem(kern, smem))
+    return set_error(XOPS_ERR_CUDA, "split_rmsnorm_rope: shared-memory attribute failed");
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t tiles = cdiv64(T_ * heads, SPT);
+  const unsigned grid = (unsigned)(tiles < 2 * (int64_t)sms ? tiles : 2 * (int64_t)sms);
+  kern<<<grid, RP_NT, smem, st>>>((const T*)in, (const TS*)s, (const TS*)c, (T*)q, (T*)k, (T*)v,
+                                  (const TW*)qw, (const TW*)qb, (const TW*)kw, (const TW*)kb, T_,
+                                  qh, kvh, rd, L, eps);
+  return check_launch("split_rmsnorm_rope");
+}
+
 template <typename T, typename TW, typename TS>
 int dispatch_rope(const void* in, const void* s, const void* c, void* q, void* k, void* v,
                   const void* qw, const void* qb, const void* kw, const void* kb, int64_t T_,
                   int qh, int kvh, int hd, int rd, float eps, cudaStream_t st) {
   const int64_t items = T_ * (qh + 2 * kvh);
   const unsigned blocks = (unsigned)cdiv64(items, 8);
+  // streaming path once the input is a few MB: enough tiles for a persistent grid
+  if (items * hd * (int64_t)sizeof(T) >= (int64_t(4) << 20)) {
+    if constexpr (sizeof(T) == 4) {  // a 128-wide bf16 head is 8 bytes per lane
+      if (hd == 128)
+        return launch_rope_stream<T, TW, TS, 128>(in, s, c, q, k, v, qw, qb, kw, kb, T_, qh, kvh, rd, eps, st);
+    }
+    if (hd == 256)
+      return launch_rope_stream<T, TW, TS, 256>(in, s, c, q, k, v, qw, qb, kw, kb, T_, qh, kvh, rd, eps, st);
+    if (hd == 512)
+      return launch_rope_stream<T, TW, TS, 512>(in, s, c, q, k, v, qw, qb, kw, kb, T_, qh, kvh, rd, eps, st);
+  }
   switch (hd) {
 #define XOPS_R_CASE(EPL)                                                                      \
   case 32 * EPL:                                                                              \
@@ -101,6 +392,14 @@ int dispatch_rope(const void* in, const void* s, const void* c, void* q, void* k
 }
 
 }  // namespace
+
+int take_rope_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_rope_error, sizeof(int)) != cudaSuccess) return -1;
+  const int zero = 0;
+  cudaMemcpyToSymbol(g_rope_error, &zero, sizeof(int));
+  return v;
+}
 }  // namespace xops
 
 using namespace xops;
