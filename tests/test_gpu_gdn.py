@@ -160,6 +160,32 @@ def test_chunk_strided_qkv_views():
     assert torch.equal(o1, o2) and torch.equal(h1, h2)
 
 
+def test_chunk_strided_l2_streaming():
+    """In-kernel q/k L2 norm on >= 8192 (token, head) rows goes through the
+    bulk-copy streaming pre-pass; strided q/k views (one copy per token row)
+    and contiguous inputs (one copy per tile) agree bit for bit and match the
+    oracle."""
+    inp = workloads.chunk_config3(hk=2, hv=4, lengths=[3000, 1200], seed=5)
+    T = 4200
+    g = torch.Generator().manual_seed(10)
+    inp["q"] = torch.randn(inp["q"].shape, generator=g).to(torch.bfloat16)
+    inp["k"] = torch.randn(inp["k"].shape, generator=g).to(torch.bfloat16)
+    packed = torch.cat([inp["q"].reshape(T, -1), inp["k"].reshape(T, -1), inp["v"].reshape(T, -1)],
+                       dim=1).to(DEV)
+    qv = packed[:, :256].view(1, T, 2, 128)
+    kv = packed[:, 256:512].view(1, T, 2, 128)
+    vv = packed[:, 512:].view(1, T, 4, 128)
+    args = (_to(inp["g"]), _to(inp["beta"]), None, _to(inp["initial_state"]), True,
+            _to(inp["cu_seqlens"]), False, True)
+    o1, h1 = ops.npu_chunk_gated_delta_rule(qv, kv, vv, *args)
+    o2, h2 = ops.npu_chunk_gated_delta_rule(_to(inp["q"]), _to(inp["k"]), _to(inp["v"]), *args)
+    assert torch.equal(o1, o2) and torch.equal(h1, h2)
+    ro, rh = oracle.chunk_gated_delta_rule(inp["q"], inp["k"], inp["v"], inp["g"], inp["beta"],
+                                           None, inp["initial_state"], True, inp["cu_seqlens"], True)
+    assert_bf16(o1, ro)
+    assert_state(h1, rh)
+
+
 def test_chunk_subops_pipeline():
     """cumsum -> kkt -> solve_tril -> w/u -> fwd_h -> fwd_o on the GPU, each
     stage against the oracle's same stage, and the composition against the

@@ -1100,10 +1100,20 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
     gdn::bf16* qn = reinterpret_cast<gdn::bf16*>(ws + nchunks * H * (int64_t)gdn::WS_CHUNK);
     gdn::bf16* kn = qn + B * T * Hg * K;
     const int64_t rows = B * T * Hg;
-    gdn::l2norm_heads_kernel<<<(unsigned)cdiv64(rows, 8), 256, 0, st>>>(qq, qn, rows, Hg, qs);
-    if (int rc = check_launch("chunk_gated_delta_rule(l2norm q)")) return rc;
-    gdn::l2norm_heads_kernel<<<(unsigned)cdiv64(rows, 8), 256, 0, st>>>(kk, kn, rows, Hg, ks);
-    if (int rc = check_launch("chunk_gated_delta_rule(l2norm k)")) return rc;
+    // bulk-copy streaming path when the shape suits it, else a warp per row
+    for (int which = 0; which < 2; ++which) {
+      const gdn::bf16* src = which ? kk : qq;
+      gdn::bf16* dst = which ? kn : qn;
+      const int64_t stride = which ? ks : qs;
+      int rc = xops::l2norm_rows_stream(src, dst, B * T, Hg, stride, 1e-6f, st);
+      if (rc < 0) {
+        gdn::l2norm_heads_kernel<<<(unsigned)cdiv64(rows, 8), 256, 0, st>>>(src, dst, rows, Hg,
+                                                                            stride);
+        rc = check_launch(which ? "chunk_gated_delta_rule(l2norm k)"
+                                : "chunk_gated_delta_rule(l2norm q)");
+      }
+      if (rc) return rc;
+    }
     qq = qn;
     kk = kn;
     qs = ks = Hg * K;

@@ -18,6 +18,11 @@ int check_launch(const char* what);
 int take_norm_error();
 int take_conv_error();
 int take_rope_error();
+// L2-normalise `rows` rows of `heads` bf16 128-element segments (row stride
+// x_stride elements) into contiguous y with the bulk-copy streaming kernel;
+// -1 when the shape does not suit it (the caller then uses its own kernel)
+int l2norm_rows_stream(const void* x, void* y, int64_t rows, int64_t heads, int64_t x_stride,
+                       float eps, cudaStream_t st);
 
 #define XOPS_REQUIRE(cond, ...)                                              \
   do {                                                                       \

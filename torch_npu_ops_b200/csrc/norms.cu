@@ -328,13 +328,17 @@ __device__ __forceinline__ void silu8(const uint4 r, float2 (&g)[4]) {
 
 // Producer / ring bookkeeping shared by both widths.  Tiles hold SPT whole
 // segments of G elements; tile t of the grid-strided sequence goes to stage
-// k % RN_NS of the CTA that owns it.
+// k % RN_NS of the CTA that owns it.  x rows (ngroups segments each) are
+// contiguous when sx == ngroups * G, which makes a tile one copy; otherwise
+// each tile holds whole rows and takes one copy per row.
 template <typename TX, bool HAS_Z>
 __device__ __forceinline__ void norm_stream_produce(const TX* __restrict__ x,
                                                     const TX* __restrict__ z, unsigned char* sm,
                                                     uint64_t* full, uint64_t* empty,
                                                     int* abort_sh, int64_t total, int64_t G,
-                                                    int64_t spt, int tile_bytes, int stage) {
+                                                    int64_t spt, int tile_bytes, int stage,
+                                                    int64_t ngroups = 1, int64_t sx = -1) {
+  const bool strided = sx >= 0 && sx != ngroups * G;
   const int64_t tiles = (total + spt - 1) / spt;
   for (int64_t k = 0;; ++k) {
     const int64_t t = blockIdx.x + k * gridDim.x;
@@ -351,7 +355,13 @@ __device__ __forceinline__ void norm_stream_produce(const TX* __restrict__ x,
     const uint32_t bytes = (uint32_t)(n * G * 2);
     unsigned char* st = sm + s * stage;
     tc::mbar_arrive_expect_tx(&full[s], (HAS_Z ? 2 : 1) * bytes);
-    tc::bulk_load(st, x + s0 * G, bytes, &full[s]);
+    if (strided) {
+      const uint32_t rb = (uint32_t)(ngroups * G * 2);
+      for (int64_t r = 0; r < n / ngroups; ++r)
+        tc::bulk_load(st + r * rb, x + (s0 / ngroups + r) * sx, rb, &full[s]);
+    } else {
+      tc::bulk_load(st, x + s0 * G, bytes, &full[s]);
+    }
     if constexpr (HAS_Z) tc::bulk_load(st + tile_bytes, z + s0 * G, bytes, &full[s]);
   }
 }
@@ -360,7 +370,8 @@ template <typename TX, typename TW, int G, int KIND, bool HAS_Z, bool HAS_B>
 __global__ void __launch_bounds__(RN_NT, 2) norm_stream_kernel(
     const TX* __restrict__ x, const TW* __restrict__ w, const TW* __restrict__ b,
     const TX* __restrict__ z, TX* __restrict__ y, float* __restrict__ mean_out,
-    float* __restrict__ rstd_out, int64_t M, int64_t ngroups, float eps, bool norm_before_gate) {
+    float* __restrict__ rstd_out, int64_t M, int64_t ngroups, int64_t sx, float eps,
+    bool norm_before_gate) {
   constexpr int SEGS = RN_TILE_BYTES / (G * 2);   // segments per tile
   constexpr int LPR = G / 8;                       // lanes per segment
   constexpr int SPW = 32 / LPR;                    // segments per warp pass
@@ -385,7 +396,7 @@ __global__ void __launch_bounds__(RN_NT, 2) norm_stream_kernel(
   if (warp == 0) {
     if (lane == 0)
       norm_stream_produce<TX, HAS_Z>(x, z, sm, full, empty, &abort_sh, total, G, SEGS,
-                                     RN_TILE_BYTES, STAGE);
+                                     RN_TILE_BYTES, STAGE, ngroups, sx);
     return;
   }
   const int cw = warp - 1, sub = lane / LPR, li = lane % LPR;
@@ -636,7 +647,7 @@ int sm_count() {
 template <typename TX, typename TW, int GG, int KIND, bool HAS_Z, bool HAS_B>
 int launch_norm_stream(const void* x, const void* w, const void* b, const void* z, void* y,
                        float* mean, float* rstd, int64_t M, int64_t ng, float eps, bool nbg,
-                       cudaStream_t st, const char* what) {
+                       cudaStream_t st, const char* what, int64_t sx = -1) {
   constexpr int SEGS = RN_TILE_BYTES / (GG * 2);
   constexpr int SMEM = RN_NS * (HAS_Z ? 2 : 1) * RN_TILE_BYTES + 128;
   auto kern = norm_stream_kernel<TX, TW, GG, KIND, HAS_Z, HAS_B>;
@@ -647,7 +658,7 @@ int launch_norm_stream(const void* x, const void* w, const void* b, const void* 
   const int64_t tiles = cdiv64(M * ng, SEGS);
   const unsigned grid = (unsigned)std::min<int64_t>(tiles, 2 * (int64_t)sm_count());
   kern<<<grid, RN_NT, SMEM, st>>>((const TX*)x, (const TW*)w, (const TW*)b, (const TX*)z, (TX*)y,
-                                  mean, rstd, M, ng, eps, nbg);
+                                  mean, rstd, M, ng, sx, eps, nbg);
   return check_launch(what);
 }
 
@@ -919,6 +930,19 @@ int dispatch_l2(const void* x, void* y, int64_t rows, int64_t N, float eps, cuda
 }
 
 }  // namespace
+
+int l2norm_rows_stream(const void* x, void* y, int64_t rows, int64_t heads, int64_t x_stride,
+                       float eps, cudaStream_t st) {
+  // rows of `heads` 128-element bf16 segments; a 16 KB tile holds 64
+  // segments, which must be whole rows for the per-row copies
+  constexpr int SEGS = RN_TILE_BYTES / (128 * 2);
+  if (rows * heads < 8192 || rows * heads >= (int64_t(1) << 31) || SEGS % heads != 0) return -1;
+  if (!aligned16(x) || !aligned16(y) || (x_stride * 2) % 16 != 0 || x_stride < heads * 128)
+    return -1;
+  return launch_norm_stream<__nv_bfloat16, __nv_bfloat16, 128, K_L2, false, false>(
+      x, nullptr, nullptr, nullptr, y, nullptr, nullptr, rows, heads, eps, true, st,
+      "l2norm(q/k)", x_stride);
+}
 
 int take_norm_error() {
   int v = 0;
