@@ -873,8 +873,9 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
 // while step s computes; the serial part of a step is one 128-term dot
 // product per output.  Rows are 132 floats apart: 16-byte aligned, and a
 // quarter-warp's 16-byte row reads fall in distinct banks.
-constexpr int CB_NT = 256, CB_COLS = 8, CB_LD = 132;
-constexpr int CB_SMEM = (2 * 128 * CB_LD + 128 * CB_COLS) * 4 + 16;
+constexpr int CB_NT = 256, CB_LD = 132;
+// shared bytes of a COLS-column CTA: two X^T buffers and h_s[:, cols]
+constexpr int cb_smem(int cols) { return (2 * 128 * CB_LD + 128 * cols) * 4 + 16; }
 
 __device__ __forceinline__ void cb_load_x(float* dst, const float* src, int tid) {
   for (int e = tid; e < 128 * 32; e += CB_NT) {
@@ -884,18 +885,25 @@ __device__ __forceinline__ void cb_load_x(float* dst, const float* src, int tid)
   cp_async_commit();
 }
 
+// COLS columns per CTA (the host picks the largest grid that is still one
+// wave); thread (kk, half) computes CPT = COLS / 2 of them for row kk.  The
+// additive part B_{s+1} of the next step is fetched into registers while
+// step s computes, so no global-memory round trip sits on the serial path.
+template <int COLS>
 __global__ void __launch_bounds__(CB_NT) chunk_combine_kernel(const int32_t* __restrict__ cu,
                                                               int64_t N, int64_t T, int64_t H,
                                                               ChainPlan plan) {
+  constexpr int CPT = COLS / 2;
+  static_assert(CPT == 2 || CPT % 4 == 0, "columns per thread: 2 or a multiple of 4");
   extern __shared__ __align__(16) float cbs[];
   float* xbuf = cbs;                      // two X^T buffers [kk][r], rows CB_LD apart
-  float* cur = cbs + 2 * 128 * CB_LD;     // h_s[:, cols]  [r][CB_COLS]
+  float* cur = cbs + 2 * 128 * CB_LD;     // h_s[:, cols]  [r][COLS]
   __shared__ int64_t slot_sh;
   __shared__ int nseg_sh;
   const int tid = threadIdx.x;
   const int64_t n = blockIdx.y / H;
   const int h = (int)(blockIdx.y - n * H);
-  const int v0 = blockIdx.x * CB_COLS;
+  const int v0 = blockIdx.x * COLS;
   if (tid == 0) {
     int64_t slot = 0;
     int nseg = 1;
@@ -911,13 +919,28 @@ __global__ void __launch_bounds__(CB_NT) chunk_combine_kernel(const int32_t* __r
   const int nseg = nseg_sh;
   if (nseg < 3) return;
   const int64_t slot = slot_sh;
-  const int kk = tid >> 1, cb = (tid & 1) * 4;
+  const int kk = tid >> 1, cb = (tid & 1) * CPT;
+  auto load_b = [&](int s, float (&b)[CPT]) {
+    const float* src = seg_state(plan, slot + s, H, h, 1) + kk * 128 + v0 + cb;
+    if constexpr (CPT == 2) {
+      const float2 t = *reinterpret_cast<const float2*>(src);
+      b[0] = t.x; b[1] = t.y;
+    } else {
+#pragma unroll
+      for (int c = 0; c < CPT; c += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(src + c);
+        b[c] = t.x; b[c + 1] = t.y; b[c + 2] = t.z; b[c + 3] = t.w;
+      }
+    }
+  };
   cb_load_x(xbuf, seg_state(plan, slot + 1, H, h, 2), tid);
   {
     const float* h1 = seg_state(plan, slot + 1, H, h, 0);
-    for (int e = tid; e < 128 * CB_COLS; e += CB_NT)
-      cur[e] = h1[(e / CB_COLS) * 128 + v0 + (e % CB_COLS)];
+    for (int e = tid; e < 128 * COLS; e += CB_NT)
+      cur[e] = h1[(e / COLS) * 128 + v0 + (e % COLS)];
   }
+  float bnext[CPT];
+  load_b(1, bnext);
   for (int s = 1; s <= nseg - 2; ++s) {
     const float* xs_cur = xbuf + ((s - 1) & 1) * 128 * CB_LD;
     if (s + 1 <= nseg - 2) {
@@ -926,10 +949,11 @@ __global__ void __launch_bounds__(CB_NT) chunk_combine_kernel(const int32_t* __r
     } else {
       cp_async_wait_all();
     }
-    const float4 bv =
-        *reinterpret_cast<const float4*>(seg_state(plan, slot + s, H, h, 1) + kk * 128 + v0 + cb);
+    float acc[CPT];
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) acc[c] = bnext[c];
+    if (s + 1 <= nseg - 2) load_b(s + 1, bnext);
     __syncthreads();
-    float acc[4] = {bv.x, bv.y, bv.z, bv.w};
     const float* xrow = xs_cur + kk * CB_LD;
 #pragma unroll 4
     for (int r = 0; r < 128; r += 4) {
@@ -937,17 +961,36 @@ __global__ void __launch_bounds__(CB_NT) chunk_combine_kernel(const int32_t* __r
       const float xr[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float4 hv = *reinterpret_cast<const float4*>(cur + (r + u) * CB_COLS + cb);
-        acc[0] = fmaf(xr[u], hv.x, acc[0]);
-        acc[1] = fmaf(xr[u], hv.y, acc[1]);
-        acc[2] = fmaf(xr[u], hv.z, acc[2]);
-        acc[3] = fmaf(xr[u], hv.w, acc[3]);
+        const float* hrow = cur + (r + u) * COLS + cb;
+        if constexpr (CPT == 2) {
+          const float2 hv = *reinterpret_cast<const float2*>(hrow);
+          acc[0] = fmaf(xr[u], hv.x, acc[0]);
+          acc[1] = fmaf(xr[u], hv.y, acc[1]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < CPT; c += 4) {
+            const float4 hv = *reinterpret_cast<const float4*>(hrow + c);
+            acc[c] = fmaf(xr[u], hv.x, acc[c]);
+            acc[c + 1] = fmaf(xr[u], hv.y, acc[c + 1]);
+            acc[c + 2] = fmaf(xr[u], hv.z, acc[c + 2]);
+            acc[c + 3] = fmaf(xr[u], hv.w, acc[c + 3]);
+          }
+        }
       }
     }
     __syncthreads();  // every thread is done reading h_s and X_s
-    *reinterpret_cast<float4*>(cur + kk * CB_COLS + cb) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    *reinterpret_cast<float4*>(seg_state(plan, slot + s + 1, H, h, 0) + kk * 128 + v0 + cb) =
-        make_float4(acc[0], acc[1], acc[2], acc[3]);
+    float* gout = seg_state(plan, slot + s + 1, H, h, 0) + kk * 128 + v0 + cb;
+    if constexpr (CPT == 2) {
+      *reinterpret_cast<float2*>(cur + kk * COLS + cb) = make_float2(acc[0], acc[1]);
+      *reinterpret_cast<float2*>(gout) = make_float2(acc[0], acc[1]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < CPT; c += 4) {
+        const float4 t = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+        *reinterpret_cast<float4*>(cur + kk * COLS + cb + c) = t;
+        *reinterpret_cast<float4*>(gout + c) = t;
+      }
+    }
     __syncthreads();
   }
 }
@@ -1153,11 +1196,28 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
       mq, mk, mv, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
         plan);
   if (int rc = check_launch("chunk_gated_delta_rule(chain, first segments)")) return rc;
-  if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_combine_kernel, gdn::CB_SMEM,
-                                     "chunk_gated_delta_rule(combine)"))
-    return rc;
-  gdn::chunk_combine_kernel<<<dim3(128 / gdn::CB_COLS, (unsigned)(N * H)), gdn::CB_NT,
-                              gdn::CB_SMEM, st>>>(cu_seqlens, N, T, H, plan);
+  {
+    // the fewest columns per CTA (the most CTAs per head) whose grid is still
+    // one wave of one CTA per SM: each CTA walks every segment serially
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int cols = 4;
+    while (cols < 32 && (int64_t)N * H * (128 / cols) > sms) cols *= 2;
+    auto launch = [&](auto kern, int c) -> int {
+      if (int rc = gdn::ensure_smem_attr((const void*)kern, gdn::cb_smem(c),
+                                         "chunk_gated_delta_rule(combine)"))
+        return rc;
+      kern<<<dim3(128 / c, (unsigned)(N * H)), gdn::CB_NT, gdn::cb_smem(c), st>>>(cu_seqlens, N,
+                                                                                  T, H, plan);
+      return 0;
+    };
+    int rc = cols == 4    ? launch(gdn::chunk_combine_kernel<4>, 4)
+             : cols == 8  ? launch(gdn::chunk_combine_kernel<8>, 8)
+             : cols == 16 ? launch(gdn::chunk_combine_kernel<16>, 16)
+                          : launch(gdn::chunk_combine_kernel<32>, 32);
+    if (rc) return rc;
+  }
   if (int rc = check_launch("chunk_gated_delta_rule(combine)")) return rc;
   plan.phase = 3;
   gdn::chunk_chain_kernel<<<(unsigned)(slots * H), gdn::C_NT, gdn::C_SMEM, st>>>(
