@@ -131,8 +131,9 @@ XOPS_API int xops_causal_conv1d_varlen(const void* x, void* conv_state, const vo
  * read from slot ssm_state_indices[n] (or n); ht == h0 updates those slots
  * in place, any other ht is [N, HV, K, V] (stride ht_stride) indexed by
  * sequence.  Sequences: cu_seqlens [N+1] int32, or NULL with N == B rows of
- * T tokens.  ssm_state_indices [N] int32 or NULL (slot n).  K, V <= 128
- * (multiples of 32).  Replaces npu_fused_recurrent_gated_delta_rule
+ * T tokens.  ssm_state_indices [N] int32 or NULL (slot n); a negative
+ * index starts the sequence from a zero state and, in place, writes nothing
+ * back.  K, V in {64, 128}.  Replaces npu_fused_recurrent_gated_delta_rule
  * (triton_npu/torch_api/npu_triton_recurrent_gated_delta_rule.cpp:54-246). */
 XOPS_API int xops_fused_recurrent_gated_delta_rule(const void* q, const void* k, const void* v,
                                           const float* g, const float* beta, void* o,
@@ -143,6 +144,34 @@ XOPS_API int xops_fused_recurrent_gated_delta_rule(const void* q, const void* k,
                                           int64_t K, int64_t V, int64_t h0_stride,
                                           int64_t ht_stride, float scale,
                                           int use_qk_l2norm_in_kernel, void* stream);
+
+/* The recurrent step with the gates computed from the projections in the
+ * step: g = -exp(A_log[h]) * softplus(a + dt_bias[h]) (torch Softplus with
+ * softplus_beta / softplus_threshold), beta = sigmoid(b).  A_log, dt_bias
+ * [HV] fp32; a, b [B, T, HV] of ab_dtype; q, k [B, T, H, K], v [B, T, HV, V]
+ * bf16; o [B, T, HV, V] bf16.  cu_seqlens [N+1] int32 over the B*T
+ * flattened tokens (required).  Sequence n starts from slot
+ * initial_state_indices[n] of initial_state_source [slots, HV, K, V] fp32
+ * and writes its final state back there; a negative index starts from zeros
+ * and writes nothing.  K, V in {64, 128}.  Replaces
+ * npu_fused_sigmoid_gating_delta_rule_update
+ * (triton_npu/torch_api/npu_triton_fused_sigmoid_gating_delta_rule_update.cpp:54-179). */
+XOPS_API int xops_fused_sigmoid_gating_delta_rule_update(
+    const float* A_log, const void* a, const float* dt_bias, float softplus_beta,
+    float softplus_threshold, const void* q, const void* k, const void* v, const void* b,
+    void* o, float* initial_state_source, const int32_t* initial_state_indices,
+    const int32_t* cu_seqlens, float scale, int64_t B, int64_t T, int64_t N, int64_t H,
+    int64_t HV, int64_t K, int64_t V, int ab_dtype, int use_qk_l2norm_in_kernel, void* stream);
+
+/* GDN gates from the projections: g = -exp(A_log[h]) * softplus(a +
+ * dt_bias[h]) fp32, beta_out = sigmoid(b) in b's dtype; a, b, g, beta_out
+ * [rows, heads] (rows = batch for decode, tokens for prefill), A_log and
+ * dt_bias [heads] fp32.  Replaces npu_fused_gdn_gating
+ * (triton_npu/torch_api/npu_triton_fused_gdn_gating.cpp:33-93). */
+XOPS_API int xops_fused_gdn_gating(const float* A_log, const void* a, const void* b,
+                                   const float* dt_bias, float* g, void* beta_out, int64_t rows,
+                                   int64_t heads, int a_dtype, int b_dtype, float softplus_beta,
+                                   float softplus_threshold, void* stream);
 
 /* Chunked gated delta rule prefill on the tensor cores.  q, k [B, T, Hg, K],
  * v [B, T, H, V] bf16; g, beta [B, T, H] fp32; h0 [N, H, K, V] fp32 or NULL;

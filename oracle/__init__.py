@@ -34,5 +34,7 @@ from .gdn import (  # noqa: F401
     chunk_fwd_o,
     chunk_gated_delta_rule,
     fused_recurrent_gated_delta_rule,
+    fused_gdn_gating,
+    fused_sigmoid_gating_delta_rule_update,
     prepare_chunk_offsets,
 )

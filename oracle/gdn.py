@@ -317,3 +317,78 @@ def fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None,
         else:
             final[n] = st.to(final.dtype)
     return o.to(v.dtype), (initial_state if inplace_final_state else final)
+
+
+def _softplus(x, beta=1.0, threshold=20.0):
+    """torch Softplus semantics: log(1 + e^{beta x}) / beta, or x where
+    beta x > threshold."""
+    bx = beta * x
+    return torch.where(bx <= threshold, torch.log1p(torch.exp(bx)) / beta, x)
+
+
+def fused_gdn_gating(A_log, a, b, dt_bias, beta=1.0, threshold=20.0):
+    """GDN gates from the projections: ``g = -exp(A_log) * softplus(a +
+    dt_bias)`` (fp32) and ``beta_out = sigmoid(b)`` (b's dtype).
+
+    Restates ``torch_fused_gdn_gating``
+    (triton_npu/triton_src/test_fused_gdn_gating.py:45-57) with the output
+    shapes of ``npu_fused_gdn_gating``
+    (triton_npu/torch_api/npu_triton_fused_gdn_gating.cpp:55-63):
+    a, b are ``[batch, heads]``; both outputs are ``[1, batch, heads]``.
+    """
+    g = -torch.exp(A_log.to(torch.float32)) * _softplus(
+        a.to(torch.float32) + dt_bias.to(torch.float32), beta, threshold)
+    beta_out = torch.sigmoid(b.to(torch.float32)).to(b.dtype)
+    return g[None], beta_out[None]
+
+
+def fused_sigmoid_gating_delta_rule_update(A_log, a, dt_bias, q, k, v, b,
+                                           initial_state_source, initial_state_indices,
+                                           cu_seqlens, scale=None,
+                                           use_qk_l2norm_in_kernel=False,
+                                           softplus_beta=1.0, softplus_threshold=20.0):
+    """Recurrent gated delta rule with the gates computed from the
+    projections inside the step.
+
+    Restates ``torch_sigmoid_gating_delta_rule_update``
+    (triton_npu/triton_src/test_fused_sigmoid_gating_delta_rule_update.py:
+    178-222) with the slot rules of
+    ``fused_sigmoid_gating_delta_rule_update_kernel`` (same file :11-117):
+    per token ``g = -exp(A_log) softplus(a + dt_bias)``, ``beta =
+    sigmoid(b)`` (fp32), then the delta-rule step of
+    ``fused_recurrent_gated_delta_rule``.  Sequence n starts from slot
+    ``initial_state_indices[n]`` of ``initial_state_source`` and writes its
+    final state back there (in place); a negative index starts from zeros
+    and writes nothing.  Returns ``o [B, T, HV, V]`` in q's dtype.
+    """
+    bsz, t_all, hq, kd = k.shape
+    hv, vd = v.shape[2], v.shape[3]
+    if scale is None:
+        scale = kd ** -0.5
+    qf, kf = q.to(torch.float32), k.to(torch.float32)
+    if use_qk_l2norm_in_kernel:
+        qf = qf / torch.sqrt((qf * qf).sum(-1, keepdim=True) + 1e-6)
+        kf = kf / torch.sqrt((kf * kf).sum(-1, keepdim=True) + 1e-6)
+    qf, kf = _expand(qf, hv) * scale, _expand(kf, hv)
+    vf = v.to(torch.float32)
+    g = -torch.exp(A_log.to(torch.float32)) * _softplus(
+        a.to(torch.float32) + dt_bias.to(torch.float32), softplus_beta, softplus_threshold)
+    bt = torch.sigmoid(b.to(torch.float32))
+    qf, kf, vf = (x.reshape(bsz * t_all, hv, -1) for x in (qf, kf, vf))
+    g, bt = g.reshape(bsz * t_all, hv), bt.reshape(bsz * t_all, hv)
+    o = torch.zeros(bsz * t_all, hv, vd, dtype=torch.float32)
+    for n in range(cu_seqlens.numel() - 1):
+        s, e = int(cu_seqlens[n]), int(cu_seqlens[n + 1])
+        if e == s:
+            continue
+        slot = int(initial_state_indices[n])
+        st = (torch.zeros(hv, kd, vd) if slot < 0
+              else initial_state_source[slot].to(torch.float32).clone())
+        for t in range(s, e):
+            st = st * torch.exp(g[t])[:, None, None]
+            vn = (vf[t] - torch.einsum("hk,hkv->hv", kf[t], st)) * bt[t][:, None]
+            st = st + kf[t][:, :, None] * vn[:, None, :]
+            o[t] = torch.einsum("hk,hkv->hv", qf[t], st)
+        if slot >= 0:
+            initial_state_source[slot].copy_(st.to(initial_state_source.dtype))
+    return o.reshape(bsz, t_all, hv, vd).to(q.dtype)

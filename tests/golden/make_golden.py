@@ -39,7 +39,8 @@ def _import_reference(ref_root):
     sys.path.insert(0, os.path.join(ref_root, "triton_npu", "triton_src"))
     names = ["test_chunk_gated_delta_rule", "test_fused_recurrent_gated_delta_rule",
              "test_layernorm_fwd", "test_causal_conv1d_update",
-             "test_causal_conv1d_update_v2", "test_split_rmsnorm_rope", "test_l2norm"]
+             "test_causal_conv1d_update_v2", "test_split_rmsnorm_rope", "test_l2norm",
+             "test_fused_gdn_gating", "test_fused_sigmoid_gating_delta_rule_update"]
     return {n: importlib.import_module(n) for n in names}
 
 
@@ -268,18 +269,73 @@ def gen_recurrent(m):
     _save("fused_recurrent_gated_delta_rule", cases)
 
 
+def gen_gating(m):
+    ref = m["test_fused_gdn_gating"].torch_fused_gdn_gating
+    cases = []
+    # the reference test's head counts and token counts (test_fused_gdn_gating.py:95-97),
+    # plus a prefill-sized row count and a saturated-softplus case
+    for T, HV, dt in [(1, 1, torch.bfloat16), (4, 3, torch.bfloat16), (16, 32, torch.bfloat16),
+                      (8, 48, torch.bfloat16), (1000, 32, torch.bfloat16),
+                      (64, 16, torch.float32)]:
+        g0 = torch.Generator().manual_seed(T * 100 + HV)
+        A_log = torch.randn(HV, generator=g0)
+        a = torch.randn(T, HV, generator=g0).to(dt)
+        if dt == torch.float32:
+            a = a * 15  # a + dt_bias crosses the softplus threshold (20)
+        b = torch.randn(T, HV, generator=g0).to(dt)
+        dt_bias = torch.ones(HV) if T < 1000 else torch.rand(HV, generator=g0)
+        g, beta = ref(A_log, a, b, dt_bias)
+        cases.append({"name": f"T{T}_HV{HV}_{str(dt)[6:]}", "args": {
+            "A_log": A_log, "a": a, "b": b, "dt_bias": dt_bias, "beta": 1.0, "threshold": 20.0},
+            "out": {"g": g[None], "beta": beta[None]}})
+    _save("fused_gdn_gating", cases)
+
+
+def gen_sigmoid_gating(m):
+    ref = m["test_fused_sigmoid_gating_delta_rule_update"].torch_sigmoid_gating_delta_rule_update
+    cases = []
+    # (batch, T, H, HV, K, indices) -- small versions of the reference test's
+    # head ratios (test_fused_sigmoid_gating_delta_rule_update.py:225-247; the
+    # fp32 states keep fixtures small only at few heads), multi-token rows and
+    # a negative slot (starts from zero, writes nothing back)
+    for B, T, H, HV, K, idx in [(2, 1, 2, 4, 128, None), (2, 1, 1, 8, 64, None),
+                                (3, 1, 2, 6, 64, None), (3, 3, 2, 4, 64, [2, -1, 0])]:
+        torch.manual_seed(47 + B + H + HV)
+        q = torch.randn(B, T, H, K, dtype=torch.bfloat16)
+        k = torch.randn(B, T, H, K, dtype=torch.bfloat16)
+        v = torch.randn(B, T, HV, K, dtype=torch.bfloat16)
+        a = torch.randn(B, T, HV, dtype=torch.bfloat16)
+        b = torch.randn(B, T, HV, dtype=torch.bfloat16)
+        A_log = torch.randn(HV, dtype=torch.float32)
+        dt_bias = torch.randn(HV, dtype=torch.float32)
+        h0 = torch.randn(B, HV, K, K, dtype=torch.float32)
+        indices = (torch.arange(B, dtype=torch.int32) if idx is None
+                   else torch.tensor(idx, dtype=torch.int32))
+        cu = torch.arange(B + 1, dtype=torch.int32) * T
+        o, state = ref(A_log, a, dt_bias, q, k, v, b, h0.clone(), indices, cu, K ** -0.5, True)
+        cases.append({"name": f"B{B}_T{T}_H{H}_HV{HV}_K{K}" + ("_neg" if idx else ""), "args": {
+            "A_log": A_log, "a": a, "dt_bias": dt_bias, "q": q, "k": k, "v": v, "b": b,
+            "initial_state_source": h0, "initial_state_indices": indices, "cu_seqlens": cu,
+            "scale": K ** -0.5, "use_qk_l2norm_in_kernel": True},
+            "out": {"o": o, "state": state}})
+    _save("fused_sigmoid_gating_delta_rule_update", cases)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref-root", default="/root/reference")
+    ap.add_argument("--only", default="",
+                    help="comma-separated subset of: layernorm,l2norm,rope,conv,chunk,"
+                         "recurrent,gating,sigmoid_gating")
     args = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     m = _import_reference(args.ref_root)
-    gen_layernorm(m)
-    gen_l2norm(m)
-    gen_rope(m)
-    gen_conv(m)
-    gen_chunk(m)
-    gen_recurrent(m)
+    gens = {"layernorm": gen_layernorm, "l2norm": gen_l2norm, "rope": gen_rope,
+            "conv": gen_conv, "chunk": gen_chunk, "recurrent": gen_recurrent,
+            "gating": gen_gating, "sigmoid_gating": gen_sigmoid_gating}
+    for name, fn in gens.items():
+        if not args.only or name in args.only.split(","):
+            fn(m)
 
 
 if __name__ == "__main__":

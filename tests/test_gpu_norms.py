@@ -49,6 +49,10 @@ CASES = [  # (M, N, group, rms, bias, z, before, xdtype, wdtype)
     (4200, 1024, 512, True, True, False, True, torch.bfloat16, torch.bfloat16),    # 4 / warp
     (130, 16384, 16384, False, False, False, True, torch.bfloat16, torch.bfloat16),
     (4099, 1040, 520, False, True, False, True, torch.bfloat16, torch.bfloat16),   # odd tiles
+    # few wide segments (< 4 MB): one CTA per segment
+    (40, 512, 512, False, True, True, False, torch.bfloat16, torch.bfloat16),      # 64 threads
+    (100, 2048, 1024, True, False, True, True, torch.float16, torch.float16),      # 2 groups
+    (8, 8192, 8192, False, True, False, True, torch.bfloat16, torch.float32),      # 4 vectors
 ]
 
 
@@ -81,7 +85,8 @@ def test_layer_norm_strided_rows():
                                       ((4, 128, 4096), torch.float32), ((3, 100), torch.bfloat16),
                                       ((2048, 2048), torch.bfloat16),   # wide streaming path
                                       ((1100, 4000), torch.float16),
-                                      ((9000, 128), torch.bfloat16)])   # narrow streaming path
+                                      ((9000, 128), torch.bfloat16),    # narrow streaming path
+                                      ((300, 1024), torch.bfloat16)])   # CTA per row
 def test_gemma_rms_norm(shape, dt):
     g = torch.Generator().manual_seed(1234)
     x = torch.randn(*shape, generator=g).to(dt)
@@ -103,9 +108,11 @@ def test_l2norm_golden(case):
     (assert_fp32 if x.dtype == torch.float32 else assert_bf16)(y, ref)
 
 
-@pytest.mark.parametrize("shape", [(20000, 128), (9000, 64), (9000, 256), (3000, 1024), (700, 4104)])
+@pytest.mark.parametrize("shape", [(20000, 128), (9000, 64), (9000, 256), (3000, 1024), (700, 4104),
+                                   (50, 2048)])
 def test_l2norm_streaming(shape):
-    """bf16 rows large enough for the bulk-copy streaming path (narrow and wide)."""
+    """bf16 rows on the bulk-copy streaming paths (narrow and wide) and, below
+    4 MB, the CTA-per-row path."""
     from torch_npu_ops_b200 import _lib
     g = torch.Generator().manual_seed(shape[0] + shape[1])
     x = (3 * torch.randn(*shape, generator=g)).to(torch.bfloat16)

@@ -136,6 +136,35 @@ def test_fused_recurrent(case):
     _close(st, ref_h, atol=1e-2, rtol=5e-2)
 
 
+@pytest.mark.parametrize("case", _cases("fused_gdn_gating"), ids=lambda c: c["name"])
+def test_fused_gdn_gating(case):
+    a = case["args"]
+    g, beta = oracle.fused_gdn_gating(a["A_log"], a["a"], a["b"], a["dt_bias"], a["beta"],
+                                      a["threshold"])
+    assert g.shape == case["out"]["g"].shape and g.dtype == torch.float32
+    assert beta.shape == case["out"]["beta"].shape and beta.dtype == a["b"].dtype
+    _close(g, case["out"]["g"], atol=1e-6, rtol=1e-6)
+    _close(beta, case["out"]["beta"], atol=0.0)
+
+
+@pytest.mark.parametrize("case", _cases("fused_sigmoid_gating_delta_rule_update"),
+                         ids=lambda c: c["name"])
+def test_fused_sigmoid_gating_delta_rule_update(case):
+    a = case["args"]
+    st = a["initial_state_source"].clone()
+    o = oracle.fused_sigmoid_gating_delta_rule_update(
+        a["A_log"], a["a"], a["dt_bias"], a["q"], a["k"], a["v"], a["b"], st,
+        a["initial_state_indices"], a["cu_seqlens"], a["scale"], a["use_qk_l2norm_in_kernel"])
+    # the reference's torch path rounds the normalised q/k and sigmoid(b) to
+    # bf16; the kernel keeps them fp32.  Bounds are the reference test's own
+    # (test_fused_sigmoid_gating_delta_rule_update.py:299-304).
+    _close(o, case["out"]["o"], atol=1e-2, rtol=5e-3)
+    _close(st, case["out"]["state"], atol=2e-2, rtol=5e-2)
+    untouched = [i for i in range(st.shape[0]) if i not in a["initial_state_indices"].tolist()]
+    for i in untouched:  # slots no sequence names keep their values
+        assert torch.equal(st[i], a["initial_state_source"][i])
+
+
 def test_gemma_rms_norm_definition():
     """Parity unpinned (closed CANN op): check the written-down definition on
     a hand-computed row and the rstd shape rule."""

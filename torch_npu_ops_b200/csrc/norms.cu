@@ -637,6 +637,124 @@ __global__ void __launch_bounds__(RN_NT, 2) norm_wide_stream_kernel(
   }
 }
 
+// Few wide segments (decode-sized batches such as cfg4's [256, 2048]): one
+// CTA per (row, group) segment, G / (8 VPT) threads each holding VPT 16-byte
+// vectors, so every segment's bytes are in flight at once across the grid.
+// Statistics are warp shuffles plus one shared-memory round per statistic.
+// x and y rows may be strided (the segment is contiguous inside its row).
+template <int NW>
+__device__ __forceinline__ float block_sum(float v, float* red, int warp, int lane) {
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < NW ? red[lane] : 0.f;
+  t = warp_sum(t);
+  __syncthreads();  // red is reused by the next statistic
+  return t;
+}
+
+template <typename TX, typename TW, int KIND, bool HAS_Z, bool HAS_B, int VPT, int NT>
+__global__ void __launch_bounds__(NT) norm_rowblock_kernel(
+    const TX* __restrict__ x, const TW* __restrict__ w, const TW* __restrict__ b,
+    const TX* __restrict__ z, TX* __restrict__ y, float* __restrict__ mean_out,
+    float* __restrict__ rstd_out, int64_t M, int64_t ngroups, int64_t sx, int64_t sz,
+    int64_t sy, float eps, bool norm_before_gate) {
+  constexpr int G = NT * VPT * 8;
+  constexpr int NW = NT / 32;
+  __shared__ float red[32];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t seg = blockIdx.x;
+  const int64_t row = seg / ngroups, grp = seg - row * ngroups;
+  const TX* xr = x + row * sx + grp * G;
+  const TX* zr = HAS_Z ? z + row * sz + grp * G : nullptr;
+  float2 v[VPT][4], gz[VPT][4];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int c = (j * NT + tid) * 8;
+    unpack8<TX>(__ldg(reinterpret_cast<const uint4*>(xr + c)), v[j]);
+    if constexpr (HAS_Z) {
+      silu8<TX>(__ldg(reinterpret_cast<const uint4*>(zr + c)), gz[j]);
+      if (!norm_before_gate) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[j][u] = fmul2(v[j][u], gz[j][u]);
+      }
+    }
+  }
+  float mu = 0.f;
+  if constexpr (KIND == K_LN) {
+    float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s2 = fadd2(s2, v[j][u]);
+    mu = block_sum<NW>(s2.x + s2.y, red, warp, lane) * (1.0f / G);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[j][u] = fsub2(v[j][u], make_float2(mu, mu));
+  }
+  float2 q2 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) q2 = ffma2(v[j][u], v[j][u], q2);
+  const float ss = block_sum<NW>(q2.x + q2.y, red, warp, lane);
+  const float rstd = rsqrtf(ss * (KIND == K_L2 ? 1.0f : 1.0f / G) + eps);
+  if constexpr (KIND != K_L2) {
+    if (tid == 0) {
+      rstd_out[grp * M + row] = rstd;
+      if constexpr (KIND == K_LN) mean_out[grp * M + row] = mu;
+    }
+  }
+  const float2 r2 = make_float2(rstd, rstd);
+  TX* yr = y + row * sy + grp * G;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int c = (j * NT + tid) * 8;
+    float2 wv[4], bv[4];
+    if constexpr (KIND != K_L2) {
+      ldg_w8<TW>(w + grp * G + c, wv);
+      if constexpr (HAS_B) ldg_w8<TW>(b + grp * G + c, bv);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float2 t = fmul2(v[j][u], r2);
+      if constexpr (KIND == K_GEMMA) t = ffma2(t, wv[u], t);
+      if constexpr (KIND == K_LN || KIND == K_RMS) {
+        if constexpr (HAS_B) t = ffma2(t, wv[u], bv[u]);
+        else t = fmul2(t, wv[u]);
+      }
+      if constexpr (HAS_Z) {
+        if (norm_before_gate) t = fmul2(t, gz[j][u]);
+      }
+      v[j][u] = t;
+    }
+    *reinterpret_cast<uint4*>(yr + c) = pack8<TX>(v[j]);
+  }
+}
+
+// G = 8 * VPT * NT for the (VPT, NT) pairs compiled: 512..8192
+template <typename TX, typename TW, int KIND, bool HAS_Z, bool HAS_B>
+int launch_norm_rowblock(const void* x, const void* w, const void* b, const void* z, void* y,
+                         float* mean, float* rstd, int64_t M, int64_t ng, int64_t G, int64_t sx,
+                         int64_t sz, int64_t sy, float eps, bool nbg, cudaStream_t st,
+                         const char* what) {
+#define XOPS_RB(VPT, NT)                                                                       \
+  if (G == 8 * VPT * NT) {                                                                     \
+    norm_rowblock_kernel<TX, TW, KIND, HAS_Z, HAS_B, VPT, NT><<<(unsigned)(M * ng), NT, 0, st>>>( \
+        (const TX*)x, (const TW*)w, (const TW*)b, (const TX*)z, (TX*)y, mean, rstd, M, ng, sx,  \
+        sz, sy, eps, nbg);                                                                     \
+    return check_launch(what);                                                                 \
+  }
+  XOPS_RB(1, 64)
+  XOPS_RB(1, 128)
+  XOPS_RB(1, 256)
+  XOPS_RB(2, 256)
+  XOPS_RB(4, 256)
+#undef XOPS_RB
+  return -1;
+}
+
 int sm_count() {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess)
@@ -708,7 +826,10 @@ int dispatch_stream(const void* x, const void* w, const void* b, const void* z, 
       if (G == 256) return launch_norm_stream<TX, TW, 256, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st, what);
       return -1;
     }
-    if (G > (HAS_Z ? 8192 : 16384) || segs * G * 2 < (int64_t(4) << 20)) return -1;
+    if (G > (HAS_Z ? 8192 : 16384)) return -1;
+    if (segs * G * 2 < (int64_t(4) << 20))  // too small to fill a persistent grid
+      return launch_norm_rowblock<TX, TW, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, G,
+                                                              N, N, N, eps, nbg, st, what);
     return launch_norm_wide<TX, TW, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, G, eps,
                                                         nbg, st, what);
   }

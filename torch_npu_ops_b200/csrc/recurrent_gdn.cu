@@ -14,10 +14,41 @@
 // coalesced 16-byte vector (for V = 128) and each thread has K/4
 // independent loads in flight.  The two reductions over K (S^T k and S^T q)
 // finish across the 4 warps through shared memory.
+//
+// The same kernel serves fused_sigmoid_gating_delta_rule_update
+// (triton_npu/triton_src/test_fused_sigmoid_gating_delta_rule_update.py:11-117):
+// there the gates come from the projections inside the step,
+//   g = -exp(A_log[h]) softplus(a + dt_bias[h]),  beta = sigmoid(b),
+// and a negative slot index means "start from zeros, write nothing back".
+// A negative slot gets that meaning on the plain path too (the reference
+// kernel there would address memory before the state buffer).
 #include "common.cuh"
 
 namespace xops {
 namespace {
+
+// Gates computed in the step from the projections (a.a == nullptr: the
+// precomputed g / beta arrays are used instead).
+struct GateSrc {
+  const float* A_log;
+  const void* a;
+  const float* dt_bias;
+  const void* b;
+  int ab_dtype;
+  float sp_beta, sp_thr;
+};
+
+__device__ __forceinline__ float load_any(const void* p, int64_t i, int dtype) {
+  if (dtype == XOPS_F32) return static_cast<const float*>(p)[i];
+  if (dtype == XOPS_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+// torch Softplus: log(1 + e^{beta x}) / beta, or x once beta x > threshold
+__device__ __forceinline__ float softplus_f(float x, float beta, float thr) {
+  const float bx = beta * x;
+  return bx <= thr ? log1pf(expf(bx)) / beta : x;
+}
 
 template <int K, int V>
 __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
@@ -26,7 +57,7 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
     const float* __restrict__ beta, __nv_bfloat16* __restrict__ o,
     const float* h0, float* ht, const int32_t* __restrict__ cu,
     const int32_t* __restrict__ slots, int64_t T, int64_t H, int64_t HV, int64_t h0_stride,
-    int64_t ht_stride, float scale, bool l2norm) {
+    int64_t ht_stride, float scale, bool l2norm, GateSrc gs) {
   constexpr int ROWS = K / 4;    // state rows per warp
   constexpr int COLS = V / 32;   // state columns per lane
   __shared__ float s_q[K], s_k[K];
@@ -46,10 +77,14 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
     eos = bos + T;
   }
   const int64_t slot = slots ? (int64_t)slots[n] : n;
-  const float* hsrc = h0 + slot * h0_stride + (int64_t)hv * K * V;
+  const bool inplace = (const float*)ht == h0;
+  // a negative slot: zero initial state, and (in place) no write-back
+  const bool has_slot = slot >= 0;
+  const float* hsrc = h0 + (has_slot ? slot : 0) * h0_stride + (int64_t)hv * K * V;
   // in place (ht == h0): back into the same slot; otherwise ht is indexed by
   // sequence (the reference's INPLACE_FINAL_STATE split, :169-188)
-  float* hdst = ht + ((const float*)ht == h0 ? slot : n) * ht_stride + (int64_t)hv * K * V;
+  float* hdst = ht + (inplace ? (has_slot ? slot : 0) : n) * ht_stride + (int64_t)hv * K * V;
+  const bool write_back = !inplace || has_slot;
   const int r0 = warp * ROWS, c0 = lane * COLS;
 
   // h0 and ht may be the same buffer (in-place update): each thread reads
@@ -59,7 +94,10 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
   for (int r = 0; r < ROWS; ++r) {
     float tmp[COLS];
     const float* src = hsrc + (int64_t)(r0 + r) * V + c0;
-    if constexpr (COLS == 4) {
+    if (!has_slot) {
+#pragma unroll
+      for (int c = 0; c < COLS; ++c) tmp[c] = 0.f;
+    } else if constexpr (COLS == 4) {
       const float4 t4 = *reinterpret_cast<const float4*>(src);
       tmp[0] = t4.x; tmp[1] = t4.y; tmp[2] = t4.z; tmp[3] = t4.w;
     } else {
@@ -69,6 +107,8 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
 #pragma unroll
     for (int c = 0; c < COLS; ++c) S[r][c] = tmp[c];
   }
+  const float neg_a = gs.a ? -expf(gs.A_log[hv]) : 0.f;
+  const float dtb = gs.a ? gs.dt_bias[hv] : 0.f;
 
   for (int64_t t = bos; t < eos; ++t) {
     // stage q, k (fp32) in shared memory, optionally L2-normalised
@@ -94,8 +134,15 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
     }
     __syncthreads();
     const float qs = s_scal[0], ks = s_scal[1];
-    const float decay = __expf(g[t * HV + hv]);
-    const float b = beta ? beta[t * HV + hv] : 1.0f;
+    float decay, b;
+    if (gs.a) {
+      decay = __expf(neg_a * softplus_f(load_any(gs.a, t * HV + hv, gs.ab_dtype) + dtb,
+                                        gs.sp_beta, gs.sp_thr));
+      b = 1.0f / (1.0f + expf(-load_any(gs.b, t * HV + hv, gs.ab_dtype)));
+    } else {
+      decay = __expf(g[t * HV + hv]);
+      b = beta ? beta[t * HV + hv] : 1.0f;
+    }
 
     float part[COLS];
 #pragma unroll
@@ -148,6 +195,7 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
     __syncthreads();  // s_q/s_k/s_red reused by the next token
   }
 
+  if (!write_back) return;
 #pragma unroll
   for (int r = 0; r < ROWS; ++r) {
     float tmp[COLS];
@@ -155,6 +203,29 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
     for (int c = 0; c < COLS; ++c) tmp[c] = S[r][c];
     store_vec<float, COLS>(hdst + (int64_t)(r0 + r) * V + c0, tmp);
   }
+}
+
+int launch_recurrent(const void* q, const void* k, const void* v, const float* g,
+                     const float* beta, void* o, const float* h0, float* ht,
+                     const int32_t* cu_seqlens, const int32_t* slots, int64_t T, int64_t N,
+                     int64_t H, int64_t HV, int64_t K, int64_t V, int64_t h0_stride,
+                     int64_t ht_stride, float scale, bool l2, GateSrc gs, cudaStream_t st,
+                     const char* what) {
+  const unsigned grid = (unsigned)(N * HV);
+#define XOPS_REC(KK, VV)                                                                      \
+  if (K == KK && V == VV) {                                                                   \
+    recurrent_gdn_kernel<KK, VV><<<grid, 128, 0, st>>>(                                       \
+        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta,   \
+        (__nv_bfloat16*)o, h0, ht, cu_seqlens, slots, T, H, HV, h0_stride, ht_stride, scale,  \
+        l2, gs);                                                                              \
+    return check_launch(what);                                                                \
+  }
+  XOPS_REC(128, 128)
+  XOPS_REC(64, 64)
+  XOPS_REC(128, 64)
+  XOPS_REC(64, 128)
+#undef XOPS_REC
+  return set_error(XOPS_ERR_UNSUPPORTED, "%s: unreachable", what);
 }
 
 }  // namespace
@@ -187,21 +258,40 @@ extern "C" int xops_fused_recurrent_gated_delta_rule(
   XOPS_REQUIRE(aligned16(h0) && aligned16(ht) && aligned16(v) && aligned16(o) &&
                    (h0_stride % 4) == 0 && (ht_stride % 4) == 0,
                "fused_recurrent_gated_delta_rule: state/v/o must be 16-byte aligned");
-  cudaStream_t st = (cudaStream_t)stream;
-  const unsigned grid = (unsigned)(N * HV);
-  const bool l2 = use_qk_l2norm_in_kernel != 0;
-#define XOPS_REC(KK, VV)                                                                      \
-  if (K == KK && V == VV) {                                                                   \
-    recurrent_gdn_kernel<KK, VV><<<grid, 128, 0, st>>>(                                       \
-        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta,   \
-        (__nv_bfloat16*)o, h0, ht, cu_seqlens, ssm_state_indices, T, H, HV, h0_stride,        \
-        ht_stride, scale, l2);                                                                \
-    return check_launch("fused_recurrent_gated_delta_rule");                                  \
-  }
-  XOPS_REC(128, 128)
-  XOPS_REC(64, 64)
-  XOPS_REC(128, 64)
-  XOPS_REC(64, 128)
-#undef XOPS_REC
-  return set_error(XOPS_ERR_UNSUPPORTED, "fused_recurrent_gated_delta_rule: unreachable");
+  GateSrc none{};
+  return launch_recurrent(q, k, v, g, beta, o, h0, ht, cu_seqlens, ssm_state_indices, T, N, H,
+                          HV, K, V, h0_stride, ht_stride, scale, use_qk_l2norm_in_kernel != 0,
+                          none, (cudaStream_t)stream, "fused_recurrent_gated_delta_rule");
+}
+
+extern "C" int xops_fused_sigmoid_gating_delta_rule_update(
+    const float* A_log, const void* a, const float* dt_bias, float softplus_beta,
+    float softplus_threshold, const void* q, const void* k, const void* v, const void* b,
+    void* o, float* initial_state_source, const int32_t* initial_state_indices,
+    const int32_t* cu_seqlens, float scale, int64_t B, int64_t T, int64_t N, int64_t H,
+    int64_t HV, int64_t K, int64_t V, int ab_dtype, int use_qk_l2norm_in_kernel,
+    void* stream) {
+  const char* what = "fused_sigmoid_gating_delta_rule_update";
+  XOPS_REQUIRE(B >= 1 && T >= 0 && N >= 0 && H >= 1 && HV >= 1, "%s: bad shape", what);
+  XOPS_REQUIRE(HV % H == 0, "%s: HV=%lld not divisible by H=%lld", what, (long long)HV,
+               (long long)H);
+  XOPS_REQUIRE(ab_dtype == XOPS_F32 || ab_dtype == XOPS_BF16 || ab_dtype == XOPS_F16,
+               "%s: a/b dtype must be fp32, bf16 or fp16", what);
+  XOPS_REQUIRE(softplus_beta > 0.f, "%s: softplus_beta must be positive", what);
+  XOPS_UNSUPPORTED((K == 128 || K == 64) && (V == 128 || V == 64),
+                   "%s: K, V must be 64 or 128 (got %lld, %lld)", what, (long long)K,
+                   (long long)V);
+  if (N == 0) return XOPS_OK;
+  XOPS_REQUIRE(A_log && a && dt_bias && q && k && v && b && o && initial_state_source &&
+                   initial_state_indices && cu_seqlens,
+               "%s: null pointer", what);
+  XOPS_REQUIRE(aligned16(initial_state_source) && aligned16(v) && aligned16(o),
+               "%s: state/v/o must be 16-byte aligned", what);
+  GateSrc gs{A_log, a, dt_bias, b, ab_dtype, softplus_beta, softplus_threshold};
+  // cu_seqlens index the flattened B*T tokens; the kernel's T only matters
+  // without cu_seqlens
+  return launch_recurrent(q, k, v, nullptr, nullptr, o, initial_state_source,
+                          initial_state_source, cu_seqlens, initial_state_indices, T, N, H, HV,
+                          K, V, HV * K * V, HV * K * V, scale, use_qk_l2norm_in_kernel != 0, gs,
+                          (cudaStream_t)stream, what);
 }

@@ -28,6 +28,10 @@ const Entry kTable[] = {
      (void*)&xops_causal_conv1d_varlen},
     {"fused_recurrent_gated_delta_rule_fwd_kernel", "xops_fused_recurrent_gated_delta_rule",
      (void*)&xops_fused_recurrent_gated_delta_rule},
+    {"fused_gdn_gating_decode_kernel", "xops_fused_gdn_gating", (void*)&xops_fused_gdn_gating},
+    {"fused_sigmoid_gating_delta_rule_update_kernel",
+     "xops_fused_sigmoid_gating_delta_rule_update",
+     (void*)&xops_fused_sigmoid_gating_delta_rule_update},
     {"chunk_local_cumsum_scalar_kernel", "xops_chunk_local_cumsum",
      (void*)&xops_chunk_local_cumsum},
     {"chunk_scaled_dot_kkt_fwd_kernel", "xops_chunk_scaled_dot_kkt_fwd",

@@ -69,6 +69,8 @@ XOPS_DECLARE_OP(ChunkForwardOOp, "chunk_fwd_kernel_o")
 XOPS_DECLARE_OP(CausalConv1dUpdateNoCacheNoMtpOp, "_causal_conv1d_update_kernel_no_cache_len_no_mtp")
 XOPS_DECLARE_OP(CausalConv1dUpdateQwenDecodeOp, "_causal_conv1d_update_qwen_decode_kernel")
 XOPS_DECLARE_OP(CausalConv1dUpdateTiledV2Op, "_causal_conv1d_update_kernel_npu_tiled_v2")
+XOPS_DECLARE_OP(FusedGdnGatingOp, "fused_gdn_gating_decode_kernel")
+XOPS_DECLARE_OP(FusedSigmoidGatingDeltaRuleUpdateOp, "fused_sigmoid_gating_delta_rule_update_kernel")
 #undef XOPS_DECLARE_OP
 
 class SplitRmsnormRopeOp final : public OperationBase {
@@ -114,6 +116,13 @@ class OperationFactory {
   }
   CausalConv1dUpdateTiledV2Op& causal_conv1d_update_tiled_v2() {
     return get<CausalConv1dUpdateTiledV2Op>("_causal_conv1d_update_kernel_npu_tiled_v2");
+  }
+  FusedGdnGatingOp& fused_gdn_gating() {
+    return get<FusedGdnGatingOp>("fused_gdn_gating_decode_kernel");
+  }
+  FusedSigmoidGatingDeltaRuleUpdateOp& fused_sigmoid_gating_delta_rule_update() {
+    return get<FusedSigmoidGatingDeltaRuleUpdateOp>(
+        "fused_sigmoid_gating_delta_rule_update_kernel");
   }
   SplitRmsnormRopeOp& split_rmsnorm_rope(const std::string& kernel_name) {
     std::lock_guard<std::mutex> g(mu_);

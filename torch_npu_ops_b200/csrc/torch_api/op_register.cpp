@@ -81,6 +81,27 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale") = py::none(), py::arg("initial_state") = py::none(),
         py::arg("inplace_final_state") = true, py::arg("cu_seqlens") = py::none(),
         py::arg("ssm_state_indices") = py::none(), py::arg("use_qk_l2norm_in_kernel") = false);
+  m.def("npu_fused_gdn_gating",
+        [](torch::Tensor A_log, torch::Tensor a, torch::Tensor b, torch::Tensor dt_bias,
+           float beta, float threshold) {
+          return xn::npu_fused_gdn_gating(A_log, a, b, dt_bias, beta, threshold);
+        },
+        py::arg("A_log"), py::arg("a"), py::arg("b"), py::arg("dt_bias"), py::arg("beta") = 1.0f,
+        py::arg("threshold") = 20.0f);
+  m.def("npu_fused_sigmoid_gating_delta_rule_update",
+        [](torch::Tensor A_log, torch::Tensor a, torch::Tensor dt_bias, torch::Tensor q,
+           torch::Tensor k, torch::Tensor v, torch::Tensor b, torch::Tensor h0,
+           torch::Tensor idx, torch::Tensor cu, std::optional<float> scale, bool l2,
+           float sp_beta, float sp_thr) {
+          return xn::npu_fused_sigmoid_gating_delta_rule_update(A_log, a, dt_bias, q, k, v, b,
+                                                                h0, idx, cu, scale, l2, sp_beta,
+                                                                sp_thr);
+        },
+        py::arg("A_log"), py::arg("a"), py::arg("dt_bias"), py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("b"), py::arg("initial_state_source"),
+        py::arg("initial_state_indices"), py::arg("cu_seqlens"), py::arg("scale") = py::none(),
+        py::arg("use_qk_l2norm_in_kernel") = false, py::arg("softplus_beta") = 1.0f,
+        py::arg("softplus_threshold") = 20.0f);
   m.def("npu_chunk_gated_delta_rule",
         [](torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
            std::optional<float> scale, std::optional<torch::Tensor> h0, bool out_final,

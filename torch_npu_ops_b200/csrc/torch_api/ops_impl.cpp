@@ -171,11 +171,32 @@ void rope_inplace(torch::Tensor&, torch::Tensor&, torch::Tensor&, uint32_t) {
   TORCH_CHECK(false, "rope_inplace is not part of this build (out of the GDN hot path)");
 }
 
-std::pair<torch::Tensor, torch::Tensor> npu_fused_gdn_gating(torch::Tensor&, torch::Tensor&,
-                                                             torch::Tensor&, torch::Tensor&,
-                                                             float, float) {
-  TORCH_CHECK(false, "npu_fused_gdn_gating is not part of this build");
-  return {};
+std::pair<torch::Tensor, torch::Tensor> npu_fused_gdn_gating(torch::Tensor& A_log,
+                                                             torch::Tensor& a, torch::Tensor& b,
+                                                             torch::Tensor& dt_bias, float beta,
+                                                             float threshold) {
+  for (auto* t : {&A_log, &a, &b, &dt_bias}) {
+    TORCH_CHECK(t->defined(), "gating tensor is not defined");
+    TORCH_CHECK(t->is_contiguous(), "gating tensors must be contiguous");
+    on_cuda(*t, "gating tensor");
+  }
+  TORCH_CHECK(A_log.scalar_type() == torch::kFloat32, "A_log must be float32");
+  TORCH_CHECK(dt_bias.scalar_type() == torch::kFloat32, "dt_bias must be float32");
+  TORCH_CHECK(A_log.dim() == 1, "A_log must be 1D tensor");
+  TORCH_CHECK(a.dim() == 2, "a must be 2D tensor (batch, num_heads)");
+  TORCH_CHECK(b.dim() == 2, "b must be 2D tensor (batch, num_heads)");
+  TORCH_CHECK(dt_bias.dim() == 1, "dt_bias must be 1D tensor");
+  const int64_t batch = a.size(0), heads = a.size(1);
+  TORCH_CHECK(b.sizes() == a.sizes(), "a and b must have the same shape");
+  TORCH_CHECK(A_log.numel() == heads && dt_bias.numel() == heads,
+              "A_log and dt_bias must have num_heads elements");
+  auto g = torch::empty({1, batch, heads}, a.options().dtype(torch::kFloat32));
+  auto beta_output = torch::empty({1, batch, heads}, b.options());
+  ok(xops_fused_gdn_gating(PT<float>(A_log), P(a), P(b), PT<float>(dt_bias), PT<float>(g),
+                           P(beta_output), batch, heads, dtype_code(a), dtype_code(b), beta,
+                           threshold, stream_of(a)),
+     "npu_fused_gdn_gating");
+  return {g, beta_output};
 }
 
 std::pair<torch::Tensor, torch::Tensor> npu_fused_recurrent_gated_delta_rule(
@@ -219,11 +240,65 @@ std::pair<torch::Tensor, torch::Tensor> npu_fused_recurrent_gated_delta_rule(
 }
 
 torch::Tensor npu_fused_sigmoid_gating_delta_rule_update(
-    torch::Tensor&, torch::Tensor&, torch::Tensor&, torch::Tensor&, torch::Tensor&,
-    torch::Tensor&, torch::Tensor&, torch::Tensor&, torch::Tensor&, torch::Tensor&,
-    const std::optional<float>&, bool, float, float) {
-  TORCH_CHECK(false, "npu_fused_sigmoid_gating_delta_rule_update is not part of this build");
-  return {};
+    torch::Tensor& A_log, torch::Tensor& a, torch::Tensor& dt_bias, torch::Tensor& q,
+    torch::Tensor& k, torch::Tensor& v, torch::Tensor& b, torch::Tensor& initial_state_source,
+    torch::Tensor& initial_state_indices, torch::Tensor& cu_seqlens,
+    const std::optional<float>& scale, bool use_qk_l2norm_in_kernel, float softplus_beta,
+    float softplus_threshold) {
+  const std::pair<const char*, torch::Tensor*> named[] = {
+      {"A_log", &A_log}, {"a", &a}, {"dt_bias", &dt_bias}, {"q", &q}, {"k", &k}, {"v", &v},
+      {"b", &b}, {"initial_state_source", &initial_state_source},
+      {"initial_state_indices", &initial_state_indices}, {"cu_seqlens", &cu_seqlens}};
+  for (const auto& nt : named) {
+    TORCH_CHECK(nt.second->defined(), nt.first, " must be defined");
+    TORCH_CHECK(nt.second->is_contiguous(), nt.first, " must be contiguous");
+    on_cuda(*nt.second, nt.first);
+  }
+  TORCH_CHECK(q.dim() == 4, "q must be 4D [B, T, H, K]");
+  TORCH_CHECK(k.dim() == 4, "k must be 4D [B, T, H, K]");
+  TORCH_CHECK(v.dim() == 4, "v must be 4D [B, T, HV, V]");
+  TORCH_CHECK(a.dim() == 3, "a must be 3D [B, T, HV]");
+  TORCH_CHECK(b.dim() == 3, "b must be 3D [B, T, HV]");
+  TORCH_CHECK(A_log.dim() == 1, "A_log must be 1D [HV]");
+  TORCH_CHECK(dt_bias.dim() == 1, "dt_bias must be 1D [HV]");
+  TORCH_CHECK(initial_state_source.dim() == 4,
+              "initial_state_source must be 4D [slots, HV, K, V]");
+  TORCH_CHECK(initial_state_indices.dim() == 1, "initial_state_indices must be 1D [N]");
+  TORCH_CHECK(cu_seqlens.dim() == 1, "cu_seqlens must be 1D [N + 1]");
+  const int64_t B = k.size(0), T = k.size(1), H = k.size(2), K = k.size(3);
+  const int64_t HV = v.size(2), V = v.size(3), N = cu_seqlens.numel() - 1;
+  TORCH_CHECK(q.sizes() == k.sizes(), "q/k shape mismatch");
+  TORCH_CHECK(v.size(0) == B && v.size(1) == T, "v B/T mismatch");
+  TORCH_CHECK(a.size(0) == B && a.size(1) == T && a.size(2) == HV, "a shape mismatch");
+  TORCH_CHECK(b.sizes() == a.sizes(), "a/b shape mismatch");
+  TORCH_CHECK(A_log.numel() == HV, "A_log HV mismatch");
+  TORCH_CHECK(dt_bias.numel() == HV, "dt_bias HV mismatch");
+  TORCH_CHECK(initial_state_source.size(1) == HV && initial_state_source.size(2) == K &&
+                  initial_state_source.size(3) == V,
+              "initial_state_source shape mismatch");
+  TORCH_CHECK(initial_state_indices.numel() == N,
+              "initial_state_indices size must equal cu_seqlens size - 1");
+  TORCH_CHECK(HV % H == 0, "HV must be divisible by H");
+  TORCH_CHECK(A_log.scalar_type() == torch::kFloat32, "A_log must be float32");
+  TORCH_CHECK(dt_bias.scalar_type() == torch::kFloat32, "dt_bias must be float32");
+  TORCH_CHECK(initial_state_source.scalar_type() == torch::kFloat32,
+              "initial_state_source must be float32");
+  TORCH_CHECK(initial_state_indices.scalar_type() == torch::kInt32,
+              "initial_state_indices must be int32");
+  TORCH_CHECK(cu_seqlens.scalar_type() == torch::kInt32, "cu_seqlens must be int32");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && k.scalar_type() == torch::kBFloat16 &&
+                  v.scalar_type() == torch::kBFloat16,
+              "npu_fused_sigmoid_gating_delta_rule_update expects q/k/v to be bfloat16");
+  TORCH_CHECK(a.scalar_type() == b.scalar_type(), "a and b must have the same dtype");
+  const float sc = scale.has_value() ? scale.value() : 1.0f / std::sqrt((float)K);
+  auto o = torch::empty({B, T, HV, V}, q.options());
+  ok(xops_fused_sigmoid_gating_delta_rule_update(
+         PT<float>(A_log), P(a), PT<float>(dt_bias), softplus_beta, softplus_threshold, P(q),
+         P(k), P(v), P(b), P(o), PT<float>(initial_state_source),
+         PT<int32_t>(initial_state_indices), PT<int32_t>(cu_seqlens), sc, B, T, N, H, HV, K, V,
+         dtype_code(a), use_qk_l2norm_in_kernel ? 1 : 0, stream_of(q)),
+     "npu_fused_sigmoid_gating_delta_rule_update");
+  return o;
 }
 
 std::pair<torch::Tensor, torch::Tensor> npu_chunk_gated_delta_rule(

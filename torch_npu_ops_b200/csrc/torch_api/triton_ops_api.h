@@ -46,7 +46,8 @@ torch::Tensor npu_chunk_fwd_o(const torch::Tensor& q, const torch::Tensor& k,
 void rope_inplace(torch::Tensor& x, torch::Tensor& sin, torch::Tensor& cos,
                   uint32_t rope_dim = 64);
 
-// Outside this build's scope (GDN gate pre-activation): throws.
+// GDN gates from the projections: g = -exp(A_log) softplus(a + dt_bias) fp32,
+// beta = sigmoid(b); both [1, batch, heads].
 std::pair<torch::Tensor, torch::Tensor> npu_fused_gdn_gating(torch::Tensor& A_log,
                                                              torch::Tensor& a, torch::Tensor& b,
                                                              torch::Tensor& dt_bias,
@@ -64,7 +65,8 @@ std::pair<torch::Tensor, torch::Tensor> npu_fused_recurrent_gated_delta_rule(
     const std::optional<torch::Tensor>& num_accepted_tokens = std::nullopt,
     bool use_qk_l2norm_in_kernel = false);
 
-// Outside this build's scope (gating fused into the recurrent update): throws.
+// The recurrent update with the gates computed from the projections in the
+// step; updates initial_state_source in place, returns o [B, T, HV, V].
 torch::Tensor npu_fused_sigmoid_gating_delta_rule_update(
     torch::Tensor& A_log, torch::Tensor& a, torch::Tensor& dt_bias, torch::Tensor& q,
     torch::Tensor& k, torch::Tensor& v, torch::Tensor& b, torch::Tensor& initial_state_source,

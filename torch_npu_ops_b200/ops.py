@@ -354,6 +354,94 @@ def npu_fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None, init
     return o, final
 
 
+def npu_fused_gdn_gating(A_log, a, b, dt_bias, beta=1.0, threshold=20.0):
+    """GDN gates from the projections: ``g = -exp(A_log) * softplus(a +
+    dt_bias)`` (fp32) and ``beta_output = sigmoid(b)`` (b's dtype), both
+    ``[1, batch, heads]`` (npu_triton_fused_gdn_gating.cpp:33-93)."""
+    for t, name in ((A_log, "A_log"), (a, "a"), (b, "b"), (dt_bias, "dt_bias")):
+        _check(t is not None, f"{name} tensor is not defined")
+        _check(t.is_contiguous(), f"{name} tensor must be contiguous")
+    _cuda(A_log, a, b, dt_bias)
+    _check(A_log.dtype == torch.float32, "A_log must be float32")
+    _check(dt_bias.dtype == torch.float32, "dt_bias must be float32")
+    _check(A_log.dim() == 1, "A_log must be 1D tensor")
+    _check(a.dim() == 2, "a must be 2D tensor (batch, num_heads)")
+    _check(b.dim() == 2, "b must be 2D tensor (batch, num_heads)")
+    _check(dt_bias.dim() == 1, "dt_bias must be 1D tensor")
+    batch, heads = a.shape
+    _check(b.shape == a.shape, "a and b must have the same shape")
+    _check(A_log.numel() == heads and dt_bias.numel() == heads,
+           "A_log and dt_bias must have num_heads elements")
+    g = torch.empty((1, batch, heads), dtype=torch.float32, device=a.device)
+    beta_output = torch.empty((1, batch, heads), dtype=b.dtype, device=b.device)
+    _lib.call("xops_fused_gdn_gating", A_log.data_ptr(), a.data_ptr(), b.data_ptr(),
+              dt_bias.data_ptr(), g.data_ptr(), beta_output.data_ptr(), batch, heads,
+              _dt(a, "npu_fused_gdn_gating"), _dt(b, "npu_fused_gdn_gating"), float(beta),
+              float(threshold), _stream(a))
+    return g, beta_output
+
+
+def npu_fused_sigmoid_gating_delta_rule_update(A_log, a, dt_bias, q, k, v, b,
+                                               initial_state_source, initial_state_indices,
+                                               cu_seqlens, scale=None,
+                                               use_qk_l2norm_in_kernel=False, softplus_beta=1.0,
+                                               softplus_threshold=20.0):
+    """Recurrent gated delta rule with the gates computed from the
+    projections in the step; updates ``initial_state_source`` in place (slot
+    ``initial_state_indices[n]``; a negative index starts from zeros and
+    writes nothing) and returns ``o [B, T, HV, V]``
+    (npu_triton_fused_sigmoid_gating_delta_rule_update.cpp:54-179)."""
+    named = (("A_log", A_log), ("a", a), ("dt_bias", dt_bias), ("q", q), ("k", k), ("v", v),
+             ("b", b), ("initial_state_source", initial_state_source),
+             ("initial_state_indices", initial_state_indices), ("cu_seqlens", cu_seqlens))
+    for name, t in named:
+        _check(t is not None, f"{name} must be defined")
+        _check(t.is_contiguous(), f"{name} must be contiguous")
+    _cuda(*[t for _, t in named])
+    _check(q.dim() == 4, "q must be 4D [B, T, H, K]")
+    _check(k.dim() == 4, "k must be 4D [B, T, H, K]")
+    _check(v.dim() == 4, "v must be 4D [B, T, HV, V]")
+    _check(a.dim() == 3, "a must be 3D [B, T, HV]")
+    _check(b.dim() == 3, "b must be 3D [B, T, HV]")
+    _check(A_log.dim() == 1, "A_log must be 1D [HV]")
+    _check(dt_bias.dim() == 1, "dt_bias must be 1D [HV]")
+    _check(initial_state_source.dim() == 4,
+           "initial_state_source must be 4D [slots, HV, K, V]")
+    _check(initial_state_indices.dim() == 1, "initial_state_indices must be 1D [N]")
+    _check(cu_seqlens.dim() == 1, "cu_seqlens must be 1D [N + 1]")
+    B, T, H, K = k.shape
+    HV, V = v.shape[2], v.shape[3]
+    N = cu_seqlens.numel() - 1
+    _check(q.shape == k.shape, "q/k shape mismatch")
+    _check(v.shape[0] == B and v.shape[1] == T, "v B/T mismatch")
+    _check(a.shape == (B, T, HV), "a shape mismatch")
+    _check(b.shape == a.shape, "a/b shape mismatch")
+    _check(A_log.numel() == HV, "A_log HV mismatch")
+    _check(dt_bias.numel() == HV, "dt_bias HV mismatch")
+    _check(initial_state_source.shape[1:] == (HV, K, V), "initial_state_source shape mismatch")
+    _check(initial_state_indices.numel() == N,
+           "initial_state_indices size must equal cu_seqlens size - 1")
+    _check(HV % H == 0, "HV must be divisible by H")
+    _check(A_log.dtype == torch.float32, "A_log must be float32")
+    _check(dt_bias.dtype == torch.float32, "dt_bias must be float32")
+    _check(initial_state_source.dtype == torch.float32, "initial_state_source must be float32")
+    _check(initial_state_indices.dtype == torch.int32, "initial_state_indices must be int32")
+    _check(cu_seqlens.dtype == torch.int32, "cu_seqlens must be int32")
+    _check(q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16,
+           "npu_fused_sigmoid_gating_delta_rule_update expects q/k/v to be bfloat16")
+    _check(a.dtype == b.dtype, "a and b must have the same dtype")
+    scale = float(scale) if scale is not None else 1.0 / math.sqrt(K)
+    o = torch.empty((B, T, HV, V), dtype=q.dtype, device=q.device)
+    _lib.call("xops_fused_sigmoid_gating_delta_rule_update", A_log.data_ptr(), a.data_ptr(),
+              dt_bias.data_ptr(), float(softplus_beta), float(softplus_threshold), q.data_ptr(),
+              k.data_ptr(), v.data_ptr(), b.data_ptr(), o.data_ptr(),
+              initial_state_source.data_ptr(), initial_state_indices.data_ptr(),
+              cu_seqlens.data_ptr(), scale, B, T, N, H, HV, K, V,
+              _dt(a, "npu_fused_sigmoid_gating_delta_rule_update"),
+              int(bool(use_qk_l2norm_in_kernel)), _stream(q))
+    return o
+
+
 def _token_rows(x, B):
     """x [B, T, H, D] as rows of tokens: heads and dims contiguous inside a
     token, any 16-byte aligned token stride (slices of a packed projection
