@@ -313,6 +313,14 @@ def kernel_sweep(dev, peaks):
         gb = torch.randn(rows, 32, device=dev).to(torch.bfloat16)
         add(f"fused_gdn_gating [{rows},32]",
             lambda: ops.npu_fused_gdn_gating(A_log, ga, gb, dtb), (2 + 2 + 4 + 2) * rows * 32)
+    # de-interleave of the input projections (16 -> 32 heads of 128): a decode
+    # batch and a 16,384-token prefill chunk
+    for rows in (256, 16384):
+        mq = torch.randn(rows, 16 * (256 + 512), device=dev).to(torch.bfloat16)
+        mb = torch.randn(rows, 16 * 4, device=dev).to(torch.bfloat16)
+        add(f"fused_qkvzba_split_reshape_cat [{rows}, 16->32]",
+            lambda: ops.npu_fused_qkvzba_split_reshape_cat(mq, mb, 16, 32, 128, 128),
+            2 * (mq.numel() + mb.numel()) * 2)
     # the recurrent step with in-step gates, cfg4 decode shape
     sa = torch.randn(1, 256, 32, device=dev).to(torch.bfloat16)
     sb = torch.randn(1, 256, 32, device=dev).to(torch.bfloat16)

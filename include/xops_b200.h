@@ -123,6 +123,20 @@ XOPS_API int xops_causal_conv1d_varlen(const void* x, void* conv_state, const vo
                               int64_t num_cache_lines, int silu, int32_t pad_slot_id, int dtype,
                               void* stream);
 
+/* De-interleave of the GDN input projections.  mixed_qkvz [rows, nqk *
+ * (2 hqk + 2 r hv)] holds per key head q | k | v (r heads) | z (r heads),
+ * r = num_heads_v / num_heads_qk in [1, 4]; mixed_ba [rows, nqk * 2r] holds
+ * b (r) | a (r).  Outputs: mixed_qkv [rows, 2 nqk hqk + nv hv] (all q, all
+ * k, all v), z [rows, nv, hv] in qkvz_dtype; b, a [rows, nv] in ba_dtype.
+ * All contiguous.  Replaces npu_fused_qkvzba_split_reshape_cat
+ * (triton_npu/torch_api/npu_triton_fused_qkvzba_split_reshape.cpp:105-206). */
+XOPS_API int xops_fused_qkvzba_split_reshape_cat(const void* mixed_qkvz, const void* mixed_ba,
+                                                 void* mixed_qkv, void* z, void* b, void* a,
+                                                 int64_t rows, int64_t num_heads_qk,
+                                                 int64_t num_heads_v, int64_t head_qk,
+                                                 int64_t head_v, int qkvz_dtype, int ba_dtype,
+                                                 void* stream);
+
 /* ---------------------------------------------------- gated delta rule -- */
 
 /* Token-serial gated delta rule (decode).  q, k [B, T, H, K], v [B, T, HV, V]

@@ -36,5 +36,6 @@ from .gdn import (  # noqa: F401
     fused_recurrent_gated_delta_rule,
     fused_gdn_gating,
     fused_sigmoid_gating_delta_rule_update,
+    fused_qkvzba_split_reshape_cat,
     prepare_chunk_offsets,
 )

@@ -392,3 +392,29 @@ def fused_sigmoid_gating_delta_rule_update(A_log, a, dt_bias, q, k, v, b,
         if slot >= 0:
             initial_state_source[slot].copy_(st.to(initial_state_source.dtype))
     return o.reshape(bsz, t_all, hv, vd).to(q.dtype)
+
+
+def fused_qkvzba_split_reshape_cat(mixed_qkvz, mixed_ba, num_heads_qk, num_heads_v, head_qk,
+                                   head_v):
+    """De-interleave the GDN input projections.
+
+    Restates ``fused_qkvzba_split_reshape_cat_ref``
+    (triton_npu/triton_src/test_fused_qkvzba_split_reshape.py:463-507):
+    ``mixed_qkvz [rows, nqk * (2 hqk + 2 r hv)]`` holds, per key head,
+    ``q | k | v (r heads) | z (r heads)`` and ``mixed_ba [rows, nqk * 2r]``
+    holds ``b (r) | a (r)``, r = num_heads_v / num_heads_qk.  Returns
+    ``mixed_qkv [rows, 2 nqk hqk + nv hv]`` (all q, then all k, then all v),
+    ``z [rows, nv, hv]``, ``b`` and ``a [rows, nv]``.  A pure permutation:
+    every output value is an input value.
+    """
+    rows = mixed_qkvz.shape[0]
+    r = num_heads_v // num_heads_qk
+    qkvz = mixed_qkvz.reshape(rows, num_heads_qk, 2 * head_qk + 2 * r * head_v)
+    ba = mixed_ba.reshape(rows, num_heads_qk, 2 * r)
+    q = qkvz[..., :head_qk].reshape(rows, num_heads_qk * head_qk)
+    k = qkvz[..., head_qk:2 * head_qk].reshape(rows, num_heads_qk * head_qk)
+    v = qkvz[..., 2 * head_qk:2 * head_qk + r * head_v].reshape(rows, num_heads_v * head_v)
+    z = qkvz[..., 2 * head_qk + r * head_v:].reshape(rows, num_heads_v, head_v)
+    b = ba[..., :r].reshape(rows, num_heads_v)
+    a = ba[..., r:].reshape(rows, num_heads_v)
+    return torch.cat([q, k, v], dim=-1).contiguous(), z.contiguous(), b.contiguous(), a.contiguous()

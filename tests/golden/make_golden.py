@@ -40,7 +40,8 @@ def _import_reference(ref_root):
     names = ["test_chunk_gated_delta_rule", "test_fused_recurrent_gated_delta_rule",
              "test_layernorm_fwd", "test_causal_conv1d_update",
              "test_causal_conv1d_update_v2", "test_split_rmsnorm_rope", "test_l2norm",
-             "test_fused_gdn_gating", "test_fused_sigmoid_gating_delta_rule_update"]
+             "test_fused_gdn_gating", "test_fused_sigmoid_gating_delta_rule_update",
+             "test_fused_qkvzba_split_reshape"]
     return {n: importlib.import_module(n) for n in names}
 
 
@@ -321,18 +322,40 @@ def gen_sigmoid_gating(m):
     _save("fused_sigmoid_gating_delta_rule_update", cases)
 
 
+def gen_qkvzba(m):
+    ref = m["test_fused_qkvzba_split_reshape"].fused_qkvzba_split_reshape_cat_ref
+    cases = []
+    # ratios 1..4 of the reference test (test_fused_qkvzba_split_reshape.py:518-555),
+    # at small batch, plus an fp16 projection with fp32 b/a
+    for rows, nqk, nv, hqk, hv, dt, dba in [(4, 8, 16, 128, 128, torch.bfloat16, torch.bfloat16),
+                                           (3, 4, 4, 128, 128, torch.bfloat16, torch.bfloat16),
+                                           (2, 2, 6, 128, 128, torch.bfloat16, torch.bfloat16),
+                                           (5, 2, 8, 128, 128, torch.bfloat16, torch.bfloat16),
+                                           (7, 3, 6, 64, 32, torch.float16, torch.float32)]:
+        r = nv // nqk
+        g0 = torch.Generator().manual_seed(rows * 1000 + nqk * 10 + nv)
+        mixed_qkvz = torch.randn(rows, nqk * (2 * hqk + 2 * r * hv), generator=g0).to(dt)
+        mixed_ba = torch.randn(rows, nqk * 2 * r, generator=g0).to(dba)
+        qkv, z, b, a = ref(mixed_qkvz, mixed_ba, nqk, nv, hqk, hv)
+        cases.append({"name": f"rows{rows}_qk{nqk}_v{nv}_h{hqk}x{hv}", "args": {
+            "mixed_qkvz": mixed_qkvz, "mixed_ba": mixed_ba, "num_heads_qk": nqk,
+            "num_heads_v": nv, "head_qk": hqk, "head_v": hv},
+            "out": {"mixed_qkv": qkv, "z": z, "b": b, "a": a}})
+    _save("fused_qkvzba_split_reshape_cat", cases)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref-root", default="/root/reference")
     ap.add_argument("--only", default="",
                     help="comma-separated subset of: layernorm,l2norm,rope,conv,chunk,"
-                         "recurrent,gating,sigmoid_gating")
+                         "recurrent,gating,sigmoid_gating,qkvzba")
     args = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     m = _import_reference(args.ref_root)
     gens = {"layernorm": gen_layernorm, "l2norm": gen_l2norm, "rope": gen_rope,
             "conv": gen_conv, "chunk": gen_chunk, "recurrent": gen_recurrent,
-            "gating": gen_gating, "sigmoid_gating": gen_sigmoid_gating}
+            "gating": gen_gating, "sigmoid_gating": gen_sigmoid_gating, "qkvzba": gen_qkvzba}
     for name, fn in gens.items():
         if not args.only or name in args.only.split(","):
             fn(m)

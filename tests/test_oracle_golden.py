@@ -165,6 +165,15 @@ def test_fused_sigmoid_gating_delta_rule_update(case):
         assert torch.equal(st[i], a["initial_state_source"][i])
 
 
+@pytest.mark.parametrize("case", _cases("fused_qkvzba_split_reshape_cat"), ids=lambda c: c["name"])
+def test_fused_qkvzba_split_reshape_cat(case):
+    a = case["args"]
+    outs = oracle.fused_qkvzba_split_reshape_cat(a["mixed_qkvz"], a["mixed_ba"], a["num_heads_qk"],
+                                                 a["num_heads_v"], a["head_qk"], a["head_v"])
+    for got, name in zip(outs, ("mixed_qkv", "z", "b", "a")):  # a permutation: bit-exact
+        assert torch.equal(got, case["out"][name]), name
+
+
 def test_gemma_rms_norm_definition():
     """Parity unpinned (closed CANN op): check the written-down definition on
     a hand-computed row and the rstd shape rule."""

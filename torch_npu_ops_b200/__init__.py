@@ -13,6 +13,7 @@ from .ops import (  # noqa: F401
     npu_causal_conv1d_update_v2,
     npu_fused_recurrent_gated_delta_rule,
     npu_fused_gdn_gating,
+    npu_fused_qkvzba_split_reshape_cat,
     npu_fused_sigmoid_gating_delta_rule_update,
     npu_chunk_gated_delta_rule,
     npu_chunk_local_cumsum,

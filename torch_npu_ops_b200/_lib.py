@@ -35,6 +35,8 @@ SIGNATURES = {
     "xops_fused_sigmoid_gating_delta_rule_update": [_p, _p, _p, _f, _f, _p, _p, _p, _p, _p, _p,
                                                     _p, _p, _f, _i64, _i64, _i64, _i64, _i64,
                                                     _i64, _i64, _int, _int, _p],
+    "xops_fused_qkvzba_split_reshape_cat": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
+                                            _i64, _int, _int, _p],
     "xops_fused_gdn_gating": [_p, _p, _p, _p, _p, _p, _i64, _i64, _int, _int, _f, _f, _p],
     "xops_chunk_gated_delta_rule": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _i64, _i64, _i64, _i64, _f, _int, _p, _i64, _p],

@@ -71,6 +71,10 @@ XOPS_DECLARE_OP(CausalConv1dUpdateQwenDecodeOp, "_causal_conv1d_update_qwen_deco
 XOPS_DECLARE_OP(CausalConv1dUpdateTiledV2Op, "_causal_conv1d_update_kernel_npu_tiled_v2")
 XOPS_DECLARE_OP(FusedGdnGatingOp, "fused_gdn_gating_decode_kernel")
 XOPS_DECLARE_OP(FusedSigmoidGatingDeltaRuleUpdateOp, "fused_sigmoid_gating_delta_rule_update_kernel")
+XOPS_DECLARE_OP(FusedQkvzbaSplitReshapeGqaR1Op, "fused_qkvzba_split_reshape_cat_gqa_r1_kernel")
+XOPS_DECLARE_OP(FusedQkvzbaSplitReshapeGqaR2Op, "fused_qkvzba_split_reshape_cat_gqa_r2_kernel")
+XOPS_DECLARE_OP(FusedQkvzbaSplitReshapeGqaR3Op, "fused_qkvzba_split_reshape_cat_gqa_r3_kernel")
+XOPS_DECLARE_OP(FusedQkvzbaSplitReshapeGqaR4Op, "fused_qkvzba_split_reshape_cat_gqa_r4_kernel")
 #undef XOPS_DECLARE_OP
 
 class SplitRmsnormRopeOp final : public OperationBase {
@@ -123,6 +127,18 @@ class OperationFactory {
   FusedSigmoidGatingDeltaRuleUpdateOp& fused_sigmoid_gating_delta_rule_update() {
     return get<FusedSigmoidGatingDeltaRuleUpdateOp>(
         "fused_sigmoid_gating_delta_rule_update_kernel");
+  }
+  FusedQkvzbaSplitReshapeGqaR1Op& fused_qkvzba_split_reshape_gqa_r1() {
+    return get<FusedQkvzbaSplitReshapeGqaR1Op>("fused_qkvzba_split_reshape_cat_gqa_r1_kernel");
+  }
+  FusedQkvzbaSplitReshapeGqaR2Op& fused_qkvzba_split_reshape_gqa_r2() {
+    return get<FusedQkvzbaSplitReshapeGqaR2Op>("fused_qkvzba_split_reshape_cat_gqa_r2_kernel");
+  }
+  FusedQkvzbaSplitReshapeGqaR3Op& fused_qkvzba_split_reshape_gqa_r3() {
+    return get<FusedQkvzbaSplitReshapeGqaR3Op>("fused_qkvzba_split_reshape_cat_gqa_r3_kernel");
+  }
+  FusedQkvzbaSplitReshapeGqaR4Op& fused_qkvzba_split_reshape_gqa_r4() {
+    return get<FusedQkvzbaSplitReshapeGqaR4Op>("fused_qkvzba_split_reshape_cat_gqa_r4_kernel");
   }
   SplitRmsnormRopeOp& split_rmsnorm_rope(const std::string& kernel_name) {
     std::lock_guard<std::mutex> g(mu_);

@@ -81,6 +81,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale") = py::none(), py::arg("initial_state") = py::none(),
         py::arg("inplace_final_state") = true, py::arg("cu_seqlens") = py::none(),
         py::arg("ssm_state_indices") = py::none(), py::arg("use_qk_l2norm_in_kernel") = false);
+  m.def("npu_fused_qkvzba_split_reshape_cat",
+        [](torch::Tensor qkvz, torch::Tensor ba, int32_t nqk, int32_t nv, int32_t hqk,
+           int32_t hv) { return xn::npu_fused_qkvzba_split_reshape_cat(qkvz, ba, nqk, nv, hqk, hv); },
+        py::arg("mixed_qkvz"), py::arg("mixed_ba"), py::arg("num_heads_qk"),
+        py::arg("num_heads_v"), py::arg("head_qk"), py::arg("head_v"));
   m.def("npu_fused_gdn_gating",
         [](torch::Tensor A_log, torch::Tensor a, torch::Tensor b, torch::Tensor dt_bias,
            float beta, float threshold) {

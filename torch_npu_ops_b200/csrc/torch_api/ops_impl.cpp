@@ -524,10 +524,32 @@ torch::Tensor npu_causal_conv1d_update_v2(
 }
 
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor>
-npu_fused_qkvzba_split_reshape_cat(torch::Tensor&, torch::Tensor&, int32_t, int32_t, int32_t,
-                                   int32_t) {
-  TORCH_CHECK(false, "npu_fused_qkvzba_split_reshape_cat is not part of this build");
-  return {};
+npu_fused_qkvzba_split_reshape_cat(torch::Tensor& mixed_qkvz, torch::Tensor& mixed_ba,
+                                   int32_t num_heads_qk, int32_t num_heads_v, int32_t head_qk,
+                                   int32_t head_v) {
+  on_cuda(mixed_qkvz, "mixed_qkvz");
+  on_cuda(mixed_ba, "mixed_ba");
+  TORCH_CHECK(num_heads_qk > 0, "num_heads_qk must be positive");
+  const int64_t rows = mixed_qkvz.size(0);
+  const int32_t r = num_heads_v / num_heads_qk;
+  TORCH_CHECK(r >= 1 && r <= 4,
+              "npu_fused_qkvzba_split_reshape_cat only supports v_heads_per_qk in [1, 4], but got ",
+              r, " for num_heads_qk=", num_heads_qk, " num_heads_v=", num_heads_v);
+  auto qkvz = mixed_qkvz.contiguous();
+  auto ba = mixed_ba.contiguous();
+  TORCH_CHECK(qkvz.numel() == rows * num_heads_qk * (2 * head_qk + 2 * r * head_v) &&
+                  ba.numel() == rows * num_heads_qk * 2 * r,
+              "npu_fused_qkvzba_split_reshape_cat: projection widths do not match the head counts");
+  auto qkv = torch::empty({rows, (int64_t)2 * num_heads_qk * head_qk + (int64_t)num_heads_v * head_v},
+                          qkvz.options());
+  auto z = torch::empty({rows, (int64_t)num_heads_v, (int64_t)head_v}, qkvz.options());
+  auto b = torch::empty({rows, (int64_t)num_heads_v}, ba.options());
+  auto a = torch::empty({rows, (int64_t)num_heads_v}, ba.options());
+  ok(xops_fused_qkvzba_split_reshape_cat(P(qkvz), P(ba), P(qkv), P(z), P(b), P(a), rows,
+                                         num_heads_qk, num_heads_v, head_qk, head_v,
+                                         dtype_code(qkvz), dtype_code(ba), stream_of(qkvz)),
+     "npu_fused_qkvzba_split_reshape_cat");
+  return {qkv, z, b, a};
 }
 
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> npu_split_rmsnorm_rope(

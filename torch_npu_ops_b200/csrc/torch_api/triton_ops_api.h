@@ -117,7 +117,7 @@ torch::Tensor npu_causal_conv1d_update_v2(
     bool validate_data = false,
     const std::optional<torch::Tensor>& num_accepted_tokens = std::nullopt);
 
-// Outside this build's scope (in_proj de-interleave): throws.
+// De-interleave of the GDN input projections -> (mixed_qkv, z [rows, nv, hv], b, a).
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor, torch::Tensor>
 npu_fused_qkvzba_split_reshape_cat(torch::Tensor& mixed_qkvz, torch::Tensor& mixed_ba,
                                    int32_t num_heads_qk, int32_t num_heads_v, int32_t head_qk,

@@ -354,6 +354,33 @@ def npu_fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None, init
     return o, final
 
 
+def npu_fused_qkvzba_split_reshape_cat(mixed_qkvz, mixed_ba, num_heads_qk, num_heads_v,
+                                       head_qk, head_v):
+    """De-interleave the GDN input projections into ``(mixed_qkv [rows,
+    2 nqk hqk + nv hv], z [rows, nv, hv], b [rows, nv], a [rows, nv])``
+    (npu_triton_fused_qkvzba_split_reshape.cpp:105-206)."""
+    _cuda(mixed_qkvz, mixed_ba)
+    rows = mixed_qkvz.shape[0]
+    r = num_heads_v // num_heads_qk
+    _check(1 <= r <= 4, "npu_fused_qkvzba_split_reshape_cat only supports v_heads_per_qk in "
+           f"[1, 4], but got {r} for num_heads_qk={num_heads_qk} num_heads_v={num_heads_v}")
+    qkvz = mixed_qkvz.contiguous()
+    ba = mixed_ba.contiguous()
+    _check(qkvz.numel() == rows * num_heads_qk * (2 * head_qk + 2 * r * head_v)
+           and ba.numel() == rows * num_heads_qk * 2 * r,
+           "npu_fused_qkvzba_split_reshape_cat: projection widths do not match the head counts")
+    qkv = torch.empty((rows, 2 * num_heads_qk * head_qk + num_heads_v * head_v),
+                      dtype=qkvz.dtype, device=qkvz.device)
+    z = torch.empty((rows, num_heads_v, head_v), dtype=qkvz.dtype, device=qkvz.device)
+    b = torch.empty((rows, num_heads_v), dtype=ba.dtype, device=ba.device)
+    a = torch.empty((rows, num_heads_v), dtype=ba.dtype, device=ba.device)
+    _lib.call("xops_fused_qkvzba_split_reshape_cat", qkvz.data_ptr(), ba.data_ptr(),
+              qkv.data_ptr(), z.data_ptr(), b.data_ptr(), a.data_ptr(), rows, num_heads_qk,
+              num_heads_v, head_qk, head_v, _dt(qkvz, "npu_fused_qkvzba_split_reshape_cat"),
+              _dt(ba, "npu_fused_qkvzba_split_reshape_cat"), _stream(qkvz))
+    return qkv, z, b, a
+
+
 def npu_fused_gdn_gating(A_log, a, b, dt_bias, beta=1.0, threshold=20.0):
     """GDN gates from the projections: ``g = -exp(A_log) * softplus(a +
     dt_bias)`` (fp32) and ``beta_output = sigmoid(b)`` (b's dtype), both
