@@ -141,19 +141,28 @@ XOPS_API int xops_fused_qkvzba_split_reshape_cat(const void* mixed_qkvz, const v
 
 /* Token-serial gated delta rule (decode).  q, k [B, T, H, K], v [B, T, HV, V]
  * bf16; g, beta [B, T, HV] fp32 (beta may be NULL = ones); o [B, T, HV, V]
- * bf16; h0 fp32 state slots [*, HV, K, V] with slot stride h0_stride,
- * read from slot ssm_state_indices[n] (or n); ht == h0 updates those slots
- * in place, any other ht is [N, HV, K, V] (stride ht_stride) indexed by
- * sequence.  Sequences: cu_seqlens [N+1] int32, or NULL with N == B rows of
- * T tokens.  ssm_state_indices [N] int32 or NULL (slot n); a negative
- * index starts the sequence from a zero state and, in place, writes nothing
- * back.  K, V in {64, 128}.  Replaces npu_fused_recurrent_gated_delta_rule
+ * bf16; h0 fp32 state slots [*, HV, K, V] with slot stride h0_stride.
+ * Sequences: cu_seqlens [N+1] int32, or NULL with N == B rows of T tokens.
+ * State slots: ssm_state_indices NULL (slot n), or an int32 table whose
+ * entry for (sequence n, token t) is at n * idx_stride_seq + t *
+ * idx_stride_tok (idx_stride_tok == 0: one slot per sequence).  The initial
+ * state comes from token 0, or from token num_accepted_tokens[n] - 1 when
+ * num_accepted_tokens [N] int32 is given (speculative decoding).  ht == h0
+ * updates in place: with a per-token table (idx_stride_tok != 0) or under
+ * speculative decoding the state after every token t goes to slot (n, t),
+ * otherwise the final state goes back to the initial slot.  Any other ht is
+ * [N, HV, K, V] (stride ht_stride) indexed by sequence (speculative
+ * decoding still stores per token, into ht's slots).  A negative slot reads
+ * as a zero state and is never written.  K, V in {64, 128}.  Replaces
+ * npu_fused_recurrent_gated_delta_rule
  * (triton_npu/torch_api/npu_triton_recurrent_gated_delta_rule.cpp:54-246). */
 XOPS_API int xops_fused_recurrent_gated_delta_rule(const void* q, const void* k, const void* v,
                                           const float* g, const float* beta, void* o,
                                           const float* h0, float* ht,
                                           const int32_t* cu_seqlens,
-                                          const int32_t* ssm_state_indices, int64_t B,
+                                          const int32_t* ssm_state_indices,
+                                          int64_t idx_stride_seq, int64_t idx_stride_tok,
+                                          const int32_t* num_accepted_tokens, int64_t B,
                                           int64_t T, int64_t N, int64_t H, int64_t HV,
                                           int64_t K, int64_t V, int64_t h0_stride,
                                           int64_t ht_stride, float scale,

@@ -274,20 +274,26 @@ def chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None,
 def fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None,
                                      initial_state=None, inplace_final_state=True,
                                      cu_seqlens=None, ssm_state_indices=None,
-                                     use_qk_l2norm_in_kernel=False):
-    """Token-serial gated delta rule (decode).
+                                     use_qk_l2norm_in_kernel=False, num_accepted_tokens=None):
+    """Token-serial gated delta rule (decode), plain and speculative.
 
     Restates ``recurrent_gated_delta_rule_ref``
     (triton_npu/triton_src/test_fused_recurrent_gated_delta_rule.py:584-617)
     with the state addressing of ``fused_recurrent_gated_delta_rule_fwd_kernel``
-    (same file :31-190): per token ``S *= e^g; v' = beta (v - S^T k);
-    S += k v'^T; o = scale * S^T q``; the in-kernel L2 norm is
-    ``x / sqrt(sum(x^2) + 1e-6)`` (:125-127).  With ``ssm_state_indices``
-    sequence n reads its initial state from slot ``indices[n]``; with
-    ``inplace_final_state`` the final state is written back to that same
-    slot of ``initial_state`` (which is modified in place), otherwise into a
-    new ``[N, HV, K, V]`` tensor.  Returns ``(o [B, T, HV, V] in v's dtype,
-    final_state)``.
+    (same file :31-178) and ``..._spec_fwd_kernel`` (:193-307): per token
+    ``S *= e^g; v' = beta (v - S^T k); S += k v'^T; o = scale * S^T q``; the
+    in-kernel L2 norm is ``x / sqrt(sum(x^2) + 1e-6)`` (:125-127).
+
+    State slots: ``ssm_state_indices`` None (slot n), ``[N]`` (one slot per
+    sequence) or ``[N, T]`` (one per token).  The initial state is the slot
+    of token 0, or of token ``num_accepted_tokens[n] - 1`` under speculative
+    decoding (where a ``[N]`` table is read as the flat table the reference
+    kernel addresses with token stride 1).  Under speculative decoding, or
+    in place with a ``[N, T]`` table, the state after every token t is
+    written to slot (n, t); otherwise the final state goes back to the
+    initial slot (in place) or to row n of a new ``[N, HV, K, V]`` tensor.
+    A negative slot reads as zeros and is never written.  Returns
+    ``(o [B, T, HV, V] in v's dtype, final_state)``.
     """
     bsz, t_all, hq, kd = q.shape
     hv, vd = v.shape[2], v.shape[3]
@@ -301,22 +307,40 @@ def fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None,
     vf, gf = v.to(torch.float32), g.to(torch.float32)
     bf = beta.to(torch.float32) if beta is not None else torch.ones_like(gf)
     spans = _spans(bsz, t_all, cu_seqlens)
+    spec = num_accepted_tokens is not None
+    idx = None if ssm_state_indices is None else ssm_state_indices.to(torch.int64)
+    flat = None if idx is None else idx.reshape(-1)
+    if idx is not None:
+        s_seq = idx.shape[1] if idx.dim() == 2 else 1
+        s_tok = 1 if (idx.dim() == 2 or spec) else 0
+    per_token = spec or (idx is not None and idx.dim() == 2 and inplace_final_state)
     o = torch.zeros(bsz, t_all, hv, vd, dtype=torch.float32)
-    final = None if inplace_final_state else torch.empty(
+    target = initial_state if inplace_final_state else torch.zeros(
         len(spans), hv, kd, vd, dtype=initial_state.dtype)
     for n, (b, s, e) in enumerate(spans):
-        slot = n if ssm_state_indices is None else int(ssm_state_indices.reshape(-1)[n])
-        st = initial_state[slot].to(torch.float32).clone()
+        if per_token and e == s:
+            continue
+        i0 = int(num_accepted_tokens.reshape(-1)[n]) - 1 if spec else 0
+        slot = n if idx is None else int(flat[n * s_seq + i0 * s_tok])
+        st = (initial_state[slot].to(torch.float32).clone() if slot >= 0
+              else torch.zeros(hv, kd, vd))
         for t in range(s, e):
             st = st * torch.exp(gf[b, t])[:, None, None]
             vn = (vf[b, t] - torch.einsum("hk,hkv->hv", kf[b, t], st)) * bf[b, t][:, None]
             st = st + kf[b, t][:, :, None] * vn[:, None, :]
             o[b, t] = torch.einsum("hk,hkv->hv", qf[b, t], st)
+            if per_token:
+                ts = int(flat[n * s_seq + (t - s) * s_tok])
+                if ts >= 0:
+                    target[ts] = st.to(target.dtype)
+        if per_token:
+            continue
         if inplace_final_state:
-            initial_state[slot].copy_(st.to(initial_state.dtype))
+            if slot >= 0:
+                initial_state[slot].copy_(st.to(initial_state.dtype))
         else:
-            final[n] = st.to(final.dtype)
-    return o.to(v.dtype), (initial_state if inplace_final_state else final)
+            target[n] = st.to(target.dtype)
+    return o.to(v.dtype), target
 
 
 def _softplus(x, beta=1.0, threshold=20.0):

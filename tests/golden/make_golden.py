@@ -270,6 +270,54 @@ def gen_recurrent(m):
     _save("fused_recurrent_gated_delta_rule", cases)
 
 
+def gen_recurrent_spec(m):
+    """Speculative decoding: initial state from the accepted token's slot,
+    every token's state stored to its own slot.  Built the way the
+    reference's spec tests build their expectation
+    (test_fused_recurrent_gated_delta_rule.py:872-983): the reference's
+    torch recurrence one token at a time from the accepted slot's state."""
+    mod = m["test_fused_recurrent_gated_delta_rule"]
+    from einops import repeat
+    cases = []
+    for name, (N, T, H, HV, D, slots, idx, acc) in {
+        "accepted_offsets": (3, 4, 1, 2, 64, 27,
+                             [[2, 4, 6, 8], [11, 13, 15, 17], [20, 22, 24, 26]], [1, 2, 3]),
+        "all_first": (2, 3, 1, 2, 64, 6, [[0, 1, 2], [3, 4, 5]], [1, 1]),
+    }.items():
+        torch.manual_seed(44)
+        q = torch.randn(N, T, H, D, dtype=torch.bfloat16)
+        k = torch.randn(N, T, H, D, dtype=torch.bfloat16)
+        v = torch.randn(N, T, HV, D, dtype=torch.bfloat16)
+        beta = torch.rand(N, T, HV, dtype=torch.bfloat16).sigmoid()
+        g = F.logsigmoid(torch.rand(N, T, HV, dtype=torch.float32))
+        h0 = torch.randn(slots, HV, D, D, dtype=torch.float32)
+        idx_t = torch.tensor(idx, dtype=torch.int32)
+        acc_t = torch.tensor(acc, dtype=torch.int32)
+        outs, states = [], []
+        for n in range(N):
+            h = h0[int(idx_t[n, acc[n] - 1])].unsqueeze(0)
+            qn = F.normalize(repeat(q[n:n + 1], "b t h d -> b t (h g) d", g=HV // H), p=2,
+                             dim=-1, eps=1e-6).to(torch.bfloat16)
+            kn = F.normalize(repeat(k[n:n + 1], "b t h d -> b t (h g) d", g=HV // H), p=2,
+                             dim=-1, eps=1e-6).to(torch.bfloat16)
+            for t in range(T):
+                o_t, h = mod.recurrent_gated_delta_rule_ref(
+                    q=qn[:, t:t + 1], k=kn[:, t:t + 1], v=v[n:n + 1, t:t + 1],
+                    beta=beta[n:n + 1, t:t + 1], g=g[n:n + 1, t:t + 1], scale=0.5,
+                    initial_state=h, output_final_state=True)
+                outs.append(o_t)
+                states.append(h.squeeze(0))
+        cases.append({"name": name, "args": {
+            "q": q.reshape(1, N * T, H, D), "k": k.reshape(1, N * T, H, D),
+            "v": v.reshape(1, N * T, HV, D), "g": g.reshape(1, N * T, HV),
+            "beta": beta.reshape(1, N * T, HV), "scale": 0.5, "initial_state": h0,
+            "cu_seqlens": torch.arange(N + 1, dtype=torch.int32) * T,
+            "ssm_state_indices": idx_t, "num_accepted_tokens": acc_t,
+            "use_qk_l2norm_in_kernel": True},
+            "out": {"o": torch.cat(outs, 1), "token_states": torch.stack(states, 0)}})
+    _save("fused_recurrent_spec", cases)
+
+
 def gen_gating(m):
     ref = m["test_fused_gdn_gating"].torch_fused_gdn_gating
     cases = []
@@ -349,13 +397,14 @@ def main():
     ap.add_argument("--ref-root", default="/root/reference")
     ap.add_argument("--only", default="",
                     help="comma-separated subset of: layernorm,l2norm,rope,conv,chunk,"
-                         "recurrent,gating,sigmoid_gating,qkvzba")
+                         "recurrent,gating,sigmoid_gating,qkvzba,recurrent_spec")
     args = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     m = _import_reference(args.ref_root)
     gens = {"layernorm": gen_layernorm, "l2norm": gen_l2norm, "rope": gen_rope,
             "conv": gen_conv, "chunk": gen_chunk, "recurrent": gen_recurrent,
-            "gating": gen_gating, "sigmoid_gating": gen_sigmoid_gating, "qkvzba": gen_qkvzba}
+            "gating": gen_gating, "sigmoid_gating": gen_sigmoid_gating, "qkvzba": gen_qkvzba,
+            "recurrent_spec": gen_recurrent_spec}
     for name, fn in gens.items():
         if not args.only or name in args.only.split(","):
             fn(m)

@@ -275,3 +275,118 @@ def test_recurrent_slots_not_inplace_multitoken():
                                                        False, cu, slots, True)
     assert_bf16(o, ro)
     assert_state(fin, rfin)
+
+
+# ------------------------------------------------------ speculative decoding
+@pytest.mark.parametrize("case", golden("fused_recurrent_spec"), ids=lambda c: c["name"])
+def test_recurrent_spec_golden(case):
+    a = case["args"]
+    st = a["initial_state"].clone().to(DEV)
+    o, ht = ops.npu_fused_recurrent_gated_delta_rule(
+        _to(a["q"]), _to(a["k"]), _to(a["v"]), _to(a["g"]), _to(a["beta"]), a["scale"], st, True,
+        _to(a["cu_seqlens"]), _to(a["ssm_state_indices"]), _to(a["num_accepted_tokens"]),
+        a["use_qk_l2norm_in_kernel"])
+    assert ht.data_ptr() == st.data_ptr()
+    per_token = st[a["ssm_state_indices"].reshape(-1).long().to(DEV)]
+    # the reference test's bounds against its torch path
+    torch.testing.assert_close(o.cpu().float(), case["out"]["o"].reshape(o.shape).float(),
+                               rtol=5e-3, atol=1e-2)
+    torch.testing.assert_close(per_token.cpu(), case["out"]["token_states"], rtol=5e-2, atol=1e-2)
+    st_ref = a["initial_state"].clone()
+    ro, _ = oracle.fused_recurrent_gated_delta_rule(
+        a["q"], a["k"], a["v"], a["g"], a["beta"], a["scale"], st_ref, True, a["cu_seqlens"],
+        a["ssm_state_indices"], a["use_qk_l2norm_in_kernel"], a["num_accepted_tokens"])
+    assert_bf16(o, ro)
+    assert_state(st, st_ref)
+
+
+def _spec_inputs(N, T, H, HV, D, slots, seed):
+    g0 = torch.Generator().manual_seed(seed)
+    return dict(
+        q=torch.randn(1, N * T, H, D, generator=g0).to(torch.bfloat16),
+        k=torch.randn(1, N * T, H, D, generator=g0).to(torch.bfloat16),
+        v=torch.randn(1, N * T, HV, D, generator=g0).to(torch.bfloat16),
+        g=F.logsigmoid(torch.rand(1, N * T, HV, generator=g0)),
+        beta=torch.sigmoid(torch.rand(1, N * T, HV, generator=g0)),
+        h0=torch.randn(slots, HV, D, D, generator=g0))
+
+
+# the reference's spec test head pairs (test_fused_recurrent_gated_delta_rule.py:755-772)
+@pytest.mark.parametrize("H,HV", [(16, 16), (8, 8), (4, 4), (2, 2), (16, 32), (8, 16), (4, 8),
+                                  (2, 4), (16, 48), (8, 24), (4, 12), (2, 6), (16, 64), (8, 32),
+                                  (4, 16), (2, 8), (1, 8)])
+def test_recurrent_spec_shapes(H, HV):
+    N, T, D = 2, 3, 128
+    d = _spec_inputs(N, T, H, HV, D, N * T, H + HV)
+    idx = torch.arange(N * T, dtype=torch.int32).reshape(N, T)
+    acc = torch.tensor([1, 2], dtype=torch.int32)
+    cu = torch.arange(N + 1, dtype=torch.int32) * T
+    st = d["h0"].clone().to(DEV)
+    o, _ = ops.npu_fused_recurrent_gated_delta_rule(
+        _to(d["q"]), _to(d["k"]), _to(d["v"]), _to(d["g"]), _to(d["beta"]), None, st, True,
+        _to(cu), _to(idx), _to(acc), True)
+    st_ref = d["h0"].clone()
+    ro, _ = oracle.fused_recurrent_gated_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"],
+                                                    None, st_ref, True, cu, idx, True, acc)
+    assert_bf16(o, ro)
+    assert_state(st, st_ref)
+
+
+@pytest.mark.parametrize("mode", ["plain_2d_inplace", "spec_1d", "spec_not_inplace", "spec_ragged"])
+def test_recurrent_slot_tables(mode):
+    """Per-token index tables outside speculative decoding, a flat [N] table
+    under speculative decoding (read with token stride 1, as the reference
+    kernel addresses it), speculative decoding into a separate state tensor,
+    and ragged sequences with a negative (skipped) token slot."""
+    N, T, H, HV, D = 3, 2, 1, 2, 64
+    d = _spec_inputs(N, T, H, HV, D, 12, 77)
+    cu = torch.arange(N + 1, dtype=torch.int32) * T
+    acc = None
+    inplace = True
+    if mode == "plain_2d_inplace":
+        idx = torch.tensor([[3, 7], [0, 5], [9, 1]], dtype=torch.int32)
+    elif mode == "spec_1d":
+        # one-token rows: a flat [N] table under speculative decoding reads
+        # and writes entry n + t = n
+        idx = torch.tensor([4, 6, 8], dtype=torch.int32)
+        acc = torch.tensor([1, 1, 1], dtype=torch.int32)
+        cu = torch.tensor([0, 1, 2, 3], dtype=torch.int32)
+    elif mode == "spec_not_inplace":
+        # the per-token stores land in the new [N, HV, K, V] tensor; each
+        # sequence keeps to its own row so no two sequences write one slot
+        idx = torch.tensor([[0, 0], [1, 1], [2, 2]], dtype=torch.int32)
+        acc = torch.tensor([2, 1, 1], dtype=torch.int32)
+        inplace = False
+    else:
+        idx = torch.tensor([[2, -1, 4], [5, 6, 7], [8, 9, 10]], dtype=torch.int32)
+        acc = torch.tensor([1, 2, 1], dtype=torch.int32)
+        cu = torch.tensor([0, 3, 4, 6], dtype=torch.int32)
+    st = d["h0"].clone().to(DEV)
+    o, fin = ops.npu_fused_recurrent_gated_delta_rule(
+        _to(d["q"]), _to(d["k"]), _to(d["v"]), _to(d["g"]), _to(d["beta"]), 0.3, st, inplace,
+        _to(cu), _to(idx), _to(acc), True)
+    st_ref = d["h0"].clone()
+    ro, rfin = oracle.fused_recurrent_gated_delta_rule(d["q"], d["k"], d["v"], d["g"], d["beta"],
+                                                       0.3, st_ref, inplace, cu, idx, True, acc)
+    n_tok = int(cu[-1])
+    assert_bf16(o[:, :n_tok], ro[:, :n_tok])
+    assert_state(st, st_ref)
+    if not inplace:
+        assert_state(fin, rfin)
+        assert torch.equal(st.cpu(), d["h0"])
+
+
+def test_recurrent_spec_via_cpp():
+    from torch_npu_ops_b200 import _C as C
+    N, T, H, HV, D = 2, 3, 2, 4, 128
+    d = _spec_inputs(N, T, H, HV, D, N * T, 5)
+    idx = _to(torch.arange(N * T, dtype=torch.int32).reshape(N, T))
+    acc = _to(torch.tensor([2, 1], dtype=torch.int32))
+    cu = _to(torch.arange(N + 1, dtype=torch.int32) * T)
+    s1, s2 = d["h0"].clone().to(DEV), d["h0"].clone().to(DEV)
+    args = [_to(d[n]) for n in ("q", "k", "v", "g", "beta")]
+    o1, _ = C.npu_fused_recurrent_gated_delta_rule(*args, None, s1, True, cu, idx, acc, True)
+    o2, _ = ops.npu_fused_recurrent_gated_delta_rule(*args, None, s2, True, cu, idx, acc, True)
+    assert torch.equal(o1, o2) and torch.equal(s1, s2)
+    assert C.kernel_entry_point("fused_recurrent_gated_delta_rule_spec_fwd_kernel") == \
+        "xops_fused_recurrent_gated_delta_rule"

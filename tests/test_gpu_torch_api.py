@@ -48,7 +48,8 @@ def test_chunk_and_recurrent_via_cpp(C):
     a = {k: (v.to(DEV) if torch.is_tensor(v) else v) for k, v in dec.items()}
     oa, _ = C.npu_fused_recurrent_gated_delta_rule(a["q"], a["k"], a["v"], a["g"], a["beta"], None,
                                                    st1, True, a["cu_seqlens"],
-                                                   a["ssm_state_indices"], True)
+                                                   a["ssm_state_indices"],
+                                                   use_qk_l2norm_in_kernel=True)
     ob, _ = ops.npu_fused_recurrent_gated_delta_rule(a["q"], a["k"], a["v"], a["g"], a["beta"],
                                                      None, st2, True, a["cu_seqlens"],
                                                      a["ssm_state_indices"], None, True)

@@ -30,8 +30,8 @@ SIGNATURES = {
     "xops_causal_conv1d_varlen": [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int,
                                   _i32, _int, _p],
     "xops_fused_recurrent_gated_delta_rule": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64,
-                                              _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f, _int,
-                                              _p],
+                                              _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                              _i64, _f, _int, _p],
     "xops_fused_sigmoid_gating_delta_rule_update": [_p, _p, _p, _f, _f, _p, _p, _p, _p, _p, _p,
                                                     _p, _p, _f, _i64, _i64, _i64, _i64, _i64,
                                                     _i64, _i64, _int, _int, _p],

@@ -15,6 +15,13 @@
 // independent loads in flight.  The two reductions over K (S^T k and S^T q)
 // finish across the 4 warps through shared memory.
 //
+// Speculative decoding (fused_recurrent_gated_delta_rule_spec_fwd_kernel,
+// test_fused_recurrent_gated_delta_rule.py:193-307): the initial state is
+// read from slot (n, num_accepted_tokens[n] - 1) of a per-token index table
+// and the state after every token t is stored to slot (n, t); the plain
+// in-place path with a [N, T] index table stores per token the same way
+// (:124-165).
+//
 // The same kernel serves fused_sigmoid_gating_delta_rule_update
 // (triton_npu/triton_src/test_fused_sigmoid_gating_delta_rule_update.py:11-117):
 // there the gates come from the projections inside the step,
@@ -26,6 +33,19 @@
 
 namespace xops {
 namespace {
+
+// Where a sequence's states live.  idx == nullptr: slot n.  Otherwise the
+// slot of (sequence n, token t) is idx[n * stride_seq + t * stride_tok]; the
+// initial state comes from token i0 = accepted[n] - 1 (speculative decoding)
+// or 0.  per_token: the state after every token t is stored to slot (n, t)
+// (the reference's speculative / multi-token in-place path); otherwise the
+// final state is stored once.
+struct SlotSrc {
+  const int32_t* idx;
+  int64_t stride_seq, stride_tok;
+  const int32_t* accepted;
+  bool per_token;
+};
 
 // Gates computed in the step from the projections (a.a == nullptr: the
 // precomputed g / beta arrays are used instead).
@@ -55,9 +75,9 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
     const __nv_bfloat16* __restrict__ v, const float* __restrict__ g,
     const float* __restrict__ beta, __nv_bfloat16* __restrict__ o,
-    const float* h0, float* ht, const int32_t* __restrict__ cu,
-    const int32_t* __restrict__ slots, int64_t T, int64_t H, int64_t HV, int64_t h0_stride,
-    int64_t ht_stride, float scale, bool l2norm, GateSrc gs) {
+    const float* h0, float* ht, const int32_t* __restrict__ cu, SlotSrc sl, int64_t T,
+    int64_t H, int64_t HV, int64_t h0_stride, int64_t ht_stride, float scale, bool l2norm,
+    GateSrc gs) {
   constexpr int ROWS = K / 4;    // state rows per warp
   constexpr int COLS = V / 32;   // state columns per lane
   __shared__ float s_q[K], s_k[K];
@@ -76,7 +96,10 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
     bos = n * T;
     eos = bos + T;
   }
-  const int64_t slot = slots ? (int64_t)slots[n] : n;
+  if (sl.per_token && eos == bos) return;  // nothing to read back or store
+  const int64_t i0 = sl.accepted ? (int64_t)sl.accepted[n] - 1 : 0;
+  const int64_t slot =
+      sl.idx ? (int64_t)sl.idx[n * sl.stride_seq + i0 * sl.stride_tok] : n;
   const bool inplace = (const float*)ht == h0;
   // a negative slot: zero initial state, and (in place) no write-back
   const bool has_slot = slot >= 0;
@@ -84,7 +107,7 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
   // in place (ht == h0): back into the same slot; otherwise ht is indexed by
   // sequence (the reference's INPLACE_FINAL_STATE split, :169-188)
   float* hdst = ht + (inplace ? (has_slot ? slot : 0) : n) * ht_stride + (int64_t)hv * K * V;
-  const bool write_back = !inplace || has_slot;
+  const bool write_back = !sl.per_token && (!inplace || has_slot);
   const int r0 = warp * ROWS, c0 = lane * COLS;
 
   // h0 and ht may be the same buffer (in-place update): each thread reads
@@ -192,6 +215,19 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
         ov[c] = s_red[0][c0 + c] + s_red[1][c0 + c] + s_red[2][c0 + c] + s_red[3][c0 + c];
       store_vec<__nv_bfloat16, COLS>(o + (t * HV + hv) * V + c0, ov);
     }
+    if (sl.per_token) {  // the state after token t, to slot (n, t)
+      const int64_t st = sl.idx[n * sl.stride_seq + (t - bos) * sl.stride_tok];
+      if (st >= 0) {
+        float* dst = ht + st * ht_stride + (int64_t)hv * K * V;
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+          float tmp[COLS];
+#pragma unroll
+          for (int c = 0; c < COLS; ++c) tmp[c] = S[r][c];
+          store_vec<float, COLS>(dst + (int64_t)(r0 + r) * V + c0, tmp);
+        }
+      }
+    }
     __syncthreads();  // s_q/s_k/s_red reused by the next token
   }
 
@@ -207,7 +243,7 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
 
 int launch_recurrent(const void* q, const void* k, const void* v, const float* g,
                      const float* beta, void* o, const float* h0, float* ht,
-                     const int32_t* cu_seqlens, const int32_t* slots, int64_t T, int64_t N,
+                     const int32_t* cu_seqlens, SlotSrc slots, int64_t T, int64_t N,
                      int64_t H, int64_t HV, int64_t K, int64_t V, int64_t h0_stride,
                      int64_t ht_stride, float scale, bool l2, GateSrc gs, cudaStream_t st,
                      const char* what) {
@@ -236,6 +272,7 @@ using namespace xops;
 extern "C" int xops_fused_recurrent_gated_delta_rule(
     const void* q, const void* k, const void* v, const float* g, const float* beta, void* o,
     const float* h0, float* ht, const int32_t* cu_seqlens, const int32_t* ssm_state_indices,
+    int64_t idx_stride_seq, int64_t idx_stride_tok, const int32_t* num_accepted_tokens,
     int64_t B, int64_t T, int64_t N, int64_t H, int64_t HV, int64_t K, int64_t V,
     int64_t h0_stride, int64_t ht_stride, float scale, int use_qk_l2norm_in_kernel,
     void* stream) {
@@ -258,10 +295,21 @@ extern "C" int xops_fused_recurrent_gated_delta_rule(
   XOPS_REQUIRE(aligned16(h0) && aligned16(ht) && aligned16(v) && aligned16(o) &&
                    (h0_stride % 4) == 0 && (ht_stride % 4) == 0,
                "fused_recurrent_gated_delta_rule: state/v/o must be 16-byte aligned");
+  XOPS_REQUIRE(!num_accepted_tokens || (cu_seqlens && ssm_state_indices),
+               "fused_recurrent_gated_delta_rule: speculative decoding needs cu_seqlens and "
+               "ssm_state_indices");
+  XOPS_REQUIRE(!ssm_state_indices || (idx_stride_seq >= 0 && idx_stride_tok >= 0),
+               "fused_recurrent_gated_delta_rule: bad state index strides");
   GateSrc none{};
-  return launch_recurrent(q, k, v, g, beta, o, h0, ht, cu_seqlens, ssm_state_indices, T, N, H,
-                          HV, K, V, h0_stride, ht_stride, scale, use_qk_l2norm_in_kernel != 0,
-                          none, (cudaStream_t)stream, "fused_recurrent_gated_delta_rule");
+  // speculative decoding stores every token's state; so does an in-place
+  // update with a per-token index table (idx_stride_tok != 0)
+  const bool per_token = num_accepted_tokens != nullptr ||
+                         (ssm_state_indices && idx_stride_tok != 0 && (const float*)ht == h0);
+  SlotSrc sl{ssm_state_indices, ssm_state_indices ? idx_stride_seq : 0,
+             ssm_state_indices ? idx_stride_tok : 0, num_accepted_tokens, per_token};
+  return launch_recurrent(q, k, v, g, beta, o, h0, ht, cu_seqlens, sl, T, N, H, HV, K, V,
+                          h0_stride, ht_stride, scale, use_qk_l2norm_in_kernel != 0, none,
+                          (cudaStream_t)stream, "fused_recurrent_gated_delta_rule");
 }
 
 extern "C" int xops_fused_sigmoid_gating_delta_rule_update(
@@ -290,8 +338,9 @@ extern "C" int xops_fused_sigmoid_gating_delta_rule_update(
   GateSrc gs{A_log, a, dt_bias, b, ab_dtype, softplus_beta, softplus_threshold};
   // cu_seqlens index the flattened B*T tokens; the kernel's T only matters
   // without cu_seqlens
+  SlotSrc sl{initial_state_indices, 1, 0, nullptr, false};
   return launch_recurrent(q, k, v, nullptr, nullptr, o, initial_state_source,
-                          initial_state_source, cu_seqlens, initial_state_indices, T, N, H, HV,
-                          K, V, HV * K * V, HV * K * V, scale, use_qk_l2norm_in_kernel != 0, gs,
+                          initial_state_source, cu_seqlens, sl, T, N, H, HV, K, V, HV * K * V,
+                          HV * K * V, scale, use_qk_l2norm_in_kernel != 0, gs,
                           (cudaStream_t)stream, what);
 }

@@ -28,6 +28,8 @@ const Entry kTable[] = {
      (void*)&xops_causal_conv1d_varlen},
     {"fused_recurrent_gated_delta_rule_fwd_kernel", "xops_fused_recurrent_gated_delta_rule",
      (void*)&xops_fused_recurrent_gated_delta_rule},
+    {"fused_recurrent_gated_delta_rule_spec_fwd_kernel", "xops_fused_recurrent_gated_delta_rule",
+     (void*)&xops_fused_recurrent_gated_delta_rule},
     {"fused_gdn_gating_decode_kernel", "xops_fused_gdn_gating", (void*)&xops_fused_gdn_gating},
     {"fused_qkvzba_split_reshape_cat_gqa_r*", "xops_fused_qkvzba_split_reshape_cat",
      (void*)&xops_fused_qkvzba_split_reshape_cat},

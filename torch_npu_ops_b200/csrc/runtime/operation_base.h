@@ -59,6 +59,7 @@ class OperationBase {
 XOPS_DECLARE_OP(L2NormFwdOp, "l2norm_fwd_kernel2_loop")
 XOPS_DECLARE_OP(LayerNormFwdOp, "layer_norm_fwd_kernel")
 XOPS_DECLARE_OP(RecurrentGatedDeltaRuleFwdOp, "fused_recurrent_gated_delta_rule_fwd_kernel")
+XOPS_DECLARE_OP(RecurrentGatedDeltaRuleSpecFwdOp, "fused_recurrent_gated_delta_rule_spec_fwd_kernel")
 XOPS_DECLARE_OP(ChunkGatedDeltaRuleFwdHOp, "chunk_gated_delta_rule_fwd_kernel_h_blockdim64")
 XOPS_DECLARE_OP(ChunkLocalCumsumScalarOp, "chunk_local_cumsum_scalar_kernel")
 XOPS_DECLARE_OP(ChunkScaledDotKktFwdOp, "chunk_scaled_dot_kkt_fwd_kernel")
@@ -94,6 +95,9 @@ class OperationFactory {
   LayerNormFwdOp& layer_norm_fwd() { return get<LayerNormFwdOp>("layer_norm_fwd_kernel"); }
   RecurrentGatedDeltaRuleFwdOp& recurrent_gated_delta_rule_fwd() {
     return get<RecurrentGatedDeltaRuleFwdOp>("fused_recurrent_gated_delta_rule_fwd_kernel");
+  }
+  RecurrentGatedDeltaRuleSpecFwdOp& recurrent_gated_delta_rule_spec_fwd() {
+    return get<RecurrentGatedDeltaRuleSpecFwdOp>("fused_recurrent_gated_delta_rule_spec_fwd_kernel");
   }
   ChunkGatedDeltaRuleFwdHOp& chunk_gated_delta_rule_fwd_h() {
     return get<ChunkGatedDeltaRuleFwdHOp>("chunk_gated_delta_rule_fwd_kernel_h_blockdim64");

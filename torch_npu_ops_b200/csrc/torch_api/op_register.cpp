@@ -73,14 +73,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         [](torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
            std::optional<torch::Tensor> beta, std::optional<float> scale,
            std::optional<torch::Tensor> h0, bool inplace, std::optional<torch::Tensor> cu,
-           std::optional<torch::Tensor> idx, bool l2) {
+           std::optional<torch::Tensor> idx, std::optional<torch::Tensor> acc, bool l2) {
           return xn::npu_fused_recurrent_gated_delta_rule(q, k, v, g, beta, scale, h0, inplace,
-                                                          cu, idx, std::nullopt, l2);
+                                                          cu, idx, acc, l2);
         },
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("g"), py::arg("beta") = py::none(),
         py::arg("scale") = py::none(), py::arg("initial_state") = py::none(),
         py::arg("inplace_final_state") = true, py::arg("cu_seqlens") = py::none(),
-        py::arg("ssm_state_indices") = py::none(), py::arg("use_qk_l2norm_in_kernel") = false);
+        py::arg("ssm_state_indices") = py::none(), py::arg("num_accepted_tokens") = py::none(),
+        py::arg("use_qk_l2norm_in_kernel") = false);
   m.def("npu_fused_qkvzba_split_reshape_cat",
         [](torch::Tensor qkvz, torch::Tensor ba, int32_t nqk, int32_t nv, int32_t hqk,
            int32_t hv) { return xn::npu_fused_qkvzba_split_reshape_cat(qkvz, ba, nqk, nv, hqk, hv); },

@@ -206,12 +206,16 @@ std::pair<torch::Tensor, torch::Tensor> npu_fused_recurrent_gated_delta_rule(
     const std::optional<torch::Tensor>& cu_seqlens,
     const std::optional<torch::Tensor>& ssm_state_indices,
     const std::optional<torch::Tensor>& num_accepted_tokens, bool use_qk_l2norm_in_kernel) {
-  TORCH_CHECK(!num_accepted_tokens.has_value(),
-              "npu_fused_recurrent_gated_delta_rule: speculative decoding is not supported");
+  const bool spec = num_accepted_tokens.has_value();
   if (!cu_seqlens.has_value())
     TORCH_CHECK(q.size(0) == 1, "batch size is not 1 when cu_seqlens is not provided");
   TORCH_CHECK(initial_state.has_value(), "initial_state must be provided when inplace_final_state is ",
               inplace_final_state ? "true" : "false");
+  if (spec) {
+    TORCH_CHECK(cu_seqlens.has_value(), "cu_seqlens must be provided for spec decoding");
+    TORCH_CHECK(ssm_state_indices.has_value(),
+                "ssm_state_indices must be provided for spec decoding");
+  }
   on_cuda(q, "q");
   TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && k.scalar_type() == torch::kBFloat16 &&
                   v.scalar_type() == torch::kBFloat16,
@@ -223,8 +227,18 @@ std::pair<torch::Tensor, torch::Tensor> npu_fused_recurrent_gated_delta_rule(
   const float sc = scale.has_value() ? scale.value() : 1.0f / std::sqrt((float)K);
   auto cu = i32(cu_seqlens);
   const int64_t N = cu.defined() ? cu.numel() - 1 : B;
-  auto idx = i32(ssm_state_indices);
-  if (idx.defined() && idx.dim() == 2) idx = idx.select(1, 0).contiguous();
+  torch::Tensor idx;
+  int64_t ss = 0, st = 0;
+  if (ssm_state_indices.has_value()) {
+    idx = ssm_state_indices->to(torch::kInt32);
+    TORCH_CHECK(idx.dim() == 1 || idx.dim() == 2, "ssm_state_indices must be 1D or 2D");
+    TORCH_CHECK(idx.size(0) == N, "ssm_state_indices must have one row per sequence");
+    ss = idx.stride(0);
+    // a [N] table under speculative decoding is addressed like the
+    // reference's (token stride 1); otherwise one slot per sequence
+    st = idx.dim() == 2 ? idx.stride(1) : (spec ? 1 : 0);
+  }
+  auto acc = i32(num_accepted_tokens);
   auto gg = g.to(torch::kFloat32).contiguous();
   auto bb = beta.has_value() ? beta->to(torch::kFloat32).contiguous() : torch::Tensor();
   torch::Tensor final_state =
@@ -233,8 +247,9 @@ std::pair<torch::Tensor, torch::Tensor> npu_fused_recurrent_gated_delta_rule(
   auto qc = q.contiguous(), kc = k.contiguous(), vc = v.contiguous();
   ok(xops_fused_recurrent_gated_delta_rule(
          P(qc), P(kc), P(vc), PT<float>(gg), PT<float>(bb), P(o), PT<float>(h0),
-         PT<float>(final_state), PT<int32_t>(cu), PT<int32_t>(idx), B, T, N, H, HV, K, V,
-         h0.stride(0), final_state.stride(0), sc, use_qk_l2norm_in_kernel ? 1 : 0, stream_of(q)),
+         PT<float>(final_state), PT<int32_t>(cu), PT<int32_t>(idx), ss, st, PT<int32_t>(acc), B,
+         T, N, H, HV, K, V, h0.stride(0), final_state.stride(0), sc,
+         use_qk_l2norm_in_kernel ? 1 : 0, stream_of(q)),
      "npu_fused_recurrent_gated_delta_rule");
   return {o, final_state};
 }

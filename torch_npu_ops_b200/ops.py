@@ -311,16 +311,23 @@ def npu_fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None, init
                                          use_qk_l2norm_in_kernel=False):
     """Token-serial gated delta rule; returns ``(o, final_state)``
     (npu_triton_recurrent_gated_delta_rule.cpp:54-246).  ``initial_state``
-    is required; with ``inplace_final_state`` the final state is written back
-    into it (slot ``ssm_state_indices[n]`` for sequence n) and returned."""
-    _check(num_accepted_tokens is None,
-           "npu_fused_recurrent_gated_delta_rule: speculative decoding is not supported")
+    is required.  ``ssm_state_indices`` is ``[N]`` (one slot per sequence)
+    or ``[N, T]`` (one slot per token).  With ``inplace_final_state`` the
+    states go back into ``initial_state``: per token for a ``[N, T]`` table
+    or under speculative decoding (``num_accepted_tokens`` given: the initial
+    state is token ``num_accepted_tokens[n] - 1``'s slot), else the final
+    state to the sequence's slot."""
+    spec = num_accepted_tokens is not None
     if cu_seqlens is None:
         _check(q.shape[0] == 1, "batch size is not 1 when cu_seqlens is not provided")
     _check(initial_state is not None,
            "initial_state must be provided when inplace_final_state is "
            + ("true" if inplace_final_state else "false"))
-    _cuda(q, k, v, g, beta, initial_state, cu_seqlens, ssm_state_indices)
+    if spec:
+        _check(cu_seqlens is not None, "cu_seqlens must be provided for spec decoding")
+        _check(ssm_state_indices is not None,
+               "ssm_state_indices must be provided for spec decoding")
+    _cuda(q, k, v, g, beta, initial_state, cu_seqlens, ssm_state_indices, num_accepted_tokens)
     _check(q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16,
            "npu_fused_recurrent_gated_delta_rule expects q/k/v to be bfloat16")
     _check(initial_state.dtype == torch.float32, "initial_state must be float32")
@@ -332,11 +339,19 @@ def npu_fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None, init
     N = cu.numel() - 1 if cu is not None else B
     gg = g.to(torch.float32).contiguous()
     bb = beta.to(torch.float32).contiguous() if beta is not None else None
-    idx = _i32(ssm_state_indices)
+    idx = ssm_state_indices
+    ss = st = 0
     if idx is not None:
-        if idx.dim() == 2:
-            idx = idx[:, 0].contiguous()
-        _check(idx.numel() == N, "ssm_state_indices must have one slot per sequence")
+        _check(idx.dim() in (1, 2), "ssm_state_indices must be 1D or 2D")
+        idx = idx if idx.dtype == torch.int32 else idx.to(torch.int32)
+        _check(idx.shape[0] == N, "ssm_state_indices must have one row per sequence")
+        ss = idx.stride(0)
+        # a [N] table under speculative decoding is addressed like the
+        # reference's (token stride 1); otherwise one slot per sequence
+        st = idx.stride(1) if idx.dim() == 2 else (1 if spec else 0)
+    acc = _i32(num_accepted_tokens)
+    if acc is not None:
+        _check(acc.numel() == N, "num_accepted_tokens must have one entry per sequence")
     _check(initial_state.is_contiguous() or initial_state.stride(0) >= HV * K * V,
            "initial_state slots must be contiguous")
     _check(initial_state.shape[1:] == (HV, K, V), "initial_state must be [slots, HV, K, V]")
@@ -348,7 +363,7 @@ def npu_fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None, init
     qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
     _lib.call("xops_fused_recurrent_gated_delta_rule", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(),
               gg.data_ptr(), _ptr(bb), o.data_ptr(), initial_state.data_ptr(), final.data_ptr(),
-              _ptr(cu), _ptr(idx),
+              _ptr(cu), _ptr(idx), ss, st, _ptr(acc),
               B, T, N, H, HV, K, V, initial_state.stride(0), final.stride(0), scale,
               int(bool(use_qk_l2norm_in_kernel)), _stream(q))
     return o, final
