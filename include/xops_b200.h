@@ -137,6 +137,27 @@ XOPS_API int xops_fused_qkvzba_split_reshape_cat(const void* mixed_qkvz, const v
                                                  int64_t head_v, int qkvz_dtype, int ba_dtype,
                                                  void* stream);
 
+/* npu_causal_conv1d_update_v2 with slot tables: speculative decoding
+ * (num_accepted_tokens [batch]) and prefix-cache block tables
+ * (conv_state_indices [batch, *] with row stride indices_stride, plus
+ * initial_state_idx / block_idx_last_scheduled_token [batch], both or
+ * neither).  x, out [num_tokens, dim] token-major with query_start_loc
+ * [batch+1]; conv_state [num_cache_lines, dim, state_len], state_len >=
+ * width - 1, updated in place.  Sequence b reads line idx[b, init[b]]
+ * (idx[b] for a [batch] table, b without one) from column
+ * num_accepted_tokens[b] - 1 (0 without), and writes columns [0, L) of line
+ * idx[b, last[b]], L = width - 1 + (speculative ? len_b - 1 : 0).  A line
+ * equal to pad_slot_id or outside the cache skips the row.  Replaces the
+ * slot-table paths of npu_causal_conv1d_update_v2
+ * (triton_npu/torch_api/npu_triton_causal_conv1d_update_v2.cpp:99-239). */
+XOPS_API int xops_causal_conv1d_update_v2_slots(
+    const void* x, void* conv_state, const void* weight, const void* bias,
+    const int32_t* conv_state_indices, int64_t indices_stride, const int32_t* num_accepted_tokens,
+    const int32_t* initial_state_idx, const int32_t* block_idx_last_scheduled_token,
+    const int32_t* query_start_loc, void* out, int64_t batch, int64_t dim, int64_t width,
+    int64_t state_len, int64_t num_cache_lines, int silu, int32_t pad_slot_id, int dtype,
+    void* stream);
+
 /* ---------------------------------------------------- gated delta rule -- */
 
 /* Token-serial gated delta rule (decode).  q, k [B, T, H, K], v [B, T, HV, V]

@@ -24,7 +24,8 @@ NeoX RoPE of ``split_rmsnorm_rope``.
 
 from .norms import layer_norm_fwd, gemma_rms_norm, l2norm_last_dim  # noqa: F401
 from .rope import split_rmsnorm_rope  # noqa: F401
-from .conv1d import causal_conv1d_update, causal_conv1d_varlen  # noqa: F401
+from .conv1d import (  # noqa: F401
+    causal_conv1d_update, causal_conv1d_varlen, causal_conv1d_update_v2_slots)
 from .gdn import (  # noqa: F401
     chunk_local_cumsum,
     chunk_scaled_dot_kkt_fwd,

@@ -83,3 +83,57 @@ def causal_conv1d_varlen(x, conv_state, weight, bias=None, activation=True,
         cat = torch.cat([hist.to(torch.float32), xs.to(torch.float32)], dim=-1)
         conv_state[line, :, :hist_len].copy_(cat[:, cat.shape[1] - hist_len:].to(conv_state.dtype))
     return out.to(x.dtype)
+
+
+def causal_conv1d_update_v2_slots(x, conv_state, weight, bias=None, activation=True,
+                                  query_start_loc=None, conv_state_indices=None,
+                                  num_accepted_tokens=None, initial_state_idx=None,
+                                  block_idx_last_scheduled_token=None, pad_slot_id=-1):
+    """Slot-table conv (speculative decoding, prefix-cache block tables):
+    ``causal_conv1d_update_ref_v2``
+    (triton_npu/triton_src/test_causal_conv1d_update_v2.py:260-345) with each
+    sequence's window length taken from its own length (the reference takes
+    it from ``max_query_len``, which breaks for shorter sequences).
+
+    Sequence b reads line ``idx[b, initial_state_idx[b]]`` (``idx[b]`` for a
+    [B] table, b without one) and writes line ``idx[b, last[b]]``; a read
+    line equal to ``pad_slot_id`` skips it.  History = state columns
+    ``[off, off + width - 1)`` with ``off = num_accepted_tokens[b] - 1`` (0
+    without).  ``L = width - 1 + (len - 1 if speculative else 0)`` state
+    columns are rewritten: the last L columns of cat(state[off + shift :],
+    x_seq), shift = 1 (speculative) or len.  x: [T, dim] token-major;
+    conv_state [lines, dim, state_len] updated IN PLACE.
+    """
+    width = weight.shape[1]
+    out = torch.zeros(x.shape, dtype=torch.float32)
+    spec = num_accepted_tokens is not None
+    for b in range(query_start_loc.numel() - 1):
+        if conv_state_indices is None:
+            in_line = out_line = b
+        elif conv_state_indices.dim() == 1:
+            in_line = out_line = int(conv_state_indices[b])
+        else:
+            i0 = int(initial_state_idx[b]) if initial_state_idx is not None else 0
+            i1 = int(block_idx_last_scheduled_token[b]) if initial_state_idx is not None else 0
+            in_line, out_line = int(conv_state_indices[b, i0]), int(conv_state_indices[b, i1])
+        if in_line == pad_slot_id:
+            continue
+        s, e = int(query_start_loc[b]), int(query_start_loc[b + 1])
+        n = e - s
+        if n <= 0:
+            continue
+        off = int(num_accepted_tokens[b]) - 1 if spec else 0
+        L = width - 1 + (n - 1 if spec else 0)
+        xs = x[s:e].t()
+        src = conv_state[in_line].to(torch.float32)
+        y = _taps(src[:, off:off + width - 1], xs, weight, bias)
+        if activation:
+            y = F.silu(y)
+        out[s:e] = y.t()
+        if n >= L:
+            new = xs.to(torch.float32)[:, n - L:]
+        else:
+            shift = 1 if spec else n
+            new = torch.cat([src[:, off + shift:off + shift + L - n], xs.to(torch.float32)], -1)
+        conv_state[out_line, :, :L].copy_(new.to(conv_state.dtype))
+    return out.to(x.dtype)

@@ -318,6 +318,59 @@ def gen_recurrent_spec(m):
     _save("fused_recurrent_spec", cases)
 
 
+def gen_conv_slots(m):
+    """Speculative decoding and prefix-cache block tables of the v2 conv,
+    in the shapes of the reference's own tests
+    (test_causal_conv1d_update_v2.py:502-750), with equal lengths per call so
+    the reference function's max_query_len window is each sequence's own."""
+    ref = m["test_causal_conv1d_update_v2"].causal_conv1d_update_ref_v2
+    cases = []
+    g0 = torch.Generator().manual_seed(712)
+    # spec decoding, [B, D, T] rows (the reference test at :712)
+    for name, (batch, dim, width, seqlen, acc) in {
+            "spec_w4_t2": (2, 256, 4, 2, [1, 2]),
+            "spec_w3_t3": (3, 128, 3, 3, [3, 1, 2])}.items():
+        x = torch.randn(batch, dim, seqlen, generator=g0).to(torch.bfloat16)
+        st = torch.randn(batch, dim, width - 1 + seqlen - 1, generator=g0).to(torch.bfloat16)
+        w = torch.randn(dim, width, generator=g0).to(torch.bfloat16)
+        idx = torch.arange(batch, dtype=torch.int32)
+        acc_t = torch.tensor(acc, dtype=torch.int32)
+        st_ref = st.clone()
+        out = ref(x, st_ref, w, activation="silu", conv_state_indices=idx,
+                  num_accepted_tokens=acc_t)
+        cases.append({"name": name, "args": {
+            "x": x, "conv_state": st, "weight": w, "bias": None, "activation": True,
+            "conv_state_indices": idx, "num_accepted_tokens": acc_t, "query_start_loc": None,
+            "max_query_len": -1, "pad_slot_id": -1, "initial_state_idx": None,
+            "block_idx_last_scheduled_token": None},
+            "out": {"out": out, "conv_state": st_ref}})
+    # prefix-cache block tables: read one line, write another; a padded row
+    # (the reference tests at :502 and :602, equal lengths)
+    for name, (dim, width, lens, idx, last, pad) in {
+            "apc_decode": (256, 4, [1, 1, 1], [[0, 0], [1, 1], [2, 2]], [0, 0, 0], -1),
+            "apc_move_pad_w5": (128, 5, [2, 0, 2], [[0, 1], [-7, -7], [2, 3]], [1, 0, 1], -7)}.items():
+        total = sum(lens)
+        x = torch.randn(total, dim, generator=g0).to(torch.bfloat16)
+        st = torch.randn(4, dim, width - 1, generator=g0).to(torch.bfloat16)
+        w = torch.randn(dim, width, generator=g0).to(torch.bfloat16)
+        b = torch.zeros(dim).to(torch.bfloat16)
+        qsl = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+        idx_t = torch.tensor(idx, dtype=torch.int32)
+        ini = torch.zeros(len(lens), dtype=torch.int32)
+        last_t = torch.tensor(last, dtype=torch.int32)
+        st_ref = st.clone()
+        out = ref(x, st_ref, w, bias=b, activation="silu", conv_state_indices=idx_t,
+                  query_start_loc=qsl, max_query_len=max(lens), pad_slot_id=pad,
+                  block_idx_last_scheduled_token=last_t, initial_state_idx=ini)
+        cases.append({"name": name, "args": {
+            "x": x, "conv_state": st, "weight": w, "bias": b, "activation": True,
+            "conv_state_indices": idx_t, "num_accepted_tokens": None, "query_start_loc": qsl,
+            "max_query_len": max(lens), "pad_slot_id": pad, "initial_state_idx": ini,
+            "block_idx_last_scheduled_token": last_t},
+            "out": {"out": out, "conv_state": st_ref}})
+    _save("causal_conv1d_slots", cases)
+
+
 def gen_gating(m):
     ref = m["test_fused_gdn_gating"].torch_fused_gdn_gating
     cases = []
@@ -397,14 +450,14 @@ def main():
     ap.add_argument("--ref-root", default="/root/reference")
     ap.add_argument("--only", default="",
                     help="comma-separated subset of: layernorm,l2norm,rope,conv,chunk,"
-                         "recurrent,gating,sigmoid_gating,qkvzba,recurrent_spec")
+                         "recurrent,gating,sigmoid_gating,qkvzba,recurrent_spec,conv_slots")
     args = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     m = _import_reference(args.ref_root)
     gens = {"layernorm": gen_layernorm, "l2norm": gen_l2norm, "rope": gen_rope,
             "conv": gen_conv, "chunk": gen_chunk, "recurrent": gen_recurrent,
             "gating": gen_gating, "sigmoid_gating": gen_sigmoid_gating, "qkvzba": gen_qkvzba,
-            "recurrent_spec": gen_recurrent_spec}
+            "recurrent_spec": gen_recurrent_spec, "conv_slots": gen_conv_slots}
     for name, fn in gens.items():
         if not args.only or name in args.only.split(","):
             fn(m)

@@ -175,3 +175,68 @@ def test_conv_decode_pad_slot_untouched():
     ops.npu_causal_conv1d_update(x.to(DEV), st_d, wt.to(DEV), True, None,
                                  conv_state_indices=slots.to(DEV), pad_slot_id=-1)
     assert torch.equal(st_d.cpu()[1], st[1])
+
+
+# ------------------------------------- conv v2 slot tables (spec decode, APC)
+@pytest.mark.parametrize("case", golden("causal_conv1d_slots"), ids=lambda c: c["name"])
+def test_conv_slots_golden(case):
+    a = case["args"]
+    st = a["conv_state"].clone().to(DEV)
+    y = ops.npu_causal_conv1d_update_v2(
+        _to(a["x"]), st, _to(a["weight"]), a["activation"], _to(a["bias"]),
+        _to(a["conv_state_indices"]), _to(a["query_start_loc"]), a["max_query_len"],
+        a["pad_slot_id"], _to(a["block_idx_last_scheduled_token"]), _to(a["initial_state_idx"]),
+        False, _to(a["num_accepted_tokens"]))
+    assert torch.equal(st.cpu(), case["out"]["conv_state"])
+    # the reference test's own output bound (it convolves in bf16)
+    torch.testing.assert_close(y.cpu().float(), case["out"]["out"].float(), rtol=1e-2, atol=5e-2)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_conv_slots_varlen_spec(dt):
+    """Varlen speculative decoding with different lengths per sequence (each
+    sequence's window from its own length), a [B, blocks] table with
+    prefix-cache read / write blocks, and a padded row."""
+    g = torch.Generator().manual_seed(31)
+    dim, width, lens = 320, 4, [3, 1, 0, 2]
+    B = len(lens)
+    x = torch.randn(sum(lens), dim, generator=g).to(dt)
+    lines = 8
+    st = torch.randn(lines, dim, width - 1 + max(lens) - 1, generator=g).to(dt)
+    w = torch.randn(dim, width, generator=g).to(dt)
+    b = torch.randn(dim, generator=g).to(dt)
+    qsl = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    idx = torch.tensor([[1, 2, 3], [4, 5, 6], [-1, -1, -1], [7, 0, 0]], dtype=torch.int32)
+    ini = torch.tensor([0, 1, 0, 0], dtype=torch.int32)
+    last = torch.tensor([2, 1, 0, 1], dtype=torch.int32)
+    acc = torch.tensor([2, 1, 1, 3], dtype=torch.int32)
+    st_d = st.clone().to(DEV)
+    y = ops.npu_causal_conv1d_update_v2(_to(x), st_d, _to(w), True, _to(b), _to(idx), _to(qsl),
+                                        max(lens), -1, _to(last), _to(ini), False, _to(acc))
+    st_ref = st.clone()
+    ref = oracle.causal_conv1d_update_v2_slots(x, st_ref, w, b, True, qsl, idx, acc, ini, last, -1)
+    (assert_fp32 if dt == torch.float32 else assert_bf16)(y, ref)
+    assert torch.equal(st_d.cpu(), st_ref)
+
+
+def test_conv_slots_wide_state_no_spec_and_cpp():
+    """A cache wider than width - 1 without speculative decoding rewrites
+    only the first width - 1 columns; the C++ API takes the same path."""
+    from torch_npu_ops_b200 import _C as C
+    g = torch.Generator().manual_seed(32)
+    B, dim, width, T = 3, 256, 4, 2
+    x = torch.randn(B, dim, T, generator=g).to(torch.bfloat16)
+    st = torch.randn(B, dim, 6, generator=g).to(torch.bfloat16)
+    w = torch.randn(dim, width, generator=g).to(torch.bfloat16)
+    idx = torch.tensor([2, 0, 1], dtype=torch.int32)
+    s1, s2 = st.clone().to(DEV), st.clone().to(DEV)
+    y1 = ops.npu_causal_conv1d_update_v2(_to(x), s1, _to(w), True, None, _to(idx))
+    y2 = C.npu_causal_conv1d_update_v2(_to(x), s2, _to(w), True, None, _to(idx))
+    assert torch.equal(y1, y2) and torch.equal(s1, s2)
+    st_ref = st.clone()
+    xt = x.transpose(1, 2).reshape(B * T, dim)
+    qsl = torch.arange(B + 1, dtype=torch.int32) * T
+    ref = oracle.causal_conv1d_update_v2_slots(xt, st_ref, w, None, True, qsl, idx)
+    assert_bf16(y1.transpose(1, 2).reshape(B * T, dim), ref)
+    assert torch.equal(s1.cpu(), st_ref)
+    assert torch.equal(s1.cpu()[:, :, width - 1:], st[:, :, width - 1:])  # columns 3.. untouched

@@ -188,6 +188,33 @@ def test_fused_recurrent_spec(case):
     _close(per_token, case["out"]["token_states"], atol=1e-2, rtol=5e-2)
 
 
+def _conv_slots_args(a):
+    """Token-major x and query_start_loc for a [B, D, T] or varlen case."""
+    x = a["x"]
+    if a["query_start_loc"] is None:
+        b, d, t = x.shape
+        return x.transpose(1, 2).reshape(b * t, d), torch.arange(b + 1, dtype=torch.int32) * t
+    return x, a["query_start_loc"]
+
+
+@pytest.mark.parametrize("case", _cases("causal_conv1d_slots"), ids=lambda c: c["name"])
+def test_causal_conv1d_slots(case):
+    a = case["args"]
+    xt, qsl = _conv_slots_args(a)
+    st = a["conv_state"].clone()
+    out = oracle.causal_conv1d_update_v2_slots(
+        xt, st, a["weight"], a["bias"], a["activation"], qsl, a["conv_state_indices"],
+        a["num_accepted_tokens"], a["initial_state_idx"], a["block_idx_last_scheduled_token"],
+        a["pad_slot_id"])
+    ref = case["out"]["out"]
+    if a["query_start_loc"] is None:
+        b, d, t = a["x"].shape
+        ref = ref.transpose(1, 2).reshape(b * t, d)
+    # the reference convolves in bf16; the state is a copy and must match exactly
+    _close(out, ref, atol=5e-2, rtol=1e-2)
+    assert torch.equal(st, case["out"]["conv_state"])
+
+
 def test_gemma_rms_norm_definition():
     """Parity unpinned (closed CANN op): check the written-down definition on
     a hand-computed row and the rstd shape rule."""

@@ -569,6 +569,112 @@ int launch_varlen_w(int W, const void* x, void* state, const void* w, const void
   }
 }
 
+// ----------------------------------------------------------------------------
+// Slot-table path of npu_causal_conv1d_update_v2: speculative decoding and
+// prefix-cache (APC) block tables (_causal_conv1d_update_kernel_npu_tiled_v2,
+// triton_npu/triton_src/test_causal_conv1d_update_v2.py:34-233, torch
+// reference :260-345).  Per sequence b:
+//   in  = idx[b, initial_state_idx[b]]   out = idx[b, block_idx_last[b]]
+//         (a [B] table: idx[b] for both; no table: b); in == pad_slot_id skips
+//   off = num_accepted_tokens[b] - 1 (speculative) or 0
+//   L   = width - 1 + (speculative ? len - 1 : 0)   state columns rewritten
+// outputs convolve cat(state[in, :, off : off + width - 1], x_seq); the new
+// state[out, :, 0:L] is the last L of cat(state[in, :, off + shift :], x_seq)
+// with shift = 1 (speculative) or len.  L is per sequence: the reference
+// derives it from max_query_len, which for sequences shorter than that
+// rewrites only part of the window.
+// One thread per (sequence, channel); everything read from the input line is
+// read before the output line is written, so in == out is safe.
+template <typename T, int W>
+__global__ void __launch_bounds__(256) conv1d_v2_slots_kernel(
+    const T* __restrict__ x, T* conv_state, const T* __restrict__ w, const T* __restrict__ bias,
+    const int32_t* __restrict__ idx, int64_t idx_stride, const int32_t* __restrict__ accepted,
+    const int32_t* __restrict__ init_idx, const int32_t* __restrict__ last_idx,
+    const int32_t* __restrict__ qsl, T* __restrict__ out, int64_t dim, int64_t state_len,
+    int64_t num_lines, bool silu, int32_t pad_slot_id) {
+  const int64_t b = blockIdx.y;
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t in_line = b, out_line = b;
+  if (idx) {
+    const int64_t i0 = init_idx ? init_idx[b] : 0, i1 = last_idx ? last_idx[b] : 0;
+    in_line = idx[b * idx_stride + i0];
+    out_line = idx[b * idx_stride + i1];
+  }
+  // a padded row, or a line outside the cache: nothing is read or written
+  if (in_line == pad_slot_id || in_line < 0 || in_line >= num_lines || out_line < 0 ||
+      out_line >= num_lines)
+    return;
+  const int64_t qs = qsl[b], len = (int64_t)qsl[b + 1] - qs;
+  if (len <= 0 || c >= dim) return;
+  const bool spec = accepted != nullptr;
+  const int64_t off = spec ? (int64_t)accepted[b] - 1 : 0;
+  const int64_t L = (W - 1) + (spec ? len - 1 : 0);
+  const T* src = conv_state + (in_line * dim + c) * state_len;
+  T* dst = conv_state + (out_line * dim + c) * state_len;
+  auto st = [&](int64_t j) { return j >= 0 && j < state_len ? to_f32<T>(src[j]) : 0.f; };
+  float wv[W], hist[W > 1 ? W - 1 : 1], keepv[W > 2 ? W - 2 : 1];
+#pragma unroll
+  for (int j = 0; j < W; ++j) wv[j] = to_f32<T>(w[c * W + j]);
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) hist[j] = st(off + j);
+  const int64_t shift = spec ? 1 : len;
+  const int64_t keep = len < L ? L - len : 0;  // <= W - 2
+#pragma unroll
+  for (int j = 0; j < W - 2; ++j) keepv[j] = j < keep ? st(off + shift + j) : 0.f;
+  const float bsum = bias ? to_f32<T>(bias[c]) : 0.f;
+  for (int64_t t = 0; t < len; ++t) {
+    const float xv = to_f32<T>(x[(qs + t) * dim + c]);
+    float acc = bsum + xv * wv[W - 1];
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) acc = fmaf(hist[j], wv[j], acc);
+#pragma unroll
+    for (int j = 0; j + 1 < W - 1; ++j) hist[j] = hist[j + 1];
+    if (W > 1) hist[W > 1 ? W - 2 : 0] = xv;
+    out[(qs + t) * dim + c] = from_f32<T>(silu ? silu_f(acc) : acc);
+  }
+  // new window: keep carried columns, then the sequence's last tokens
+  for (int64_t j = 0; j < L && j < state_len; ++j) {
+    float v;
+    if (j < keep) {
+      v = 0.f;
+#pragma unroll
+      for (int u = 0; u < W - 2; ++u)
+        if (u == j) v = keepv[u];
+    } else {
+      v = to_f32<T>(x[(qs + len - L + j) * dim + c]);
+    }
+    dst[j] = from_f32<T>(v);
+  }
+}
+
+int launch_v2_slots(int W, const void* x, void* state, const void* w, const void* b,
+                    const int32_t* idx, int64_t idx_stride, const int32_t* accepted,
+                    const int32_t* init_idx, const int32_t* last_idx, const int32_t* qsl,
+                    void* out, int64_t batch, int64_t dim, int64_t state_len,
+                    int64_t num_lines, bool silu, int32_t pad, int dtype, cudaStream_t st) {
+  const dim3 grid((unsigned)cdiv64(dim, 256), (unsigned)batch);
+  auto run = [&](auto t) {
+    using T = decltype(t);
+    switch (W) {
+#define XOPS_V2S(WW)                                                                              \
+  case WW:                                                                                        \
+    conv1d_v2_slots_kernel<T, WW><<<grid, 256, 0, st>>>(                                          \
+        (const T*)x, (T*)state, (const T*)w, (const T*)b, idx, idx_stride, accepted, init_idx,   \
+        last_idx, qsl, (T*)out, dim, state_len, num_lines, silu, pad);                            \
+    return check_launch("causal_conv1d_update_v2(slots)");
+      XOPS_V2S(1) XOPS_V2S(2) XOPS_V2S(3) XOPS_V2S(4) XOPS_V2S(5) XOPS_V2S(6)
+#undef XOPS_V2S
+      default:
+        return set_error(XOPS_ERR_UNSUPPORTED, "causal_conv1d_update_v2: width %d", W);
+    }
+  };
+  switch (dtype) {
+    case XOPS_F32: return run(float{});
+    case XOPS_BF16: return run(__nv_bfloat16{});
+    default: return run(__half{});
+  }
+}
+
 }  // namespace
 
 int take_conv_error() {
@@ -670,4 +776,32 @@ extern "C" int xops_causal_conv1d_update(const void* x, void* conv_state, const 
     case XOPS_F16: return run(__half{});
     default: return run(float{});
   }
+}
+
+extern "C" int xops_causal_conv1d_update_v2_slots(
+    const void* x, void* conv_state, const void* weight, const void* bias,
+    const int32_t* conv_state_indices, int64_t indices_stride, const int32_t* num_accepted_tokens,
+    const int32_t* initial_state_idx, const int32_t* block_idx_last_scheduled_token,
+    const int32_t* query_start_loc, void* out, int64_t batch, int64_t dim, int64_t width,
+    int64_t state_len, int64_t num_cache_lines, int silu, int32_t pad_slot_id, int dtype,
+    void* stream) {
+  const char* what = "causal_conv1d_update_v2";
+  XOPS_REQUIRE(batch >= 0 && batch < 65536 && dim >= 1, "%s: bad shape", what);
+  XOPS_REQUIRE(width >= 1 && width <= 6, "%s expects width in [1, 6], got %lld", what,
+               (long long)width);
+  XOPS_REQUIRE(state_len >= width - 1, "%s: conv_state holds %lld columns, width %lld needs %lld",
+               what, (long long)state_len, (long long)width, (long long)(width - 1));
+  XOPS_REQUIRE((initial_state_idx == nullptr) == (block_idx_last_scheduled_token == nullptr),
+               "%s expects both APC tensors or neither.", what);
+  XOPS_REQUIRE(!initial_state_idx || conv_state_indices,
+               "%s: APC block tables need a 2D conv_state_indices", what);
+  XOPS_REQUIRE(dtype == XOPS_F32 || dtype == XOPS_BF16 || dtype == XOPS_F16, "%s: bad dtype",
+               what);
+  if (batch == 0) return XOPS_OK;
+  XOPS_REQUIRE(x && conv_state && weight && query_start_loc && out, "%s: null pointer", what);
+  return launch_v2_slots((int)width, x, conv_state, weight, bias, conv_state_indices,
+                         indices_stride, num_accepted_tokens, initial_state_idx,
+                         block_idx_last_scheduled_token, query_start_loc, out, batch, dim,
+                         state_len, num_cache_lines, silu != 0, pad_slot_id, dtype,
+                         (cudaStream_t)stream);
 }

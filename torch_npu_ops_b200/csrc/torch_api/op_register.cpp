@@ -62,13 +62,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("npu_causal_conv1d_update_v2",
         [](torch::Tensor x, torch::Tensor st, torch::Tensor w, bool act,
            std::optional<torch::Tensor> b, std::optional<torch::Tensor> idx,
-           std::optional<torch::Tensor> qsl, int32_t max_q, int32_t pad) {
-          return xn::npu_causal_conv1d_update_v2(x, st, w, act, b, idx, qsl, max_q, pad);
+           std::optional<torch::Tensor> qsl, int32_t max_q, int32_t pad,
+           std::optional<torch::Tensor> last, std::optional<torch::Tensor> init, bool validate,
+           std::optional<torch::Tensor> acc) {
+          return xn::npu_causal_conv1d_update_v2(x, st, w, act, b, idx, qsl, max_q, pad, last,
+                                                 init, validate, acc);
         },
         py::arg("x"), py::arg("conv_state"), py::arg("weight"), py::arg("activation") = true,
         py::arg("bias") = py::none(), py::arg("conv_state_indices") = py::none(),
         py::arg("query_start_loc") = py::none(), py::arg("max_query_len") = -1,
-        py::arg("pad_slot_id") = -1);
+        py::arg("pad_slot_id") = -1, py::arg("block_idx_last_scheduled_token") = py::none(),
+        py::arg("initial_state_idx") = py::none(), py::arg("validate_data") = false,
+        py::arg("num_accepted_tokens") = py::none());
   m.def("npu_fused_recurrent_gated_delta_rule",
         [](torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g,
            std::optional<torch::Tensor> beta, std::optional<float> scale,

@@ -490,8 +490,6 @@ torch::Tensor npu_causal_conv1d_update_v2(
   TORCH_CHECK(weight.dim() == 2, "causal_conv1d_update_v2 expects weight shape [dim, width].");
   TORCH_CHECK(block_idx_last_scheduled_token.has_value() == initial_state_idx.has_value(),
               "causal_conv1d_update_v2 expects both APC tensors or neither.");
-  TORCH_CHECK(!block_idx_last_scheduled_token.has_value() && !num_accepted_tokens.has_value(),
-              "causal_conv1d_update_v2: APC and speculative slot tables are not supported");
   TORCH_CHECK(conv_state.dim() == 3, "causal_conv1d_update_v2 expects conv_state shape "
                                      "[num_cache_lines, dim, state_len].");
   on_cuda(x, "x");
@@ -521,13 +519,36 @@ torch::Tensor npu_causal_conv1d_update_v2(
   TORCH_CHECK(weight.size(0) == dim, "weight dim mismatch. Expected ", dim, ", got ", weight.size(0));
   TORCH_CHECK(conv_state.size(1) == dim, "conv_state dim mismatch. Expected ", dim, ", got ",
               conv_state.size(1));
-  TORCH_CHECK(conv_state.size(2) == width - 1,
-              "causal_conv1d_update_v2: conv_state must hold exactly width - 1 history columns");
+  TORCH_CHECK(conv_state.size(2) >= width - 1,
+              "causal_conv1d_update_v2: conv_state must hold at least width - 1 history columns");
   auto b = bias.has_value() ? bias->to(xv.scalar_type()).contiguous() : torch::Tensor();
   auto idx = i32(conv_state_indices);
+  auto w = weight.contiguous();
+  const bool slots = num_accepted_tokens.has_value() || initial_state_idx.has_value() ||
+                     (idx.defined() && idx.dim() == 2 && idx.size(1) > 1) ||
+                     conv_state.size(2) != width - 1;
+  if (slots) {  // speculative decoding / prefix-cache block tables
+    if (idx.defined())
+      TORCH_CHECK((idx.dim() == 1 || idx.dim() == 2) && idx.size(0) == batch,
+                  "conv_state_indices batch mismatch. Expected ", batch, ", got ", idx.size(0));
+    auto acc = i32(num_accepted_tokens), ini = i32(initial_state_idx),
+         last = i32(block_idx_last_scheduled_token);
+    for (const auto* t : {&acc, &ini, &last})
+      TORCH_CHECK(!t->defined() || t->numel() == batch,
+                  "slot tables must have one entry per sequence");
+    auto out = torch::empty_like(xv);
+    ok(xops_causal_conv1d_update_v2_slots(
+           P(xv), P(conv_state), P(w), P(b), PT<int32_t>(idx), idx.defined() ? idx.stride(0) : 0,
+           PT<int32_t>(acc), PT<int32_t>(ini), PT<int32_t>(last), PT<int32_t>(qsl), P(out),
+           batch, dim, width, conv_state.size(2), conv_state.size(0), activation ? 1 : 0,
+           pad_slot_id, dtype_code(xv), stream_of(x)),
+       "npu_causal_conv1d_update_v2");
+    if (query_start_loc.has_value()) return out;
+    auto o3 = out.view({batch, seqlen, dim}).transpose(1, 2);
+    return unsq ? o3.squeeze(-1) : o3;
+  }
   if (idx.defined() && idx.dim() == 2) idx = idx.select(1, 0).contiguous();
   auto out = torch::empty_like(xv);
-  auto w = weight.contiguous();
   ok(xops_causal_conv1d_varlen(P(xv), P(conv_state), P(w), P(b), PT<int32_t>(qsl),
                                PT<int32_t>(idx), P(out), batch, xv.size(0), dim, width,
                                conv_state.size(0), activation ? 1 : 0, pad_slot_id,

@@ -229,18 +229,19 @@ def npu_causal_conv1d_update_v2(x, conv_state, weight, activation=True, bias=Non
     ``query_start_loc`` x is [num_tokens, dim] token-major and every
     sequence convolves over cat(conv_state history, its tokens); without it
     x is [B, D] or [B, D, T] (each row one sequence of T tokens).
-    conv_state [lines, dim, width-1] is updated IN PLACE.  The APC
-    (``block_idx_last_scheduled_token``/``initial_state_idx``) and
-    speculative (``num_accepted_tokens``) slot tables are outside this
-    build's scope and rejected."""
+    conv_state [lines, dim, state_len] is updated IN PLACE.  Speculative
+    decoding (``num_accepted_tokens``: history from column accepted - 1,
+    width - 1 + len - 1 columns rewritten) and prefix-cache block tables
+    (a [B, blocks] ``conv_state_indices`` with ``initial_state_idx`` /
+    ``block_idx_last_scheduled_token`` choosing the read and the written
+    line) run on the slot-table kernel."""
     _check(weight.dim() == 2, "causal_conv1d_update_v2 expects weight shape [dim, width].")
     _check((block_idx_last_scheduled_token is None) == (initial_state_idx is None),
            "causal_conv1d_update_v2 expects both APC tensors or neither.")
-    _check(block_idx_last_scheduled_token is None and num_accepted_tokens is None,
-           "causal_conv1d_update_v2: APC and speculative slot tables are not supported")
     _check(conv_state.dim() == 3,
            "causal_conv1d_update_v2 expects conv_state shape [num_cache_lines, dim, state_len].")
-    _cuda(x, conv_state, weight, bias, conv_state_indices, query_start_loc)
+    _cuda(x, conv_state, weight, bias, conv_state_indices, query_start_loc,
+          block_idx_last_scheduled_token, initial_state_idx, num_accepted_tokens)
     width = weight.size(1)
     _check(1 <= width <= 6, f"causal_conv1d_update_v2 expects width in [1, 6], got {width}")
     unsq = False
@@ -264,8 +265,8 @@ def npu_causal_conv1d_update_v2(x, conv_state, weight, activation=True, bias=Non
     _check(weight.size(0) == dim, f"weight dim mismatch. Expected {dim}, got {weight.size(0)}")
     _check(conv_state.size(1) == dim,
            f"conv_state dim mismatch. Expected {dim}, got {conv_state.size(1)}")
-    _check(conv_state.size(2) == width - 1,
-           "causal_conv1d_update_v2: conv_state must hold exactly width - 1 history columns")
+    _check(conv_state.size(2) >= width - 1,
+           "causal_conv1d_update_v2: conv_state must hold at least width - 1 history columns")
     _check(conv_state.is_contiguous(), "causal_conv1d_update_v2: conv_state must be contiguous")
     _check(conv_state.dtype == xv.dtype and weight.dtype == xv.dtype,
            "causal_conv1d_update_v2: x, conv_state and weight must share a dtype")
@@ -274,6 +275,29 @@ def npu_causal_conv1d_update_v2(x, conv_state, weight, activation=True, bias=Non
                "bias must have shape [dim] for causal_conv1d_update_v2.")
     b = bias.to(xv.dtype).contiguous() if bias is not None else None
     idx = _i32(conv_state_indices)
+    slots = (num_accepted_tokens is not None or initial_state_idx is not None
+             or (idx is not None and idx.dim() == 2 and idx.size(1) > 1)
+             or conv_state.size(2) != width - 1)
+    if slots:
+        if idx is not None:
+            _check(idx.dim() in (1, 2) and idx.size(0) == batch,
+                   f"conv_state_indices batch mismatch. Expected {batch}, got {idx.size(0)}")
+        acc, ini, last = (_i32(num_accepted_tokens), _i32(initial_state_idx),
+                          _i32(block_idx_last_scheduled_token))
+        for t, name in ((acc, "num_accepted_tokens"), (ini, "initial_state_idx"),
+                        (last, "block_idx_last_scheduled_token")):
+            _check(t is None or t.numel() == batch, f"{name} must have one entry per sequence")
+        out = torch.empty_like(xv)
+        _lib.call("xops_causal_conv1d_update_v2_slots", xv.data_ptr(), conv_state.data_ptr(),
+                  weight.contiguous().data_ptr(), _ptr(b), _ptr(idx),
+                  idx.stride(0) if idx is not None else 0, _ptr(acc), _ptr(ini), _ptr(last),
+                  qsl.data_ptr(), out.data_ptr(), batch, dim, width, conv_state.size(2),
+                  conv_state.size(0), int(bool(activation)), int(pad_slot_id),
+                  _dt(xv, "causal_conv1d_update_v2"), _stream(x))
+        if query_start_loc is not None:
+            return out
+        out = out.view(batch, -1, dim).transpose(1, 2)
+        return out.squeeze(-1) if unsq else out
     if idx is not None:
         if idx.dim() == 2:
             idx = idx[:, 0].contiguous()
