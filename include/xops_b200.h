@@ -94,6 +94,18 @@ XOPS_API int xops_split_rmsnorm_rope(const void* input, const void* sin, const v
                             int64_t rotary_dim, float eps, int dtype, int w_dtype,
                             int sincos_dtype, void* stream);
 
+/* Interleaved RoPE on the last rope_dim dims of x [rows, heads, hidden]
+ * (row stride x_stride_row, head stride x_stride_head, unit element
+ * stride), in place: pairs (2i, 2i+1) -> (x0 cos0 - x1 sin0, x1 cos1 +
+ * x0 sin1).  sin, cos [rows, >= rope_dim] with row stride sincos_stride,
+ * shared by a row's heads.  Replaces rope_inplace
+ * (triton_npu/torch_api/npu_triton_rope_inplace.cpp:22-66). */
+XOPS_API int xops_rope_inplace(void* x, const void* sin, const void* cos, int64_t rows,
+                               int64_t heads, int64_t hidden, int64_t rope_dim,
+                               int64_t x_stride_row, int64_t x_stride_head,
+                               int64_t sincos_stride, int x_dtype, int sincos_dtype,
+                               void* stream);
+
 /* --------------------------------------------------------------- conv1d -- */
 
 /* Decode-style depthwise causal conv update.  x [batch, dim, seqlen] with

@@ -23,7 +23,7 @@ NeoX RoPE of ``split_rmsnorm_rope``.
 """
 
 from .norms import layer_norm_fwd, gemma_rms_norm, l2norm_last_dim  # noqa: F401
-from .rope import split_rmsnorm_rope  # noqa: F401
+from .rope import split_rmsnorm_rope, rope_inplace  # noqa: F401
 from .conv1d import (  # noqa: F401
     causal_conv1d_update, causal_conv1d_varlen, causal_conv1d_update_v2_slots)
 from .gdn import (  # noqa: F401

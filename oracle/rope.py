@@ -57,3 +57,25 @@ def split_rmsnorm_rope(inp, sin, cos, q_weight, k_weight, q_hidden_size,
     ko = _neox(kn, sin, cos).reshape(t, -1)
     return qo, ko, v.clone()
 
+
+
+def rope_inplace(x, sin, cos, rope_dim=64):
+    """Interleaved (GPT-J style) RoPE on the last ``rope_dim`` dims, in place.
+
+    Restates ``rope_ref`` (triton_npu/triton_src/test_rope_inplace.py:73-98):
+    for each pair (2i, 2i+1) of the rotated tail,
+    ``out[2i] = x[2i] cos[2i] - x[2i+1] sin[2i]`` and
+    ``out[2i+1] = x[2i+1] cos[2i+1] + x[2i] sin[2i+1]``, computed in fp32 and
+    rounded to x's dtype.  x is [bsz, hidden] or [bsz, heads, hidden]; sin
+    and cos are [bsz, >= rope_dim] (one row per batch entry, shared by its
+    heads).  Modifies x and returns it.
+    """
+    x3 = x if x.dim() == 3 else x.unsqueeze(1)
+    tail = x3[..., x3.shape[-1] - rope_dim:].to(torch.float32)
+    s = sin[:, :rope_dim].to(torch.float32).unsqueeze(1)
+    c = cos[:, :rope_dim].to(torch.float32).unsqueeze(1)
+    rot = torch.empty_like(tail)
+    rot[..., 0::2] = -tail[..., 1::2]
+    rot[..., 1::2] = tail[..., 0::2]
+    x3[..., x3.shape[-1] - rope_dim:] = (tail * c + rot * s).to(x.dtype)
+    return x

@@ -41,7 +41,7 @@ def _import_reference(ref_root):
              "test_layernorm_fwd", "test_causal_conv1d_update",
              "test_causal_conv1d_update_v2", "test_split_rmsnorm_rope", "test_l2norm",
              "test_fused_gdn_gating", "test_fused_sigmoid_gating_delta_rule_update",
-             "test_fused_qkvzba_split_reshape"]
+             "test_fused_qkvzba_split_reshape", "test_rope_inplace"]
     return {n: importlib.import_module(n) for n in names}
 
 
@@ -371,6 +371,25 @@ def gen_conv_slots(m):
     _save("causal_conv1d_slots", cases)
 
 
+def gen_rope_inplace(m):
+    ref = m["test_rope_inplace"].rope_ref
+    cases = []
+    # the reference test's (batch, head) list with hidden 512, rope_dim 64
+    # (test_rope_inplace.py:100-112), plus 2D x and a 128-wide tail
+    g0 = torch.Generator().manual_seed(100)
+    for batch, head, hidden, rd in [(1, 8, 512, 64), (4, 8, 512, 64), (8, 1, 512, 64),
+                                    (4, 0, 512, 64), (3, 4, 576, 128)]:
+        shape = (batch, hidden) if head == 0 else (batch, head, hidden)
+        x = torch.randn(*shape, generator=g0).to(torch.bfloat16)
+        sin = torch.randn(batch, rd, generator=g0).to(torch.bfloat16)
+        cos = torch.randn(batch, rd, generator=g0).to(torch.bfloat16)
+        out = ref(x if head else x.unsqueeze(1), sin, cos, rd)
+        cases.append({"name": f"b{batch}_h{head}_d{hidden}_r{rd}", "args": {
+            "x": x, "sin": sin, "cos": cos, "rope_dim": rd},
+            "out": {"x": out if head else out.squeeze(1)}})
+    _save("rope_inplace", cases)
+
+
 def gen_gating(m):
     ref = m["test_fused_gdn_gating"].torch_fused_gdn_gating
     cases = []
@@ -450,14 +469,16 @@ def main():
     ap.add_argument("--ref-root", default="/root/reference")
     ap.add_argument("--only", default="",
                     help="comma-separated subset of: layernorm,l2norm,rope,conv,chunk,"
-                         "recurrent,gating,sigmoid_gating,qkvzba,recurrent_spec,conv_slots")
+                         "recurrent,gating,sigmoid_gating,qkvzba,recurrent_spec,conv_slots,"
+                         "rope_inplace")
     args = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     m = _import_reference(args.ref_root)
     gens = {"layernorm": gen_layernorm, "l2norm": gen_l2norm, "rope": gen_rope,
             "conv": gen_conv, "chunk": gen_chunk, "recurrent": gen_recurrent,
             "gating": gen_gating, "sigmoid_gating": gen_sigmoid_gating, "qkvzba": gen_qkvzba,
-            "recurrent_spec": gen_recurrent_spec, "conv_slots": gen_conv_slots}
+            "recurrent_spec": gen_recurrent_spec, "conv_slots": gen_conv_slots,
+            "rope_inplace": gen_rope_inplace}
     for name, fn in gens.items():
         if not args.only or name in args.only.split(","):
             fn(m)

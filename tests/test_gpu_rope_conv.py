@@ -240,3 +240,46 @@ def test_conv_slots_wide_state_no_spec_and_cpp():
     assert_bf16(y1.transpose(1, 2).reshape(B * T, dim), ref)
     assert torch.equal(s1.cpu(), st_ref)
     assert torch.equal(s1.cpu()[:, :, width - 1:], st[:, :, width - 1:])  # columns 3.. untouched
+
+
+# -------------------------------------------------------------- rope_inplace
+@pytest.mark.parametrize("case", golden("rope_inplace"), ids=lambda c: c["name"])
+def test_rope_inplace_golden(case):
+    a = case["args"]
+    x = a["x"].clone().to(DEV)
+    y = ops.rope_inplace(x, _to(a["sin"]), _to(a["cos"]), a["rope_dim"])
+    assert y.data_ptr() == x.data_ptr()
+    assert_bf16(x, case["out"]["x"])
+    pre = a["x"].shape[-1] - a["rope_dim"]
+    assert torch.equal(x.cpu()[..., :pre], a["x"][..., :pre])  # the head part is untouched
+
+
+@pytest.mark.parametrize("dt,sdt", [(torch.float32, torch.float32), (torch.bfloat16, torch.float32),
+                                    (torch.float16, torch.float16)])
+def test_rope_inplace_strided_views(dt, sdt):
+    """q_pe-style views: the rotated vectors are slices of a wider packed
+    tensor (row and head strides), sin / cos rows wider than rope_dim."""
+    g = torch.Generator().manual_seed(9)
+    bsz, heads, hidden, rd = 5, 3, 192, 64
+    packed = torch.randn(bsz, heads, 2 * hidden, generator=g).to(dt)
+    sin = torch.randn(bsz, 96, generator=g).to(sdt)
+    cos = torch.randn(bsz, 96, generator=g).to(sdt)
+    pd = packed.clone().to(DEV)
+    view = pd[:, :, hidden:]
+    ops.rope_inplace(view, _to(sin), _to(cos), rd)
+    ref = packed.clone()
+    oracle.rope_inplace(ref[:, :, hidden:], sin, cos, rd)
+    (assert_fp32 if dt == torch.float32 else assert_bf16)(pd, ref)
+    assert torch.equal(pd.cpu()[:, :, :hidden], packed[:, :, :hidden])
+
+
+def test_rope_inplace_cpp():
+    from torch_npu_ops_b200 import _C as C
+    g = torch.Generator().manual_seed(10)
+    x = torch.randn(4, 8, 512, generator=g).to(torch.bfloat16)
+    sin = torch.randn(4, 64, generator=g).to(torch.bfloat16)
+    cos = torch.randn(4, 64, generator=g).to(torch.bfloat16)
+    x1, x2 = x.clone().to(DEV), x.clone().to(DEV)
+    C.rope_inplace(x1, _to(sin), _to(cos), 64)
+    ops.rope_inplace(x2, _to(sin), _to(cos), 64)
+    assert torch.equal(x1, x2)

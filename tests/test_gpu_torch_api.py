@@ -78,4 +78,5 @@ def test_registry_maps_reference_kernel_names(C):
         "xops_chunk_gated_delta_rule_fwd_h"
     assert C.kernel_entry_point("layer_norm_fwd_kernel_fast_rms_bf16_z_nobias_nomask") == \
         "xops_layer_norm_fwd"
-    assert C.kernel_entry_point("rope_inplace_kernel") == ""
+    assert C.kernel_entry_point("rope_inplace_kernel") == "xops_rope_inplace"
+    assert C.kernel_entry_point("a_kernel_the_reference_does_not_have") == ""

@@ -215,6 +215,15 @@ def test_causal_conv1d_slots(case):
     assert torch.equal(st, case["out"]["conv_state"])
 
 
+@pytest.mark.parametrize("case", _cases("rope_inplace"), ids=lambda c: c["name"])
+def test_rope_inplace(case):
+    a = case["args"]
+    x = a["x"].clone()
+    out = oracle.rope_inplace(x, a["sin"], a["cos"], a["rope_dim"])
+    assert out.data_ptr() == x.data_ptr()
+    _close(x, case["out"]["x"], atol=1e-2, rtol=1e-2)  # one bf16 rounding apart at most
+
+
 def test_gemma_rms_norm_definition():
     """Parity unpinned (closed CANN op): check the written-down definition on
     a hand-computed row and the rstd shape rule."""

@@ -9,6 +9,7 @@ from .ops import (  # noqa: F401
     layer_norm_fwd_with_stats,
     npu_gemma_rms_norm,
     npu_split_rmsnorm_rope,
+    rope_inplace,
     npu_causal_conv1d_update,
     npu_causal_conv1d_update_v2,
     npu_fused_recurrent_gated_delta_rule,

@@ -25,6 +25,7 @@ SIGNATURES = {
     "xops_gemma_rms_norm": [_p, _p, _p, _p, _i64, _i64, _f, _int, _int, _p],
     "xops_split_rmsnorm_rope": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                 _i64, _f, _int, _int, _int, _p],
+    "xops_rope_inplace": [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _int, _p],
     "xops_causal_conv1d_update": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _i64, _int, _i32, _int, _p],
     "xops_causal_conv1d_varlen": [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int,

@@ -391,6 +391,34 @@ int dispatch_rope(const void* in, const void* s, const void* c, void* q, void* k
   }
 }
 
+// ----------------------------------------------------------------------------
+// rope_inplace: interleaved (GPT-J style) RoPE on the last rope_dim dims of
+// every (row, head) vector, in place (rope_inplace_kernel,
+// triton_npu/triton_src/test_rope_inplace.py:17-46): pairs (2i, 2i+1) become
+//   (x0 c0 - x1 s0,  x1 c1 + x0 s1)
+// with sin / cos rows per batch entry shared by its heads.  One thread per
+// pair, both elements loaded and stored as one 2-element vector.
+// ----------------------------------------------------------------------------
+template <typename T, typename TS>
+__global__ void __launch_bounds__(256) rope_inplace_kernel(
+    T* x, const TS* __restrict__ sin_t, const TS* __restrict__ cos_t, int64_t rows,
+    int heads, int64_t sb, int64_t sh, int tail0, int pairs, int64_t scs) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * heads * pairs) return;
+  const int64_t v = i / pairs;
+  const int p = (int)(i - v * pairs);
+  const int64_t b = v / heads;
+  const int h = (int)(v - b * heads);
+  T* e = x + b * sb + h * sh + tail0 + 2 * p;
+  const TS* sr = sin_t + b * scs + 2 * p;
+  const TS* cr = cos_t + b * scs + 2 * p;
+  const float x0 = to_f32<T>(e[0]), x1 = to_f32<T>(e[1]);
+  const float o0 = x0 * to_f32<TS>(cr[0]) - x1 * to_f32<TS>(sr[0]);
+  const float o1 = x1 * to_f32<TS>(cr[1]) + x0 * to_f32<TS>(sr[1]);
+  e[0] = from_f32<T>(o0);
+  e[1] = from_f32<T>(o1);
+}
+
 }  // namespace
 
 int take_rope_error() {
@@ -446,4 +474,43 @@ extern "C" int xops_split_rmsnorm_rope(const void* input, const void* sin, const
     return w_dtype == XOPS_F32 ? with_s(t, float{}) : with_s(t, __nv_bfloat16{});
   };
   return dtype == XOPS_F32 ? with_w(float{}) : with_w(__nv_bfloat16{});
+}
+
+extern "C" int xops_rope_inplace(void* x, const void* sin, const void* cos, int64_t rows,
+                                 int64_t heads, int64_t hidden, int64_t rope_dim,
+                                 int64_t x_stride_row, int64_t x_stride_head,
+                                 int64_t sincos_stride, int x_dtype, int sincos_dtype,
+                                 void* stream) {
+  const char* what = "rope_inplace";
+  XOPS_REQUIRE(rows >= 0 && heads >= 1 && hidden >= 1, "%s: bad shape", what);
+  XOPS_REQUIRE(rope_dim >= 2 && rope_dim % 2 == 0 && rope_dim <= hidden,
+               "%s: rope_dim must be even and in [2, hidden] (got %lld, hidden %lld)", what,
+               (long long)rope_dim, (long long)hidden);
+  XOPS_REQUIRE(sincos_stride >= rope_dim, "%s: sin/cos rows shorter than rope_dim", what);
+  auto ok = [](int d) { return d == XOPS_F32 || d == XOPS_BF16 || d == XOPS_F16; };
+  XOPS_REQUIRE(ok(x_dtype) && ok(sincos_dtype), "%s: unsupported dtype", what);
+  const int64_t n = rows * heads * (rope_dim / 2);
+  if (n == 0) return XOPS_OK;
+  XOPS_REQUIRE(x && sin && cos, "%s: null pointer", what);
+  cudaStream_t st = (cudaStream_t)stream;
+  auto run = [&](auto tx, auto ts) {
+    using TX = decltype(tx);
+    using TS = decltype(ts);
+    rope_inplace_kernel<TX, TS><<<(unsigned)cdiv64(n, 256), 256, 0, st>>>(
+        (TX*)x, (const TS*)sin, (const TS*)cos, rows, (int)heads, x_stride_row, x_stride_head,
+        (int)(hidden - rope_dim), (int)(rope_dim / 2), sincos_stride);
+    return check_launch(what);
+  };
+  auto with_s = [&](auto tx) {
+    switch (sincos_dtype) {
+      case XOPS_F32: return run(tx, float{});
+      case XOPS_BF16: return run(tx, __nv_bfloat16{});
+      default: return run(tx, __half{});
+    }
+  };
+  switch (x_dtype) {
+    case XOPS_F32: return with_s(float{});
+    case XOPS_BF16: return with_s(__nv_bfloat16{});
+    default: return with_s(__half{});
+  }
 }

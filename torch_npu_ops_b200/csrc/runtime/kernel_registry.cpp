@@ -31,6 +31,7 @@ const Entry kTable[] = {
     {"fused_recurrent_gated_delta_rule_spec_fwd_kernel", "xops_fused_recurrent_gated_delta_rule",
      (void*)&xops_fused_recurrent_gated_delta_rule},
     {"fused_gdn_gating_decode_kernel", "xops_fused_gdn_gating", (void*)&xops_fused_gdn_gating},
+    {"rope_inplace_kernel", "xops_rope_inplace", (void*)&xops_rope_inplace},
     {"fused_qkvzba_split_reshape_cat_gqa_r*", "xops_fused_qkvzba_split_reshape_cat",
      (void*)&xops_fused_qkvzba_split_reshape_cat},
     {"fused_sigmoid_gating_delta_rule_update_kernel",

@@ -71,6 +71,7 @@ XOPS_DECLARE_OP(CausalConv1dUpdateNoCacheNoMtpOp, "_causal_conv1d_update_kernel_
 XOPS_DECLARE_OP(CausalConv1dUpdateQwenDecodeOp, "_causal_conv1d_update_qwen_decode_kernel")
 XOPS_DECLARE_OP(CausalConv1dUpdateTiledV2Op, "_causal_conv1d_update_kernel_npu_tiled_v2")
 XOPS_DECLARE_OP(FusedGdnGatingOp, "fused_gdn_gating_decode_kernel")
+XOPS_DECLARE_OP(RopeInplaceOp, "rope_inplace_kernel")
 XOPS_DECLARE_OP(FusedSigmoidGatingDeltaRuleUpdateOp, "fused_sigmoid_gating_delta_rule_update_kernel")
 XOPS_DECLARE_OP(FusedQkvzbaSplitReshapeGqaR1Op, "fused_qkvzba_split_reshape_cat_gqa_r1_kernel")
 XOPS_DECLARE_OP(FusedQkvzbaSplitReshapeGqaR2Op, "fused_qkvzba_split_reshape_cat_gqa_r2_kernel")
@@ -125,6 +126,7 @@ class OperationFactory {
   CausalConv1dUpdateTiledV2Op& causal_conv1d_update_tiled_v2() {
     return get<CausalConv1dUpdateTiledV2Op>("_causal_conv1d_update_kernel_npu_tiled_v2");
   }
+  RopeInplaceOp& rope_inplace() { return get<RopeInplaceOp>("rope_inplace_kernel"); }
   FusedGdnGatingOp& fused_gdn_gating() {
     return get<FusedGdnGatingOp>("fused_gdn_gating_decode_kernel");
   }

@@ -87,6 +87,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("inplace_final_state") = true, py::arg("cu_seqlens") = py::none(),
         py::arg("ssm_state_indices") = py::none(), py::arg("num_accepted_tokens") = py::none(),
         py::arg("use_qk_l2norm_in_kernel") = false);
+  m.def("rope_inplace",
+        [](torch::Tensor x, torch::Tensor sin, torch::Tensor cos, uint32_t rope_dim) {
+          xn::rope_inplace(x, sin, cos, rope_dim);
+          return x;
+        },
+        py::arg("x"), py::arg("sin"), py::arg("cos"), py::arg("rope_dim") = 64);
   m.def("npu_fused_qkvzba_split_reshape_cat",
         [](torch::Tensor qkvz, torch::Tensor ba, int32_t nqk, int32_t nv, int32_t hqk,
            int32_t hv) { return xn::npu_fused_qkvzba_split_reshape_cat(qkvz, ba, nqk, nv, hqk, hv); },

@@ -167,8 +167,22 @@ torch::Tensor npu_chunk_fwd_o(const torch::Tensor& q, const torch::Tensor& k,
   return o;
 }
 
-void rope_inplace(torch::Tensor&, torch::Tensor&, torch::Tensor&, uint32_t) {
-  TORCH_CHECK(false, "rope_inplace is not part of this build (out of the GDN hot path)");
+void rope_inplace(torch::Tensor& x, torch::Tensor& sin, torch::Tensor& cos, uint32_t rope_dim) {
+  on_cuda(x, "x");
+  TORCH_CHECK(x.dim() == 2 || x.dim() == 3,
+              "rope_inplace expects x of shape [bsz, hidden] or [bsz, heads, hidden]");
+  TORCH_CHECK(x.stride(-1) == 1, "rope_inplace expects x's last dimension to be contiguous");
+  auto x3 = x.dim() == 3 ? x : x.unsqueeze(1);
+  const int64_t bsz = x3.size(0), heads = x3.size(1), hidden = x3.size(2);
+  TORCH_CHECK(sin.dim() == 2 && cos.dim() == 2 && sin.sizes() == cos.sizes() &&
+                  sin.size(0) == bsz && sin.size(1) >= (int64_t)rope_dim,
+              "rope_inplace expects sin and cos of shape [bsz, rope_dim]");
+  TORCH_CHECK(sin.stride(-1) == 1 && cos.stride(-1) == 1 && sin.stride(0) == cos.stride(0),
+              "rope_inplace expects sin and cos rows with the same stride");
+  ok(xops_rope_inplace(P(x), P(sin), P(cos), bsz, heads, hidden, rope_dim, x3.stride(0),
+                       x3.stride(1), sin.stride(0), dtype_code(x), dtype_code(sin),
+                       stream_of(x)),
+     "rope_inplace");
 }
 
 std::pair<torch::Tensor, torch::Tensor> npu_fused_gdn_gating(torch::Tensor& A_log,

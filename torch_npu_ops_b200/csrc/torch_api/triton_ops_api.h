@@ -42,7 +42,7 @@ torch::Tensor npu_chunk_fwd_o(const torch::Tensor& q, const torch::Tensor& k,
                               const torch::Tensor& g_cumsum, float scale, int64_t chunk_size,
                               const std::optional<torch::Tensor>& cu_seqlens);
 
-// Outside this build's scope (MLA interleaved tail RoPE): throws.
+// Interleaved RoPE on the last rope_dim dims of x (MLA tail), in place.
 void rope_inplace(torch::Tensor& x, torch::Tensor& sin, torch::Tensor& cos,
                   uint32_t rope_dim = 64);
 

@@ -137,6 +137,27 @@ def npu_gemma_rms_norm(x, gamma, epsilon=1e-6):
 
 
 # ---------------------------------------------------------------------- rope
+def rope_inplace(x, sin, cos, rope_dim=64):
+    """Interleaved RoPE on the last ``rope_dim`` dims of x ([bsz, hidden] or
+    [bsz, heads, hidden]) in place, sin / cos [bsz, rope_dim] shared by a
+    row's heads (npu_triton_rope_inplace.cpp:22-66).  Returns x."""
+    _cuda(x, sin, cos)
+    _check(x.dim() in (2, 3), "rope_inplace expects x of shape [bsz, hidden] or "
+                              "[bsz, heads, hidden]")
+    _check(x.stride(-1) == 1, "rope_inplace expects x's last dimension to be contiguous")
+    x3 = x if x.dim() == 3 else x.unsqueeze(1)
+    bsz, heads, hidden = x3.shape
+    _check(sin.dim() == 2 and cos.dim() == 2 and sin.shape == cos.shape
+           and sin.shape[0] == bsz and sin.shape[1] >= rope_dim,
+           "rope_inplace expects sin and cos of shape [bsz, rope_dim]")
+    _check(sin.stride(-1) == 1 and cos.stride(-1) == 1 and sin.stride(0) == cos.stride(0),
+           "rope_inplace expects sin and cos rows with the same stride")
+    _lib.call("xops_rope_inplace", x.data_ptr(), sin.data_ptr(), cos.data_ptr(), bsz, heads,
+              hidden, int(rope_dim), x3.stride(0), x3.stride(1), sin.stride(0),
+              _dt(x, "rope_inplace"), _dt(sin, "rope_inplace"), _stream(x))
+    return x
+
+
 def npu_split_rmsnorm_rope(input, sin, cos, q_weight, k_weight, q_hidden_size, kv_hidden_size,
                            head_dim, eps, q_bias=None, k_bias=None, bias=False):
     """Split packed qkv, per-head RMSNorm on q/k, NeoX RoPE, copy v; returns
