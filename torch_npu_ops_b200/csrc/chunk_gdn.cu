@@ -324,6 +324,224 @@ __global__ void __launch_bounds__(P_NT, 4) chunk_prep_kernel(
   if (warp == 0) tc::tmem_dealloc(tm, P_TM_COLS);
 }
 
+// ----------------------------------------------------------------------------
+// Kernel 1b: the same preparation for a key head with exactly two value heads
+// (H == 2 Hg), both heads at once.  The Gram epilogue reads each TMEM row
+// once and builds both heads' A and Aqk; threads [0, 128) then invert head
+// 0's A while threads [128, 256) invert head 1's, so every barrier phase
+// carries twice the work.  Head 0's W accumulator reuses the Gram columns
+// (dead by then), which keeps the CTA at 128 TMEM columns and ~68 KB of
+// shared memory: three CTAs per SM.
+// ----------------------------------------------------------------------------
+constexpr int P2_OFF_HS0 = P_OFF_Q;               // head 0: inverse scratch, then T''
+constexpr int P2_OFF_HS1 = P_OFF_Q + P_KQ_HALF;   // head 1: inverse scratch, then T''
+constexpr int P2_FA_BYTES = 64 * LDF * 4;
+constexpr int P2_OFF_FA = 32768;                  // fp32 A_h, then T_h, h = 0, 1
+constexpr int P2_OFF_G = P2_OFF_FA + 2 * P2_FA_BYTES;  // per head: graw, gc, beta, e^gc
+constexpr int P2_SMEM = P2_OFF_G + 2 * 4 * 64 * 4 + 1024;
+constexpr uint32_t P2_TM_G = 0, P2_TM_W0 = 0, P2_TM_W1 = 64, P2_TM_COLS = 128;
+
+__global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
+    const float* __restrict__ beta, unsigned char* __restrict__ ws,
+    const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H,
+    int64_t q_stride, int64_t k_stride) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_sh;
+  __shared__ int64_t pos[4];
+  __shared__ int ok_sh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int quarter = warp & 3, colhalf = warp >> 2;
+  const int hk = blockIdx.y;
+  if (tid == 0) {
+    int64_t seq = 0, t0 = 0, eos = 0, cis = 0;
+    const bool ok = locate_chunk(cu, N, T, blockIdx.x, seq, t0, eos, cis);
+    pos[0] = ok ? chunk_offset(cu, seq, T) + cis : -1;
+    pos[1] = t0;
+    pos[2] = eos;
+    ok_sh = ok ? 1 : 0;
+  }
+  __syncthreads();
+  if (!ok_sh) return;
+  const int64_t gci = pos[0], t0 = pos[1];
+  const int L = (int)((pos[2] - t0) < BT ? (pos[2] - t0) : BT);
+  const int hv0 = 2 * hk;
+  // per head h: graw, gc, beta, e^gc (64 floats each)
+  float* gsm = reinterpret_cast<float*>(sm + P2_OFF_G);
+  auto graw = [&](int h) { return gsm + h * 256; };
+  auto gcs = [&](int h) { return gsm + h * 256 + 64; };
+  auto bet = [&](int h) { return gsm + h * 256 + 128; };
+  auto egc = [&](int h) { return gsm + h * 256 + 192; };
+  auto fa = [&](int h) { return reinterpret_cast<float*>(sm + P2_OFF_FA + h * P2_FA_BYTES); };
+  auto wsb = [&](int h) { return ws + (gci * H + hv0 + h) * (int64_t)WS_CHUNK; };
+  const uint32_t sb = tc::smem_addr(sm);
+
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_sh, P2_TM_COLS);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::mbar_fence_init();
+  }
+  cp_tile128(sm + P_OFF_KQ, P_KQ_HALF, k + t0 * k_stride + (int64_t)hk * 128, k_stride, L, tid, P_NT);
+  cp_tile128(sm + P_OFF_Q, P_KQ_HALF, q + t0 * q_stride + (int64_t)hk * 128, q_stride, L, tid, P_NT);
+  cp_async_commit();
+  if (tid < 128) {  // both heads' gates
+    const int h = tid >> 6, t = tid & 63;
+    graw(h)[t] = t < L ? g[(t0 + t) * H + hv0 + h] : 0.f;
+    bet(h)[t] = t < L ? beta[(t0 + t) * H + hv0 + h] : 0.f;
+  }
+  cp_async_wait_all();
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tm = tmem_sh;
+  uint32_t phase = 0;
+  bool alive = true;
+  if (tid == 0) {
+    const uint32_t id = tc::idesc_bf16(128, 64, false, false);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      tc::mma_bf16(tm + P2_TM_G, kdesc(sb + P_OFF_KQ, P_KQ_HALF, j), kdesc(sb + P_OFF_KQ, P_KQ_HALF, j),
+                   id, j > 0);
+    tc::commit(&bar);
+  }
+  if (warp == 0 || warp == 4) {  // cumsum of each head while the Gram product runs
+    const int h = warp >> 2;
+    chunk_cumsum_warp(graw(h), gcs(h), lane);
+    __syncwarp();
+    egc(h)[lane] = __expf(gcs(h)[lane]);
+    egc(h)[lane + 32] = __expf(gcs(h)[lane + 32]);
+  }
+  auto wait_mma = [&]() {
+    const bool ok = tc::mbar_wait(&bar, phase, WAIT_LIMIT);
+    phase ^= 1u;
+    if (!ok) {
+      record_error();
+      atomicExch(&ok_sh, 0);
+    }
+    tc::fence_after();
+    __syncthreads();
+    alive = ok_sh != 0;
+  };
+  wait_mma();
+  if (alive) {  // Gram epilogue: one TMEM row read serves both heads
+    const int row = quarter * 32 + lane;
+    const int c0 = colhalf * 32;
+    float vals[32];
+    tc::tmem_ld32(tm_addr(tm, quarter, P2_TM_G + c0), vals);
+    tc::tmem_wait_ld();
+    if (row < 64) {
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        float* far = fa(h) + row * LDF;
+        const float bi = bet(h)[row], gi = gcs(h)[row];
+        const float* gc = gcs(h);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int j = c0 + c;
+          far[j] = (j < row) ? vals[c] * bi * __expf(fminf(gi - gc[j], 0.f)) : 0.f;
+        }
+      }
+    } else {
+      const int i = row - 64;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        const float gi = gcs(h)[i];
+        const float* gc = gcs(h);
+        unsigned char* aqk = wsb(h) + WS_AQK;
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          float e[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int j = c0 + c + u;
+            e[u] = (j <= i) ? vals[c + u] * __expf(fminf(gi - gc[j], 0.f)) : 0.f;
+          }
+          uint4 pk;
+          pk.x = pack_bf16(e[0], e[1]); pk.y = pack_bf16(e[2], e[3]);
+          pk.z = pack_bf16(e[4], e[5]); pk.w = pack_bf16(e[6], e[7]);
+          *reinterpret_cast<uint4*>(aqk + chunk_off(i, (c0 + c) >> 3, 0)) = pk;
+        }
+      }
+    }
+  }
+  // every thread reaches the same barriers whether or not the MMA timed out
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const int hh = tid >> 7, ht = tid & 127;  // head and index within that head's half
+  {
+    float* ft = fa(hh);
+    float* fm = reinterpret_cast<float*>(sm + (hh ? P2_OFF_HS1 : P2_OFF_HS0));
+    tri_inverse_64_half(ft, fm, ht);
+    const float* bt = bet(hh);
+    const float* eg = egc(hh);
+    unsigned char* tpp = sm + (hh ? P2_OFF_HS1 : P2_OFF_HS0);
+    unsigned char* tpw = wsb(hh) + WS_TP;
+    for (int e = ht; e < 64 * 8; e += 128) {
+      const int i = e >> 3, cc = e & 7;
+      float tp[8], tq[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = cc * 8 + u;
+        const float tv = ft[i * LDF + j] * bt[j];
+        tp[u] = tv;  // diagonal = bf16(beta_i); the chain adds beta_i - bf16(beta_i)
+        tq[u] = tv * eg[j];
+      }
+      uint4 a, b;
+      a.x = pack_bf16(tp[0], tp[1]); a.y = pack_bf16(tp[2], tp[3]);
+      a.z = pack_bf16(tp[4], tp[5]); a.w = pack_bf16(tp[6], tp[7]);
+      b.x = pack_bf16(tq[0], tq[1]); b.y = pack_bf16(tq[2], tq[3]);
+      b.z = pack_bf16(tq[4], tq[5]); b.w = pack_bf16(tq[6], tq[7]);
+      *reinterpret_cast<uint4*>(tpw + chunk_off(i, cc, 0)) = a;
+      *reinterpret_cast<uint4*>(tpp + (uint32_t)(i * 128 + ((cc ^ (i & 7)) << 4))) = b;
+    }
+  }
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  if (tid == 0 && alive) {
+    const uint32_t id = tc::idesc_bf16(128, 64, true, false);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t tpp = sb + (h ? P2_OFF_HS1 : P2_OFF_HS0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        tc::mma_bf16(tm + (h ? P2_TM_W1 : P2_TM_W0), mndesc(sb + P_OFF_KQ, P_KQ_HALF, j),
+                     kdesc64(tpp, j), id, j > 0);
+    }
+    tc::commit(&bar);
+  }
+  if (alive) wait_mma();
+  if (alive) {  // -w [t][kk] (bf16, row-major, SW128) from w^T in TMEM (lane = kk)
+    const int kk = quarter * 32 + lane;
+    const int h = colhalf;  // warps 0-3: head 0, warps 4-7: head 1
+    const int kc = (kk & 63) >> 3;
+#pragma unroll 1
+    for (int part = 0; part < 2; ++part) {
+      const int c0 = part * 32;
+      float vals[32];
+      tc::tmem_ld32(tm_addr(tm, quarter, (h ? P2_TM_W1 : P2_TM_W0) + c0), vals);
+      tc::tmem_wait_ld();
+      unsigned char* wrow = wsb(h) + WS_W + (kk >> 6) * 8192 + (kk & 7) * 2 + c0 * 128;
+#pragma unroll
+      for (int c = 0; c < 32; ++c)
+        *reinterpret_cast<bf16*>(wrow + c * 128 + ((kc ^ (c & 7)) << 4)) =
+            __float2bfloat16_rn(-vals[c]);
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tm, P2_TM_COLS);
+}
+
 // ============================================================================
 // Kernel 2: the chunk chain
 // ============================================================================
@@ -1161,11 +1379,19 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
     kk = kn;
     qs = ks = Hg * K;
   }
-  if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_prep_kernel, gdn::P_SMEM,
-                                     "chunk_gated_delta_rule(prep)"))
-    return rc;
-  gdn::chunk_prep_kernel<<<dim3((unsigned)nchunks, (unsigned)Hg), gdn::P_NT, gdn::P_SMEM, st>>>(
-      qq, kk, g, beta, ws, cu_seqlens, N, T, Hg, H, qs, ks);
+  if (H == 2 * Hg) {  // two value heads per key head: both in one CTA
+    if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_prep_pair_kernel, gdn::P2_SMEM,
+                                       "chunk_gated_delta_rule(prep)"))
+      return rc;
+    gdn::chunk_prep_pair_kernel<<<dim3((unsigned)nchunks, (unsigned)Hg), gdn::P_NT, gdn::P2_SMEM,
+                                  st>>>(qq, kk, g, beta, ws, cu_seqlens, N, T, Hg, H, qs, ks);
+  } else {
+    if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_prep_kernel, gdn::P_SMEM,
+                                       "chunk_gated_delta_rule(prep)"))
+      return rc;
+    gdn::chunk_prep_kernel<<<dim3((unsigned)nchunks, (unsigned)Hg), gdn::P_NT, gdn::P_SMEM, st>>>(
+        qq, kk, g, beta, ws, cu_seqlens, N, T, Hg, H, qs, ks);
+  }
   if (int rc = check_launch("chunk_gated_delta_rule(prep)")) return rc;
   if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_chain_kernel, gdn::C_SMEM,
                                      "chunk_gated_delta_rule(chain)"))
