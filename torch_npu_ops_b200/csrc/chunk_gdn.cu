@@ -436,16 +436,25 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
     float vals[32];
     tc::tmem_ld32(tm_addr(tm, quarter, P2_TM_G + c0), vals);
     tc::tmem_wait_ld();
+    // this thread's 32 columns of each head's cumulative gates, as vectors
+    auto load_gc = [&](int h, float (&gc)[32]) {
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const float4 t = *reinterpret_cast<const float4*>(gcs(h) + c0 + 4 * v);
+        gc[4 * v] = t.x; gc[4 * v + 1] = t.y; gc[4 * v + 2] = t.z; gc[4 * v + 3] = t.w;
+      }
+    };
     if (row < 64) {
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         float* far = fa(h) + row * LDF;
         const float bi = bet(h)[row], gi = gcs(h)[row];
-        const float* gc = gcs(h);
+        float gc[32];
+        load_gc(h, gc);
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const int j = c0 + c;
-          far[j] = (j < row) ? vals[c] * bi * __expf(fminf(gi - gc[j], 0.f)) : 0.f;
+          far[j] = (j < row) ? vals[c] * bi * __expf(fminf(gi - gc[c], 0.f)) : 0.f;
         }
       }
     } else {
@@ -453,7 +462,8 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         const float gi = gcs(h)[i];
-        const float* gc = gcs(h);
+        float gcv[32];
+        load_gc(h, gcv);
         unsigned char* aqk = wsb(h) + WS_AQK;
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
@@ -461,7 +471,7 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const int j = c0 + c + u;
-            e[u] = (j <= i) ? vals[c + u] * __expf(fminf(gi - gc[j], 0.f)) : 0.f;
+            e[u] = (j <= i) ? vals[c + u] * __expf(fminf(gi - gcv[c + u], 0.f)) : 0.f;
           }
           uint4 pk;
           pk.x = pack_bf16(e[0], e[1]); pk.y = pack_bf16(e[2], e[3]);
@@ -486,13 +496,16 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
     unsigned char* tpw = wsb(hh) + WS_TP;
     for (int e = ht; e < 64 * 8; e += 128) {
       const int i = e >> 3, cc = e & 7;
-      float tp[8], tq[8];
+      float tp[8], tq[8], bv[8], ev[8];
+      *reinterpret_cast<float4*>(bv) = *reinterpret_cast<const float4*>(bt + cc * 8);
+      *reinterpret_cast<float4*>(bv + 4) = *reinterpret_cast<const float4*>(bt + cc * 8 + 4);
+      *reinterpret_cast<float4*>(ev) = *reinterpret_cast<const float4*>(eg + cc * 8);
+      *reinterpret_cast<float4*>(ev + 4) = *reinterpret_cast<const float4*>(eg + cc * 8 + 4);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int j = cc * 8 + u;
-        const float tv = ft[i * LDF + j] * bt[j];
+        const float tv = ft[i * LDF + cc * 8 + u] * bv[u];
         tp[u] = tv;  // diagonal = bf16(beta_i); the chain adds beta_i - bf16(beta_i)
-        tq[u] = tv * eg[j];
+        tq[u] = tv * ev[u];
       }
       uint4 a, b;
       a.x = pack_bf16(tp[0], tp[1]); a.y = pack_bf16(tp[2], tp[3]);

@@ -313,7 +313,8 @@ __device__ __forceinline__ void tri_inverse_64_inplace(float* __restrict__ sA,
 // reached by both halves, and each thread computes more outputs per level
 // (4 per 16x16 product, 2 x 4 per 32x32 product) with packed fp32 pairs.
 // The upper triangles of the blocks are zero, so the products run over
-// full index ranges without predicates.  sM needs 32 x 33 floats.
+// full index ranges without predicates.  sM needs 32 x 36 floats, 16-byte
+// aligned.
 __device__ __forceinline__ void tri_inverse_64_half(float* __restrict__ sA,
                                                     float* __restrict__ sM, int t) {
   {  // 8x8 diagonal blocks by forward substitution
@@ -372,16 +373,15 @@ __device__ __forceinline__ void tri_inverse_64_half(float* __restrict__ sA,
       s0 = ffma2(make_float2(a, a), make_float2(tr[0], tr[1]), s0);
       s1 = ffma2(make_float2(a, a), make_float2(tr[2], tr[3]), s1);
     }
-    float* mrow = sM + p * 256 + rr * 16 + cc;
-    mrow[0] = s0.x; mrow[1] = s0.y; mrow[2] = s1.x; mrow[3] = s1.y;
+    *reinterpret_cast<float4*>(sM + p * 256 + rr * 16 + cc) = make_float4(s0.x, s0.y, s1.x, s1.y);
     __syncthreads();
     float2 u0 = make_float2(0.f, 0.f), u1 = make_float2(0.f, 0.f);
 #pragma unroll 4
     for (int m = 0; m < 16; ++m) {
       const float a = sA[(r + rr) * LDF + r + m];
-      const float* mr = sM + p * 256 + m * 16 + cc;
-      u0 = ffma2(make_float2(a, a), make_float2(mr[0], mr[1]), u0);
-      u1 = ffma2(make_float2(a, a), make_float2(mr[2], mr[3]), u1);
+      const float4 mr = *reinterpret_cast<const float4*>(sM + p * 256 + m * 16 + cc);
+      u0 = ffma2(make_float2(a, a), make_float2(mr.x, mr.y), u0);
+      u1 = ffma2(make_float2(a, a), make_float2(mr.z, mr.w), u1);
     }
     float* out = sA + (r + rr) * LDF + cb + cc;
     out[0] = -u0.x; out[1] = -u0.y; out[2] = -u1.x; out[3] = -u1.y;
@@ -402,18 +402,17 @@ __device__ __forceinline__ void tri_inverse_64_half(float* __restrict__ sA,
       s[1][1] = ffma2(make_float2(a1, a1), tb, s[1][1]);
     }
 #pragma unroll
-    for (int a = 0; a < 2; ++a) {
-      float* mrow = sM + (rr + a) * 33 + cc;
-      mrow[0] = s[a][0].x; mrow[1] = s[a][0].y; mrow[2] = s[a][1].x; mrow[3] = s[a][1].y;
-    }
+    for (int a = 0; a < 2; ++a)
+      *reinterpret_cast<float4*>(sM + (rr + a) * 36 + cc) =
+          make_float4(s[a][0].x, s[a][0].y, s[a][1].x, s[a][1].y);
     __syncthreads();
     float2 u[2][2] = {{make_float2(0.f, 0.f), make_float2(0.f, 0.f)},
                       {make_float2(0.f, 0.f), make_float2(0.f, 0.f)}};
 #pragma unroll 4
     for (int m = 0; m < 32; ++m) {
       const float a0 = sA[(32 + rr) * LDF + 32 + m], a1 = sA[(33 + rr) * LDF + 32 + m];
-      const float* mr = sM + m * 33 + cc;
-      const float2 ma = make_float2(mr[0], mr[1]), mb = make_float2(mr[2], mr[3]);
+      const float4 mr = *reinterpret_cast<const float4*>(sM + m * 36 + cc);
+      const float2 ma = make_float2(mr.x, mr.y), mb = make_float2(mr.z, mr.w);
       u[0][0] = ffma2(make_float2(a0, a0), ma, u[0][0]);
       u[0][1] = ffma2(make_float2(a0, a0), mb, u[0][1]);
       u[1][0] = ffma2(make_float2(a1, a1), ma, u[1][0]);
