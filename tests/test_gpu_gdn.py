@@ -92,6 +92,7 @@ def _segmented(B, T, N, hk, hv, varlen):
     ([8192], 1, 2, False),                     # one long sequence: 16 segments of 8 chunks
     ([5000, 130, 64, 1, 0, 3000], 1, 2, True),  # long and short sequences share the plan
     ([16384], 2, 4, False),                    # GQA, longer segments
+    ([16384], 8, 16, True),                    # 16 heads, in-kernel L2 norm
 ])
 def test_chunk_segmented_chain(lens, hk, hv, l2):
     """Long sequences on few heads run as local / transition / output passes
