@@ -37,9 +37,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "GDN prefill tokens/s/GPU; norm/RoPE/conv1d HBM GB/s vs B200 peak"
-# 1,489 MB of DRAM traffic for 16,384 tokens x 32 value heads (q/k L2 pre-pass,
+# 1,466 MB of DRAM traffic for 16,384 tokens x 32 value heads (q/k L2 pre-pass,
 # prep, both chain phases, combine), measured by ncu
-GDN_DRAM_BYTES_PER_TOKEN_HEAD = 1.489e9 / (16384 * 32)
+GDN_DRAM_BYTES_PER_TOKEN_HEAD = 1.466e9 / (16384 * 32)
 
 
 def _peaks():
@@ -444,11 +444,12 @@ def main():
     flops = workloads.chunk_flops(cfg["lengths"], cfg["hv"])
     gdn_ms = stage_ms["gdn"]
     achieved = flops / (gdn_ms / 1000.0) / 1e12
-    # DRAM bytes (read + write) of the GDN stage's kernels from one ncu capture
-    # of the cfg5 shape at 16,384 tokens (profiles/gdn_cfg5_traffic.md), per
-    # (token, value head) and scaled by the tokens and heads of this run.
+    # DRAM bytes (read + write) of the GDN stage's kernels (q/k L2 pre-pass,
+    # prep, both chain phases, combine) from one ncu capture of the cfg5 shape
+    # at 16,384 tokens, per (token, value head), scaled by this run's tokens
+    # and heads.
     traffic = GDN_DRAM_BYTES_PER_TOKEN_HEAD * cfg["T"] * cfg["hv"]
-    roofline = {"kernel": "chunked GDN stage (prep + chain + combine)", "bound": "tensor",
+    roofline = {"kernel": "chunked GDN stage (q/k L2 + prep + chain + combine)", "bound": "tensor",
                 "achieved": achieved,
                 "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops_sustained"],
