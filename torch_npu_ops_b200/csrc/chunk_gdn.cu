@@ -14,17 +14,19 @@
 //      Aqk  = tril(q k^T * D)                     -> workspace (bf16)
 //    per value head, where gc is the in-chunk cumsum of g.
 //
-// 2. chunk_chain_kernel -- one CTA per (sequence, value head) walks the
-//    chunks in order.  Warp-specialised: warp 0 prefetches the next chunk's
-//    tiles (k, q, v from the inputs; w, T', Aqk from the workspace) into a
-//    second stage with cp.async; warp 1 issues every MMA from one thread;
-//    warps 2-17 hold the fp32 state S^T[v][kk] in registers (32 values per
-//    thread) and run the epilogues.  Per chunk:
+// 2. chunk_chain_kernel -- one CTA per work item (a run of chunks of one
+//    sequence and value head) walks the chunks in order.  Warp-specialised:
+//    warp 0 prefetches the next chunk's tiles (k, q, v by TMA from the
+//    inputs; w, T', Aqk by bulk copy from the workspace) into a second
+//    stage; warp 1 issues every MMA from one thread; warps 2-17 hold the
+//    fp32 state S^T[v][kk] in registers (32 values per thread) and run the
+//    epilogues.  Per chunk:
 //      D_u   = v^T T'^T + v^T diag(beta - bf16(beta))   (issued one chunk ahead)
-//      D_u  += S^T (-w)^T           (so v_new^T = D_u, beta_i v_i kept fp32)
-//      D_qh  = S^T q^T
+//      [D_u | D_qh] += S^T [-w; q]^T  (one N = 128 product; v_new^T = D_u with
+//                                      beta_i v_i kept fp32, D_qh = S^T q^T)
 //      dS    = vt_hi^T k + vt_lo^T k,  vt = v_new e^{gc_last - gc} split bf16 hi+lo
-//      D_o   = e^{gc} D_qh + v_new^T Aqk^T
+//      D_o   = e^{gc} D_qh + v_new^T Aqk^T   (the product issued behind the
+//                                             next chunk's [-w; q] product)
 //      S    <- e^{gc_last} S + dS,  o = scale * D_o
 //    The beta_i v_i diagonal term stays fp32 and the hi/lo split keeps the
 //    fp32 state within ~1e-5 of the fp32 recurrence.
@@ -611,7 +613,8 @@ __device__ __forceinline__ int seq_chunks(const int32_t* cu, int64_t n, int64_t 
 // 128-byte swizzle): the box lands exactly as one half of an SW128 tile.
 __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-    const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ g,
+    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+    const float* __restrict__ g,
     const float* __restrict__ beta, const float* __restrict__ h0,
     const unsigned char* __restrict__ ws, bf16* __restrict__ o, float* __restrict__ ht,
     const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H, float scale,
@@ -619,8 +622,8 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  __shared__ uint64_t full[2], empty[2], early_free[2], tma[2], bar_ht, bar_v, bar_q, bar_vt,
-      bar_s, bar_o, bar_od, bar_fin;
+  __shared__ uint64_t full[2], empty[2], early_free[2], tma[2], tma_a[2], aqk_free[2], bar_ht,
+      bar_v, bar_q, bar_vt, bar_s, bar_o, bar_od, bar_fin;
   __shared__ uint32_t tmem_sh;
   __shared__ int abort_sh;
   __shared__ int64_t it_n;
@@ -715,6 +718,8 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       tc::mbar_init(&empty[s], 1);
       tc::mbar_init(&early_free[s], 1);
       tc::mbar_init(&tma[s], 1);
+      tc::mbar_init(&tma_a[s], 1);
+      tc::mbar_init(&aqk_free[s], 1);
     }
     tc::mbar_init(&bar_ht, C_EPI_WARPS);
     tc::mbar_init(&bar_v, 1);
@@ -740,9 +745,9 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     // diagonal correction tile, so the epilogue and MMA warps only consume.
     for (int i = 0; i < NI; ++i) {
       const int s = i & 1, c = c0 + i;
-      // The stage is released in two parts: v, T', -w, q once chunk i-2's
-      // [-w; q] product is done (early_free), k and Aqk once its state and
-      // output products are (empty).
+      // The stage is released in three parts: v, T', -w, q once chunk i-2's
+      // [-w; q] product is done (early_free), k once its state product is
+      // (empty), Aqk once its output product is (aqk_free).
       if (i >= 2 && !tc::mbar_wait(&early_free[s], ((i - 2) >> 1) & 1, WAIT_LIMIT)) {
         record_error();
         atomicExch(&abort_sh, 1);
@@ -755,7 +760,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       const int y = (int)t0;
       if (lane == 0) {
         // the workspace pieces are stored as shared-memory images already
-        const uint32_t bytes = 32768 + (write_o ? 16384 + 8192 : 0) + (has_v ? 16384 + 8192 : 0);
+        const uint32_t bytes = 32768 + (write_o ? 16384 : 0) + (has_v ? 16384 + 8192 : 0);
         tc::mbar_arrive_expect_tx(&tma[s], bytes);
         for (int hf = 0; hf < 2; ++hf) {
           tc::bulk_load(st + S_WQ + hf * 16384, wsb + WS_W + hf * 8192, 8192, &tma[s]);
@@ -772,7 +777,6 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       if (lane == 0 && !*(volatile int*)&abort_sh) {
         for (int hf = 0; hf < 2; ++hf)
           tc::tma_load_2d(st + S_K + hf * 8192, &tm_k, hk * K + hf * 64, y, &tma[s]);
-        if (write_o) tc::bulk_load(st + S_AQK, wsb + WS_AQK, 8192, &tma[s]);
       }
       // gates of tokens 2*lane, 2*lane+1: in-chunk cumsum (same association
       // as chunk_cumsum_warp, so it matches the preparation kernel bit for bit)
@@ -835,24 +839,65 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       tc::fence_proxy_async();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&full[s]);
+      if (write_o) {
+        // Aqk is read last (by the output product, a chunk later): it has its
+        // own buffer release and transaction barrier
+        if (i >= 2 && !tc::mbar_wait(&aqk_free[s], ((i - 2) >> 1) & 1, WAIT_LIMIT)) {
+          record_error();
+          atomicExch(&abort_sh, 1);
+          break;
+        }
+        if (lane == 0) {
+          tc::mbar_arrive_expect_tx(&tma_a[s], 8192);
+          tc::bulk_load(st + S_AQK, wsb + WS_AQK, 8192, &tma_a[s]);
+        }
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // These products are short (N <= 128, K <= 128), so the issue rate of
+    // tcgen05.mma bounds them, not the tensor pipe: every descriptor is a
+    // per-stage base plus a compile-time offset (one 64-bit add per MMA).
     if (lane == 0 && NI > 0) {
       const uint32_t id_u = tc::idesc_bf16(128, 64, true, false);
-      const uint32_t id_vq = tc::idesc_bf16(128, 64, false, false);
+      const uint32_t id_w = tc::idesc_bf16(128, 64, false, false);
+      const uint32_t id_wq = tc::idesc_bf16(128, 128, false, false);
       const uint32_t id_s = tc::idesc_bf16(128, 128, false, true);
       const uint32_t id_o = tc::idesc_bf16(128, 64, false, false);
+      const uint64_t d_tpl = kdesc64(sb + C_OFF_TPL, 0);
+      // descriptor address steps (16-byte units): K-step j of a K-major
+      // [rows x 64] tile is 32 bytes on; of the [128 x 128] [-w; q] tile,
+      // (j / 4) halves of 16 KB plus (j % 4) * 32 bytes; of an MN-major tile,
+      // 16 rows (2 KB) on
+      constexpr uint64_t KSTEP64 = 32 >> 4, MNSTEP = 2048 >> 4;
+      auto wq_step = [](int j) -> uint64_t { return (uint64_t)(((j >> 2) * 16384 + (j & 3) * 32) >> 4); };
       // D_u = v^T T'^T with T' = T diag(beta) in bf16, plus v^T diag(beta -
       // bf16(beta)): the unit diagonal's beta_i v_i term is exact to ~2^-17.
       auto issue_u = [&](int i) {
         const uint32_t st = sb + (i & 1) * STAGE;
+        const uint64_t dv = mndesc(st + S_V, 8192, 0), dtp = kdesc64(st + S_TP, 0);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::mma_bf16(tm + C_TM_U, mndesc(st + S_V, 8192, j), kdesc64(st + S_TP, j), id_u, j > 0);
+          tc::mma_bf16(tm + C_TM_U, dv + j * MNSTEP, dtp + j * KSTEP64, id_u, j > 0);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::mma_bf16(tm + C_TM_U, mndesc(st + S_V, 8192, j), kdesc64(sb + C_OFF_TPL, j), id_u, true);
+          tc::mma_bf16(tm + C_TM_U, dv + j * MNSTEP, d_tpl + j * KSTEP64, id_u, true);
+      };
+      // D_o(c) += v_new^T Aqk^T, once the epilogue has put e^{gc} D_qh there
+      // (it does so while dS is formed).
+      auto issue_o = [&](int c) -> bool {
+        const int sc = c & 1;
+        if (!tc::mbar_wait(&bar_o, c & 1, WAIT_LIMIT) ||
+            !tc::mbar_wait(&tma_a[sc], (c >> 1) & 1, WAIT_LIMIT))
+          return false;
+        tc::fence_after();
+        const uint64_t da = kdesc64(sb + sc * STAGE + S_AQK, 0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::mma_bf16_ts(tm + C_TM_O, tm + C_TM_VN + 8 * j, da + j * KSTEP64, id_o, true);
+        tc::commit(&bar_od);
+        tc::commit(&aqk_free[sc]);
+        return true;
       };
       bool live = true;
       if (has_v) {
@@ -866,50 +911,44 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         if (!has_v && !(live = tc::mbar_wait(&full[s], (i >> 1) & 1, WAIT_LIMIT))) break;
         if (!(live = tc::mbar_wait(&bar_ht, i & 1, WAIT_LIMIT))) break;
         tc::fence_after();
-        // D_u (+)= S^T (-w)^T, A = bf16 S^T in TMEM: the state path gets its
-        // own barrier; D_qh = S^T q^T follows while the epilogue forms vt.
-        // (Loops kept rolled so their descriptors are not hoisted into registers.)
-#pragma unroll 1
-        for (int j = 0; j < 8; ++j)
-          tc::mma_bf16_ts(tm + C_TM_U, tm + C_TM_HT + 8 * j, kdesc(st + S_WQ, 16384, j), id_vq,
-                          has_v || j > 0);
-        tc::commit(&bar_v);
+        const uint64_t dwq = kdesc(st + S_WQ, 16384, 0);
         if (write_o) {
-#pragma unroll 1
+          // one N = 128 product over the [-w; q] tile: D_u += S^T (-w)^T next
+          // to D_qh = S^T q^T (the epilogue zeroed D_qh after reading it)
+#pragma unroll
           for (int j = 0; j < 8; ++j)
-            tc::mma_bf16_ts(tm + C_TM_QH, tm + C_TM_HT + 8 * j, kdesc(st + S_WQ + 8192, 16384, j),
-                            id_vq, j > 0);
+            tc::mma_bf16_ts(tm + C_TM_U, tm + C_TM_HT + 8 * j, dwq + wq_step(j), id_wq, true);
+          tc::commit(&bar_v);
           tc::commit(&bar_q);
+        } else {
+          // D_u (+)= S^T (-w)^T
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::mma_bf16_ts(tm + C_TM_U, tm + C_TM_HT + 8 * j, dwq + wq_step(j), id_w,
+                            has_v || j > 0);
+          tc::commit(&bar_v);
         }
         tc::commit(&early_free[s]);
         if (!(live = tc::mbar_wait(&bar_vt, i & 1, WAIT_LIMIT))) break;
         tc::fence_after();
         // dS = vt_hi^T k + vt_lo^T k
+        const uint64_t dk = mndesc(st + S_K, 8192, 0);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::mma_bf16_ts(tm + C_TM_DS, tm + C_TM_VTH + 8 * j, mndesc(st + S_K, 8192, j), id_s,
-                          j > 0);
+          tc::mma_bf16_ts(tm + C_TM_DS, tm + C_TM_VTH + 8 * j, dk + j * MNSTEP, id_s, j > 0);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc::mma_bf16_ts(tm + C_TM_DS, tm + C_TM_VTL + 8 * j, mndesc(st + S_K, 8192, j), id_s,
-                          true);
+          tc::mma_bf16_ts(tm + C_TM_DS, tm + C_TM_VTL + 8 * j, dk + j * MNSTEP, id_s, true);
         tc::commit(&bar_s);
-        // the next chunk's D_u runs while the epilogue applies dS
+        tc::commit(&empty[s]);
+        if (write_o && !(live = issue_o(i))) break;
+        // the output product and the next chunk's D_u run while the epilogue
+        // applies dS
         if (has_v && i + 1 < NI) {
           if (!(live = tc::mbar_wait(&full[s ^ 1], ((i + 1) >> 1) & 1, WAIT_LIMIT))) break;
           tc::fence_after();
           issue_u(i + 1);
         }
-        if (write_o) {
-          // D_o += v_new^T Aqk^T, once the epilogue has put e^{gc} D_qh there
-          if (!(live = tc::mbar_wait(&bar_o, i & 1, WAIT_LIMIT))) break;
-          tc::fence_after();
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            tc::mma_bf16_ts(tm + C_TM_O, tm + C_TM_VN + 8 * j, kdesc64(st + S_AQK, j), id_o, true);
-          tc::commit(&bar_od);
-        }
-        tc::commit(&empty[s]);
       }
       if (!live) {
         record_error();
@@ -966,19 +1005,31 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     };
     static_assert(C_TCOLS == 16 && C_SCOLS == 32, "epilogue tiling assumes 16 warps");
     // o = scale * D_o of a finished chunk.  A warp owns 16 tokens x 32 values
-    // (lane = value): it transposes them through its shared buffer so that
-    // each lane stores two 16-byte pieces of token rows.
+    // (lane = value): it writes them as bf16 rows [token][value] into its own
+    // 1 KB shared buffer and lane 0 stores the box with one TMA store.  A warp
+    // whose rows cross the sequence end (the rows after it belong to the next
+    // sequence) stores its valid rows with plain 16-byte stores instead.
     unsigned char* ost = sm + C_OFF_OST + cw * 2048;
     auto write_out = [&](int64_t tb, int Lc) {
       float ov[16];
       tc::tmem_ld16(tm_addr(tm, quarter, C_TM_O + tc0), ov);
+      if (lane == 0) tc::bulk_wait_read<0>();  // the previous store has read the buffer
       tc::tmem_wait_ld();
-      __syncwarp();  // the previous transpose has been read out
+      __syncwarp();
 #pragma unroll
       for (int c = 0; c < 16; c += 2) {
         const uint32_t w = pack2<bf16>(fmul2(make_float2(ov[c], ov[c + 1]), make_float2(scale, scale)));
         *reinterpret_cast<uint16_t*>(ost + c * 64 + lane * 2) = (uint16_t)(w & 0xffffu);
         *reinterpret_cast<uint16_t*>(ost + (c + 1) * 64 + lane * 2) = (uint16_t)(w >> 16);
+      }
+      if (tc0 + C_TCOLS <= Lc) {
+        tc::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          tc::tma_store_2d(&tm_o, (int)(h * V + quarter * 32), (int)(tb + tc0), ost);
+          tc::bulk_commit_group();
+        }
+        return;
       }
       __syncwarp();
 #pragma unroll
@@ -1003,6 +1054,8 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
           S[cb * 8 + m] = ffma2(S[cb * 8 + m], dl2, make_float2(d[2 * m], d[2 * m + 1]));
       }
     };
+    // D_qh starts at zero: the [-w; q] product accumulates into it
+    if (write_o) tc::tmem_st16_zero(tm_addr(tm, quarter, C_TM_QH + tc0));
     for (int i = 0; i < NI; ++i) {
       const int s = i & 1;
       if (i > 0) {
@@ -1018,6 +1071,12 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         tc::tmem_st16u(tm_addr(tm, quarter, C_TM_HT + kc0 / 2), pk);
       }
       warp_arrive(&bar_ht);
+      // the previous chunk's output runs while the tensor core forms this
+      // chunk's [-w; q] product
+      if (write_o && i > 0) {
+        if (!(live = wait_ok(&bar_od, (i - 1) & 1))) break;
+        write_out(t0_prev, L_prev);
+      }
       if (!(live = wait_ok(&full[s], (i >> 1) & 1))) break;
       if (!(live = wait_ok(&bar_v, i & 1))) break;
       const float* tab = reinterpret_cast<const float*>(sm + C_OFF_TAB + (i & 3) * C_TAB);
@@ -1048,17 +1107,13 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       warp_arrive(&bar_vt);
       gl_prev = tab[128];
       if (write_o) {
-        // previous chunk's output (its product also frees D_o and v_new)
-        // overlaps this chunk's state product
-        if (i > 0) {
-          if (!(live = wait_ok(&bar_od, (i - 1) & 1))) break;
-          write_out(t0_prev, L_prev);
-        }
-        // E1b: D_o = e^{gc} D_qh, bf16 v_new -> TMEM
+        // E1b, while the tensor core forms dS: D_o = e^{gc} D_qh (the previous
+        // output has been read out above), bf16 v_new -> TMEM
         if (!(live = wait_ok(&bar_q, i & 1))) break;
         float qh[16];
         tc::tmem_ld16(tm_addr(tm, quarter, C_TM_QH + tc0), qh);
         tc::tmem_wait_ld();
+        tc::tmem_st16_zero(tm_addr(tm, quarter, C_TM_QH + tc0));
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           const float4 e4 = *reinterpret_cast<const float4*>(tab + 64 + tc0 + 4 * q4);
@@ -1089,6 +1144,8 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       }
     }
   }
+  // the output stores have completed before the CTA exits
+  if (warp >= 2 && lane == 0) tc::bulk_wait_all();
   tc::fence_before();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tm, C_TM_COLS);
@@ -1417,12 +1474,17 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
   if (int rc = token_rows_map(&mv, v, H * V, B * T, v_token_stride,
                               "chunk_gated_delta_rule(v map)"))
     return rc;
+  // o as [tokens, H * V]: each epilogue warp stores 16 tokens x 32 values
+  CUtensorMap mo;
+  if (int rc = token_rows_map(&mo, o, H * V, B * T, H * V, "chunk_gated_delta_rule(o map)", 32,
+                              16, false))
+    return rc;
   const bool varlen = cu_seqlens != nullptr;
   const int seg = chain_segment_chunks(B, T, N, H, varlen);
   gdn::ChainPlan plan{seg, 1, nullptr};
   if (seg == 0) {
     gdn::chunk_chain_kernel<<<(unsigned)(N * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-        mq, mk, mv, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+        mq, mk, mv, mo, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
         plan);
     return check_launch("chunk_gated_delta_rule(chain)");
   }
@@ -1432,7 +1494,7 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
   plan.scratch = reinterpret_cast<float*>(ws + off);
   const int64_t slots = chain_segment_slots(T, N, varlen, seg);
   gdn::chunk_chain_kernel<<<(unsigned)((N + 2 * slots) * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-      mq, mk, mv, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+      mq, mk, mv, mo, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
         plan);
   if (int rc = check_launch("chunk_gated_delta_rule(chain, first segments)")) return rc;
   {
@@ -1460,7 +1522,7 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
   if (int rc = check_launch("chunk_gated_delta_rule(combine)")) return rc;
   plan.phase = 3;
   gdn::chunk_chain_kernel<<<(unsigned)(slots * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-      mq, mk, mv, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+      mq, mk, mv, mo, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
         plan);
   return check_launch("chunk_gated_delta_rule(chain, remaining segments)");
 }
