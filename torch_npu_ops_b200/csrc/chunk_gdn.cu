@@ -883,8 +883,8 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         for (int j = 0; j < 4; ++j)
           tc::mma_bf16(tm + C_TM_U, dv + j * MNSTEP, d_tpl + j * KSTEP64, id_u, true);
       };
-      // D_o(c) += v_new^T Aqk^T, once the epilogue has put e^{gc} D_qh there
-      // (it does so while dS is formed).
+      // D_o(c) += v_new^T Aqk^T, once the epilogue has put e^{gc} D_qh there.
+      // Issued behind the next chunk's [-w; q] product, off the state path.
       auto issue_o = [&](int c) -> bool {
         const int sc = c & 1;
         if (!tc::mbar_wait(&bar_o, c & 1, WAIT_LIMIT) ||
@@ -929,6 +929,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
           tc::commit(&bar_v);
         }
         tc::commit(&early_free[s]);
+        if (write_o && i > 0 && !(live = issue_o(i - 1))) break;
         if (!(live = tc::mbar_wait(&bar_vt, i & 1, WAIT_LIMIT))) break;
         tc::fence_after();
         // dS = vt_hi^T k + vt_lo^T k
@@ -941,15 +942,14 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
           tc::mma_bf16_ts(tm + C_TM_DS, tm + C_TM_VTL + 8 * j, dk + j * MNSTEP, id_s, true);
         tc::commit(&bar_s);
         tc::commit(&empty[s]);
-        if (write_o && !(live = issue_o(i))) break;
-        // the output product and the next chunk's D_u run while the epilogue
-        // applies dS
+        // the next chunk's D_u runs while the epilogue applies dS
         if (has_v && i + 1 < NI) {
           if (!(live = tc::mbar_wait(&full[s ^ 1], ((i + 1) >> 1) & 1, WAIT_LIMIT))) break;
           tc::fence_after();
           issue_u(i + 1);
         }
       }
+      if (live && write_o) live = issue_o(NI - 1);
       if (!live) {
         record_error();
         atomicExch(&abort_sh, 1);
@@ -1071,12 +1071,6 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         tc::tmem_st16u(tm_addr(tm, quarter, C_TM_HT + kc0 / 2), pk);
       }
       warp_arrive(&bar_ht);
-      // the previous chunk's output runs while the tensor core forms this
-      // chunk's [-w; q] product
-      if (write_o && i > 0) {
-        if (!(live = wait_ok(&bar_od, (i - 1) & 1))) break;
-        write_out(t0_prev, L_prev);
-      }
       if (!(live = wait_ok(&full[s], (i >> 1) & 1))) break;
       if (!(live = wait_ok(&bar_v, i & 1))) break;
       const float* tab = reinterpret_cast<const float*>(sm + C_OFF_TAB + (i & 3) * C_TAB);
@@ -1107,8 +1101,14 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       warp_arrive(&bar_vt);
       gl_prev = tab[128];
       if (write_o) {
+        // the previous chunk's output (its product ran behind this chunk's
+        // [-w; q] product) while the tensor core forms dS
+        if (i > 0) {
+          if (!(live = wait_ok(&bar_od, (i - 1) & 1))) break;
+          write_out(t0_prev, L_prev);
+        }
         // E1b, while the tensor core forms dS: D_o = e^{gc} D_qh (the previous
-        // output has been read out above), bf16 v_new -> TMEM
+        // chunk's output has just been read out of it), bf16 v_new -> TMEM
         if (!(live = wait_ok(&bar_q, i & 1))) break;
         float qh[16];
         tc::tmem_ld16(tm_addr(tm, quarter, C_TM_QH + tc0), qh);
