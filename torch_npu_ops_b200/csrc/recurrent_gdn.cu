@@ -70,8 +70,11 @@ __device__ __forceinline__ float softplus_f(float x, float beta, float thr) {
   return bx <= thr ? log1pf(expf(bx)) / beta : x;
 }
 
-template <int K, int V>
-__global__ void __launch_bounds__(128) recurrent_gdn_kernel(
+// PT: the per-token state stores of speculative decoding, compiled separately
+// so the plain decode step keeps its register budget (three CTAs per SM for
+// the 128 x 128 state).
+template <int K, int V, bool PT>
+__global__ void __launch_bounds__(128, PT ? 1 : 3) recurrent_gdn_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
     const __nv_bfloat16* __restrict__ v, const float* __restrict__ g,
     const float* __restrict__ beta, __nv_bfloat16* __restrict__ o,
@@ -96,10 +99,12 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
     bos = n * T;
     eos = bos + T;
   }
-  if (sl.per_token && eos == bos) return;  // nothing to read back or store
-  const int64_t i0 = sl.accepted ? (int64_t)sl.accepted[n] - 1 : 0;
+  if (PT && eos == bos) return;  // nothing to read back or store
+  // without per-token stores there is no accepted-token count (it implies
+  // them), so the initial slot is the sequence's first index entry
+  const int64_t i0 = PT && sl.accepted ? (int64_t)sl.accepted[n] - 1 : 0;
   const int64_t slot =
-      sl.idx ? (int64_t)sl.idx[n * sl.stride_seq + i0 * sl.stride_tok] : n;
+      sl.idx ? (int64_t)sl.idx[n * sl.stride_seq + (PT ? i0 * sl.stride_tok : 0)] : n;
   const bool inplace = (const float*)ht == h0;
   // a negative slot: zero initial state, and (in place) no write-back
   const bool has_slot = slot >= 0;
@@ -107,7 +112,7 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
   // in place (ht == h0): back into the same slot; otherwise ht is indexed by
   // sequence (the reference's INPLACE_FINAL_STATE split, :169-188)
   float* hdst = ht + (inplace ? (has_slot ? slot : 0) : n) * ht_stride + (int64_t)hv * K * V;
-  const bool write_back = !sl.per_token && (!inplace || has_slot);
+  const bool write_back = !PT && (!inplace || has_slot);
   const int r0 = warp * ROWS, c0 = lane * COLS;
 
   // h0 and ht may be the same buffer (in-place update): each thread reads
@@ -215,7 +220,7 @@ __global__ void __launch_bounds__(128) recurrent_gdn_kernel(
         ov[c] = s_red[0][c0 + c] + s_red[1][c0 + c] + s_red[2][c0 + c] + s_red[3][c0 + c];
       store_vec<__nv_bfloat16, COLS>(o + (t * HV + hv) * V + c0, ov);
     }
-    if (sl.per_token) {  // the state after token t, to slot (n, t)
+    if constexpr (PT) {  // the state after token t, to slot (n, t)
       const int64_t st = sl.idx[n * sl.stride_seq + (t - bos) * sl.stride_tok];
       if (st >= 0) {
         float* dst = ht + st * ht_stride + (int64_t)hv * K * V;
@@ -250,7 +255,9 @@ int launch_recurrent(const void* q, const void* k, const void* v, const float* g
   const unsigned grid = (unsigned)(N * HV);
 #define XOPS_REC(KK, VV)                                                                      \
   if (K == KK && V == VV) {                                                                   \
-    recurrent_gdn_kernel<KK, VV><<<grid, 128, 0, st>>>(                                       \
+    auto kern = slots.per_token ? recurrent_gdn_kernel<KK, VV, true>                          \
+                                : recurrent_gdn_kernel<KK, VV, false>;                        \
+    kern<<<grid, 128, 0, st>>>(                                                               \
         (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta,   \
         (__nv_bfloat16*)o, h0, ht, cu_seqlens, slots, T, H, HV, h0_stride, ht_stride, scale,  \
         l2, gs);                                                                              \

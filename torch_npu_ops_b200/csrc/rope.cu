@@ -250,8 +250,10 @@ __global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
         const float* brow = wrow + HD;
 #pragma unroll
         for (int j = 0; j < P; j += 2) {
+          // without a bias the shared-memory read of the zero row is skipped
           const float4 w4 = *reinterpret_cast<const float4*>(wrow + d0 + 2 * j);
-          const float4 b4 = *reinterpret_cast<const float4*>(brow + d0 + 2 * j);
+          const float4 b4 = has_b ? *reinterpret_cast<const float4*>(brow + d0 + 2 * j)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
           v[j] = ffma2(fmul2(x[u][j], r2), make_float2(w4.x, w4.y), make_float2(b4.x, b4.y));
           v[j + 1] = ffma2(fmul2(x[u][j + 1], r2), make_float2(w4.z, w4.w), make_float2(b4.z, b4.w));
         }
