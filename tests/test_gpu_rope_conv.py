@@ -149,6 +149,7 @@ def test_conv_varlen_ragged_and_slots():
     (16, 2048, 1, 4, 3, False, torch.bfloat16),
     (7, 64, 3, 4, 5, True, torch.float32),
     (4, 128, 2, 3, 2, True, torch.float16),
+    (9, 512, 1, 4, 3, True, torch.float16),   # odd batch on the two-rows-per-thread path
 ])
 def test_conv_decode(B, dim, L, width, state_len, bias, dt):
     g = torch.Generator().manual_seed(B + dim)
@@ -163,6 +164,24 @@ def test_conv_decode(B, dim, L, width, state_len, bias, dt):
     st_ref = st.clone()
     ref = oracle.causal_conv1d_update(x, st_ref, wt, b, True, slots)
     (assert_fp32 if dt == torch.float32 else assert_bf16)(y, ref)
+    assert torch.equal(st_d.cpu(), st_ref)
+
+
+@pytest.mark.parametrize("B,bias", [(5, False), (4096, True)])
+def test_conv_decode_rows_without_slots(B, bias):
+    # rows map to their own state lines; an odd batch leaves the second row
+    # of the last thread empty
+    g = torch.Generator().manual_seed(B)
+    dim = 8192 if B > 64 else 128
+    x = torch.randn(B, dim, generator=g).to(torch.bfloat16)
+    st = torch.randn(B, dim, 3, generator=g).to(torch.bfloat16)
+    wt = (0.5 * torch.randn(dim, 4, generator=g)).to(torch.bfloat16)
+    b = (0.5 * torch.randn(dim, generator=g)).to(torch.bfloat16) if bias else None
+    st_d = st.clone().to(DEV)
+    y = ops.npu_causal_conv1d_update(x.to(DEV), st_d, wt.to(DEV), True, _to(b))
+    st_ref = st.clone()
+    ref = oracle.causal_conv1d_update(x, st_ref, wt, b, True)
+    assert_bf16(y, ref)
     assert torch.equal(st_d.cpu(), st_ref)
 
 
