@@ -557,6 +557,17 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
   if (warp == 0) tc::tmem_dealloc(tm, P2_TM_COLS);
 }
 
+// Four 8 x 8 bf16 blocks from the mma fragment layout (thread t holds row
+// t / 4, elements 2 (t % 4) + {0, 1} of each) to shared memory transposed:
+// block b's row i (its column i) goes to the address lane 8 b + i gives.
+__device__ __forceinline__ void stmatrix_x4_trans(void* row, uint32_t b0, uint32_t b1, uint32_t b2,
+                                                  uint32_t b3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};\n" ::"r"(
+                   tc::smem_addr(row)),
+               "r"(b0), "r"(b1), "r"(b2), "r"(b3)
+               : "memory");
+}
+
 // ============================================================================
 // Kernel 2: the chunk chain
 // ============================================================================
@@ -1005,22 +1016,32 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     };
     static_assert(C_TCOLS == 16 && C_SCOLS == 32, "epilogue tiling assumes 16 warps");
     // o = scale * D_o of a finished chunk.  A warp owns 16 tokens x 32 values
-    // (lane = value): it writes them as bf16 rows [token][value] into its own
-    // 1 KB shared buffer and lane 0 stores the box with one TMA store.  A warp
-    // whose rows cross the sequence end (the rows after it belong to the next
-    // sequence) stores its valid rows with plain 16-byte stores instead.
+    // (TMEM lane = value): two 16-lane TMEM loads deliver them in the mma
+    // fragment layout, and two transposing stmatrix stores write them as bf16
+    // rows [token][value] into the warp's own 1 KB shared buffer; lane 0 then
+    // stores the box with one TMA store.  A warp whose rows cross the
+    // sequence end (the rows after it belong to the next sequence) stores its
+    // valid rows with plain 16-byte stores instead.
     unsigned char* ost = sm + C_OFF_OST + cw * 2048;
     auto write_out = [&](int64_t tb, int Lc) {
-      float ov[16];
-      tc::tmem_ld16(tm_addr(tm, quarter, C_TM_O + tc0), ov);
+      uint32_t ra[8], rb[8];  // values 0-15 and 16-31 of the warp's lanes
+      tc::tmem_ld16x256b_x2(tm_addr(tm, quarter, C_TM_O + tc0), ra);
+      tc::tmem_ld16x256b_x2(tm_addr(tm, quarter, C_TM_O + tc0) + (16u << 16), rb);
       if (lane == 0) tc::bulk_wait_read<0>();  // the previous store has read the buffer
       tc::tmem_wait_ld();
       __syncwarp();
-#pragma unroll
-      for (int c = 0; c < 16; c += 2) {
-        const uint32_t w = pack2<bf16>(fmul2(make_float2(ov[c], ov[c + 1]), make_float2(scale, scale)));
-        *reinterpret_cast<uint16_t*>(ost + c * 64 + lane * 2) = (uint16_t)(w & 0xffffu);
-        *reinterpret_cast<uint16_t*>(ost + (c + 1) * 64 + lane * 2) = (uint16_t)(w >> 16);
+      {
+        const float2 sc2 = make_float2(scale, scale);
+        auto pk = [&](uint32_t x, uint32_t y) {
+          return pack2<bf16>(fmul2(make_float2(__uint_as_float(x), __uint_as_float(y)), sc2));
+        };
+        // 8 x 8 blocks (values vb.., tokens 8 (mi >> 1)..): thread t gives
+        // the shared row of token row t % 8 of block t / 8
+        const int mi = lane >> 3, tok = ((mi >> 1) << 3) + (lane & 7), vb = (mi & 1) << 3;
+        stmatrix_x4_trans(ost + tok * 64 + vb * 2, pk(ra[0], ra[1]), pk(ra[2], ra[3]),
+                          pk(ra[4], ra[5]), pk(ra[6], ra[7]));
+        stmatrix_x4_trans(ost + tok * 64 + (16 + vb) * 2, pk(rb[0], rb[1]), pk(rb[2], rb[3]),
+                          pk(rb[4], rb[5]), pk(rb[6], rb[7]));
       }
       if (tc0 + C_TCOLS <= Lc) {
         tc::fence_proxy_async();

@@ -214,6 +214,16 @@ __device__ __forceinline__ void tmem_st16_zero(uint32_t taddr) {
       "%1,%1};\n" ::"r"(taddr),
       "r"(0u));
 }
+// 16 lanes x 256 bits, twice along the columns: thread t receives lane
+// (t / 4) columns 2 (t % 4) + {0, 1} in v[0..1], lane 8 + t / 4 in v[2..3],
+// and the same 8 columns further on in v[4..7] (the mma accumulator fragment
+// layout of two 16 x 8 tiles).  Lane base = the address's lane field.
+__device__ __forceinline__ void tmem_ld16x256b_x2(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                 "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
