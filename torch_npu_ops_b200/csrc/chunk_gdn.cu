@@ -114,6 +114,17 @@ __global__ void __launch_bounds__(256) l2norm_heads_kernel(const bf16* __restric
   *reinterpret_cast<uint2*>(y + r * 128 + lane * 4) = out;
 }
 
+// Four 8 x 8 bf16 blocks from the mma fragment layout (thread t holds row
+// t / 4, elements 2 (t % 4) + {0, 1} of each) to shared memory transposed:
+// block b's row i (its column i) goes to the address lane 8 b + i gives.
+__device__ __forceinline__ void stmatrix_x4_trans(void* row, uint32_t b0, uint32_t b1, uint32_t b2,
+                                                  uint32_t b3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};\n" ::"r"(
+                   tc::smem_addr(row)),
+               "r"(b0), "r"(b1), "r"(b2), "r"(b3)
+               : "memory");
+}
+
 // ============================================================================
 // Kernel 1: per-chunk preparation
 // ============================================================================
@@ -535,37 +546,46 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
     tc::commit(&bar);
   }
   if (alive) wait_mma();
-  if (alive) {  // -w [t][kk] (bf16, row-major, SW128) from w^T in TMEM (lane = kk)
-    const int kk = quarter * 32 + lane;
+  if (alive) {
+    // -w [t][kk] (bf16, SW128 image) from w^T in TMEM (lane = kk).  The k and
+    // T'' tiles are dead now: head h's image is staged at 16 KB x h.  16-lane
+    // TMEM loads give 8 x 8 blocks in the mma fragment layout; transposing
+    // stmatrix stores put each block's 8 token rows (8 kk each, one 16-byte
+    // chunk) at their swizzled places; one bulk store per head follows.
     const int h = colhalf;  // warps 0-3: head 0, warps 4-7: head 1
-    const int kc = (kk & 63) >> 3;
+    unsigned char* stage = sm + h * 16384;
+    const uint32_t wcol = h ? P2_TM_W1 : P2_TM_W0;
+    const int mi = lane >> 3;
 #pragma unroll 1
-    for (int part = 0; part < 2; ++part) {
-      const int c0 = part * 32;
-      float vals[32];
-      tc::tmem_ld32(tm_addr(tm, quarter, (h ? P2_TM_W1 : P2_TM_W0) + c0), vals);
+    for (int tb = 0; tb < 64; tb += 16) {
+      uint32_t ra[8], rb[8];  // kk 32 q + 0..15 and 32 q + 16..31, tokens tb..tb + 15
+      tc::tmem_ld16x256b_x2(tm_addr(tm, quarter, wcol + tb), ra);
+      tc::tmem_ld16x256b_x2(tm_addr(tm, quarter, wcol + tb) + (16u << 16), rb);
       tc::tmem_wait_ld();
-      unsigned char* wrow = wsb(h) + WS_W + (kk >> 6) * 8192 + (kk & 7) * 2 + c0 * 128;
+      auto pk = [](uint32_t x, uint32_t y) {
+        return pack2<bf16>(make_float2(-__uint_as_float(x), -__uint_as_float(y)));
+      };
+      const int t = tb + ((mi >> 1) << 3) + (lane & 7);
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        *reinterpret_cast<bf16*>(wrow + c * 128 + ((kc ^ (c & 7)) << 4)) =
-            __float2bfloat16_rn(-vals[c]);
+      for (int lb = 0; lb < 32; lb += 16) {
+        const int kk8 = quarter * 32 + lb + ((mi & 1) << 3);  // first kk of the row's chunk
+        unsigned char* row =
+            stage + (kk8 >> 6) * 8192 + t * 128 + ((((kk8 & 63) >> 3) ^ (t & 7)) << 4);
+        const uint32_t(&r)[8] = lb ? rb : ra;
+        stmatrix_x4_trans(row, pk(r[0], r[1]), pk(r[2], r[3]), pk(r[4], r[5]), pk(r[6], r[7]));
+      }
     }
+    tc::fence_proxy_async();
+  }
+  __syncthreads();
+  if (alive && tid == 0) {
+    for (int h = 0; h < 2; ++h) tc::bulk_store(wsb(h) + WS_W, sm + h * 16384, 16384);
+    tc::bulk_commit_group();
+    tc::bulk_wait_all();
   }
   tc::fence_before();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tm, P2_TM_COLS);
-}
-
-// Four 8 x 8 bf16 blocks from the mma fragment layout (thread t holds row
-// t / 4, elements 2 (t % 4) + {0, 1} of each) to shared memory transposed:
-// block b's row i (its column i) goes to the address lane 8 b + i gives.
-__device__ __forceinline__ void stmatrix_x4_trans(void* row, uint32_t b0, uint32_t b1, uint32_t b2,
-                                                  uint32_t b3) {
-  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};\n" ::"r"(
-                   tc::smem_addr(row)),
-               "r"(b0), "r"(b1), "r"(b2), "r"(b3)
-               : "memory");
 }
 
 // ============================================================================
