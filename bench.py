@@ -114,7 +114,8 @@ def build_cfg5(rank, world, T, dev):
     w = workloads.long_config5_shard(rank, world, T=T)
     (v0, v1), (k0, k1) = w["heads"], w["k_heads"]
     hv, hk = v1 - v0, k1 - k0
-    host = {"x": w["x"], "g": w["g"], "beta": w["beta"], "z": w["z"]}
+    host = {"x": w["x"], "g": w["g"], "beta": w["beta"], "initial_state": w["initial_state"],
+            "z": w["z"]}
     dev_t = {n: t.to(dev) for n, t in host.items()}
     consts = {"weight": w["weight"].to(dev), "bias": w["bias"].to(dev),
               "norm_w": w["norm_w"].to(dev)}
@@ -133,7 +134,8 @@ def build_cfg3(dev):
 
 
 def make_step(cfg, kind, dev):
-    """Returns step(inputs) -> output tensor, plus per-stage event hooks."""
+    """Returns step(inputs) -> tuple of output tensors, plus the stage names
+    its optional event list brackets."""
     import torch_npu_ops_b200 as ops
     c = cfg["consts"]
     if kind == "cfg3":
@@ -143,28 +145,19 @@ def make_step(cfg, kind, dev):
                                                    inp["beta"], None, inp["initial_state"], True,
                                                    c["cu"])
             if ev: ev[1].record()
-            return o
+            return o, ht
         return step, ["gdn"]
-    T, hv, hk, d = cfg["T"], cfg["hv"], cfg["hk"], 128
+    from torch_npu_ops_b200.pipeline import gdn_prefill
+    T, hv, hk = cfg["T"], cfg["hv"], cfg["hk"]
     state = torch.zeros(1, cfg["C"], 3, dtype=torch.bfloat16, device=dev)
     qsl = torch.tensor([0, T], dtype=torch.int32, device=dev)
 
     def step(inp, ev=None):
-        if ev: ev[0].record()
         state.zero_()  # fresh prefill: zero conv history
-        y = ops.npu_causal_conv1d_update_v2(inp["x"], state, c["weight"], True, c["bias"],
-                                            query_start_loc=qsl)
-        if ev: ev[1].record()
-        q = y[:, : hk * d].view(1, T, hk, d)
-        k = y[:, hk * d: 2 * hk * d].view(1, T, hk, d)
-        v = y[:, 2 * hk * d:].view(1, T, hv, d)
-        o, _ = ops.npu_chunk_gated_delta_rule(q, k, v, inp["g"], inp["beta"], None, None, True,
-                                              None, False, True)
-        if ev: ev[2].record()
-        out = ops.layer_norm_fwd(o.view(-1, d), c["norm_w"], None, 1e-6, inp["z"].view(-1, d), d,
-                                 True, True)
-        if ev: ev[3].record()
-        return out
+        _, _, ht, out = gdn_prefill(inp["x"], state, c["weight"], c["bias"], inp["g"], inp["beta"],
+                                    inp["initial_state"], inp["z"], c["norm_w"], hk, hv,
+                                    query_start_loc=qsl, events=ev)
+        return out, ht
     return step, ["conv", "gdn", "norm"]
 
 
@@ -200,8 +193,8 @@ def cpu_reference(kind, T_sample, reps=3, warmup=1):
             q = y[:, : hk * d].reshape(1, T_sample, hk, d)
             k = y[:, hk * d: 2 * hk * d].reshape(1, T_sample, hk, d)
             v = y[:, 2 * hk * d:].reshape(1, T_sample, hv, d)
-            o, _ = oracle.chunk_gated_delta_rule(q, k, v, w["g"], w["beta"], None, None, True,
-                                                 None, True)
+            o, _ = oracle.chunk_gated_delta_rule(q, k, v, w["g"], w["beta"], None,
+                                                 w["initial_state"], True, None, True)
             return oracle.layer_norm_fwd(o.reshape(-1, d), w["norm_w"], None, 1e-6,
                                          w["z"].reshape(-1, d), d, True, True)[0]
         sample = (f"conv->chunk GDN->gated RMSNorm oracle on the first {T_sample} tokens of the "
@@ -215,7 +208,10 @@ def cpu_reference(kind, T_sample, reps=3, warmup=1):
         ts.append(time.perf_counter() - t)
     med = statistics.median(ts)
     return {"value": T_sample / med, "unit": "tokens/s", "cores": torch.get_num_threads(),
-            "kind": "port", "sample": sample, "seconds_per_sample": med}
+            "kind": "port", "sample": sample, "seconds_per_sample": med,
+            "extrapolated": True,
+            "extrapolation": f"tokens/s = {T_sample} sample tokens / sample seconds; the oracle's "
+                             "cost is linear in tokens (chunk-serial over the sequence)"}
 
 
 # ------------------------------------------------------------------ main ----
@@ -358,8 +354,11 @@ def main():
     kind = a.workload
     T = a.tokens if kind == "cfg5" else 16384
     config = ({"workload": "cfg5: 1 x 65536-token prefill, conv1d(8192ch,w4,SiLU) -> chunked GDN "
-                           "(Hk16->Hv32, dk=dv=128, qk L2 in kernel) -> gated RMSNorm(g128)",
+                           "(Hk16->Hv32, dk=dv=128, qk L2 in kernel, initial state ~N(0,0.02), "
+                           "final state returned) -> gated RMSNorm(g128)",
                "tokens": T, "heads_per_gpu": 32 // max(1, world), "parallelism": f"head-shard x{world}",
+               "value_is": "whole-job tokens/s (all ranks; the sequence's 32 heads are split over "
+                           "them); value_per_gpu = value / n_gpus",
                "l2_flush": "inputs > L2 (>1 GB per step)"}
               if kind == "cfg5" else
               {"workload": "cfg3: 8 seqs / 16384 tokens varlen chunked GDN (Hk16->Hv32)",
@@ -395,8 +394,9 @@ def main():
         return
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        # gloo, not NCCL: nothing on the data path is a collective, and the
+        # barrier and the max over ranks of the CUDA-event times are host work
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
 
     cfg = build_cfg5(rank, world, T, dev) if kind == "cfg5" else build_cfg3(dev)
     step, stages = make_step(cfg, kind, dev)
@@ -434,7 +434,7 @@ def main():
     clk = clocks.stop()
     stage_ms = {s: statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs)
                 for j, s in enumerate(stages)}
-    t_local = torch.tensor([elapsed], device=dev)
+    t_local = torch.tensor([elapsed])
     if world > 1:
         torch.distributed.all_reduce(t_local, op=torch.distributed.ReduceOp.MAX)
     ms_step = t_local.item() / a.steps
@@ -468,19 +468,20 @@ def main():
     if not a.no_e2e:
         host = {n: t.pin_memory() for n, t in cfg["host"].items()}
         dbuf = {n: torch.empty_like(t) for n, t in cfg["dev"].items()}
-        out0 = step(inp)
-        hout = torch.empty(out0.shape, dtype=out0.dtype, pin_memory=True)
+        outs0 = step(inp)
         h2d = sum(t.numel() * t.element_size() for t in host.values())
-        d2h = hout.numel() * hout.element_size()
+        d2h = sum(t.numel() * t.element_size() for t in outs0)
 
-        # Every step uploads its own inputs and reads back its own result.
-        # The copies run on two copy streams (PCIe is full duplex) into two
-        # alternating device buffer sets, so step i+1's upload overlaps step
-        # i's compute and readback; compute itself stays on one stream.
+        # Every step uploads its own inputs and reads back its own results
+        # (the normed output and the final state).  The copies run on two copy
+        # streams (PCIe is full duplex) into two alternating device buffer
+        # sets, so step i+1's upload overlaps step i's compute and readback;
+        # compute itself stays on one stream.
         comp = torch.cuda.current_stream(dev)
         h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
         dbufs = [dbuf, {n: torch.empty_like(t) for n, t in cfg["dev"].items()}]
-        houts = [hout, torch.empty(out0.shape, dtype=out0.dtype, pin_memory=True)]
+        houts = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs0]
+                 for _ in range(2)]
         in_free = [torch.cuda.Event(), torch.cuda.Event()]
 
         def e2e_step(i):
@@ -492,14 +493,15 @@ def main():
                 loaded = torch.cuda.Event()
                 loaded.record(h2d_s)
             comp.wait_event(loaded)
-            out = step(dbufs[b])
+            outs = step(dbufs[b])
             in_free[b].record(comp)
             done = torch.cuda.Event()
             done.record(comp)
             with torch.cuda.stream(d2h_s):
                 d2h_s.wait_event(done)
-                houts[b].copy_(out, non_blocking=True)
-                out.record_stream(d2h_s)
+                for h, t in zip(houts[b], outs):
+                    h.copy_(t, non_blocking=True)
+                    t.record_stream(d2h_s)
 
         for i in range(2):
             e2e_step(i)
@@ -515,7 +517,7 @@ def main():
         t2.record(comp)
         torch.cuda.synchronize(dev)
         barrier()
-        te = torch.tensor([s2.elapsed_time(t2)], device=dev)
+        te = torch.tensor([s2.elapsed_time(t2)])
         if world > 1:
             torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
         e2e = {"value": T / (te.item() / a.steps / 1000.0), "unit": "tokens/s",
@@ -528,7 +530,8 @@ def main():
         cpu = cpu_reference(kind, a.cpu_sample)
 
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        line = {"metric": METRIC, "value": value, "value_per_gpu": value / world,
+                "unit": "tokens/s", "n_gpus": world,
                 "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step,
                 "higher_is_better": True, "scaling": "strong" if kind == "cfg5" else "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,

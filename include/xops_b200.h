@@ -261,10 +261,14 @@ XOPS_API int64_t xops_chunk_gated_delta_rule_workspace_size(int64_t B, int64_t T
  * counterpart in the reference.  Its scratch is one fixed 64 MiB array of
  * the library's own device memory, so problems whose
  * xops_chunk_gated_delta_rule_workspace_size() exceeds 64 MiB are rejected
- * with XOPS_ERR_WORKSPACE.  The array's address is looked up on the first
- * call on each device: make that call before any stream capture.  All calls
- * on a device share the array, so calls that may overlap on the GPU (e.g.
- * unordered streams) race; keep them ordered.  Arguments are those of
+ * with XOPS_ERR_WORKSPACE.  The array's address is looked up again on every
+ * call made outside stream capture (so a reset or a new context on the
+ * device is followed); a call made during capture reuses the last address
+ * found on that device, so make the first call on each device before any
+ * stream capture.  All calls on a device share the array, so calls that may
+ * overlap on the GPU (e.g. unordered streams) race; keep them ordered.  The
+ * 64 MiB is reserved on every device where the library's chunked-GDN module
+ * is loaded, whether or not this entry is called.  Arguments are those of
  * xops_chunk_gated_delta_rule minus the workspace. */
 XOPS_API int xops_chunk_gated_delta_rule_noalloc(const void* q, const void* k, const void* v,
                                         const float* g, const float* beta, const float* h0,

@@ -6,13 +6,19 @@ import torch.nn.functional as F
 
 def _taps(hist, xs, weight, bias):
     """Depthwise causal conv of ``xs`` [dim, L] preceded by ``hist``
-    [dim, width-1]; returns fp32 [dim, L]."""
+    [dim, width-1]; returns fp32 [dim, L]:
+    ``out[:, t] = bias + sum_j weight[:, j] * cat(hist, xs)[:, t + j]`` (the
+    valid cross-correlation the reference's ``F.conv1d(..., groups=dim)``
+    computes, written as width shifted multiply-adds)."""
     width = weight.shape[1]
     cat = torch.cat([hist.to(torch.float32), xs.to(torch.float32)], dim=-1)
-    out = F.conv1d(cat.unsqueeze(0), weight.to(torch.float32).unsqueeze(1),
-                   None if bias is None else bias.to(torch.float32),
-                   groups=weight.shape[0])[0]
-    return out[:, -xs.shape[-1]:] if width > 1 else out
+    L = xs.shape[-1]
+    w = weight.to(torch.float32)
+    out = (torch.zeros(cat.shape[0], L) if bias is None
+           else bias.to(torch.float32)[:, None].expand(-1, L).clone())
+    for j in range(width):
+        out += w[:, j:j + 1] * cat[:, j:j + L]
+    return out
 
 
 def causal_conv1d_update(x, conv_state, weight, bias=None, activation=True,

@@ -1,9 +1,10 @@
 """Generate the golden fixtures in this directory from the reference's OWN
 torch-native implementations.
 
-Runs only where the reference project is importable (the build container,
-``--ref-root``, default ``/root/reference``); the fixtures it writes travel
-with the repository, so nothing else ever needs the reference at run time.
+Runs only where the reference project is importable: ``--ref-root`` names its
+checkout (the directory holding ``triton_npu/``); the fixtures it writes
+travel with the repository, so nothing else ever needs the reference at run
+time.
 
 The reference's test modules import ``torch_npu`` and Ascend-only Triton
 extensions at module level; two empty stand-in modules are registered in
@@ -11,7 +12,7 @@ extensions at module level; two empty stand-in modules are registered in
 pure-torch reference functions are called -- never a Triton kernel.
 
 Fixtures: ``<op>.pt`` = ``{"cases": [{"name", "args": {...}, "out": {...}}]}``.
-Usage: ``python tests/golden/make_golden.py [--ref-root DIR]``.
+Usage: ``python tests/golden/make_golden.py --ref-root DIR [--only ...]``.
 """
 
 import argparse
@@ -466,7 +467,8 @@ def gen_qkvzba(m):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-root", default="/root/reference")
+    ap.add_argument("--ref-root", required=True,
+                    help="root of the reference checkout (the directory holding triton_npu/)")
     ap.add_argument("--only", default="",
                     help="comma-separated subset of: layernorm,l2norm,rope,conv,chunk,"
                          "recurrent,gating,sigmoid_gating,qkvzba,recurrent_spec,conv_slots,"

@@ -69,7 +69,9 @@ def test_layer_norm_vs_oracle(M, N, G, rms, bias, z, before, xdt, wdt):
     (assert_fp32 if xdt == torch.float32 else assert_bf16)(y, ry)
     assert_fp32(rstd, rrstd)
     if not rms:
-        assert_fp32(mean, rmean, tol=1e-3)
+        # a row mean comes out of a cancellation: its floor is set by the
+        # magnitude of the summed elements, not by the mean itself
+        assert_fp32(mean, rmean, scale=x.float().abs().max().item())
 
 
 def test_layer_norm_strided_rows():

@@ -32,6 +32,27 @@ def test_head_shards_partition_heads_and_channels(world):
     assert torch.equal(torch.sort(allc).values, torch.arange(workloads.CONV_DIM))
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_shard_inputs_are_slices_of_the_full_draw(world):
+    """Every rank's cfg-5 inputs are exactly its slice of the world-1 draw, so
+    one oracle run over all heads checks every shard (the GPU parity test of
+    the bench configuration relies on this)."""
+    T = 128
+    full = workloads.long_config5_shard(0, 1, T=T)
+    for r in range(world):
+        w = workloads.long_config5_shard(r, world, T=T)
+        v0, v1 = w["heads"]
+        ch = workloads.conv_channels(r, world)
+        assert torch.equal(w["x"], full["x"][:, ch])
+        assert torch.equal(w["weight"], full["weight"][ch])
+        assert torch.equal(w["bias"], full["bias"][ch])
+        assert torch.equal(w["g"], full["g"][:, :, v0:v1])
+        assert torch.equal(w["beta"], full["beta"][:, :, v0:v1])
+        assert torch.equal(w["z"], full["z"][:, v0:v1])
+        assert torch.equal(w["initial_state"], full["initial_state"][:, v0:v1])
+        assert torch.equal(w["norm_w"], full["norm_w"])
+
+
 def _pipeline(w, T):
     """conv1d -> chunk GDN (q/k L2 in the op) -> gated RMSNorm on one shard."""
     (v0, v1), (k0, k1) = w["heads"], w["k_heads"]
@@ -42,7 +63,8 @@ def _pipeline(w, T):
     q = y[:, : hk * d].reshape(1, T, hk, d)
     k = y[:, hk * d: 2 * hk * d].reshape(1, T, hk, d)
     v = y[:, 2 * hk * d:].reshape(1, T, hv, d)
-    o, _ = oracle.chunk_gated_delta_rule(q, k, v, w["g"], w["beta"], None, None, True, None, True)
+    o, _ = oracle.chunk_gated_delta_rule(q, k, v, w["g"], w["beta"], None, w["initial_state"], True,
+                                         None, True)
     out, _, _ = oracle.layer_norm_fwd(o.reshape(-1, d), w["norm_w"], None, 1e-6,
                                       w["z"].reshape(-1, d), d, True, True)
     return out.reshape(T, hv, d)

@@ -19,9 +19,13 @@ def _args(d, o, ht, T, N, hk, hv):
 
 
 @pytest.mark.gpu
-def test_noalloc_matches_workspace_entry_on_consecutive_calls():
+@pytest.mark.parametrize("lens,hk,hv", [
+    ([600, 401], 2, 4),   # short sequences: one chain pass per (sequence, head)
+    ([4096], 2, 4),       # one long sequence on few heads: the segment-parallel
+                          # chain, whose segment states sit at the scratch's tail
+])
+def test_noalloc_matches_workspace_entry_on_consecutive_calls(lens, hk, hv):
     lib = _lib.load()
-    lens, hk, hv = [600, 401], 2, 4
     w = workloads.chunk_config3(hk=hk, hv=hv, lengths=lens, seed=77)
     g = torch.Generator().manual_seed(78)  # raw q/k: the in-kernel L2 norm is exercised
     w["q"] = torch.randn(w["q"].shape, generator=g).to(torch.bfloat16)
@@ -31,6 +35,9 @@ def test_noalloc_matches_workspace_entry_on_consecutive_calls():
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
 
     need = lib.xops_chunk_gated_delta_rule_workspace_size(1, T, N, hk, hv, 128, 1, 1)
+    assert need <= 64 << 20
+    if len(lens) == 1:  # the plan is segmented: segment states follow the per-chunk part
+        assert need > (T // 64 + N) * hv * 32768 + 2 * T * hk * 128 * 2
     ws = torch.empty(need, dtype=torch.uint8, device="cuda")
     o_ref = torch.empty_like(d["v"])
     ht_ref = torch.empty(N, hv, 128, 128, device="cuda")

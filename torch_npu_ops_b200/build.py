@@ -50,7 +50,8 @@ def _deps(path, seen=None):
     with open(path) as f:
         text = f.read()
     for name in _INC.findall(text):
-        for d in (os.path.dirname(path), CSRC, INCLUDE):
+        for d in (os.path.dirname(path), CSRC, INCLUDE, os.path.join(CSRC, "runtime"),
+                  os.path.join(CSRC, "torch_api")):
             cand = os.path.join(d, name)
             if os.path.exists(cand):
                 _deps(cand, seen)
@@ -104,7 +105,7 @@ def build(force=False, jobs=None, verbose=False):
 
 
 TORCH_API_SRCS = ["torch_api/ops_impl.cpp", "torch_api/op_register.cpp",
-                  "runtime/kernel_registry.cpp"]
+                  "runtime/kernel_registry.cpp", "runtime/packed_launch.cpp"]
 
 
 def _ext_path():
@@ -124,7 +125,8 @@ def build_torch_api(force=False, jobs=None):
     objs = [os.path.join(BUILD, "api_" + os.path.basename(s)[:-4] + ".o") for s in srcs]
     cxx = os.environ.get("CXX", "g++")
     inc = ce.include_paths(device_type="cuda") + [sysconfig.get_paths()["include"], INCLUDE, CSRC,
-                                                  os.path.join(CSRC, "torch_api")]
+                                                  os.path.join(CSRC, "torch_api"),
+                                                  os.path.join(CSRC, "runtime")]
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     flags = ["-O2", "-std=c++17", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
              "-DTORCH_EXTENSION_NAME=_C", "-DTORCH_API_INCLUDE_EXTENSION_H", "-w"]

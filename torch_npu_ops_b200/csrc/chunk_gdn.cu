@@ -1588,13 +1588,24 @@ extern "C" int xops_device_error_count(void) {
 // memory, kStaticScratchBytes long.  Problems whose workspace would exceed
 // that size are rejected (XOPS_ERR_WORKSPACE) rather than partially served.
 //
-// The array's device address is looked up once per device with
-// cudaGetSymbolAddress, on the first call made on that device; make that
-// first call before any stream capture begins.  The array is shared by every
-// call on a device, so two calls whose kernels may overlap on the GPU (for
-// example on two streams without ordering between them) race on it; keep
-// such calls ordered.  No scratch byte needs to start at zero: every byte
-// the kernels read is written earlier in the same call.
+// The array's device address comes from cudaGetSymbolAddress, called with
+// the caller's device current.  It is looked up again on every call made
+// outside stream capture, so a new context on that device (after
+// cudaDeviceReset, or a non-primary driver context, both of which load the
+// module anew at another address) gets its own array.  A call made while its
+// stream is capturing reuses the address found by the last uncaptured call on
+// that device: make the first call on each device before any capture begins
+// (a captured call with no earlier uncaptured one is rejected).  The array is
+// shared by every call on a device, so two calls whose kernels may overlap on
+// the GPU (for example on two streams without ordering between them) race on
+// it; keep such calls ordered.  No scratch byte needs to start at zero: every
+// byte the kernels read is written earlier in the same call.
+//
+// The array belongs to this file's device module: whenever that module is
+// loaded on a device (on the first launch of any chunked-GDN kernel under
+// lazy module loading, at context creation under eager loading) the device
+// gives up kStaticScratchBytes for it until the process exits, whether or not
+// this entry point is ever called.
 // ---------------------------------------------------------------------------
 namespace {
 constexpr int64_t kStaticScratchBytes = 64ll << 20;  // 64 MiB
@@ -1603,7 +1614,7 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 std::mutex g_static_scratch_mu;
 void* g_static_scratch_ptr[kMaxDevices] = {};
 
-int static_scratch(void** out) {
+int static_scratch(cudaStream_t stream, void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess)
@@ -1612,8 +1623,13 @@ int static_scratch(void** out) {
   if (dev < 0 || dev >= kMaxDevices)
     return set_error(XOPS_ERR_UNSUPPORTED, "chunk_gated_delta_rule_noalloc: device %d >= %d", dev,
                      kMaxDevices);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(stream, &cs);
+  if (e != cudaSuccess)
+    return set_error(XOPS_ERR_CUDA, "chunk_gated_delta_rule_noalloc: cudaStreamIsCapturing: %s",
+                     cudaGetErrorString(e));
   std::lock_guard<std::mutex> lock(g_static_scratch_mu);
-  if (!g_static_scratch_ptr[dev]) {
+  if (cs == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess || !p)
@@ -1621,6 +1637,11 @@ int static_scratch(void** out) {
                        "chunk_gated_delta_rule_noalloc: cudaGetSymbolAddress of the scratch: %s",
                        cudaGetErrorString(e));
     g_static_scratch_ptr[dev] = p;
+  } else if (!g_static_scratch_ptr[dev]) {
+    return set_error(XOPS_ERR_INVALID_ARGUMENT,
+                     "chunk_gated_delta_rule_noalloc: the first call on device %d was made during "
+                     "stream capture; make one call outside capture first",
+                     dev);
   }
   *out = g_static_scratch_ptr[dev];
   return XOPS_OK;
@@ -1644,7 +1665,7 @@ extern "C" int xops_chunk_gated_delta_rule_noalloc(
                      "workspace instead",
                      (long long)need, (long long)kStaticScratchBytes);
   void* ws = nullptr;
-  if (int rc = static_scratch(&ws)) return rc;
+  if (int rc = static_scratch((cudaStream_t)stream, &ws)) return rc;
   return xops_chunk_gated_delta_rule(q, k, v, g, beta, h0, o, ht, cu_seqlens, B, T, N, Hg, H, K,
                                      V, q_token_stride, k_token_stride, v_token_stride, scale,
                                      use_qk_l2norm_in_kernel, ws, kStaticScratchBytes, stream);

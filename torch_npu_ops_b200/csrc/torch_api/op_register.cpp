@@ -2,16 +2,76 @@
 // schemas of the reference's pybind module npu_python_extension_lib
 // (npu_python_extension/op_register.cpp:52-63); the rest expose the
 // xllm::kernel::npu operators and the runtime registry.
+#include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
 #include "../runtime/kernel_registry.h"
 #include "ascendc_ops_api.h"
+#include "operation_factory.h"
 #include "triton_ops_api.h"
 
 namespace py = pybind11;
 namespace xn = xllm::kernel::npu;
 
 namespace {
+
+// The reference runtime's launch path, driven from Python for tests: packs
+// `args` (pairs of kind and value; kinds "ptr", "i32", "i64", "f32") with
+// ArgsBuilder in order, exactly as a reference call site's build_args lambda
+// does, and calls OperationBase::execute of the op bound to `kernel_name`.
+std::tuple<int64_t, std::string, int64_t> py_runtime_execute(const std::string& kernel_name,
+                                                             int32_t gx, int32_t gy, int32_t gz,
+                                                             const py::list& args,
+                                                             uintptr_t stream) {
+  auto& op = xn::OperationFactory::instance().by_kernel_name(kernel_name);
+  const int32_t rc = op.execute(reinterpret_cast<void*>(stream), gx, gy, gz,
+                                [&](xn::ArgsBuilder& ab) {
+    for (const auto& item : args) {
+      auto t = item.cast<py::tuple>();
+      const std::string kind = t[0].cast<std::string>();
+      if (kind == "ptr")
+        ab.add<void*>(t[1].is_none() ? nullptr
+                                     : reinterpret_cast<void*>(t[1].cast<uintptr_t>()));
+      else if (kind == "i32")
+        ab.add<int32_t>(t[1].cast<int32_t>());
+      else if (kind == "i64")
+        ab.add<int64_t>(t[1].cast<int64_t>());
+      else if (kind == "f32")
+        ab.add<float>(t[1].cast<float>());
+      else
+        throw std::invalid_argument("argument kind must be ptr, i32, i64 or f32");
+    }
+  });
+  return std::make_tuple((int64_t)rc, op.last_error(), (int64_t)op.last_args_size());
+}
+
+// The reference's group_size > 128 layer_norm_fwd launch
+// (triton_npu/torch_api/npu_triton_layernorm_fwd.cpp:295-333) written as a
+// caller of the reference runtime writes it: OperationFactory's
+// layer_norm_fwd() op, execute() with the same argument list, on the current
+// stream.  Returns (y, rstd).
+std::tuple<torch::Tensor, torch::Tensor> py_runtime_layer_norm_fwd(const torch::Tensor& x,
+                                                                   const torch::Tensor& weight,
+                                                                   const c10::optional<torch::Tensor>& z,
+                                                                   double eps, int64_t group_size) {
+  TORCH_CHECK(x.dim() == 2 && x.scalar_type() == torch::kBFloat16, "x must be [M, N] bf16");
+  const int64_t M = x.size(0), N = x.size(1), ngroups = N / group_size;
+  auto y = torch::empty_like(x);
+  auto rstd = torch::empty({ngroups * M}, x.options().dtype(torch::kFloat32));
+  void* zp = z.has_value() ? z->data_ptr() : nullptr;
+  const int32_t sx = (int32_t)x.stride(0), sy = (int32_t)y.stride(0),
+                sz = z.has_value() ? (int32_t)z->stride(0) : 0;
+  const int32_t gridX = (int32_t)std::max<int64_t>(1, std::min<int64_t>(40, M));
+  auto& op = xn::OperationFactory::instance().layer_norm_fwd();
+  const int32_t rc = op.execute(at::cuda::getCurrentCUDAStream().stream(), gridX,
+                                (int32_t)ngroups, 1, [&](xn::ArgsBuilder& ab) {
+    ab.constructArgs(x.data_ptr(), y.data_ptr(), weight.data_ptr(), zp, rstd.data_ptr(), sx, sy,
+                     sz, static_cast<int32_t>(M), static_cast<int32_t>(group_size),
+                     static_cast<float>(eps));
+  });
+  TORCH_CHECK(rc == 0, "OperationBase::execute failed (", rc, "): ", op.last_error());
+  return std::make_tuple(y, rstd);
+}
 
 std::tuple<torch::Tensor, torch::Tensor> py_gemma_rms_norm(const torch::Tensor& x,
                                                            const torch::Tensor& gamma,
@@ -132,5 +192,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("head_first") = false, py::arg("use_qk_l2norm_in_kernel") = false);
   m.def("kernel_entry_point", [](const std::string& name) {
     return xn::KernelRegistry::get_instance().entry_point(name);
+  });
+  m.def("_runtime_execute", &py_runtime_execute, py::arg("kernel_name"), py::arg("grid_x"),
+        py::arg("grid_y"), py::arg("grid_z"), py::arg("args"), py::arg("stream"));
+  m.def("_runtime_layer_norm_fwd", &py_runtime_layer_norm_fwd, py::arg("x"), py::arg("weight"),
+        py::arg("z"), py::arg("eps"), py::arg("group_size"));
+  m.def("_runtime_has_decoder", [](const std::string& name) {
+    return xn::has_packed_decoder(name);
   });
 }

@@ -1,0 +1,56 @@
+"""The GDN layer's prefill core as one call: causal conv1d -> chunked gated
+delta rule -> gated RMSNorm.
+
+This is the sequence the xLLM Qwen3-Next / Qwen3.5 GDN layer runs between
+its input and output projections, built only from this package's operators
+(the same calls a caller of the reference makes:
+``npu_causal_conv1d_update_v2`` -> ``npu_chunk_gated_delta_rule`` ->
+``layer_norm_fwd``).  ``bench.py`` times it and the bench-configuration
+parity test checks it, so both exercise exactly one code path.
+"""
+
+import torch
+
+from . import ops
+
+
+def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z, norm_weight,
+                num_k_heads, num_v_heads, head_dim=128, eps=1e-6, query_start_loc=None,
+                events=None):
+    """Runs one prefill of a GDN layer on the current CUDA stream.
+
+    x: [T, (2 num_k_heads + num_v_heads) head_dim] conv input (q | k | v
+    channel blocks), bf16.  conv_state: [N, channels, width - 1], updated in
+    place (a fresh prefill passes zeros).  g, beta: [1, T, num_v_heads] fp32.
+    initial_state: [N, num_v_heads, head_dim, head_dim] fp32 or None.
+    z: [T, num_v_heads, head_dim] gate of the output norm.  query_start_loc:
+    [N + 1] int32 on the device (None: one sequence of T tokens).
+    ``events``: optional list of 4 CUDA events recorded before the conv and
+    after each stage.
+
+    Returns (conv output [T, channels], o [1, T, num_v_heads, head_dim],
+    final state [N, num_v_heads, head_dim, head_dim] fp32, normed output
+    [T * num_v_heads, head_dim]).
+    """
+    T = x.shape[0]
+    hk, hv, d = num_k_heads, num_v_heads, head_dim
+    if query_start_loc is None:
+        query_start_loc = torch.tensor([0, T], dtype=torch.int32, device=x.device)
+    if events:
+        events[0].record()
+    y = ops.npu_causal_conv1d_update_v2(x, conv_state, conv_weight, True, conv_bias,
+                                        query_start_loc=query_start_loc)
+    if events:
+        events[1].record()
+    q = y[:, : hk * d].view(1, T, hk, d)
+    k = y[:, hk * d: 2 * hk * d].view(1, T, hk, d)
+    v = y[:, 2 * hk * d:].view(1, T, hv, d)
+    cu = None if query_start_loc.numel() == 2 else query_start_loc
+    o, ht = ops.npu_chunk_gated_delta_rule(q, k, v, g, beta, None, initial_state, True, cu, False,
+                                           True)
+    if events:
+        events[2].record()
+    out = ops.layer_norm_fwd(o.view(-1, d), norm_weight, None, eps, z.view(-1, d), d, True, True)
+    if events:
+        events[3].record()
+    return y, o, ht, out

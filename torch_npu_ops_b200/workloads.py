@@ -15,8 +15,9 @@ Configs:
      dk = dv = 128.
   4  decode batch 256: recurrent GDN, gated RMSNorm on [256*32, 128],
      layer_norm / gemma on [256, 2048].
-  5  single 65536-token sequence: conv -> chunk GDN -> gated RMSNorm, heads
-     sharded over ranks.
+  5  single 65536-token sequence: conv -> chunk GDN (initial state
+     ~N(0, 0.02), final state returned) -> gated RMSNorm, heads sharded over
+     ranks.
 """
 
 import math
@@ -177,10 +178,14 @@ def long_config5_shard(rank, world, T=65536, seed=5):
     for hh in range(v0, v1):
         gz = torch.Generator().manual_seed(seed * 1000 + 300 + hh)
         zs.append(torch.randn(T, d, generator=gz).to(torch.bfloat16))
+    # initial recurrent state of the one sequence, fp32 ~N(0, 0.02) as in
+    # config 3, drawn per value head so a shard never draws the others
+    h0 = torch.stack([0.02 * torch.randn(d, d, generator=torch.Generator().manual_seed(
+        seed * 1000 + 400 + hh)) for hh in range(v0, v1)])[None]
     return {"x": x, "weight": w_full[ch].contiguous(), "bias": b_full[ch].contiguous(),
             "g": gate_full[:, v0:v1].contiguous()[None], "beta": beta_full[:, v0:v1].contiguous()[None],
-            "z": torch.stack(zs, dim=1), "norm_w": nw, "heads": (v0, v1), "k_heads": (k0, k1),
-            "T": T}
+            "z": torch.stack(zs, dim=1), "norm_w": nw, "initial_state": h0, "heads": (v0, v1),
+            "k_heads": (k0, k1), "T": T}
 
 
 def chunk_flops(lengths, hv):
