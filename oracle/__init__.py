@@ -22,6 +22,7 @@ pin against and are marked "parity unpinned" in their docstrings:
 NeoX RoPE of ``split_rmsnorm_rope``.
 """
 
+from ._out import fp32_outputs  # noqa: F401
 from .norms import layer_norm_fwd, gemma_rms_norm, l2norm_last_dim  # noqa: F401
 from .rope import split_rmsnorm_rope, rope_inplace  # noqa: F401
 from .conv1d import (  # noqa: F401

@@ -3,6 +3,8 @@
 import torch
 import torch.nn.functional as F
 
+from . import _out
+
 
 def _taps(hist, xs, weight, bias):
     """Depthwise causal conv of ``xs`` [dim, L] preceded by ``hist``
@@ -51,7 +53,7 @@ def causal_conv1d_update(x, conv_state, weight, bias=None, activation=True,
             y = F.silu(y)
         out[b] = y
         conv_state[line].copy_(cat[:, -state_len:].to(conv_state.dtype))
-    out = out.to(x.dtype)
+    out = _out.out(out, x.dtype)
     return out.squeeze(-1) if squeeze else out
 
 
@@ -88,7 +90,7 @@ def causal_conv1d_varlen(x, conv_state, weight, bias=None, activation=True,
         out[s:e] = y.t()
         cat = torch.cat([hist.to(torch.float32), xs.to(torch.float32)], dim=-1)
         conv_state[line, :, :hist_len].copy_(cat[:, cat.shape[1] - hist_len:].to(conv_state.dtype))
-    return out.to(x.dtype)
+    return _out.out(out, x.dtype)
 
 
 def causal_conv1d_update_v2_slots(x, conv_state, weight, bias=None, activation=True,
@@ -142,4 +144,4 @@ def causal_conv1d_update_v2_slots(x, conv_state, weight, bias=None, activation=T
             shift = 1 if spec else n
             new = torch.cat([src[:, off + shift:off + shift + L - n], xs.to(torch.float32)], -1)
         conv_state[out_line, :, :L].copy_(new.to(conv_state.dtype))
-    return out.to(x.dtype)
+    return _out.out(out, x.dtype)

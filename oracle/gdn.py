@@ -9,6 +9,8 @@ computed in fp32.
 
 import torch
 
+from . import _out
+
 CHUNK = 64
 
 
@@ -268,7 +270,7 @@ def chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None,
             kt = kc * torch.exp((gl[:, None] - gc).clamp(max=0.0))[:, :, None]
             st = st * torch.exp(gl)[:, None, None] + kt.transpose(-1, -2) @ vn
         final[n] = st
-    return o.to(v.dtype), (final if output_final_state else None)
+    return _out.out(o, v.dtype), (final if output_final_state else None)
 
 
 def fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None,
@@ -340,7 +342,7 @@ def fused_recurrent_gated_delta_rule(q, k, v, g, beta=None, scale=None,
                 initial_state[slot].copy_(st.to(initial_state.dtype))
         else:
             target[n] = st.to(target.dtype)
-    return o.to(v.dtype), target
+    return _out.out(o, v.dtype), target
 
 
 def _softplus(x, beta=1.0, threshold=20.0):
@@ -362,7 +364,7 @@ def fused_gdn_gating(A_log, a, b, dt_bias, beta=1.0, threshold=20.0):
     """
     g = -torch.exp(A_log.to(torch.float32)) * _softplus(
         a.to(torch.float32) + dt_bias.to(torch.float32), beta, threshold)
-    beta_out = torch.sigmoid(b.to(torch.float32)).to(b.dtype)
+    beta_out = _out.out(torch.sigmoid(b.to(torch.float32)), b.dtype)
     return g[None], beta_out[None]
 
 
@@ -415,7 +417,7 @@ def fused_sigmoid_gating_delta_rule_update(A_log, a, dt_bias, q, k, v, b,
             o[t] = torch.einsum("hk,hkv->hv", qf[t], st)
         if slot >= 0:
             initial_state_source[slot].copy_(st.to(initial_state_source.dtype))
-    return o.reshape(bsz, t_all, hv, vd).to(q.dtype)
+    return _out.out(o.reshape(bsz, t_all, hv, vd), q.dtype)
 
 
 def fused_qkvzba_split_reshape_cat(mixed_qkvz, mixed_ba, num_heads_qk, num_heads_v, head_qk,

@@ -2,6 +2,8 @@
 
 import torch
 
+from . import _out
+
 
 def layer_norm_fwd(x, weight, bias=None, eps=1e-6, z=None, group_size=None,
                    norm_before_gate=True, is_rms_norm=False):
@@ -52,7 +54,7 @@ def layer_norm_fwd(x, weight, bias=None, eps=1e-6, z=None, group_size=None,
         y = y + bias.to(torch.float32)
     if z2 is not None and norm_before_gate:
         y = y * (z2 * torch.sigmoid(z2))
-    return y.to(x.dtype).reshape(shape), mean, rstd
+    return _out.out(y, x.dtype).reshape(shape), mean, rstd
 
 
 def gemma_rms_norm(x, gamma, eps=1e-6):
@@ -74,11 +76,11 @@ def gemma_rms_norm(x, gamma, eps=1e-6):
     rstd = torch.rsqrt((xf * xf).mean(dim=-1, keepdim=True) + eps)
     y = xf * rstd * (1.0 + gamma.reshape(-1).to(torch.float32))
     rstd_shape = tuple(lead) + (1,) * gd if x.dim() > gd else (1,) * x.dim()
-    return rstd.reshape(rstd_shape), y.to(x.dtype).reshape(x.shape)
+    return rstd.reshape(rstd_shape), _out.out(y, x.dtype).reshape(x.shape)
 
 
 def l2norm_last_dim(x, eps=1e-6):
     """``x * rsqrt(sum(x^2) + eps)`` over the last axis, computed in fp32 and
     cast back (``l2norm_ref``, triton_npu/triton_src/test_l2norm.py:95-98)."""
     xf = x.to(torch.float32)
-    return (xf * torch.rsqrt((xf * xf).sum(dim=-1, keepdim=True) + eps)).to(x.dtype)
+    return _out.out(xf * torch.rsqrt((xf * xf).sum(dim=-1, keepdim=True) + eps), x.dtype)

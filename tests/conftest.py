@@ -13,6 +13,20 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "slow: long-running case")
 
 
+@pytest.fixture(autouse=True)
+def _oracle_fp32_outputs(request):
+    """GPU parity tests compare a kernel's output with the oracle's value
+    before the final rounding to the output dtype (the stated bars are
+    against that fp32 value); the CPU pins of the oracle keep the
+    reference's rounding."""
+    if request.node.get_closest_marker("gpu") is None:
+        yield
+        return
+    import oracle
+    with oracle.fp32_outputs():
+        yield
+
+
 def pytest_collection_modifyitems(config, items):
     try:
         import torch

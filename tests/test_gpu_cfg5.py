@@ -4,18 +4,29 @@ in-kernel q/k L2 norm, initial state) -> gated RMSNorm, exactly as
 ``bench.py`` runs it (``torch_npu_ops_b200.pipeline.gdn_prefill``), on one GPU
 and on every rank's head shard of worlds 2, 4 and 8.
 
-References, all CPU oracle (restating the reference's torch code):
+References, all CPU oracle (restating the reference's torch code), taken
+before their final rounding to bf16:
   conv   ``causal_conv1d_update_ref_v2``
          (triton_npu/triton_src/test_causal_conv1d_update_v2.py:260)
   GDN    ``chunk_gated_delta_rule_ref``
          (triton_npu/triton_src/test_chunk_gated_delta_rule.py:134)
   norm   ``_golden_ref`` (triton_npu/triton_src/test_layernorm_fwd.py:1529)
 
-Each stage is checked on the GPU's own input to that stage, and the whole
-chain once more against the oracle run end to end from x (its intermediates
-rounded to bf16 where the reference's pipeline stores bf16).  The bars are
-the stated ones (``tests/parity.py``): bf16 outputs 2e-2 max-abs, final
-state 1e-3 relative.
+Each stage is checked on the GPU's own input to that stage at the stated
+bars (``tests/parity.py``): bf16 outputs 2e-2 max-abs, final state 1e-3
+relative.  The GDN output of this workload is small (row RMS ~3e-3 at the
+median, strongly decaying gates), so 2e-2 absolute says little about it: o
+is also held to 1e-2 relative (Frobenius), about ten times the bf16 rounding
+of o itself.
+
+The whole chain is checked once more against the oracle run end to end from
+x (its intermediates rounded to bf16 where the reference's pipeline stores
+bf16): o and the final state at the same bars.  The gated RMSNorm divides
+each (token, head) row by its RMS, so a one-ulp difference in the chain's
+bf16 intermediates moves a normalised element by up to ~1/RMS times that
+ulp (~300x at the median row); its end-to-end comparison is therefore the
+relative Frobenius error (1e-2), while its element-wise bar is checked on
+the GPU's own o.
 
 The shards take their inputs as slices of the world-1 draw (the CPU test
 ``test_shard_inputs_are_slices_of_the_full_draw`` shows that is what each
@@ -31,7 +42,9 @@ import pytest
 import torch
 
 import oracle
-from parity import assert_bf16, assert_state, maxabs
+from parity import assert_bf16, assert_state, rel_fro
+
+O_REL = 1e-2  # relative (Frobenius) bar on the small GDN output and on the end-to-end norm
 from torch_npu_ops_b200 import _lib, workloads
 from torch_npu_ops_b200.pipeline import gdn_prefill
 
@@ -80,17 +93,26 @@ def world1(full):
 
 @pytest.fixture(scope="module")
 def ref(full, world1):
-    """Stage oracles on the GPU's own stage inputs, and the oracle chain."""
+    """Stage oracles on the GPU's own stage inputs, and the oracle chain (a
+    module fixture is set up outside the per-test fp32-output context, so it
+    enters that context itself)."""
+    with oracle.fp32_outputs():
+        return _reference(full, world1)
+
+
+def _reference(full, world1):
     hk, hv = workloads.QK_HEADS, workloads.V_HEADS
     st = torch.zeros(1, full["x"].shape[1], 3, dtype=torch.bfloat16)
     y = oracle.causal_conv1d_varlen(full["x"], st, full["weight"], full["bias"], True,
                                     torch.tensor([0, T], dtype=torch.int32))
     o, ht = _oracle_gdn(world1["y"], full, hk, hv)
     out = _oracle_norm(world1["o"], full, hv)
-    if torch.equal(y, world1["y"]):
+    # the oracle chain stores bf16 between the stages, as the reference's does
+    y16 = y.to(torch.bfloat16)
+    if torch.equal(y16, world1["y"]):
         o_c, ht_c = o, ht
     else:
-        o_c, ht_c = _oracle_gdn(y, full, hk, hv)
+        o_c, ht_c = _oracle_gdn(y16, full, hk, hv)
     out_c = _oracle_norm(o_c.to(torch.bfloat16), full, hv)
     return {"y": y, "state": st, "o": o, "ht": ht, "out": out, "o_c": o_c, "ht_c": ht_c,
             "out_c": out_c}
@@ -114,6 +136,7 @@ def test_cfg5_conv(world1, ref):
 
 def test_cfg5_gdn(world1, ref):
     assert_bf16(world1["o"], ref["o"])
+    assert rel_fro(world1["o"], ref["o"]) <= O_REL
     assert_state(world1["ht"], ref["ht"])
 
 
@@ -122,8 +145,10 @@ def test_cfg5_gated_norm(world1, ref):
 
 
 def test_cfg5_end_to_end(world1, ref):
-    assert_bf16(world1["out"], ref["out_c"])
+    assert_bf16(world1["o"], ref["o_c"])
+    assert rel_fro(world1["o"], ref["o_c"]) <= O_REL
     assert_state(world1["ht"], ref["ht_c"])
+    assert rel_fro(world1["out"], ref["out_c"]) <= O_REL
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
@@ -139,7 +164,9 @@ def test_cfg5_head_shards(full, world1, ref, world):
         got = _run(w, k1 - k0, v1 - v0)
         assert torch.equal(got["y"], world1["y"][:, ch]), f"rank {r}: conv output differs"
         assert_bf16(got["o"], ref["o"][:, :, v0:v1])
+        assert rel_fro(got["o"], ref["o"][:, :, v0:v1]) <= O_REL
         assert_state(got["ht"], ref["ht"][:, v0:v1])
-        assert_bf16(got["out"], ref["out_c"][:, v0:v1])
+        with oracle.fp32_outputs():
+            assert_bf16(got["out"], _oracle_norm(got["o"], w, v1 - v0))
         # against the world-1 GPU result: same maths, other segment plan
-        assert maxabs(got["o"], world1["o"][:, :, v0:v1]) <= 2e-2
+        assert rel_fro(got["o"], world1["o"][:, :, v0:v1]) <= O_REL
