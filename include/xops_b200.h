@@ -135,6 +135,22 @@ XOPS_API int xops_causal_conv1d_varlen(const void* x, void* conv_state, const vo
                               int64_t num_cache_lines, int silu, int32_t pad_slot_id, int dtype,
                               void* stream);
 
+/* The varlen prefill conv of xops_causal_conv1d_varlen with the GDN layer's
+ * q/k L2 normalisation fused into its output: the first l2_channels output
+ * channels (whole 128-channel heads: the q and k blocks of the layer's conv
+ * output) are written as y / sqrt(sum y^2 + l2_eps) over each head, computed
+ * from the bf16-rounded conv output, exactly as npu_l2norm_last_dim would
+ * compute it in a separate pass (npu_triton_chunk_gated_delta_rule.cpp:608-609
+ * calls it on q and k when use_qk_l2norm_in_kernel).  The chunked rule then
+ * runs with use_qk_l2norm_in_kernel = 0 on views of this output.  16-bit
+ * activations, dim a multiple of 128.  This fused form has no single
+ * counterpart in the reference, which runs the two steps separately. */
+XOPS_API int xops_causal_conv1d_varlen_qk_l2norm(
+    const void* x, void* conv_state, const void* weight, const void* bias,
+    const int32_t* query_start_loc, const int32_t* conv_state_indices, void* out, int64_t batch,
+    int64_t total_tokens, int64_t dim, int64_t width, int64_t num_cache_lines, int silu,
+    int32_t pad_slot_id, int dtype, int64_t l2_channels, float l2_eps, void* stream);
+
 /* De-interleave of the GDN input projections.  mixed_qkvz [rows, nqk *
  * (2 hqk + 2 r hv)] holds per key head q | k | v (r heads) | z (r heads),
  * r = num_heads_v / num_heads_qk in [1, 4]; mixed_ba [rows, nqk * 2r] holds

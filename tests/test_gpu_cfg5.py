@@ -1,13 +1,15 @@
 """GPU parity of the bench configuration itself (config 5): one 65,536-token
-sequence through causal conv1d -> chunked gated delta rule (Hk 16 -> Hv 32,
-in-kernel q/k L2 norm, initial state) -> gated RMSNorm, exactly as
-``bench.py`` runs it (``torch_npu_ops_b200.pipeline.gdn_prefill``), on one GPU
-and on every rank's head shard of worlds 2, 4 and 8.
+sequence through causal conv1d (its q/k blocks L2-normalised in the same
+kernel) -> chunked gated delta rule (Hk 16 -> Hv 32, initial state) -> gated
+RMSNorm, exactly as ``bench.py`` runs it
+(``torch_npu_ops_b200.pipeline.gdn_prefill``), on one GPU and on every rank's
+head shard of worlds 2, 4 and 8.
 
 References, all CPU oracle (restating the reference's torch code), taken
 before their final rounding to bf16:
   conv   ``causal_conv1d_update_ref_v2``
-         (triton_npu/triton_src/test_causal_conv1d_update_v2.py:260)
+         (triton_npu/triton_src/test_causal_conv1d_update_v2.py:260), then
+         ``l2norm_ref`` (triton_npu/triton_src/test_l2norm.py:95) on q and k
   GDN    ``chunk_gated_delta_rule_ref``
          (triton_npu/triton_src/test_chunk_gated_delta_rule.py:134)
   norm   ``_golden_ref`` (triton_npu/triton_src/test_layernorm_fwd.py:1529)
@@ -66,12 +68,19 @@ def _run(w, hk, hv):
             "state": st.cpu()}
 
 
-def _oracle_gdn(y, w, hk, hv):
+def _oracle_gdn(y, w, hk, hv, l2):
     q = y[:, : hk * D].reshape(1, T, hk, D)
     k = y[:, hk * D: 2 * hk * D].reshape(1, T, hk, D)
     v = y[:, 2 * hk * D:].reshape(1, T, hv, D)
     return oracle.chunk_gated_delta_rule(q, k, v, w["g"], w["beta"], None, w["initial_state"], True,
-                                         None, True)
+                                         None, l2)
+
+
+def _oracle_conv_l2(y16, hk):
+    """The conv output as the GPU writes it: the q and k blocks (bf16 conv
+    output) L2-normalised per 128-channel head, the v block as it is."""
+    qk = oracle.l2norm_last_dim(y16[:, : 2 * hk * D].reshape(-1, D), 1e-6).reshape(T, -1)
+    return torch.cat([qk.float(), y16[:, 2 * hk * D:].float()], dim=1)
 
 
 def _oracle_norm(o_bf16, w, hv):
@@ -105,16 +114,18 @@ def _reference(full, world1):
     st = torch.zeros(1, full["x"].shape[1], 3, dtype=torch.bfloat16)
     y = oracle.causal_conv1d_varlen(full["x"], st, full["weight"], full["bias"], True,
                                     torch.tensor([0, T], dtype=torch.int32))
-    o, ht = _oracle_gdn(world1["y"], full, hk, hv)
-    out = _oracle_norm(world1["o"], full, hv)
     # the oracle chain stores bf16 between the stages, as the reference's does
     y16 = y.to(torch.bfloat16)
-    if torch.equal(y16, world1["y"]):
-        o_c, ht_c = o, ht
-    else:
-        o_c, ht_c = _oracle_gdn(y16, full, hk, hv)
+    # stage references: the conv (+ q/k L2 norm) on x, the GDN on the GPU's
+    # own (already normalised) conv output, the norm on the GPU's own o
+    y_ref = torch.cat([_oracle_conv_l2(y16, hk)[:, : 2 * hk * D], y[:, 2 * hk * D:]], dim=1)
+    o, ht = _oracle_gdn(world1["y"], full, hk, hv, False)
+    out = _oracle_norm(world1["o"], full, hv)
+    # the chain as the reference runs it: conv -> chunked rule with its
+    # in-kernel q/k L2 norm -> gated norm
+    o_c, ht_c = _oracle_gdn(y16, full, hk, hv, True)
     out_c = _oracle_norm(o_c.to(torch.bfloat16), full, hv)
-    return {"y": y, "state": st, "o": o, "ht": ht, "out": out, "o_c": o_c, "ht_c": ht_c,
+    return {"y": y_ref, "state": st, "o": o, "ht": ht, "out": out, "o_c": o_c, "ht_c": ht_c,
             "out_c": out_c}
 
 

@@ -302,3 +302,40 @@ def test_rope_inplace_cpp():
     C.rope_inplace(x1, _to(sin), _to(cos), 64)
     ops.rope_inplace(x2, _to(sin), _to(cos), 64)
     assert torch.equal(x1, x2)
+
+
+@pytest.mark.parametrize("lens,dim,qk,dt", [
+    ([300, 5, 1000], 1024, 512, torch.bfloat16),    # ragged, half the channels normalised
+    ([4096, 2048], 8192, 4096, torch.bfloat16),     # the GDN layer's channel split
+    ([129, 64], 768, 256, torch.float16),
+])
+def test_conv_varlen_qk_l2norm(lens, dim, qk, dt):
+    """The fused conv + q/k L2 norm against the reference's two steps: the conv
+    output rounded to the activation dtype, then x / sqrt(sum x^2 + eps) per
+    128-channel head (l2norm_ref, test_l2norm.py:95) on the first qk channels."""
+    g = torch.Generator().manual_seed(dim + qk)
+    T = sum(lens)
+    x = torch.randn(T, dim, generator=g).to(dt)
+    wt = (0.5 * torch.randn(dim, 4, generator=g)).to(dt)
+    b = (0.5 * torch.randn(dim, generator=g)).to(dt)
+    st = torch.randn(len(lens), dim, 3, generator=g).to(dt)
+    qsl = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    st_d = st.clone().to(DEV)
+    y = ops.causal_conv1d_varlen_qk_l2norm(x.to(DEV), st_d, wt.to(DEV), b.to(DEV), qsl.to(DEV), qk)
+    st_ref = st.clone()
+    with oracle.fp32_outputs():
+        ref = oracle.causal_conv1d_varlen(x, st_ref, wt, b, True, qsl)
+    y16 = ref.to(dt)  # the reference stores the conv output in the activation dtype
+    with oracle.fp32_outputs():
+        qk_ref = oracle.l2norm_last_dim(y16[:, :qk].reshape(-1, 128), 1e-6).reshape(T, qk)
+    assert_bf16(y[:, :qk], qk_ref)
+    assert_bf16(y[:, qk:], ref[:, qk:])
+    assert torch.equal(st_d.cpu(), st_ref)
+    # the un-normalised channels are exactly those of the plain conv
+    st2 = st.clone().to(DEV)
+    y2 = ops.npu_causal_conv1d_update_v2(x.to(DEV), st2, wt.to(DEV), True, b.to(DEV),
+                                         query_start_loc=qsl.to(DEV))
+    assert torch.equal(y[:, qk:], y2[:, qk:])
+    if dt == torch.bfloat16:  # the separate l2norm operator takes bf16, as the reference's
+        assert_bf16(y[:, :qk],
+                    ops.npu_l2norm_last_dim(y2[:, :qk].reshape(-1, 128), 1e-6).reshape(T, qk))

@@ -30,6 +30,8 @@ SIGNATURES = {
                                   _i64, _i64, _i64, _int, _i32, _int, _p],
     "xops_causal_conv1d_varlen": [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _int,
                                   _i32, _int, _p],
+    "xops_causal_conv1d_varlen_qk_l2norm": [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
+                                            _i64, _int, _i32, _int, _i64, _f, _p],
     "xops_causal_conv1d_update_v2_slots": [_p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _i64,
                                            _i64, _i64, _i64, _i64, _int, _i32, _int, _p],
     "xops_fused_recurrent_gated_delta_rule": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64,

@@ -404,7 +404,8 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
     const __grid_constant__ CUtensorMap xmap, const T* __restrict__ x, T* __restrict__ state,
     const T* __restrict__ weight, const T* __restrict__ bias, const int32_t* __restrict__ qsl,
     const int32_t* __restrict__ slots, T* __restrict__ out, int nseq, int64_t dim,
-    int64_t tiles_per_slab, int64_t total_tiles, int box_c, bool silu, int32_t pad_slot) {
+    int64_t tiles_per_slab, int64_t total_tiles, int box_c, bool silu, int32_t pad_slot,
+    int64_t l2_channels, float l2_eps) {
   constexpr int H = W - 1;
   extern __shared__ unsigned char rb_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(
@@ -518,6 +519,10 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
       const int64_t tb = ti.t0 + tg * 16;
       const int64_t nvalid = ti.send - tb;  // tokens of this group inside the sequence
       T* dst = out + tb * dim + c0;
+      // the warp's 128 channels are one q or k head of the GDN layer: its
+      // output row is L2-normalised (x / sqrt(sum x^2 + eps) over the head,
+      // from the rounded conv output, as the separate l2norm pass would do)
+      const bool l2 = c0 < l2_channels;
 #pragma unroll
       for (int u = 0; u < 16; ++u) {
         const uint2 raw = *reinterpret_cast<const uint2*>(stg + (H + u) * rstride);
@@ -531,6 +536,13 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
           for (int j = 0; j < H; ++j) a = ffma2(hist[j][p], w[p][j], a);
           a = ffma2(cur[p], w[p][H], a);
           pk[p] = pack2<T>(silu ? silu2_lowp(a) : a);
+        }
+        if (l2) {
+          const float2 r0 = unpack2<T>(pk[0]), r1 = unpack2<T>(pk[1]);
+          const float rn =
+              rsqrtf(warp_sum(r0.x * r0.x + r0.y * r0.y + r1.x * r1.x + r1.y * r1.y) + l2_eps);
+          pk[0] = pack2<T>(make_float2(r0.x * rn, r0.y * rn));
+          pk[1] = pack2<T>(make_float2(r1.x * rn, r1.y * rn));
         }
         if (u < nvalid) *reinterpret_cast<uint2*>(dst + (int64_t)u * dim) = packed;
 #pragma unroll
@@ -585,7 +597,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 conv_map_encoder() {
 template <typename T>
 int launch_varlen_tma(int W, const void* x, void* state, const void* w, const void* b,
                       const int32_t* qsl, const int32_t* slots, void* out, int nseq,
-                      int64_t total, int64_t dim, bool silu, int32_t pad, cudaStream_t st) {
+                      int64_t total, int64_t dim, bool silu, int32_t pad, cudaStream_t st,
+                      int64_t l2_channels = 0, float l2_eps = 0.f) {
   auto enc = conv_map_encoder();
   if (!enc) return set_error(XOPS_ERR_CUDA, "causal_conv1d_varlen: cuTensorMapEncodeTiled is unavailable");
   CUtensorMap m;
@@ -621,7 +634,7 @@ int launch_varlen_tma(int W, const void* x, void* state, const void* w, const vo
       return set_error(XOPS_ERR_CUDA, "causal_conv1d_varlen: shared-memory attribute failed"); \
     kern<<<grid, RB_NT, RB_SMEM, st>>>(m, (const T*)x, (T*)state, (const T*)w, (const T*)b,    \
                                        qsl, slots, (T*)out, nseq, dim, tiles_per_slab,          \
-                                       total_tiles, box_c, silu, pad);                          \
+                                       total_tiles, box_c, silu, pad, l2_channels, l2_eps);     \
     return check_launch("causal_conv1d_varlen");                                               \
   }
     XOPS_CT(2) XOPS_CT(3) XOPS_CT(4) XOPS_CT(5) XOPS_CT(6)
@@ -806,6 +819,38 @@ extern "C" int xops_causal_conv1d_varlen(const void* x, void* conv_state, const 
                                     conv_state_indices, out, (int)batch, tiles, dim, silu != 0,
                                     pad_slot_id, st);
   }
+}
+
+extern "C" int xops_causal_conv1d_varlen_qk_l2norm(
+    const void* x, void* conv_state, const void* weight, const void* bias,
+    const int32_t* query_start_loc, const int32_t* conv_state_indices, void* out, int64_t batch,
+    int64_t total_tokens, int64_t dim, int64_t width, int64_t num_cache_lines, int silu,
+    int32_t pad_slot_id, int dtype, int64_t l2_channels, float l2_eps, void* stream) {
+  XOPS_REQUIRE(batch >= 0 && total_tokens >= 0 && dim > 0, "causal_conv1d_varlen_qk_l2norm: bad shape");
+  XOPS_REQUIRE(width >= 2 && width <= 6,
+               "causal_conv1d_varlen_qk_l2norm expects width in [2, 6], got %lld", (long long)width);
+  XOPS_REQUIRE(l2_channels >= 0 && l2_channels % 128 == 0 && l2_channels <= dim && dim % 128 == 0,
+               "causal_conv1d_varlen_qk_l2norm: the normalised channels must be whole 128-channel "
+               "heads at the front of a dim that is a multiple of 128 (got %lld of %lld)",
+               (long long)l2_channels, (long long)dim);
+  XOPS_UNSUPPORTED(dtype == XOPS_BF16 || dtype == XOPS_F16,
+                   "causal_conv1d_varlen_qk_l2norm: 16-bit activations only");
+  XOPS_REQUIRE(conv_state_indices || num_cache_lines >= batch,
+               "causal_conv1d_varlen_qk_l2norm: conv_state has fewer lines than sequences");
+  if (batch == 0 || total_tokens == 0) return XOPS_OK;
+  XOPS_REQUIRE(x && conv_state && weight && query_start_loc && out,
+               "causal_conv1d_varlen_qk_l2norm: null pointer");
+  XOPS_REQUIRE(aligned16(x) && aligned16(out),
+               "causal_conv1d_varlen_qk_l2norm: x/out must be 16-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == XOPS_BF16)
+    return launch_varlen_tma<__nv_bfloat16>((int)width, x, conv_state, weight, bias,
+                                            query_start_loc, conv_state_indices, out, (int)batch,
+                                            total_tokens, dim, silu != 0, pad_slot_id, st,
+                                            l2_channels, l2_eps);
+  return launch_varlen_tma<__half>((int)width, x, conv_state, weight, bias, query_start_loc,
+                                   conv_state_indices, out, (int)batch, total_tokens, dim,
+                                   silu != 0, pad_slot_id, st, l2_channels, l2_eps);
 }
 
 extern "C" int xops_causal_conv1d_update(const void* x, void* conv_state, const void* weight,

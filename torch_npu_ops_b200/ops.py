@@ -340,6 +340,44 @@ def npu_causal_conv1d_update_v2(x, conv_state, weight, activation=True, bias=Non
     return out.squeeze(-1) if unsq else out
 
 
+def causal_conv1d_varlen_qk_l2norm(x, conv_state, weight, bias, query_start_loc, qk_channels,
+                                   activation=True, eps=1e-6, conv_state_indices=None,
+                                   pad_slot_id=-1):
+    """The GDN layer's prefill conv with its q/k L2 normalisation fused in.
+
+    Computes ``npu_causal_conv1d_update_v2(x, conv_state, weight, activation,
+    bias, conv_state_indices, query_start_loc)`` (x [num_tokens, dim]
+    token-major, conv_state updated IN PLACE) and, in the same kernel,
+    L2-normalises the first ``qk_channels`` output channels per 128-channel
+    head, as ``npu_l2norm_last_dim`` would on the q and k blocks
+    (npu_triton_chunk_gated_delta_rule.cpp:608-609).  Feed views of the
+    result to ``npu_chunk_gated_delta_rule`` with
+    ``use_qk_l2norm_in_kernel=False``.  bf16 / fp16 only."""
+    _cuda(x, conv_state, weight, bias, query_start_loc, conv_state_indices)
+    _check(x.dim() == 2 and weight.dim() == 2 and conv_state.dim() == 3,
+           "causal_conv1d_varlen_qk_l2norm expects x [tokens, dim], weight [dim, width], "
+           "conv_state [lines, dim, width - 1]")
+    _check(x.dtype in (torch.bfloat16, torch.float16),
+           "causal_conv1d_varlen_qk_l2norm expects bf16 or fp16 activations")
+    dim, width = x.size(1), weight.size(1)
+    _check(weight.size(0) == dim and conv_state.size(1) == dim and conv_state.size(2) >= width - 1,
+           "causal_conv1d_varlen_qk_l2norm: shape mismatch")
+    _check(conv_state.is_contiguous() and conv_state.dtype == x.dtype,
+           "causal_conv1d_varlen_qk_l2norm: conv_state must be contiguous in x's dtype")
+    xv = x.contiguous()
+    qsl = _i32(query_start_loc)
+    idx = _i32(conv_state_indices)
+    batch = qsl.numel() - 1
+    b = bias.to(x.dtype).contiguous() if bias is not None else None
+    out = torch.empty_like(xv)
+    _lib.call("xops_causal_conv1d_varlen_qk_l2norm", xv.data_ptr(), conv_state.data_ptr(),
+              weight.to(x.dtype).contiguous().data_ptr(), _ptr(b), qsl.data_ptr(), _ptr(idx),
+              out.data_ptr(), batch, xv.size(0), dim, width, conv_state.size(0),
+              int(bool(activation)), int(pad_slot_id), _dt(xv, "causal_conv1d_varlen_qk_l2norm"),
+              int(qk_channels), float(eps), _stream(x))
+    return out
+
+
 # ---------------------------------------------------------- gated delta rule
 def _seq_info(q, cu_seqlens):
     b, t = q.shape[0], q.shape[1]

@@ -2,10 +2,12 @@
 delta rule -> gated RMSNorm.
 
 This is the sequence the xLLM Qwen3-Next / Qwen3.5 GDN layer runs between
-its input and output projections, built only from this package's operators
-(the same calls a caller of the reference makes:
-``npu_causal_conv1d_update_v2`` -> ``npu_chunk_gated_delta_rule`` ->
-``layer_norm_fwd``).  ``bench.py`` times it and the bench-configuration
+its input and output projections.  A caller of the reference makes the calls
+``npu_causal_conv1d_update_v2`` -> ``npu_chunk_gated_delta_rule(...,
+use_qk_l2norm_in_kernel=True)`` -> ``layer_norm_fwd``; here the q/k L2
+normalisation moves out of the chunked rule into the conv kernel's output
+(``causal_conv1d_varlen_qk_l2norm``), which saves one read and one write of
+q and k.  ``bench.py`` times this function and the bench-configuration
 parity test checks it, so both exercise exactly one code path.
 """
 
@@ -28,8 +30,9 @@ def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z
     ``events``: optional list of 4 CUDA events recorded before the conv and
     after each stage.
 
-    Returns (conv output [T, channels], o [1, T, num_v_heads, head_dim],
-    final state [N, num_v_heads, head_dim, head_dim] fp32, normed output
+    Returns (conv output [T, channels] with its q and k blocks
+    L2-normalised per head, o [1, T, num_v_heads, head_dim], final state
+    [N, num_v_heads, head_dim, head_dim] fp32, normed output
     [T * num_v_heads, head_dim]).
     """
     T = x.shape[0]
@@ -38,8 +41,8 @@ def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z
         query_start_loc = torch.tensor([0, T], dtype=torch.int32, device=x.device)
     if events:
         events[0].record()
-    y = ops.npu_causal_conv1d_update_v2(x, conv_state, conv_weight, True, conv_bias,
-                                        query_start_loc=query_start_loc)
+    y = ops.causal_conv1d_varlen_qk_l2norm(x, conv_state, conv_weight, conv_bias, query_start_loc,
+                                           2 * hk * d)
     if events:
         events[1].record()
     q = y[:, : hk * d].view(1, T, hk, d)
@@ -47,7 +50,7 @@ def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z
     v = y[:, 2 * hk * d:].view(1, T, hv, d)
     cu = None if query_start_loc.numel() == 2 else query_start_loc
     o, ht = ops.npu_chunk_gated_delta_rule(q, k, v, g, beta, None, initial_state, True, cu, False,
-                                           True)
+                                           False)
     if events:
         events[2].record()
     out = ops.layer_norm_fwd(o.view(-1, d), norm_weight, None, eps, z.view(-1, d), d, True, True)
