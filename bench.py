@@ -37,9 +37,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "GDN prefill tokens/s/GPU; norm/RoPE/conv1d HBM GB/s vs B200 peak"
-# 1,466 MB of DRAM traffic for 16,384 tokens x 32 value heads (q/k L2 pre-pass,
-# prep, both chain phases, combine), measured by ncu
-GDN_DRAM_BYTES_PER_TOKEN_HEAD = 1.466e9 / (16384 * 32)
+# 1,305 MB of DRAM traffic for 16,384 tokens x 32 value heads (prep, both
+# chain phases, combine), measured by ncu (profiles/gdn_cfg5_traffic.md)
+GDN_DRAM_BYTES_PER_TOKEN_HEAD = 1.305e9 / (16384 * 32)
 
 
 def _peaks():
@@ -361,9 +361,10 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     kind = a.workload
     T = a.tokens if kind == "cfg5" else 16384
-    config = ({"workload": "cfg5: 1 x 65536-token prefill, conv1d(8192ch,w4,SiLU) -> chunked GDN "
-                           "(Hk16->Hv32, dk=dv=128, qk L2 in kernel, initial state ~N(0,0.02), "
-                           "final state returned) -> gated RMSNorm(g128)",
+    config = ({"workload": "cfg5: 1 x 65536-token prefill, conv1d(8192ch,w4,SiLU; q/k blocks "
+                           "L2-normalised in the conv kernel) -> chunked GDN (Hk16->Hv32, "
+                           "dk=dv=128, initial state ~N(0,0.02), final state returned) -> gated "
+                           "RMSNorm(g128)",
                "tokens": T, "heads_per_gpu": 32 // max(1, world), "parallelism": f"head-shard x{world}",
                "value_is": "whole-job tokens/s (all ranks; the sequence's 32 heads are split over "
                            "them); value_per_gpu = value / n_gpus",
@@ -452,12 +453,11 @@ def main():
     flops = workloads.chunk_flops(cfg["lengths"], cfg["hv"])
     gdn_ms = stage_ms["gdn"]
     achieved = flops / (gdn_ms / 1000.0) / 1e12
-    # DRAM bytes (read + write) of the GDN stage's kernels (q/k L2 pre-pass,
-    # prep, both chain phases, combine) from one ncu capture of the cfg5 shape
-    # at 16,384 tokens, per (token, value head), scaled by this run's tokens
-    # and heads.
+    # DRAM bytes (read + write) of the GDN stage's kernels (prep, both chain
+    # phases, combine) from one ncu capture of the cfg5 shape at 16,384
+    # tokens, per (token, value head), scaled by this run's tokens and heads.
     traffic = GDN_DRAM_BYTES_PER_TOKEN_HEAD * cfg["T"] * cfg["hv"]
-    roofline = {"kernel": "chunked GDN stage (q/k L2 + prep + chain + combine)", "bound": "tensor",
+    roofline = {"kernel": "chunked GDN stage (prep + chain + combine)", "bound": "tensor",
                 "achieved": achieved,
                 "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops_sustained"],

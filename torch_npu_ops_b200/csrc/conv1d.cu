@@ -523,37 +523,57 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
       // output row is L2-normalised (x / sqrt(sum x^2 + eps) over the head,
       // from the rounded conv output, as the separate l2norm pass would do)
       const bool l2 = c0 < l2_channels;
+      // tokens in pairs: the two rows' sums of squares reduce across the
+      // warp together, so their shuffle latencies overlap
 #pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(stg + (H + u) * rstride);
-        float2 cur[2] = {unpack2<T>(raw.x), unpack2<T>(raw.y)};
-        uint2 packed;
-        uint32_t* pk = &packed.x;
+      for (int ug = 0; ug < 16; ug += 2) {
+        uint2 packed[2];
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          float2 a = b[p];
+        for (int du = 0; du < 2; ++du) {
+          const int u = ug + du;
+          const uint2 raw = *reinterpret_cast<const uint2*>(stg + (H + u) * rstride);
+          float2 cur[2] = {unpack2<T>(raw.x), unpack2<T>(raw.y)};
+          uint32_t* pk = &packed[du].x;
 #pragma unroll
-          for (int j = 0; j < H; ++j) a = ffma2(hist[j][p], w[p][j], a);
-          a = ffma2(cur[p], w[p][H], a);
-          pk[p] = pack2<T>(silu ? silu2_lowp(a) : a);
+          for (int p = 0; p < 2; ++p) {
+            float2 a = b[p];
+#pragma unroll
+            for (int j = 0; j < H; ++j) a = ffma2(hist[j][p], w[p][j], a);
+            a = ffma2(cur[p], w[p][H], a);
+            pk[p] = pack2<T>(silu ? silu2_lowp(a) : a);
+          }
+#pragma unroll
+          for (int j = 0; j + 1 < H; ++j) {
+            hist[j][0] = hist[j + 1][0];
+            hist[j][1] = hist[j + 1][1];
+          }
+          if constexpr (H > 0) {
+            hist[H - 1][0] = cur[0];
+            hist[H - 1][1] = cur[1];
+          }
         }
         if (l2) {
-          const float2 r0 = unpack2<T>(pk[0]), r1 = unpack2<T>(pk[1]);
-          const float rn =
-              rsqrtf(warp_sum(r0.x * r0.x + r0.y * r0.y + r1.x * r1.x + r1.y * r1.y) + l2_eps);
-          pk[0] = pack2<T>(make_float2(r0.x * rn, r0.y * rn));
-          pk[1] = pack2<T>(make_float2(r1.x * rn, r1.y * rn));
-        }
-        if (u < nvalid) *reinterpret_cast<uint2*>(dst + (int64_t)u * dim) = packed;
+          float ss[2];
 #pragma unroll
-        for (int j = 0; j + 1 < H; ++j) {
-          hist[j][0] = hist[j + 1][0];
-          hist[j][1] = hist[j + 1][1];
+          for (int du = 0; du < 2; ++du) {
+            const float2 r0 = unpack2<T>(packed[du].x), r1 = unpack2<T>(packed[du].y);
+            ss[du] = r0.x * r0.x + r0.y * r0.y + r1.x * r1.x + r1.y * r1.y;
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int du = 0; du < 2; ++du) ss[du] += __shfl_xor_sync(0xffffffffu, ss[du], o);
+#pragma unroll
+          for (int du = 0; du < 2; ++du) {
+            const float rn = rsqrtf(ss[du] + l2_eps);
+            const float2 r0 = unpack2<T>(packed[du].x), r1 = unpack2<T>(packed[du].y);
+            packed[du].x = pack2<T>(make_float2(r0.x * rn, r0.y * rn));
+            packed[du].y = pack2<T>(make_float2(r1.x * rn, r1.y * rn));
+          }
         }
-        if constexpr (H > 0) {
-          hist[H - 1][0] = cur[0];
-          hist[H - 1][1] = cur[1];
-        }
+#pragma unroll
+        for (int du = 0; du < 2; ++du)
+          if (ug + du < nvalid) *reinterpret_cast<uint2*>(dst + (int64_t)(ug + du) * dim) = packed[du];
       }
       if (first) {
         // final state = last H entries of cat(old_state, x_seq).  Entry j
