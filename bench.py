@@ -5,7 +5,7 @@
 
 Default workload (cfg5): one 65536-token sequence through causal_conv1d
 (8192 channels, width 4, SiLU) -> chunked gated delta rule (Hk 16 -> Hv 32,
-dk = dv = 128, q/k L2-normalised in kernel) -> gated RMSNorm (group 128,
+dk = dv = 128; the q/k L2 norm fused into the conv kernel) -> gated RMSNorm (group 128,
 SiLU(z) gate).  The 32 value heads, their key heads and conv channels are
 split over the N ranks (one process per GPU, no collective on the data path);
 the sequence is the unit of work, so `value` = 65536 tokens / max-over-ranks

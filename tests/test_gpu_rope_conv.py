@@ -48,6 +48,12 @@ def test_rope_config1():
     (1500, 16, 2, 256, 64, torch.bfloat16, True),
     (700, 4, 2, 512, 200, torch.float32, False),     # rotary half not a lane multiple
     (800, 4, 2, 256, 42, torch.float32, True),       # cos/sin rows not 16-byte multiples
+    # partner in the same lane's chunk half / (32 V) rows away
+    (1200, 8, 2, 256, 256, torch.float32, True),
+    (600, 4, 2, 512, 512, torch.float32, False),
+    (900, 4, 2, 512, 256, torch.float32, False),
+    (700, 4, 2, 512, 512, torch.bfloat16, False),
+    (800, 4, 2, 512, 128, torch.bfloat16, True),     # partner lane of chunk 0, two chunks
 ])
 def test_rope_shapes(T, qh, kvh, hd, rd, dt, bias):
     g = torch.Generator().manual_seed(T)

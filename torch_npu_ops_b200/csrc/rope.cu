@@ -84,10 +84,16 @@ __global__ void __launch_bounds__(256) split_rmsnorm_rope_kernel(
 // with 1-D bulk copies (warp 0), together with the cos / sin rows of the
 // tokens the tile touches (when those rows are 16-byte multiples), and 8
 // consumer warps take two segments at a time: v heads are copied out, q / k
-// heads are normalised and rotated.  The rotate-half partner of a slice is
-// the slice of lane +- (rotary_dim / 2) / EPL (a shuffle) when rotary_dim / 2
-// is a multiple of the lane width, else it is recomputed from the raw input
-// of element d +- rotary_dim / 2 in the stage (same r, weight and bias).
+// heads are normalised and rotated.  A lane owns interleaved 16-byte chunks
+// of a segment (chunk c of lane l holds elements (32 c + l) V .. + V - 1, V
+// elements per 16 bytes), so every shared-memory read of the segment, of the
+// weight rows and every global store of a warp is one contiguous, bank- and
+// sector-aligned 512-byte access.  The rotate-half partner of element d is
+// element d +- rotary_dim / 2: (mode 1) in chunk 0 of lane +- half / V, a
+// shuffle, when every rotated element is in chunk 0 and half is a whole
+// number of chunks; (mode 2) in the same lane's chunk c +- half / (32 V)
+// when half is a whole number of chunk rows; (mode 0) otherwise recomputed
+// from the raw input of the partner in the stage (same r, weight and bias).
 // Weight and bias rows live in shared memory for the whole kernel.
 // ----------------------------------------------------------------------------
 constexpr int RP_NS = 3, RP_TILE = 32768, RP_NT = 32 + 256;
@@ -100,7 +106,7 @@ struct RopeStage {
   int maxtok;   // tokens one tile can touch
 };
 
-template <typename T, typename TW, typename TS, int HD>
+template <typename T, typename TW, typename TS, int HD, int MODE>
 __global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
     const T* __restrict__ in, const TS* __restrict__ sin_t, const TS* __restrict__ cos_t,
     T* __restrict__ qo, T* __restrict__ ko, T* __restrict__ vo, const TW* __restrict__ qw,
@@ -131,11 +137,20 @@ __global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
     tc::mbar_fence_init();
     abort_sh = 0;
   }
+  constexpr int V = 16 / (int)sizeof(T);  // elements per 16-byte chunk
+  constexpr int HV = V / 2;                // element pairs per chunk
+  // weight rows in float4 units ordered [chunk][quarter of chunk][lane], so
+  // that the float4 of pairs (j, j + 1) of every lane is one conflict-free read
+  auto widx = [](int d) {
+    const int m = d / V, e = d % V;
+    return (((m >> 5) * (V / 4) + e / 4) * 32 + (m & 31)) * 4 + (e & 3);
+  };
   for (int i = tid; i < HD; i += blockDim.x) {
-    swt[i] = to_f32<TW>(qw[i]);
-    swt[2 * HD + i] = to_f32<TW>(kw[i]);
-    swt[HD + i] = has_b ? to_f32<TW>(qb[i]) : 0.f;
-    swt[3 * HD + i] = has_b ? to_f32<TW>(kb[i]) : 0.f;
+    const int w = widx(i);
+    swt[w] = to_f32<TW>(qw[i]);
+    swt[2 * HD + w] = to_f32<TW>(kw[i]);
+    swt[HD + w] = has_b ? to_f32<TW>(qb[i]) : 0.f;
+    swt[3 * HD + w] = has_b ? to_f32<TW>(kb[i]) : 0.f;
   }
   __syncthreads();
   if (warp == 0) {
@@ -171,13 +186,12 @@ __global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
   }
   const int cw = warp - 1;
   const int half = rd >> 1;
-  const int d0 = lane * EPL;
-  // vec: half is a multiple of EPL, so this lane's slice lies wholly in
-  // [0, half), [half, rd) or [rd, HD) and its partner slice is the one of
-  // lane +- half / EPL
-  const bool vec = half % EPL == 0;
-  const int src = !vec ? lane : d0 < half ? lane + half / EPL : d0 < rd ? lane - half / EPL : lane;
-  const bool rot = d0 < rd;
+  constexpr int NC = EPL / V;  // chunks per lane
+  // MODE (the partner rule, chosen at launch by rope_partner_mode):
+  // 1: partner lane of chunk 0; 2: partner chunk distance; 0: recompute
+  const int db0 = lane * V;
+  const int src = MODE != 1 ? lane : db0 < half ? lane + half / V : db0 < rd ? lane - half / V : lane;
+  const int coff = MODE == 2 ? half / (32 * V) : 0;
   constexpr int NSEG = EPL <= 8 ? 2 : 1;  // segments in flight per warp
   constexpr int P = EPL / 2;              // element pairs per lane
   for (int64_t k = 0;; ++k) {
@@ -197,7 +211,8 @@ __global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
     const int h0 = (int)(s0 - tf * heads);  // its head
 #pragma unroll 1
     for (int i0 = cw; i0 < SPT; i0 += 8 * NSEG) {
-      // element pairs (2j, 2j + 1) of the lane's slice as packed fp32 pairs
+      // element pairs of the lane's chunks as packed fp32 pairs: pair j is
+      // elements (32 (j / HV) + lane) V + 2 (j % HV) and the next one
       float2 x[NSEG][P];
       float ss[NSEG];
       int dt[NSEG], hh[NSEG];  // token offset from tf, head
@@ -209,10 +224,10 @@ __global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
         const int a = h0 + (live[u] ? i : 0);
         dt[u] = a / heads;
         hh[u] = live[u] ? a - dt[u] * heads : heads - 1;
-        const T* xs = st + (live[u] ? i : 0) * HD;
+        const uint4* xs = reinterpret_cast<const uint4*>(st + (live[u] ? i : 0) * HD);
 #pragma unroll
-        for (int c = 0; c < EPL * (int)sizeof(T) / 16; ++c) {
-          const uint4 r = reinterpret_cast<const uint4*>(xs + d0)[c];
+        for (int c = 0; c < NC; ++c) {
+          const uint4 r = xs[c * 32 + lane];
           if constexpr (sizeof(T) == 4) {
             x[u][2 * c] = make_float2(__uint_as_float(r.x), __uint_as_float(r.y));
             x[u][2 * c + 1] = make_float2(__uint_as_float(r.z), __uint_as_float(r.w));
@@ -224,8 +239,6 @@ __global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
           }
         }
       }
-      // the rotate-half sign, folded into sin
-      const float sg = d0 < half ? -1.f : 1.f;
 #pragma unroll
       for (int u = 0; u < NSEG; ++u) {
         float2 q2 = fmul2(x[u][0], x[u][0]);
@@ -242,61 +255,97 @@ __global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
       for (int u = 0; u < NSEG; ++u) {
         const bool is_v = hh[u] >= qh + kvh;
         const bool is_q = hh[u] < qh;
-        const bool apply = rot && !is_v;
         float2 v[P];
         const float r = rsqrtf(ss[u] * (1.0f / HD) + eps);
         const float2 r2 = make_float2(r, r);
         const float* wrow = swt + (is_q ? 0 : 2 * HD);
         const float* brow = wrow + HD;
+        const float4* w4p = reinterpret_cast<const float4*>(wrow) + lane;
+        const float4* b4p = reinterpret_cast<const float4*>(brow) + lane;
 #pragma unroll
         for (int j = 0; j < P; j += 2) {
           // without a bias the shared-memory read of the zero row is skipped
-          const float4 w4 = *reinterpret_cast<const float4*>(wrow + d0 + 2 * j);
-          const float4 b4 = has_b ? *reinterpret_cast<const float4*>(brow + d0 + 2 * j)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 w4 = w4p[(j / 2) * 32];
+          const float4 b4 = has_b ? b4p[(j / 2) * 32] : make_float4(0.f, 0.f, 0.f, 0.f);
           v[j] = ffma2(fmul2(x[u][j], r2), make_float2(w4.x, w4.y), make_float2(b4.x, b4.y));
           v[j + 1] = ffma2(fmul2(x[u][j + 1], r2), make_float2(w4.z, w4.w), make_float2(b4.z, b4.w));
         }
-        // cos / sin of element d of this segment's token
+        // cos / sin pair of elements (d, d + 1) of this segment's token
         const int64_t tok_u = tf + dt[u];
+        const bool cs_vec = staged && sizeof(TS) == 4;
         auto cos_at = [&](int d) {
           return staged ? to_f32<TS>(scos[dt[u] * rd + d]) : to_f32<TS>(cos_t[tok_u * rd + d]);
         };
         auto sin_at = [&](int d) {
           return staged ? to_f32<TS>(ssin[dt[u] * rd + d]) : to_f32<TS>(sin_t[tok_u * rd + d]);
         };
-        if (vec) {
-          // every lane shuffles (uniform); only rotated, live q / k slices use
-          // it.  Pair j of every lane is read by the shuffles before any lane
-          // updates its own pair j.
-          const bool cs_vec = staged && sizeof(TS) == 4;
+        auto cs2 = [&](int d, float2& c2, float2& s2) {
+          if (cs_vec) {
+            c2 = *reinterpret_cast<const float2*>(scos + dt[u] * rd + d);
+            s2 = *reinterpret_cast<const float2*>(ssin + dt[u] * rd + d);
+          } else {
+            c2 = make_float2(cos_at(d), cos_at(d + 1));
+            s2 = make_float2(sin_at(d), sin_at(d + 1));
+          }
+        };
+        if constexpr (MODE == 1) {
+          // every lane shuffles (uniform); only rotated, live q / k chunks
+          // use it.  Pair j of every lane is read by the shuffles before any
+          // lane updates its own pair j.
+          const bool apply = db0 < rd && !is_v;
+          const float sg = db0 < half ? -1.f : 1.f;  // the rotate-half sign
 #pragma unroll
-          for (int j = 0; j < P; ++j) {
+          for (int j = 0; j < HV; ++j) {
             const float2 pv = make_float2(__shfl_sync(0xffffffffu, v[j].x, src),
                                           __shfl_sync(0xffffffffu, v[j].y, src));
             if (apply) {
               float2 c2, s2;
-              if (cs_vec) {
-                c2 = *reinterpret_cast<const float2*>(scos + dt[u] * rd + d0 + 2 * j);
-                s2 = *reinterpret_cast<const float2*>(ssin + dt[u] * rd + d0 + 2 * j);
-              } else {
-                c2 = make_float2(cos_at(d0 + 2 * j), cos_at(d0 + 2 * j + 1));
-                s2 = make_float2(sin_at(d0 + 2 * j), sin_at(d0 + 2 * j + 1));
-              }
+              cs2(db0 + 2 * j, c2, s2);
               v[j] = ffma2(v[j], c2, fmul2(pv, fmul2(s2, make_float2(sg, sg))));
             }
           }
-        } else if (apply) {
-          // partner from the raw input in the stage, normalised the same way
-          const T* xs = st + (i0 + 8 * u) * HD;
+        } else if constexpr (MODE == 2) {
+          if (!is_v) {
+            // chunk rows c < coff hold the first rotary half and pair with
+            // c + coff, rows [coff, 2 coff) the second half: the distance is
+            // one of a few compile-time values, so every register index is
+            // static
 #pragma unroll
-          for (int j = 0; j < EPL; ++j) {
-            const int d = d0 + j;
-            if (d < rd) {
-              const int p = d < half ? d + half : d - half;
-              const float pvv = to_f32<T>(xs[p]) * r * wrow[p] + brow[p];
-              float& e = (j & 1) ? v[j >> 1].y : v[j >> 1].x;
-              e = e * cos_at(d) + (d < half ? -pvv : pvv) * sin_at(d);
+            for (int o = 1; o <= NC / 2; ++o) {
+              if (coff != o) continue;
+              float2 w[P];
+#pragma unroll
+              for (int j = 0; j < P; ++j) w[j] = v[j];
+#pragma unroll
+              for (int c = 0; c < 2 * o; ++c) {
+                const int db = (c * 32 + lane) * V;
+                const bool lo = c < o;
+                const int pc = lo ? c + o : c - o;
+                const float sg = lo ? -1.f : 1.f;
+#pragma unroll
+                for (int jj = 0; jj < HV; ++jj) {
+                  float2 c2, s2;
+                  cs2(db + 2 * jj, c2, s2);
+                  v[c * HV + jj] =
+                      ffma2(w[c * HV + jj], c2, fmul2(w[pc * HV + jj], fmul2(s2, make_float2(sg, sg))));
+                }
+              }
+            }
+          }
+        } else {
+          if (!is_v) {
+            // partner from the raw input in the stage, normalised the same way
+            const T* xs = st + (i0 + 8 * u) * HD;
+#pragma unroll
+            for (int j = 0; j < 2 * P; ++j) {
+              const int d = ((j / V) * 32 + lane) * V + (j % V);
+              if (d < rd) {
+                const int p = d < half ? d + half : d - half;
+                const int wp = widx(p);
+                const float pvv = to_f32<T>(xs[p]) * r * wrow[wp] + brow[wp];
+                float& e = (j & 1) ? v[j >> 1].y : v[j >> 1].x;
+                e = e * cos_at(d) + (d < half ? -pvv : pvv) * sin_at(d);
+              }
             }
           }
         }
@@ -305,9 +354,11 @@ __global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
         T* dst = is_v ? vo + tok * (int64_t)kvh * HD + (int64_t)(hh[u] - qh - kvh) * HD
                  : is_q ? qo + tok * (int64_t)qh * HD + (int64_t)hh[u] * HD
                         : ko + tok * (int64_t)kvh * HD + (int64_t)(hh[u] - qh) * HD;
-        const float2* o = is_v ? x[u] : v;
+        float2 o[P];  // v heads are copied through unchanged
 #pragma unroll
-        for (int c = 0; c < EPL * (int)sizeof(T) / 16; ++c) {
+        for (int j = 0; j < P; ++j) o[j] = is_v ? x[u][j] : v[j];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
           uint4 w;
           if constexpr (sizeof(T) == 4) {
             w = make_uint4(__float_as_uint(o[2 * c].x), __float_as_uint(o[2 * c].y),
@@ -316,13 +367,21 @@ __global__ void __launch_bounds__(RP_NT, 2) split_rmsnorm_rope_stream_kernel(
             w = make_uint4(pack2<T>(o[4 * c]), pack2<T>(o[4 * c + 1]), pack2<T>(o[4 * c + 2]),
                            pack2<T>(o[4 * c + 3]));
           }
-          reinterpret_cast<uint4*>(dst + d0)[c] = w;
+          reinterpret_cast<uint4*>(dst)[c * 32 + lane] = w;
         }
       }
     }
     __syncwarp();
     if (lane == 0) tc::mbar_arrive(&empty[s]);
   }
+}
+
+// partner rule of the streaming kernel for a rotary width (see the kernel)
+template <typename T>
+int rope_partner_mode(int rd) {
+  constexpr int V = 16 / (int)sizeof(T);
+  const int half = rd >> 1;
+  return (half % V == 0 && rd <= 32 * V) ? 1 : (half % (32 * V) == 0 ? 2 : 0);
 }
 
 template <typename T, typename TW, typename TS, int HD>
@@ -344,7 +403,10 @@ int launch_rope_stream(const void* in, const void* s, const void* c, void* q, vo
     L.stage = RP_TILE;
   }
   const int smem = RP_NS * L.stage + WB + 128;
-  auto kern = split_rmsnorm_rope_stream_kernel<T, TW, TS, HD>;
+  const int mode = rope_partner_mode<T>(rd);
+  auto kern = mode == 1   ? split_rmsnorm_rope_stream_kernel<T, TW, TS, HD, 1>
+              : mode == 2 ? split_rmsnorm_rope_stream_kernel<T, TW, TS, HD, 2>
+                          : split_rmsnorm_rope_stream_kernel<T, TW, TS, HD, 0>;
   if (!set_stream_smem(kern, smem))
     return set_error(XOPS_ERR_CUDA, "split_rmsnorm_rope: shared-memory attribute failed");
   int dev = 0, sms = 148;
