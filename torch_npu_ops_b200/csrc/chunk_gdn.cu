@@ -1195,44 +1195,108 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
 // ============================================================================
 // Kernel 3: segment start states, h_{s+1} = X_s^T h_s + B_s (fp32)
 // ============================================================================
-// Serial over the middle segments of one (sequence, head).  The value columns
-// are independent, so CTA x owns columns [8x, 8x + 8): thread (kk, half)
-// computes 4 of them for row kk.  The transitions X_s do not depend on the
-// states, so X_{s+1} streams into the second of two shared buffers (cp.async)
-// while step s computes; the serial part of a step is one 128-term dot
-// product per output.  Rows are 132 floats apart: 16-byte aligned, and a
-// quarter-warp's 16-byte row reads fall in distinct banks.
-constexpr int CB_NT = 256, CB_LD = 132;
-// shared bytes of a COLS-column CTA: two X^T buffers and h_s[:, cols]
-constexpr int cb_smem(int cols) { return (2 * 128 * CB_LD + 128 * cols) * 4 + 16; }
-
-__device__ __forceinline__ void cb_load_x(float* dst, const float* src, int tid) {
-  for (int e = tid; e < 128 * 32; e += CB_NT) {
-    const int r = e >> 5, q4 = e & 31;
-    cp_async16(dst + r * CB_LD + q4 * 4, src + r * 128 + q4 * 4, 16);
-  }
-  cp_async_commit();
+// Serial over the middle segments of one (sequence, head):
+//   h_{s+1}[kk][c] = sum_r X_s^T[kk][r] h_s[r][c] + B_s[kk][c].
+// The value columns c are independent, so each (sequence, head) is cut into
+// column slices of COLS; and the sum over r is cut over a cluster of CB_CR
+// CTAs: CTA j of a slice holds rows r in [32 j, 32 j + 32) of h_s and only
+// those 32 columns of every X^T row (16 KB a step, not the whole 64 KB
+// matrix; the transitions stream through L2 once per slice, not once per
+// CTA).  CTA j computes the partial sums of all 128 output rows and sends
+// those of rows [32 q, 32 q + 32) to CTA q's receive slot j with
+// asynchronous distributed-shared-memory stores that complete on CTA q's
+// transaction barrier `full`; CTA q adds its four slots (in rank order) and
+// B, which gives exactly the rows of h_{s+1} it holds for the next step, and
+// hands the slot set back to the writers through their `empty` barriers.
+// Slot sets alternate between steps.  X_{s+1} and B_{s+1} are requested
+// (cp.async) at the start of step s.  Every wait is bounded: on a timeout the
+// CTA records the error and leaves its loop; the cluster then meets at the
+// exit barrier, so no CTA leaves while another may still write into it.
+// CB_NT worker threads compute; one more warp (the producer) issues the copies
+constexpr int CB_NT = 256, CB_THREADS = CB_NT + 32, CB_CR = 4, CB_XLD = 36;  // X^T part rows: 32 floats + 4 padding
+// shared bytes of a COLS-column CTA: two X^T parts, h_s rows, two B row sets,
+// two sets of CB_CR receive slots [32][COLS]
+constexpr int cb_smem(int cols) {
+  return (2 * 128 * CB_XLD + 32 * cols + 2 * 32 * cols + 2 * CB_CR * 32 * cols) * 4 + 16;
 }
 
-// COLS columns per CTA (the host picks the largest grid that is still one
-// wave); thread (kk, half) computes CPT = COLS / 2 of them for row kk.  The
-// additive part B_{s+1} of the next step is fetched into registers while
-// step s computes, so no global-memory round trip sits on the serial path.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::
+                   : "memory");
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(local), "r"(rank));
+  return remote;
+}
+// 16 bytes into another CTA's shared memory, completing on its barrier
+__device__ __forceinline__ void st_async_f4(uint32_t raddr, uint32_t rbar, float4 v) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];\n" ::"r"(
+          raddr),
+      "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rbar)
+      : "memory");
+}
+// announce `bytes` of incoming transfers on a local barrier (this arrival
+// publishes no data of its own, so it needs no release ordering)
+__device__ __forceinline__ void mbar_expect_relaxed(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.relaxed.cta.shared::cta.b64 _, [%0], %1;\n" ::"r"(
+                   tc::smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t rbar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t limit) {
+  const uint32_t addr = tc::smem_addr(bar);
+  for (uint32_t i = 0; i < limit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
 template <int COLS>
-__global__ void __launch_bounds__(CB_NT) chunk_combine_kernel(const int32_t* __restrict__ cu,
+__global__ void __launch_bounds__(CB_THREADS) chunk_combine_kernel(const int32_t* __restrict__ cu,
                                                               int64_t N, int64_t T, int64_t H,
                                                               ChainPlan plan) {
-  constexpr int CPT = COLS / 2;
-  static_assert(CPT == 2 || CPT % 4 == 0, "columns per thread: 2 or a multiple of 4");
+  constexpr int NCC = COLS / 4;            // 4-column chunks
+  constexpr int NKG = CB_NT / NCC;         // output row groups
+  constexpr int KB = 128 / NKG;            // rows per group: kg, kg + NKG, ...
+  constexpr int FPT = (32 * NCC) / CB_NT > 0 ? (32 * NCC) / CB_NT : 1;  // finals per thread
+  constexpr int FT = 32 * NCC < CB_NT ? 32 * NCC : CB_NT;  // threads that finalise
+  constexpr int SLOT = 32 * COLS;          // floats per receive slot
+  constexpr uint32_t RX_BYTES = (CB_CR - 1) * SLOT * 4;  // remote bytes per step
+  static_assert(COLS % 16 == 0 && COLS <= 128 && KB * NKG == 128, "combine tiling");
   extern __shared__ __align__(16) float cbs[];
-  float* xbuf = cbs;                      // two X^T buffers [kk][r], rows CB_LD apart
-  float* cur = cbs + 2 * 128 * CB_LD;     // h_s[:, cols]  [r][COLS]
+  float* xbuf = cbs;                             // two X^T parts [128][CB_XLD]
+  float* hcur = xbuf + 2 * 128 * CB_XLD;         // h_s rows [32][COLS]
+  float* bbuf = hcur + SLOT;                     // two B row sets [32][COLS]
+  float* rbuf = bbuf + 2 * SLOT;                 // [2][CB_CR][32][COLS] receive slots
+  __shared__ uint64_t full[2], empty[2];
   __shared__ int64_t slot_sh;
-  __shared__ int nseg_sh;
+  __shared__ int nseg_sh, abort_sh;
   const int tid = threadIdx.x;
+  const bool producer = tid >= CB_NT;
+  const int lane = tid & 31;
+  const int j = (int)cluster_rank();
   const int64_t n = blockIdx.y / H;
   const int h = (int)(blockIdx.y - n * H);
-  const int v0 = blockIdx.x * COLS;
+  const int v0 = (blockIdx.x / CB_CR) * COLS;
   if (tid == 0) {
     int64_t slot = 0;
     int nseg = 1;
@@ -1243,85 +1307,130 @@ __global__ void __launch_bounds__(CB_NT) chunk_combine_kernel(const int32_t* __r
     }
     slot_sh = slot;
     nseg_sh = nseg;
+    abort_sh = 0;
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&full[b], 1);
+      tc::mbar_init(&empty[b], CB_CR - 1);
+    }
+    tc::mbar_fence_init();
   }
-  __syncthreads();
+  // barriers initialised cluster-wide before any CTA stores into another
+  cluster_sync();
   const int nseg = nseg_sh;
-  if (nseg < 3) return;
   const int64_t slot = slot_sh;
-  const int kk = tid >> 1, cb = (tid & 1) * CPT;
-  auto load_b = [&](int s, float (&b)[CPT]) {
-    const float* src = seg_state(plan, slot + s, H, h, 1) + kk * 128 + v0 + cb;
-    if constexpr (CPT == 2) {
-      const float2 t = *reinterpret_cast<const float2*>(src);
-      b[0] = t.x; b[1] = t.y;
-    } else {
-#pragma unroll
-      for (int c = 0; c < CPT; c += 4) {
-        const float4 t = *reinterpret_cast<const float4*>(src + c);
-        b[c] = t.x; b[c + 1] = t.y; b[c + 2] = t.z; b[c + 3] = t.w;
-      }
+  const int cc = tid % NCC, kg = tid / NCC;
+  // X^T rows [kk][32 j .. 32 j + 31] and B rows [32 j .. 32 j + 31][v0 ..
+  // v0 + COLS) of transition s, as one cp.async group of the producer warp
+  auto load_step = [&](int s, int buf) {
+    const float* xs = seg_state(plan, slot + s, H, h, 2);
+    float* xd = xbuf + buf * 128 * CB_XLD;
+    for (int e = lane; e < 128 * 8; e += 32) {
+      const int row = e >> 3, q4 = e & 7;
+      cp_async16(xd + row * CB_XLD + q4 * 4, xs + row * 128 + 32 * j + q4 * 4, 16);
     }
+    const float* bs = seg_state(plan, slot + s, H, h, 1) + v0;
+    float* bd = bbuf + buf * SLOT;
+    for (int e = lane; e < 32 * NCC; e += 32) {
+      const int r = e / NCC, c4 = e % NCC;
+      cp_async16(bd + r * COLS + 4 * c4, bs + (32 * j + r) * 128 + 4 * c4, 16);
+    }
+    cp_async_commit();
   };
-  cb_load_x(xbuf, seg_state(plan, slot + 1, H, h, 2), tid);
-  {
-    const float* h1 = seg_state(plan, slot + 1, H, h, 0);
-    for (int e = tid; e < 128 * COLS; e += CB_NT)
-      cur[e] = h1[(e / COLS) * 128 + v0 + (e % COLS)];
-  }
-  float bnext[CPT];
-  load_b(1, bnext);
-  for (int s = 1; s <= nseg - 2; ++s) {
-    const float* xs_cur = xbuf + ((s - 1) & 1) * 128 * CB_LD;
-    if (s + 1 <= nseg - 2) {
-      cb_load_x(xbuf + (s & 1) * 128 * CB_LD, seg_state(plan, slot + s + 1, H, h, 2), tid);
-      cp_async_wait_group<1>();  // X_s has landed; X_{s+1} may still be in flight
-    } else {
-      cp_async_wait_all();
+  if (nseg >= 3) {
+    if (producer) load_step(1, 0);
+    const float* h1 = seg_state(plan, slot + 1, H, h, 0) + v0;
+    for (int e = tid; e < 32 * NCC; e += CB_THREADS) {
+      const int r = e / NCC, c4 = e % NCC;
+      *reinterpret_cast<float4*>(hcur + r * COLS + 4 * c4) =
+          *reinterpret_cast<const float4*>(h1 + (32 * j + r) * 128 + 4 * c4);
     }
-    float acc[CPT];
-#pragma unroll
-    for (int c = 0; c < CPT; ++c) acc[c] = bnext[c];
-    if (s + 1 <= nseg - 2) load_b(s + 1, bnext);
+    cp_async_wait_all();
     __syncthreads();
-    const float* xrow = xs_cur + kk * CB_LD;
-#pragma unroll 4
-    for (int r = 0; r < 128; r += 4) {
-      const float4 xv = *reinterpret_cast<const float4*>(xrow + r);
-      const float xr[4] = {xv.x, xv.y, xv.z, xv.w};
+  }
+  const uint32_t rbuf_a = tc::smem_addr(rbuf);
+  for (int s = 1; s <= nseg - 2; ++s) {
+    const int b = (s - 1) & 1;
+    const uint32_t use = (uint32_t)((s - 1) >> 1);  // how often slot set b was used before
+    if (producer) {
+      if (s + 1 <= nseg - 2) load_step(s + 1, b ^ 1);
+      if (lane == 0) mbar_expect_relaxed(&full[b], RX_BYTES);
+      __syncthreads();
+      if (*(volatile int*)&abort_sh) break;
+      if (s + 1 <= nseg - 2) cp_async_wait_all();  // X_{s+1}, B_{s+1} have landed
+      __syncthreads();
+      continue;
+    }
+    const float* xs = xbuf + b * 128 * CB_XLD;
+    float acc[KB][4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float* hrow = cur + (r + u) * COLS + cb;
-        if constexpr (CPT == 2) {
-          const float2 hv = *reinterpret_cast<const float2*>(hrow);
-          acc[0] = fmaf(xr[u], hv.x, acc[0]);
-          acc[1] = fmaf(xr[u], hv.y, acc[1]);
-        } else {
+    for (int i = 0; i < KB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 #pragma unroll
-          for (int c = 0; c < CPT; c += 4) {
-            const float4 hv = *reinterpret_cast<const float4*>(hrow + c);
-            acc[c] = fmaf(xr[u], hv.x, acc[c]);
-            acc[c + 1] = fmaf(xr[u], hv.y, acc[c + 1]);
-            acc[c + 2] = fmaf(xr[u], hv.z, acc[c + 2]);
-            acc[c + 3] = fmaf(xr[u], hv.w, acc[c + 3]);
-          }
+    for (int r = 0; r < 32; r += 4) {
+      float4 hv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        hv[u] = *reinterpret_cast<const float4*>(hcur + (r + u) * COLS + 4 * cc);
+#pragma unroll
+      for (int i = 0; i < KB; ++i) {
+        const float4 x4 = *reinterpret_cast<const float4*>(xs + (kg + i * NKG) * CB_XLD + r);
+        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          acc[i][0] = fmaf(xv[u], hv[u].x, acc[i][0]);
+          acc[i][1] = fmaf(xv[u], hv[u].y, acc[i][1]);
+          acc[i][2] = fmaf(xv[u], hv[u].z, acc[i][2]);
+          acc[i][3] = fmaf(xv[u], hv[u].w, acc[i][3]);
         }
       }
     }
-    __syncthreads();  // every thread is done reading h_s and X_s
-    float* gout = seg_state(plan, slot + s + 1, H, h, 0) + kk * 128 + v0 + cb;
-    if constexpr (CPT == 2) {
-      *reinterpret_cast<float2*>(cur + kk * COLS + cb) = make_float2(acc[0], acc[1]);
-      *reinterpret_cast<float2*>(gout) = make_float2(acc[0], acc[1]);
-    } else {
+    // the owners have read this slot set's previous use
+    bool ok = use == 0 || mbar_wait_cluster(&empty[b], (use - 1) & 1, WAIT_LIMIT);
+    // row kk's partial goes to slot j of its owner CTA kk / 32
+    const uint32_t slot_off = (uint32_t)((b * CB_CR + j) * SLOT) * 4u;
 #pragma unroll
-      for (int c = 0; c < CPT; c += 4) {
-        const float4 t = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
-        *reinterpret_cast<float4*>(cur + kk * COLS + cb + c) = t;
-        *reinterpret_cast<float4*>(gout + c) = t;
-      }
+    for (int i = 0; i < KB && ok; ++i) {
+      const int kk = kg + i * NKG;
+      const int q = kk >> 5;
+      const float4 v = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      const uint32_t off = slot_off + (uint32_t)(((kk & 31) * COLS + 4 * cc) * 4);
+      if (q == j)
+        *reinterpret_cast<float4*>(reinterpret_cast<unsigned char*>(rbuf) + off) = v;
+      else
+        st_async_f4(mapa(rbuf_a + off, (uint32_t)q), mapa(tc::smem_addr(&full[b]), (uint32_t)q), v);
     }
-    __syncthreads();
+    ok = ok && mbar_wait_cluster(&full[b], use & 1, WAIT_LIMIT);
+    if (!ok) {
+      record_error();
+      atomicExch(&abort_sh, 1);
+    }
+    __syncthreads();  // own slot written, every read of h_s done, abort flag seen
+    if (*(volatile int*)&abort_sh) break;
+    float* gout = seg_state(plan, slot + s + 1, H, h, 0) + v0;
+    const float* bsrc = bbuf + b * SLOT;
+    const float* rb = rbuf + b * CB_CR * SLOT;
+#pragma unroll
+    for (int f = 0; f < FPT; ++f) {
+      if (tid >= FT) break;
+      const int e = tid + f * CB_NT, fr = e / NCC, fc = e % NCC;
+      const float* src = rb + fr * COLS + 4 * fc;
+      float4 t = *reinterpret_cast<const float4*>(src);
+#pragma unroll
+      for (int q = 1; q < CB_CR; ++q) {  // partials in cluster-rank order
+        const float4 p = *reinterpret_cast<const float4*>(src + q * SLOT);
+        t.x += p.x; t.y += p.y; t.z += p.z; t.w += p.w;
+      }
+      const float4 bb = *reinterpret_cast<const float4*>(bsrc + fr * COLS + 4 * fc);
+      t.x += bb.x; t.y += bb.y; t.z += bb.z; t.w += bb.w;
+      *reinterpret_cast<float4*>(hcur + fr * COLS + 4 * fc) = t;
+      *reinterpret_cast<float4*>(gout + (32 * j + fr) * 128 + 4 * fc) = t;
+    }
+    __syncthreads();  // slot set b read; h_{s+1} rows, X_{s+1}, B_{s+1} visible
+    if (tid < CB_CR && tid != j)  // hand slot set b back to the other writers
+      mbar_arrive_remote(mapa(tc::smem_addr(&empty[b]), (uint32_t)tid));
   }
+  cp_async_wait_all();
+  // no CTA leaves while another may still store into its receive slots
+  cluster_sync();
 }
 
 }  // namespace
@@ -1539,25 +1648,37 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
         plan);
   if (int rc = check_launch("chunk_gated_delta_rule(chain, first segments)")) return rc;
   {
-    // the fewest columns per CTA (the most CTAs per head) whose grid is still
-    // one wave of one CTA per SM: each CTA walks every segment serially
+    // the narrowest column slice whose clusters (4 CTAs each) still fit one
+    // wave of one CTA per SM
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess)
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int cols = 4;
-    while (cols < 32 && (int64_t)N * H * (128 / cols) > sms) cols *= 2;
+    int cols = 16;
+    while (cols < 128 && (int64_t)N * H * (128 / cols) * gdn::CB_CR > sms) cols *= 2;
     auto launch = [&](auto kern, int c) -> int {
       if (int rc = gdn::ensure_smem_attr((const void*)kern, gdn::cb_smem(c),
                                          "chunk_gated_delta_rule(combine)"))
         return rc;
-      kern<<<dim3(128 / c, (unsigned)(N * H)), gdn::CB_NT, gdn::cb_smem(c), st>>>(cu_seqlens, N,
-                                                                                  T, H, plan);
+      cudaLaunchConfig_t lc = {};
+      lc.gridDim = dim3((unsigned)((128 / c) * gdn::CB_CR), (unsigned)(N * H));
+      lc.blockDim = dim3(gdn::CB_THREADS);
+      lc.dynamicSmemBytes = (size_t)gdn::cb_smem(c);
+      lc.stream = st;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = gdn::CB_CR;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      lc.attrs = at;
+      lc.numAttrs = 1;
+      if (cudaLaunchKernelEx(&lc, kern, (const int32_t*)cu_seqlens, N, T, H, plan) != cudaSuccess)
+        return set_error(XOPS_ERR_CUDA, "chunk_gated_delta_rule(combine): cluster launch failed");
       return 0;
     };
-    int rc = cols == 4    ? launch(gdn::chunk_combine_kernel<4>, 4)
-             : cols == 8  ? launch(gdn::chunk_combine_kernel<8>, 8)
-             : cols == 16 ? launch(gdn::chunk_combine_kernel<16>, 16)
-                          : launch(gdn::chunk_combine_kernel<32>, 32);
+    int rc = cols == 16   ? launch(gdn::chunk_combine_kernel<16>, 16)
+             : cols == 32 ? launch(gdn::chunk_combine_kernel<32>, 32)
+             : cols == 64 ? launch(gdn::chunk_combine_kernel<64>, 64)
+                          : launch(gdn::chunk_combine_kernel<128>, 128);
     if (rc) return rc;
   }
   if (int rc = check_launch("chunk_gated_delta_rule(combine)")) return rc;
