@@ -266,6 +266,26 @@ XOPS_API int xops_chunk_gated_delta_rule(const void* q, const void* k, const voi
                                 int use_qk_l2norm_in_kernel, void* workspace,
                                 int64_t workspace_bytes, void* stream);
 
+/* The same rule with fused_gdn_gating folded into its prologue: the gates
+ * are computed where the kernels read them, from the layer's projections a,
+ * b [B, T, H] (fp32, bf16 or fp16 each, a_dtype / b_dtype XOPS_F32 /
+ * XOPS_BF16 / XOPS_F16) and A_log, dt_bias [H] fp32:
+ *   g = -exp(A_log[h]) * softplus(a + dt_bias[h]),  beta = sigmoid(b) in b's dtype
+ * with the arithmetic of xops_fused_gdn_gating, so the result equals
+ * xops_fused_gdn_gating followed by xops_chunk_gated_delta_rule (beta widened
+ * to fp32) bit for bit, without the g / beta round trip through HBM and
+ * the extra launch.  The GDN layer's prefill calls fused_gdn_gating
+ * (npu_triton_fused_gdn_gating.cpp:33-93) then npu_chunk_gated_delta_rule
+ * (npu_triton_chunk_gated_delta_rule.cpp:556-642); this entry replaces the
+ * pair.  Other arguments and the workspace as xops_chunk_gated_delta_rule. */
+XOPS_API int xops_chunk_gated_delta_rule_gated(
+    const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b,
+    const float* dt_bias, int a_dtype, int b_dtype, float softplus_beta, float softplus_threshold,
+    const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
+    int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
+    int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
+    void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Workspace bytes xops_chunk_gated_delta_rule needs (an upper bound computed
  * from shapes only, no device access); varlen = cu_seqlens given. */
 XOPS_API int64_t xops_chunk_gated_delta_rule_workspace_size(int64_t B, int64_t T, int64_t N,

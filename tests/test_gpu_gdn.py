@@ -391,3 +391,64 @@ def test_recurrent_spec_via_cpp():
     assert torch.equal(o1, o2) and torch.equal(s1, s2)
     assert C.kernel_entry_point("fused_recurrent_gated_delta_rule_spec_fwd_kernel") == \
         "xops_fused_recurrent_gated_delta_rule"
+
+
+# ------------------------------------------------- gating fused into the rule
+def _gating_inputs(T, H, adt, bdt, seed):
+    g = torch.Generator().manual_seed(seed)
+    A_log = torch.rand(H, generator=g) * 2.7
+    a = torch.randn(T, H, generator=g).to(adt)
+    b = torch.randn(T, H, generator=g).to(bdt)
+    dt_bias = torch.rand(H, generator=g)
+    return A_log, a, b, dt_bias
+
+
+@pytest.mark.parametrize("lens,hk,hv,adt,bdt,l2", [
+    ([1, 63, 64, 65, 0, 129, 700], 4, 8, torch.bfloat16, torch.bfloat16, False),  # pair prep
+    ([900, 33], 2, 8, torch.float16, torch.float32, True),                          # per-head prep
+    ([4096], 16, 32, torch.float32, torch.bfloat16, False),                         # cfg3 heads
+    ([8192], 1, 2, torch.bfloat16, torch.bfloat16, False),                          # segmented chain
+])
+def test_chunk_gated_equals_gating_then_rule(lens, hk, hv, adt, bdt, l2):
+    """npu_fused_gdn_gating followed by npu_chunk_gated_delta_rule and the
+    fused-gating entry give the same bits; both match the composed oracle."""
+    inp = workloads.chunk_config3(hk=hk, hv=hv, lengths=lens, seed=11)
+    T = sum(lens)
+    A_log, a, b, dt_bias = _gating_inputs(T, hv, adt, bdt, seed=len(lens) + hv)
+    g, beta = ops.npu_fused_gdn_gating(_to(A_log), _to(a), _to(b), _to(dt_bias))
+    o1, h1 = ops.npu_chunk_gated_delta_rule(
+        _to(inp["q"]), _to(inp["k"]), _to(inp["v"]), g, beta.float(), None,
+        _to(inp["initial_state"]), True, _to(inp["cu_seqlens"]), False, l2)
+    o2, h2 = ops.chunk_gated_delta_rule_gated(
+        _to(inp["q"]), _to(inp["k"]), _to(inp["v"]), _to(A_log), _to(a[None]), _to(b), _to(dt_bias),
+        None, _to(inp["initial_state"]), True, _to(inp["cu_seqlens"]), l2)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(h1, h2)
+    rg, rb = oracle.fused_gdn_gating(A_log, a, b, dt_bias)
+    rb = rb.to(bdt).float()  # beta as the gating operator stores it (b's dtype)
+    ro, rh = oracle.chunk_gated_delta_rule(inp["q"], inp["k"], inp["v"], rg, rb, None,
+                                           inp["initial_state"], True, inp["cu_seqlens"], l2)
+    assert_bf16_rel(o2.cpu(), ro)
+    assert_state(h2.cpu(), rh)
+
+
+def test_gdn_prefill_gating_option():
+    """The layer pipeline with the gating folded into the rule equals the
+    pipeline fed by npu_fused_gdn_gating, bit for bit (a head shard of the
+    bench configuration, 8192 tokens)."""
+    from torch_npu_ops_b200.pipeline import gdn_prefill
+    w = workloads.long_config5_shard(0, 8, T=8192)
+    hv, hk = w["heads"][1] - w["heads"][0], w["k_heads"][1] - w["k_heads"][0]
+    T = w["T"]
+    A_log, a, b, dt_bias = _gating_inputs(T, hv, torch.bfloat16, torch.bfloat16, seed=5)
+    g, beta = ops.npu_fused_gdn_gating(_to(A_log), _to(a), _to(b), _to(dt_bias))
+    outs = []
+    for gating in (None, (_to(A_log), _to(a), _to(b), _to(dt_bias))):
+        st = torch.zeros(1, w["x"].shape[1], 3, dtype=torch.bfloat16, device=DEV)
+        gg, bb = (g, beta.float()) if gating is None else (None, None)
+        outs.append(gdn_prefill(_to(w["x"]), st, _to(w["weight"]), _to(w["bias"]), gg, bb,
+                                _to(w["initial_state"]), _to(w["z"]), _to(w["norm_w"]), hk, hv,
+                                gating=gating))
+    torch.cuda.synchronize()
+    for x1, x2 in zip(*outs):
+        assert torch.equal(x1, x2)

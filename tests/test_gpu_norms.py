@@ -102,6 +102,25 @@ def test_gemma_rms_norm(shape, dt):
     assert torch.equal(y2, y)
 
 
+@pytest.mark.parametrize("xshape,gshape", [((4, 8, 16, 128), (16, 128)), ((6, 32, 64), (32, 64)),
+                                           ((32, 64), (32, 64)), ((3, 2, 4, 256), (2, 4, 256))])
+def test_gemma_rms_norm_multidim_gamma(xshape, gshape):
+    """gamma over the trailing gamma.dim() axes: rstd has shape
+    x.shape[:-gamma.dim()] + (1,) * gamma.dim() (ascendc_npu/gemma_rms_norm.cpp:35-49)."""
+    g = torch.Generator().manual_seed(77)
+    x = torch.randn(*xshape, generator=g).to(torch.bfloat16)
+    gamma = (0.1 * torch.randn(*gshape, generator=g)).to(torch.bfloat16)
+    rstd, y = ops.npu_gemma_rms_norm(x.to(DEV), gamma.to(DEV), 1e-6)
+    rr, ry = oracle.gemma_rms_norm(x, gamma, 1e-6)
+    lead = xshape[: len(xshape) - len(gshape)]
+    expect = tuple(lead) + (1,) * len(gshape) if len(xshape) > len(gshape) else (1,) * len(xshape)
+    assert tuple(rstd.shape) == tuple(rr.shape) == expect and y.shape == x.shape
+    assert_fp32(rstd, rr)
+    assert_bf16(y, ry)
+    rstd2, y2 = ops.npu_python_extension_lib.gemma_rms_norm(x.to(DEV), gamma.to(DEV), 1e-6)
+    assert tuple(rstd2.shape) == expect and torch.equal(y2, y)
+
+
 @pytest.mark.parametrize("case", golden("l2norm"), ids=lambda c: c["name"])
 def test_l2norm_golden(case):
     x = case["args"]["x"]

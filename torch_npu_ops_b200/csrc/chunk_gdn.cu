@@ -43,6 +43,7 @@
 
 #include <mutex>
 
+#include "gate_math.cuh"
 #include "gdn_common.cuh"
 #include "tcgen05.cuh"
 
@@ -79,6 +80,40 @@ __device__ __forceinline__ uint32_t tm_addr(uint32_t base, int quarter, uint32_t
   return base + ((uint32_t)(quarter * 32) << 16) + col;
 }
 __device__ __forceinline__ void record_error() { atomicExch(&g_tc_error, 1); }
+
+// Gates of the rule per (token, value head): precomputed g / beta [T, H]
+// fp32, or computed where they are read from the layer's projections a, b
+// [T, H] (the fused-gating entry) with the arithmetic of fused_gdn_gating
+// (gate_math.cuh), so both entries see the same values bit for bit.
+struct GateSrc {
+  const float* g;     // precomputed gates; nullptr: computed from a / b
+  const float* beta;
+  const void* a;
+  const void* b;
+  const float* A_log;
+  const float* dt_bias;
+  float sp_beta, sp_thr;
+  int a_dt, b_dt;     // XOPS_F32 / XOPS_BF16 / XOPS_F16
+};
+__device__ __forceinline__ float gate_elem(const void* p, int dt, int64_t i) {
+  return dt == XOPS_BF16 ? __bfloat162float(static_cast<const bf16*>(p)[i])
+         : dt == XOPS_F16 ? __half2float(static_cast<const __half*>(p)[i])
+                          : static_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void gate_load(const GateSrc& s, int64_t t, int64_t H, int h, float& g,
+                                          float& beta) {
+  const int64_t i = t * H + h;
+  if (s.g) {
+    g = s.g[i];
+    beta = s.beta[i];
+    return;
+  }
+  g = gate_g(-expf(s.A_log[h]), gate_elem(s.a, s.a_dt, i), s.dt_bias[h], s.sp_beta, s.sp_thr);
+  const float bv = gate_elem(s.b, s.b_dt, i);
+  beta = s.b_dt == XOPS_BF16  ? gate_beta<bf16>(bv)
+         : s.b_dt == XOPS_F16 ? gate_beta<__half>(bv)
+                              : gate_beta<float>(bv);
+}
 
 // [64 x 128] bf16 rows (global row stride in elements) -> SW128 tile
 __device__ __forceinline__ void cp_tile128(unsigned char* dst, uint32_t half_stride,
@@ -143,8 +178,8 @@ constexpr int P_SMEM = P_OFF_G + 4 * 64 * 4 + 1024;
 constexpr uint32_t P_TM_G = 0, P_TM_W = 64, P_TM_COLS = 128;
 
 __global__ void __launch_bounds__(P_NT, 4) chunk_prep_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
-    const float* __restrict__ beta, unsigned char* __restrict__ ws,
+    const bf16* __restrict__ q, const bf16* __restrict__ k, const GateSrc gs,
+    unsigned char* __restrict__ ws,
     const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H,
     int64_t q_stride, int64_t k_stride) {
   extern __shared__ unsigned char smem_raw[];
@@ -191,8 +226,7 @@ __global__ void __launch_bounds__(P_NT, 4) chunk_prep_kernel(
   const int grp = (int)(H / Hg);
   float g_next = 0.f, b_next = 0.f;
   if (tid < L) {
-    g_next = g[(t0 + tid) * H + hk * grp];
-    b_next = beta[(t0 + tid) * H + hk * grp];
+    gate_load(gs, t0 + tid, H, hk * grp, g_next, b_next);
   }
   cp_async_wait_all();
   tc::fence_proxy_async();
@@ -230,8 +264,7 @@ __global__ void __launch_bounds__(P_NT, 4) chunk_prep_kernel(
       bet[tid] = b_next;
       g_next = b_next = 0.f;
       if (tid < L && hv + 1 < (hk + 1) * grp) {
-        g_next = g[(t0 + tid) * H + hv + 1];
-        b_next = beta[(t0 + tid) * H + hv + 1];
+        gate_load(gs, t0 + tid, H, hv + 1, g_next, b_next);
       }
     }
     __syncthreads();
@@ -355,8 +388,8 @@ constexpr int P2_SMEM = P2_OFF_G + 2 * 4 * 64 * 4 + 1024;
 constexpr uint32_t P2_TM_G = 0, P2_TM_W0 = 0, P2_TM_W1 = 64, P2_TM_COLS = 128;
 
 __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ k, const float* __restrict__ g,
-    const float* __restrict__ beta, unsigned char* __restrict__ ws,
+    const bf16* __restrict__ q, const bf16* __restrict__ k, const GateSrc gs,
+    unsigned char* __restrict__ ws,
     const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H,
     int64_t q_stride, int64_t k_stride) {
   extern __shared__ unsigned char smem_raw[];
@@ -405,8 +438,10 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
   cp_async_commit();
   if (tid < 128) {  // both heads' gates
     const int h = tid >> 6, t = tid & 63;
-    graw(h)[t] = t < L ? g[(t0 + t) * H + hv0 + h] : 0.f;
-    bet(h)[t] = t < L ? beta[(t0 + t) * H + hv0 + h] : 0.f;
+    float gv = 0.f, bv = 0.f;
+    if (t < L) gate_load(gs, t0 + t, H, hv0 + h, gv, bv);
+    graw(h)[t] = gv;
+    bet(h)[t] = bv;
   }
   cp_async_wait_all();
   tc::fence_proxy_async();
@@ -645,8 +680,7 @@ __device__ __forceinline__ int seq_chunks(const int32_t* cu, int64_t n, int64_t 
 __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-    const float* __restrict__ g,
-    const float* __restrict__ beta, const float* __restrict__ h0,
+    const GateSrc gs, const float* __restrict__ h0,
     const unsigned char* __restrict__ ws, bf16* __restrict__ o, float* __restrict__ ht,
     const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H, float scale,
     ChainPlan plan) {
@@ -813,14 +847,8 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       // as chunk_cumsum_warp, so it matches the preparation kernel bit for bit)
       float ga = 0.f, gb2 = 0.f, ba = 0.f, bb = 0.f;
       const int i0 = 2 * lane;
-      if (i0 < L) {
-        ga = g[(t0 + i0) * H + h];
-        ba = beta[(t0 + i0) * H + h];
-      }
-      if (i0 + 1 < L) {
-        gb2 = g[(t0 + i0 + 1) * H + h];
-        bb = beta[(t0 + i0 + 1) * H + h];
-      }
+      if (i0 < L) gate_load(gs, t0 + i0, H, h, ga, ba);
+      if (i0 + 1 < L) gate_load(gs, t0 + i0 + 1, H, h, gb2, bb);
       const float pair = ga + gb2;
       float incl = pair;
 #pragma unroll
@@ -1536,15 +1564,14 @@ extern "C" int64_t xops_chunk_gated_delta_rule_workspace_size(int64_t B, int64_t
   return bytes;
 }
 
-extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const void* v,
-                                           const float* g, const float* beta, const float* h0,
-                                           void* o, float* ht, const int32_t* cu_seqlens,
-                                           int64_t B, int64_t T, int64_t N, int64_t Hg,
-                                           int64_t H, int64_t K, int64_t V,
-                                           int64_t q_token_stride, int64_t k_token_stride,
-                                           int64_t v_token_stride, float scale,
-                                           int use_qk_l2norm_in_kernel, void* workspace,
-                                           int64_t workspace_bytes, void* stream) {
+// The chunked rule behind both C-ABI entries; `gs` says where the gates
+// come from.
+static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn::GateSrc& gs,
+                         const float* h0, void* o, float* ht, const int32_t* cu_seqlens,
+                         int64_t B, int64_t T, int64_t N, int64_t Hg, int64_t H, int64_t K,
+                         int64_t V, int64_t q_token_stride, int64_t k_token_stride,
+                         int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
+                         void* workspace, int64_t workspace_bytes, void* stream) {
   XOPS_REQUIRE(B >= 1 && T >= 0 && N >= 0 && Hg >= 1 && H >= 1,
                "chunk_gated_delta_rule: bad shape");
   XOPS_REQUIRE(H % Hg == 0,
@@ -1562,7 +1589,9 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
                    q_token_stride % 8 == 0 && k_token_stride % 8 == 0 && v_token_stride % 8 == 0,
                "chunk_gated_delta_rule: token strides must cover the heads and be multiples of 8");
   if (N == 0 || T == 0) return XOPS_OK;
-  XOPS_REQUIRE(q && k && v && g && beta && o, "chunk_gated_delta_rule: null pointer");
+  XOPS_REQUIRE(q && k && v && o && (gs.g ? gs.beta != nullptr
+                                           : gs.a && gs.b && gs.A_log && gs.dt_bias),
+               "chunk_gated_delta_rule: null pointer");
   XOPS_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o),
                "chunk_gated_delta_rule: tensors must be 16-byte aligned");
   const int64_t need = xops_chunk_gated_delta_rule_workspace_size(
@@ -1604,13 +1633,13 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
                                        "chunk_gated_delta_rule(prep)"))
       return rc;
     gdn::chunk_prep_pair_kernel<<<dim3((unsigned)nchunks, (unsigned)Hg), gdn::P_NT, gdn::P2_SMEM,
-                                  st>>>(qq, kk, g, beta, ws, cu_seqlens, N, T, Hg, H, qs, ks);
+                                  st>>>(qq, kk, gs, ws, cu_seqlens, N, T, Hg, H, qs, ks);
   } else {
     if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_prep_kernel, gdn::P_SMEM,
                                        "chunk_gated_delta_rule(prep)"))
       return rc;
     gdn::chunk_prep_kernel<<<dim3((unsigned)nchunks, (unsigned)Hg), gdn::P_NT, gdn::P_SMEM, st>>>(
-        qq, kk, g, beta, ws, cu_seqlens, N, T, Hg, H, qs, ks);
+        qq, kk, gs, ws, cu_seqlens, N, T, Hg, H, qs, ks);
   }
   if (int rc = check_launch("chunk_gated_delta_rule(prep)")) return rc;
   if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_chain_kernel, gdn::C_SMEM,
@@ -1634,7 +1663,7 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
   gdn::ChainPlan plan{seg, 1, nullptr};
   if (seg == 0) {
     gdn::chunk_chain_kernel<<<(unsigned)(N * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-        mq, mk, mv, mo, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+        mq, mk, mv, mo, gs, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
         plan);
     return check_launch("chunk_gated_delta_rule(chain)");
   }
@@ -1644,7 +1673,7 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
   plan.scratch = reinterpret_cast<float*>(ws + off);
   const int64_t slots = chain_segment_slots(T, N, varlen, seg);
   gdn::chunk_chain_kernel<<<(unsigned)((N + 2 * slots) * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-      mq, mk, mv, mo, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+      mq, mk, mv, mo, gs, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
         plan);
   if (int rc = check_launch("chunk_gated_delta_rule(chain, first segments)")) return rc;
   {
@@ -1684,9 +1713,51 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
   if (int rc = check_launch("chunk_gated_delta_rule(combine)")) return rc;
   plan.phase = 3;
   gdn::chunk_chain_kernel<<<(unsigned)(slots * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-      mq, mk, mv, mo, g, beta, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+      mq, mk, mv, mo, gs, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
         plan);
   return check_launch("chunk_gated_delta_rule(chain, remaining segments)");
+}
+
+extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const void* v,
+                                           const float* g, const float* beta, const float* h0,
+                                           void* o, float* ht, const int32_t* cu_seqlens,
+                                           int64_t B, int64_t T, int64_t N, int64_t Hg,
+                                           int64_t H, int64_t K, int64_t V,
+                                           int64_t q_token_stride, int64_t k_token_stride,
+                                           int64_t v_token_stride, float scale,
+                                           int use_qk_l2norm_in_kernel, void* workspace,
+                                           int64_t workspace_bytes, void* stream) {
+  gdn::GateSrc gs{};
+  gs.g = g;
+  gs.beta = beta;
+  return chunk_gdn_run(q, k, v, gs, h0, o, ht, cu_seqlens, B, T, N, Hg, H, K, V, q_token_stride,
+                       k_token_stride, v_token_stride, scale, use_qk_l2norm_in_kernel, workspace,
+                       workspace_bytes, stream);
+}
+
+extern "C" int xops_chunk_gated_delta_rule_gated(
+    const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b,
+    const float* dt_bias, int a_dtype, int b_dtype, float softplus_beta, float softplus_threshold,
+    const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
+    int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
+    int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
+    void* workspace, int64_t workspace_bytes, void* stream) {
+  auto ok_dtype = [](int d) { return d == XOPS_F32 || d == XOPS_BF16 || d == XOPS_F16; };
+  XOPS_REQUIRE(ok_dtype(a_dtype) && ok_dtype(b_dtype),
+               "chunk_gated_delta_rule_gated: a and b must be fp32, bf16 or fp16");
+  XOPS_REQUIRE(softplus_beta > 0.f, "chunk_gated_delta_rule_gated: softplus beta must be positive");
+  gdn::GateSrc gs{};
+  gs.a = a;
+  gs.b = b;
+  gs.A_log = A_log;
+  gs.dt_bias = dt_bias;
+  gs.sp_beta = softplus_beta;
+  gs.sp_thr = softplus_threshold;
+  gs.a_dt = a_dtype;
+  gs.b_dt = b_dtype;
+  return chunk_gdn_run(q, k, v, gs, h0, o, ht, cu_seqlens, B, T, N, Hg, H, K, V, q_token_stride,
+                       k_token_stride, v_token_stride, scale, use_qk_l2norm_in_kernel, workspace,
+                       workspace_bytes, stream);
 }
 
 extern "C" int xops_device_error_count(void) {

@@ -2,12 +2,10 @@
 //
 // Follows fused_gdn_gating_decode_kernel
 // (triton_npu/triton_src/test_fused_gdn_gating.py:10-43) and its torch
-// reference (:45-57):
-//   g    = -exp(A_log[h]) * softplus(a + dt_bias[h])      (fp32)
-//   beta = sigmoid(b)                                      (b's dtype)
-// with torch's Softplus(beta, threshold): log(1 + e^{beta x}) / beta, or x
-// where beta x > threshold.  a and b are [rows, heads] (rows = batch for
-// decode, tokens for prefill), g and beta are [1, rows, heads].
+// reference (:45-57); the arithmetic lives in gate_math.cuh, shared with the
+// chunked gated delta rule's fused-gating entry.  a and b are [rows, heads]
+// (rows = batch for decode, tokens for prefill), g and beta are
+// [1, rows, heads].
 //
 // Elementwise and HBM-bound; each thread handles four adjacent elements
 // (one 8- or 16-byte load per input) in a grid-stride loop, and A_log /
@@ -15,14 +13,10 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "gate_math.cuh"
 
 namespace xops {
 namespace {
-
-__device__ __forceinline__ float gate_softplus(float x, float beta, float thr) {
-  const float bx = beta * x;
-  return bx <= thr ? log1pf(expf(bx)) / beta : x;
-}
 
 // Per-head constants -exp(A_log[h]) and dt_bias[h] are computed once per
 // CTA into shared memory (heads <= GATE_SMEM_HEADS; beyond that they are
@@ -63,13 +57,8 @@ __global__ void __launch_bounds__(256) gdn_gating_kernel(
     for (int u = 0; u < 4; ++u) {
       const float nega = cached ? s_nega[h] : -expf(__ldg(A_log + h));
       const float dtb = cached ? s_dtb[h] : __ldg(dt_bias + h);
-      gv[u] = nega * gate_softplus(av[u] + dtb, sp_beta, sp_thr);
-      // sigmoid for an output rounded to b's dtype (fp32 b keeps the full
-      // precision exp and divide)
-      if constexpr (sizeof(TB) == 2)
-        ov[u] = __fdividef(1.0f, 1.0f + __expf(-bv[u]));
-      else
-        ov[u] = 1.0f / (1.0f + expf(-bv[u]));
+      gv[u] = gate_g(nega, av[u], dtb, sp_beta, sp_thr);
+      ov[u] = gate_beta_f32<TB>(bv[u]);
       h = h + 1 == heads ? 0 : h + 1;
     }
     if (full) {

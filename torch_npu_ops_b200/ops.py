@@ -617,6 +617,59 @@ def npu_chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None,
     return o, ht
 
 
+def chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, scale=None, initial_state=None,
+                                 output_final_state=False, cu_seqlens=None,
+                                 use_qk_l2norm_in_kernel=False, softplus_beta=1.0,
+                                 softplus_threshold=20.0):
+    """``npu_fused_gdn_gating`` followed by ``npu_chunk_gated_delta_rule`` as
+    one call: the gates ``g = -exp(A_log) * softplus(a + dt_bias)`` and
+    ``beta = sigmoid(b)`` (rounded to b's dtype) are computed inside the
+    chunked rule's kernels from a, b ``[B, T, H]`` (or ``[T, H]`` with B = 1)
+    and A_log, dt_bias ``[H]`` fp32, with the same arithmetic as the gating
+    operator (npu_triton_fused_gdn_gating.cpp:33-93), so the result equals
+    the two-call sequence bit for bit.  Returns ``(o, final_state or None)``."""
+    _check(q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16,
+           "chunk_gated_delta_rule expects q/k/v to be bfloat16.")
+    _cuda(q, k, v, A_log, a, b, dt_bias, initial_state, cu_seqlens)
+    B, T, Hg, K = q.shape
+    H, V = v.shape[2], v.shape[3]
+    _check(q.shape == k.shape, "q and k must have the same shape.")
+    _check(H % Hg == 0, "chunk_gated_delta_rule expects num_heads_v to be divisible by "
+                        f"num_heads_qk, got {H} and {Hg}")
+    a3 = a if a.dim() == 3 else a.unsqueeze(0)
+    b3 = b if b.dim() == 3 else b.unsqueeze(0)
+    _check(tuple(a3.shape) == (B, T, H) and tuple(b3.shape) == (B, T, H),
+           "a and b must have shape [B, T, H] (or [T, H] with B == 1)")
+    _check(A_log.dtype == torch.float32 and dt_bias.dtype == torch.float32,
+           "A_log and dt_bias must be float32")
+    _check(A_log.numel() == H and dt_bias.numel() == H, "A_log and dt_bias must have H elements")
+    if initial_state is not None:
+        _check(initial_state.dtype in (torch.bfloat16, torch.float32),
+               "chunk_gated_delta_rule expects initial_state to be bfloat16 or float32, got "
+               f"{initial_state.dtype}")
+    cu, _, _, N = _seq_info(q, cu_seqlens)
+    scale_v = float(scale) if scale is not None else K ** -0.5
+    h0 = initial_state.to(torch.float32).contiguous() if initial_state is not None else None
+    if h0 is not None:
+        _check(tuple(h0.shape) == (N, H, K, V), "initial_state must have shape [N, H, K, V]")
+    o = torch.empty((B, T, H, V), dtype=v.dtype, device=v.device)
+    ht = torch.empty((N, H, K, V), dtype=torch.float32, device=v.device) if output_final_state else None
+    qc, kc, vc = _token_rows(q, B), _token_rows(k, B), _token_rows(v, B)
+    ac, bc = a3.contiguous(), b3.contiguous()
+    Al, dtb = A_log.contiguous(), dt_bias.contiguous()
+    l2 = int(bool(use_qk_l2norm_in_kernel))
+    wsb = _lib.load().xops_chunk_gated_delta_rule_workspace_size(B, T, N, Hg, H, K, l2,
+                                                                 int(cu is not None))
+    ws = torch.empty(max(int(wsb), 16), dtype=torch.uint8, device=q.device)
+    _lib.call("xops_chunk_gated_delta_rule_gated", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+              Al.data_ptr(), ac.data_ptr(), bc.data_ptr(), dtb.data_ptr(),
+              _dt(ac, "chunk_gated_delta_rule_gated"), _dt(bc, "chunk_gated_delta_rule_gated"),
+              float(softplus_beta), float(softplus_threshold), _ptr(h0), o.data_ptr(), _ptr(ht),
+              _ptr(cu), B, T, N, Hg, H, K, V, qc.stride(1), kc.stride(1), vc.stride(1), scale_v, l2,
+              ws.data_ptr(), ws.numel(), _stream(q))
+    return o, ht
+
+
 # ---- chunk pipeline sub-operators (reference decomposition, chunk.py:31-73)
 def _ncu(q_like, cu_seqlens):
     cu, b, t, n = _seq_info(q_like, cu_seqlens)

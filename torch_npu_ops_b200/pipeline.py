@@ -18,12 +18,15 @@ from . import ops
 
 def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z, norm_weight,
                 num_k_heads, num_v_heads, head_dim=128, eps=1e-6, query_start_loc=None,
-                events=None):
+                events=None, gating=None):
     """Runs one prefill of a GDN layer on the current CUDA stream.
 
     x: [T, (2 num_k_heads + num_v_heads) head_dim] conv input (q | k | v
     channel blocks), bf16.  conv_state: [N, channels, width - 1], updated in
-    place (a fresh prefill passes zeros).  g, beta: [1, T, num_v_heads] fp32.
+    place (a fresh prefill passes zeros).  g, beta: [1, T, num_v_heads] fp32;
+    or, with ``gating=(A_log, a, b, dt_bias)`` (the inputs of
+    ``npu_fused_gdn_gating``, a and b [T, num_v_heads]), g and beta are None
+    and the gates are computed inside the chunked rule's kernels.
     initial_state: [N, num_v_heads, head_dim, head_dim] fp32 or None.
     z: [T, num_v_heads, head_dim] gate of the output norm.  query_start_loc:
     [N + 1] int32 on the device (None: one sequence of T tokens).
@@ -49,8 +52,13 @@ def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z
     k = y[:, hk * d: 2 * hk * d].view(1, T, hk, d)
     v = y[:, 2 * hk * d:].view(1, T, hv, d)
     cu = None if query_start_loc.numel() == 2 else query_start_loc
-    o, ht = ops.npu_chunk_gated_delta_rule(q, k, v, g, beta, None, initial_state, True, cu, False,
-                                           False)
+    if gating is None:
+        o, ht = ops.npu_chunk_gated_delta_rule(q, k, v, g, beta, None, initial_state, True, cu,
+                                               False, False)
+    else:
+        A_log, a, b, dt_bias = gating
+        o, ht = ops.chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, None, initial_state,
+                                                 True, cu, False)
     if events:
         events[2].record()
     out = ops.layer_norm_fwd(o.view(-1, d), norm_weight, None, eps, z.view(-1, d), d, True, True)
