@@ -151,6 +151,25 @@ XOPS_API int xops_causal_conv1d_varlen_qk_l2norm(
     int64_t total_tokens, int64_t dim, int64_t width, int64_t num_cache_lines, int silu,
     int32_t pad_slot_id, int dtype, int64_t l2_channels, float l2_eps, void* stream);
 
+/* Prefill conv reading the GDN layer's input projection in place:
+ * mixed_qkvz [total_tokens, num_k_heads * (2 + 2r) * 128] (row stride x_ld
+ * elements), per key head q (128) | k (128) | v (r value heads x 128) | z
+ * (r x 128), r = num_v_heads / num_k_heads, the layout
+ * fused_qkvzba_split_reshape_cat de-interleaves
+ * (triton_npu/triton_src/test_fused_qkvzba_split_reshape.py:463-507).  The
+ * conv channels are all q heads, then all k heads, then all v heads
+ * (dim = (2 num_k_heads + num_v_heads) * 128, the order of the split's
+ * mixed_qkv); weight [dim, width], bias [dim], conv_state and out as
+ * xops_causal_conv1d_varlen_qk_l2norm, whose q/k L2 normalisation is applied
+ * when qk_l2norm is set.  Equals the split followed by that conv, without
+ * the split's read and write of the projection. */
+XOPS_API int xops_causal_conv1d_varlen_qkvz(
+    const void* mixed_qkvz, int64_t x_ld, int64_t num_k_heads, int64_t num_v_heads,
+    void* conv_state, const void* weight, const void* bias, const int32_t* query_start_loc,
+    const int32_t* conv_state_indices, void* out, int64_t batch, int64_t total_tokens,
+    int64_t width, int64_t num_cache_lines, int silu, int32_t pad_slot_id, int dtype,
+    int qk_l2norm, float l2_eps, void* stream);
+
 /* De-interleave of the GDN input projections.  mixed_qkvz [rows, nqk *
  * (2 hqk + 2 r hv)] holds per key head q | k | v (r heads) | z (r heads),
  * r = num_heads_v / num_heads_qk in [1, 4]; mixed_ba [rows, nqk * 2r] holds
@@ -269,7 +288,11 @@ XOPS_API int xops_chunk_gated_delta_rule(const void* q, const void* k, const voi
 /* The same rule with fused_gdn_gating folded into its prologue: the gates
  * are computed where the kernels read them, from the layer's projections a,
  * b [B, T, H] (fp32, bf16 or fp16 each, a_dtype / b_dtype XOPS_F32 /
- * XOPS_BF16 / XOPS_F16) and A_log, dt_bias [H] fp32:
+ * XOPS_BF16 / XOPS_F16; ab_token_stride elements between tokens, 0 =
+ * contiguous) or, with ba_interleaved, from the un-split projection
+ * mixed_ba [T, Hg * 2r] itself (a == b; per key head b (r heads) | a (r),
+ * r = H / Hg, the layout fused_qkvzba_split_reshape_cat de-interleaves),
+ * and A_log, dt_bias [H] fp32:
  *   g = -exp(A_log[h]) * softplus(a + dt_bias[h]),  beta = sigmoid(b) in b's dtype
  * with the arithmetic of xops_fused_gdn_gating, so the result equals
  * xops_fused_gdn_gating followed by xops_chunk_gated_delta_rule (beta widened
@@ -280,7 +303,8 @@ XOPS_API int xops_chunk_gated_delta_rule(const void* q, const void* k, const voi
  * pair.  Other arguments and the workspace as xops_chunk_gated_delta_rule. */
 XOPS_API int xops_chunk_gated_delta_rule_gated(
     const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b,
-    const float* dt_bias, int a_dtype, int b_dtype, float softplus_beta, float softplus_threshold,
+    const float* dt_bias, int a_dtype, int b_dtype, int64_t ab_token_stride, int ba_interleaved,
+    float softplus_beta, float softplus_threshold,
     const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
     int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
     int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,

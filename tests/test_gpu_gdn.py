@@ -452,3 +452,49 @@ def test_gdn_prefill_gating_option():
     torch.cuda.synchronize()
     for x1, x2 in zip(*outs):
         assert torch.equal(x1, x2)
+
+
+@pytest.mark.parametrize("T,hk,hv,lens", [(8192, 2, 4, None), (3000, 4, 8, [1000, 64, 1936]),
+                                          (4096, 2, 8, None)])
+def test_gdn_layer_prefill_from_projections(T, hk, hv, lens):
+    """Conv, gating and gated norm read the un-split projections in place;
+    the results equal split -> conv -> gating -> rule -> norm bit for bit,
+    and the rule's output matches the composed oracle."""
+    from torch_npu_ops_b200.pipeline import gdn_layer_prefill, gdn_prefill
+    g = torch.Generator().manual_seed(T + hv)
+    d, r = 128, hv // hk
+    mixed_qkvz = torch.randn(T, hk * (2 + 2 * r) * d, generator=g).to(torch.bfloat16)
+    mixed_ba = torch.randn(T, hk * 2 * r, generator=g).to(torch.bfloat16)
+    C = (2 * hk + hv) * d
+    w = (0.5 * torch.randn(C, 4, generator=g)).to(torch.bfloat16)
+    cb = (0.5 * torch.randn(C, generator=g)).to(torch.bfloat16)
+    A_log = torch.rand(hv, generator=g) * 2.7
+    dt_bias = torch.rand(hv, generator=g)
+    nw = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    lens = lens or [T]
+    N = len(lens)
+    h0 = 0.02 * torch.randn(N, hv, d, d, generator=g)
+    qsl = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    st1 = torch.zeros(N, C, 3, dtype=torch.bfloat16, device=DEV)
+    st2 = st1.clone()
+    fused = gdn_layer_prefill(_to(mixed_qkvz), _to(mixed_ba), st1, _to(w), _to(cb), _to(A_log),
+                              _to(dt_bias), _to(h0), _to(nw), hk, hv, query_start_loc=qsl)
+    mixed_qkv, z, b, a = ops.npu_fused_qkvzba_split_reshape_cat(_to(mixed_qkvz), _to(mixed_ba), hk,
+                                                                hv, d, d)
+    gt, beta = ops.npu_fused_gdn_gating(_to(A_log), a, b, _to(dt_bias))
+    plain = gdn_prefill(mixed_qkv, st2, _to(w), _to(cb), gt, beta.float(), _to(h0), z, _to(nw), hk,
+                        hv, query_start_loc=qsl)
+    torch.cuda.synchronize()
+    for x1, x2 in zip(fused, plain):
+        assert torch.equal(x1, x2)
+    assert torch.equal(st1, st2)
+    # the rule's output against the oracle, from the conv output both paths share
+    y = fused[0].cpu()
+    q = y[:, : hk * d].view(1, T, hk, d)
+    k = y[:, hk * d: 2 * hk * d].view(1, T, hk, d)
+    v = y[:, 2 * hk * d:].view(1, T, hv, d)
+    rg, rb = oracle.fused_gdn_gating(A_log, a.cpu(), b.cpu(), dt_bias)
+    ro, rh = oracle.chunk_gated_delta_rule(q, k, v, rg, rb.to(torch.bfloat16).float(), None, h0, True,
+                                           qsl.cpu() if N > 1 else None, False)
+    assert_bf16_rel(fused[1].cpu(), ro)
+    assert_state(fused[2].cpu(), rh)

@@ -13,6 +13,7 @@ from .ops import (  # noqa: F401
     npu_causal_conv1d_update,
     npu_causal_conv1d_update_v2,
     causal_conv1d_varlen_qk_l2norm,
+    causal_conv1d_varlen_qkvz,
     npu_fused_recurrent_gated_delta_rule,
     npu_fused_gdn_gating,
     npu_fused_qkvzba_split_reshape_cat,

@@ -94,6 +94,8 @@ struct GateSrc {
   const float* dt_bias;
   float sp_beta, sp_thr;
   int a_dt, b_dt;     // XOPS_F32 / XOPS_BF16 / XOPS_F16
+  int64_t ab_ld;      // elements between tokens of a and b
+  int ba_r;           // 0: a, b [T, H]; r > 0: a = b = mixed_ba, per key head b (r) | a (r)
 };
 __device__ __forceinline__ float gate_elem(const void* p, int dt, int64_t i) {
   return dt == XOPS_BF16 ? __bfloat162float(static_cast<const bf16*>(p)[i])
@@ -108,8 +110,13 @@ __device__ __forceinline__ void gate_load(const GateSrc& s, int64_t t, int64_t H
     beta = s.beta[i];
     return;
   }
-  g = gate_g(-expf(s.A_log[h]), gate_elem(s.a, s.a_dt, i), s.dt_bias[h], s.sp_beta, s.sp_thr);
-  const float bv = gate_elem(s.b, s.b_dt, i);
+  int64_t ia = t * s.ab_ld + h, ib = ia;
+  if (s.ba_r) {
+    ib = t * s.ab_ld + (int64_t)(h / s.ba_r) * 2 * s.ba_r + h % s.ba_r;
+    ia = ib + s.ba_r;
+  }
+  g = gate_g(-expf(s.A_log[h]), gate_elem(s.a, s.a_dt, ia), s.dt_bias[h], s.sp_beta, s.sp_thr);
+  const float bv = gate_elem(s.b, s.b_dt, ib);
   beta = s.b_dt == XOPS_BF16  ? gate_beta<bf16>(bv)
          : s.b_dt == XOPS_F16 ? gate_beta<__half>(bv)
                               : gate_beta<float>(bv);
@@ -1737,7 +1744,8 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
 
 extern "C" int xops_chunk_gated_delta_rule_gated(
     const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b,
-    const float* dt_bias, int a_dtype, int b_dtype, float softplus_beta, float softplus_threshold,
+    const float* dt_bias, int a_dtype, int b_dtype, int64_t ab_token_stride, int ba_interleaved,
+    float softplus_beta, float softplus_threshold,
     const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
     int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
     int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
@@ -1746,6 +1754,12 @@ extern "C" int xops_chunk_gated_delta_rule_gated(
   XOPS_REQUIRE(ok_dtype(a_dtype) && ok_dtype(b_dtype),
                "chunk_gated_delta_rule_gated: a and b must be fp32, bf16 or fp16");
   XOPS_REQUIRE(softplus_beta > 0.f, "chunk_gated_delta_rule_gated: softplus beta must be positive");
+  XOPS_REQUIRE(!ba_interleaved || (a == b && a_dtype == b_dtype && Hg >= 1 && H % Hg == 0),
+               "chunk_gated_delta_rule_gated: an interleaved mixed_ba passes the same tensor as "
+               "a and b");
+  if (ab_token_stride == 0) ab_token_stride = ba_interleaved ? 2 * H : H;
+  XOPS_REQUIRE(ab_token_stride >= (ba_interleaved ? 2 * H : H),
+               "chunk_gated_delta_rule_gated: a/b token stride smaller than the row");
   gdn::GateSrc gs{};
   gs.a = a;
   gs.b = b;
@@ -1755,6 +1769,8 @@ extern "C" int xops_chunk_gated_delta_rule_gated(
   gs.sp_thr = softplus_threshold;
   gs.a_dt = a_dtype;
   gs.b_dt = b_dtype;
+  gs.ab_ld = ab_token_stride;
+  gs.ba_r = ba_interleaved ? (int)(H / Hg) : 0;
   return chunk_gdn_run(q, k, v, gs, h0, o, ht, cu_seqlens, B, T, N, Hg, H, K, V, q_token_stride,
                        k_token_stride, v_token_stride, scale, use_qk_l2norm_in_kernel, workspace,
                        workspace_bytes, stream);

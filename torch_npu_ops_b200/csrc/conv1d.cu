@@ -353,11 +353,34 @@ __global__ void __launch_bounds__(256, 3) conv1d_decode_w4_rows_kernel(
 // and the lanes that read a state line are the ones that write its final
 // value, as in the per-thread kernel above.
 // ----------------------------------------------------------------------------
-constexpr int RB_T = 64, RB_C = 256, RB_NS = 2, RB_STAGE = 35840;  // (64 + 5) rows x 512 B, rounded
+// A slab of RB_C channels arrives as two boxes of RB_B channels, each at the
+// source columns of its 128-channel block: the columns are the channels
+// (plain input), or the block's place in the GDN layer's interleaved
+// projection mixed_qkvz (QkvzMap), so the conv reads the projection output
+// directly and the de-interleave pass disappears.
+constexpr int RB_T = 64, RB_C = 256, RB_B = 128, RB_NS = 2, RB_STAGE = 35840;  // 2 x (64 + 5) rows x 256 B, rounded
 constexpr int RB_NT = 32 + 256;
 constexpr int RB_CV = 4;  // channels per consumer lane
 constexpr int RB_SMEM = RB_NS * RB_STAGE + 1024;
 constexpr uint32_t RB_WAIT = 1u << 26;
+
+// Source column of conv channel c.  nqk == 0: c.  Otherwise the input is
+// mixed_qkvz [T, nqk * group] with, per key head i, q (128) | k (128) |
+// v (r value heads x 128) | z (r x 128) (fused_qkvzba_split_reshape_cat,
+// triton_npu/triton_src/test_fused_qkvzba_split_reshape.py:463-507), and
+// the conv channels are all q heads, then all k heads, then all v heads.
+struct QkvzMap {
+  int nqk, r;
+  int64_t group;
+};
+__device__ __forceinline__ int64_t qkvz_col(const QkvzMap& m, int64_t c) {
+  if (m.nqk == 0) return c;
+  const int64_t blk = c >> 7, in = c & 127;
+  if (blk < m.nqk) return blk * m.group + in;
+  if (blk < 2 * m.nqk) return (blk - m.nqk) * m.group + 128 + in;
+  const int64_t j = blk - 2 * m.nqk;
+  return (j / m.r) * m.group + 256 + (j % m.r) * 128 + in;
+}
 
 struct RbTile {
   int64_t t0, sstart, send;
@@ -405,7 +428,7 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
     const T* __restrict__ weight, const T* __restrict__ bias, const int32_t* __restrict__ qsl,
     const int32_t* __restrict__ slots, T* __restrict__ out, int nseq, int64_t dim,
     int64_t tiles_per_slab, int64_t total_tiles, int box_c, bool silu, int32_t pad_slot,
-    int64_t l2_channels, float l2_eps) {
+    int64_t l2_channels, float l2_eps, int64_t x_ld, QkvzMap cm) {
   constexpr int H = W - 1;
   extern __shared__ unsigned char rb_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(
@@ -461,8 +484,12 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
           rb_mbar_arrive(&full[s]);
           continue;
         }
-        rb_expect_tx(&full[s], (uint32_t)((RB_T + H) * box_c * sizeof(T)));
-        rb_tma_load(sm + s * RB_STAGE, &xmap, ti.slab * RB_C, (int)(ti.t0 - H), &full[s]);
+        const int64_t ch0 = (int64_t)ti.slab * RB_C;
+        const int nb = ch0 + box_c < dim ? 2 : 1;  // boxes of this slab
+        rb_expect_tx(&full[s], (uint32_t)(nb * (RB_T + H) * box_c * sizeof(T)));
+        for (int bb = 0; bb < nb; ++bb)
+          rb_tma_load(sm + s * RB_STAGE + bb * (RB_T + H) * box_c * (int)sizeof(T), &xmap,
+                      (int)qkvz_col(cm, ch0 + bb * box_c), (int)(ti.t0 - H), &full[s]);
       }
     }
     return;
@@ -496,8 +523,11 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
                       : make_float2(0.f, 0.f);
         }
       }
-      const unsigned char* stg = sm + s * RB_STAGE + quad * (RB_CV * 2) + tg * 16 * (box_c * 2);
+      // channel quad * 4 of the slab: box quad * 4 / box_c, rows box_c apart
+      const int qb = quad * RB_CV / box_c, qin = quad * RB_CV - qb * box_c;
       const int rstride = box_c * 2;
+      const unsigned char* stg = sm + s * RB_STAGE + qb * (RB_T + H) * rstride + qin * 2 +
+                                 tg * 16 * rstride;
       float2 hist[H > 0 ? H : 1][2];
       const bool first = ti.t0 == ti.sstart && tg == 0;
       T* st_line = state + ((int64_t)ti.line * dim + c0) * H;
@@ -585,7 +615,7 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
           const int64_t pos = len - H + j;
           float v[RB_CV];
           if (pos >= 0) {
-            load_vec<T, RB_CV>(x + (ti.sstart + pos) * dim + c0, v);
+            load_vec<T, RB_CV>(x + (ti.sstart + pos) * x_ld + qkvz_col(cm, c0), v);
           } else {
 #pragma unroll
             for (int c = 0; c < RB_CV; ++c) v[c] = to_f32<T>(st_line[c * H + H + pos]);
@@ -618,13 +648,17 @@ template <typename T>
 int launch_varlen_tma(int W, const void* x, void* state, const void* w, const void* b,
                       const int32_t* qsl, const int32_t* slots, void* out, int nseq,
                       int64_t total, int64_t dim, bool silu, int32_t pad, cudaStream_t st,
-                      int64_t l2_channels = 0, float l2_eps = 0.f) {
+                      int64_t l2_channels = 0, float l2_eps = 0.f, int64_t x_ld = 0,
+                      QkvzMap cm = QkvzMap{0, 1, 0}) {
   auto enc = conv_map_encoder();
   if (!enc) return set_error(XOPS_ERR_CUDA, "causal_conv1d_varlen: cuTensorMapEncodeTiled is unavailable");
+  if (x_ld == 0) x_ld = dim;
   CUtensorMap m;
-  cuuint64_t dims[2] = {(cuuint64_t)dim, (cuuint64_t)total};
-  cuuint64_t strides[1] = {(cuuint64_t)(dim * (int64_t)sizeof(T))};
-  const int box_c = (int)std::min<int64_t>(dim, RB_C);  // slab width; dim is a multiple of 8
+  // the map spans the source rows: the channels, or the projection's columns
+  const int64_t src_cols = cm.nqk ? cm.nqk * cm.group : dim;
+  cuuint64_t dims[2] = {(cuuint64_t)src_cols, (cuuint64_t)total};
+  cuuint64_t strides[1] = {(cuuint64_t)(x_ld * (int64_t)sizeof(T))};
+  const int box_c = (int)std::min<int64_t>(dim, RB_B);  // box width; dim is a multiple of 8
   cuuint32_t box[2] = {(cuuint32_t)box_c, (cuuint32_t)(RB_T + W - 1)};
   cuuint32_t es[2] = {1, 1};
   const CUresult r = enc(&m, sizeof(T) == 2 ? (std::is_same<T, __half>::value
@@ -654,7 +688,8 @@ int launch_varlen_tma(int W, const void* x, void* state, const void* w, const vo
       return set_error(XOPS_ERR_CUDA, "causal_conv1d_varlen: shared-memory attribute failed"); \
     kern<<<grid, RB_NT, RB_SMEM, st>>>(m, (const T*)x, (T*)state, (const T*)w, (const T*)b,    \
                                        qsl, slots, (T*)out, nseq, dim, tiles_per_slab,          \
-                                       total_tiles, box_c, silu, pad, l2_channels, l2_eps);     \
+                                       total_tiles, box_c, silu, pad, l2_channels, l2_eps,      \
+                                       x_ld, cm);                                               \
     return check_launch("causal_conv1d_varlen");                                               \
   }
     XOPS_CT(2) XOPS_CT(3) XOPS_CT(4) XOPS_CT(5) XOPS_CT(6)
@@ -871,6 +906,46 @@ extern "C" int xops_causal_conv1d_varlen_qk_l2norm(
   return launch_varlen_tma<__half>((int)width, x, conv_state, weight, bias, query_start_loc,
                                    conv_state_indices, out, (int)batch, total_tokens, dim,
                                    silu != 0, pad_slot_id, st, l2_channels, l2_eps);
+}
+
+extern "C" int xops_causal_conv1d_varlen_qkvz(
+    const void* mixed_qkvz, int64_t x_ld, int64_t num_k_heads, int64_t num_v_heads,
+    void* conv_state, const void* weight, const void* bias, const int32_t* query_start_loc,
+    const int32_t* conv_state_indices, void* out, int64_t batch, int64_t total_tokens,
+    int64_t width, int64_t num_cache_lines, int silu, int32_t pad_slot_id, int dtype,
+    int qk_l2norm, float l2_eps, void* stream) {
+  XOPS_REQUIRE(batch >= 0 && total_tokens >= 0 && num_k_heads >= 1 && num_v_heads >= 1 &&
+                   num_v_heads % num_k_heads == 0,
+               "causal_conv1d_varlen_qkvz: bad shape (num_v_heads must be a multiple of "
+               "num_k_heads)");
+  XOPS_REQUIRE(width >= 2 && width <= 6,
+               "causal_conv1d_varlen_qkvz expects width in [2, 6], got %lld", (long long)width);
+  XOPS_UNSUPPORTED(dtype == XOPS_BF16 || dtype == XOPS_F16,
+                   "causal_conv1d_varlen_qkvz: 16-bit activations only");
+  const int64_t r = num_v_heads / num_k_heads, group = 128 * (2 + 2 * r);
+  const int64_t dim = 128 * (2 * num_k_heads + num_v_heads);
+  XOPS_REQUIRE(x_ld >= num_k_heads * group && x_ld % 8 == 0,
+               "causal_conv1d_varlen_qkvz: the projection's row stride must cover its %lld "
+               "columns and be a multiple of 8", (long long)(num_k_heads * group));
+  XOPS_REQUIRE(conv_state_indices || num_cache_lines >= batch,
+               "causal_conv1d_varlen_qkvz: conv_state has fewer lines than sequences");
+  if (batch == 0 || total_tokens == 0) return XOPS_OK;
+  XOPS_REQUIRE(mixed_qkvz && conv_state && weight && query_start_loc && out,
+               "causal_conv1d_varlen_qkvz: null pointer");
+  XOPS_REQUIRE(aligned16(mixed_qkvz) && aligned16(out),
+               "causal_conv1d_varlen_qkvz: mixed_qkvz/out must be 16-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  const QkvzMap cm{(int)num_k_heads, (int)r, group};
+  const int64_t l2c = qk_l2norm ? 2 * 128 * num_k_heads : 0;
+  if (dtype == XOPS_BF16)
+    return launch_varlen_tma<__nv_bfloat16>((int)width, mixed_qkvz, conv_state, weight, bias,
+                                            query_start_loc, conv_state_indices, out, (int)batch,
+                                            total_tokens, dim, silu != 0, pad_slot_id, st, l2c,
+                                            l2_eps, x_ld, cm);
+  return launch_varlen_tma<__half>((int)width, mixed_qkvz, conv_state, weight, bias,
+                                   query_start_loc, conv_state_indices, out, (int)batch,
+                                   total_tokens, dim, silu != 0, pad_slot_id, st, l2c, l2_eps, x_ld,
+                                   cm);
 }
 
 extern "C" int xops_causal_conv1d_update(const void* x, void* conv_state, const void* weight,

@@ -337,8 +337,13 @@ __device__ __forceinline__ void norm_stream_produce(const TX* __restrict__ x,
                                                     uint64_t* full, uint64_t* empty,
                                                     int* abort_sh, int64_t total, int64_t G,
                                                     int64_t spt, int tile_bytes, int stage,
-                                                    int64_t ngroups = 1, int64_t sx = -1) {
+                                                    int64_t ngroups = 1, int64_t sx = -1,
+                                                    int64_t sz = -1) {
+  // strided rows (one copy per row of ngroups segments): x of the GDN q/k
+  // L2 pre-pass, z of the gated norm read in place from the layer's
+  // interleaved projection
   const bool strided = sx >= 0 && sx != ngroups * G;
+  const bool zstrided = sz >= 0 && sz != ngroups * G;
   const int64_t tiles = (total + spt - 1) / spt;
   for (int64_t k = 0;; ++k) {
     const int64_t t = blockIdx.x + k * gridDim.x;
@@ -362,7 +367,15 @@ __device__ __forceinline__ void norm_stream_produce(const TX* __restrict__ x,
     } else {
       tc::bulk_load(st, x + s0 * G, bytes, &full[s]);
     }
-    if constexpr (HAS_Z) tc::bulk_load(st + tile_bytes, z + s0 * G, bytes, &full[s]);
+    if constexpr (HAS_Z) {
+      if (zstrided) {
+        const uint32_t rb = (uint32_t)(ngroups * G * 2);
+        for (int64_t r = 0; r < n / ngroups; ++r)
+          tc::bulk_load(st + tile_bytes + r * rb, z + (s0 / ngroups + r) * sz, rb, &full[s]);
+      } else {
+        tc::bulk_load(st + tile_bytes, z + s0 * G, bytes, &full[s]);
+      }
+    }
   }
 }
 
@@ -370,7 +383,7 @@ template <typename TX, typename TW, int G, int KIND, bool HAS_Z, bool HAS_B>
 __global__ void __launch_bounds__(RN_NT, 2) norm_stream_kernel(
     const TX* __restrict__ x, const TW* __restrict__ w, const TW* __restrict__ b,
     const TX* __restrict__ z, TX* __restrict__ y, float* __restrict__ mean_out,
-    float* __restrict__ rstd_out, int64_t M, int64_t ngroups, int64_t sx, float eps,
+    float* __restrict__ rstd_out, int64_t M, int64_t ngroups, int64_t sx, int64_t sz, float eps,
     bool norm_before_gate) {
   constexpr int SEGS = RN_TILE_BYTES / (G * 2);   // segments per tile
   constexpr int LPR = G / 8;                       // lanes per segment
@@ -396,7 +409,7 @@ __global__ void __launch_bounds__(RN_NT, 2) norm_stream_kernel(
   if (warp == 0) {
     if (lane == 0)
       norm_stream_produce<TX, HAS_Z>(x, z, sm, full, empty, &abort_sh, total, G, SEGS,
-                                     RN_TILE_BYTES, STAGE, ngroups, sx);
+                                     RN_TILE_BYTES, STAGE, ngroups, sx, sz);
     return;
   }
   const int cw = warp - 1, sub = lane / LPR, li = lane % LPR;
@@ -765,7 +778,7 @@ int sm_count() {
 template <typename TX, typename TW, int GG, int KIND, bool HAS_Z, bool HAS_B>
 int launch_norm_stream(const void* x, const void* w, const void* b, const void* z, void* y,
                        float* mean, float* rstd, int64_t M, int64_t ng, float eps, bool nbg,
-                       cudaStream_t st, const char* what, int64_t sx = -1) {
+                       cudaStream_t st, const char* what, int64_t sx = -1, int64_t sz = -1) {
   constexpr int SEGS = RN_TILE_BYTES / (GG * 2);
   constexpr int SMEM = RN_NS * (HAS_Z ? 2 : 1) * RN_TILE_BYTES + 128;
   auto kern = norm_stream_kernel<TX, TW, GG, KIND, HAS_Z, HAS_B>;
@@ -776,7 +789,7 @@ int launch_norm_stream(const void* x, const void* w, const void* b, const void* 
   const int64_t tiles = cdiv64(M * ng, SEGS);
   const unsigned grid = (unsigned)std::min<int64_t>(tiles, 2 * (int64_t)sm_count());
   kern<<<grid, RN_NT, SMEM, st>>>((const TX*)x, (const TW*)w, (const TW*)b, (const TX*)z, (TX*)y,
-                                  mean, rstd, M, ng, sx, eps, nbg);
+                                  mean, rstd, M, ng, sx, sz, eps, nbg);
   return check_launch(what);
 }
 
@@ -809,21 +822,24 @@ int launch_norm_wide(const void* x, const void* w, const void* b, const void* z,
 template <typename TX, typename TW, int KIND, bool HAS_Z, bool HAS_B>
 int dispatch_stream(const void* x, const void* w, const void* b, const void* z, void* y,
                     float* mean, float* rstd, int64_t M, int64_t N, int64_t G, float eps,
-                    bool nbg, cudaStream_t st, const char* what) {
+                    bool nbg, cudaStream_t st, const char* what, int64_t sz = -1) {
   if constexpr (sizeof(TX) != 2) {
     return -1;
   } else {
     const int64_t ng = N / G;
     const int64_t segs = M * ng;
+    const bool zstr = HAS_Z && sz >= 0 && sz != N;  // z rows sz elements apart
     if (segs >= (int64_t(1) << 31) || G % 8 != 0) return -1;
     if (!aligned16(x) || !aligned16(y) || (HAS_Z && !aligned16(z))) return -1;
     if (KIND != K_L2 && !aligned16(w)) return -1;
     if (HAS_B && !aligned16(b)) return -1;
+    // strided z: each tile must hold whole rows, and each row copy starts on 16 bytes
+    if (zstr && (G > 256 || (RN_TILE_BYTES / (G * 2)) % ng != 0 || (sz * 2) % 16 != 0)) return -1;
     if (G <= 256) {
       if (segs < 8192) return -1;
-      if (G == 64) return launch_norm_stream<TX, TW, 64, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st, what);
-      if (G == 128) return launch_norm_stream<TX, TW, 128, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st, what);
-      if (G == 256) return launch_norm_stream<TX, TW, 256, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st, what);
+      if (G == 64) return launch_norm_stream<TX, TW, 64, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st, what, -1, sz);
+      if (G == 128) return launch_norm_stream<TX, TW, 128, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st, what, -1, sz);
+      if (G == 256) return launch_norm_stream<TX, TW, 256, KIND, HAS_Z, HAS_B>(x, w, b, z, y, mean, rstd, M, ng, eps, nbg, st, what, -1, sz);
       return -1;
     }
     if (G > (HAS_Z ? 8192 : 16384)) return -1;
@@ -840,10 +856,11 @@ int dispatch_ln(const void* x, const void* w, const void* b, const void* z, void
                 float* rstd, int64_t M, int64_t N, int64_t G, int64_t sx, int64_t sz, int64_t sy,
                 float eps, bool nbg, cudaStream_t st) {
   const int64_t ng = N / G;
-  // streaming path: 16-bit, contiguous rows (segments adjacent in memory)
-  if (sx == N && sy == N && (!HAS_Z || sz == N)) {
+  // streaming path: 16-bit, contiguous x and y rows (segments adjacent in
+  // memory); z rows contiguous or strided
+  if (sx == N && sy == N && (!HAS_Z || sz >= N)) {
     const int rc = dispatch_stream<TX, TW, RMS ? K_RMS : K_LN, HAS_Z, HAS_B>(
-        x, w, b, z, y, mean, rstd, M, N, G, eps, nbg, st, "layer_norm_fwd");
+        x, w, b, z, y, mean, rstd, M, N, G, eps, nbg, st, "layer_norm_fwd", HAS_Z ? sz : -1);
     if (rc >= 0) return rc;
   }
   // packed path: 16-byte lanes, several short segments per warp

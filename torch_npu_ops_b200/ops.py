@@ -378,6 +378,48 @@ def causal_conv1d_varlen_qk_l2norm(x, conv_state, weight, bias, query_start_loc,
     return out
 
 
+def causal_conv1d_varlen_qkvz(mixed_qkvz, conv_state, weight, bias, query_start_loc,
+                              num_k_heads, num_v_heads, activation=True, qk_l2norm=True, eps=1e-6,
+                              conv_state_indices=None, pad_slot_id=-1):
+    """The GDN layer's prefill conv fed straight from its input projection.
+
+    ``mixed_qkvz [num_tokens, num_k_heads * (2 + 2r) * 128]`` holds, per key
+    head, q | k | v (r value heads) | z (r heads), r = num_v_heads /
+    num_k_heads (the input of ``npu_fused_qkvzba_split_reshape_cat``).  The
+    result equals that split's ``mixed_qkv`` through
+    ``causal_conv1d_varlen_qk_l2norm`` (q/k L2-normalised when
+    ``qk_l2norm``), computed without materialising ``mixed_qkv``.  Returns
+    the conv output ``[num_tokens, (2 num_k_heads + num_v_heads) * 128]``;
+    conv_state (``[lines, dim, width - 1]``) is updated in place."""
+    _cuda(mixed_qkvz, conv_state, weight, bias, query_start_loc, conv_state_indices)
+    _check(mixed_qkvz.dim() == 2 and mixed_qkvz.stride(1) == 1,
+           "causal_conv1d_varlen_qkvz expects mixed_qkvz [tokens, cols] with contiguous rows")
+    _check(mixed_qkvz.dtype in (torch.bfloat16, torch.float16),
+           "causal_conv1d_varlen_qkvz expects bf16 or fp16 activations")
+    _check(num_v_heads % num_k_heads == 0, "num_v_heads must be a multiple of num_k_heads")
+    r = num_v_heads // num_k_heads
+    _check(mixed_qkvz.size(1) == num_k_heads * (2 + 2 * r) * 128,
+           "mixed_qkvz must hold num_k_heads * (2 + 2r) * 128 columns")
+    dim, width = (2 * num_k_heads + num_v_heads) * 128, weight.size(1)
+    _check(weight.size(0) == dim and conv_state.size(1) == dim and conv_state.size(2) >= width - 1,
+           "causal_conv1d_varlen_qkvz: shape mismatch")
+    _check(conv_state.is_contiguous() and conv_state.dtype == mixed_qkvz.dtype,
+           "causal_conv1d_varlen_qkvz: conv_state must be contiguous in x's dtype")
+    qsl = _i32(query_start_loc)
+    idx = _i32(conv_state_indices)
+    batch = qsl.numel() - 1
+    b = bias.to(mixed_qkvz.dtype).contiguous() if bias is not None else None
+    T = mixed_qkvz.size(0)
+    out = torch.empty((T, dim), dtype=mixed_qkvz.dtype, device=mixed_qkvz.device)
+    _lib.call("xops_causal_conv1d_varlen_qkvz", mixed_qkvz.data_ptr(), mixed_qkvz.stride(0),
+              num_k_heads, num_v_heads, conv_state.data_ptr(),
+              weight.to(mixed_qkvz.dtype).contiguous().data_ptr(), _ptr(b), qsl.data_ptr(),
+              _ptr(idx), out.data_ptr(), batch, T, width, conv_state.size(0),
+              int(bool(activation)), int(pad_slot_id), _dt(mixed_qkvz, "causal_conv1d_varlen_qkvz"),
+              int(bool(qk_l2norm)), float(eps), _stream(mixed_qkvz))
+    return out
+
+
 # ---------------------------------------------------------- gated delta rule
 def _seq_info(q, cu_seqlens):
     b, t = q.shape[0], q.shape[1]
@@ -620,14 +662,17 @@ def npu_chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None,
 def chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, scale=None, initial_state=None,
                                  output_final_state=False, cu_seqlens=None,
                                  use_qk_l2norm_in_kernel=False, softplus_beta=1.0,
-                                 softplus_threshold=20.0):
+                                 softplus_threshold=20.0, mixed_ba=None):
     """``npu_fused_gdn_gating`` followed by ``npu_chunk_gated_delta_rule`` as
     one call: the gates ``g = -exp(A_log) * softplus(a + dt_bias)`` and
     ``beta = sigmoid(b)`` (rounded to b's dtype) are computed inside the
     chunked rule's kernels from a, b ``[B, T, H]`` (or ``[T, H]`` with B = 1)
     and A_log, dt_bias ``[H]`` fp32, with the same arithmetic as the gating
     operator (npu_triton_fused_gdn_gating.cpp:33-93), so the result equals
-    the two-call sequence bit for bit.  Returns ``(o, final_state or None)``."""
+    the two-call sequence bit for bit.  With ``mixed_ba [T, Hg * 2r]`` (the
+    un-split projection: per key head b (r heads) | a (r heads)) a and b are
+    None and the gates are read from it in place.  Returns
+    ``(o, final_state or None)``."""
     _check(q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16,
            "chunk_gated_delta_rule expects q/k/v to be bfloat16.")
     _cuda(q, k, v, A_log, a, b, dt_bias, initial_state, cu_seqlens)
@@ -636,10 +681,17 @@ def chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, scale=None, init
     _check(q.shape == k.shape, "q and k must have the same shape.")
     _check(H % Hg == 0, "chunk_gated_delta_rule expects num_heads_v to be divisible by "
                         f"num_heads_qk, got {H} and {Hg}")
-    a3 = a if a.dim() == 3 else a.unsqueeze(0)
-    b3 = b if b.dim() == 3 else b.unsqueeze(0)
-    _check(tuple(a3.shape) == (B, T, H) and tuple(b3.shape) == (B, T, H),
-           "a and b must have shape [B, T, H] (or [T, H] with B == 1)")
+    if mixed_ba is not None:
+        _check(a is None and b is None, "pass either a and b or mixed_ba")
+        _check(B == 1 and mixed_ba.dim() == 2 and tuple(mixed_ba.shape) == (T, 2 * H)
+               and mixed_ba.stride(1) == 1, "mixed_ba must have shape [T, 2 H] with contiguous rows")
+        _cuda(mixed_ba)
+        a3 = b3 = mixed_ba
+    else:
+        a3 = a if a.dim() == 3 else a.unsqueeze(0)
+        b3 = b if b.dim() == 3 else b.unsqueeze(0)
+        _check(tuple(a3.shape) == (B, T, H) and tuple(b3.shape) == (B, T, H),
+               "a and b must have shape [B, T, H] (or [T, H] with B == 1)")
     _check(A_log.dtype == torch.float32 and dt_bias.dtype == torch.float32,
            "A_log and dt_bias must be float32")
     _check(A_log.numel() == H and dt_bias.numel() == H, "A_log and dt_bias must have H elements")
@@ -655,7 +707,12 @@ def chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, scale=None, init
     o = torch.empty((B, T, H, V), dtype=v.dtype, device=v.device)
     ht = torch.empty((N, H, K, V), dtype=torch.float32, device=v.device) if output_final_state else None
     qc, kc, vc = _token_rows(q, B), _token_rows(k, B), _token_rows(v, B)
-    ac, bc = a3.contiguous(), b3.contiguous()
+    if mixed_ba is not None:
+        ac = bc = mixed_ba
+        ab_ld, inter = mixed_ba.stride(0), 1
+    else:
+        ac, bc = a3.contiguous(), b3.contiguous()
+        ab_ld, inter = H, 0
     Al, dtb = A_log.contiguous(), dt_bias.contiguous()
     l2 = int(bool(use_qk_l2norm_in_kernel))
     wsb = _lib.load().xops_chunk_gated_delta_rule_workspace_size(B, T, N, Hg, H, K, l2,
@@ -664,7 +721,8 @@ def chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, scale=None, init
     _lib.call("xops_chunk_gated_delta_rule_gated", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(),
               Al.data_ptr(), ac.data_ptr(), bc.data_ptr(), dtb.data_ptr(),
               _dt(ac, "chunk_gated_delta_rule_gated"), _dt(bc, "chunk_gated_delta_rule_gated"),
-              float(softplus_beta), float(softplus_threshold), _ptr(h0), o.data_ptr(), _ptr(ht),
+              ab_ld, inter, float(softplus_beta), float(softplus_threshold), _ptr(h0), o.data_ptr(),
+              _ptr(ht),
               _ptr(cu), B, T, N, Hg, H, K, V, qc.stride(1), kc.stride(1), vc.stride(1), scale_v, l2,
               ws.data_ptr(), ws.numel(), _stream(q))
     return o, ht

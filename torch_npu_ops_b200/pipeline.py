@@ -65,3 +65,52 @@ def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z
     if events:
         events[3].record()
     return y, o, ht, out
+
+
+def gdn_layer_prefill(mixed_qkvz, mixed_ba, conv_state, conv_weight, conv_bias, A_log, dt_bias,
+                      initial_state, norm_weight, num_k_heads, num_v_heads, head_dim=128,
+                      eps=1e-6, query_start_loc=None, events=None):
+    """One prefill of a GDN layer from its input projections.
+
+    A caller of the reference runs ``npu_fused_qkvzba_split_reshape_cat`` ->
+    conv -> ``npu_fused_gdn_gating`` -> ``npu_chunk_gated_delta_rule`` ->
+    gated ``layer_norm_fwd``.  Here nothing is de-interleaved: the conv
+    reads q, k, v from ``mixed_qkvz [T, Hk * (2 + 2r) * 128]`` in place
+    (``causal_conv1d_varlen_qkvz``), the chunked rule computes its gates
+    from ``mixed_ba [T, Hk * 2r]`` in place, and the gated norm reads z from
+    ``mixed_qkvz`` as a strided view (r = num_v_heads / num_k_heads).  The
+    results equal the five-call sequence bit for bit.
+
+    Returns (conv output [T, (2 Hk + Hv) 128] with q/k L2-normalised, o
+    [1, T, Hv, 128], final state [N, Hv, 128, 128] fp32, normed output
+    [T * Hv, 128]).  ``events``: optional list of 4 CUDA events recorded
+    before the conv and after each stage.
+    """
+    T = mixed_qkvz.shape[0]
+    hk, hv, d = num_k_heads, num_v_heads, head_dim
+    r = hv // hk
+    gw = (2 + 2 * r) * d
+    if query_start_loc is None:
+        query_start_loc = torch.tensor([0, T], dtype=torch.int32, device=mixed_qkvz.device)
+    if events:
+        events[0].record()
+    y = ops.causal_conv1d_varlen_qkvz(mixed_qkvz, conv_state, conv_weight, conv_bias,
+                                      query_start_loc, hk, hv, True, True, eps)
+    if events:
+        events[1].record()
+    q = y[:, : hk * d].view(1, T, hk, d)
+    k = y[:, hk * d: 2 * hk * d].view(1, T, hk, d)
+    v = y[:, 2 * hk * d:].view(1, T, hv, d)
+    cu = None if query_start_loc.numel() == 2 else query_start_loc
+    o, ht = ops.chunk_gated_delta_rule_gated(q, k, v, A_log, None, None, dt_bias, None,
+                                             initial_state, True, cu, False, mixed_ba=mixed_ba)
+    if events:
+        events[2].record()
+    # rows of r value heads: o's r heads of (token, key head) are adjacent, and
+    # so are their z heads in the projection, a row of gw elements further on
+    z = mixed_qkvz.view(T * hk, gw)[:, (2 + r) * d:]
+    out = ops.layer_norm_fwd(o.view(T * hk, r * d), norm_weight.repeat(r), None, eps, z, d, True,
+                             True)
+    if events:
+        events[3].record()
+    return y, o, ht, out.view(T * hv, d)
