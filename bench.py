@@ -338,14 +338,72 @@ def kernel_sweep(dev, peaks, profile=False):
     return out
 
 
+def layer_compare(dev, T, steps, warmup):
+    """cfg5-shaped GDN layer prefill (Hk 16 -> Hv 32) from the projection
+    outputs mixed_qkvz / mixed_ba: the fused path (no split, gates and z read
+    in place) against the reference's sequence of five operators on the same
+    kernels.  Times are CUDA events around each step, median of `steps`."""
+    import torch_npu_ops_b200 as ops
+    from torch_npu_ops_b200.pipeline import gdn_layer_prefill, gdn_prefill
+    hk, hv, d = 16, 32, 128
+    r = hv // hk
+    C = (2 * hk + hv) * d
+    g = torch.Generator(device=dev).manual_seed(6)
+    mixed_qkvz = torch.randn(T, hk * (2 + 2 * r) * d, generator=g, device=dev).to(torch.bfloat16)
+    mixed_ba = torch.randn(T, hk * 2 * r, generator=g, device=dev).to(torch.bfloat16)
+    w = (0.5 * torch.randn(C, 4, generator=g, device=dev)).to(torch.bfloat16)
+    cb = (0.5 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
+    A_log = torch.rand(hv, generator=g, device=dev) * 2.7
+    dt_bias = torch.rand(hv, generator=g, device=dev)
+    nw = (1 + 0.1 * torch.randn(d, generator=g, device=dev)).to(torch.bfloat16)
+    h0 = 0.02 * torch.randn(1, hv, d, d, generator=g, device=dev)
+    qsl = torch.tensor([0, T], dtype=torch.int32, device=dev)
+    st = torch.zeros(1, C, 3, dtype=torch.bfloat16, device=dev)
+
+    def fused():
+        st.zero_()
+        return gdn_layer_prefill(mixed_qkvz, mixed_ba, st, w, cb, A_log, dt_bias, h0, nw, hk, hv,
+                                 query_start_loc=qsl)
+
+    def unfused():
+        st.zero_()
+        mixed_qkv, z, b, a = ops.npu_fused_qkvzba_split_reshape_cat(mixed_qkvz, mixed_ba, hk, hv,
+                                                                    d, d)
+        gt, beta = ops.npu_fused_gdn_gating(A_log, a, b, dt_bias)
+        return gdn_prefill(mixed_qkv, st, w, cb, gt, beta.float(), h0, z, nw, hk, hv,
+                           query_start_loc=qsl)
+
+    res = {}
+    for name, fn in (("fused", fused), ("five_operators", unfused)):
+        for _ in range(warmup):
+            fn()
+        ts = []
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ms = sorted(ts)[len(ts) // 2]
+        res[name] = {"ms_per_step": ms, "tokens_per_s": T / (ms / 1000.0)}
+    res["speedup"] = res["five_operators"]["ms_per_step"] / res["fused"]["ms_per_step"]
+    return {"metric": "GDN layer prefill from the input projections, tokens/s", "workload": "layer",
+            "config": {"tokens": T, "k_heads": hk, "v_heads": hv, "head_dim": d,
+                       "inputs": "mixed_qkvz [T, 12288], mixed_ba [T, 64] bf16 ~N(0,1), resident",
+                       "l2_flush": "inputs > L2 (1.6 GB per step)"}, **res}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cfg5", choices=["cfg5", "cfg3", "kernels"],
-                    help="kernels: HBM bandwidth of every bandwidth-bound operator")
+    ap.add_argument("--workload", default="cfg5", choices=["cfg5", "cfg3", "kernels", "layer"],
+                    help="kernels: HBM bandwidth of every bandwidth-bound operator; layer: the "
+                         "GDN layer prefill from its un-split projections, fused against the "
+                         "split -> conv -> gating -> rule -> norm sequence")
     ap.add_argument("--tokens", type=int, default=65536)
     ap.add_argument("--cpu-sample", type=int, default=8192)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -400,6 +458,10 @@ def main():
                               "back_to_back": "ms_back_to_back: 20 replays between one event pair, no flush",
                               "hbm_peak_gbs": peaks["hbm_gbs"], "peak_source": peaks["source"],
                               "kernels": kernel_sweep(dev, peaks, a.profile)}))
+        return
+    if kind == "layer":
+        if rank == 0:
+            print(json.dumps(layer_compare(dev, a.tokens, a.steps, a.warmup)))
         return
     if world > 1:
         import torch.distributed as dist

@@ -85,14 +85,14 @@ def test_empty_inputs_are_noops(lib):
 
 def test_chunk_workspace_rules(lib):
     assert lib.xops_chunk_gated_delta_rule_workspace_size(1, 16384, 8, 16, 32, 128, 0, 1) == \
-        (16384 // 64 + 8) * 32 * 32768
+        (16384 // 64 + 8) * 32 * 33280
     with_l2 = lib.xops_chunk_gated_delta_rule_workspace_size(2, 100, 2, 2, 4, 128, 1, 0)
-    assert with_l2 == 2 * 2 * 4 * 32768 + 2 * 2 * 100 * 2 * 128 * 2
+    assert with_l2 == 2 * 2 * 4 * 33280 + 2 * 2 * 100 * 2 * 128 * 2
     # one long sequence over few heads: the chain is cut into 205-chunk
     # segments and three fp32 states per (segment slot, head) are added
     long_seq = lib.xops_chunk_gated_delta_rule_workspace_size(1, 65536, 1, 16, 32, 128, 0, 1)
     slots = (1024 + 1 + 204) // 205 + 1
-    assert long_seq == (1024 + 1) * 32 * 32768 + slots * 32 * 3 * 128 * 128 * 4
+    assert long_seq == (1024 + 1) * 32 * 33280 + slots * 32 * 3 * 128 * 128 * 4
     rc, msg = _call(lib, "xops_chunk_gated_delta_rule", 16, 16, 16, 16, 16, None, 16, None, None,
                     1, 64, 1, 1, 1, 128, 128, 0, 0, 0, 0.1, 0, None, 0, None)
     assert rc == 4 and "workspace" in msg

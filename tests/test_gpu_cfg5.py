@@ -134,7 +134,7 @@ def test_cfg5_runs_the_segmented_chain():
     (the workspace then holds segment states past the per-chunk part)."""
     lib = _lib.load()
     for hv in (32, 16, 8, 4):
-        per_chunk = (T // 64) * hv * 32768 + 2 * T * (hv // 2) * D * 2
+        per_chunk = (T // 64) * hv * 33280 + 2 * T * (hv // 2) * D * 2
         assert lib.xops_chunk_gated_delta_rule_workspace_size(1, T, 1, hv // 2, hv, D, 1, 0) > \
             per_chunk
 

@@ -85,7 +85,7 @@ def _segmented(B, T, N, hk, hv, varlen):
     lib = _lib.load()
     chunks = T // 64 + N if varlen else B * ((T + 63) // 64)
     return lib.xops_chunk_gated_delta_rule_workspace_size(B, T, N, hk, hv, 128, 0, int(varlen)) > \
-        chunks * hv * 32768
+        chunks * hv * 33280
 
 
 @pytest.mark.parametrize("lens,hk,hv,l2", [

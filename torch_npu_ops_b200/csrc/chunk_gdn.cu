@@ -55,8 +55,11 @@ __device__ int g_tc_error = 0;
 namespace {
 
 constexpr uint32_t WAIT_LIMIT = 1u << 26;
-constexpr int WS_CHUNK = 32768;   // workspace bytes per (chunk, value head)
-constexpr int WS_W = 0, WS_TP = 16384, WS_AQK = 24576;
+constexpr int WS_CHUNK = 33280;   // workspace bytes per (chunk, value head)
+// -w image, T' image, Aqk image, then the chunk's gates as the preparation
+// read or computed them: g[64], beta[64] fp32 (zero past the sequence end),
+// so the chain reads one contiguous row and never evaluates a gate
+constexpr int WS_W = 0, WS_TP = 16384, WS_AQK = 24576, WS_GB = 32768;
 
 __device__ __forceinline__ uint64_t kdesc(uint32_t tile, uint32_t half_stride, int kstep) {
   return tc::smem_desc(tile + (uint32_t)((kstep >> 2) * half_stride + (kstep & 3) * 32), 16, 1024);
@@ -269,6 +272,8 @@ __global__ void __launch_bounds__(P_NT, 4) chunk_prep_kernel(
     if (tid < 64) {
       graw[tid] = g_next;
       bet[tid] = b_next;
+      reinterpret_cast<float*>(wsb + WS_GB)[tid] = g_next;
+      reinterpret_cast<float*>(wsb + WS_GB)[64 + tid] = b_next;
       g_next = b_next = 0.f;
       if (tid < L && hv + 1 < (hk + 1) * grp) {
         gate_load(gs, t0 + tid, H, hv + 1, g_next, b_next);
@@ -449,6 +454,8 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
     if (t < L) gate_load(gs, t0 + t, H, hv0 + h, gv, bv);
     graw(h)[t] = gv;
     bet(h)[t] = bv;
+    reinterpret_cast<float*>(wsb(h) + WS_GB)[t] = gv;
+    reinterpret_cast<float*>(wsb(h) + WS_GB)[64 + t] = bv;
   }
   cp_async_wait_all();
   tc::fence_proxy_async();
@@ -687,7 +694,7 @@ __device__ __forceinline__ int seq_chunks(const int32_t* cu, int64_t n, int64_t 
 __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-    const GateSrc gs, const float* __restrict__ h0,
+    const float* __restrict__ h0,
     const unsigned char* __restrict__ ws, bf16* __restrict__ o, float* __restrict__ ht,
     const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H, float scale,
     ChainPlan plan) {
@@ -854,8 +861,15 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       // as chunk_cumsum_warp, so it matches the preparation kernel bit for bit)
       float ga = 0.f, gb2 = 0.f, ba = 0.f, bb = 0.f;
       const int i0 = 2 * lane;
-      if (i0 < L) gate_load(gs, t0 + i0, H, h, ga, ba);
-      if (i0 + 1 < L) gate_load(gs, t0 + i0 + 1, H, h, gb2, bb);
+      {
+        // the preparation kernel's copy of the chunk's gates (zero past L)
+        const float2 gg = *reinterpret_cast<const float2*>(wsb + WS_GB + 8 * lane);
+        const float2 bb2 = *reinterpret_cast<const float2*>(wsb + WS_GB + 256 + 8 * lane);
+        ga = gg.x;
+        gb2 = gg.y;
+        ba = bb2.x;
+        bb = bb2.y;
+      }
       const float pair = ga + gb2;
       float incl = pair;
 #pragma unroll
@@ -1670,7 +1684,7 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
   gdn::ChainPlan plan{seg, 1, nullptr};
   if (seg == 0) {
     gdn::chunk_chain_kernel<<<(unsigned)(N * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-        mq, mk, mv, mo, gs, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+        mq, mk, mv, mo, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
         plan);
     return check_launch("chunk_gated_delta_rule(chain)");
   }
@@ -1680,7 +1694,7 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
   plan.scratch = reinterpret_cast<float*>(ws + off);
   const int64_t slots = chain_segment_slots(T, N, varlen, seg);
   gdn::chunk_chain_kernel<<<(unsigned)((N + 2 * slots) * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-      mq, mk, mv, mo, gs, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+      mq, mk, mv, mo, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
         plan);
   if (int rc = check_launch("chunk_gated_delta_rule(chain, first segments)")) return rc;
   {
@@ -1720,7 +1734,7 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
   if (int rc = check_launch("chunk_gated_delta_rule(combine)")) return rc;
   plan.phase = 3;
   gdn::chunk_chain_kernel<<<(unsigned)(slots * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-      mq, mk, mv, mo, gs, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+      mq, mk, mv, mo, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
         plan);
   return check_launch("chunk_gated_delta_rule(chain, remaining segments)");
 }
