@@ -353,12 +353,11 @@ __global__ void __launch_bounds__(256, 3) conv1d_decode_w4_rows_kernel(
 // and the lanes that read a state line are the ones that write its final
 // value, as in the per-thread kernel above.
 // ----------------------------------------------------------------------------
-// A slab of RB_C channels arrives as two boxes of RB_B channels, each at the
-// source columns of its 128-channel block: the columns are the channels
-// (plain input), or the block's place in the GDN layer's interleaved
-// projection mixed_qkvz (QkvzMap), so the conv reads the projection output
-// directly and the de-interleave pass disappears.
-constexpr int RB_T = 64, RB_C = 256, RB_B = 128, RB_NS = 2, RB_STAGE = 35840;  // 2 x (64 + 5) rows x 256 B, rounded
+// A slab of RB_C channels arrives as one box of a plain input, or as two
+// boxes of RB_B channels, each at its 128-channel block's place in the GDN
+// layer's interleaved projection mixed_qkvz (QkvzMap): the conv then reads
+// the projection output directly and the de-interleave pass disappears.
+constexpr int RB_T = 64, RB_C = 256, RB_B = 128, RB_NS = 2, RB_STAGE = 35840;  // (64 + 5) rows x 512 B, rounded
 constexpr int RB_NT = 32 + 256;
 constexpr int RB_CV = 4;  // channels per consumer lane
 constexpr int RB_SMEM = RB_NS * RB_STAGE + 1024;
@@ -422,7 +421,7 @@ __device__ __forceinline__ void rb_tma_load(void* dst, const void* tmap, int x, 
 
 __device__ int g_conv_error = 0;
 
-template <typename T, int W>
+template <typename T, int W, bool MAP>
 __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
     const __grid_constant__ CUtensorMap xmap, const T* __restrict__ x, T* __restrict__ state,
     const T* __restrict__ weight, const T* __restrict__ bias, const int32_t* __restrict__ qsl,
@@ -485,11 +484,17 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
           continue;
         }
         const int64_t ch0 = (int64_t)ti.slab * RB_C;
-        const int nb = ch0 + box_c < dim ? 2 : 1;  // boxes of this slab
-        rb_expect_tx(&full[s], (uint32_t)(nb * (RB_T + H) * box_c * sizeof(T)));
-        for (int bb = 0; bb < nb; ++bb)
-          rb_tma_load(sm + s * RB_STAGE + bb * (RB_T + H) * box_c * (int)sizeof(T), &xmap,
-                      (int)qkvz_col(cm, ch0 + bb * box_c), (int)(ti.t0 - H), &full[s]);
+        if constexpr (MAP) {
+          // two 128-channel boxes, one per head block, at their projection columns
+          const int nb = ch0 + box_c < dim ? 2 : 1;
+          rb_expect_tx(&full[s], (uint32_t)(nb * (RB_T + H) * box_c * sizeof(T)));
+          for (int bb = 0; bb < nb; ++bb)
+            rb_tma_load(sm + s * RB_STAGE + bb * (RB_T + H) * box_c * (int)sizeof(T), &xmap,
+                        (int)qkvz_col(cm, ch0 + bb * box_c), (int)(ti.t0 - H), &full[s]);
+        } else {
+          rb_expect_tx(&full[s], (uint32_t)((RB_T + H) * box_c * sizeof(T)));
+          rb_tma_load(sm + s * RB_STAGE, &xmap, (int)ch0, (int)(ti.t0 - H), &full[s]);
+        }
       }
     }
     return;
@@ -523,9 +528,9 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
                       : make_float2(0.f, 0.f);
         }
       }
-      // channel quad * 4 of the slab: box quad * 4 / box_c, rows box_c apart
-      const int qb = quad * RB_CV / box_c, qin = quad * RB_CV - qb * box_c;
+      // channel quad * 4 of the slab: with the map, in box quad * 4 / 128
       const int rstride = box_c * 2;
+      const int qb = MAP ? quad * RB_CV / RB_B : 0, qin = quad * RB_CV - qb * RB_B;
       const unsigned char* stg = sm + s * RB_STAGE + qb * (RB_T + H) * rstride + qin * 2 +
                                  tg * 16 * rstride;
       float2 hist[H > 0 ? H : 1][2];
@@ -615,7 +620,7 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
           const int64_t pos = len - H + j;
           float v[RB_CV];
           if (pos >= 0) {
-            load_vec<T, RB_CV>(x + (ti.sstart + pos) * x_ld + qkvz_col(cm, c0), v);
+            load_vec<T, RB_CV>(x + (ti.sstart + pos) * x_ld + (MAP ? qkvz_col(cm, c0) : c0), v);
           } else {
 #pragma unroll
             for (int c = 0; c < RB_CV; ++c) v[c] = to_f32<T>(st_line[c * H + H + pos]);
@@ -658,7 +663,8 @@ int launch_varlen_tma(int W, const void* x, void* state, const void* w, const vo
   const int64_t src_cols = cm.nqk ? cm.nqk * cm.group : dim;
   cuuint64_t dims[2] = {(cuuint64_t)src_cols, (cuuint64_t)total};
   cuuint64_t strides[1] = {(cuuint64_t)(x_ld * (int64_t)sizeof(T))};
-  const int box_c = (int)std::min<int64_t>(dim, RB_B);  // box width; dim is a multiple of 8
+  // box width: a slab (plain input) or a 128-channel head block; dim is a multiple of 8
+  const int box_c = (int)std::min<int64_t>(dim, cm.nqk ? RB_B : RB_C);
   cuuint32_t box[2] = {(cuuint32_t)box_c, (cuuint32_t)(RB_T + W - 1)};
   cuuint32_t es[2] = {1, 1};
   const CUresult r = enc(&m, sizeof(T) == 2 ? (std::is_same<T, __half>::value
@@ -683,7 +689,8 @@ int launch_varlen_tma(int W, const void* x, void* state, const void* w, const vo
   switch (W) {
 #define XOPS_CT(WW)                                                                            \
   case WW: {                                                                                   \
-    auto kern = conv1d_varlen_tma_kernel<T, WW>;                                               \
+    auto kern = cm.nqk ? conv1d_varlen_tma_kernel<T, WW, true>                                 \
+                       : conv1d_varlen_tma_kernel<T, WW, false>;                               \
     if (!set_stream_smem(kern, RB_SMEM))                                                        \
       return set_error(XOPS_ERR_CUDA, "causal_conv1d_varlen: shared-memory attribute failed"); \
     kern<<<grid, RB_NT, RB_SMEM, st>>>(m, (const T*)x, (T*)state, (const T*)w, (const T*)b,    \
