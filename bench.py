@@ -405,6 +405,9 @@ def main():
                          "GDN layer prefill from its un-split projections, fused against the "
                          "split -> conv -> gating -> rule -> norm sequence")
     ap.add_argument("--tokens", type=int, default=65536)
+    ap.add_argument("--shard", type=int, default=0,
+                    help="cfg5 only, for profiling on one GPU: run rank 0's head shard of an "
+                         "N-GPU job in this single process (N in 2, 4, 8)")
     ap.add_argument("--cpu-sample", type=int, default=8192)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -416,6 +419,11 @@ def main():
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    shard_world = world
+    if a.shard:
+        if world != 1 or a.workload != "cfg5" or a.shard not in (2, 4, 8):
+            raise SystemExit("--shard N: one process, cfg5, N in 2, 4, 8")
+        shard_world = a.shard
     local = int(os.environ.get("LOCAL_RANK", "0"))
     kind = a.workload
     T = a.tokens if kind == "cfg5" else 16384
@@ -423,7 +431,9 @@ def main():
                            "L2-normalised in the conv kernel) -> chunked GDN (Hk16->Hv32, "
                            "dk=dv=128, initial state ~N(0,0.02), final state returned) -> gated "
                            "RMSNorm(g128)",
-               "tokens": T, "heads_per_gpu": 32 // max(1, world), "parallelism": f"head-shard x{world}",
+               "tokens": T, "heads_per_gpu": 32 // max(1, world, a.shard),
+               "parallelism": f"head-shard x{world}" if not a.shard else
+                              f"rank 0 of a head-shard x{a.shard} job, run alone",
                "value_is": "whole-job tokens/s (all ranks; the sequence's 32 heads are split over "
                            "them); value_per_gpu = value / n_gpus",
                "l2_flush": "inputs > L2 (>1 GB per step)"}
@@ -431,6 +441,9 @@ def main():
               {"workload": "cfg3: 8 seqs / 16384 tokens varlen chunked GDN (Hk16->Hv32)",
                "tokens": T, "parallelism": "replica", "l2_flush": "inputs > L2 (~0.45 GB per step)"})
 
+    if a.shard:
+        config["value_is"] = (f"tokens/s of rank 0's shard run alone on one GPU (profiling mode); "
+                              f"the {a.shard}-GPU job runs {a.shard} such shards at once")
     if a.impl == "reference":
         if rank != 0:
             return
@@ -469,7 +482,7 @@ def main():
         # barrier and the max over ranks of the CUDA-event times are host work
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
 
-    cfg = build_cfg5(rank, world, T, dev) if kind == "cfg5" else build_cfg3(dev)
+    cfg = build_cfg5(rank, shard_world, T, dev) if kind == "cfg5" else build_cfg3(dev)
     step, stages = make_step(cfg, kind, dev)
     inp = cfg["dev"]
 
