@@ -187,11 +187,13 @@ def test_chunk_strided_l2_streaming():
     assert_state(h1, rh)
 
 
-def test_chunk_subops_pipeline():
+@pytest.mark.parametrize("lens,hk,hv", [([130, 1, 64, 250], 2, 4), ([300, 64], 1, 4),
+                                         ([700], 4, 4), ([129, 63], 2, 16)])
+def test_chunk_subops_pipeline(lens, hk, hv):
     """cumsum -> kkt -> solve_tril -> w/u -> fwd_h -> fwd_o on the GPU, each
     stage against the oracle's same stage, and the composition against the
     fused op."""
-    inp = workloads.chunk_config3(hk=2, hv=4, lengths=[130, 1, 64, 250], seed=8)
+    inp = workloads.chunk_config3(hk=hk, hv=hv, lengths=lens, seed=8)
     q, k, v, g, beta, h0, cu = (inp[n] for n in ("q", "k", "v", "g", "beta", "initial_state",
                                                  "cu_seqlens"))
     gc = ops.npu_chunk_local_cumsum(_to(g), 64, _to(cu))

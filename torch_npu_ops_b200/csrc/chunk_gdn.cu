@@ -45,6 +45,7 @@
 
 #include "gate_math.cuh"
 #include "gdn_common.cuh"
+#include "gdn_tc.cuh"
 #include "tcgen05.cuh"
 
 namespace xops {
@@ -61,27 +62,6 @@ constexpr int WS_CHUNK = 33280;   // workspace bytes per (chunk, value head)
 // so the chain reads one contiguous row and never evaluates a gate
 constexpr int WS_W = 0, WS_TP = 16384, WS_AQK = 24576, WS_GB = 32768;
 
-__device__ __forceinline__ uint64_t kdesc(uint32_t tile, uint32_t half_stride, int kstep) {
-  return tc::smem_desc(tile + (uint32_t)((kstep >> 2) * half_stride + (kstep & 3) * 32), 16, 1024);
-}
-__device__ __forceinline__ uint64_t kdesc64(uint32_t tile, int kstep) {
-  return tc::smem_desc(tile + (uint32_t)(kstep * 32), 16, 1024);
-}
-// MN-major: tile rows = K index (16 per k-step), LBO = distance between MN halves
-__device__ __forceinline__ uint64_t mndesc(uint32_t tile, uint32_t half_stride, int kstep) {
-  return tc::smem_desc(tile + (uint32_t)(kstep * 2048), half_stride, 1024);
-}
-// 16-byte chunk c of row r of an SW128 tile (c < 8: first half)
-__device__ __forceinline__ uint32_t chunk_off(int r, int c, uint32_t half_stride) {
-  return (uint32_t)((c >> 3) * half_stride + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-__device__ __forceinline__ uint32_t elem_off(int r, int col, uint32_t half_stride) {
-  return (uint32_t)((col >> 6) * half_stride + r * 128 + ((((col & 63) >> 3) ^ (r & 7)) << 4) +
-                    (col & 7) * 2);
-}
-__device__ __forceinline__ uint32_t tm_addr(uint32_t base, int quarter, uint32_t col) {
-  return base + ((uint32_t)(quarter * 32) << 16) + col;
-}
 __device__ __forceinline__ void record_error() { atomicExch(&g_tc_error, 1); }
 
 // Gates of the rule per (token, value head): precomputed g / beta [T, H]
@@ -125,18 +105,6 @@ __device__ __forceinline__ void gate_load(const GateSrc& s, int64_t t, int64_t H
                               : gate_beta<float>(bv);
 }
 
-// [64 x 128] bf16 rows (global row stride in elements) -> SW128 tile
-__device__ __forceinline__ void cp_tile128(unsigned char* dst, uint32_t half_stride,
-                                           const bf16* src, int64_t stride, int L, int t,
-                                           int nthr) {
-  for (int e = t; e < 64 * 16; e += nthr) {
-    const int r = e >> 4, c = e & 15;
-    const bool ok = r < L;
-    cp_async16(dst + chunk_off(r, c, half_stride), src + (int64_t)(ok ? r : 0) * stride + c * 8,
-               ok ? 16 : 0);
-  }
-}
-
 // ============================================================================
 // q/k L2 normalisation pre-pass: x / sqrt(sum x^2 + 1e-6) per 128-wide head,
 // rounded to bf16 (npu_l2norm_last_dim, npu_triton_chunk_gated_delta_rule.cpp:608-609).
@@ -159,16 +127,6 @@ __global__ void __launch_bounds__(256) l2norm_heads_kernel(const bf16* __restric
   *reinterpret_cast<uint2*>(y + r * 128 + lane * 4) = out;
 }
 
-// Four 8 x 8 bf16 blocks from the mma fragment layout (thread t holds row
-// t / 4, elements 2 (t % 4) + {0, 1} of each) to shared memory transposed:
-// block b's row i (its column i) goes to the address lane 8 b + i gives.
-__device__ __forceinline__ void stmatrix_x4_trans(void* row, uint32_t b0, uint32_t b1, uint32_t b2,
-                                                  uint32_t b3) {
-  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};\n" ::"r"(
-                   tc::smem_addr(row)),
-               "r"(b0), "r"(b1), "r"(b2), "r"(b3)
-               : "memory");
-}
 
 // ============================================================================
 // Kernel 1: per-chunk preparation
@@ -1796,9 +1754,9 @@ extern "C" int xops_device_error_count(void) {
   const int zero = 0;
   cudaMemcpyToSymbol(gdn::g_tc_error, &zero, sizeof(int));
   const int vn = xops::take_norm_error(), vc = xops::take_conv_error();
-  const int vr = xops::take_rope_error();
-  if (vn < 0 || vc < 0 || vr < 0) return -1;
-  return v + vn + vc + vr;
+  const int vr = xops::take_rope_error(), vs = xops::take_subop_error();
+  if (vn < 0 || vc < 0 || vr < 0 || vs < 0) return -1;
+  return v + vn + vc + vr + vs;
 }
 
 // ---------------------------------------------------------------------------

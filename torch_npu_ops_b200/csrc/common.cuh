@@ -18,6 +18,7 @@ int check_launch(const char* what);
 int take_norm_error();
 int take_conv_error();
 int take_rope_error();
+int take_subop_error();
 // L2-normalise `rows` rows of `heads` bf16 128-element segments (row stride
 // x_stride elements) into contiguous y with the bulk-copy streaming kernel;
 // -1 when the shape does not suit it (the caller then uses its own kernel)

@@ -1,6 +1,6 @@
-// Building blocks shared by the chunked gated-delta-rule kernels: bf16
-// warp-tile MMA fragments, cp.async tile loads, the 64x64 unit-lower-
-// triangular inverse and per-chunk sequence bookkeeping.
+// Building blocks shared by the chunked gated-delta-rule kernels: cp.async
+// copies, the 64x64 unit-lower-triangular inverse and per-chunk sequence
+// bookkeeping (the tensor-core tile helpers are in gdn_tc.cuh).
 #pragma once
 
 #include "common.cuh"
@@ -9,8 +9,6 @@ namespace xops {
 namespace gdn {
 
 constexpr int BT = 64;     // chunk length (tokens)
-constexpr int LD128 = 136;  // bf16 row stride of 128-wide smem tiles (+16 B pad)
-constexpr int LD64 = 72;    // bf16 row stride of 64-wide smem tiles
 constexpr int LDF = 65;     // fp32 row stride of 64x64 tiles
 
 using bf16 = __nv_bfloat16;
@@ -18,109 +16,6 @@ using bf16 = __nv_bfloat16;
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-
-// D(16x8, fp32) += A(16x16, bf16 row) * B(16x8, bf16 col)
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// A fragment (rows m0..m0+15, k0..k0+15) of a row-major [m][k] tile.
-__device__ __forceinline__ void frag_a(uint32_t (&a)[4], const bf16* base, int ld, int m0, int k0,
-                                       int lane) {
-  ldsm_x4(a, base + (m0 + (lane & 15)) * ld + k0 + ((lane >> 4) << 3));
-}
-// A fragment of A = S^T where S is stored row-major [k][m].
-__device__ __forceinline__ void frag_a_t(uint32_t (&a)[4], const bf16* base, int ld, int m0,
-                                         int k0, int lane) {
-  ldsm_x4_t(a, base + (k0 + (lane & 7) + ((lane >> 4) << 3)) * ld + m0 + (((lane >> 3) & 1) << 3));
-}
-// B fragments of two n-tiles (n0..n0+15, k0..k0+15) from storage [n][k].
-__device__ __forceinline__ void frag_b_nk(uint32_t (&b)[4], const bf16* base, int ld, int n0,
-                                          int k0, int lane) {
-  ldsm_x4(b, base + (n0 + (lane & 7) + ((lane >> 4) << 3)) * ld + k0 + (((lane >> 3) & 1) << 3));
-}
-// B fragments of two n-tiles from storage [k][n].
-__device__ __forceinline__ void frag_b_kn(uint32_t (&b)[4], const bf16* base, int ld, int n0,
-                                          int k0, int lane) {
-  ldsm_x4_t(b, base + (k0 + (lane & 7) + (((lane >> 3) & 1) << 3)) * ld + n0 + ((lane >> 4) << 3));
-}
-
-// acc[NT][4] += A(16 x KD, rows m0) * B(KD x 8*NT, cols n0) ; A [m][k], B [k][n]
-template <int NT, int KD>
-__device__ __forceinline__ void warp_gemm_a_bkn(float (&acc)[NT][4], const bf16* A, int lda, int m0,
-                                                const bf16* B, int ldb, int n0, int lane) {
-#pragma unroll
-  for (int k0 = 0; k0 < KD; k0 += 16) {
-    uint32_t a[4];
-    frag_a(a, A, lda, m0, k0, lane);
-#pragma unroll
-    for (int j = 0; j < NT; j += 2) {
-      uint32_t b[4];
-      frag_b_kn(b, B, ldb, n0 + 8 * j, k0, lane);
-      mma16816(acc[j], a, b[0], b[1]);
-      mma16816(acc[j + 1], a, b[2], b[3]);
-    }
-  }
-}
-
-// acc[NT][4] += A(16 x KD) * B with B stored [n][k]
-template <int NT, int KD>
-__device__ __forceinline__ void warp_gemm_a_bnk(float (&acc)[NT][4], const bf16* A, int lda, int m0,
-                                                const bf16* B, int ldb, int n0, int lane) {
-#pragma unroll
-  for (int k0 = 0; k0 < KD; k0 += 16) {
-    uint32_t a[4];
-    frag_a(a, A, lda, m0, k0, lane);
-#pragma unroll
-    for (int j = 0; j < NT; j += 2) {
-      uint32_t b[4];
-      frag_b_nk(b, B, ldb, n0 + 8 * j, k0, lane);
-      mma16816(acc[j], a, b[0], b[1]);
-      mma16816(acc[j + 1], a, b[2], b[3]);
-    }
-  }
-}
-
-// acc[NT][4] += S^T(16 x KD) * B, S stored [k][m], B stored [k][n]
-template <int NT, int KD>
-__device__ __forceinline__ void warp_gemm_at_bkn(float (&acc)[NT][4], const bf16* S, int lds,
-                                                 int m0, const bf16* B, int ldb, int n0, int lane) {
-#pragma unroll
-  for (int k0 = 0; k0 < KD; k0 += 16) {
-    uint32_t a[4];
-    frag_a_t(a, S, lds, m0, k0, lane);
-#pragma unroll
-    for (int j = 0; j < NT; j += 2) {
-      uint32_t b[4];
-      frag_b_kn(b, B, ldb, n0 + 8 * j, k0, lane);
-      mma16816(acc[j], a, b[0], b[1]);
-      mma16816(acc[j + 1], a, b[2], b[3]);
-    }
-  }
-}
-
-template <int NT>
-__device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
-#pragma unroll
-  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -137,17 +32,6 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
-}
-
-// Loads a [64 x 128] bf16 tile (rows t0..t0+63 with global row stride
-// `stride` elements; rows >= L are zero) into smem with row stride LD128.
-__device__ __forceinline__ void load_tile_64x128(bf16* dst, const bf16* src, int64_t stride, int L,
-                                                 int tid, int nthreads) {
-  for (int e = tid; e < 64 * 16; e += nthreads) {
-    const int r = e >> 4, c = (e & 15) << 3;
-    const bool ok = r < L;
-    cp_async16(dst + r * LD128 + c, src + (int64_t)(ok ? r : 0) * stride + c, ok ? 16 : 0);
-  }
 }
 
 // T = (I + A)^-1 for a strictly lower 64x64 A (fp32, stride LDF), by blocks:
