@@ -8,7 +8,11 @@
 //      G    = [k; q] k^T                          (one MMA, shared by the
 //                                                  value heads of the key head)
 //      A    = strict_tril(beta_i D_ij (k k^T)_ij),  D_ij = e^{gc_i - gc_j}
-//      T    = (I + A)^-1                          (blocked, fp32, CUDA cores)
+//      T    = (I + A)^-1                          (for two value heads per key
+//                                                  head: 16 x 16 diagonal blocks
+//                                                  in registers, the rest as
+//                                                  tf32 tcgen05 products; else
+//                                                  blocked fp32 on CUDA cores)
 //      T'   = T diag(beta)                        -> workspace (bf16)
 //      -w   = -T diag(beta e^{gc}) k              (MMA)   -> workspace (bf16)
 //      Aqk  = tril(q k^T * D)                     -> workspace (bf16)
@@ -340,37 +344,122 @@ __global__ void __launch_bounds__(P_NT, 4) chunk_prep_kernel(
   if (warp == 0) tc::tmem_dealloc(tm, P_TM_COLS);
 }
 
-// ----------------------------------------------------------------------------
-// Kernel 1b: the same preparation for a key head with exactly two value heads
-// (H == 2 Hg), both heads at once.  The Gram epilogue reads each TMEM row
-// once and builds both heads' A and Aqk; threads [0, 128) then invert head
-// 0's A while threads [128, 256) invert head 1's, so every barrier phase
-// carries twice the work.  Head 0's W accumulator reuses the Gram columns
-// (dead by then), which keeps the CTA at 128 TMEM columns and ~68 KB of
-// shared memory: three CTAs per SM.
-// ----------------------------------------------------------------------------
-constexpr int P2_OFF_HS0 = P_OFF_Q;               // head 0: inverse scratch, then T''
-constexpr int P2_OFF_HS1 = P_OFF_Q + P_KQ_HALF;   // head 1: inverse scratch, then T''
-constexpr int P2_FA_BYTES = 64 * LDF * 4;
-constexpr int P2_OFF_FA = 32768;                  // fp32 A_h, then T_h, h = 0, 1
-constexpr int P2_OFF_G = P2_OFF_FA + 2 * P2_FA_BYTES;  // per head: graw, gc, beta, e^gc
-constexpr int P2_SMEM = P2_OFF_G + 2 * 4 * 64 * 4 + 1024;
-constexpr uint32_t P2_TM_G = 0, P2_TM_W0 = 0, P2_TM_W1 = 64, P2_TM_COLS = 128;
+// TMEM columns of the two heads' -w accumulators in the paired preparation
+constexpr uint32_t P2_TM_W0 = 0, P2_TM_W1 = 64;
 
-__global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ k, const GateSrc gs,
-    unsigned char* __restrict__ ws,
+// ----------------------------------------------------------------------------
+// Kernel 1c: the pair preparation with the triangular inverse on the tensor
+// cores.  Let D = I + (the four 16 x 16 diagonal blocks of A) and L = the
+// rest of A (strictly block-lower).  Then I + A = D (I + N) with
+// N = D^-1 L, nilpotent of index 4, so
+//     T = (I + A)^-1 = (I - N + N^2 - N^3) D^-1 = X_3,
+//     X_0 = D^-1,  X_{r+1} = D^-1 + (-N) X_r.
+// D^-1 is solved in registers by the two warps that hold those rows in the
+// Gram epilogue (row-wise forward substitution, rows broadcast by shuffle).
+// N and the three X products are tcgen05 kind::tf32 products with both
+// heads stacked (M = 128 rows (head, row), N = 128 columns (head, column));
+// each thread reads only its own head's quadrant.  Only 48 of the 64
+// contraction indices carry anything: L's first block row and N's last
+// block column are zero, so N = D^-1 L runs over rows 16..63 of L and the
+// X products over columns 0..47 of N.  Operands are rounded to tf32
+// (nearest) as they are written, so the inverse's error stays well below
+// the bf16 rounding of T' and T'' that follows.  The 32 x 32 blocks above
+// the diagonal are zero in A, L, D^-1, N and every X: the warps that own
+// them only write zeros where a later reader needs them.
+//
+// Operand tiles (fp32, K-major, 128 rows): contraction indices 0-31 in an
+// SW128 part (128-byte rows, 16-byte chunk c of row r at c ^ (r & 7)),
+// 32-47 in an SW64 part (64-byte rows, chunk c at c ^ ((r >> 1) & 3)) that
+// lives in a q tile left dead by the Gram product.  That keeps the CTA at
+// ~69 KB, three per SM.  The A tile's rows are (head, row) and are written a
+// row at a time; the B tile's rows are (head, column) with K = the row of
+// the matrix, so a thread holding a matrix row writes one element into
+// each of 32 B rows (one 128-byte warp store per column).  Aqk goes
+// straight to the workspace; the T' and -w images are staged in shared
+// memory and leave by bulk copy.
+// ----------------------------------------------------------------------------
+constexpr int P3_OFF_AM = 32768;     // A tile, K 0..31: D^-1 (shifted), then -N; later T''
+constexpr int P3_OFF_BM = 49152;     // B tile, K 0..31: L (shifted), then X_r; later T'
+constexpr int P3_OFF_AT = P_OFF_Q;              // A tile, K 32..47 (in the dead q half 0)
+constexpr int P3_OFF_BT = P_OFF_Q + P_KQ_HALF;  // B tile, K 32..47 (in the dead q half 1)
+constexpr int P3_OFF_G = 65536;      // per head: graw, gc, beta, e^gc (64 floats each)
+constexpr int P3_OFF_D0 = 67584;     // per head: D^-1 of the first diagonal block [16][16]
+constexpr int P3_SMEM = P3_OFF_D0 + 2048 + 1024;
+constexpr uint32_t P3_TM_COLS = 128;
+
+__device__ __forceinline__ float4 tf32x4(const float* v) {
+  return make_float4(tc::to_tf32(v[0]), tc::to_tf32(v[1]), tc::to_tf32(v[2]), tc::to_tf32(v[3]));
+}
+// byte offset of the 16-byte chunk holding contraction indices 4 k4 .. 4 k4 + 3
+// of operand row r (k4 < 12), from the tile's SW128 part (main) or SW64 part (tail)
+__device__ __forceinline__ uint32_t op_chunk(uint32_t main, uint32_t tail, int r, int k4) {
+  return k4 < 8 ? main + (uint32_t)(r * 128 + ((k4 ^ (r & 7)) << 4))
+                : tail + (uint32_t)(r * 64 + (((k4 - 8) ^ ((r >> 1) & 3)) << 4));
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ float4 ld_shared_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+// Column-wise stores into a B tile: element (row nbase + c, K = k), c < 32,
+// nbase a multiple of 32, k < 48.  Rows 8 apart repeat the swizzle, so the
+// address is base[c & 7] + c * stride (stride = the part's row bytes).
+struct BColumn {
+  uint32_t base[8];
+  uint32_t stride;
+  __device__ __forceinline__ BColumn(uint32_t main, uint32_t tail, int nbase, int k) {
+    if (k < 32) {
+      stride = 128;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        base[u] = main + (uint32_t)(nbase * 128 + ((((k >> 2) & 7) ^ u) << 4) + (k & 3) * 4);
+    } else {
+      stride = 64;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        base[u] = tail + (uint32_t)(nbase * 64 + (((((k - 32) >> 2) & 3) ^ ((u >> 1) & 3)) << 4) +
+                                    (k & 3) * 4);
+    }
+  }
+  __device__ __forceinline__ void st(int c, float v) const {
+    asm volatile("st.shared.f32 [%0], %1;\n" ::"r"(base[c & 7] + stride * (uint32_t)c), "f"(v)
+                 : "memory");
+  }
+  // the same when the caller knows the part (S = 128: K < 32, S = 64: K >= 32)
+  template <int S>
+  __device__ __forceinline__ void st_s(int c, float v) const {
+    asm volatile("st.shared.f32 [%0], %1;\n" ::"r"(base[c & 7] + (uint32_t)(S * c)), "f"(v)
+                 : "memory");
+  }
+};
+__device__ __forceinline__ uint64_t op_desc(uint32_t main, uint32_t tail, int kstep) {
+  return kstep < 4 ? tc::smem_desc(main + (uint32_t)(kstep * 32), 16, 1024)
+                   : tc::smem_desc_sw64(tail + (uint32_t)((kstep - 4) * 32));
+}
+
+__global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const GateSrc gs, unsigned char* __restrict__ ws,
     const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H,
-    int64_t q_stride, int64_t k_stride) {
+    int resident) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  __shared__ uint64_t bar;
+  __shared__ uint64_t bar, ldbar;
   __shared__ uint32_t tmem_sh;
   __shared__ int64_t pos[4];
   __shared__ int ok_sh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int quarter = warp & 3, colhalf = warp >> 2;
+  const int c0 = colhalf * 32;  // this thread's 32 columns of a head's 64
   const int hk = blockIdx.y;
   if (tid == 0) {
     int64_t seq = 0, t0 = 0, eos = 0, cis = 0;
@@ -385,27 +474,43 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
   const int64_t gci = pos[0], t0 = pos[1];
   const int L = (int)((pos[2] - t0) < BT ? (pos[2] - t0) : BT);
   const int hv0 = 2 * hk;
-  // per head h: graw, gc, beta, e^gc (64 floats each)
-  float* gsm = reinterpret_cast<float*>(sm + P2_OFF_G);
+  float* gsm = reinterpret_cast<float*>(sm + P3_OFF_G);
   auto graw = [&](int h) { return gsm + h * 256; };
   auto gcs = [&](int h) { return gsm + h * 256 + 64; };
   auto bet = [&](int h) { return gsm + h * 256 + 128; };
   auto egc = [&](int h) { return gsm + h * 256 + 192; };
-  auto fa = [&](int h) { return reinterpret_cast<float*>(sm + P2_OFF_FA + h * P2_FA_BYTES); };
   auto wsb = [&](int h) { return ws + (gci * H + hv0 + h) * (int64_t)WS_CHUNK; };
   const uint32_t sb = tc::smem_addr(sm);
+  const uint32_t am = sb + P3_OFF_AM, at = sb + P3_OFF_AT, bm = sb + P3_OFF_BM, bt = sb + P3_OFF_BT;
+  float* d0s = reinterpret_cast<float*>(sm + P3_OFF_D0);
 
   if (warp == 0) {
-    tc::tmem_alloc(&tmem_sh, P2_TM_COLS);
+    tc::tmem_alloc(&tmem_sh, P3_TM_COLS);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
     tc::mbar_init(&bar, 1);
+    tc::mbar_init(&ldbar, 1);
     tc::mbar_fence_init();
+    // k and q of the chunk as four 64 x 64 boxes: [K0 | Q0 | K1 | Q1]
+    tc::mbar_arrive_expect_tx(&ldbar, 32768);
+    for (int hf = 0; hf < 2; ++hf) {
+      tc::tma_load_2d(sm + P_OFF_KQ + hf * P_KQ_HALF, &tm_k, hk * 128 + hf * 64, (int)t0, &ldbar);
+      tc::tma_load_2d(sm + P_OFF_Q + hf * P_KQ_HALF, &tm_q, hk * 128 + hf * 64, (int)t0, &ldbar);
+    }
+    // Into L2 ahead of time: the tiles of the CTA that will most likely take
+    // this one's place (`resident` CTAs run at once, launched in linear
+    // order).  Chunk slot x starts near token 64 x; a miss only costs the
+    // prefetch, coordinates past the tensor are dropped.
+    const int64_t nxt = (int64_t)blockIdx.y * gridDim.x + blockIdx.x + resident;
+    if (nxt < (int64_t)gridDim.x * gridDim.y) {
+      const int px = (int)(nxt % gridDim.x), py = (int)(nxt / gridDim.x);
+      for (int hf = 0; hf < 2; ++hf) {
+        tc::tma_prefetch_2d(&tm_k, py * 128 + hf * 64, px * BT);
+        tc::tma_prefetch_2d(&tm_q, py * 128 + hf * 64, px * BT);
+      }
+    }
   }
-  cp_tile128(sm + P_OFF_KQ, P_KQ_HALF, k + t0 * k_stride + (int64_t)hk * 128, k_stride, L, tid, P_NT);
-  cp_tile128(sm + P_OFF_Q, P_KQ_HALF, q + t0 * q_stride + (int64_t)hk * 128, q_stride, L, tid, P_NT);
-  cp_async_commit();
   if (tid < 128) {  // both heads' gates
     const int h = tid >> 6, t = tid & 63;
     float gv = 0.f, bv = 0.f;
@@ -415,20 +520,34 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
     reinterpret_cast<float*>(wsb(h) + WS_GB)[t] = gv;
     reinterpret_cast<float*>(wsb(h) + WS_GB)[64 + t] = bv;
   }
-  cp_async_wait_all();
+  __syncthreads();  // barrier inits visible before anyone waits
+  if (tid == 0 && !tc::mbar_wait(&ldbar, 0, WAIT_LIMIT)) {
+    record_error();
+    ok_sh = 0;
+  }
+  __syncthreads();
+  bool alive = ok_sh != 0;
+  if (alive && L < BT) {
+    // rows past the sequence end came from the next sequence (or the
+    // tensor's zero fill): clear them so the Gram product sees only the chunk
+    for (int e = tid; e < (BT - L) * 32; e += P_NT) {
+      const int r = L + (e >> 5), part = e & 31;  // part: K0, Q0, K1, Q1 x 8 chunks
+      *reinterpret_cast<uint4*>(sm + (part >> 3) * 8192 + r * 128 + (part & 7) * 16) =
+          make_uint4(0, 0, 0, 0);
+    }
+  }
   tc::fence_proxy_async();
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
   const uint32_t tm = tmem_sh;
   uint32_t phase = 0;
-  bool alive = true;
-  if (tid == 0) {
+  if (tid == 0 && alive) {
     const uint32_t id = tc::idesc_bf16(128, 64, false, false);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      tc::mma_bf16(tm + P2_TM_G, kdesc(sb + P_OFF_KQ, P_KQ_HALF, j), kdesc(sb + P_OFF_KQ, P_KQ_HALF, j),
-                   id, j > 0);
+      tc::mma_bf16(tm, kdesc(sb + P_OFF_KQ, P_KQ_HALF, j), kdesc(sb + P_OFF_KQ, P_KQ_HALF, j), id,
+                   j > 0);
     tc::commit(&bar);
   }
   if (warp == 0 || warp == 4) {  // cumsum of each head while the Gram product runs
@@ -438,134 +557,314 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
     egc(h)[lane] = __expf(gcs(h)[lane]);
     egc(h)[lane + 32] = __expf(gcs(h)[lane + 32]);
   }
+  // One thread polls the MMA barrier; the others wait at the block barrier,
+  // which takes no issue slots.
   auto wait_mma = [&]() {
-    const bool ok = tc::mbar_wait(&bar, phase, WAIT_LIMIT);
-    phase ^= 1u;
-    if (!ok) {
+    if (tid == 0 && !tc::mbar_wait(&bar, phase, WAIT_LIMIT)) {
       record_error();
-      atomicExch(&ok_sh, 0);
+      ok_sh = 0;
     }
-    tc::fence_after();
+    phase ^= 1u;
     __syncthreads();
+    tc::fence_after();
     alive = ok_sh != 0;
   };
-  wait_mma();
-  if (alive) {  // Gram epilogue: one TMEM row read serves both heads
+  // The 32 x 32 block of (rows of this quarter, columns 32 half ..): entirely
+  // above the diagonal (zero everywhere), straddling it, or entirely below.
+  const bool blk_zero = colhalf > (quarter & 1), blk_diag = colhalf == (quarter & 1);
+  if (alive) wait_mma();
+  if (alive) {  // Gram epilogue: k rows give L and D^-1, q rows give Aqk; warp (quarter,
+                // colhalf) takes head colhalf's 64 columns of its 32 rows
     const int row = quarter * 32 + lane;
-    const int c0 = colhalf * 32;
-    float vals[32];
-    tc::tmem_ld32(tm_addr(tm, quarter, P2_TM_G + c0), vals);
-    tc::tmem_wait_ld();
-    // this thread's 32 columns of each head's cumulative gates, as vectors
-    auto load_gc = [&](int h, float (&gc)[32]) {
+    // v[c] * s * e^{min(gi - gc_j, 0)}, j = cb + c, c < 16 (TMEM columns cb ..)
+    auto decayed16 = [&](int h, int cb, float gi, float s, float (&a)[16]) {
+      float v[16];
+      tc::tmem_ld16(tm_addr(tm, quarter, cb), v);
+      tc::tmem_wait_ld();
+      const float2 s2 = make_float2(s, s), gi2 = make_float2(gi, gi);
 #pragma unroll
-      for (int v = 0; v < 8; ++v) {
-        const float4 t = *reinterpret_cast<const float4*>(gcs(h) + c0 + 4 * v);
-        gc[4 * v] = t.x; gc[4 * v + 1] = t.y; gc[4 * v + 2] = t.z; gc[4 * v + 3] = t.w;
+      for (int c = 0; c < 16; c += 4) {
+        const float4 g4 = *reinterpret_cast<const float4*>(gcs(h) + cb + c);
+        const float2 d0 = fsub2(gi2, make_float2(g4.x, g4.y)), d1 = fsub2(gi2, make_float2(g4.z, g4.w));
+        const float2 e0 = make_float2(__expf(fminf(d0.x, 0.f)), __expf(fminf(d0.y, 0.f)));
+        const float2 e1 = make_float2(__expf(fminf(d1.x, 0.f)), __expf(fminf(d1.y, 0.f)));
+        const float2 p0 = fmul2(fmul2(make_float2(v[c], v[c + 1]), s2), e0);
+        const float2 p1 = fmul2(fmul2(make_float2(v[c + 2], v[c + 3]), s2), e1);
+        a[c] = p0.x; a[c + 1] = p0.y; a[c + 2] = p1.x; a[c + 3] = p1.y;
       }
     };
     if (row < 64) {
+      // k row i; in a diagonal block i = c0 + lane, so column c is strictly
+      // below the diagonal when c < lane.  L enters N = D^-1 L through its
+      // rows 16..63: row i is contraction index i - 16 of both tiles.
+      const int i = row, sub = lane >> 4, li = lane & 15;
+      const bool has_k = i >= 16;
+      const int h = colhalf;  // this warp's head; it covers all 64 columns
+      const int r = 64 * h + i;
+      const float bi = bet(h)[i], gi = gcs(h)[i];
 #pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        float* far = fa(h) + row * LDF;
-        const float bi = bet(h)[row], gi = gcs(h)[row];
-        float gc[32];
-        load_gc(h, gc);
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = 32 * half;
+        const bool blk_zero = half > (quarter & 1), blk_diag = half == (quarter & 1);
+        const BColumn lcol(bm, bt, 64 * h + c0, has_k ? i - 16 : 0);  // L[i][c0 + c]
+        if (blk_zero) {  // L and D^-1 are zero here
+          if (has_k) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int j = c0 + c;
-          far[j] = (j < row) ? vals[c] * bi * __expf(fminf(gi - gc[c], 0.f)) : 0.f;
-        }
-      }
-    } else {
-      const int i = row - 64;
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        const float gi = gcs(h)[i];
-        float gcv[32];
-        load_gc(h, gcv);
-        unsigned char* aqk = wsb(h) + WS_AQK;
-#pragma unroll
-        for (int c = 0; c < 32; c += 8) {
-          float e[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int j = c0 + c + u;
-            e[u] = (j <= i) ? vals[c + u] * __expf(fminf(gi - gcv[c + u], 0.f)) : 0.f;
+            for (int c = 0; c < 32; ++c) lcol.st(c, 0.f);
           }
-          uint4 pk;
-          pk.x = pack_bf16(e[0], e[1]); pk.y = pack_bf16(e[2], e[3]);
-          pk.z = pack_bf16(e[4], e[5]); pk.w = pack_bf16(e[6], e[7]);
-          *reinterpret_cast<uint4*>(aqk + chunk_off(i, (c0 + c) >> 3, 0)) = pk;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) st_shared_v4(op_chunk(am, at, r, 4 + u), make_float4(0.f, 0.f, 0.f, 0.f));
+          continue;
+        }
+        if (!blk_diag) {  // rows 32-63 x columns 0-31: all of it is L, D^-1 is zero
+#pragma unroll
+          for (int cb = 0; cb < 32; cb += 16) {
+            float a[16];
+            decayed16(h, c0 + cb, gi, bi, a);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) lcol.st(cb + c, tc::to_tf32(a[c]));
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) st_shared_v4(op_chunk(am, at, r, u), make_float4(0.f, 0.f, 0.f, 0.f));
+          continue;
+        }
+        // Diagonal block pair: columns 0-15 are lanes 0-15's diagonal block
+        // and lanes 16-31's L; columns 16-31 are lanes 16-31's diagonal block.
+        float dr[16];
+        {
+          float a[16];
+          decayed16(h, c0, gi, bi, a);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            if (c >= lane) a[c] = 0.f;
+            dr[c] = a[c];
+            if (has_k) lcol.st(c, sub ? tc::to_tf32(a[c]) : 0.f);
+          }
+        }
+        {
+          float a[16];
+          decayed16(h, c0 + 16, gi, bi, a);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            if (16 + c >= lane) a[c] = 0.f;
+            if (sub) dr[c] = a[c];
+            if (has_k) lcol.st(16 + c, 0.f);
+          }
+        }
+        // row li of (I + A_blk)^-1 of the row's 16 x 16 diagonal block
+        float y[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) y[m] = (m == li) ? 1.f : 0.f;
+        const int src0 = lane & 16;
+#pragma unroll
+        for (int m = 0; m < 15; ++m) {
+#pragma unroll
+          for (int c = 0; c <= m; ++c) {
+            const float ym = __shfl_sync(0xffffffffu, y[c], src0 + m);
+            y[c] = fmaf(-dr[m], ym, y[c]);
+          }
+        }
+        // D^-1 row i, columns c0..c0+31, as contraction indices (column - 16)
+        // of the A tile; the first block (columns 0-15) goes to its own scratch
+        if (half == 0 && sub == 0) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            *reinterpret_cast<float4*>(d0s + (h * 16 + li) * 16 + 4 * u) = make_float4(y[4 * u], y[4 * u + 1], y[4 * u + 2], y[4 * u + 3]);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (half == 0 && u < 4) continue;  // columns 0-15: the first block, stored above
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if ((u >> 2) == sub) v = tf32x4(y + (u & 3) * 4);
+          st_shared_v4(op_chunk(am, at, r, (c0 >> 2) - 4 + u), v);
         }
       }
-    }
-  }
-  // every thread reaches the same barriers whether or not the MMA timed out
-  tc::fence_before();
-  __syncthreads();
-  tc::fence_after();
-  const int hh = tid >> 7, ht = tid & 127;  // head and index within that head's half
-  {
-    float* ft = fa(hh);
-    float* fm = reinterpret_cast<float*>(sm + (hh ? P2_OFF_HS1 : P2_OFF_HS0));
-    tri_inverse_64_half(ft, fm, ht);
-    const float* bt = bet(hh);
-    const float* eg = egc(hh);
-    unsigned char* tpp = sm + (hh ? P2_OFF_HS1 : P2_OFF_HS0);
-    unsigned char* tpw = wsb(hh) + WS_TP;
-    for (int e = ht; e < 64 * 8; e += 128) {
-      const int i = e >> 3, cc = e & 7;
-      float tp[8], tq[8], bv[8], ev[8];
-      *reinterpret_cast<float4*>(bv) = *reinterpret_cast<const float4*>(bt + cc * 8);
-      *reinterpret_cast<float4*>(bv + 4) = *reinterpret_cast<const float4*>(bt + cc * 8 + 4);
-      *reinterpret_cast<float4*>(ev) = *reinterpret_cast<const float4*>(eg + cc * 8);
-      *reinterpret_cast<float4*>(ev + 4) = *reinterpret_cast<const float4*>(eg + cc * 8 + 4);
+    } else {  // Aqk rows, straight to the workspace image
+      const int i = row - 64;
+      const int h = colhalf;
+      unsigned char* img = wsb(h) + WS_AQK;
+      const float gi = gcs(h)[i];
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = 32 * half;
+        const bool blk_zero = half > (quarter & 1), blk_diag = half == (quarter & 1);
+        if (blk_zero) {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float tv = ft[i * LDF + cc * 8 + u] * bv[u];
-        tp[u] = tv;  // diagonal = bf16(beta_i); the chain adds beta_i - bf16(beta_i)
-        tq[u] = tv * ev[u];
+          for (int c = 0; c < 32; c += 8)
+            *reinterpret_cast<uint4*>(img + chunk_off(i, (c0 + c) >> 3, 0)) = make_uint4(0, 0, 0, 0);
+          continue;
+        }
+#pragma unroll
+        for (int cb = 0; cb < 32; cb += 16) {
+          float e[16];
+          decayed16(h, c0 + cb, gi, 1.f, e);
+          if (blk_diag) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              if (cb + c > lane) e[c] = 0.f;
+          }
+#pragma unroll
+          for (int c = 0; c < 16; c += 8) {
+            uint4 pk;
+            pk.x = pack_bf16(e[c], e[c + 1]); pk.y = pack_bf16(e[c + 2], e[c + 3]);
+            pk.z = pack_bf16(e[c + 4], e[c + 5]); pk.w = pack_bf16(e[c + 6], e[c + 7]);
+            *reinterpret_cast<uint4*>(img + chunk_off(i, (c0 + cb + c) >> 3, 0)) = pk;
+          }
+        }
       }
-      uint4 a, b;
-      a.x = pack_bf16(tp[0], tp[1]); a.y = pack_bf16(tp[2], tp[3]);
-      a.z = pack_bf16(tp[4], tp[5]); a.w = pack_bf16(tp[6], tp[7]);
-      b.x = pack_bf16(tq[0], tq[1]); b.y = pack_bf16(tq[2], tq[3]);
-      b.z = pack_bf16(tq[4], tq[5]); b.w = pack_bf16(tq[6], tq[7]);
-      *reinterpret_cast<uint4*>(tpw + chunk_off(i, cc, 0)) = a;
-      *reinterpret_cast<uint4*>(tpp + (uint32_t)(i * 128 + ((cc ^ (i & 7)) << 4))) = b;
     }
   }
   tc::fence_proxy_async();
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
-  if (tid == 0 && alive) {
-    const uint32_t id = tc::idesc_bf16(128, 64, true, false);
+  // N = D^-1 L (A = D^-1, B = L, over L's rows 16..63), stored negated; then
+  // X_{r+1} = D^-1 + (-N) X_r (A = -N, B = X_r, over N's columns 0..47)
+  const uint32_t id_inv = tc::idesc_tf32(128, 128);
+  auto issue_inv = [&]() {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t tpp = sb + (h ? P2_OFF_HS1 : P2_OFF_HS0);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        tc::mma_bf16(tm + (h ? P2_TM_W1 : P2_TM_W0), mndesc(sb + P_OFF_KQ, P_KQ_HALF, j),
-                     kdesc64(tpp, j), id, j > 0);
-    }
+    for (int j = 0; j < 6; ++j)
+      tc::mma_tf32(tm, op_desc(am, at, j), op_desc(bm, bt, j), id_inv, j > 0);
     tc::commit(&bar);
+  };
+  if (tid == 0 && alive) issue_inv();
+  // Round epilogues: TMEM lane 64 h + m holds row (h, m); this thread's
+  // columns c0..c0+31 of its head are at TMEM column 64 h + c0.
+  const int eh = quarter >> 1, em = (quarter & 1) * 32 + lane, er = 64 * eh + em;
+  const int esub = (em >> 4) & 1;  // in a diagonal block: which 16 of the 32 columns are D^-1's
+  const uint32_t tcol = 64u * eh + c0;
+  const bool has_x = em < 48;      // X row em is contraction index em of the B tile
+  float dinv[16];
+#pragma unroll
+  for (int m = 0; m < 16; ++m) dinv[m] = 0.f;
+#pragma unroll 1
+  for (int rd = 0; rd < 4; ++rd) {
+    if (alive) wait_mma();
+    if (rd == 0) {
+      // this row's D^-1 block, read before -N overwrites the A tile
+      if (alive && blk_diag) {
+        const int blk = em >> 4;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float4 t = blk == 0 ? *reinterpret_cast<const float4*>(d0s + (eh * 16 + em) * 16 + 4 * u)
+                                    : ld_shared_v4(op_chunk(am, at, er, 4 * (blk - 1) + u));
+          dinv[4 * u] = t.x; dinv[4 * u + 1] = t.y; dinv[4 * u + 2] = t.z; dinv[4 * u + 3] = t.w;
+        }
+      }
+      __syncthreads();
+    }
+    if (alive && !blk_zero) {
+      // 16 columns at a time: cb = 0 holds the diagonal block when esub == 0
+#pragma unroll
+      for (int cb = 0; cb < 32; cb += 16) {
+        float acc[16];
+        tc::tmem_ld16(tm_addr(tm, quarter, tcol + cb), acc);
+        tc::tmem_wait_ld();
+        const bool dblk = blk_diag && (cb >> 4) == esub;
+        if (rd == 0) {  // acc = N: -N -> A tile (columns 0..47), X_0 = D^-1 -> B tile
+#pragma unroll
+          for (int c = 0; c < 16; ++c) acc[c] = -acc[c];
+          if (c0 + cb < 48) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              st_shared_v4(op_chunk(am, at, er, ((c0 + cb) >> 2) + u), tf32x4(acc + 4 * u));
+          }
+          if (has_x) {
+            const BColumn xcol(bm, bt, 64 * eh + c0, em);  // X[em][c0 + c]
+            if (em < 32) {
+#pragma unroll
+              for (int c = 0; c < 16; ++c) xcol.st_s<128>(cb + c, dblk ? dinv[c] : 0.f);
+            } else {
+#pragma unroll
+              for (int c = 0; c < 16; ++c) xcol.st_s<64>(cb + c, dblk ? dinv[c] : 0.f);
+            }
+          }
+        } else {  // acc = -N X_{rd-1}: X_rd = D^-1 + acc
+          if (dblk) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) acc[c] += dinv[c];
+          }
+          if (rd < 3) {
+            if (has_x) {
+              const BColumn xcol(bm, bt, 64 * eh + c0, em);
+              if (em < 32) {
+#pragma unroll
+                for (int c = 0; c < 16; ++c) xcol.st_s<128>(cb + c, tc::to_tf32(acc[c]));
+              } else {
+#pragma unroll
+                for (int c = 0; c < 16; ++c) xcol.st_s<64>(cb + c, tc::to_tf32(acc[c]));
+              }
+            }
+          } else {  // acc = T: T' image (staged in the B tile) and T'' (in the A tile)
+            unsigned char* tpi = sm + P3_OFF_BM + eh * 8192;
+            unsigned char* tppi = sm + P3_OFF_AM + eh * 8192;
+#pragma unroll
+            for (int c = 0; c < 16; c += 8) {
+              const int col = c0 + cb + c;
+              uint32_t pa[4], pb[4];
+#pragma unroll
+              for (int u = 0; u < 8; u += 2) {
+                // diagonal = bf16(beta); the chain adds beta - bf16(beta)
+                const float2 bv = *reinterpret_cast<const float2*>(bet(eh) + col + u);
+                const float2 ev = *reinterpret_cast<const float2*>(egc(eh) + col + u);
+                const float2 p = fmul2(make_float2(acc[c + u], acc[c + u + 1]), bv);
+                pa[u >> 1] = pack_bf16(p.x, p.y);
+                const float2 qv = fmul2(p, ev);
+                pb[u >> 1] = pack_bf16(qv.x, qv.y);
+              }
+              const uint4 a = make_uint4(pa[0], pa[1], pa[2], pa[3]);
+              const uint4 b = make_uint4(pb[0], pb[1], pb[2], pb[3]);
+              *reinterpret_cast<uint4*>(tpi + chunk_off(em, col >> 3, 0)) = a;
+              *reinterpret_cast<uint4*>(tppi + chunk_off(em, col >> 3, 0)) = b;
+            }
+          }
+        }
+      }
+    } else if (alive && rd == 3) {  // T is zero above the diagonal blocks
+      unsigned char* tpi = sm + P3_OFF_BM + eh * 8192;
+      unsigned char* tppi = sm + P3_OFF_AM + eh * 8192;
+#pragma unroll
+      for (int c = 0; c < 32; c += 8) {
+        *reinterpret_cast<uint4*>(tpi + chunk_off(em, (c0 + c) >> 3, 0)) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(tppi + chunk_off(em, (c0 + c) >> 3, 0)) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    tc::fence_proxy_async();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (tid == 0 && alive) {
+      if (rd < 3) {
+        issue_inv();
+      } else {
+        for (int h = 0; h < 2; ++h)
+          tc::bulk_store(wsb(h) + WS_TP, sm + P3_OFF_BM + h * 8192, 8192);
+        tc::bulk_commit_group();
+        const uint32_t id = tc::idesc_bf16(128, 64, true, false);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tc::mma_bf16(tm + (h ? P2_TM_W1 : P2_TM_W0), mndesc(sb + P_OFF_KQ, P_KQ_HALF, j),
+                         kdesc64(am + h * 8192, j), id, j > 0);
+        }
+        tc::commit(&bar);
+      }
+    }
   }
   if (alive) wait_mma();
   if (alive) {
-    // -w [t][kk] (bf16, SW128 image) from w^T in TMEM (lane = kk).  The k and
-    // T'' tiles are dead now: head h's image is staged at 16 KB x h.  16-lane
-    // TMEM loads give 8 x 8 blocks in the mma fragment layout; transposing
-    // stmatrix stores put each block's 8 token rows (8 kk each, one 16-byte
-    // chunk) at their swizzled places; one bulk store per head follows.
-    const int h = colhalf;  // warps 0-3: head 0, warps 4-7: head 1
+    // -w [t][kk] (bf16, SW128 image) from w^T in TMEM (lane = kk), staged in
+    // the dead k / q tiles (head h at 16 KB x h): 16-lane TMEM loads give
+    // 8 x 8 blocks in the mma fragment layout, transposing stmatrix stores put
+    // each block's token rows at their swizzled places
+    const int h = colhalf;
     unsigned char* stage = sm + h * 16384;
     const uint32_t wcol = h ? P2_TM_W1 : P2_TM_W0;
     const int mi = lane >> 3;
 #pragma unroll 1
     for (int tb = 0; tb < 64; tb += 16) {
-      uint32_t ra[8], rb[8];  // kk 32 q + 0..15 and 32 q + 16..31, tokens tb..tb + 15
+      uint32_t ra[8], rb[8];
       tc::tmem_ld16x256b_x2(tm_addr(tm, quarter, wcol + tb), ra);
       tc::tmem_ld16x256b_x2(tm_addr(tm, quarter, wcol + tb) + (16u << 16), rb);
       tc::tmem_wait_ld();
@@ -575,24 +874,28 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_kernel(
       const int t = tb + ((mi >> 1) << 3) + (lane & 7);
 #pragma unroll
       for (int lb = 0; lb < 32; lb += 16) {
-        const int kk8 = quarter * 32 + lb + ((mi & 1) << 3);  // first kk of the row's chunk
-        unsigned char* row =
+        const int kk8 = quarter * 32 + lb + ((mi & 1) << 3);
+        unsigned char* rowp =
             stage + (kk8 >> 6) * 8192 + t * 128 + ((((kk8 & 63) >> 3) ^ (t & 7)) << 4);
         const uint32_t(&r)[8] = lb ? rb : ra;
-        stmatrix_x4_trans(row, pk(r[0], r[1]), pk(r[2], r[3]), pk(r[4], r[5]), pk(r[6], r[7]));
+        stmatrix_x4_trans(rowp, pk(r[0], r[1]), pk(r[2], r[3]), pk(r[4], r[5]), pk(r[6], r[7]));
       }
     }
     tc::fence_proxy_async();
   }
   __syncthreads();
-  if (alive && tid == 0) {
-    for (int h = 0; h < 2; ++h) tc::bulk_store(wsb(h) + WS_W, sm + h * 16384, 16384);
-    tc::bulk_commit_group();
-    tc::bulk_wait_all();
+  if (tid == 0) {
+    if (alive) {
+      for (int h = 0; h < 2; ++h) tc::bulk_store(wsb(h) + WS_W, sm + h * 16384, 16384);
+      tc::bulk_commit_group();
+    }
+    // shared memory may be released once the copies have read it; their
+    // writes complete before the kernel does
+    tc::bulk_wait_read<0>();
   }
   tc::fence_before();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tm, P2_TM_COLS);
+  if (warp == 0) tc::tmem_dealloc(tm, P3_TM_COLS);
 }
 
 // ============================================================================
@@ -1607,12 +1910,32 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
     kk = kn;
     qs = ks = Hg * K;
   }
+  CUtensorMap mq, mk, mv;
+  if (int rc = token_rows_map(&mq, qq, Hg * K, B * T, qs, "chunk_gated_delta_rule(q map)"))
+    return rc;
+  if (int rc = token_rows_map(&mk, kk, Hg * K, B * T, ks, "chunk_gated_delta_rule(k map)"))
+    return rc;
   if (H == 2 * Hg) {  // two value heads per key head: both in one CTA
-    if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_prep_pair_kernel, gdn::P2_SMEM,
+    if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_prep_pair_tc_kernel, gdn::P3_SMEM,
                                        "chunk_gated_delta_rule(prep)"))
       return rc;
-    gdn::chunk_prep_pair_kernel<<<dim3((unsigned)nchunks, (unsigned)Hg), gdn::P_NT, gdn::P2_SMEM,
-                                  st>>>(qq, kk, gs, ws, cu_seqlens, N, T, Hg, H, qs, ks);
+    // CTAs of the kernel that run at once (three per SM), per device: each
+    // CTA prefetches the tiles of the one expected to take its place
+    static int resident_by_dev[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int resident = dev < 64 ? resident_by_dev[dev] : 0;
+    if (!resident) {
+      int sms = 0, per_sm = 0;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gdn::chunk_prep_pair_tc_kernel,
+                                                    gdn::P_NT, gdn::P3_SMEM);
+      resident = (sms > 0 ? sms : 1) * (per_sm > 0 ? per_sm : 1);
+      if (dev < 64) resident_by_dev[dev] = resident;
+    }
+    gdn::chunk_prep_pair_tc_kernel<<<dim3((unsigned)nchunks, (unsigned)Hg), gdn::P_NT,
+                                     gdn::P3_SMEM, st>>>(mq, mk, gs, ws, cu_seqlens, N, T, Hg, H,
+                                                         resident);
   } else {
     if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_prep_kernel, gdn::P_SMEM,
                                        "chunk_gated_delta_rule(prep)"))
@@ -1623,11 +1946,6 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
   if (int rc = check_launch("chunk_gated_delta_rule(prep)")) return rc;
   if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_chain_kernel, gdn::C_SMEM,
                                      "chunk_gated_delta_rule(chain)"))
-    return rc;
-  CUtensorMap mq, mk, mv;
-  if (int rc = token_rows_map(&mq, qq, Hg * K, B * T, qs, "chunk_gated_delta_rule(q map)"))
-    return rc;
-  if (int rc = token_rows_map(&mk, kk, Hg * K, B * T, ks, "chunk_gated_delta_rule(k map)"))
     return rc;
   if (int rc = token_rows_map(&mv, v, H * V, B * T, v_token_stride,
                               "chunk_gated_delta_rule(v map)"))

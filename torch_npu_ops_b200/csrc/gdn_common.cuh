@@ -192,125 +192,6 @@ __device__ __forceinline__ void tri_inverse_64_inplace(float* __restrict__ sA,
   __syncthreads();
 }
 
-// The same blocked inverse run by 128 threads (t in [0, 128)), so that the
-// two halves of a CTA invert two matrices at once: every __syncthreads is
-// reached by both halves, and each thread computes more outputs per level
-// (4 per 16x16 product, 2 x 4 per 32x32 product) with packed fp32 pairs.
-// The upper triangles of the blocks are zero, so the products run over
-// full index ranges without predicates.  sM needs 32 x 36 floats, 16-byte
-// aligned.
-__device__ __forceinline__ void tri_inverse_64_half(float* __restrict__ sA,
-                                                    float* __restrict__ sM, int t) {
-  {  // 8x8 diagonal blocks by forward substitution
-    float x[8];
-    const int b = t >> 3, c = t & 7;
-    if (t < 64) {
-      const float* Ab = sA + (8 * b) * LDF + 8 * b;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = (i == c) ? 1.f : 0.f;
-#pragma unroll
-      for (int i = 1; i < 8; ++i) {
-        float s = 0.f;
-#pragma unroll
-        for (int m = 0; m < i; ++m) s = fmaf(Ab[i * LDF + m], x[m], s);
-        if (i > c) x[i] = -s;
-      }
-    }
-    __syncthreads();
-    if (t < 64) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sA[(8 * b + i) * LDF + 8 * b + c] = x[i];
-    }
-    __syncthreads();
-  }
-  {  // 8 -> 16: T10 = -T11 (A10 T00) in the four 16x16 diagonal blocks
-    const int p = t >> 5, e = t & 31, rr = e >> 2, cc = (e & 3) * 2;
-    const int r0 = 16 * p + 8, c0 = 16 * p;
-    float2 s = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      const float a = sA[(r0 + rr) * LDF + c0 + m];
-      const float* tr = sA + (c0 + m) * LDF + c0 + cc;
-      s = ffma2(make_float2(a, a), make_float2(tr[0], tr[1]), s);
-    }
-    sM[p * 64 + rr * 8 + cc] = s.x;
-    sM[p * 64 + rr * 8 + cc + 1] = s.y;
-    __syncthreads();
-    float2 u = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      const float a = sA[(r0 + rr) * LDF + r0 + m];
-      u = ffma2(make_float2(a, a), make_float2(sM[p * 64 + m * 8 + cc], sM[p * 64 + m * 8 + cc + 1]), u);
-    }
-    sA[(r0 + rr) * LDF + c0 + cc] = -u.x;
-    sA[(r0 + rr) * LDF + c0 + cc + 1] = -u.y;
-  }
-  __syncthreads();
-  {  // 16 -> 32: T10 = -T11 A10 T00 and T32 = -T33 A32 T22; 4 outputs per thread
-    const int p = t >> 6, e = t & 63, rr = e >> 2, cc = (e & 3) * 4;
-    const int r = 16 * (2 * p + 1), cb = 32 * p;
-    float2 s0 = make_float2(0.f, 0.f), s1 = make_float2(0.f, 0.f);
-#pragma unroll 4
-    for (int m = 0; m < 16; ++m) {
-      const float a = sA[(r + rr) * LDF + cb + m];
-      const float* tr = sA + (cb + m) * LDF + cb + cc;
-      s0 = ffma2(make_float2(a, a), make_float2(tr[0], tr[1]), s0);
-      s1 = ffma2(make_float2(a, a), make_float2(tr[2], tr[3]), s1);
-    }
-    *reinterpret_cast<float4*>(sM + p * 256 + rr * 16 + cc) = make_float4(s0.x, s0.y, s1.x, s1.y);
-    __syncthreads();
-    float2 u0 = make_float2(0.f, 0.f), u1 = make_float2(0.f, 0.f);
-#pragma unroll 4
-    for (int m = 0; m < 16; ++m) {
-      const float a = sA[(r + rr) * LDF + r + m];
-      const float4 mr = *reinterpret_cast<const float4*>(sM + p * 256 + m * 16 + cc);
-      u0 = ffma2(make_float2(a, a), make_float2(mr.x, mr.y), u0);
-      u1 = ffma2(make_float2(a, a), make_float2(mr.z, mr.w), u1);
-    }
-    float* out = sA + (r + rr) * LDF + cb + cc;
-    out[0] = -u0.x; out[1] = -u0.y; out[2] = -u1.x; out[3] = -u1.y;
-  }
-  __syncthreads();
-  {  // 32 -> 64: T[32:64][0:32] = -T11 (A10 T00); 2 x 4 outputs per thread
-    const int rr = (t >> 3) * 2, cc = (t & 7) * 4;
-    float2 s[2][2] = {{make_float2(0.f, 0.f), make_float2(0.f, 0.f)},
-                      {make_float2(0.f, 0.f), make_float2(0.f, 0.f)}};
-#pragma unroll 4
-    for (int m = 0; m < 32; ++m) {
-      const float a0 = sA[(32 + rr) * LDF + m], a1 = sA[(33 + rr) * LDF + m];
-      const float* tr = sA + m * LDF + cc;
-      const float2 ta = make_float2(tr[0], tr[1]), tb = make_float2(tr[2], tr[3]);
-      s[0][0] = ffma2(make_float2(a0, a0), ta, s[0][0]);
-      s[0][1] = ffma2(make_float2(a0, a0), tb, s[0][1]);
-      s[1][0] = ffma2(make_float2(a1, a1), ta, s[1][0]);
-      s[1][1] = ffma2(make_float2(a1, a1), tb, s[1][1]);
-    }
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-      *reinterpret_cast<float4*>(sM + (rr + a) * 36 + cc) =
-          make_float4(s[a][0].x, s[a][0].y, s[a][1].x, s[a][1].y);
-    __syncthreads();
-    float2 u[2][2] = {{make_float2(0.f, 0.f), make_float2(0.f, 0.f)},
-                      {make_float2(0.f, 0.f), make_float2(0.f, 0.f)}};
-#pragma unroll 4
-    for (int m = 0; m < 32; ++m) {
-      const float a0 = sA[(32 + rr) * LDF + 32 + m], a1 = sA[(33 + rr) * LDF + 32 + m];
-      const float4 mr = *reinterpret_cast<const float4*>(sM + m * 36 + cc);
-      const float2 ma = make_float2(mr.x, mr.y), mb = make_float2(mr.z, mr.w);
-      u[0][0] = ffma2(make_float2(a0, a0), ma, u[0][0]);
-      u[0][1] = ffma2(make_float2(a0, a0), mb, u[0][1]);
-      u[1][0] = ffma2(make_float2(a1, a1), ma, u[1][0]);
-      u[1][1] = ffma2(make_float2(a1, a1), mb, u[1][1]);
-    }
-#pragma unroll
-    for (int a = 0; a < 2; ++a) {
-      float* out = sA + (32 + rr + a) * LDF + cc;
-      out[0] = -u[a][0].x; out[1] = -u[a][0].y; out[2] = -u[a][1].x; out[3] = -u[a][1].y;
-    }
-  }
-  __syncthreads();
-}
-
 // Inclusive cumsum of g[0..63] (rows >= L zero) by warp 0 into sG; returns
 // nothing, sG[L-1] is the chunk's last cumulative gate.
 __device__ __forceinline__ void chunk_cumsum_warp(const float* __restrict__ graw, float* sG,

@@ -53,6 +53,18 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
   return d;
 }
 
+// K-major operand with 64-byte rows (SWIZZLE_64B: 16-byte chunk c of row r
+// at c ^ ((r >> 1) & 3), 8-row groups 512 bytes apart).
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= (uint64_t)1 << 46;  // version (sm_100)
+  d |= (uint64_t)4 << 61;  // SWIZZLE_64B
+  return d;
+}
+
 // K-major SW128 operand, K-step j (16 bf16) of a [rows x 128] tile.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile, int rows, int kstep) {
   const uint32_t a = tile + (uint32_t)((kstep >> 2) * rows * 128 + (kstep & 3) * 32);
@@ -73,6 +85,29 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool 
   return (1u << 4) | (1u << 7) | (1u << 10) | ((neg_b ? 1u : 0u) << 14) |
          ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
+}
+
+// kind::tf32: fp32 operands read as tf32 (K-step = 8 elements = 32 bytes, so
+// SW128 K-major descriptors advance exactly as for bf16), fp32 accumulate.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool b_mn = false,
+                                                  bool neg_a = false) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((neg_a ? 1u : 0u) << 13) |
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate));
+}
+// fp32 -> tf32 rounded to nearest (ties away), low 13 bits zero, so the
+// tensor core reads exactly this value instead of truncating.
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
 }
 
 // D[tmem] (+)= A * B ; single issuing thread.
@@ -271,6 +306,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
       " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_addr(bar))
       : "memory");
+}
+// Pull the box at (x, y) into L2 (no shared memory, no completion tracking).
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];\n" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y)
+               : "memory");
 }
 // 2-D tiled store shared -> global of the box at (x, y), tracked by this
 // thread's bulk async-group.
