@@ -37,9 +37,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "GDN prefill tokens/s/GPU; norm/RoPE/conv1d HBM GB/s vs B200 peak"
-# 1,308.7 MB of DRAM traffic for 16,384 tokens x 32 value heads (prep, both
+# 1,312.3 MB of DRAM traffic for 16,384 tokens x 32 value heads (prep, both
 # chain phases, combine), measured by ncu (dram__bytes_read.sum + write.sum)
-GDN_DRAM_BYTES_PER_TOKEN_HEAD = 1.3087e9 / (16384 * 32)
+GDN_DRAM_BYTES_PER_TOKEN_HEAD = 1.3123e9 / (16384 * 32)
 
 
 def _peaks():

@@ -484,10 +484,6 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_tc_kernel(
   const uint32_t am = sb + P3_OFF_AM, at = sb + P3_OFF_AT, bm = sb + P3_OFF_BM, bt = sb + P3_OFF_BT;
   float* d0s = reinterpret_cast<float*>(sm + P3_OFF_D0);
 
-  if (warp == 0) {
-    tc::tmem_alloc(&tmem_sh, P3_TM_COLS);
-    tc::tmem_relinquish();
-  }
   if (tid == 0) {
     tc::mbar_init(&bar, 1);
     tc::mbar_init(&ldbar, 1);
@@ -509,6 +505,19 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_tc_kernel(
         tc::tma_prefetch_2d(&tm_k, py * 128 + hf * 64, px * BT);
         tc::tma_prefetch_2d(&tm_q, py * 128 + hf * 64, px * BT);
       }
+    }
+  }
+  if (warp == 0) {  // after the loads are on their way
+    tc::tmem_alloc(&tmem_sh, P3_TM_COLS);
+    tc::tmem_relinquish();
+  }
+  if (tid >= 128 && tid < 128 + BT && gs.g) {  // the successor's gate rows, into L2
+    const int64_t nxt = (int64_t)blockIdx.y * gridDim.x + blockIdx.x + resident;
+    const int64_t tok = (nxt % gridDim.x) * BT + (tid - 128);
+    if (nxt < (int64_t)gridDim.x * gridDim.y && tok < T) {
+      const int64_t off = tok * H + 2 * (nxt / gridDim.x);
+      asm volatile("prefetch.global.L2 [%0];\n" ::"l"(gs.g + off));
+      asm volatile("prefetch.global.L2 [%0];\n" ::"l"(gs.beta + off));
     }
   }
   if (tid < 128) {  // both heads' gates
