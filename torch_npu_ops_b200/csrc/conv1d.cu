@@ -594,10 +594,17 @@ __global__ void __launch_bounds__(RB_NT, 3) conv1d_varlen_tma_kernel(
             const float2 r0 = unpack2<T>(packed[du].x), r1 = unpack2<T>(packed[du].y);
             ss[du] = r0.x * r0.x + r0.y * r0.y + r1.x * r1.x + r1.y * r1.y;
           }
+          // two sums in six shuffles: the first exchange leaves token 0's
+          // partial sums in lanes 0-15 and token 1's in lanes 16-31, each
+          // half reduces its own, and one exchange hands every lane both
+          const bool hi = lane & 16;
+          float keep = hi ? ss[1] : ss[0];
+          keep += __shfl_xor_sync(0xffffffffu, hi ? ss[0] : ss[1], 16);
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int du = 0; du < 2; ++du) ss[du] += __shfl_xor_sync(0xffffffffu, ss[du], o);
+          for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+          const float other = __shfl_xor_sync(0xffffffffu, keep, 16);
+          ss[0] = hi ? other : keep;
+          ss[1] = hi ? keep : other;
 #pragma unroll
           for (int du = 0; du < 2; ++du) {
             const float rn = rsqrtf(ss[du] + l2_eps);
