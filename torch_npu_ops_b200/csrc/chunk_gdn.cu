@@ -448,8 +448,7 @@ __device__ __forceinline__ uint64_t op_desc(uint32_t main, uint32_t tail, int ks
 __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const GateSrc gs, unsigned char* __restrict__ ws,
-    const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H,
-    int resident) {
+    const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -494,31 +493,10 @@ __global__ void __launch_bounds__(P_NT, 3) chunk_prep_pair_tc_kernel(
       tc::tma_load_2d(sm + P_OFF_KQ + hf * P_KQ_HALF, &tm_k, hk * 128 + hf * 64, (int)t0, &ldbar);
       tc::tma_load_2d(sm + P_OFF_Q + hf * P_KQ_HALF, &tm_q, hk * 128 + hf * 64, (int)t0, &ldbar);
     }
-    // Into L2 ahead of time: the tiles of the CTA that will most likely take
-    // this one's place (`resident` CTAs run at once, launched in linear
-    // order).  Chunk slot x starts near token 64 x; a miss only costs the
-    // prefetch, coordinates past the tensor are dropped.
-    const int64_t nxt = (int64_t)blockIdx.y * gridDim.x + blockIdx.x + resident;
-    if (nxt < (int64_t)gridDim.x * gridDim.y) {
-      const int px = (int)(nxt % gridDim.x), py = (int)(nxt / gridDim.x);
-      for (int hf = 0; hf < 2; ++hf) {
-        tc::tma_prefetch_2d(&tm_k, py * 128 + hf * 64, px * BT);
-        tc::tma_prefetch_2d(&tm_q, py * 128 + hf * 64, px * BT);
-      }
-    }
   }
   if (warp == 0) {  // after the loads are on their way
     tc::tmem_alloc(&tmem_sh, P3_TM_COLS);
     tc::tmem_relinquish();
-  }
-  if (tid >= 128 && tid < 128 + BT && gs.g) {  // the successor's gate rows, into L2
-    const int64_t nxt = (int64_t)blockIdx.y * gridDim.x + blockIdx.x + resident;
-    const int64_t tok = (nxt % gridDim.x) * BT + (tid - 128);
-    if (nxt < (int64_t)gridDim.x * gridDim.y && tok < T) {
-      const int64_t off = tok * H + 2 * (nxt / gridDim.x);
-      asm volatile("prefetch.global.L2 [%0];\n" ::"l"(gs.g + off));
-      asm volatile("prefetch.global.L2 [%0];\n" ::"l"(gs.beta + off));
-    }
   }
   if (tid < 128) {  // both heads' gates
     const int h = tid >> 6, t = tid & 63;
@@ -1928,23 +1906,8 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
     if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_prep_pair_tc_kernel, gdn::P3_SMEM,
                                        "chunk_gated_delta_rule(prep)"))
       return rc;
-    // CTAs of the kernel that run at once (three per SM), per device: each
-    // CTA prefetches the tiles of the one expected to take its place
-    static int resident_by_dev[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int resident = dev < 64 ? resident_by_dev[dev] : 0;
-    if (!resident) {
-      int sms = 0, per_sm = 0;
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gdn::chunk_prep_pair_tc_kernel,
-                                                    gdn::P_NT, gdn::P3_SMEM);
-      resident = (sms > 0 ? sms : 1) * (per_sm > 0 ? per_sm : 1);
-      if (dev < 64) resident_by_dev[dev] = resident;
-    }
     gdn::chunk_prep_pair_tc_kernel<<<dim3((unsigned)nchunks, (unsigned)Hg), gdn::P_NT,
-                                     gdn::P3_SMEM, st>>>(mq, mk, gs, ws, cu_seqlens, N, T, Hg, H,
-                                                         resident);
+                                     gdn::P3_SMEM, st>>>(mq, mk, gs, ws, cu_seqlens, N, T, Hg, H);
   } else {
     if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_prep_kernel, gdn::P_SMEM,
                                        "chunk_gated_delta_rule(prep)"))

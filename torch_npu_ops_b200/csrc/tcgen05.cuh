@@ -307,13 +307,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_addr(bar))
       : "memory");
 }
-// Pull the box at (x, y) into L2 (no shared memory, no completion tracking).
-__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];\n" ::"l"(
-                   reinterpret_cast<uint64_t>(tmap)),
-               "r"(x), "r"(y)
-               : "memory");
-}
 // 2-D tiled store shared -> global of the box at (x, y), tracked by this
 // thread's bulk async-group.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, const void* src) {
