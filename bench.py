@@ -556,12 +556,21 @@ def main():
         d2h = sum(t.numel() * t.element_size() for t in outs0)
 
         # Every step uploads its own inputs and reads back its own results
-        # (the normed output and the final state).  The copies run on two copy
+        # (the normed output and the final state).  The copies run on their own
         # streams (PCIe is full duplex) into two alternating device buffer
         # sets, so step i+1's upload overlaps step i's compute and readback;
-        # compute itself stays on one stream.
+        # compute itself stays on one stream.  The upload is split over two
+        # streams by bytes, so two copy engines share it.
         comp = torch.cuda.current_stream(dev)
         h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        h2d_s2 = torch.cuda.Stream(device=dev)
+        order = sorted(host, key=lambda n: -host[n].numel() * host[n].element_size())
+        lanes = ([], [])
+        loads = [0, 0]
+        for n in order:
+            j = 0 if loads[0] <= loads[1] else 1
+            lanes[j].append(n)
+            loads[j] += host[n].numel() * host[n].element_size()
         dbufs = [dbuf, {n: torch.empty_like(t) for n, t in cfg["dev"].items()}]
         houts = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs0]
                  for _ in range(2)]
@@ -569,13 +578,14 @@ def main():
 
         def e2e_step(i):
             b = i & 1
-            with torch.cuda.stream(h2d_s):
-                h2d_s.wait_event(in_free[b])  # the compute that read this buffer set is done
-                for n in host:
-                    dbufs[b][n].copy_(host[n], non_blocking=True)
-                loaded = torch.cuda.Event()
-                loaded.record(h2d_s)
-            comp.wait_event(loaded)
+            for cs, names in zip((h2d_s, h2d_s2), lanes):
+                with torch.cuda.stream(cs):
+                    cs.wait_event(in_free[b])  # the compute that read this buffer set is done
+                    for n in names:
+                        dbufs[b][n].copy_(host[n], non_blocking=True)
+                    loaded = torch.cuda.Event()
+                    loaded.record(cs)
+                comp.wait_event(loaded)
             outs = step(dbufs[b])
             in_free[b].record(comp)
             done = torch.cuda.Event()
@@ -596,6 +606,7 @@ def main():
         for i in range(a.steps):
             e2e_step(i)
         comp.wait_stream(h2d_s)
+        comp.wait_stream(h2d_s2)
         comp.wait_stream(d2h_s)
         t2.record(comp)
         torch.cuda.synchronize(dev)
