@@ -1237,7 +1237,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         const int s = i & 1;
         const uint32_t st = sb + s * STAGE;
         if (!has_v && !(live = tc::mbar_wait(&full[s], (i >> 1) & 1, WAIT_LIMIT))) break;
-        if (!(live = tc::mbar_wait_spin(&bar_ht, i & 1, WAIT_LIMIT))) break;
+        if (!(live = tc::mbar_wait(&bar_ht, i & 1, WAIT_LIMIT))) break;
         tc::fence_after();
         const uint64_t dwq = kdesc(st + S_WQ, 16384, 0);
         if (write_o) {
@@ -1258,7 +1258,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         }
         tc::commit(&early_free[s]);
         if (write_o && i > 0 && !(live = issue_o(i - 1))) break;
-        if (!(live = tc::mbar_wait_spin(&bar_vt, i & 1, WAIT_LIMIT))) break;
+        if (!(live = tc::mbar_wait(&bar_vt, i & 1, WAIT_LIMIT))) break;
         tc::fence_after();
         // dS = vt_hi^T k + vt_lo^T k
         const uint64_t dk = mndesc(st + S_K, 8192, 0);

@@ -371,13 +371,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 // The same for warps that share a scheduler with a latency-critical issuer:
 // between polls the warp sleeps briefly, so its polling does not take issue
 // slots from the thread it is waiting on.
-// The same without the suspend of try_wait: for a single latency-critical
-// thread whose wake-up delay would sit on the critical path.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, uint32_t limit) {
-  for (uint32_t i = 0; i < limit; ++i)
-    if (mbar_test_wait(bar, parity)) return true;
-  return false;
-}
 __device__ __forceinline__ bool mbar_wait_polite(uint64_t* bar, uint32_t parity, uint32_t limit) {
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
