@@ -1237,9 +1237,9 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         const int s = i & 1;
         const uint32_t st = sb + s * STAGE;
         if (!has_v && !(live = tc::mbar_wait(&full[s], (i >> 1) & 1, WAIT_LIMIT))) break;
+        const uint64_t dwq = kdesc(st + S_WQ, 16384, 0);
         if (!(live = tc::mbar_wait(&bar_ht, i & 1, WAIT_LIMIT))) break;
         tc::fence_after();
-        const uint64_t dwq = kdesc(st + S_WQ, 16384, 0);
         if (write_o) {
           // one N = 128 product over the [-w; q] tile: D_u += S^T (-w)^T next
           // to D_qh = S^T q^T (the epilogue zeroed D_qh after reading it)
@@ -1258,10 +1258,10 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         }
         tc::commit(&early_free[s]);
         if (write_o && i > 0 && !(live = issue_o(i - 1))) break;
-        if (!(live = tc::mbar_wait(&bar_vt, i & 1, WAIT_LIMIT))) break;
-        tc::fence_after();
         // dS = vt_hi^T k + vt_lo^T k
         const uint64_t dk = mndesc(st + S_K, 8192, 0);
+        if (!(live = tc::mbar_wait(&bar_vt, i & 1, WAIT_LIMIT))) break;
+        tc::fence_after();
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           tc::mma_bf16_ts(tm + C_TM_DS, tm + C_TM_VTH + 8 * j, dk + j * MNSTEP, id_s, j > 0);
@@ -1382,23 +1382,21 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     };
     auto apply_ds = [&](float dl) {  // S = e^{gl} S + dS
       const float2 dl2 = make_float2(dl, dl);
+      float d[32];  // both 16-column loads in flight before one wait
+      tc::tmem_ld16(tm_addr(tm, quarter, C_TM_DS + kc0), *reinterpret_cast<float(*)[16]>(d));
+      tc::tmem_ld16(tm_addr(tm, quarter, C_TM_DS + kc0 + 16), *reinterpret_cast<float(*)[16]>(d + 16));
+      tc::tmem_wait_ld();
 #pragma unroll
-      for (int cb = 0; cb < 2; ++cb) {  // 16 columns at a time keeps registers under 96
-        float d[16];
-        tc::tmem_ld16(tm_addr(tm, quarter, C_TM_DS + kc0 + cb * 16), d);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int m = 0; m < 8; ++m)
-          S[cb * 8 + m] = ffma2(S[cb * 8 + m], dl2, make_float2(d[2 * m], d[2 * m + 1]));
-      }
+      for (int m = 0; m < 16; ++m) S[m] = ffma2(S[m], dl2, make_float2(d[2 * m], d[2 * m + 1]));
     };
     // D_qh starts at zero: the [-w; q] product accumulates into it
     if (write_o) tc::tmem_st16_zero(tm_addr(tm, quarter, C_TM_QH + tc0));
     for (int i = 0; i < NI; ++i) {
       const int s = i & 1;
       if (i > 0) {
+        const float dl = __expf(gl_prev);  // ahead of the wait, off the critical path
         if (!(live = wait_ok(&bar_s, (i - 1) & 1))) break;
-        apply_ds(__expf(gl_prev));
+        apply_ds(dl);
       }
       if (*(volatile int*)&abort_sh) { live = false; break; }
       // E0: bf16 S^T -> TMEM (columns kc0/2 .. kc0/2 + 15), then let the MMA warp go
@@ -1410,8 +1408,11 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       }
       warp_arrive(&bar_ht);
       if (!(live = wait_ok(&full[s], (i >> 1) & 1))) break;
-      if (!(live = wait_ok(&bar_v, i & 1))) break;
       const float* tab = reinterpret_cast<const float*>(sm + C_OFF_TAB + (i & 3) * C_TAB);
+      float4 ev[4];  // the chunk's e^{gl-gc} (ready with the stage), before the product lands
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) ev[q4] = *reinterpret_cast<const float4*>(tab + tc0 + 4 * q4);
+      if (!(live = wait_ok(&bar_v, i & 1))) break;
       const int64_t t0 = bos + (int64_t)(c0 + i) * BT;
       const int L = (int)((eos - t0) < BT ? (eos - t0) : BT);
       // E1a: v_new = D_u (exact diagonal included); vt = v_new e^{gl-gc} as
@@ -1423,7 +1424,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         uint32_t hi[8], lo[8];
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
-          const float4 e4 = *reinterpret_cast<const float4*>(tab + tc0 + 4 * q4);
+          const float4 e4 = ev[q4];
 #pragma unroll
           for (int p = 0; p < 2; ++p) {
             const int u = 2 * q4 + p;
