@@ -1393,12 +1393,14 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     if (write_o) tc::tmem_st16_zero(tm_addr(tm, quarter, C_TM_QH + tc0));
     for (int i = 0; i < NI; ++i) {
       const int s = i & 1;
+      // the abort flag and e^{gl} are read ahead of the wait, off the critical path
+      const bool aborted = *(volatile int*)&abort_sh != 0;
       if (i > 0) {
-        const float dl = __expf(gl_prev);  // ahead of the wait, off the critical path
+        const float dl = __expf(gl_prev);
         if (!(live = wait_ok(&bar_s, (i - 1) & 1))) break;
         apply_ds(dl);
       }
-      if (*(volatile int*)&abort_sh) { live = false; break; }
+      if (aborted) { live = false; break; }
       // E0: bf16 S^T -> TMEM (columns kc0/2 .. kc0/2 + 15), then let the MMA warp go
       {
         uint32_t pk[16];
@@ -1412,9 +1414,9 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
       float4 ev[4];  // the chunk's e^{gl-gc} (ready with the stage), before the product lands
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) ev[q4] = *reinterpret_cast<const float4*>(tab + tc0 + 4 * q4);
-      if (!(live = wait_ok(&bar_v, i & 1))) break;
       const int64_t t0 = bos + (int64_t)(c0 + i) * BT;
       const int L = (int)((eos - t0) < BT ? (eos - t0) : BT);
+      if (!(live = wait_ok(&bar_v, i & 1))) break;
       // E1a: v_new = D_u (exact diagonal included); vt = v_new e^{gl-gc} as
       // bf16 hi + lo for the state product (critical path: hand it over first)
       float du[16];
