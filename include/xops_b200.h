@@ -310,6 +310,28 @@ XOPS_API int xops_chunk_gated_delta_rule_gated(
     int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
     void* workspace, int64_t workspace_bytes, void* stream);
 
+/* The rule followed by the GDN layer's output norm, as one operator: each
+ * (token, value head) row of V values of o (as the bf16 value
+ * xops_chunk_gated_delta_rule would store) becomes
+ *   y = ((o * rstd) * w) * silu(z),  rstd = 1 / sqrt(mean(o^2) + eps)
+ * inside the chain kernel's output epilogue, so o makes no round trip
+ * through HBM.  This is layer_norm_fwd with is_rms_norm, norm_before_gate,
+ * no bias and group size V (npu_triton_layernorm_fwd.cpp:48-333), which the
+ * layer runs on the rule's output.  z: bf16 rows of H * V per token,
+ * z_token_stride elements apart (0 = H * V), 16-byte aligned; norm_weight
+ * [V] of weight_dtype XOPS_F32 or XOPS_BF16; y [B, T, H, V] bf16.  o may be
+ * NULL (only y is written) or a buffer that also receives o.  Other
+ * arguments and the workspace as xops_chunk_gated_delta_rule.  This fusion
+ * has no single counterpart in the reference; it replaces the pair
+ * npu_chunk_gated_delta_rule -> layer_norm_fwd. */
+XOPS_API int xops_chunk_gated_delta_rule_out_norm(
+    const void* q, const void* k, const void* v, const float* g, const float* beta,
+    const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
+    int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
+    int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
+    const void* z, int64_t z_token_stride, const void* norm_weight, int weight_dtype, float eps,
+    void* y, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Workspace bytes xops_chunk_gated_delta_rule needs (an upper bound computed
  * from shapes only, no device access); varlen = cu_seqlens given. */
 XOPS_API int64_t xops_chunk_gated_delta_rule_workspace_size(int64_t B, int64_t T, int64_t N,

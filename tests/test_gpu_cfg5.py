@@ -2,8 +2,9 @@
 sequence through causal conv1d (its q/k blocks L2-normalised in the same
 kernel) -> chunked gated delta rule (Hk 16 -> Hv 32, initial state) -> gated
 RMSNorm, exactly as ``bench.py`` runs it
-(``torch_npu_ops_b200.pipeline.gdn_prefill``), on one GPU and on every rank's
-head shard of worlds 2, 4 and 8.
+(``torch_npu_ops_b200.pipeline.gdn_prefill``, the norm inside the chunked
+rule's chain kernel), on one GPU and on every rank's head shard of worlds 2,
+4 and 8.
 
 References, all CPU oracle (restating the reference's torch code), taken
 before their final rounding to bf16:
@@ -57,13 +58,22 @@ D = workloads.HEAD_DIM
 
 
 def _run(w, hk, hv):
+    """The bench's call (the norm inside the chain, o not written), and the
+    same call asked to write o too for the stage checks: both give the same
+    normalised output bit for bit."""
     dev = {n: w[n].to(DEV) for n in ("x", "weight", "bias", "g", "beta", "initial_state", "z",
                                      "norm_w")}
-    st = torch.zeros(1, w["x"].shape[1], 3, dtype=torch.bfloat16, device=DEV)
-    y, o, ht, out = gdn_prefill(dev["x"], st, dev["weight"], dev["bias"], dev["g"], dev["beta"],
-                                dev["initial_state"], dev["z"], dev["norm_w"], hk, hv)
+    res = []
+    for return_o in (False, True):
+        st = torch.zeros(1, w["x"].shape[1], 3, dtype=torch.bfloat16, device=DEV)
+        res.append((st,) + gdn_prefill(dev["x"], st, dev["weight"], dev["bias"], dev["g"],
+                                       dev["beta"], dev["initial_state"], dev["z"], dev["norm_w"],
+                                       hk, hv, return_o=return_o))
     torch.cuda.synchronize()
     assert _lib.load().xops_device_error_count() == 0
+    (st0, y0, o0, ht0, out0), (st, y, o, ht, out) = res
+    assert o0 is None
+    assert torch.equal(out0, out) and torch.equal(ht0, ht) and torch.equal(y0, y)
     return {"y": y.cpu(), "o": o.cpu(), "ht": ht.cpu(), "out": out.cpu().view(T, hv, D),
             "state": st.cpu()}
 

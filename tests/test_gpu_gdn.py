@@ -450,10 +450,59 @@ def test_gdn_prefill_gating_option():
         gg, bb = (g, beta.float()) if gating is None else (None, None)
         outs.append(gdn_prefill(_to(w["x"]), st, _to(w["weight"]), _to(w["bias"]), gg, bb,
                                 _to(w["initial_state"]), _to(w["z"]), _to(w["norm_w"]), hk, hv,
-                                gating=gating))
+                                gating=gating, fuse_norm=False))
     torch.cuda.synchronize()
     for x1, x2 in zip(*outs):
         assert torch.equal(x1, x2)
+
+
+@pytest.mark.parametrize("T,hk,hv,lens", [
+    (8192, 2, 4, None),             # a head shard of the bench configuration: one segment plan
+    (65536, 2, 4, None),            # the 8-GPU shard: segmented chain (phase 1 + phase 3 outputs)
+    (3000, 4, 8, [1000, 64, 1936]),  # varlen, chunks cut by sequence ends
+    (4160, 4, 8, [77, 4000, 83]),   # short sequences and partial 16-token row groups
+])
+def test_out_norm_fused_equals_rule_then_norm(T, hk, hv, lens):
+    """The gated RMSNorm inside the chain's output epilogue
+    (chunk_gated_delta_rule_out_norm) equals npu_chunk_gated_delta_rule
+    followed by layer_norm_fwd (its streaming kernel, which every shape
+    here takes) bit for bit: y, the final state, and o when it is asked
+    for; asking for o leaves y unchanged."""
+    from torch_npu_ops_b200.pipeline import gdn_prefill
+    g = torch.Generator().manual_seed(T + 7 * hv)
+    d = 128
+    C = (2 * hk + hv) * d
+    x = torch.randn(T, C, generator=g).to(torch.bfloat16)
+    cw = (0.5 * torch.randn(C, 4, generator=g)).to(torch.bfloat16)
+    cb = (0.5 * torch.randn(C, generator=g)).to(torch.bfloat16)
+    gate, beta = workloads.gdn_gates(T, hv, g)
+    lens = lens or [T]
+    assert sum(lens) == T
+    N = len(lens)
+    h0 = 0.02 * torch.randn(N, hv, d, d, generator=g)
+    z = torch.randn(T, hv, d, generator=g).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    qsl = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    outs = []
+    for fuse, ret_o in ((True, False), (True, True), (False, True)):
+        st = torch.zeros(N, C, 3, dtype=torch.bfloat16, device=DEV)
+        outs.append(gdn_prefill(_to(x), st, _to(cw), _to(cb), _to(gate)[None], _to(beta)[None],
+                                _to(h0), _to(z), _to(nw), hk, hv, query_start_loc=qsl,
+                                return_o=ret_o, fuse_norm=fuse))
+    torch.cuda.synchronize()
+    assert _lib_errors() == 0
+    (y0, o0, h0a, n0), (y1, o1, h1, n1), (y2, o2, h2, n2) = outs
+    assert o0 is None
+    assert torch.equal(y0, y2) and torch.equal(y1, y2)
+    assert torch.equal(o1, o2)
+    assert torch.equal(h0a, h2) and torch.equal(h1, h2)
+    assert torch.equal(n0, n2), (n0.float() - n2.float()).abs().max().item()
+    assert torch.equal(n1, n2)
+
+
+def _lib_errors():
+    from torch_npu_ops_b200 import _lib
+    return _lib.load().xops_device_error_count()
 
 
 @pytest.mark.parametrize("T,hk,hv,lens", [(8192, 2, 4, None), (3000, 4, 8, [1000, 64, 1936]),
@@ -485,7 +534,7 @@ def test_gdn_layer_prefill_from_projections(T, hk, hv, lens):
                                                                 hv, d, d)
     gt, beta = ops.npu_fused_gdn_gating(_to(A_log), a, b, _to(dt_bias))
     plain = gdn_prefill(mixed_qkv, st2, _to(w), _to(cb), gt, beta.float(), _to(h0), z, _to(nw), hk,
-                        hv, query_start_loc=qsl)
+                        hv, query_start_loc=qsl, fuse_norm=False)
     torch.cuda.synchronize()
     for x1, x2 in zip(fused, plain):
         assert torch.equal(x1, x2)

@@ -898,8 +898,13 @@ constexpr int S_K = 0, S_WQ = 16384, S_V = 49152, S_TP = 65536, S_AQK = 73728;
 constexpr int C_OFF_TPL = 2 * STAGE;          // diag(beta - bf16(beta)) [64 x 64]
 constexpr int C_OFF_TAB = C_OFF_TPL + 8192;   // 4 slots (chunk & 3): e^{gl-gc}[64], e^{gc}[64], gl
 constexpr int C_TAB = 1024;
-constexpr int C_OFF_OST = C_OFF_TAB + 4 * C_TAB;  // output transpose: [warp][16 x 32] bf16
-constexpr int C_SMEM = C_OFF_OST + C_EPI_WARPS * 2048 + 1024;
+// per epilogue warp: the output transpose [16 x 32] bf16, then the norm's
+// gate rows z (and the normalised rows, in place) [16 x 32] bf16
+constexpr int C_OFF_OST = C_OFF_TAB + 4 * C_TAB;
+// fused output norm: weight [128] fp32, then the partial sums of squares of
+// 8 values each [column quarter][2 alternating sets][16 tokens][16 pieces] fp32
+constexpr int C_OFF_NRM = C_OFF_OST + C_EPI_WARPS * 2048;
+constexpr int C_SMEM = C_OFF_NRM + 512 + 8192 + 1024;
 // TMEM columns.  fp32 accumulators: D_u, D_qh (adjacent: one N = 128 product
 // fills both), D_o, dS.  bf16 A operands written by the epilogue (packed in
 // pairs, so a [128 x K] operand takes K/2 columns): S^T, vt hi, vt lo, v_new.
@@ -927,6 +932,22 @@ struct ChainPlan {
   float* scratch;  // [slot][H][3][K*V]: start state, B, X (slot = segment index over all sequences)
 };
 
+// Gated RMSNorm of the output, fused into the chain's output epilogue: each
+// (token, value head) row of V values becomes
+//   y = ((o * rstd) * w) * silu(z),  rstd = 1 / sqrt(mean(o^2) + eps),
+// o taken as the bf16 value the unfused operator would store.  This is the
+// layer_norm_fwd (is_rms_norm, norm_before_gate, no bias, group = V) that
+// the GDN layer applies to the rule's output next.  z == nullptr: no norm.
+struct OutNorm {
+  const bf16* z;   // [tokens, H * V] gate rows, ldz elements between tokens
+  const void* w;   // [V] weight, fp32 (w_f32) or bf16
+  bf16* y;         // [tokens, H * V] normalised output
+  int64_t ldz;
+  float eps;
+  int w_f32;
+  int keep_o;      // also store o itself
+};
+
 __device__ __forceinline__ float* seg_state(const ChainPlan& p, int64_t slot, int64_t H, int h,
                                             int which) {
   return p.scratch + ((slot * H + h) * 3 + which) * (int64_t)KV;
@@ -939,18 +960,22 @@ __device__ __forceinline__ int seq_chunks(const int32_t* cu, int64_t n, int64_t 
 
 // q, k, v are read through 2-D tensor maps (rows = tokens, 64 x 64 boxes,
 // 128-byte swizzle): the box lands exactly as one half of an SW128 tile.
+// NORM: the fused output norm (a separate instantiation, so the plain rule
+// keeps its own register allocation).
+template <bool NORM>
 __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-    const float* __restrict__ h0,
+    const __grid_constant__ CUtensorMap tm_y, const float* __restrict__ h0,
     const unsigned char* __restrict__ ws, bf16* __restrict__ o, float* __restrict__ ht,
     const int32_t* __restrict__ cu, int64_t N, int64_t T, int64_t Hg, int64_t H, float scale,
-    ChainPlan plan) {
+    ChainPlan plan, OutNorm nrm) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   __shared__ uint64_t full[2], empty[2], early_free[2], tma[2], tma_a[2], aqk_free[2], bar_ht,
       bar_v, bar_q, bar_vt, bar_s, bar_o, bar_od, bar_fin;
+  __shared__ uint64_t nbar[8];  // fused norm: [column quarter][set], the four lane-quarter warps
   __shared__ uint32_t tmem_sh;
   __shared__ int abort_sh;
   __shared__ int64_t it_n;
@@ -1056,11 +1081,16 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     tc::mbar_init(&bar_od, 1);
     tc::mbar_init(&bar_q, 1);
     tc::mbar_init(&bar_fin, 1);
+    for (int e = 0; e < 8; ++e) tc::mbar_init(&nbar[e], 4);
     tc::mbar_fence_init();
     abort_sh = 0;
   }
   for (int e = tid; e < 8192 / 16; e += C_NT)  // diagonal-correction tile starts at zero
     reinterpret_cast<uint4*>(sm + C_OFF_TPL)[e] = make_uint4(0, 0, 0, 0);
+  if (NORM && kind == ITEM_OUT && tid < 128)
+    reinterpret_cast<float*>(sm + C_OFF_NRM)[tid] =
+        nrm.w_f32 ? static_cast<const float*>(nrm.w)[tid]
+                  : __bfloat162float(static_cast<const bf16*>(nrm.w)[tid]);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
@@ -1340,6 +1370,121 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     // sequence end (the rows after it belong to the next sequence) stores its
     // valid rows with plain 16-byte stores instead.
     unsigned char* ost = sm + C_OFF_OST + cw * 2048;
+    // Fused output norm.  A row's 128 values are spread over the four warps
+    // of one column quarter (one per TMEM lane quarter), 8 values per lane.
+    // Each lane's sum of squares of its 8 values goes to shared memory; after
+    // an mbarrier on which the four warps meet (bounded wait, two sets
+    // alternating by call) every lane reads the row's 16 partial sums and
+    // adds them in the butterfly order of the stand-alone gated-norm kernel
+    // (pieces 8 apart, then 4, 2, 1), so y equals that kernel's result on
+    // the stored o bit for bit.  Lane (r, m) loads, normalises and stores
+    // back exactly the 16 bytes it reads (token rows r and r + 8, values
+    // 8m .. 8m + 7 of the warp's 32), in place over o.
+    // The norm of chunk c runs one chunk late, while the tensor core forms
+    // chunk c + 2's [-w; q] product (the epilogue's idle wait), not in the
+    // dS window that bounds the chain; chunk c's z rows arrive by cp.async
+    // into the second half of the warp's buffer one chunk ahead of that.
+    const bool norm = NORM && write_o;
+    const bool store_o = !NORM || nrm.keep_o;
+    unsigned char* zst = ost + 1024;
+    uint32_t ncall = 0;
+    auto load_z = [&](int64_t tb, int Lc) {
+      __syncwarp();  // every lane has read the previous chunk's z
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = (lane >> 2) + 8 * j, m = lane & 3;
+        const bool in = tc0 + r < Lc;
+        cp_async16(zst + r * 64 + m * 16,
+                   nrm.z + (in ? tb + tc0 + r : tb) * nrm.ldz + (int64_t)h * V + quarter * 32 + m * 8,
+                   in ? 16 : 0);
+      }
+      cp_async_commit();
+    };
+    // (the o pieces are read from shared memory twice, before and after the
+    // exchange, rather than held in registers across it)
+    auto norm_rows = [&]() -> bool {
+      const int m = lane & 3;
+      const int set = colq * 2 + (int)(ncall & 1);
+      float* red = reinterpret_cast<float*>(sm + C_OFF_NRM + 512) + set * 256;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = (lane >> 2) + 8 * j;
+        const uint4 p = *reinterpret_cast<const uint4*>(ost + r * 64 + m * 16);
+        const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+        float2 s2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 x = unpack2<bf16>(pw[u]);
+          s2 = ffma2(x, x, s2);
+        }
+        red[r * 16 + quarter * 4 + m] = s2.x + s2.y;
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&nbar[set]);
+      cp_async_wait_all();  // this lane's z pieces, while the other warps arrive
+      if (!wait_ok(&nbar[set], (ncall >> 1) & 1)) return false;
+      ++ncall;
+      const float* wt = reinterpret_cast<const float*>(sm + C_OFF_NRM) + quarter * 32 + m * 8;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = (lane >> 2) + 8 * j;
+        float a[8];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float4 lo = *reinterpret_cast<const float4*>(red + r * 16 + 4 * e);
+          const float4 hi = *reinterpret_cast<const float4*>(red + r * 16 + 8 + 4 * e);
+          a[4 * e] = lo.x + hi.x;
+          a[4 * e + 1] = lo.y + hi.y;
+          a[4 * e + 2] = lo.z + hi.z;
+          a[4 * e + 3] = lo.w + hi.w;
+        }
+        const float b0 = a[0] + a[4], b1 = a[1] + a[5], b2 = a[2] + a[6], b3 = a[3] + a[7];
+        const float tot = (b0 + b2) + (b1 + b3);
+        const float rs = rsqrtf(tot * (1.0f / 128) + nrm.eps);
+        const float2 r2 = make_float2(rs, rs);
+        uint4* op = reinterpret_cast<uint4*>(ost + r * 64 + m * 16);
+        const uint4 p = *op;
+        const uint4 zr = *reinterpret_cast<const uint4*>(zst + r * 64 + m * 16);
+        const uint32_t pw[4] = {p.x, p.y, p.z, p.w}, zw[4] = {zr.x, zr.y, zr.z, zr.w};
+        uint32_t yw[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 w2 = *reinterpret_cast<const float2*>(wt + 2 * u);
+          const float2 g = silu2_lowp(unpack2<bf16>(zw[u]));
+          yw[u] = pack2<bf16>(fmul2(fmul2(fmul2(unpack2<bf16>(pw[u]), r2), w2), g));
+        }
+        if (j == 0 && nrm.keep_o) {  // o's own store has read the buffer
+          if (lane == 0) tc::bulk_wait_read<0>();
+          __syncwarp();
+        }
+        *op = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+      }
+      return true;
+    };
+    // rows [tc0, tc0 + 16) of the staged buffer buf to dst: one TMA store
+    // when all 16 are in the sequence, else the valid rows by 16-byte stores
+    auto store_rows = [&](const CUtensorMap* map, bf16* dst, const unsigned char* buf,
+                          int64_t tb, int Lc) {
+      if (tc0 + C_TCOLS <= Lc) {
+        tc::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          tc::tma_store_2d(map, (int)(h * V + quarter * 32), (int)(tb + tc0), buf);
+          tc::bulk_commit_group();
+        }
+        return;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = (lane >> 2) + 8 * j, m = lane & 3;  // token row, 8-value piece
+        if (tc0 + r < Lc) {
+          const uint4 piece = *reinterpret_cast<const uint4*>(buf + r * 64 + m * 16);
+          *reinterpret_cast<uint4*>(dst + (tb + tc0 + r) * (H * V) + (int64_t)h * V +
+                                    quarter * 32 + m * 8) = piece;
+        }
+      }
+    };
     auto write_out = [&](int64_t tb, int Lc) {
       uint32_t ra[8], rb[8];  // values 0-15 and 16-31 of the warp's lanes
       tc::tmem_ld16x256b_x2(tm_addr(tm, quarter, C_TM_O + tc0), ra);
@@ -1360,25 +1505,14 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         stmatrix_x4_trans(ost + tok * 64 + (16 + vb) * 2, pk(rb[0], rb[1]), pk(rb[2], rb[3]),
                           pk(rb[4], rb[5]), pk(rb[6], rb[7]));
       }
-      if (tc0 + C_TCOLS <= Lc) {
-        tc::fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) {
-          tc::tma_store_2d(&tm_o, (int)(h * V + quarter * 32), (int)(tb + tc0), ost);
-          tc::bulk_commit_group();
-        }
-        return;
-      }
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int r = (lane >> 2) + 8 * j, m = lane & 3;  // token row, 8-value piece
-        if (tc0 + r < Lc) {
-          const uint4 piece = *reinterpret_cast<const uint4*>(ost + r * 64 + m * 16);
-          *reinterpret_cast<uint4*>(o + (tb + tc0 + r) * (H * V) + (int64_t)h * V + quarter * 32 +
-                                    m * 8) = piece;
-        }
-      }
+      if (store_o) store_rows(&tm_o, o, ost, tb, Lc);
+    };
+    // chunk c's y from the o rows write_out left in ost (and its z rows)
+    auto norm_out = [&](int64_t tb, int Lc) -> bool {
+      __syncwarp();  // every lane's transposed rows are in ost
+      if (!norm_rows()) return false;
+      store_rows(&tm_y, nrm.y, ost, tb, Lc);
+      return true;
     };
     auto apply_ds = [&](float dl) {  // S = e^{gl} S + dS
       const float2 dl2 = make_float2(dl, dl);
@@ -1409,6 +1543,11 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         tc::tmem_st16u(tm_addr(tm, quarter, C_TM_HT + kc0 / 2), pk);
       }
       warp_arrive(&bar_ht);
+      if (norm && i > 0) {  // while the tensor core forms [-w; q] of this chunk
+        // chunk i - 2: a whole chunk (only a sequence's last chunk is partial)
+        if (i > 1 && !(live = norm_out(t0_prev - BT, BT))) break;
+        load_z(t0_prev, L_prev);
+      }
       if (!(live = wait_ok(&full[s], (i >> 1) & 1))) break;
       const float* tab = reinterpret_cast<const float*>(sm + C_OFF_TAB + (i & 3) * C_TAB);
       float4 ev[4];  // the chunk's e^{gl-gc} (ready with the stage), before the product lands
@@ -1474,8 +1613,16 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     }
     if (live && NI > 0) {
       if ((live = wait_ok(&bar_s, (NI - 1) & 1))) apply_ds(__expf(gl_prev));
-      if (live && write_o && (live = wait_ok(&bar_od, (NI - 1) & 1))) write_out(t0_prev, L_prev);
+      if (live && norm) {
+        if (NI > 1) live = norm_out(t0_prev - BT, BT);
+        load_z(t0_prev, L_prev);
+      }
+      if (live && write_o && (live = wait_ok(&bar_od, (NI - 1) & 1))) {
+        write_out(t0_prev, L_prev);
+        if (norm) live = norm_out(t0_prev, L_prev);
+      }
     }
+    cp_async_wait_all();  // no z copy outlives the loop
     if (live && it_out) {
       float* dst = it_out;
 #pragma unroll
@@ -1843,7 +1990,8 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
                          int64_t B, int64_t T, int64_t N, int64_t Hg, int64_t H, int64_t K,
                          int64_t V, int64_t q_token_stride, int64_t k_token_stride,
                          int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
-                         void* workspace, int64_t workspace_bytes, void* stream) {
+                         void* workspace, int64_t workspace_bytes, void* stream,
+                         const gdn::OutNorm* nrm = nullptr) {
   XOPS_REQUIRE(B >= 1 && T >= 0 && N >= 0 && Hg >= 1 && H >= 1,
                "chunk_gated_delta_rule: bad shape");
   XOPS_REQUIRE(H % Hg == 0,
@@ -1861,10 +2009,10 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
                    q_token_stride % 8 == 0 && k_token_stride % 8 == 0 && v_token_stride % 8 == 0,
                "chunk_gated_delta_rule: token strides must cover the heads and be multiples of 8");
   if (N == 0 || T == 0) return XOPS_OK;
-  XOPS_REQUIRE(q && k && v && o && (gs.g ? gs.beta != nullptr
-                                           : gs.a && gs.b && gs.A_log && gs.dt_bias),
+  XOPS_REQUIRE(q && k && v && (o || nrm) && (gs.g ? gs.beta != nullptr
+                                                  : gs.a && gs.b && gs.A_log && gs.dt_bias),
                "chunk_gated_delta_rule: null pointer");
-  XOPS_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o),
+  XOPS_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && (!o || aligned16(o)),
                "chunk_gated_delta_rule: tensors must be 16-byte aligned");
   const int64_t need = xops_chunk_gated_delta_rule_workspace_size(
       B, T, N, Hg, H, K, use_qk_l2norm_in_kernel, cu_seqlens != nullptr);
@@ -1919,24 +2067,34 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
         qq, kk, gs, ws, cu_seqlens, N, T, Hg, H, qs, ks);
   }
   if (int rc = check_launch("chunk_gated_delta_rule(prep)")) return rc;
-  if (int rc = gdn::ensure_smem_attr((const void*)gdn::chunk_chain_kernel, gdn::C_SMEM,
+  auto chain = nrm ? gdn::chunk_chain_kernel<true> : gdn::chunk_chain_kernel<false>;
+  if (int rc = gdn::ensure_smem_attr((const void*)chain, gdn::C_SMEM,
                                      "chunk_gated_delta_rule(chain)"))
     return rc;
   if (int rc = token_rows_map(&mv, v, H * V, B * T, v_token_stride,
                               "chunk_gated_delta_rule(v map)"))
     return rc;
-  // o as [tokens, H * V]: each epilogue warp stores 16 tokens x 32 values
-  CUtensorMap mo;
-  if (int rc = token_rows_map(&mo, o, H * V, B * T, H * V, "chunk_gated_delta_rule(o map)", 32,
-                              16, false))
+  // o (and y) as [tokens, H * V]: each epilogue warp stores 16 tokens x 32 values
+  CUtensorMap mo, my;
+  gdn::OutNorm on{};
+  if (nrm) {
+    on = *nrm;
+    on.keep_o = o != nullptr;
+    if (int rc = token_rows_map(&my, on.y, H * V, B * T, H * V, "chunk_gated_delta_rule(y map)",
+                                32, 16, false))
+      return rc;
+  }
+  if (int rc = token_rows_map(&mo, o ? o : on.y, H * V, B * T, H * V,
+                              "chunk_gated_delta_rule(o map)", 32, 16, false))
     return rc;
+  if (!nrm) my = mo;
   const bool varlen = cu_seqlens != nullptr;
   const int seg = chain_segment_chunks(B, T, N, H, varlen);
   gdn::ChainPlan plan{seg, 1, nullptr};
   if (seg == 0) {
-    gdn::chunk_chain_kernel<<<(unsigned)(N * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-        mq, mk, mv, mo, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
-        plan);
+    chain<<<(unsigned)(N * H), gdn::C_NT, gdn::C_SMEM, st>>>(
+        mq, mk, mv, mo, my, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+      plan, on);
     return check_launch("chunk_gated_delta_rule(chain)");
   }
   // Segment-parallel chain: grids are upper bounds, spare CTAs exit at once.
@@ -1944,9 +2102,9 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
   if (use_qk_l2norm_in_kernel) off += round_up256(2 * B * T * Hg * K * 2);
   plan.scratch = reinterpret_cast<float*>(ws + off);
   const int64_t slots = chain_segment_slots(T, N, varlen, seg);
-  gdn::chunk_chain_kernel<<<(unsigned)((N + 2 * slots) * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-      mq, mk, mv, mo, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
-        plan);
+  chain<<<(unsigned)((N + 2 * slots) * H), gdn::C_NT, gdn::C_SMEM, st>>>(
+      mq, mk, mv, mo, my, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+      plan, on);
   if (int rc = check_launch("chunk_gated_delta_rule(chain, first segments)")) return rc;
   {
     // the narrowest column slice whose clusters (4 CTAs each) still fit one
@@ -1984,9 +2142,9 @@ static int chunk_gdn_run(const void* q, const void* k, const void* v, const gdn:
   }
   if (int rc = check_launch("chunk_gated_delta_rule(combine)")) return rc;
   plan.phase = 3;
-  gdn::chunk_chain_kernel<<<(unsigned)(slots * H), gdn::C_NT, gdn::C_SMEM, st>>>(
-      mq, mk, mv, mo, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
-        plan);
+  chain<<<(unsigned)(slots * H), gdn::C_NT, gdn::C_SMEM, st>>>(
+      mq, mk, mv, mo, my, h0, ws, (gdn::bf16*)o, ht, cu_seqlens, N, T, Hg, H, scale,
+      plan, on);
   return check_launch("chunk_gated_delta_rule(chain, remaining segments)");
 }
 
@@ -2039,6 +2197,38 @@ extern "C" int xops_chunk_gated_delta_rule_gated(
   return chunk_gdn_run(q, k, v, gs, h0, o, ht, cu_seqlens, B, T, N, Hg, H, K, V, q_token_stride,
                        k_token_stride, v_token_stride, scale, use_qk_l2norm_in_kernel, workspace,
                        workspace_bytes, stream);
+}
+
+extern "C" int xops_chunk_gated_delta_rule_out_norm(
+    const void* q, const void* k, const void* v, const float* g, const float* beta,
+    const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
+    int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
+    int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
+    const void* z, int64_t z_token_stride, const void* norm_weight, int weight_dtype, float eps,
+    void* y, void* workspace, int64_t workspace_bytes, void* stream) {
+  XOPS_REQUIRE(weight_dtype == XOPS_F32 || weight_dtype == XOPS_BF16,
+               "chunk_gated_delta_rule_out_norm: the norm weight must be fp32 or bf16");
+  if (z_token_stride == 0) z_token_stride = H * V;
+  XOPS_REQUIRE(z_token_stride >= H * V && z_token_stride % 8 == 0,
+               "chunk_gated_delta_rule_out_norm: z token stride must cover the heads and be a "
+               "multiple of 8");
+  if (N > 0 && T > 0)
+    XOPS_REQUIRE(z && norm_weight && y && aligned16(z) && aligned16(y),
+                 "chunk_gated_delta_rule_out_norm: z, weight and y must be given, z and y "
+                 "16-byte aligned");
+  gdn::GateSrc gs{};
+  gs.g = g;
+  gs.beta = beta;
+  gdn::OutNorm nrm{};
+  nrm.z = static_cast<const gdn::bf16*>(z);
+  nrm.w = norm_weight;
+  nrm.y = static_cast<gdn::bf16*>(y);
+  nrm.ldz = z_token_stride;
+  nrm.eps = eps;
+  nrm.w_f32 = weight_dtype == XOPS_F32;
+  return chunk_gdn_run(q, k, v, gs, h0, o, ht, cu_seqlens, B, T, N, Hg, H, K, V, q_token_stride,
+                       k_token_stride, v_token_stride, scale, use_qk_l2norm_in_kernel, workspace,
+                       workspace_bytes, stream, &nrm);
 }
 
 extern "C" int xops_device_error_count(void) {

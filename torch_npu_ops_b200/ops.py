@@ -659,6 +659,64 @@ def npu_chunk_gated_delta_rule(q, k, v, g, beta, scale=None, initial_state=None,
     return o, ht
 
 
+def chunk_gated_delta_rule_out_norm(q, k, v, g, beta, z, norm_weight, scale=None,
+                                    initial_state=None, output_final_state=False,
+                                    cu_seqlens=None, use_qk_l2norm_in_kernel=False, eps=1e-6,
+                                    return_o=False):
+    """``npu_chunk_gated_delta_rule`` followed by the GDN layer's output norm
+    ``layer_norm_fwd(o, norm_weight, None, eps, z, V, norm_before_gate=True,
+    is_rms_norm=True)`` (npu_triton_layernorm_fwd.cpp:48-333) as one call:
+    the chain kernel normalises each (token, head) row of its bf16 output as
+    it writes it, so o makes no round trip through HBM.  z: ``[B, T, H, V]``
+    (or any shape of those elements with V contiguous and a token stride),
+    bf16; norm_weight ``[V]`` fp32 or bf16.  Returns ``(y [B, T, H, V],
+    final_state or None, o or None)``; o (the rule's own output) is written
+    only with ``return_o``."""
+    _check(q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16
+           and z.dtype == torch.bfloat16,
+           "chunk_gated_delta_rule_out_norm expects q/k/v/z to be bfloat16.")
+    _check(norm_weight.dtype in (torch.float32, torch.bfloat16),
+           "chunk_gated_delta_rule_out_norm: norm weight must be fp32 or bf16")
+    if initial_state is not None:
+        _check(initial_state.dtype in (torch.bfloat16, torch.float32),
+               "chunk_gated_delta_rule expects initial_state to be bfloat16 or float32, got "
+               f"{initial_state.dtype}")
+    _cuda(q, k, v, g, beta, z, norm_weight, initial_state, cu_seqlens)
+    B, T, Hg, K = q.shape
+    H, V = v.shape[2], v.shape[3]
+    _check(q.shape == k.shape, "q and k must have the same shape.")
+    _check(H % Hg == 0, "chunk_gated_delta_rule expects num_heads_v to be divisible by "
+                        f"num_heads_qk, got {H} and {Hg}")
+    _check(beta.dim() == 3 and tuple(beta.shape) == (B, T, H), "beta must have shape [B, T, H].")
+    _check(g.dim() == 3 and tuple(g.shape) == (B, T, H), "g must have shape [B, T, H].")
+    _check(z.numel() == B * T * H * V and norm_weight.numel() == V,
+           "chunk_gated_delta_rule_out_norm: z must hold [B, T, H, V] and the weight [V]")
+    cu, _, _, N = _seq_info(q, cu_seqlens)
+    scale_v = float(scale) if scale is not None else K ** -0.5
+    h0 = initial_state.to(torch.float32).contiguous() if initial_state is not None else None
+    if h0 is not None:
+        _check(tuple(h0.shape) == (N, H, K, V), "initial_state must have shape [N, H, K, V]")
+    zr = z.reshape(B * T, H * V)
+    if zr.stride(1) != 1 or zr.stride(0) % 8 or zr.data_ptr() % 16:
+        zr = zr.contiguous()
+    w = norm_weight.contiguous()
+    y = torch.empty((B, T, H, V), dtype=v.dtype, device=v.device)
+    o = torch.empty((B, T, H, V), dtype=v.dtype, device=v.device) if return_o else None
+    ht = torch.empty((N, H, K, V), dtype=torch.float32, device=v.device) if output_final_state else None
+    qc, kc, vc = _token_rows(q, B), _token_rows(k, B), _token_rows(v, B)
+    gg, bb = g.to(torch.float32).contiguous(), beta.to(torch.float32).contiguous()
+    l2 = int(bool(use_qk_l2norm_in_kernel))
+    wsb = _lib.load().xops_chunk_gated_delta_rule_workspace_size(B, T, N, Hg, H, K, l2,
+                                                                 int(cu is not None))
+    ws = torch.empty(max(int(wsb), 16), dtype=torch.uint8, device=q.device)
+    _lib.call("xops_chunk_gated_delta_rule_out_norm", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+              gg.data_ptr(), bb.data_ptr(), _ptr(h0), _ptr(o), _ptr(ht), _ptr(cu), B, T, N, Hg, H,
+              K, V, qc.stride(1), kc.stride(1), vc.stride(1), scale_v, l2, zr.data_ptr(),
+              zr.stride(0), w.data_ptr(), _dt(w, "chunk_gated_delta_rule_out_norm"), float(eps),
+              y.data_ptr(), ws.data_ptr(), ws.numel(), _stream(q))
+    return y, ht, o
+
+
 def chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, scale=None, initial_state=None,
                                  output_final_state=False, cu_seqlens=None,
                                  use_qk_l2norm_in_kernel=False, softplus_beta=1.0,

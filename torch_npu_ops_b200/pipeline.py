@@ -7,7 +7,9 @@ its input and output projections.  A caller of the reference makes the calls
 use_qk_l2norm_in_kernel=True)`` -> ``layer_norm_fwd``; here the q/k L2
 normalisation moves out of the chunked rule into the conv kernel's output
 (``causal_conv1d_varlen_qk_l2norm``), which saves one read and one write of
-q and k.  ``bench.py`` times this function and the bench-configuration
+q and k, and the gated RMSNorm moves into the chunked rule's output
+epilogue (``chunk_gated_delta_rule_out_norm``), which saves one write and
+one read of o.  ``bench.py`` times this function and the bench-configuration
 parity test checks it, so both exercise exactly one code path.
 """
 
@@ -18,7 +20,7 @@ from . import ops
 
 def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z, norm_weight,
                 num_k_heads, num_v_heads, head_dim=128, eps=1e-6, query_start_loc=None,
-                events=None, gating=None):
+                events=None, gating=None, return_o=False, fuse_norm=True):
     """Runs one prefill of a GDN layer on the current CUDA stream.
 
     x: [T, (2 num_k_heads + num_v_heads) head_dim] conv input (q | k | v
@@ -30,12 +32,17 @@ def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z
     initial_state: [N, num_v_heads, head_dim, head_dim] fp32 or None.
     z: [T, num_v_heads, head_dim] gate of the output norm.  query_start_loc:
     [N + 1] int32 on the device (None: one sequence of T tokens).
-    ``events``: optional list of 4 CUDA events recorded before the conv and
-    after each stage.
+    ``events``: optional list of 4 CUDA events recorded before the conv,
+    after it, after the chunked rule and after the norm.  With g and beta
+    given and ``fuse_norm`` (the default), the norm runs inside the chunked
+    rule's chain kernel (``chunk_gated_delta_rule_out_norm``), so the last
+    two events bracket nothing and o is written only with ``return_o``;
+    ``fuse_norm=False`` runs the rule and ``layer_norm_fwd`` as two
+    operators (the reference's sequence).
 
     Returns (conv output [T, channels] with its q and k blocks
-    L2-normalised per head, o [1, T, num_v_heads, head_dim], final state
-    [N, num_v_heads, head_dim, head_dim] fp32, normed output
+    L2-normalised per head, o [1, T, num_v_heads, head_dim] or None, final
+    state [N, num_v_heads, head_dim, head_dim] fp32, normed output
     [T * num_v_heads, head_dim]).
     """
     T = x.shape[0]
@@ -52,13 +59,20 @@ def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z
     k = y[:, hk * d: 2 * hk * d].view(1, T, hk, d)
     v = y[:, 2 * hk * d:].view(1, T, hv, d)
     cu = None if query_start_loc.numel() == 2 else query_start_loc
+    if gating is None and fuse_norm:
+        out, ht, o = ops.chunk_gated_delta_rule_out_norm(q, k, v, g, beta, z, norm_weight, None,
+                                                         initial_state, True, cu, False, eps,
+                                                         return_o)
+        for e in (events or [])[2:]:
+            e.record()
+        return y, o, ht, out.view(-1, d)
     if gating is None:
         o, ht = ops.npu_chunk_gated_delta_rule(q, k, v, g, beta, None, initial_state, True, cu,
                                                False, False)
     else:
         A_log, a, b, dt_bias = gating
-        o, ht = ops.chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, None, initial_state,
-                                                 True, cu, False)
+        o, ht = ops.chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, None,
+                                                 initial_state, True, cu, False)
     if events:
         events[2].record()
     out = ops.layer_norm_fwd(o.view(-1, d), norm_weight, None, eps, z.view(-1, d), d, True, True)
