@@ -6,7 +6,8 @@
 Default workload (cfg5): one 65536-token sequence through causal_conv1d
 (8192 channels, width 4, SiLU) -> chunked gated delta rule (Hk 16 -> Hv 32,
 dk = dv = 128; the q/k L2 norm fused into the conv kernel) -> gated RMSNorm (group 128,
-SiLU(z) gate).  The 32 value heads, their key heads and conv channels are
+SiLU(z) gate; fused into the chunked rule's chain kernel, which writes the
+normalised output instead of o).  The 32 value heads, their key heads and conv channels are
 split over the N ranks (one process per GPU, no collective on the data path);
 the sequence is the unit of work, so `value` = 65536 tokens / max-over-ranks
 step time ("scaling": "strong").  cfg3 is the varlen 8-sequence 16384-token
@@ -37,9 +38,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "GDN prefill tokens/s/GPU; norm/RoPE/conv1d HBM GB/s vs B200 peak"
-# 1,312.3 MB of DRAM traffic for 16,384 tokens x 32 value heads (prep, both
-# chain phases, combine), measured by ncu (dram__bytes_read.sum + write.sum)
-GDN_DRAM_BYTES_PER_TOKEN_HEAD = 1.3123e9 / (16384 * 32)
+# 1,444.3 MB of DRAM traffic for 16,384 tokens x 32 value heads (prep, both
+# chain phases with the fused output norm, combine), measured by ncu
+# (dram__bytes_read.sum + write.sum)
+GDN_DRAM_BYTES_PER_TOKEN_HEAD = 1.4443e9 / (16384 * 32)
 
 
 def _peaks():
@@ -161,6 +163,38 @@ def make_step(cfg, kind, dev):
     # the gated RMSNorm runs inside the chunked rule's chain kernel: the
     # "gdn" stage is the rule and the norm together
     return step, ["conv", "gdn"]
+
+
+def rule_only_ms(cfg, dev, reps=5):
+    """cfg5: the chunked rule alone (npu_chunk_gated_delta_rule, the same
+    preparation / chain / combine kernels without the fused norm) on the
+    step's own conv output, median of `reps` CUDA-event timings; run after
+    the timed steps, outside them."""
+    import torch_npu_ops_b200 as ops
+    c, inp = cfg["consts"], cfg["dev"]
+    T, hv, hk, d = cfg["T"], cfg["hv"], cfg["hk"], 128
+    state = torch.zeros(1, cfg["C"], 3, dtype=torch.bfloat16, device=dev)
+    qsl = torch.tensor([0, T], dtype=torch.int32, device=dev)
+    y = ops.causal_conv1d_varlen_qk_l2norm(inp["x"], state, c["weight"], c["bias"], qsl,
+                                           2 * hk * d)
+    q = y[:, : hk * d].view(1, T, hk, d)
+    k = y[:, hk * d: 2 * hk * d].view(1, T, hk, d)
+    v = y[:, 2 * hk * d:].view(1, T, hv, d)
+
+    def rule():
+        return ops.npu_chunk_gated_delta_rule(q, k, v, inp["g"], inp["beta"], None,
+                                              inp["initial_state"], True, None, False, False)
+    for _ in range(2):
+        rule()
+    ts = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        rule()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
 
 
 def stage_bytes(cfg, kind):
@@ -413,7 +447,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile", action="store_true",
-                    help="for profiler runs: no clock soak, no e2e, no CPU baseline")
+                    help="for profiler runs: no clock soak, no e2e, no CPU baseline, no "
+                         "rule-only timing")
     a = ap.parse_args()
     if a.profile:
         a.no_e2e = a.no_cpu_baseline = True
@@ -431,7 +466,7 @@ def main():
     config = ({"workload": "cfg5: 1 x 65536-token prefill, conv1d(8192ch,w4,SiLU; q/k blocks "
                            "L2-normalised in the conv kernel) -> chunked GDN (Hk16->Hv32, "
                            "dk=dv=128, initial state ~N(0,0.02), final state returned) -> gated "
-                           "RMSNorm(g128)",
+                           "RMSNorm(g128, fused into the chain kernel's output epilogue)",
                "tokens": T, "heads_per_gpu": 32 // max(1, world, a.shard),
                "parallelism": f"head-shard x{world}" if not a.shard else
                               f"rank 0 of a head-shard x{a.shard} job, run alone",
@@ -533,7 +568,8 @@ def main():
     # phases, combine) from one ncu capture of the cfg5 shape at 16,384
     # tokens, per (token, value head), scaled by this run's tokens and heads.
     traffic = GDN_DRAM_BYTES_PER_TOKEN_HEAD * cfg["T"] * cfg["hv"]
-    roofline = {"kernel": "chunked GDN stage (prep + chain + combine)", "bound": "tensor",
+    roofline = {"kernel": "chunked GDN stage (prep + chain with the gated RMSNorm fused into "
+                          "its output + combine)", "bound": "tensor",
                 "achieved": achieved,
                 "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops_sustained"],
@@ -541,6 +577,13 @@ def main():
                 "flops_per_launch": flops, "launch_ms": gdn_ms, "traffic": traffic,
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, cfg5 shape "
                                   "at 16384 tokens, scaled by tokens x heads"}
+    if kind == "cfg5" and not a.profile:
+        r_ms = rule_only_ms(cfg, dev)
+        r_tf = flops / (r_ms / 1000.0) / 1e12
+        roofline["rule_only"] = {
+            "ms": r_ms, "achieved": r_tf, "frac": r_tf / peaks["bf16_tflops_sustained"],
+            "what": "the same rule kernels without the fused norm (npu_chunk_gated_delta_rule), "
+                    "timed after the steps"}
     kernels = {}
     for s, byt in stage_bytes(cfg, kind).items():
         gbs = byt / (stage_ms[s] / 1000.0) / 1e9
