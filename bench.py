@@ -406,7 +406,7 @@ def layer_compare(dev, T, steps, warmup):
                                                                     d, d)
         gt, beta = ops.npu_fused_gdn_gating(A_log, a, b, dt_bias)
         return gdn_prefill(mixed_qkv, st, w, cb, gt, beta.float(), h0, z, nw, hk, hv,
-                           query_start_loc=qsl)
+                           query_start_loc=qsl, fuse_norm=False)
 
     res = {}
     for name, fn in (("fused", fused), ("five_operators", unfused)):

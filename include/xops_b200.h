@@ -332,6 +332,29 @@ XOPS_API int xops_chunk_gated_delta_rule_out_norm(
     const void* z, int64_t z_token_stride, const void* norm_weight, int weight_dtype, float eps,
     void* y, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* xops_chunk_gated_delta_rule_gated with the output norm of
+ * xops_chunk_gated_delta_rule_out_norm: the GDN layer's prefill from its
+ * projections (fused_gdn_gating -> npu_chunk_gated_delta_rule ->
+ * layer_norm_fwd) with gates and norm inside the rule's kernels.  The z row
+ * of value head h of token t is read at z + t * z_token_stride +
+ * (h / z_heads_per_group) * z_group_stride + (h % z_heads_per_group) * V
+ * (elements; all multiples of 8, z 16-byte aligned), so z can be read in
+ * place from the layer's projection mixed_qkvz, whose key-head groups
+ * interleave their z heads with q, k and v (z_heads_per_group = H / Hg,
+ * z_group_stride = the group's width).  0 for z_heads_per_group,
+ * z_group_stride or z_token_stride selects 1, V and H * V.  Other arguments
+ * as the two entries it combines. */
+XOPS_API int xops_chunk_gated_delta_rule_gated_out_norm(
+    const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b,
+    const float* dt_bias, int a_dtype, int b_dtype, int64_t ab_token_stride, int ba_interleaved,
+    float softplus_beta, float softplus_threshold,
+    const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
+    int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
+    int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
+    const void* z, int64_t z_token_stride, int64_t z_heads_per_group, int64_t z_group_stride,
+    const void* norm_weight, int weight_dtype, float eps, void* y, void* workspace,
+    int64_t workspace_bytes, void* stream);
+
 /* Workspace bytes xops_chunk_gated_delta_rule needs (an upper bound computed
  * from shapes only, no device access); varlen = cu_seqlens given. */
 XOPS_API int64_t xops_chunk_gated_delta_rule_workspace_size(int64_t B, int64_t T, int64_t N,

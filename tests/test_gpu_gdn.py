@@ -508,9 +508,10 @@ def _lib_errors():
 @pytest.mark.parametrize("T,hk,hv,lens", [(8192, 2, 4, None), (3000, 4, 8, [1000, 64, 1936]),
                                           (4096, 2, 8, None)])
 def test_gdn_layer_prefill_from_projections(T, hk, hv, lens):
-    """Conv, gating and gated norm read the un-split projections in place;
-    the results equal split -> conv -> gating -> rule -> norm bit for bit,
-    and the rule's output matches the composed oracle."""
+    """Conv, gating and gated norm read the un-split projections in place
+    (the norm inside the rule's chain kernel); the results equal split ->
+    conv -> gating -> rule -> norm bit for bit, and the rule's output
+    matches the composed oracle."""
     from torch_npu_ops_b200.pipeline import gdn_layer_prefill, gdn_prefill
     g = torch.Generator().manual_seed(T + hv)
     d, r = 128, hv // hk
@@ -529,7 +530,13 @@ def test_gdn_layer_prefill_from_projections(T, hk, hv, lens):
     st1 = torch.zeros(N, C, 3, dtype=torch.bfloat16, device=DEV)
     st2 = st1.clone()
     fused = gdn_layer_prefill(_to(mixed_qkvz), _to(mixed_ba), st1, _to(w), _to(cb), _to(A_log),
-                              _to(dt_bias), _to(h0), _to(nw), hk, hv, query_start_loc=qsl)
+                              _to(dt_bias), _to(h0), _to(nw), hk, hv, query_start_loc=qsl,
+                              return_o=True)
+    # the layer's own call (o not written) gives the same normalised output
+    st3 = torch.zeros(N, C, 3, dtype=torch.bfloat16, device=DEV)
+    lean = gdn_layer_prefill(_to(mixed_qkvz), _to(mixed_ba), st3, _to(w), _to(cb), _to(A_log),
+                             _to(dt_bias), _to(h0), _to(nw), hk, hv, query_start_loc=qsl)
+    assert lean[1] is None
     mixed_qkv, z, b, a = ops.npu_fused_qkvzba_split_reshape_cat(_to(mixed_qkvz), _to(mixed_ba), hk,
                                                                 hv, d, d)
     gt, beta = ops.npu_fused_gdn_gating(_to(A_log), a, b, _to(dt_bias))
@@ -539,6 +546,7 @@ def test_gdn_layer_prefill_from_projections(T, hk, hv, lens):
     for x1, x2 in zip(fused, plain):
         assert torch.equal(x1, x2)
     assert torch.equal(st1, st2)
+    assert torch.equal(lean[3], plain[3]) and torch.equal(lean[2], plain[2])
     # the rule's output against the oracle, from the conv output both paths share
     y = fused[0].cpu()
     q = y[:, : hk * d].view(1, T, hk, d)

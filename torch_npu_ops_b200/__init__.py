@@ -21,6 +21,7 @@ from .ops import (  # noqa: F401
     npu_chunk_gated_delta_rule,
     chunk_gated_delta_rule_gated,
     chunk_gated_delta_rule_out_norm,
+    chunk_gated_delta_rule_gated_out_norm,
     npu_chunk_local_cumsum,
     npu_chunk_scaled_dot_kkt_fwd,
     npu_solve_tril,

@@ -51,6 +51,11 @@ SIGNATURES = {
     "xops_chunk_gated_delta_rule_out_norm": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64,
                                              _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f,
                                              _int, _p, _i64, _p, _int, _f, _p, _p, _i64, _p],
+    "xops_chunk_gated_delta_rule_gated_out_norm": [_p, _p, _p, _p, _p, _p, _p, _int, _int, _i64,
+                                                   _int, _f, _f, _p, _p, _p, _p, _i64, _i64, _i64,
+                                                   _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f,
+                                                   _int, _p, _i64, _i64, _i64, _p, _int, _f, _p,
+                                                   _p, _i64, _p],
     "xops_causal_conv1d_varlen_qkvz": [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64,
                                        _i64, _i64, _int, _i32, _int, _int, _f, _p],
     "xops_chunk_gated_delta_rule_workspace_size": [_i64, _i64, _i64, _i64, _i64, _i64, _int, _int],

@@ -939,10 +939,15 @@ struct ChainPlan {
 // layer_norm_fwd (is_rms_norm, norm_before_gate, no bias, group = V) that
 // the GDN layer applies to the rule's output next.  z == nullptr: no norm.
 struct OutNorm {
-  const bf16* z;   // [tokens, H * V] gate rows, ldz elements between tokens
+  // gate rows: head h of token t at z + t * ldz + (h / zr) * zgs + (h % zr) * V
+  // (zr = 1, zgs = V: [tokens, H * V] rows; a layer's projection interleaves
+  // the z heads of each key head with its other blocks: zr = H / Hg)
+  const bf16* z;
   const void* w;   // [V] weight, fp32 (w_f32) or bf16
   bf16* y;         // [tokens, H * V] normalised output
   int64_t ldz;
+  int64_t zgs;
+  int zr;
   float eps;
   int w_f32;
   int keep_o;      // also store o itself
@@ -1387,6 +1392,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
     const bool norm = NORM && write_o;
     const bool store_o = !NORM || nrm.keep_o;
     unsigned char* zst = ost + 1024;
+    const int64_t zh = NORM ? (int64_t)(h / nrm.zr) * nrm.zgs + (int64_t)(h % nrm.zr) * V : 0;
     uint32_t ncall = 0;
     auto load_z = [&](int64_t tb, int Lc) {
       __syncwarp();  // every lane has read the previous chunk's z
@@ -1395,7 +1401,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
         const int r = (lane >> 2) + 8 * j, m = lane & 3;
         const bool in = tc0 + r < Lc;
         cp_async16(zst + r * 64 + m * 16,
-                   nrm.z + (in ? tb + tc0 + r : tb) * nrm.ldz + (int64_t)h * V + quarter * 32 + m * 8,
+                   nrm.z + (in ? tb + tc0 + r : tb) * nrm.ldz + zh + quarter * 32 + m * 8,
                    in ? 16 : 0);
       }
       cp_async_commit();
@@ -2165,14 +2171,11 @@ extern "C" int xops_chunk_gated_delta_rule(const void* q, const void* k, const v
                        workspace_bytes, stream);
 }
 
-extern "C" int xops_chunk_gated_delta_rule_gated(
-    const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b,
-    const float* dt_bias, int a_dtype, int b_dtype, int64_t ab_token_stride, int ba_interleaved,
-    float softplus_beta, float softplus_threshold,
-    const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
-    int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
-    int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
-    void* workspace, int64_t workspace_bytes, void* stream) {
+// The gates of the fused-gating entries, from the layer's projections.
+static int gated_source(const float* A_log, const void* a, const void* b, const float* dt_bias,
+                        int a_dtype, int b_dtype, int64_t ab_token_stride, int ba_interleaved,
+                        float softplus_beta, float softplus_threshold, int64_t Hg, int64_t H,
+                        gdn::GateSrc* out) {
   auto ok_dtype = [](int d) { return d == XOPS_F32 || d == XOPS_BF16 || d == XOPS_F16; };
   XOPS_REQUIRE(ok_dtype(a_dtype) && ok_dtype(b_dtype),
                "chunk_gated_delta_rule_gated: a and b must be fp32, bf16 or fp16");
@@ -2194,9 +2197,81 @@ extern "C" int xops_chunk_gated_delta_rule_gated(
   gs.b_dt = b_dtype;
   gs.ab_ld = ab_token_stride;
   gs.ba_r = ba_interleaved ? (int)(H / Hg) : 0;
+  *out = gs;
+  return XOPS_OK;
+}
+
+extern "C" int xops_chunk_gated_delta_rule_gated(
+    const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b,
+    const float* dt_bias, int a_dtype, int b_dtype, int64_t ab_token_stride, int ba_interleaved,
+    float softplus_beta, float softplus_threshold,
+    const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
+    int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
+    int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
+    void* workspace, int64_t workspace_bytes, void* stream) {
+  gdn::GateSrc gs{};
+  if (int rc = gated_source(A_log, a, b, dt_bias, a_dtype, b_dtype, ab_token_stride,
+                            ba_interleaved, softplus_beta, softplus_threshold, Hg, H, &gs))
+    return rc;
   return chunk_gdn_run(q, k, v, gs, h0, o, ht, cu_seqlens, B, T, N, Hg, H, K, V, q_token_stride,
                        k_token_stride, v_token_stride, scale, use_qk_l2norm_in_kernel, workspace,
                        workspace_bytes, stream);
+}
+
+// Checks and fills the fused output norm of the _out_norm entries.
+static int out_norm_args(const void* z, int64_t z_token_stride, int64_t z_heads_per_group,
+                         int64_t z_group_stride, const void* norm_weight, int weight_dtype,
+                         float eps, void* y, int64_t N, int64_t T, int64_t H, int64_t V,
+                         gdn::OutNorm* out) {
+  XOPS_REQUIRE(weight_dtype == XOPS_F32 || weight_dtype == XOPS_BF16,
+               "chunk_gated_delta_rule_out_norm: the norm weight must be fp32 or bf16");
+  if (z_heads_per_group <= 0) z_heads_per_group = 1;
+  if (z_group_stride == 0) z_group_stride = z_heads_per_group * V;
+  if (z_token_stride == 0) z_token_stride = (H / z_heads_per_group) * z_group_stride;
+  XOPS_REQUIRE(H % z_heads_per_group == 0 && z_group_stride >= z_heads_per_group * V &&
+                   z_group_stride % 8 == 0 && z_token_stride % 8 == 0 &&
+                   z_token_stride >= ((H / z_heads_per_group - 1) * z_group_stride +
+                                      z_heads_per_group * V),
+               "chunk_gated_delta_rule_out_norm: z strides must cover the heads and be "
+               "multiples of 8");
+  if (N > 0 && T > 0)
+    XOPS_REQUIRE(z && norm_weight && y && aligned16(z) && aligned16(y),
+                 "chunk_gated_delta_rule_out_norm: z, weight and y must be given, z and y "
+                 "16-byte aligned");
+  gdn::OutNorm nrm{};
+  nrm.z = static_cast<const gdn::bf16*>(z);
+  nrm.w = norm_weight;
+  nrm.y = static_cast<gdn::bf16*>(y);
+  nrm.ldz = z_token_stride;
+  nrm.zgs = z_group_stride;
+  nrm.zr = (int)z_heads_per_group;
+  nrm.eps = eps;
+  nrm.w_f32 = weight_dtype == XOPS_F32;
+  *out = nrm;
+  return XOPS_OK;
+}
+
+extern "C" int xops_chunk_gated_delta_rule_gated_out_norm(
+    const void* q, const void* k, const void* v, const float* A_log, const void* a, const void* b,
+    const float* dt_bias, int a_dtype, int b_dtype, int64_t ab_token_stride, int ba_interleaved,
+    float softplus_beta, float softplus_threshold,
+    const float* h0, void* o, float* ht, const int32_t* cu_seqlens, int64_t B, int64_t T,
+    int64_t N, int64_t Hg, int64_t H, int64_t K, int64_t V, int64_t q_token_stride,
+    int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
+    const void* z, int64_t z_token_stride, int64_t z_heads_per_group, int64_t z_group_stride,
+    const void* norm_weight, int weight_dtype, float eps, void* y, void* workspace,
+    int64_t workspace_bytes, void* stream) {
+  gdn::GateSrc gs{};
+  if (int rc = gated_source(A_log, a, b, dt_bias, a_dtype, b_dtype, ab_token_stride,
+                            ba_interleaved, softplus_beta, softplus_threshold, Hg, H, &gs))
+    return rc;
+  gdn::OutNorm nrm{};
+  if (int rc = out_norm_args(z, z_token_stride, z_heads_per_group, z_group_stride, norm_weight,
+                             weight_dtype, eps, y, N, T, H, V, &nrm))
+    return rc;
+  return chunk_gdn_run(q, k, v, gs, h0, o, ht, cu_seqlens, B, T, N, Hg, H, K, V, q_token_stride,
+                       k_token_stride, v_token_stride, scale, use_qk_l2norm_in_kernel, workspace,
+                       workspace_bytes, stream, &nrm);
 }
 
 extern "C" int xops_chunk_gated_delta_rule_out_norm(
@@ -2206,26 +2281,13 @@ extern "C" int xops_chunk_gated_delta_rule_out_norm(
     int64_t k_token_stride, int64_t v_token_stride, float scale, int use_qk_l2norm_in_kernel,
     const void* z, int64_t z_token_stride, const void* norm_weight, int weight_dtype, float eps,
     void* y, void* workspace, int64_t workspace_bytes, void* stream) {
-  XOPS_REQUIRE(weight_dtype == XOPS_F32 || weight_dtype == XOPS_BF16,
-               "chunk_gated_delta_rule_out_norm: the norm weight must be fp32 or bf16");
-  if (z_token_stride == 0) z_token_stride = H * V;
-  XOPS_REQUIRE(z_token_stride >= H * V && z_token_stride % 8 == 0,
-               "chunk_gated_delta_rule_out_norm: z token stride must cover the heads and be a "
-               "multiple of 8");
-  if (N > 0 && T > 0)
-    XOPS_REQUIRE(z && norm_weight && y && aligned16(z) && aligned16(y),
-                 "chunk_gated_delta_rule_out_norm: z, weight and y must be given, z and y "
-                 "16-byte aligned");
+  gdn::OutNorm nrm{};
+  if (int rc = out_norm_args(z, z_token_stride, 1, V, norm_weight, weight_dtype, eps, y, N, T,
+                             H, V, &nrm))
+    return rc;
   gdn::GateSrc gs{};
   gs.g = g;
   gs.beta = beta;
-  gdn::OutNorm nrm{};
-  nrm.z = static_cast<const gdn::bf16*>(z);
-  nrm.w = norm_weight;
-  nrm.y = static_cast<gdn::bf16*>(y);
-  nrm.ldz = z_token_stride;
-  nrm.eps = eps;
-  nrm.w_f32 = weight_dtype == XOPS_F32;
   return chunk_gdn_run(q, k, v, gs, h0, o, ht, cu_seqlens, B, T, N, Hg, H, K, V, q_token_stride,
                        k_token_stride, v_token_stride, scale, use_qk_l2norm_in_kernel, workspace,
                        workspace_bytes, stream, &nrm);

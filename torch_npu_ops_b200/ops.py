@@ -731,6 +731,49 @@ def chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, scale=None, init
     un-split projection: per key head b (r heads) | a (r heads)) a and b are
     None and the gates are read from it in place.  Returns
     ``(o, final_state or None)``."""
+    o, ht, _ = _chunk_gated_call(q, k, v, A_log, a, b, dt_bias, scale, initial_state,
+                                 output_final_state, cu_seqlens, use_qk_l2norm_in_kernel,
+                                 softplus_beta, softplus_threshold, mixed_ba, None)
+    return o, ht
+
+
+def chunk_gated_delta_rule_gated_out_norm(q, k, v, A_log, a, b, dt_bias, z, norm_weight,
+                                          scale=None, initial_state=None,
+                                          output_final_state=False, cu_seqlens=None,
+                                          use_qk_l2norm_in_kernel=False, eps=1e-6,
+                                          softplus_beta=1.0, softplus_threshold=20.0,
+                                          mixed_ba=None, z_heads_per_group=1,
+                                          z_group_stride=None, return_o=False):
+    """``chunk_gated_delta_rule_gated`` followed by the layer's gated RMSNorm
+    ``layer_norm_fwd(o, norm_weight, None, eps, z, V, True, True)`` as one
+    call (the norm inside the chain kernel, as in
+    ``chunk_gated_delta_rule_out_norm``).  z: a bf16 view whose first
+    element is the gate of token 0, head 0; head h of token t starts
+    ``t * z.stride(0) + (h // z_heads_per_group) * z_group_stride +
+    (h % z_heads_per_group) * V`` elements further on (z_group_stride
+    defaults to z_heads_per_group * V), so it can be read in place from the
+    layer's projection.  Returns ``(y [B, T, H, V], final_state or None, o
+    or None)``."""
+    _check(z.dtype == torch.bfloat16 and z.stride(-1) == 1,
+           "chunk_gated_delta_rule_gated_out_norm: z must be bf16 with unit inner stride")
+    _check(norm_weight.dtype in (torch.float32, torch.bfloat16),
+           "chunk_gated_delta_rule_out_norm: norm weight must be fp32 or bf16")
+    _cuda(z, norm_weight)
+    V = v.shape[3]
+    zr = int(z_heads_per_group)
+    zgs = int(z_group_stride) if z_group_stride is not None else zr * V
+    w = norm_weight.contiguous()
+    _check(w.numel() == V, "chunk_gated_delta_rule_out_norm: the weight must have V elements")
+    norm = (z, z.stride(0), zr, zgs, w, float(eps), bool(return_o))
+    o, ht, y = _chunk_gated_call(q, k, v, A_log, a, b, dt_bias, scale, initial_state,
+                                 output_final_state, cu_seqlens, use_qk_l2norm_in_kernel,
+                                 softplus_beta, softplus_threshold, mixed_ba, norm)
+    return y, ht, o
+
+
+def _chunk_gated_call(q, k, v, A_log, a, b, dt_bias, scale, initial_state, output_final_state,
+                      cu_seqlens, use_qk_l2norm_in_kernel, softplus_beta, softplus_threshold,
+                      mixed_ba, norm):
     _check(q.dtype == torch.bfloat16 and k.dtype == torch.bfloat16 and v.dtype == torch.bfloat16,
            "chunk_gated_delta_rule expects q/k/v to be bfloat16.")
     _cuda(q, k, v, A_log, a, b, dt_bias, initial_state, cu_seqlens)
@@ -762,7 +805,8 @@ def chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, scale=None, init
     h0 = initial_state.to(torch.float32).contiguous() if initial_state is not None else None
     if h0 is not None:
         _check(tuple(h0.shape) == (N, H, K, V), "initial_state must have shape [N, H, K, V]")
-    o = torch.empty((B, T, H, V), dtype=v.dtype, device=v.device)
+    want_o = norm is None or norm[6]
+    o = torch.empty((B, T, H, V), dtype=v.dtype, device=v.device) if want_o else None
     ht = torch.empty((N, H, K, V), dtype=torch.float32, device=v.device) if output_final_state else None
     qc, kc, vc = _token_rows(q, B), _token_rows(k, B), _token_rows(v, B)
     if mixed_ba is not None:
@@ -776,14 +820,21 @@ def chunk_gated_delta_rule_gated(q, k, v, A_log, a, b, dt_bias, scale=None, init
     wsb = _lib.load().xops_chunk_gated_delta_rule_workspace_size(B, T, N, Hg, H, K, l2,
                                                                  int(cu is not None))
     ws = torch.empty(max(int(wsb), 16), dtype=torch.uint8, device=q.device)
-    _lib.call("xops_chunk_gated_delta_rule_gated", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(),
-              Al.data_ptr(), ac.data_ptr(), bc.data_ptr(), dtb.data_ptr(),
-              _dt(ac, "chunk_gated_delta_rule_gated"), _dt(bc, "chunk_gated_delta_rule_gated"),
-              ab_ld, inter, float(softplus_beta), float(softplus_threshold), _ptr(h0), o.data_ptr(),
-              _ptr(ht),
-              _ptr(cu), B, T, N, Hg, H, K, V, qc.stride(1), kc.stride(1), vc.stride(1), scale_v, l2,
+    head = (qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), Al.data_ptr(), ac.data_ptr(),
+            bc.data_ptr(), dtb.data_ptr(), _dt(ac, "chunk_gated_delta_rule_gated"),
+            _dt(bc, "chunk_gated_delta_rule_gated"), ab_ld, inter, float(softplus_beta),
+            float(softplus_threshold), _ptr(h0), _ptr(o), _ptr(ht), _ptr(cu), B, T, N, Hg, H, K, V,
+            qc.stride(1), kc.stride(1), vc.stride(1), scale_v, l2)
+    if norm is None:
+        _lib.call("xops_chunk_gated_delta_rule_gated", *head, ws.data_ptr(), ws.numel(),
+                  _stream(q))
+        return o, ht, None
+    z, zld, zr, zgs, w, eps, _ = norm
+    y = torch.empty((B, T, H, V), dtype=v.dtype, device=v.device)
+    _lib.call("xops_chunk_gated_delta_rule_gated_out_norm", *head, z.data_ptr(), zld, zr, zgs,
+              w.data_ptr(), _dt(w, "chunk_gated_delta_rule_out_norm"), eps, y.data_ptr(),
               ws.data_ptr(), ws.numel(), _stream(q))
-    return o, ht
+    return o, ht, y
 
 
 # ---- chunk pipeline sub-operators (reference decomposition, chunk.py:31-73)

@@ -83,7 +83,8 @@ def gdn_prefill(x, conv_state, conv_weight, conv_bias, g, beta, initial_state, z
 
 def gdn_layer_prefill(mixed_qkvz, mixed_ba, conv_state, conv_weight, conv_bias, A_log, dt_bias,
                       initial_state, norm_weight, num_k_heads, num_v_heads, head_dim=128,
-                      eps=1e-6, query_start_loc=None, events=None):
+                      eps=1e-6, query_start_loc=None, events=None, return_o=False,
+                      fuse_norm=True):
     """One prefill of a GDN layer from its input projections.
 
     A caller of the reference runs ``npu_fused_qkvzba_split_reshape_cat`` ->
@@ -92,13 +93,16 @@ def gdn_layer_prefill(mixed_qkvz, mixed_ba, conv_state, conv_weight, conv_bias, 
     reads q, k, v from ``mixed_qkvz [T, Hk * (2 + 2r) * 128]`` in place
     (``causal_conv1d_varlen_qkvz``), the chunked rule computes its gates
     from ``mixed_ba [T, Hk * 2r]`` in place, and the gated norm reads z from
-    ``mixed_qkvz`` as a strided view (r = num_v_heads / num_k_heads).  The
-    results equal the five-call sequence bit for bit.
+    ``mixed_qkvz`` as a strided view (r = num_v_heads / num_k_heads) inside
+    the rule's chain kernel (``chunk_gated_delta_rule_gated_out_norm``;
+    ``fuse_norm=False`` runs ``layer_norm_fwd`` after the rule instead).
+    The results equal the five-call sequence bit for bit.
 
     Returns (conv output [T, (2 Hk + Hv) 128] with q/k L2-normalised, o
-    [1, T, Hv, 128], final state [N, Hv, 128, 128] fp32, normed output
-    [T * Hv, 128]).  ``events``: optional list of 4 CUDA events recorded
-    before the conv and after each stage.
+    [1, T, Hv, 128] (None when the norm is fused and ``return_o`` is not
+    set), final state [N, Hv, 128, 128] fp32, normed output [T * Hv, 128]).
+    ``events``: optional list of 4 CUDA events recorded before the conv and
+    after each stage (with the fused norm the last two bracket nothing).
     """
     T = mixed_qkvz.shape[0]
     hk, hv, d = num_k_heads, num_v_heads, head_dim
@@ -116,6 +120,17 @@ def gdn_layer_prefill(mixed_qkvz, mixed_ba, conv_state, conv_weight, conv_bias, 
     k = y[:, hk * d: 2 * hk * d].view(1, T, hk, d)
     v = y[:, 2 * hk * d:].view(1, T, hv, d)
     cu = None if query_start_loc.numel() == 2 else query_start_loc
+    if fuse_norm:
+        # z head h of token t: in key head h // r's group of the projection
+        # row, after its q, k and r v heads
+        zv = mixed_qkvz[:, (2 + r) * d:]
+        out, ht, o = ops.chunk_gated_delta_rule_gated_out_norm(
+            q, k, v, A_log, None, None, dt_bias, zv, norm_weight, None, initial_state, True, cu,
+            False, eps, mixed_ba=mixed_ba, z_heads_per_group=r, z_group_stride=gw,
+            return_o=return_o)
+        for e in (events or [])[2:]:
+            e.record()
+        return y, o, ht, out.view(T * hv, d)
     o, ht = ops.chunk_gated_delta_rule_gated(q, k, v, A_log, None, None, dt_bias, None,
                                              initial_state, True, cu, False, mixed_ba=mixed_ba)
     if events:
