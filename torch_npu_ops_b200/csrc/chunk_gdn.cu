@@ -902,7 +902,9 @@ constexpr int C_TAB = 1024;
 // gate rows z (and the normalised rows, in place) [16 x 32] bf16
 constexpr int C_OFF_OST = C_OFF_TAB + 4 * C_TAB;
 // fused output norm: weight [128] fp32, then the partial sums of squares of
-// 8 values each [column quarter][2 alternating sets][16 tokens][16 pieces] fp32
+// 8 values each [column quarter][2 alternating sets][token half][TMEM lane
+// quarter][piece within the quarter][token % 8] fp32 (a lane's reads and
+// writes fall in 32 distinct banks)
 constexpr int C_OFF_NRM = C_OFF_OST + C_EPI_WARPS * 2048;
 constexpr int C_SMEM = C_OFF_NRM + 512 + 8192 + 1024;
 // TMEM columns.  fp32 accumulators: D_u, D_qh (adjacent: one N = 128 product
@@ -1423,7 +1425,7 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
           const float2 x = unpack2<bf16>(pw[u]);
           s2 = ffma2(x, x, s2);
         }
-        red[r * 16 + quarter * 4 + m] = s2.x + s2.y;
+        red[j * 128 + quarter * 32 + m * 8 + (lane >> 2)] = s2.x + s2.y;
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&nbar[set]);
@@ -1434,18 +1436,12 @@ __global__ void __launch_bounds__(C_NT, 1) chunk_chain_kernel(
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int r = (lane >> 2) + 8 * j;
-        float a[8];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float4 lo = *reinterpret_cast<const float4*>(red + r * 16 + 4 * e);
-          const float4 hi = *reinterpret_cast<const float4*>(red + r * 16 + 8 + 4 * e);
-          a[4 * e] = lo.x + hi.x;
-          a[4 * e + 1] = lo.y + hi.y;
-          a[4 * e + 2] = lo.z + hi.z;
-          a[4 * e + 3] = lo.w + hi.w;
-        }
-        const float b0 = a[0] + a[4], b1 = a[1] + a[5], b2 = a[2] + a[6], b3 = a[3] + a[7];
-        const float tot = (b0 + b2) + (b1 + b3);
+        // the row's pieces P = 4 q + m: this lane reads the four with its m
+        // and the butterfly's last two levels (m ^ 2, m ^ 1) are shuffles
+        const float* rp = red + j * 128 + m * 8 + (lane >> 2);
+        float b = (rp[0] + rp[64]) + (rp[32] + rp[96]);  // (P_m + P_m+8) + (P_m+4 + P_m+12)
+        b += __shfl_xor_sync(0xffffffffu, b, 2);
+        const float tot = b + __shfl_xor_sync(0xffffffffu, b, 1);
         const float rs = rsqrtf(tot * (1.0f / 128) + nrm.eps);
         const float2 r2 = make_float2(rs, rs);
         uint4* op = reinterpret_cast<uint4*>(ost + r * 64 + m * 16);
