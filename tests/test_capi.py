@@ -69,6 +69,37 @@ def test_host_validation_gqa(lib):
     assert rc == 1 and "divisible" in msg
 
 
+def _out_norm(lib, z, zld, w_dtype, y, T=64, H=4):
+    # q k v g beta h0 o ht cu | B T N Hg H K V | strides | scale l2 | z zld w wdt eps y | ws
+    return _call(lib, "xops_chunk_gated_delta_rule_out_norm", None, None, None, None, None, None,
+                 None, None, None, 1, T, 1, 2, H, 128, 128, 0, 0, 0, 0.1, 0, z, zld, 16, w_dtype,
+                 1e-6, y, None, 0, None)
+
+
+def test_host_validation_out_norm(lib):
+    # the norm weight is fp32 or bf16 only
+    rc, msg = _out_norm(lib, 16, 0, 2, 16)
+    assert rc == 1 and "fp32 or bf16" in msg
+    # z token stride below the heads, or not a multiple of 8
+    rc, msg = _out_norm(lib, 16, 4 * 128 - 8, 1, 16)
+    assert rc == 1 and "stride" in msg
+    rc, msg = _out_norm(lib, 16, 4 * 128 + 4, 1, 16)
+    assert rc == 1 and "stride" in msg
+    # z and y are required (o is optional)
+    rc, msg = _out_norm(lib, None, 0, 1, 16)
+    assert rc == 1 and "must be given" in msg
+    # nothing to do: OK without touching the device
+    assert _out_norm(lib, None, 0, 1, None, T=0)[0] == 0
+
+
+def test_host_validation_gated_out_norm(lib):
+    # z heads grouped per key head: the group size must divide H
+    rc, msg = _call(lib, "xops_chunk_gated_delta_rule_gated_out_norm", None, None, None, None,
+                    None, None, None, 1, 1, 0, 1, 1.0, 20.0, None, None, None, None, 1, 64, 1, 2,
+                    4, 128, 128, 0, 0, 0, 0.1, 0, 16, 0, 3, 0, 16, 1, 1e-6, 16, None, 0, None)
+    assert rc == 1 and "stride" in msg
+
+
 def test_host_validation_conv_width(lib):
     rc, msg = _call(lib, "xops_causal_conv1d_varlen", None, None, None, None, None, None, None,
                     2, 10, 64, 9, 2, 1, -1, 1, None)
