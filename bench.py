@@ -466,7 +466,7 @@ def main():
     config = ({"workload": "cfg5: 1 x 65536-token prefill, conv1d(8192ch,w4,SiLU; q/k blocks "
                            "L2-normalised in the conv kernel) -> chunked GDN (Hk16->Hv32, "
                            "dk=dv=128, initial state ~N(0,0.02), final state returned) -> gated "
-                           "RMSNorm(g128, fused into the chain kernel's output epilogue)",
+                           "RMSNorm(g128)",
                "tokens": T, "heads_per_gpu": 32 // max(1, world, a.shard),
                "parallelism": f"head-shard x{world}" if not a.shard else
                               f"rank 0 of a head-shard x{a.shard} job, run alone",
