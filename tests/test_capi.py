@@ -146,6 +146,13 @@ def test_ops_fail_loudly_off_gpu():
     g = torch.zeros(1, 8, 4)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.npu_chunk_gated_delta_rule(q, q, v, g, g)
+    z = torch.randn(1, 8, 4, 128, dtype=torch.bfloat16)
+    w = torch.ones(128)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.chunk_gated_delta_rule_out_norm(q, q, v, g, g, z, w)
+    A_log, dt = torch.zeros(4), torch.zeros(4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.chunk_gated_delta_rule_gated_out_norm(q, q, v, A_log, g[0], g[0], dt, z, w)
 
 
 def test_ops_reject_like_reference():
